@@ -1,0 +1,380 @@
+#!/usr/bin/env python
+"""Benchmark: atom-steps/s of DPA4C-style energy + force + virial evaluation.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200dp|reference]
+
+One step = one evaluation of the hot path (neighbour graph from coordinates,
+descriptor, fitting forward + backward, force / virial assembly) over the
+12,288-atom water system of the 1-GPU configuration (4096 H2O, 49.68 A cube,
+water model sel [46,92], embedding [25,50,100], axis 16, fitting [240]*3,
+random-init weights, seed 0).  Inputs are seeded synthetic data.
+
+* ``value``: device-timed throughput, inputs resident in HBM, CUDA events on
+  the launch stream around each step; L2 is flushed (256 MB write) before
+  every timed step, outside the events.  Multi-GPU: one process per GPU, each
+  rank evaluates its own replica (weak scaling), time = max over ranks.
+* ``e2e``: the same metric through the host C entry (b200dp_compute_host) with
+  pinned host buffers: H2D of coordinates and types, D2H of forces, energy
+  and virial inside the timed region.
+* ``roofline``: the dominant kernel (descriptor backward), algorithmic FLOPs
+  per launch over its CUDA-event duration, against the measured bf16 peak.
+* ``cpu_baseline``: the CPU oracle (C++ fp64, OpenMP) on the host cores.
+
+``--impl reference`` times the reference arm: the reference ships no CPU (or
+NVIDIA) implementation of this path, so it is the CPU restatement (oracle)
+run with all host threads on the same configuration.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "dpa4c-scale-aware-md_b200")
+sys.path.insert(0, PKG)
+
+import modelgen  # noqa: E402
+import systems  # noqa: E402
+
+METRIC = "atom-steps/s (E+F+virial)"
+WORKLOAD = "c1_water_12288"
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200dp", choices=["b200dp", "reference"])
+    ap.add_argument("--precision", default="mixed", choices=["mixed", "fp64"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def model_path(kind="water"):
+    d = tempfile.mkdtemp(prefix="b200dp_bench_")
+    p = os.path.join(d, f"{kind}.b2dp")
+    modelgen.save(modelgen.random_model(kind, seed=0), p)
+    return p
+
+
+# ----------------------------------------------------------------- clocks
+REASON_COLS = ["clocks_event_reasons.hw_slowdown", "clocks_event_reasons.hw_thermal_slowdown",
+               "clocks_event_reasons.sw_thermal_slowdown", "clocks_event_reasons.sw_power_cap"]
+
+
+def start_clocks(gpu: int, path: str):
+    q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active," + ",".join(REASON_COLS))
+    try:
+        f = open(path, "w")
+        p = subprocess.Popen(["nvidia-smi", "-i", str(gpu), f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                              "-lms", "200"], stdout=f, stderr=subprocess.DEVNULL)
+        return p, f
+    except OSError:
+        return None, None
+
+
+def stop_clocks(p, f, path):
+    if p is None:
+        return None
+    p.terminate()
+    try:
+        p.wait(timeout=5)
+    except subprocess.TimeoutExpired:
+        p.kill()
+    f.close()
+    sm, smax, reasons = [], None, set()
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    for line in open(path):
+        parts = [x.strip() for x in line.split(",")]
+        if len(parts) < 9:
+            continue
+        try:
+            sm.append(float(parts[1]))
+            smax = float(parts[2])
+        except ValueError:
+            continue
+        for n, v in zip(names, parts[5:9]):
+            if v.lower() == "active":
+                reasons.add(n)
+    if not sm:
+        return None
+    return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": smax, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------- roofline inputs
+def model_flops(m: modelgen.SeaModel, nloc: int, edges: int):
+    """Algorithmic FLOPs (2 per multiply-add) per evaluation, split by kernel."""
+    dims = m.emb_dims()
+    emb_mac = sum(dims[l] * dims[l + 1] for l in range(len(dims) - 1))
+    emb_bwd_mac = sum(dims[l] * dims[l + 1] for l in range(1, len(dims) - 1)) + dims[1]
+    M1, M2 = m.emb[-1], m.axis
+    fwd = 2 * (edges * (emb_mac + 4 * M1) + nloc * 4 * M1 * M2)
+    bwd = 2 * (edges * (emb_mac + emb_bwd_mac + 8 * M1) + nloc * 8 * M1 * M2)
+    fd = m.fit_dims()
+    fit_mac = sum(fd[l] * fd[l + 1] for l in range(len(fd) - 1))
+    fit = 2 * nloc * (2 * fit_mac)
+    return {"descriptor_fwd": fwd, "fitting": fit, "descriptor_bwd": bwd, "total": fwd + fit + bwd}
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def ncu_traffic(kernel: str):
+    """DRAM bytes per launch of `kernel` recorded in the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", f"{kernel}_c1_water.md")
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        m = re.match(r"\s*traffic_bytes_per_launch:\s*([0-9.eE+]+)", line)
+        if m:
+            return float(m.group(1))
+    return None
+
+
+# ----------------------------------------------------------------- arms
+def cpu_oracle_rate(model_file, system, threads=None, repeats=1):
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+
+    used = oracle.set_threads(threads or os.cpu_count() or 1)
+    o = oracle.Oracle(model_file)
+    o.compute(system.coord[:192], system.atype[:192], None)  # load / first-touch
+    t0 = time.perf_counter()
+    for _ in range(repeats):
+        o.compute(system.coord, system.atype, system.box, atomic=False)
+    dt = (time.perf_counter() - t0) / repeats
+    return system.natoms / dt, used, dt
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    system = systems.config1()
+    mp = model_path("water")
+    for _ in range(args.warmup):
+        cpu_oracle_rate(mp, system)
+    t0 = time.perf_counter()
+    used = None
+    for _ in range(args.steps):
+        _, used, _ = cpu_oracle_rate(mp, system)
+    dt = (time.perf_counter() - t0) / args.steps
+    value = system.natoms / dt
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "atom-steps/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic (seeded)",
+        "config": {"workload": WORKLOAD, "atoms": system.natoms, "model": "water se_e2_a-type, random init"},
+        "cpu_baseline": {"value": value, "unit": "atom-steps/s", "cores": used, "kind": "port",
+                         "sample": "one full evaluation of the 12,288-atom system per step"},
+        "e2e": {"value": value, "unit": "atom-steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference has no CPU or NVIDIA implementation of this path; the reference arm is the "
+                "C++ fp64 restatement (oracle/) on all host threads",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_b200dp(args, world, rank, local):
+    import torch
+
+    import b200dp
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120))
+    system = systems.water(16, seed=rank, name=WORKLOAD) if rank else systems.config1()
+    n = system.natoms
+    mp = model_path("water")
+    m = modelgen.load(mp)
+    prec = b200dp.MIXED if args.precision == "mixed" else b200dp.FP64
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(dev)
+    x = torch.tensor(system.coord, device=dev)
+    t = torch.tensor(system.atype, device=dev)
+    e = torch.zeros(1, dtype=torch.float64, device=dev)
+    f = torch.zeros(n, 3, dtype=torch.float64, device=dev)
+    v = torch.zeros(9, dtype=torch.float64, device=dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    def device_loop(dp, steps, warmup, stage_timing):
+        def step():
+            dp.compute_device(stream.cuda_stream, n, 0, x.data_ptr(), t.data_ptr(), system.box, None, e.data_ptr(),
+                              f.data_ptr(), v.data_ptr())
+
+        for _ in range(warmup):
+            step()
+        dp.check()
+        dp.set_stage_timing(stage_timing)
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        stages = []
+        l0 = b200dp.kernel_launches()
+        for k in range(steps):
+            flush.fill_(k & 0xFF)
+            starts[k].record(stream)
+            step()
+            ends[k].record(stream)
+            if stage_timing:
+                stages.append(dp.stage_times())
+        torch.cuda.synchronize()
+        launches = b200dp.kernel_launches() - l0
+        if dist:
+            dist.barrier()
+        dp.check()
+        ms = sum(s.elapsed_time(en) for s, en in zip(starts, ends))
+        return ms, launches, stages
+
+    dp = b200dp.DeepPot(mp, precision=prec, device=local)
+    clk_path = os.path.join(tempfile.gettempdir(), f"b200dp_clocks_{rank}.csv")
+    cp, cf = start_clocks(local, clk_path)
+    ms, launches, stages = device_loop(dp, args.steps, args.warmup, True)
+    clocks = stop_clocks(cp, cf, clk_path)
+    if dist:
+        tt = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    value = world * n * args.steps / (ms / 1e3)
+    # edges (real neighbours) of this workload for the FLOP count
+    nl = dp.last_nlist(n)["nlist"]
+    edges = int((nl >= 0).sum())
+    fl = model_flops(m, n, edges)
+    st = np.array(stages)  # [steps, 5]
+    stage_ms = st.mean(0) if len(st) else np.zeros(5)
+    pk, pk_kind = peaks()
+    bwd_ms = float(stage_ms[3])
+    achieved = fl["descriptor_bwd"] / (bwd_ms / 1e3) / 1e12 if bwd_ms > 0 else 0.0
+    peak = float(pk["bf16_tflops"])
+    roofline = {"kernel": "k_descriptor_bwd", "bound": "tensor", "achieved": achieved, "peak": peak,
+                "unit": "TFLOP/s", "frac": achieved / peak, "traffic": ncu_traffic("descriptor_bwd"),
+                "peak_source": f"{pk_kind} bf16 burst (MEASURED_PEAKS.json)" if pk_kind == "measured"
+                else "fallback 1.59 PFLOP/s",
+                "flops_per_launch": fl["descriptor_bwd"], "avg_launch_ms": bwd_ms,
+                "note": "SIMT fp32 kernel measured against the tensor-core peak it is to be moved onto"}
+    # e2e through the host C entry with pinned buffers
+    e2e = None
+    try:
+        e2e = e2e_loop(dp, system, args.steps, max(1, min(args.warmup, 3)), torch)
+    except Exception as ex:  # report, never hide
+        e2e = {"error": repr(ex)}
+    if dist:
+        ev = torch.tensor([e2e.get("seconds", 0.0)], dtype=torch.float64, device=dev)
+        dist.all_reduce(ev, op=dist.ReduceOp.MAX)
+        if "seconds" in e2e:
+            e2e["value"] = world * n * args.steps / float(ev.item())
+    # fp64 mode (secondary line item)
+    fp64 = None
+    if prec == b200dp.MIXED:
+        dp64 = b200dp.DeepPot(mp, precision=b200dp.FP64, device=local)
+        k64 = max(2, min(args.steps, 5))
+        ms64, _, st64 = device_loop(dp64, k64, max(1, min(args.warmup, 2)), True)
+        if dist:
+            tt = torch.tensor([ms64], dtype=torch.float64, device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            ms64 = float(tt.item())
+        fp64 = {"value": world * n * k64 / (ms64 / 1e3), "ms_per_step": ms64 / k64,
+                "stage_ms": [round(float(q), 4) for q in np.array(st64).mean(0)]}
+        dp64.close()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, used, dt = cpu_oracle_rate(mp, system)
+        cpu = {"value": rate, "unit": "atom-steps/s", "cores": used, "kind": "port",
+               "sample": f"one full evaluation of the 12,288-atom system ({dt:.2f} s), fp64 C++ oracle, OpenMP"}
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "atom-steps/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32-mixed" if prec == b200dp.MIXED else "f64",
+            "data": "synthetic (seeded water, random-init weights)",
+            "config": {"workload": WORKLOAD, "atoms": n, "edges": edges, "model": "water se_e2_a-type",
+                       "precision": args.precision, "parallelism": f"replicas x{world}" if world > 1 else "single",
+                       "l2": "flushed before every timed step (256 MB write), flush outside the events"},
+            "stage_ms": {k: round(float(q), 4) for k, q in
+                         zip(["neighbour", "descriptor_fwd", "fitting", "descriptor_bwd", "assembly"], stage_ms)},
+            "gpu_launches": int(launches),
+            "roofline": roofline,
+            "e2e": e2e,
+            "fp64": fp64,
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+            "flops_per_step": fl["total"],
+        }
+        print(json.dumps(line), flush=True)
+    dp.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def e2e_loop(dp, system, steps, warmup, torch):
+    import ctypes
+
+    import b200dp
+
+    n = system.natoms
+    coord = torch.tensor(system.coord).pin_memory()
+    atype = torch.tensor(system.atype).pin_memory()
+    force = torch.zeros(n, 3, dtype=torch.float64).pin_memory()
+    e = torch.zeros(1, dtype=torch.float64).pin_memory()
+    v = torch.zeros(9, dtype=torch.float64).pin_memory()
+    box = np.ascontiguousarray(system.box.reshape(9))
+    L = dp.L
+    dptr = ctypes.POINTER(ctypes.c_double)
+    iptr = ctypes.POINTER(ctypes.c_int)
+
+    def call():
+        rc = L.b200dp_compute_host(dp.h, n, 0, ctypes.cast(coord.data_ptr(), dptr), ctypes.cast(atype.data_ptr(), iptr),
+                                   box.ctypes.data_as(dptr), ctypes.cast(e.data_ptr(), dptr),
+                                   ctypes.cast(force.data_ptr(), dptr), ctypes.cast(v.data_ptr(), dptr), None, None)
+        if rc != 0:
+            raise b200dp.B200DPError(rc, L.b200dp_last_error(dp.h).decode())
+
+    for _ in range(warmup):
+        call()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        call()
+    dt = time.perf_counter() - t0
+    return {"value": n * steps / dt, "unit": "atom-steps/s", "seconds": dt,
+            "h2d_bytes_per_step": n * 3 * 8 + n * 4, "d2h_bytes_per_step": n * 3 * 8 + 8 * 10,
+            "entry": "b200dp_compute_host (pinned host buffers, synchronous)"}
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_env()
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        return
+    run_b200dp(args, world, rank, local)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,221 @@
+"""Python binding of the b200dp C ABI (include/b200dp.h) over ctypes.
+
+Mirrors DeePMD's ``DeepPot`` surface for this path: ``DeepPot(model).compute
+(coord, atype, box)`` returns energy, forces and virial (plus atomic terms),
+and ``compute(..., nghost=...)`` follows the LAMMPS ghost-atom convention of
+``DeepPot::compute(..., nghost, lmp_list, ago)``
+(components/deepmd-op/overlays/api_cc/include/DeepPot.h:605-690 in the
+reference).  Errors are raised as ``B200DPError`` carrying the C status.
+
+The shared library is the only compute path: there is no CPU fallback, and a
+missing or unloadable ``libb200dp.so`` raises at import of the engine.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libb200dp.so")
+
+FP64 = 0
+MIXED = 1
+
+STATUS = {0: "OK", 1: "INVALID", 2: "IO", 3: "CUDA", 4: "SEL_OVERFLOW", 5: "CAPACITY", 6: "BAD_TYPE",
+          7: "UNSUPPORTED"}
+
+EXPORTS = [
+    "b200dp_options_default", "b200dp_create", "b200dp_destroy", "b200dp_last_error", "b200dp_model_info_get",
+    "b200dp_compute_host", "b200dp_compute_host_nlist", "b200dp_compute_device", "b200dp_check",
+    "b200dp_sel_overflow_count", "b200dp_last_nlist", "b200dp_last_descriptor", "b200dp_set_stage_timing",
+    "b200dp_stage_times", "b200dp_kernel_launches",
+]
+
+
+class B200DPError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"b200dp status {STATUS.get(status, status)}: {msg}")
+        self.status = status
+
+
+class Options(ctypes.Structure):
+    _fields_ = [("precision", ctypes.c_int), ("device", ctypes.c_int), ("sel_overflow_is_error", ctypes.c_int),
+                ("reserved", ctypes.c_int * 13)]
+
+
+class ModelInfo(ctypes.Structure):
+    _fields_ = [("ntypes", ctypes.c_int), ("sel_total", ctypes.c_int), ("descriptor_dim", ctypes.c_int),
+                ("embedding_out", ctypes.c_int), ("axis", ctypes.c_int), ("n_embedding_layers", ctypes.c_int),
+                ("n_fitting_layers", ctypes.c_int), ("type_one_side", ctypes.c_int), ("rcut", ctypes.c_double),
+                ("rcut_smth", ctypes.c_double)]
+
+
+class NList(ctypes.Structure):
+    _fields_ = [("inum", ctypes.c_int), ("ilist", ctypes.POINTER(ctypes.c_int)),
+                ("numneigh", ctypes.POINTER(ctypes.c_int)),
+                ("firstneigh", ctypes.POINTER(ctypes.POINTER(ctypes.c_int)))]
+
+
+_dp = ctypes.POINTER(ctypes.c_double)
+_ip = ctypes.POINTER(ctypes.c_int)
+_vp = ctypes.c_void_p
+_L = None
+
+
+def load_library(path: str = LIB_PATH):
+    """Loads libb200dp.so (raises OSError if it is missing)."""
+    global _L
+    if _L is not None:
+        return _L
+    if not os.path.exists(path):
+        raise OSError(f"{path} not built; run dpa4c-scale-aware-md_b200/build.py")
+    L = ctypes.CDLL(path)
+    L.b200dp_options_default.argtypes = [ctypes.POINTER(Options)]
+    L.b200dp_create.argtypes = [ctypes.c_char_p, ctypes.POINTER(Options), ctypes.POINTER(_vp)]
+    L.b200dp_create.restype = ctypes.c_int
+    L.b200dp_destroy.argtypes = [_vp]
+    L.b200dp_last_error.argtypes = [_vp]
+    L.b200dp_last_error.restype = ctypes.c_char_p
+    L.b200dp_model_info_get.argtypes = [_vp, ctypes.POINTER(ModelInfo)]
+    L.b200dp_compute_host.argtypes = [_vp, ctypes.c_int, ctypes.c_int, _dp, _ip, _dp, _dp, _dp, _dp, _dp, _dp]
+    L.b200dp_compute_host_nlist.argtypes = [_vp, ctypes.c_int, ctypes.c_int, _dp, _ip, ctypes.POINTER(NList), _dp,
+                                            _dp, _dp, _dp, _dp]
+    L.b200dp_compute_device.argtypes = [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp, _vp, _dp, _dp, _vp, _vp, _vp,
+                                        _vp, _vp]
+    L.b200dp_check.argtypes = [_vp]
+    L.b200dp_sel_overflow_count.argtypes = [_vp]
+    L.b200dp_sel_overflow_count.restype = ctypes.c_longlong
+    L.b200dp_last_nlist.argtypes = [_vp, _ip, _ip, _dp]
+    L.b200dp_last_descriptor.argtypes = [_vp, _dp, _dp]
+    L.b200dp_set_stage_timing.argtypes = [_vp, ctypes.c_int]
+    L.b200dp_stage_times.argtypes = [_vp, ctypes.POINTER(ctypes.c_float)]
+    L.b200dp_kernel_launches.argtypes = []
+    L.b200dp_kernel_launches.restype = ctypes.c_longlong
+    for name in EXPORTS:
+        getattr(L, name)  # every declared symbol must resolve
+    _L = L
+    return L
+
+
+def _p(a, t):
+    return None if a is None else a.ctypes.data_as(t)
+
+
+class DeepPot:
+    """One engine = one model on one device with one precision."""
+
+    def __init__(self, model_path: str, precision: int = MIXED, device: int = 0, sel_overflow_is_error: bool = False):
+        L = load_library()
+        o = Options()
+        L.b200dp_options_default(ctypes.byref(o))
+        o.precision = precision
+        o.device = device
+        o.sel_overflow_is_error = int(sel_overflow_is_error)
+        h = _vp()
+        rc = L.b200dp_create(model_path.encode(), ctypes.byref(o), ctypes.byref(h))
+        if rc != 0:
+            raise B200DPError(rc, f"cannot create engine for {model_path}")
+        self.h = h
+        self.L = L
+        info = ModelInfo()
+        L.b200dp_model_info_get(h, ctypes.byref(info))
+        self.info = info
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.L.b200dp_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _raise(self, rc):
+        if rc != 0:
+            raise B200DPError(rc, self.L.b200dp_last_error(self.h).decode())
+
+    def compute(self, coord, atype, box=None, nghost: int = 0, atomic: bool = False, nlist=None):
+        """Energy, force [nall,3], virial [3,3] (+ atom_energy, atom_virial)."""
+        coord = np.ascontiguousarray(coord, dtype=np.float64).reshape(-1, 3)
+        atype = np.ascontiguousarray(atype, dtype=np.int32)
+        nall = coord.shape[0]
+        nloc = nall - nghost
+        b = None if box is None else np.ascontiguousarray(box, dtype=np.float64).reshape(9)
+        e = np.zeros(1)
+        f = np.zeros((nall, 3))
+        v = np.zeros(9)
+        ae = np.zeros(nloc) if atomic else None
+        av = np.zeros((nall, 9)) if atomic else None
+        if nlist is None:
+            rc = self.L.b200dp_compute_host(self.h, nloc, nghost, _p(coord, _dp), _p(atype, _ip), _p(b, _dp),
+                                            _p(e, _dp), _p(f, _dp), _p(v, _dp), _p(ae, _dp), _p(av, _dp))
+        else:
+            nl, keep = _make_nlist(nlist)
+            rc = self.L.b200dp_compute_host_nlist(self.h, nloc, nghost, _p(coord, _dp), _p(atype, _ip),
+                                                  ctypes.byref(nl), _p(e, _dp), _p(f, _dp), _p(v, _dp),
+                                                  _p(ae, _dp), _p(av, _dp))
+        self._raise(rc)
+        out = dict(energy=float(e[0]), force=f, virial=v.reshape(3, 3))
+        if atomic:
+            out["atom_energy"] = ae
+            out["atom_virial"] = av
+        return out
+
+    def compute_device(self, stream: int, nloc: int, nghost: int, coord_ptr: int, atype_ptr: int, box, region,
+                       energy_ptr: int, force_ptr: int, virial_ptr: int, atom_energy_ptr: int = 0,
+                       atom_virial_ptr: int = 0):
+        b = None if box is None else np.ascontiguousarray(box, dtype=np.float64).reshape(9)
+        r = None if region is None else np.ascontiguousarray(region, dtype=np.float64).reshape(6)
+        rc = self.L.b200dp_compute_device(self.h, stream or None, nloc, nghost, coord_ptr, atype_ptr, _p(b, _dp),
+                                          _p(r, _dp), energy_ptr, force_ptr, virial_ptr, atom_energy_ptr or None,
+                                          atom_virial_ptr or None)
+        self._raise(rc)
+
+    def check(self):
+        self._raise(self.L.b200dp_check(self.h))
+
+    def sel_overflow_count(self) -> int:
+        return int(self.L.b200dp_sel_overflow_count(self.h))
+
+    def last_nlist(self, nloc: int):
+        selt = self.info.sel_total
+        nl = np.empty((nloc, selt), np.int32)
+        code = np.empty((nloc, selt), np.int32)
+        rij = np.empty((nloc, selt, 3))
+        self._raise(self.L.b200dp_last_nlist(self.h, _p(nl, _ip), _p(code, _ip), _p(rij, _dp)))
+        return dict(nlist=nl, code=code, rij=rij)
+
+    def last_descriptor(self, nloc: int):
+        d = np.empty((nloc, self.info.descriptor_dim))
+        dd = np.empty_like(d)
+        self._raise(self.L.b200dp_last_descriptor(self.h, _p(d, _dp), _p(dd, _dp)))
+        return d, dd
+
+    def set_stage_timing(self, on: bool):
+        self._raise(self.L.b200dp_set_stage_timing(self.h, int(on)))
+
+    def stage_times(self):
+        ms = (ctypes.c_float * 5)()
+        self._raise(self.L.b200dp_stage_times(self.h, ms))
+        return list(ms)
+
+
+def kernel_launches() -> int:
+    return int(load_library().b200dp_kernel_launches())
+
+
+def _make_nlist(nlist):
+    """nlist: list of neighbour index arrays, one per local atom (ilist = 0..n-1)."""
+    n = len(nlist)
+    arrs = [np.ascontiguousarray(a, dtype=np.int32) for a in nlist]
+    ilist = np.arange(n, dtype=np.int32)
+    numneigh = np.array([len(a) for a in arrs], dtype=np.int32)
+    firstneigh = (ctypes.POINTER(ctypes.c_int) * max(n, 1))()
+    for k, a in enumerate(arrs):
+        firstneigh[k] = a.ctypes.data_as(ctypes.POINTER(ctypes.c_int))
+    nl = NList(n, ilist.ctypes.data_as(_ip), numneigh.ctypes.data_as(_ip), firstneigh)
+    return nl, (arrs, ilist, numneigh, firstneigh)

@@ -1,0 +1,721 @@
+// Engine: device-resident weights, grow-only scratch, stage sequencing, and
+// the C ABI declared in include/b200dp.h.
+//
+// Stage sequence of one evaluation (all on the caller's stream, no host sync):
+//   bin -> scan -> fill -> format (neighbour graph)  -> reverse index -> type partition
+//   descriptor forward -> fitting forward/backward per centre type
+//   descriptor backward (edge gradients) -> assembly -> deterministic reductions
+// The reference runs the same roles as forward / fitting / node VJP / edge
+// force / widen (components/deepmd-op/overlays/op/pt/dpa4c/graph_compress.cu:1690-1900).
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/b200dp.h"
+#include "engine.hpp"
+#include "model.hpp"
+#include "nlist.cuh"
+#include "sea.cuh"
+
+namespace b200dp {
+
+b200dp_status cuda_fail(cudaError_t e, const char* expr, const char* file, int line);
+
+namespace {
+thread_local std::string* g_err_sink = nullptr;
+std::atomic<long long> g_launches{0};
+}  // namespace
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+long long launch_count() { return g_launches.load(std::memory_order_relaxed); }
+
+b200dp_status cuda_fail(cudaError_t e, const char* expr, const char* file, int line) {
+  if (g_err_sink) {
+    char buf[512];
+    std::snprintf(buf, sizeof(buf), "CUDA error %s (%s) at %s:%d: %s", cudaGetErrorName(e), cudaGetErrorString(e),
+                  file, line, expr);
+    *g_err_sink = buf;
+  }
+  return B200DP_ERR_CUDA;
+}
+
+void DevBuf::release() {
+  if (ptr) cudaFree(ptr);
+  ptr = nullptr;
+  bytes = 0;
+}
+
+cudaError_t DevBuf::ensure(size_t need) {
+  if (need <= bytes) return cudaSuccess;
+  release();
+  const size_t alloc = std::max<size_t>(need + need / 8, 256);
+  cudaError_t e = cudaMalloc(&ptr, alloc);
+  if (e == cudaSuccess) bytes = alloc;
+  return e;
+}
+
+template <typename P>
+static cudaError_t upload(DevBuf& dst, const std::vector<double>& src) {
+  std::vector<P> tmp(src.begin(), src.end());
+  cudaError_t e = dst.ensure(tmp.size() * sizeof(P));
+  if (e != cudaSuccess) return e;
+  return cudaMemcpy(dst.ptr, tmp.data(), tmp.size() * sizeof(P), cudaMemcpyHostToDevice);
+}
+
+b200dp_status Engine::init(const char* path, const b200dp_options* o) {
+  if (o) opt = *o;
+  std::string msg = load_model(path, hm);
+  if (!msg.empty()) {
+    err = msg;
+    return B200DP_ERR_IO;
+  }
+  if (opt.precision != B200DP_FP64 && opt.precision != B200DP_MIXED) {
+    err = "unknown precision";
+    return B200DP_ERR_INVALID;
+  }
+  if (hm.m1() > kSeaThreads) {
+    err = "embedding output width above 128 is not supported";
+    return B200DP_ERR_UNSUPPORTED;
+  }
+  B200DP_CUDA_TRY(cudaSetDevice(opt.device));
+  // shapes
+  SeaDev& s = sd;
+  std::memset(&s, 0, sizeof(s));
+  s.ntypes = hm.ntypes;
+  s.nnets = hm.n_emb_nets();
+  s.type_one_side = hm.type_one_side;
+  s.nl = (int)hm.emb.size();
+  s.ed[0] = 1;
+  s.maxd = 1;
+  for (int l = 0; l < s.nl; ++l) {
+    s.ed[l + 1] = hm.emb[l];
+    s.maxd = std::max(s.maxd, hm.emb[l]);
+  }
+  s.M1 = hm.m1();
+  s.M2 = hm.axis;
+  s.dim = hm.dim();
+  s.selt = hm.sel_total();
+  s.off[0] = 0;
+  for (int t = 0; t < hm.ntypes; ++t) {
+    s.sel[t] = hm.sel[t];
+    s.off[t + 1] = s.off[t] + hm.sel[t];
+  }
+  s.rcut = hm.rcut;
+  s.rcut_smth = hm.rcut_smth;
+  s.inv_nnei = 1.0 / (double)s.selt;
+  int o_ = 0;
+  for (int l = 0; l < s.nl; ++l) {
+    s.w_off[l] = o_;
+    o_ += s.ed[l] * s.ed[l + 1];
+    s.b_off[l] = o_;
+    o_ += s.ed[l + 1];
+  }
+  s.net_stride = o_;
+  // packed embedding weights (W and W^T layouts share offsets)
+  std::vector<double> emb((size_t)s.nnets * s.net_stride), embT(emb.size());
+  for (int n = 0; n < s.nnets; ++n) {
+    double* base = emb.data() + (size_t)n * s.net_stride;
+    double* baseT = embT.data() + (size_t)n * s.net_stride;
+    for (int l = 0; l < s.nl; ++l) {
+      const HostLayer& L = hm.emb_nets[n][l];
+      for (int k = 0; k < L.din; ++k)
+        for (int m = 0; m < L.dout; ++m) {
+          base[s.w_off[l] + k * L.dout + m] = L.w[(size_t)k * L.dout + m];
+          baseT[s.w_off[l] + m * L.din + k] = L.w[(size_t)k * L.dout + m];
+        }
+      for (int m = 0; m < L.dout; ++m) base[s.b_off[l] + m] = baseT[s.b_off[l] + m] = L.b[m];
+    }
+  }
+  const bool fp64 = opt.precision == B200DP_FP64;
+  if (fp64) {
+    B200DP_CUDA_TRY(upload<double>(w_emb, emb));
+    B200DP_CUDA_TRY(upload<double>(w_embT, embT));
+  } else {
+    B200DP_CUDA_TRY(upload<float>(w_emb, emb));
+    B200DP_CUDA_TRY(upload<float>(w_embT, embT));
+  }
+  fit_w.resize(hm.ntypes);
+  fit_b.resize(hm.ntypes);
+  fit_bo.resize(hm.ntypes);
+  for (int t = 0; t < hm.ntypes; ++t) {
+    const auto& net = hm.fit_nets[t];
+    fit_w[t].resize(net.size());
+    fit_b[t].resize(net.size());
+    for (size_t l = 0; l < net.size(); ++l) {
+      if (fp64) {
+        B200DP_CUDA_TRY(upload<double>(fit_w[t][l], net[l].w));
+        B200DP_CUDA_TRY(upload<double>(fit_b[t][l], net[l].b));
+      } else {
+        B200DP_CUDA_TRY(upload<float>(fit_w[t][l], net[l].w));
+        B200DP_CUDA_TRY(upload<float>(fit_b[t][l], net[l].b));
+      }
+    }
+    fit_bo[t] = net.back().b[0] + hm.bias_atom_e[t];
+  }
+  maxfit = 1;
+  for (int v : hm.fit) maxfit = std::max(maxfit, v);
+  cap = std::max(256, ((2 * s.selt + 31) / 32) * 32);
+  B200DP_CUDA_TRY(cudaStreamCreateWithFlags(&own_stream, cudaStreamNonBlocking));
+  for (auto& ev : events) B200DP_CUDA_TRY(cudaEventCreate(&ev));
+  B200DP_CUDA_TRY(err_buf.ensure(sizeof(int) * kErrCount));
+  B200DP_CUDA_TRY(cudaMemset(err_buf.ptr, 0, sizeof(int) * kErrCount));
+  B200DP_CUDA_TRY(reduce_part.ensure(sizeof(double) * kReduceBlocks * 9));
+  B200DP_CUDA_TRY(scalars.ensure(sizeof(double) * 16));
+  ch_fwd = 32;
+  ch_bwd = 32;
+  const size_t budget = 110 * 1024;
+  auto bwd_smem = [&](int ch) {
+    return fp64 ? descriptor_bwd_smem<double>(sd, ch) : descriptor_bwd_smem<float>(sd, ch);
+  };
+  while (ch_bwd > 8 && bwd_smem(ch_bwd) > budget) ch_bwd /= 2;
+  return B200DP_OK;
+}
+
+void Engine::release() {
+  for (DevBuf* b : {&w_emb, &w_embT, &xw, &cell_of, &cell_count, &cell_start, &cell_cursor, &cell_atoms, &nl_j,
+                    &nl_code, &nl_rij, &nl_cnt, &rev_count, &rev_start, &rev_cursor, &rev_tmp, &rev_slot,
+                    &blk_counts, &type_start, &perm_pos, &perm_atom, &Tbuf, &Dbuf, &dDbuf, &atom_e, &gslot,
+                    &vrows, &err_buf, &reduce_part, &scalars, &h_coord, &h_atype, &h_force, &h_aviral, &h_ae,
+                    &cand_start, &cand_list, &ilist_d})
+    b->release();
+  for (auto& v : fit_w)
+    for (auto& b : v) b.release();
+  for (auto& v : fit_b)
+    for (auto& b : v) b.release();
+  for (auto& b : th_l) b.release();
+  for (auto& b : y_l) b.release();
+  for (auto& b : dy_l) b.release();
+  for (auto& b : dz_l) b.release();
+  for (auto& ev : events)
+    if (ev) cudaEventDestroy(ev);
+  if (own_stream) cudaStreamDestroy(own_stream);
+  own_stream = nullptr;
+}
+
+b200dp_status Engine::ensure_buffers(int nloc, int nall, int ncells, int ncand) {
+  const bool fp64 = opt.precision == B200DP_FP64;
+  const size_t ps = fp64 ? sizeof(double) : sizeof(float);
+  const size_t L = (size_t)std::max(nloc, 1), A = (size_t)std::max(nall, 1), C = (size_t)std::max(ncells, 1);
+  const size_t S = L * sd.selt;
+  B200DP_CUDA_TRY(xw.ensure(sizeof(double) * 3 * A));
+  B200DP_CUDA_TRY(cell_of.ensure(sizeof(int) * A));
+  B200DP_CUDA_TRY(cell_count.ensure(sizeof(int) * C));
+  B200DP_CUDA_TRY(cell_start.ensure(sizeof(int) * (C + 1)));
+  B200DP_CUDA_TRY(cell_cursor.ensure(sizeof(int) * C));
+  B200DP_CUDA_TRY(cell_atoms.ensure(sizeof(int) * A));
+  B200DP_CUDA_TRY(nl_j.ensure(sizeof(int) * S));
+  B200DP_CUDA_TRY(nl_code.ensure(sizeof(int) * S));
+  B200DP_CUDA_TRY(nl_rij.ensure(sizeof(double) * 3 * S));
+  B200DP_CUDA_TRY(nl_cnt.ensure(sizeof(int) * L * sd.ntypes));
+  B200DP_CUDA_TRY(rev_count.ensure(sizeof(int) * A));
+  B200DP_CUDA_TRY(rev_start.ensure(sizeof(int) * (A + 1)));
+  B200DP_CUDA_TRY(rev_cursor.ensure(sizeof(int) * A));
+  B200DP_CUDA_TRY(rev_tmp.ensure(sizeof(int) * S));
+  B200DP_CUDA_TRY(rev_slot.ensure(sizeof(int) * S));
+  B200DP_CUDA_TRY(blk_counts.ensure(sizeof(int) * (type_partition_blocks((int)L) + 1) * sd.ntypes));
+  B200DP_CUDA_TRY(type_start.ensure(sizeof(int) * (sd.ntypes + 1)));
+  B200DP_CUDA_TRY(perm_pos.ensure(sizeof(int) * L));
+  B200DP_CUDA_TRY(perm_atom.ensure(sizeof(int) * L));
+  B200DP_CUDA_TRY(Tbuf.ensure(ps * L * 4 * sd.M1));
+  B200DP_CUDA_TRY(Dbuf.ensure(ps * L * sd.dim));
+  B200DP_CUDA_TRY(dDbuf.ensure(ps * L * sd.dim));
+  const int nfl = (int)hm.fit.size();
+  th_l.resize(nfl);
+  y_l.resize(nfl);
+  for (int l = 0; l < nfl; ++l) {
+    B200DP_CUDA_TRY(th_l[l].ensure(ps * L * hm.fit[l]));
+    B200DP_CUDA_TRY(y_l[l].ensure(ps * L * hm.fit[l]));
+  }
+  for (auto& b : dy_l) B200DP_CUDA_TRY(b.ensure(ps * L * maxfit));
+  for (auto& b : dz_l) B200DP_CUDA_TRY(b.ensure(ps * L * maxfit));
+  B200DP_CUDA_TRY(atom_e.ensure(sizeof(double) * L));
+  B200DP_CUDA_TRY(gslot.ensure(sizeof(double) * 3 * S));
+  B200DP_CUDA_TRY(vrows.ensure(sizeof(double) * 9 * A));
+  if (ncand > 0) B200DP_CUDA_TRY(cand_list.ensure(sizeof(int) * (size_t)ncand));
+  return B200DP_OK;
+}
+
+// Grid set-up on the host: cell counts and stencil reach from the box (periodic)
+// or the region (open).  Cells are at least rcut wide in every direction.
+b200dp_status Engine::make_grid(int nall, const double* box, const double* region, bool periodic, GridSpec& g) {
+  std::memset(&g, 0, sizeof(g));
+  const double rc = hm.rcut;
+  const long long max_cells = std::max<long long>(4096, 4LL * nall);
+  g.periodic = periodic ? 1 : 0;
+  if (periodic) {
+    double width[3];
+    for (int k = 0; k < 9; ++k) g.B[k] = box[k];
+    make_box_inverse(box, g.Binv, width);
+    for (int d = 0; d < 3; ++d)
+      if (!(width[d] > 0) || !std::isfinite(width[d])) {
+        err = "degenerate box";
+        return B200DP_ERR_INVALID;
+      }
+    double scale = 1.0;
+    for (;;) {
+      long long tot = 1;
+      for (int d = 0; d < 3; ++d) {
+        g.n[d] = std::max(1, (int)std::floor(width[d] / (rc * scale)));
+        tot *= g.n[d];
+      }
+      if (tot <= max_cells) break;
+      scale *= 1.25;
+    }
+    for (int d = 0; d < 3; ++d) {
+      g.reach[d] = (int)std::ceil(rc * g.n[d] / width[d] * (1.0 + 1e-12));
+      if (2 * g.reach[d] + 1 > 32) {
+        err = "box narrower than rcut/15 along a cell vector";
+        return B200DP_ERR_UNSUPPORTED;
+      }
+    }
+  } else {
+    double scale = 1.0;
+    double ext[3];
+    for (int d = 0; d < 3; ++d) {
+      g.lo[d] = region[d];
+      ext[d] = std::max(region[3 + d] - region[d], 1e-9);
+    }
+    for (;;) {
+      long long tot = 1;
+      for (int d = 0; d < 3; ++d) {
+        g.n[d] = std::max(1, (int)std::floor(ext[d] / (rc * scale)));
+        tot *= g.n[d];
+      }
+      if (tot <= max_cells) break;
+      scale *= 1.25;
+    }
+    for (int d = 0; d < 3; ++d) {
+      g.inv_h[d] = g.n[d] / ext[d];
+      g.reach[d] = 1;
+    }
+  }
+  g.ncells = g.n[0] * g.n[1] * g.n[2];
+  return B200DP_OK;
+}
+
+void Engine::mark(cudaStream_t st, int k) {
+  if (timing) cudaEventRecord(events[k], st);
+}
+
+FormatSpec Engine::format_spec(int nloc, int nall) const {
+  FormatSpec f;
+  std::memset(&f, 0, sizeof(f));
+  f.nloc = nloc;
+  f.nall = nall;
+  f.ntypes = hm.ntypes;
+  f.selt = sd.selt;
+  f.cap = cap;
+  for (int t = 0; t < hm.ntypes; ++t) f.sel[t] = sd.sel[t];
+  for (int t = 0; t <= hm.ntypes; ++t) f.off[t] = sd.off[t];
+  f.rc2 = hm.rcut * hm.rcut;
+  return f;
+}
+
+// Model stages after the neighbour list is formatted.
+template <typename P>
+b200dp_status Engine::run_model(cudaStream_t st, int nloc, int nall, const int* d_atype, double* d_force,
+                                double* d_atom_energy, double* d_atom_virial, double* d_energy, double* d_virial) {
+  int* err_d = static_cast<int*>(err_buf.ptr);
+  launch_reverse_index(st, nloc, nall, sd.selt, nl_j.as<int>(), rev_count.as<int>(), rev_start.as<int>(),
+                       rev_cursor.as<int>(), rev_tmp.as<int>(), rev_slot.as<int>());
+  launch_type_partition(st, nloc, hm.ntypes, d_atype, blk_counts.as<int>(), type_start.as<int>(),
+                        perm_pos.as<int>(), perm_atom.as<int>(), err_d);
+  mark(st, 1);
+  const int gf = descriptor_grid<P>(sd, ch_fwd, false, nloc);
+  launch_descriptor_fwd<P>(st, sd, nloc, ch_fwd, gf, nl_rij.as<double>(), nl_cnt.as<int>(), d_atype,
+                           perm_pos.as<int>(), w_emb.as<P>(), Tbuf.as<P>(), Dbuf.as<P>());
+  mark(st, 2);
+  // fitting, per centre type over its row range [type_start[t], type_start[t+1])
+  const int nfl = (int)hm.fit.size();
+  for (int t = 0; t < hm.ntypes; ++t) {
+    const int* range = type_start.as<int>() + t;
+    const P* x = Dbuf.as<P>();
+    int dx = sd.dim;
+    for (int l = 0; l < nfl; ++l) {
+      const int dout = hm.fit[l];
+      const bool res = (l >= 1 && dout == dx);
+      launch_fit_forward_layer<P>(st, nloc, range, dout, dx, x, dx, fit_w[t][l].as<P>(), fit_b[t][l].as<P>(), res,
+                                  th_l[l].as<P>(), y_l[l].as<P>());
+      x = y_l[l].as<P>();
+      dx = dout;
+    }
+    launch_fit_energy<P>(st, nloc, range, dx, x, fit_w[t][nfl].as<P>(), fit_bo[t], perm_atom.as<int>(),
+                         atom_e.as<double>());
+    // backward: dy_L = w_out, dz_{L-1} = w_out * (1 - th^2)
+    int cur = 0;
+    launch_fit_seed<P>(st, nloc, range, dx, fit_w[t][nfl].as<P>(), th_l[nfl - 1].as<P>(), dy_l[cur].as<P>(),
+                       dz_l[cur].as<P>());
+    for (int l = nfl - 1; l >= 0; --l) {
+      const int din = (l == 0) ? sd.dim : hm.fit[l - 1];
+      const int dout = hm.fit[l];
+      const bool res = (l >= 1 && dout == din);
+      const int nxt = cur ^ 1;
+      if (l == 0) {
+        launch_fit_backward_layer<P>(st, nloc, range, din, dout, dz_l[cur].as<P>(), fit_w[t][l].as<P>(),
+                                     res ? dy_l[cur].as<P>() : nullptr, dDbuf.as<P>(), nullptr, nullptr);
+      } else {
+        launch_fit_backward_layer<P>(st, nloc, range, din, dout, dz_l[cur].as<P>(), fit_w[t][l].as<P>(),
+                                     res ? dy_l[cur].as<P>() : nullptr, dy_l[nxt].as<P>(), th_l[l - 1].as<P>(),
+                                     dz_l[nxt].as<P>());
+      }
+      cur = nxt;
+    }
+  }
+  mark(st, 3);
+  const int gb = descriptor_grid<P>(sd, ch_bwd, true, nloc);
+  launch_descriptor_bwd<P>(st, sd, nloc, ch_bwd, gb, nl_rij.as<double>(), nl_cnt.as<int>(), d_atype,
+                           perm_pos.as<int>(), w_emb.as<P>(), w_embT.as<P>(), Tbuf.as<P>(), dDbuf.as<P>(),
+                           gslot.as<double>());
+  mark(st, 4);
+  launch_assemble(st, nloc, nall, sd.selt, nl_j.as<int>(), gslot.as<double>(), nl_rij.as<double>(),
+                  rev_start.as<int>(), rev_slot.as<int>(), d_force, d_atom_virial, vrows.as<double>());
+  launch_reduce_rows(st, nall, 9, vrows.as<double>(), reduce_part.as<double>(), d_virial);
+  launch_reduce_rows(st, nloc, 1, atom_e.as<double>(), reduce_part.as<double>(), d_energy);
+  if (d_atom_energy)
+    B200DP_CUDA_TRY(cudaMemcpyAsync(d_atom_energy, atom_e.ptr, sizeof(double) * nloc, cudaMemcpyDeviceToDevice, st));
+  mark(st, 5);
+  return B200DP_OK;
+}
+
+b200dp_status Engine::compute_device(cudaStream_t st, int nloc, int nghost, const double* d_coord, const int* d_atype,
+                                     const double* box, const double* region, double* d_energy, double* d_force,
+                                     double* d_virial, double* d_atom_energy, double* d_atom_virial) {
+  g_err_sink = &err;
+  if (nloc < 0 || nghost < 0 || !d_energy || !d_force || !d_virial || (nloc + nghost > 0 && (!d_coord || !d_atype))) {
+    err = "invalid argument";
+    return B200DP_ERR_INVALID;
+  }
+  const int nall = nloc + nghost;
+  const bool periodic = (box != nullptr) && nghost == 0;
+  if (!periodic && !region) {
+    err = "ghost mode needs a region (or use b200dp_compute_host)";
+    return B200DP_ERR_INVALID;
+  }
+  last_stream = st;
+  last_nloc = nloc;
+  last_nall = nall;
+  GridSpec g;
+  b200dp_status rc = make_grid(nall, box, region, periodic, g);
+  if (rc != B200DP_OK) return rc;
+  rc = ensure_buffers(nloc, nall, g.ncells, 0);
+  if (rc != B200DP_OK) return rc;
+  B200DP_CUDA_TRY(cudaSetDevice(opt.device));
+  mark(st, 0);
+  int* err_d = err_buf.as<int>();
+  B200DP_CUDA_TRY(cudaMemsetAsync(err_d, 0, sizeof(int) * kErrCount, st));
+  if (nall == 0) {
+    B200DP_CUDA_TRY(cudaMemsetAsync(d_energy, 0, sizeof(double), st));
+    B200DP_CUDA_TRY(cudaMemsetAsync(d_virial, 0, 9 * sizeof(double), st));
+    return B200DP_OK;
+  }
+  B200DP_CUDA_TRY(cudaMemsetAsync(cell_count.ptr, 0, sizeof(int) * g.ncells, st));
+  B200DP_CUDA_TRY(cudaMemsetAsync(cell_cursor.ptr, 0, sizeof(int) * g.ncells, st));
+  launch_bin(st, nall, d_coord, g, xw.as<double>(), cell_of.as<int>(), cell_count.as<int>());
+  launch_exclusive_scan(st, g.ncells, cell_count.as<int>(), cell_start.as<int>());
+  launch_fill_cells(st, nall, cell_of.as<int>(), cell_start.as<int>(), cell_cursor.as<int>(), cell_atoms.as<int>());
+  launch_format(st, format_spec(nloc, nall), g, xw.as<double>(), d_atype, cell_of.as<int>(), cell_start.as<int>(),
+                cell_atoms.as<int>(), nl_j.as<int>(), nl_code.as<int>(), nl_rij.as<double>(), nl_cnt.as<int>(), err_d);
+  B200DP_CUDA_TRY(cudaGetLastError());
+  rc = (opt.precision == B200DP_FP64)
+           ? run_model<double>(st, nloc, nall, d_atype, d_force, d_atom_energy, d_atom_virial, d_energy, d_virial)
+           : run_model<float>(st, nloc, nall, d_atype, d_force, d_atom_energy, d_atom_virial, d_energy, d_virial);
+  if (rc != B200DP_OK) return rc;
+  B200DP_CUDA_TRY(cudaGetLastError());
+  return B200DP_OK;
+}
+
+b200dp_status Engine::check() {
+  g_err_sink = &err;
+  if (last_stream_valid()) B200DP_CUDA_TRY(cudaStreamSynchronize(last_stream));
+  int h[kErrCount] = {0};
+  B200DP_CUDA_TRY(cudaMemcpy(h, err_buf.ptr, sizeof(h), cudaMemcpyDeviceToHost));
+  last_overflow = h[kErrSelOverflow];
+  if (h[kErrBadType]) {
+    err = "atom type outside [0, ntypes)";
+    return B200DP_ERR_BAD_TYPE;
+  }
+  if (h[kErrCandCapacity]) {
+    err = "a centre had more in-cutoff candidates than the builder buffer";
+    return B200DP_ERR_CAPACITY;
+  }
+  if (h[kErrSelOverflow] && opt.sel_overflow_is_error) {
+    err = "neighbour count exceeded sel";
+    return B200DP_ERR_SEL_OVERFLOW;
+  }
+  return B200DP_OK;
+}
+
+b200dp_status Engine::compute_host(int nloc, int nghost, const double* coord, const int* atype, const double* box,
+                                   const b200dp_nlist* nlist, double* energy, double* force, double* virial,
+                                   double* atom_energy, double* atom_virial) {
+  g_err_sink = &err;
+  if (nloc < 0 || nghost < 0 || !energy || !force || !virial || (nloc + nghost > 0 && (!coord || !atype))) {
+    err = "invalid argument";
+    return B200DP_ERR_INVALID;
+  }
+  const int nall = nloc + nghost;
+  B200DP_CUDA_TRY(cudaSetDevice(opt.device));
+  cudaStream_t st = own_stream;
+  B200DP_CUDA_TRY(h_coord.ensure(sizeof(double) * 3 * std::max(nall, 1)));
+  B200DP_CUDA_TRY(h_atype.ensure(sizeof(int) * std::max(nall, 1)));
+  B200DP_CUDA_TRY(h_force.ensure(sizeof(double) * 3 * std::max(nall, 1)));
+  if (atom_virial) B200DP_CUDA_TRY(h_aviral.ensure(sizeof(double) * 9 * std::max(nall, 1)));
+  if (atom_energy) B200DP_CUDA_TRY(h_ae.ensure(sizeof(double) * std::max(nloc, 1)));
+  if (nall > 0) {
+    B200DP_CUDA_TRY(cudaMemcpyAsync(h_coord.ptr, coord, sizeof(double) * 3 * nall, cudaMemcpyHostToDevice, st));
+    B200DP_CUDA_TRY(cudaMemcpyAsync(h_atype.ptr, atype, sizeof(int) * nall, cudaMemcpyHostToDevice, st));
+  }
+  double* d_scal = scalars.as<double>();
+  b200dp_status rc;
+  if (nlist) {
+    rc = compute_with_nlist(st, nloc, nall, h_coord.as<double>(), h_atype.as<int>(), nlist, d_scal, h_force.as<double>(),
+                            d_scal + 1, atom_energy ? h_ae.as<double>() : nullptr,
+                            atom_virial ? h_aviral.as<double>() : nullptr);
+  } else {
+    double region[6];
+    const double* reg = nullptr;
+    if (!(box && nghost == 0)) {
+      for (int d = 0; d < 3; ++d) {
+        region[d] = 1e300;
+        region[3 + d] = -1e300;
+      }
+      for (int i = 0; i < nall; ++i)
+        for (int d = 0; d < 3; ++d) {
+          region[d] = std::min(region[d], coord[3 * i + d]);
+          region[3 + d] = std::max(region[3 + d], coord[3 * i + d]);
+        }
+      if (nall == 0)
+        for (int d = 0; d < 6; ++d) region[d] = 0;
+      reg = region;
+    }
+    rc = compute_device(st, nloc, nghost, h_coord.as<double>(), h_atype.as<int>(), (box && nghost == 0) ? box : nullptr,
+                        reg, d_scal, h_force.as<double>(), d_scal + 1, atom_energy ? h_ae.as<double>() : nullptr,
+                        atom_virial ? h_aviral.as<double>() : nullptr);
+  }
+  if (rc != B200DP_OK) return rc;
+  double sc[10];
+  B200DP_CUDA_TRY(cudaMemcpyAsync(sc, d_scal, sizeof(double) * 10, cudaMemcpyDeviceToHost, st));
+  if (nall > 0) B200DP_CUDA_TRY(cudaMemcpyAsync(force, h_force.ptr, sizeof(double) * 3 * nall, cudaMemcpyDeviceToHost, st));
+  if (atom_energy && nloc > 0)
+    B200DP_CUDA_TRY(cudaMemcpyAsync(atom_energy, h_ae.ptr, sizeof(double) * nloc, cudaMemcpyDeviceToHost, st));
+  if (atom_virial && nall > 0)
+    B200DP_CUDA_TRY(cudaMemcpyAsync(atom_virial, h_aviral.ptr, sizeof(double) * 9 * nall, cudaMemcpyDeviceToHost, st));
+  B200DP_CUDA_TRY(cudaStreamSynchronize(st));
+  *energy = sc[0];
+  std::memcpy(virial, sc + 1, 9 * sizeof(double));
+  return check();
+}
+
+b200dp_status Engine::compute_with_nlist(cudaStream_t st, int nloc, int nall, const double* d_coord, const int* d_atype,
+                                         const b200dp_nlist* nl, double* d_energy, double* d_force, double* d_virial,
+                                         double* d_atom_energy, double* d_atom_virial) {
+  if (!nl || nl->inum != nloc || (nloc > 0 && (!nl->ilist || !nl->numneigh || !nl->firstneigh))) {
+    err = "neighbour list must cover every local atom (inum == nlocal)";
+    return B200DP_ERR_INVALID;
+  }
+  std::vector<int> start(nloc + 1, 0), il(nl->ilist, nl->ilist + nloc);
+  for (int r = 0; r < nloc; ++r) {
+    if (il[r] < 0 || il[r] >= nloc) {
+      err = "ilist entry outside [0, nlocal)";
+      return B200DP_ERR_INVALID;
+    }
+    start[r + 1] = start[r] + std::max(0, nl->numneigh[r]);
+  }
+  std::vector<int> flat(std::max(start[nloc], 1));
+  for (int r = 0; r < nloc; ++r)
+    for (int k = 0; k < nl->numneigh[r]; ++k) flat[start[r] + k] = nl->firstneigh[r][k];
+  last_stream = st;
+  last_nloc = nloc;
+  last_nall = nall;
+  b200dp_status rc = ensure_buffers(nloc, nall, 1, (int)flat.size());
+  if (rc != B200DP_OK) return rc;
+  B200DP_CUDA_TRY(cand_start.ensure(sizeof(int) * (nloc + 1)));
+  B200DP_CUDA_TRY(ilist_d.ensure(sizeof(int) * std::max(nloc, 1)));
+  B200DP_CUDA_TRY(cudaMemcpyAsync(cand_start.ptr, start.data(), sizeof(int) * (nloc + 1), cudaMemcpyHostToDevice, st));
+  B200DP_CUDA_TRY(cudaMemcpyAsync(ilist_d.ptr, il.data(), sizeof(int) * std::max(nloc, 1), cudaMemcpyHostToDevice, st));
+  B200DP_CUDA_TRY(cudaMemcpyAsync(cand_list.ptr, flat.data(), sizeof(int) * flat.size(), cudaMemcpyHostToDevice, st));
+  mark(st, 0);
+  int* err_d = err_buf.as<int>();
+  B200DP_CUDA_TRY(cudaMemsetAsync(err_d, 0, sizeof(int) * kErrCount, st));
+  if (nall == 0) {
+    B200DP_CUDA_TRY(cudaMemsetAsync(d_energy, 0, sizeof(double), st));
+    B200DP_CUDA_TRY(cudaMemsetAsync(d_virial, 0, 9 * sizeof(double), st));
+    return B200DP_OK;
+  }
+  B200DP_CUDA_TRY(cudaMemcpyAsync(xw.ptr, d_coord, sizeof(double) * 3 * nall, cudaMemcpyDeviceToDevice, st));
+  launch_format_candidates(st, format_spec(nloc, nall), d_coord, d_atype, ilist_d.as<int>(), cand_start.as<int>(),
+                           cand_list.as<int>(), nl_j.as<int>(), nl_code.as<int>(), nl_rij.as<double>(),
+                           nl_cnt.as<int>(), err_d);
+  B200DP_CUDA_TRY(cudaGetLastError());
+  rc = (opt.precision == B200DP_FP64)
+           ? run_model<double>(st, nloc, nall, d_atype, d_force, d_atom_energy, d_atom_virial, d_energy, d_virial)
+           : run_model<float>(st, nloc, nall, d_atype, d_force, d_atom_energy, d_atom_virial, d_energy, d_virial);
+  if (rc != B200DP_OK) return rc;
+  B200DP_CUDA_TRY(cudaGetLastError());
+  return B200DP_OK;
+}
+
+}  // namespace b200dp
+
+// ============================================================== C ABI
+using b200dp::Engine;
+
+struct b200dp_engine {
+  Engine e;
+};
+
+extern "C" {
+
+void b200dp_options_default(b200dp_options* opt) {
+  if (!opt) return;
+  std::memset(opt, 0, sizeof(*opt));
+  opt->precision = B200DP_MIXED;
+  opt->device = 0;
+  opt->sel_overflow_is_error = 0;
+}
+
+b200dp_status b200dp_create(const char* model_path, const b200dp_options* opt, b200dp_engine** out) {
+  if (!model_path || !out) return B200DP_ERR_INVALID;
+  *out = nullptr;
+  auto* h = new (std::nothrow) b200dp_engine;
+  if (!h) return B200DP_ERR_INVALID;
+  b200dp_options o;
+  b200dp_options_default(&o);
+  if (opt) o = *opt;
+  b200dp::g_err_sink = &h->e.err;
+  b200dp_status rc = h->e.init(model_path, &o);
+  if (rc != B200DP_OK) {
+    // keep the engine so the caller can read the message, then report
+    static thread_local std::string last;
+    last = h->e.err;
+    h->e.release();
+    delete h;
+    std::fprintf(stderr, "b200dp_create: %s\n", last.c_str());
+    return rc;
+  }
+  *out = h;
+  return B200DP_OK;
+}
+
+void b200dp_destroy(b200dp_engine* engine) {
+  if (!engine) return;
+  engine->e.release();
+  delete engine;
+}
+
+const char* b200dp_last_error(const b200dp_engine* engine) { return engine ? engine->e.err.c_str() : "null engine"; }
+
+b200dp_status b200dp_model_info_get(const b200dp_engine* engine, b200dp_model_info* out) {
+  if (!engine || !out) return B200DP_ERR_INVALID;
+  const auto& m = engine->e.hm;
+  out->ntypes = m.ntypes;
+  out->sel_total = m.sel_total();
+  out->descriptor_dim = m.dim();
+  out->embedding_out = m.m1();
+  out->axis = m.axis;
+  out->n_embedding_layers = (int)m.emb.size();
+  out->n_fitting_layers = (int)m.fit.size();
+  out->type_one_side = m.type_one_side;
+  out->rcut = m.rcut;
+  out->rcut_smth = m.rcut_smth;
+  return B200DP_OK;
+}
+
+b200dp_status b200dp_compute_host(b200dp_engine* engine, int nlocal, int nghost, const double* coord, const int* atype,
+                                  const double* box, double* energy, double* force, double* virial,
+                                  double* atom_energy, double* atom_virial) {
+  if (!engine) return B200DP_ERR_INVALID;
+  return engine->e.compute_host(nlocal, nghost, coord, atype, box, nullptr, energy, force, virial, atom_energy,
+                                atom_virial);
+}
+
+b200dp_status b200dp_compute_host_nlist(b200dp_engine* engine, int nlocal, int nghost, const double* coord,
+                                        const int* atype, const b200dp_nlist* nlist, double* energy, double* force,
+                                        double* virial, double* atom_energy, double* atom_virial) {
+  if (!engine || !nlist) return B200DP_ERR_INVALID;
+  return engine->e.compute_host(nlocal, nghost, coord, atype, nullptr, nlist, energy, force, virial, atom_energy,
+                                atom_virial);
+}
+
+b200dp_status b200dp_compute_device(b200dp_engine* engine, void* stream, int nlocal, int nghost, const double* d_coord,
+                                    const int* d_atype, const double* box, const double* region, double* d_energy,
+                                    double* d_force, double* d_virial, double* d_atom_energy, double* d_atom_virial) {
+  if (!engine) return B200DP_ERR_INVALID;
+  return engine->e.compute_device(static_cast<cudaStream_t>(stream), nlocal, nghost, d_coord, d_atype, box, region,
+                                  d_energy, d_force, d_virial, d_atom_energy, d_atom_virial);
+}
+
+b200dp_status b200dp_check(b200dp_engine* engine) {
+  if (!engine) return B200DP_ERR_INVALID;
+  return engine->e.check();
+}
+
+long long b200dp_sel_overflow_count(b200dp_engine* engine) {
+  if (!engine) return -1;
+  engine->e.check();
+  return engine->e.last_overflow;
+}
+
+b200dp_status b200dp_last_nlist(b200dp_engine* engine, int* nlist, int* image, double* rij) {
+  if (!engine) return B200DP_ERR_INVALID;
+  Engine& e = engine->e;
+  b200dp::g_err_sink = &e.err;
+  B200DP_CUDA_TRY(cudaDeviceSynchronize());
+  const size_t S = (size_t)e.last_nloc * e.sd.selt;
+  if (nlist && S) B200DP_CUDA_TRY(cudaMemcpy(nlist, e.nl_j.ptr, sizeof(int) * S, cudaMemcpyDeviceToHost));
+  if (image && S) B200DP_CUDA_TRY(cudaMemcpy(image, e.nl_code.ptr, sizeof(int) * S, cudaMemcpyDeviceToHost));
+  if (rij && S) B200DP_CUDA_TRY(cudaMemcpy(rij, e.nl_rij.ptr, sizeof(double) * 3 * S, cudaMemcpyDeviceToHost));
+  return B200DP_OK;
+}
+
+b200dp_status b200dp_last_descriptor(b200dp_engine* engine, double* descriptor, double* grad_descriptor) {
+  if (!engine) return B200DP_ERR_INVALID;
+  Engine& e = engine->e;
+  b200dp::g_err_sink = &e.err;
+  B200DP_CUDA_TRY(cudaDeviceSynchronize());
+  const int n = e.last_nloc, dim = e.sd.dim;
+  if (n <= 0) return B200DP_OK;
+  std::vector<int> perm(n);
+  B200DP_CUDA_TRY(cudaMemcpy(perm.data(), e.perm_pos.ptr, sizeof(int) * n, cudaMemcpyDeviceToHost));
+  const bool fp64 = e.opt.precision == B200DP_FP64;
+  for (int which = 0; which < 2; ++which) {
+    double* out = which ? grad_descriptor : descriptor;
+    if (!out) continue;
+    const void* src = which ? e.dDbuf.ptr : e.Dbuf.ptr;
+    std::vector<double> tmp((size_t)n * dim);
+    if (fp64) {
+      B200DP_CUDA_TRY(cudaMemcpy(tmp.data(), src, sizeof(double) * tmp.size(), cudaMemcpyDeviceToHost));
+    } else {
+      std::vector<float> f(tmp.size());
+      B200DP_CUDA_TRY(cudaMemcpy(f.data(), src, sizeof(float) * f.size(), cudaMemcpyDeviceToHost));
+      std::copy(f.begin(), f.end(), tmp.begin());
+    }
+    for (int i = 0; i < n; ++i) std::memcpy(out + (size_t)i * dim, tmp.data() + (size_t)perm[i] * dim, sizeof(double) * dim);
+  }
+  return B200DP_OK;
+}
+
+long long b200dp_kernel_launches(void) { return b200dp::launch_count(); }
+
+b200dp_status b200dp_set_stage_timing(b200dp_engine* engine, int enable) {
+  if (!engine) return B200DP_ERR_INVALID;
+  engine->e.timing = enable != 0;
+  return B200DP_OK;
+}
+
+b200dp_status b200dp_stage_times(b200dp_engine* engine, float* ms5) {
+  if (!engine || !ms5) return B200DP_ERR_INVALID;
+  Engine& e = engine->e;
+  b200dp::g_err_sink = &e.err;
+  if (!e.timing) return B200DP_ERR_INVALID;
+  B200DP_CUDA_TRY(cudaEventSynchronize(e.events[5]));
+  for (int k = 0; k < 5; ++k) B200DP_CUDA_TRY(cudaEventElapsedTime(ms5 + k, e.events[k], e.events[k + 1]));
+  return B200DP_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,91 @@
+// Engine state behind the C ABI (include/b200dp.h).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <array>
+#include <string>
+#include <vector>
+
+#include "../../include/b200dp.h"
+#include "model.hpp"
+#include "nlist.cuh"
+#include "sea.cuh"
+
+namespace b200dp {
+
+b200dp_status cuda_fail(cudaError_t e, const char* expr, const char* file, int line);
+
+// Grow-only device allocation.  Buffers are only (re)allocated outside the
+// hot loop, so a call that fits the current capacity allocates nothing.
+struct DevBuf {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+  cudaError_t ensure(size_t need);
+  void release();
+  template <typename T>
+  T* as() const {
+    return static_cast<T*>(ptr);
+  }
+};
+
+struct Engine {
+  HostModel hm;
+  b200dp_options opt{};
+  SeaDev sd{};
+  std::string err;
+  int cap = 256;  // per-centre in-cutoff candidate buffer
+  int maxfit = 1;
+  int ch_fwd = 32, ch_bwd = 32;
+
+  // weights
+  DevBuf w_emb, w_embT;
+  std::vector<std::vector<DevBuf>> fit_w, fit_b;  // [type][layer], last layer = output
+  std::vector<double> fit_bo;                     // output bias + bias_atom_e per type
+
+  // neighbour graph
+  DevBuf xw, cell_of, cell_count, cell_start, cell_cursor, cell_atoms;
+  DevBuf nl_j, nl_code, nl_rij, nl_cnt;
+  DevBuf rev_count, rev_start, rev_cursor, rev_tmp, rev_slot;
+  DevBuf blk_counts, type_start, perm_pos, perm_atom;
+  DevBuf cand_start, cand_list, ilist_d;
+  // model activations
+  DevBuf Tbuf, Dbuf, dDbuf;
+  std::vector<DevBuf> th_l, y_l;
+  std::array<DevBuf, 2> dy_l, dz_l;
+  DevBuf atom_e, gslot, vrows, reduce_part, scalars, err_buf;
+  // host-call staging
+  DevBuf h_coord, h_atype, h_force, h_aviral, h_ae;
+
+  cudaStream_t own_stream = nullptr;
+  cudaStream_t last_stream = nullptr;
+  bool last_stream_set = false;
+  int last_nloc = 0, last_nall = 0;
+  long long last_overflow = 0;
+  bool timing = false;
+  std::array<cudaEvent_t, 6> events{};
+
+  b200dp_status init(const char* path, const b200dp_options* o);
+  void release();
+  b200dp_status ensure_buffers(int nloc, int nall, int ncells, int ncand);
+  b200dp_status make_grid(int nall, const double* box, const double* region, bool periodic, GridSpec& g);
+  FormatSpec format_spec(int nloc, int nall) const;
+  void mark(cudaStream_t st, int k);
+  bool last_stream_valid() const { return true; }
+
+  template <typename P>
+  b200dp_status run_model(cudaStream_t st, int nloc, int nall, const int* d_atype, double* d_force,
+                          double* d_atom_energy, double* d_atom_virial, double* d_energy, double* d_virial);
+  b200dp_status compute_device(cudaStream_t st, int nloc, int nghost, const double* d_coord, const int* d_atype,
+                               const double* box, const double* region, double* d_energy, double* d_force,
+                               double* d_virial, double* d_atom_energy, double* d_atom_virial);
+  b200dp_status compute_with_nlist(cudaStream_t st, int nloc, int nall, const double* d_coord, const int* d_atype,
+                                   const b200dp_nlist* nl, double* d_energy, double* d_force, double* d_virial,
+                                   double* d_atom_energy, double* d_atom_virial);
+  b200dp_status compute_host(int nloc, int nghost, const double* coord, const int* atype, const double* box,
+                             const b200dp_nlist* nlist, double* energy, double* force, double* virial,
+                             double* atom_energy, double* atom_virial);
+  b200dp_status check();
+};
+
+}  // namespace b200dp

@@ -1,0 +1,577 @@
+// Neighbour-graph builder kernels (see nlist.cuh).
+#include <cmath>
+
+#include "nlist.cuh"
+
+namespace b200dp {
+
+// ---------------------------------------------------------------- host helpers
+void make_box_inverse(const double* box, double* Binv, double* width) {
+  // Same operation order as the oracle's make_cell (host code is compiled
+  // with -ffp-contract=off), so wrapped coordinates agree bit for bit.
+  double B[3][3];
+  for (int a = 0; a < 3; ++a)
+    for (int b = 0; b < 3; ++b) B[a][b] = box[3 * a + b];
+  double c00 = B[1][1] * B[2][2] - B[1][2] * B[2][1];
+  double c01 = B[1][2] * B[2][0] - B[1][0] * B[2][2];
+  double c02 = B[1][0] * B[2][1] - B[1][1] * B[2][0];
+  double det = (B[0][0] * c00 + B[0][1] * c01) + B[0][2] * c02;
+  double id = 1.0 / det;
+  double I[3][3];
+  I[0][0] = c00 * id;
+  I[1][0] = c01 * id;
+  I[2][0] = c02 * id;
+  I[0][1] = (B[0][2] * B[2][1] - B[0][1] * B[2][2]) * id;
+  I[1][1] = (B[0][0] * B[2][2] - B[0][2] * B[2][0]) * id;
+  I[2][1] = (B[0][1] * B[2][0] - B[0][0] * B[2][1]) * id;
+  I[0][2] = (B[0][1] * B[1][2] - B[0][2] * B[1][1]) * id;
+  I[1][2] = (B[0][2] * B[1][0] - B[0][0] * B[1][2]) * id;
+  I[2][2] = (B[0][0] * B[1][1] - B[0][1] * B[1][0]) * id;
+  for (int a = 0; a < 3; ++a)
+    for (int b = 0; b < 3; ++b) Binv[3 * a + b] = I[a][b];
+  double vol = std::fabs(det);
+  for (int d = 0; d < 3; ++d) {
+    const double* u = B[(d + 1) % 3];
+    const double* v = B[(d + 2) % 3];
+    double x = u[1] * v[2] - u[2] * v[1], y = u[2] * v[0] - u[0] * v[2], z = u[0] * v[1] - u[1] * v[0];
+    width[d] = vol / std::sqrt(x * x + y * y + z * z);
+  }
+}
+
+// ---------------------------------------------------------------- binning
+__global__ void k_bin(int nall, const double* __restrict__ coord, GridSpec g, double* __restrict__ xw,
+                      int* __restrict__ cell_of, int* __restrict__ cell_count) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= nall) return;
+  const double x[3] = {coord[3 * i], coord[3 * i + 1], coord[3 * i + 2]};
+  double w[3];
+  int c[3];
+  if (g.periodic) {
+    double f[3];
+#pragma unroll
+    for (int d = 0; d < 3; ++d) {
+      const double s = dadd(dadd(dmul(x[0], g.Binv[d]), dmul(x[1], g.Binv[3 + d])), dmul(x[2], g.Binv[6 + d]));
+      f[d] = floor(s);
+    }
+#pragma unroll
+    for (int k = 0; k < 3; ++k)
+      w[k] = dsub(x[k], dadd(dadd(dmul(f[0], g.B[k]), dmul(f[1], g.B[3 + k])), dmul(f[2], g.B[6 + k])));
+#pragma unroll
+    for (int d = 0; d < 3; ++d) {
+      const double s = (w[0] * g.Binv[d] + w[1] * g.Binv[3 + d]) + w[2] * g.Binv[6 + d];
+      double v = floor(s * g.n[d]);
+      v = fmin(fmax(v, 0.0), (double)(g.n[d] - 1));
+      c[d] = (int)v;
+    }
+  } else {
+#pragma unroll
+    for (int d = 0; d < 3; ++d) {
+      w[d] = x[d];
+      double v = floor((x[d] - g.lo[d]) * g.inv_h[d]);
+      v = fmin(fmax(v, 0.0), (double)(g.n[d] - 1));
+      c[d] = (int)v;
+    }
+  }
+  xw[3 * i] = w[0];
+  xw[3 * i + 1] = w[1];
+  xw[3 * i + 2] = w[2];
+  const int cell = (c[0] * g.n[1] + c[1]) * g.n[2] + c[2];
+  cell_of[i] = cell;
+  atomicAdd(cell_count + cell, 1);
+}
+
+void launch_bin(cudaStream_t st, int nall, const double* coord, const GridSpec& g, double* xw, int* cell_of,
+                int* cell_count) {
+  if (nall <= 0) return;
+  count_launch();
+  k_bin<<<(nall + 255) / 256, 256, 0, st>>>(nall, coord, g, xw, cell_of, cell_count);
+}
+
+// Single-block exclusive scan; out has n+1 entries (out[n] = total).
+__global__ void __launch_bounds__(1024) k_exclusive_scan(int n, const int* __restrict__ in, int* __restrict__ out) {
+  __shared__ int warp_ex[32];
+  __shared__ int block_total;
+  __shared__ int carry;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) carry = 0;
+  __syncthreads();
+  constexpr int kPer = 4;
+  for (int base = 0; base < n; base += 1024 * kPer) {
+    int v[kPer];
+    int local = 0;
+    const int i0 = base + tid * kPer;
+#pragma unroll
+    for (int q = 0; q < kPer; ++q) {
+      v[q] = (i0 + q < n) ? in[i0 + q] : 0;
+      local += v[q];
+    }
+    int wt;
+    const int ex = warp_exclusive_scan(local, lane, wt);
+    if (lane == 0) warp_ex[warp] = wt;
+    __syncthreads();
+    if (warp == 0) {
+      const int mine = warp_ex[lane];
+      int tot;
+      const int e = warp_exclusive_scan(mine, lane, tot);
+      warp_ex[lane] = e;
+      if (lane == 0) block_total = tot;
+    }
+    __syncthreads();
+    int run = carry + warp_ex[warp] + ex;
+#pragma unroll
+    for (int q = 0; q < kPer; ++q) {
+      if (i0 + q < n) out[i0 + q] = run;
+      run += v[q];
+    }
+    __syncthreads();
+    if (tid == 0) carry += block_total;
+    __syncthreads();
+  }
+  if (tid == 0) out[n] = carry;
+}
+
+void launch_exclusive_scan(cudaStream_t st, int n, const int* in, int* out) {
+  count_launch();
+  k_exclusive_scan<<<1, 1024, 0, st>>>(n, in, out);
+}
+
+__global__ void k_fill_cells(int nall, const int* __restrict__ cell_of, const int* __restrict__ cell_start,
+                             int* __restrict__ cursor, int* __restrict__ cell_atoms) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= nall) return;
+  const int c = cell_of[i];
+  cell_atoms[cell_start[c] + atomicAdd(cursor + c, 1)] = i;
+}
+
+void launch_fill_cells(cudaStream_t st, int nall, const int* cell_of, const int* cell_start, int* cursor,
+                       int* cell_atoms) {
+  if (nall <= 0) return;
+  count_launch();
+  k_fill_cells<<<(nall + 255) / 256, 256, 0, st>>>(nall, cell_of, cell_start, cursor, cell_atoms);
+}
+
+// ---------------------------------------------------------------- format
+constexpr int kFmtWarps = 4;
+
+__device__ __forceinline__ int floor_div(int a, int n) { return a >= 0 ? a / n : -((-a + n - 1) / n); }
+
+size_t format_smem_bytes(int cap) {
+  // per warp: r2 (8) + r (24) + j, code, type (12) bytes per candidate
+  return (size_t)kFmtWarps * cap * 44;
+}
+
+struct CandBuf {
+  double* r2;
+  double* r;  // [cap][3]
+  int* j;
+  int* code;
+  int* t;
+};
+
+__device__ __forceinline__ CandBuf cand_buf(unsigned char* smem, int warp, int cap) {
+  unsigned char* base = smem + (size_t)warp * cap * 44;
+  CandBuf b;
+  b.r2 = reinterpret_cast<double*>(base);
+  b.r = b.r2 + cap;
+  b.j = reinterpret_cast<int*>(b.r + 3 * cap);
+  b.code = b.j + cap;
+  b.t = b.code + cap;
+  return b;
+}
+
+// Rank sort of one centre's candidates and the row write.  Keys are unique
+// (j, image) pairs, so the order (type, r^2, j, image) is total and the output
+// does not depend on the order candidates were found in.
+__device__ void emit_row(const FormatSpec& f, int i, const CandBuf& b, int ncand, int lane, int* __restrict__ nl_j,
+                         int* __restrict__ nl_code, double* __restrict__ nl_rij, int* __restrict__ nl_cnt,
+                         int* __restrict__ err) {
+  for (int c = lane; c < ncand; c += 32) {
+    const int t = b.t[c];
+    const double r2 = b.r2[c];
+    const int j = b.j[c], code = b.code[c];
+    int rank = 0;
+    for (int c2 = 0; c2 < ncand; ++c2) {
+      if (b.t[c2] != t) continue;
+      const double q = b.r2[c2];
+      const int j2 = b.j[c2];
+      rank += (q < r2) || (q == r2 && (j2 < j || (j2 == j && b.code[c2] < code)));
+    }
+    if (rank < f.sel[t]) {
+      const size_t slot = (size_t)i * f.selt + f.off[t] + rank;
+      nl_j[slot] = j;
+      nl_code[slot] = code;
+      nl_rij[3 * slot] = b.r[3 * c];
+      nl_rij[3 * slot + 1] = b.r[3 * c + 1];
+      nl_rij[3 * slot + 2] = b.r[3 * c + 2];
+    }
+  }
+  for (int t = 0; t < f.ntypes; ++t) {
+    int local = 0;
+    for (int c = lane; c < ncand; c += 32) local += (b.t[c] == t);
+    const int nt = warp_sum(local);
+    const int keep = nt < f.sel[t] ? nt : f.sel[t];
+    if (lane == 0) {
+      nl_cnt[(size_t)i * f.ntypes + t] = keep;
+      if (nt > f.sel[t]) atomicAdd(err + kErrSelOverflow, nt - f.sel[t]);
+    }
+    const int zero_code = image_code(0, 0, 0);
+    for (int s = keep + lane; s < f.sel[t]; s += 32) {
+      const size_t slot = (size_t)i * f.selt + f.off[t] + s;
+      nl_j[slot] = -1;
+      nl_code[slot] = zero_code;
+      nl_rij[3 * slot] = 0.0;
+      nl_rij[3 * slot + 1] = 0.0;
+      nl_rij[3 * slot + 2] = 0.0;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kFmtWarps * 32)
+    k_format(FormatSpec f, GridSpec g, const double* __restrict__ xw, const int* __restrict__ atype,
+             const int* __restrict__ cell_of, const int* __restrict__ cell_start, const int* __restrict__ cell_atoms,
+             int* __restrict__ nl_j, int* __restrict__ nl_code, double* __restrict__ nl_rij, int* __restrict__ nl_cnt,
+             int* __restrict__ err) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ int rng_start[kFmtWarps][32], rng_pref[kFmtWarps][33], rng_img[kFmtWarps][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int i = blockIdx.x * kFmtWarps + warp;
+  if (i >= f.nloc) return;  // warp-uniform; no block-level barrier follows
+  CandBuf b = cand_buf(smem, warp, f.cap);
+  const double xi[3] = {xw[3 * i], xw[3 * i + 1], xw[3 * i + 2]};
+  const int cell = cell_of[i];
+  const int ci[3] = {cell / (g.n[1] * g.n[2]), (cell / g.n[2]) % g.n[1], cell % g.n[2]};
+  const int nz = 2 * g.reach[2] + 1;
+  const unsigned lt_mask = (1u << lane) - 1u;
+  int ncand = 0;
+  for (int d0 = -g.reach[0]; d0 <= g.reach[0]; ++d0) {
+    int u0 = ci[0] + d0, img0 = 0;
+    if (g.periodic) {
+      img0 = floor_div(u0, g.n[0]);
+      u0 -= img0 * g.n[0];
+    } else if (u0 < 0 || u0 >= g.n[0]) {
+      continue;
+    }
+    for (int d1 = -g.reach[1]; d1 <= g.reach[1]; ++d1) {
+      int u1 = ci[1] + d1, img1 = 0;
+      if (g.periodic) {
+        img1 = floor_div(u1, g.n[1]);
+        u1 -= img1 * g.n[1];
+      } else if (u1 < 0 || u1 >= g.n[1]) {
+        continue;
+      }
+      int cnt = 0, start = 0, img2 = 0;
+      if (lane < nz) {
+        int u2 = ci[2] + lane - g.reach[2];
+        bool ok = true;
+        if (g.periodic) {
+          img2 = floor_div(u2, g.n[2]);
+          u2 -= img2 * g.n[2];
+        } else {
+          ok = (u2 >= 0 && u2 < g.n[2]);
+        }
+        if (ok) {
+          const int cc = (u0 * g.n[1] + u1) * g.n[2] + u2;
+          start = cell_start[cc];
+          cnt = cell_start[cc + 1] - start;
+        }
+      }
+      int total;
+      const int pref = warp_exclusive_scan(cnt, lane, total);
+      rng_start[warp][lane] = start;
+      rng_pref[warp][lane] = pref;
+      rng_img[warp][lane] = img2;
+      __syncwarp();
+      double shx = 0, shy = 0, shz = 0;  // shift of (img0, img1, 0)
+      if (g.periodic) {
+        shx = dadd(dmul((double)img0, g.B[0]), dmul((double)img1, g.B[3]));
+        shy = dadd(dmul((double)img0, g.B[1]), dmul((double)img1, g.B[4]));
+        shz = dadd(dmul((double)img0, g.B[2]), dmul((double)img1, g.B[5]));
+      }
+      for (int k = lane; k - lane < total; k += 32) {
+        bool valid = false;
+        int j = -1, code = 0, tj = 0;
+        double r[3] = {0, 0, 0}, r2 = 0;
+        if (k < total) {
+          int q = 0;
+          while (q + 1 < nz && rng_pref[warp][q + 1] <= k) ++q;
+          j = cell_atoms[rng_start[warp][q] + (k - rng_pref[warp][q])];
+          const int im2 = rng_img[warp][q];
+          double s[3] = {0, 0, 0};
+          if (g.periodic) {
+            const double m2 = (double)im2;
+            s[0] = dadd(shx, dmul(m2, g.B[6]));
+            s[1] = dadd(shy, dmul(m2, g.B[7]));
+            s[2] = dadd(shz, dmul(m2, g.B[8]));
+          }
+#pragma unroll
+          for (int c = 0; c < 3; ++c) r[c] = dsub(dadd(xw[3 * j + c], s[c]), xi[c]);
+          r2 = dadd(dadd(dmul(r[0], r[0]), dmul(r[1], r[1])), dmul(r[2], r[2]));
+          const bool self = (j == i) && img0 == 0 && img1 == 0 && im2 == 0;
+          tj = atype[j];
+          const bool type_ok = (tj >= 0 && tj < f.ntypes);
+          if (!type_ok && !self && r2 < f.rc2) atomicAdd(err + kErrBadType, 1);
+          valid = !self && type_ok && (r2 < f.rc2);
+          code = image_code(img0, img1, im2);
+        }
+        const unsigned m = __ballot_sync(0xffffffffu, valid);
+        const int pos = ncand + __popc(m & lt_mask);
+        if (valid && pos < f.cap) {
+          b.r2[pos] = r2;
+          b.r[3 * pos] = r[0];
+          b.r[3 * pos + 1] = r[1];
+          b.r[3 * pos + 2] = r[2];
+          b.j[pos] = j;
+          b.code[pos] = code;
+          b.t[pos] = tj;
+        }
+        ncand += __popc(m);
+      }
+      __syncwarp();
+    }
+  }
+  if (ncand > f.cap) {
+    if (lane == 0) atomicAdd(err + kErrCandCapacity, 1);
+    ncand = f.cap;
+  }
+  __syncwarp();
+  emit_row(f, i, b, ncand, lane, nl_j, nl_code, nl_rij, nl_cnt, err);
+}
+
+void launch_format(cudaStream_t st, const FormatSpec& f, const GridSpec& g, const double* xw, const int* atype,
+                   const int* cell_of, const int* cell_start, const int* cell_atoms, int* nl_j, int* nl_code,
+                   double* nl_rij, int* nl_cnt, int* err) {
+  if (f.nloc <= 0) return;
+  const size_t smem = format_smem_bytes(f.cap);
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(k_format, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    attr_set = true;
+  }
+  count_launch();
+  k_format<<<(f.nloc + kFmtWarps - 1) / kFmtWarps, kFmtWarps * 32, smem, st>>>(
+      f, g, xw, atype, cell_of, cell_start, cell_atoms, nl_j, nl_code, nl_rij, nl_cnt, err);
+}
+
+// Caller-provided candidates (LAMMPS full list): cand_start is a CSR over
+// ilist order.  No periodic images: r = x_j - x_i on raw coordinates.
+__global__ void __launch_bounds__(kFmtWarps * 32)
+    k_format_candidates(FormatSpec f, const double* __restrict__ coord, const int* __restrict__ atype,
+                        const int* __restrict__ ilist, const int* __restrict__ cand_start,
+                        const int* __restrict__ cand, int* __restrict__ nl_j, int* __restrict__ nl_code,
+                        double* __restrict__ nl_rij, int* __restrict__ nl_cnt, int* __restrict__ err) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kFmtWarps + warp;
+  if (row >= f.nloc) return;
+  const int i = ilist[row];
+  if (i < 0 || i >= f.nloc) return;
+  CandBuf b = cand_buf(smem, warp, f.cap);
+  const double xi[3] = {coord[3 * i], coord[3 * i + 1], coord[3 * i + 2]};
+  const unsigned lt_mask = (1u << lane) - 1u;
+  const int beg = cand_start[row], end = cand_start[row + 1];
+  int ncand = 0;
+  for (int k = beg + lane; k - lane < end; k += 32) {
+    bool valid = false;
+    int j = -1, tj = 0;
+    double r[3] = {0, 0, 0}, r2 = 0;
+    if (k < end) {
+      j = cand[k];
+      if (j >= 0 && j < f.nall && j != i) {
+#pragma unroll
+        for (int c = 0; c < 3; ++c) r[c] = dsub(coord[3 * j + c], xi[c]);
+        r2 = dadd(dadd(dmul(r[0], r[0]), dmul(r[1], r[1])), dmul(r[2], r[2]));
+        tj = atype[j];
+        const bool type_ok = (tj >= 0 && tj < f.ntypes);
+        if (!type_ok && r2 < f.rc2) atomicAdd(err + kErrBadType, 1);
+        valid = type_ok && r2 < f.rc2;
+      }
+    }
+    const unsigned m = __ballot_sync(0xffffffffu, valid);
+    const int pos = ncand + __popc(m & lt_mask);
+    if (valid && pos < f.cap) {
+      b.r2[pos] = r2;
+      b.r[3 * pos] = r[0];
+      b.r[3 * pos + 1] = r[1];
+      b.r[3 * pos + 2] = r[2];
+      b.j[pos] = j;
+      b.code[pos] = image_code(0, 0, 0);
+      b.t[pos] = tj;
+    }
+    ncand += __popc(m);
+  }
+  if (ncand > f.cap) {
+    if (lane == 0) atomicAdd(err + kErrCandCapacity, 1);
+    ncand = f.cap;
+  }
+  __syncwarp();
+  emit_row(f, i, b, ncand, lane, nl_j, nl_code, nl_rij, nl_cnt, err);
+}
+
+void launch_format_candidates(cudaStream_t st, const FormatSpec& f, const double* coord, const int* atype,
+                              const int* ilist, const int* cand_start, const int* cand, int* nl_j, int* nl_code,
+                              double* nl_rij, int* nl_cnt, int* err) {
+  if (f.nloc <= 0) return;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(k_format_candidates, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    attr_set = true;
+  }
+  count_launch();
+  k_format_candidates<<<(f.nloc + kFmtWarps - 1) / kFmtWarps, kFmtWarps * 32, format_smem_bytes(f.cap), st>>>(
+      f, coord, atype, ilist, cand_start, cand, nl_j, nl_code, nl_rij, nl_cnt, err);
+}
+
+// ---------------------------------------------------------------- reverse index
+__global__ void k_rev_count(long long nslots, const int* __restrict__ nl_j, int* __restrict__ rev_count) {
+  for (long long s = blockIdx.x * (long long)blockDim.x + threadIdx.x; s < nslots;
+       s += (long long)gridDim.x * blockDim.x) {
+    const int j = nl_j[s];
+    if (j >= 0) atomicAdd(rev_count + j, 1);
+  }
+}
+
+__global__ void k_rev_fill(long long nslots, const int* __restrict__ nl_j, const int* __restrict__ rev_start,
+                           int* __restrict__ cursor, int* __restrict__ rev_tmp) {
+  for (long long s = blockIdx.x * (long long)blockDim.x + threadIdx.x; s < nslots;
+       s += (long long)gridDim.x * blockDim.x) {
+    const int j = nl_j[s];
+    if (j >= 0) rev_tmp[rev_start[j] + atomicAdd(cursor + j, 1)] = (int)s;
+  }
+}
+
+// One warp per owner: rank-sort the owner's slot ids so the force gather
+// sums them in a fixed order (deterministic, atomic-free assembly).
+constexpr int kRevWarps = 8;
+constexpr int kRevStage = 256;
+__global__ void __launch_bounds__(kRevWarps * 32)
+    k_rev_sort(int nall, const int* __restrict__ rev_start, const int* __restrict__ rev_tmp, int* __restrict__ rev_slot) {
+  __shared__ int stage[kRevWarps][kRevStage];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int j = blockIdx.x * kRevWarps + warp;
+  if (j >= nall) return;
+  const int beg = rev_start[j], len = rev_start[j + 1] - beg;
+  const int* src = rev_tmp + beg;
+  if (len <= kRevStage) {
+    for (int e = lane; e < len; e += 32) stage[warp][e] = src[e];
+    __syncwarp();
+    src = stage[warp];
+  }
+  for (int e = lane; e < len; e += 32) {
+    const int key = src[e];
+    int rank = 0;
+    for (int e2 = 0; e2 < len; ++e2) rank += (src[e2] < key);
+    rev_slot[beg + rank] = key;
+  }
+}
+
+void launch_reverse_index(cudaStream_t st, int nloc, int nall, int selt, const int* nl_j, int* rev_count,
+                          int* rev_start, int* rev_cursor, int* rev_tmp, int* rev_slot) {
+  const long long nslots = (long long)nloc * selt;
+  cudaMemsetAsync(rev_count, 0, sizeof(int) * (size_t)nall, st);
+  cudaMemsetAsync(rev_cursor, 0, sizeof(int) * (size_t)nall, st);
+  if (nslots > 0) {
+    const int blocks = (int)std::min<long long>((nslots + 255) / 256, 148 * 16);
+    count_launch();
+    k_rev_count<<<blocks, 256, 0, st>>>(nslots, nl_j, rev_count);
+    launch_exclusive_scan(st, nall, rev_count, rev_start);
+    count_launch();
+    k_rev_fill<<<blocks, 256, 0, st>>>(nslots, nl_j, rev_start, rev_cursor, rev_tmp);
+  } else {
+    launch_exclusive_scan(st, nall, rev_count, rev_start);
+  }
+  if (nall > 0) {
+    count_launch();
+    k_rev_sort<<<(nall + kRevWarps - 1) / kRevWarps, kRevWarps * 32, 0, st>>>(nall, rev_start, rev_tmp, rev_slot);
+  }
+}
+
+// ---------------------------------------------------------------- type partition
+// Stable partition of local atoms by type: perm_pos[i] is atom i's row in the
+// type-grouped order, perm_atom the inverse, type_start[t] the first row of t.
+constexpr int kPartBlock = 1024;
+
+size_t type_partition_blocks(int nloc) { return (size_t)(nloc + kPartBlock - 1) / kPartBlock; }
+
+__global__ void __launch_bounds__(kPartBlock) k_type_count(int nloc, int ntypes, const int* __restrict__ atype,
+                                                            int* __restrict__ blk_counts, int* __restrict__ err) {
+  __shared__ int cnt[kMaxTypes];
+  if (threadIdx.x < kMaxTypes) cnt[threadIdx.x] = 0;
+  __syncthreads();
+  const int i = blockIdx.x * kPartBlock + threadIdx.x;
+  if (i < nloc) {
+    const int t = atype[i];
+    if (t >= 0 && t < ntypes)
+      atomicAdd(cnt + t, 1);
+    else
+      atomicAdd(err + kErrBadType, 1);
+  }
+  __syncthreads();
+  if (threadIdx.x < ntypes) blk_counts[blockIdx.x * ntypes + threadIdx.x] = cnt[threadIdx.x];
+}
+
+__global__ void k_type_scan(int nblk, int ntypes, int* __restrict__ blk_counts, int* __restrict__ type_start) {
+  // one thread; nblk is small (nloc / 1024)
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  int base = 0;
+  for (int t = 0; t < ntypes; ++t) {
+    type_start[t] = base;
+    for (int b = 0; b < nblk; ++b) {
+      const int c = blk_counts[b * ntypes + t];
+      blk_counts[b * ntypes + t] = base;
+      base += c;
+    }
+  }
+  type_start[ntypes] = base;
+}
+
+__global__ void __launch_bounds__(kPartBlock) k_type_place(int nloc, int ntypes, const int* __restrict__ atype,
+                                                            const int* __restrict__ blk_base,
+                                                            int* __restrict__ perm_pos, int* __restrict__ perm_atom) {
+  __shared__ int wcount[32][kMaxTypes];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int i = blockIdx.x * kPartBlock + threadIdx.x;
+  const int t = (i < nloc) ? atype[i] : -1;
+  const unsigned lt = (1u << lane) - 1u;
+  int my_rank = 0;
+  for (int q = 0; q < ntypes; ++q) {
+    const unsigned m = __ballot_sync(0xffffffffu, t == q);
+    if (t == q) my_rank = __popc(m & lt);
+    if (lane == 0) wcount[warp][q] = __popc(m);
+  }
+  __syncthreads();
+  if (threadIdx.x < ntypes) {
+    int run = 0;
+    for (int w = 0; w < 32; ++w) {
+      const int c = wcount[w][threadIdx.x];
+      wcount[w][threadIdx.x] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+  if (i < nloc) {
+    if (t >= 0 && t < ntypes) {
+      const int pos = blk_base[blockIdx.x * ntypes + t] + wcount[warp][t] + my_rank;
+      perm_pos[i] = pos;
+      perm_atom[pos] = i;
+    } else {
+      perm_pos[i] = -1;  // invalid type: the model kernels skip this centre
+    }
+  }
+}
+
+void launch_type_partition(cudaStream_t st, int nloc, int ntypes, const int* atype, int* blk_counts,
+                           int* type_start, int* perm_pos, int* perm_atom, int* err) {
+  const int nblk = (int)type_partition_blocks(nloc);
+  if (nblk == 0) {
+    cudaMemsetAsync(type_start, 0, sizeof(int) * (ntypes + 1), st);
+    return;
+  }
+  count_launch();
+  k_type_count<<<nblk, kPartBlock, 0, st>>>(nloc, ntypes, atype, blk_counts, err);
+  count_launch();
+  k_type_scan<<<1, 32, 0, st>>>(nblk, ntypes, blk_counts, type_start);
+  count_launch();
+  k_type_place<<<nblk, kPartBlock, 0, st>>>(nloc, ntypes, atype, blk_counts, perm_pos, perm_atom);
+}
+
+}  // namespace b200dp

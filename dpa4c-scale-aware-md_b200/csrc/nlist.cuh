@@ -1,0 +1,60 @@
+// Neighbour-graph builder: cell binning, warp-ballot compacted candidate
+// rows, deterministic per-type (r^2, j, image) ordering, and the reverse
+// (owner-major) index used by the atomic-free force assembly.
+//
+// Replaces the LAMMPS/Kokkos candidate list and compact canonical graph of
+// the reference (LO/KOKKOS/npair_kokkos.cpp:151-460,
+// PL/compact_canonical_graph_kokkos.h:235-821) and the per-step exact cutoff
+// (P/include/dpa_chain/exact_cut.cuh:10-20).  Output format is DeePMD's
+// formatted neighbour list: per centre, sum(sel) slots, type t at offset
+// sum(sel[:t]), -1 padding.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+
+namespace b200dp {
+
+struct GridSpec {
+  int periodic;     // 1: fractional grid over the periodic cell; 0: open Cartesian grid
+  double B[9];      // cell rows (periodic)
+  double Binv[9];   // s_d = sum_a x_a Binv[a*3+d]
+  double lo[3];     // open grid origin
+  double inv_h[3];  // open grid inverse cell size
+  int n[3];         // cells per dimension
+  int reach[3];     // stencil half-width in cells
+  int ncells;
+};
+
+struct FormatSpec {
+  int nloc, nall, ntypes, selt, cap;
+  int sel[kMaxTypes];
+  int off[kMaxTypes + 1];
+  double rc2;
+};
+
+// Host helpers (identical arithmetic to the oracle's cell set-up).
+void make_box_inverse(const double* box, double* Binv, double* width);
+
+// Launchers; all enqueue on `st`.
+void launch_bin(cudaStream_t st, int nall, const double* coord, const GridSpec& g, double* xw, int* cell_of,
+                int* cell_count);
+void launch_exclusive_scan(cudaStream_t st, int n, const int* in, int* out);
+void launch_fill_cells(cudaStream_t st, int nall, const int* cell_of, const int* cell_start, int* cursor,
+                       int* cell_atoms);
+size_t format_smem_bytes(int cap);
+void launch_format(cudaStream_t st, const FormatSpec& f, const GridSpec& g, const double* xw, const int* atype,
+                   const int* cell_of, const int* cell_start, const int* cell_atoms, int* nl_j, int* nl_code,
+                   double* nl_rij, int* nl_cnt, int* err);
+// Formats a caller-provided candidate list (LAMMPS full list in CSR form).
+void launch_format_candidates(cudaStream_t st, const FormatSpec& f, const double* coord, const int* atype,
+                              const int* ilist, const int* cand_start, const int* cand, int* nl_j, int* nl_code,
+                              double* nl_rij, int* nl_cnt, int* err);
+void launch_reverse_index(cudaStream_t st, int nloc, int nall, int selt, const int* nl_j, int* rev_count,
+                          int* rev_start, int* rev_cursor, int* rev_tmp, int* rev_slot);
+void launch_type_partition(cudaStream_t st, int nloc, int ntypes, const int* atype, int* blk_counts,
+                           int* type_start, int* perm_pos, int* perm_atom, int* err);
+size_t type_partition_blocks(int nloc);
+
+}  // namespace b200dp

@@ -1,0 +1,701 @@
+// DPA4C-style model kernels (see sea.cuh).  SIMT path, templated on the
+// network precision P (double for the fp64 mode, float for the mixed mode);
+// geometry, the chain rule to r_ij and every accumulation of energy, force
+// and virial stay in fp64 in both modes.
+#include <algorithm>
+
+#include "sea.cuh"
+
+namespace b200dp {
+
+namespace {
+
+// Residual rule of DeePMD's embedding net: d_out == d_in -> x + h,
+// d_out == 2 d_in -> concat(x, x) + h, otherwise h.
+__device__ __forceinline__ int resid_mode(int din, int dout) { return dout == din ? 1 : (dout == 2 * din ? 2 : 0); }
+
+template <typename P>
+struct SmemCarve {
+  unsigned char* p;
+  __device__ explicit SmemCarve(unsigned char* base) : p(base) {}
+  template <typename T>
+  __device__ T* take(size_t n) {
+    T* r = reinterpret_cast<T*>(p);
+    p += ((n * sizeof(T) + 15) / 16) * 16;
+    return r;
+  }
+};
+
+// Scalar-input first layer: out[e][n] = tanh(s_e * w[n] + b[n]) (+ residual).
+template <typename P>
+__device__ __forceinline__ void layer_from_scalar(const P* srt, int ne, P* out, int d1, const P* __restrict__ w,
+                                                  const P* __restrict__ b) {
+  const int rm = resid_mode(1, d1);
+  for (int idx = threadIdx.x; idx < ne * d1; idx += blockDim.x) {
+    const int e = idx / d1, n = idx - e * d1;
+    const P x = srt[4 * e];
+    P h = act_tanh<P>(x * __ldg(w + n) + __ldg(b + n));
+    if (rm) h += x;
+    out[idx] = h;
+  }
+}
+
+// out[e][n] = tanh(sum_k in[e][k] W[k][n] + b[n]) (+ residual); 4 edges per
+// thread share each weight load.  Rows >= ne of `in` may hold stale values;
+// they are computed but never stored (buffers have a multiple of 4 rows).
+template <typename P>
+__device__ __forceinline__ void dense_layer(const P* in, int din, P* out, int dout, const P* __restrict__ W,
+                                            const P* __restrict__ b, int ne) {
+  const int rm = resid_mode(din, dout);
+  const int groups = (ne + 3) >> 2;
+  for (int idx = threadIdx.x; idx < groups * dout; idx += blockDim.x) {
+    const int n = idx % dout, e0 = (idx / dout) * 4;
+    const P bias = __ldg(b + n);
+    P a0 = bias, a1 = bias, a2 = bias, a3 = bias;
+    const P* x = in + e0 * din;
+    for (int k = 0; k < din; ++k) {
+      const P wv = __ldg(W + k * dout + n);
+      a0 += x[k] * wv;
+      a1 += x[din + k] * wv;
+      a2 += x[2 * din + k] * wv;
+      a3 += x[3 * din + k] * wv;
+    }
+    const P acc[4] = {a0, a1, a2, a3};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int e = e0 + q;
+      if (e < ne) {
+        P h = act_tanh<P>(acc[q]);
+        if (rm == 1)
+          h += in[e * din + n];
+        else if (rm == 2)
+          h += in[e * din + (n < din ? n : n - din)];
+        out[e * dout + n] = h;
+      }
+    }
+  }
+}
+
+// gx[e][k] = sum_n gz[e][n] W[k][n] (+ residual gradient from gy).  WT is
+// W transposed ([dout][din]) so threads over k read consecutive weights.
+template <typename P>
+__device__ __forceinline__ void dense_bwd(const P* gz, const P* gy, int dout, P* gx, int din,
+                                          const P* __restrict__ WT, int ne) {
+  const int rm = resid_mode(din, dout);
+  const int groups = (ne + 3) >> 2;
+  for (int idx = threadIdx.x; idx < groups * din; idx += blockDim.x) {
+    const int k = idx % din, e0 = (idx / din) * 4;
+    P a0 = 0, a1 = 0, a2 = 0, a3 = 0;
+    const P* z = gz + e0 * dout;
+    for (int n = 0; n < dout; ++n) {
+      const P wv = __ldg(WT + n * din + k);
+      a0 += z[n] * wv;
+      a1 += z[dout + n] * wv;
+      a2 += z[2 * dout + n] * wv;
+      a3 += z[3 * dout + n] * wv;
+    }
+    const P acc[4] = {a0, a1, a2, a3};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int e = e0 + q;
+      if (e < ne) {
+        P v = acc[q];
+        if (rm == 1)
+          v += gy[e * dout + k];
+        else if (rm == 2)
+          v += gy[e * dout + k] + gy[e * dout + k + din];
+        gx[e * din + k] = v;
+      }
+    }
+  }
+}
+
+// Environment row of one edge: rt = sw(r) * (1/r, x/r^2, y/r^2, z/r^2) and,
+// when drt != nullptr, its Jacobian d rt_k / d r_c (fp64).
+__device__ __forceinline__ void env_row(const SeaDev& s, const double* r, double* rt, double* drt) {
+  const double r2 = r[0] * r[0] + r[1] * r[1] + r[2] * r[2];
+  const double rr = sqrt(r2);
+  double sw, dsw;
+  smooth_switch(rr, s.rcut_smth, s.rcut, sw, dsw);
+  const double inv_r = 1.0 / rr, inv_r2 = inv_r * inv_r;
+  rt[0] = sw * inv_r;
+#pragma unroll
+  for (int c = 0; c < 3; ++c) rt[1 + c] = sw * r[c] * inv_r2;
+  if (drt) {
+    const double d0 = dsw * inv_r - sw * inv_r2;
+#pragma unroll
+    for (int c = 0; c < 3; ++c) drt[c] = d0 * r[c] * inv_r;
+#pragma unroll
+    for (int a = 0; a < 3; ++a)
+#pragma unroll
+      for (int c = 0; c < 3; ++c)
+        drt[3 * (1 + a) + c] =
+            dsw * r[c] * inv_r * r[a] * inv_r2 + sw * ((a == c ? inv_r2 : 0.0) - 2.0 * r[a] * r[c] * inv_r2 * inv_r2);
+  }
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------- descriptor forward
+template <typename P>
+size_t descriptor_fwd_smem(const SeaDev& s, int ch) {
+  auto al = [](size_t b) { return ((b + 15) / 16) * 16; };
+  return al(sizeof(P) * ch * 4) + 2 * al(sizeof(P) * ch * s.maxd) + al(sizeof(P) * 4 * s.M1);
+}
+
+template <typename P>
+__global__ void __launch_bounds__(kSeaThreads)
+    k_descriptor_fwd(SeaDev s, int nloc, int ch, const double* __restrict__ rij, const int* __restrict__ cnt,
+                     const int* __restrict__ atype, const int* __restrict__ perm_pos, const P* __restrict__ emb,
+                     P* __restrict__ Tg, P* __restrict__ Dg) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  SmemCarve<P> sc(smem_raw);
+  P* srt = sc.template take<P>((size_t)ch * 4);
+  P* buf0 = sc.template take<P>((size_t)ch * s.maxd);
+  P* buf1 = sc.template take<P>((size_t)ch * s.maxd);
+  P* sT = sc.template take<P>((size_t)4 * s.M1);
+  const int tid = threadIdx.x;
+  for (int i = blockIdx.x; i < nloc; i += gridDim.x) {
+    const int ti = atype[i];
+    if (ti < 0 || ti >= s.ntypes) continue;  // reported by the type partition; block-uniform
+    P tacc[4] = {0, 0, 0, 0};
+    for (int t = 0; t < s.ntypes; ++t) {
+      const int n_e = cnt[(size_t)i * s.ntypes + t];
+      const int net = s.type_one_side ? t : ti * s.ntypes + t;
+      const P* Wn = emb + (size_t)net * s.net_stride;
+      const size_t base = (size_t)i * s.selt + s.off[t];
+      for (int c0 = 0; c0 < n_e; c0 += ch) {
+        const int ne = min(ch, n_e - c0);
+        for (int e = tid; e < ne; e += blockDim.x) {
+          const double* r = rij + 3 * (base + c0 + e);
+          const double rv[3] = {r[0], r[1], r[2]};
+          double rt[4];
+          env_row(s, rv, rt, nullptr);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) srt[4 * e + k] = (P)rt[k];
+        }
+        __syncthreads();
+        layer_from_scalar<P>(srt, ne, buf0, s.ed[1], Wn + s.w_off[0], Wn + s.b_off[0]);
+        __syncthreads();
+        P* in = buf0;
+        P* out = buf1;
+        for (int l = 1; l < s.nl; ++l) {
+          dense_layer<P>(in, s.ed[l], out, s.ed[l + 1], Wn + s.w_off[l], Wn + s.b_off[l], ne);
+          __syncthreads();
+          P* tmp = in;
+          in = out;
+          out = tmp;
+        }
+        if (tid < s.M1) {
+          // one column of T per thread (M1 <= blockDim is checked at load)
+          for (int e = 0; e < ne; ++e) {
+            const P g = in[e * s.M1 + tid];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) tacc[k] += srt[4 * e + k] * g;
+          }
+        }
+        __syncthreads();
+      }
+    }
+    const P inv = (P)s.inv_nnei;
+    if (tid < s.M1) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const P v = tacc[k] * inv;
+        sT[k * s.M1 + tid] = v;
+        Tg[(size_t)i * 4 * s.M1 + k * s.M1 + tid] = v;
+      }
+    }
+    __syncthreads();
+    P* drow = Dg + (size_t)perm_pos[i] * s.dim;
+    for (int idx = tid; idx < s.M1 * s.M2; idx += blockDim.x) {
+      const int a = idx / s.M2, b = idx - a * s.M2;
+      P acc = 0;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) acc += sT[k * s.M1 + a] * sT[k * s.M1 + b];
+      drow[idx] = acc;
+    }
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------- descriptor backward
+template <typename P>
+size_t descriptor_bwd_smem(const SeaDev& s, int ch) {
+  auto al = [](size_t b) { return ((b + 15) / 16) * 16; };
+  size_t acts = 0;
+  for (int l = 1; l <= s.nl; ++l) acts += al(sizeof(P) * ch * s.ed[l]);
+  return 2 * al(sizeof(P) * 4 * s.M1) + al(sizeof(P) * s.dim) + al(sizeof(P) * ch * 4) +
+         al(sizeof(double) * ch * 12) + al(sizeof(P) * ch * 4) + acts + 3 * al(sizeof(P) * ch * s.maxd);
+}
+
+template <typename P>
+__global__ void __launch_bounds__(kSeaThreads)
+    k_descriptor_bwd(SeaDev s, int nloc, int ch, const double* __restrict__ rij, const int* __restrict__ cnt,
+                     const int* __restrict__ atype, const int* __restrict__ perm_pos, const P* __restrict__ emb,
+                     const P* __restrict__ embT, const P* __restrict__ Tg, const P* __restrict__ dDg,
+                     double* __restrict__ gslot) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  SmemCarve<P> sc(smem_raw);
+  P* sT = sc.template take<P>((size_t)4 * s.M1);
+  P* sdT = sc.template take<P>((size_t)4 * s.M1);
+  P* sdD = sc.template take<P>((size_t)s.dim);
+  P* srt = sc.template take<P>((size_t)ch * 4);
+  double* sdrt = sc.template take<double>((size_t)ch * 12);
+  P* sdR = sc.template take<P>((size_t)ch * 4);
+  P* act[kMaxLayers + 1];
+  act[0] = nullptr;
+  for (int l = 1; l <= s.nl; ++l) act[l] = sc.template take<P>((size_t)ch * s.ed[l]);
+  P* gbuf[3];
+  for (int q = 0; q < 3; ++q) gbuf[q] = sc.template take<P>((size_t)ch * s.maxd);
+  const int tid = threadIdx.x;
+  const int M1 = s.M1, M2 = s.M2;
+  for (int i = blockIdx.x; i < nloc; i += gridDim.x) {
+    const int ti = atype[i];
+    if (ti < 0 || ti >= s.ntypes) continue;  // reported by the type partition; block-uniform
+    const P* Ti = Tg + (size_t)i * 4 * M1;
+    const P* dDi = dDg + (size_t)perm_pos[i] * s.dim;
+    for (int idx = tid; idx < 4 * M1; idx += blockDim.x) sT[idx] = Ti[idx];
+    for (int idx = tid; idx < s.dim; idx += blockDim.x) sdD[idx] = dDi[idx];
+    __syncthreads();
+    // dT[k][a] = (sum_b dD[a][b] T[k][b] + [a < M2] sum_c dD[c][a] T[k][c]) / N
+    for (int idx = tid; idx < 4 * M1; idx += blockDim.x) {
+      const int k = idx / M1, a = idx - k * M1;
+      const P* tk = sT + k * M1;
+      P acc = 0;
+      for (int b = 0; b < M2; ++b) acc += sdD[a * M2 + b] * tk[b];
+      if (a < M2)
+        for (int c = 0; c < M1; ++c) acc += sdD[c * M2 + a] * tk[c];
+      sdT[idx] = acc * (P)s.inv_nnei;
+    }
+    __syncthreads();
+    for (int t = 0; t < s.ntypes; ++t) {
+      const int n_e = cnt[(size_t)i * s.ntypes + t];
+      const int net = s.type_one_side ? t : ti * s.ntypes + t;
+      const P* Wn = emb + (size_t)net * s.net_stride;
+      const P* WTn = embT + (size_t)net * s.net_stride;
+      const size_t base = (size_t)i * s.selt + s.off[t];
+      for (int c0 = 0; c0 < n_e; c0 += ch) {
+        const int ne = min(ch, n_e - c0);
+        for (int e = tid; e < ne; e += blockDim.x) {
+          const double* r = rij + 3 * (base + c0 + e);
+          const double rv[3] = {r[0], r[1], r[2]};
+          double rt[4];
+          env_row(s, rv, rt, sdrt + 12 * e);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) srt[4 * e + k] = (P)rt[k];
+        }
+        __syncthreads();
+        // forward recompute, keeping every layer output
+        layer_from_scalar<P>(srt, ne, act[1], s.ed[1], Wn + s.w_off[0], Wn + s.b_off[0]);
+        __syncthreads();
+        for (int l = 1; l < s.nl; ++l) {
+          dense_layer<P>(act[l], s.ed[l], act[l + 1], s.ed[l + 1], Wn + s.w_off[l], Wn + s.b_off[l], ne);
+          __syncthreads();
+        }
+        const P* G = act[s.nl];
+        // dG[e][a] = sum_k dT'[k][a] rt[e][k];  dR[e][k] = sum_a dT'[k][a] G[e][a]
+        P* gy = gbuf[0];
+        for (int idx = tid; idx < ne * M1; idx += blockDim.x) {
+          const int e = idx / M1, a = idx - e * M1;
+          P acc = 0;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) acc += sdT[k * M1 + a] * srt[4 * e + k];
+          gy[idx] = acc;
+        }
+        for (int idx = tid; idx < ne * 4; idx += blockDim.x) {
+          const int e = idx >> 2, k = idx & 3;
+          const P* g = G + e * M1;
+          const P* dt = sdT + k * M1;
+          P acc = 0;
+          for (int a = 0; a < M1; ++a) acc += dt[a] * g[a];
+          sdR[idx] = acc;
+        }
+        __syncthreads();
+        // back through layers nl-1 .. 1
+        P* gz = gbuf[1];
+        P* gx = gbuf[2];
+        for (int l = s.nl - 1; l >= 1; --l) {
+          const int din = s.ed[l], dout = s.ed[l + 1];
+          const int rm = resid_mode(din, dout);
+          const P* x = act[l];
+          const P* y = act[l + 1];
+          for (int idx = tid; idx < ne * dout; idx += blockDim.x) {
+            const int e = idx / dout, n = idx - e * dout;
+            P th = y[idx];
+            if (rm == 1)
+              th -= x[e * din + n];
+            else if (rm == 2)
+              th -= x[e * din + (n < din ? n : n - din)];
+            gz[idx] = gy[idx] * ((P)1 - th * th);
+          }
+          __syncthreads();
+          dense_bwd<P>(gz, gy, dout, gx, din, WTn + s.w_off[l], ne);
+          __syncthreads();
+          P* tmp = gy;
+          gy = gx;
+          gx = tmp;
+        }
+        // first layer (scalar input) and the chain rule to r_ij
+        {
+          const int d1 = s.ed[1];
+          const int rm = resid_mode(1, d1);
+          const P* y = act[1];
+          for (int idx = tid; idx < ne * d1; idx += blockDim.x) {
+            const int e = idx / d1;
+            P th = y[idx];
+            if (rm) th -= srt[4 * e];
+            gz[idx] = gy[idx] * ((P)1 - th * th);
+          }
+          __syncthreads();
+          const P* w0 = Wn + s.w_off[0];
+          for (int e = tid; e < ne; e += blockDim.x) {
+            P ds = 0;
+            for (int n = 0; n < d1; ++n) ds += gz[e * d1 + n] * __ldg(w0 + n);
+            if (rm)
+              for (int n = 0; n < d1; ++n) ds += gy[e * d1 + n];
+            double dR[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) dR[k] = (double)sdR[4 * e + k];
+            dR[0] += (double)ds;
+            const double* J = sdrt + 12 * e;
+            double* go = gslot + 3 * (base + c0 + e);
+#pragma unroll
+            for (int c = 0; c < 3; ++c) go[c] = ((dR[0] * J[c] + dR[1] * J[3 + c]) + dR[2] * J[6 + c]) + dR[3] * J[9 + c];
+          }
+          __syncthreads();
+        }
+      }
+    }
+  }
+}
+
+template <typename P>
+int descriptor_grid(const SeaDev& s, int ch, bool bwd, int nloc) {
+  int dev = 0, nsm = 148, occ = 1;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  const size_t smem = bwd ? descriptor_bwd_smem<P>(s, ch) : descriptor_fwd_smem<P>(s, ch);
+  if (bwd) {
+    cudaFuncSetAttribute(k_descriptor_bwd<P>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_descriptor_bwd<P>, kSeaThreads, smem);
+  } else {
+    cudaFuncSetAttribute(k_descriptor_fwd<P>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_descriptor_fwd<P>, kSeaThreads, smem);
+  }
+  occ = std::max(occ, 1);
+  return std::max(1, std::min(nloc, nsm * occ));
+}
+
+template <typename P>
+void launch_descriptor_fwd(cudaStream_t st, const SeaDev& s, int nloc, int ch, int grid, const double* rij,
+                           const int* cnt, const int* atype, const int* perm_pos, const P* emb, P* T, P* D) {
+  if (nloc <= 0) return;
+  count_launch();
+  k_descriptor_fwd<P><<<grid, kSeaThreads, descriptor_fwd_smem<P>(s, ch), st>>>(s, nloc, ch, rij, cnt, atype,
+                                                                                 perm_pos, emb, T, D);
+}
+
+template <typename P>
+void launch_descriptor_bwd(cudaStream_t st, const SeaDev& s, int nloc, int ch, int grid, const double* rij,
+                           const int* cnt, const int* atype, const int* perm_pos, const P* emb, const P* embT,
+                           const P* T, const P* dD, double* gslot) {
+  if (nloc <= 0) return;
+  count_launch();
+  k_descriptor_bwd<P><<<grid, kSeaThreads, descriptor_bwd_smem<P>(s, ch), st>>>(s, nloc, ch, rij, cnt, atype,
+                                                                                 perm_pos, emb, embT, T, dD, gslot);
+}
+
+// ---------------------------------------------------------------- fitting GEMMs
+namespace {
+constexpr int kBM = 64, kBN = 64, kBK = 16;
+
+// C[m][n] = sum_k A[m][k] * B(k, n), B(k, n) = BT ? B[n*ldb + k] : B[k*ldb + n].
+// 256 threads, 4x4 outputs each at stride 16 (bank-conflict free reads).
+template <typename P, bool BT, class Epi>
+__global__ void __launch_bounds__(256) k_gemm(const int* __restrict__ range, int N, int K, const P* __restrict__ A,
+                                               int lda, const P* __restrict__ B, int ldb, Epi epi) {
+  __shared__ P As[kBK][kBM + 1];
+  __shared__ P Bs[kBK][kBN + 1];
+  const int row0 = range[0], M = range[1] - row0;
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * kBN;
+  if (m0 >= M) return;
+  A += (size_t)row0 * lda;
+  P acc[4][4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+#pragma unroll
+    for (int r = 0; r < 4; ++r) acc[q][r] = 0;
+  for (int k0 = 0; k0 < K; k0 += kBK) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int idx = tid + 256 * q;  // 0..1023
+      const int mm = idx / kBK, kk = idx % kBK;
+      const int m = m0 + mm, k = k0 + kk;
+      As[kk][mm] = (m < M && k < K) ? A[(size_t)m * lda + k] : (P)0;
+      if (BT) {
+        const int nn = idx / kBK, kb = idx % kBK;
+        const int n = n0 + nn, kx = k0 + kb;
+        Bs[kb][nn] = (n < N && kx < K) ? B[(size_t)n * ldb + kx] : (P)0;
+      } else {
+        const int kb = idx / kBN, nn = idx % kBN;
+        const int n = n0 + nn, kx = k0 + kb;
+        Bs[kb][nn] = (n < N && kx < K) ? B[(size_t)kx * ldb + n] : (P)0;
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < kBK; ++kk) {
+      P a[4], b[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        a[q] = As[kk][ty + 16 * q];
+        b[q] = Bs[kk][tx + 16 * q];
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) acc[q][r] += a[q] * b[r];
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int m = m0 + ty + 16 * q, n = n0 + tx + 16 * r;
+      if (m < M && n < N) epi(row0 + m, n, acc[q][r]);
+    }
+}
+
+template <typename P>
+struct EpiForward {
+  const P* b;
+  const P* X;
+  int ldx;
+  bool residual;
+  P* th;
+  P* Y;
+  int ld;
+  __device__ void operator()(int m, int n, P acc) const {
+    const P h = act_tanh<P>(acc + b[n]);
+    th[(size_t)m * ld + n] = h;
+    Y[(size_t)m * ld + n] = residual ? X[(size_t)m * ldx + n] + h : h;
+  }
+};
+
+template <typename P>
+struct EpiBackward {
+  const P* dy_next;  // residual gradient (same shape as the output), or null
+  P* dX;
+  const P* th_prev;  // tanh of the previous layer, or null (last step: dX is the input gradient)
+  P* dz_prev;
+  int ld;
+  __device__ void operator()(int m, int n, P acc) const {
+    const size_t o = (size_t)m * ld + n;
+    const P v = dy_next ? acc + dy_next[o] : acc;
+    dX[o] = v;
+    if (th_prev) {
+      const P t = th_prev[o];
+      dz_prev[o] = v * ((P)1 - t * t);
+    }
+  }
+};
+}  // namespace
+
+template <typename P>
+void launch_fit_forward_layer(cudaStream_t st, int Mmax, const int* range, int N, int K, const P* X, int ldx,
+                              const P* W, const P* b, bool residual, P* th, P* Y) {
+  if (Mmax <= 0) return;
+  dim3 grid((N + kBN - 1) / kBN, (Mmax + kBM - 1) / kBM);
+  EpiForward<P> epi{b, X, ldx, residual, th, Y, N};
+  count_launch();
+  k_gemm<P, false, EpiForward<P>><<<grid, 256, 0, st>>>(range, N, K, X, ldx, W, N, epi);
+}
+
+template <typename P>
+void launch_fit_backward_layer(cudaStream_t st, int Mmax, const int* range, int Nin, int Nout, const P* dZ,
+                               const P* W, const P* dY_next, P* dX, const P* th_prev, P* dZ_prev) {
+  if (Mmax <= 0) return;
+  // dX[m][n] = sum_k dZ[m][k] W[n][k]   (W is [Nin][Nout] row-major)
+  dim3 grid((Nin + kBN - 1) / kBN, (Mmax + kBM - 1) / kBM);
+  EpiBackward<P> epi{dY_next, dX, th_prev, dZ_prev, Nin};
+  count_launch();
+  k_gemm<P, true, EpiBackward<P>><<<grid, 256, 0, st>>>(range, Nin, Nout, dZ, Nout, W, Nout, epi);
+}
+
+template <typename P>
+__global__ void k_fit_energy(const int* __restrict__ range, int N, const P* __restrict__ Y, const P* __restrict__ wo,
+                             double bo, const int* __restrict__ perm_atom, double* __restrict__ atom_energy) {
+  const int row0 = range[0], M = range[1] - row0;
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= M) return;
+  const int row = row0 + warp;
+  const P* y = Y + (size_t)row * N;
+  double acc = 0;
+  for (int n = lane; n < N; n += 32) acc += (double)(y[n] * wo[n]);
+  acc = warp_sum(acc);
+  if (lane == 0) atom_energy[perm_atom[row]] = acc + bo;
+}
+
+template <typename P>
+void launch_fit_energy(cudaStream_t st, int Mmax, const int* range, int N, const P* Y, const P* wo,
+                       double bo_plus_bias, const int* perm_atom, double* atom_energy) {
+  if (Mmax <= 0) return;
+  count_launch();
+  k_fit_energy<P><<<(Mmax * 32 + 255) / 256, 256, 0, st>>>(range, N, Y, wo, bo_plus_bias, perm_atom, atom_energy);
+}
+
+template <typename P>
+__global__ void k_fit_seed(const int* __restrict__ range, int N, const P* __restrict__ wo, const P* __restrict__ th,
+                           P* __restrict__ dy, P* __restrict__ dz) {
+  const size_t row0 = (size_t)range[0], M = (size_t)(range[1] - range[0]);
+  const size_t total = M * N;
+  for (size_t q = blockIdx.x * (size_t)blockDim.x + threadIdx.x; q < total; q += (size_t)gridDim.x * blockDim.x) {
+    const size_t o = row0 * N + q;
+    const int n = (int)(q % N);
+    const P w = wo[n], t = th[o];
+    dy[o] = w;
+    dz[o] = w * ((P)1 - t * t);
+  }
+}
+
+template <typename P>
+void launch_fit_seed(cudaStream_t st, int Mmax, const int* range, int N, const P* wo, const P* th, P* dy, P* dz) {
+  if (Mmax <= 0) return;
+  const size_t total = (size_t)Mmax * N;
+  const int blocks = (int)std::min<size_t>((total + 255) / 256, 148 * 32);
+  count_launch();
+  k_fit_seed<P><<<blocks, 256, 0, st>>>(range, N, wo, th, dy, dz);
+}
+
+// ---------------------------------------------------------------- assembly
+// One warp per atom j: F_j = sum_{own row} g - sum_{edges into j} g, and the
+// atom virial of j = sum_{edges into j} -g (x) r, in a fixed order (own row by
+// slot, reverse list sorted by slot id, xor-tree warp reduction).
+constexpr int kAsmWarps = 8;
+__global__ void __launch_bounds__(kAsmWarps * 32)
+    k_assemble(int nloc, int nall, int selt, const int* __restrict__ nl_j, const double* __restrict__ gslot,
+               const double* __restrict__ rij, const int* __restrict__ rev_start, const int* __restrict__ rev_slot,
+               double* __restrict__ force, double* __restrict__ atom_virial, double* __restrict__ virial_rows) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int j = blockIdx.x * kAsmWarps + warp;
+  if (j >= nall) return;
+  double f[3] = {0, 0, 0};
+  double v[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
+  if (j < nloc) {
+    const size_t row = (size_t)j * selt;
+    for (int s = lane; s < selt; s += 32) {
+      if (nl_j[row + s] >= 0) {
+        const double* g = gslot + 3 * (row + s);
+        f[0] += g[0];
+        f[1] += g[1];
+        f[2] += g[2];
+      }
+    }
+  }
+  for (int q = rev_start[j] + lane; q < rev_start[j + 1]; q += 32) {
+    const size_t slot = (size_t)rev_slot[q];
+    const double g[3] = {gslot[3 * slot], gslot[3 * slot + 1], gslot[3 * slot + 2]};
+    const double r[3] = {rij[3 * slot], rij[3 * slot + 1], rij[3 * slot + 2]};
+    f[0] -= g[0];
+    f[1] -= g[1];
+    f[2] -= g[2];
+#pragma unroll
+    for (int a = 0; a < 3; ++a)
+#pragma unroll
+      for (int b = 0; b < 3; ++b) v[3 * a + b] -= g[a] * r[b];
+  }
+#pragma unroll
+  for (int c = 0; c < 3; ++c) f[c] = warp_sum(f[c]);
+#pragma unroll
+  for (int c = 0; c < 9; ++c) v[c] = warp_sum(v[c]);
+  if (lane == 0) {
+    force[3 * (size_t)j] = f[0];
+    force[3 * (size_t)j + 1] = f[1];
+    force[3 * (size_t)j + 2] = f[2];
+#pragma unroll
+    for (int c = 0; c < 9; ++c) {
+      virial_rows[9 * (size_t)j + c] = v[c];
+      if (atom_virial) atom_virial[9 * (size_t)j + c] = v[c];
+    }
+  }
+}
+
+void launch_assemble(cudaStream_t st, int nloc, int nall, int selt, const int* nl_j, const double* gslot,
+                     const double* rij, const int* rev_start, const int* rev_slot, double* force,
+                     double* atom_virial, double* virial_rows) {
+  if (nall <= 0) return;
+  count_launch();
+  k_assemble<<<(nall + kAsmWarps - 1) / kAsmWarps, kAsmWarps * 32, 0, st>>>(nloc, nall, selt, nl_j, gslot, rij,
+                                                                            rev_start, rev_slot, force, atom_virial,
+                                                                            virial_rows);
+}
+
+// Fixed-shape two-stage column reduction (kReduceBlocks x 256 threads, then
+// one block), so the result is identical from run to run.
+__global__ void __launch_bounds__(256) k_reduce_partial(int n, int C, const double* __restrict__ rows,
+                                                         double* __restrict__ partial) {
+  __shared__ double sh[256];
+  const int chunk = (n + gridDim.x - 1) / gridDim.x;
+  const int r0 = blockIdx.x * chunk, r1 = min(n, r0 + chunk);
+  for (int c = 0; c < C; ++c) {
+    double acc = 0;
+    for (int r = r0 + threadIdx.x; r < r1; r += blockDim.x) acc += rows[(size_t)r * C + c];
+    sh[threadIdx.x] = acc;
+    __syncthreads();
+    for (int o = 128; o > 0; o >>= 1) {
+      if (threadIdx.x < o) sh[threadIdx.x] += sh[threadIdx.x + o];
+      __syncthreads();
+    }
+    if (threadIdx.x == 0) partial[blockIdx.x * C + c] = sh[0];
+    __syncthreads();
+  }
+}
+
+__global__ void __launch_bounds__(256) k_reduce_final(int nb, int C, const double* __restrict__ partial,
+                                                       double* __restrict__ out) {
+  __shared__ double sh[256];
+  for (int c = 0; c < C; ++c) {
+    double acc = 0;
+    for (int b = threadIdx.x; b < nb; b += blockDim.x) acc += partial[b * C + c];
+    sh[threadIdx.x] = acc;
+    __syncthreads();
+    for (int o = 128; o > 0; o >>= 1) {
+      if (threadIdx.x < o) sh[threadIdx.x] += sh[threadIdx.x + o];
+      __syncthreads();
+    }
+    if (threadIdx.x == 0) out[c] = sh[0];
+    __syncthreads();
+  }
+}
+
+void launch_reduce_rows(cudaStream_t st, int n, int C, const double* rows, double* partial, double* out) {
+  count_launch();
+  k_reduce_partial<<<kReduceBlocks, 256, 0, st>>>(n, C, rows, partial);
+  count_launch();
+  k_reduce_final<<<1, 256, 0, st>>>(kReduceBlocks, C, partial, out);
+}
+
+// ---------------------------------------------------------------- instantiations
+#define B200DP_INST(P)                                                                                              \
+  template size_t descriptor_fwd_smem<P>(const SeaDev&, int);                                                      \
+  template size_t descriptor_bwd_smem<P>(const SeaDev&, int);                                                      \
+  template int descriptor_grid<P>(const SeaDev&, int, bool, int);                                                  \
+  template void launch_descriptor_fwd<P>(cudaStream_t, const SeaDev&, int, int, int, const double*, const int*,    \
+                                         const int*, const int*, const P*, P*, P*);                                \
+  template void launch_descriptor_bwd<P>(cudaStream_t, const SeaDev&, int, int, int, const double*, const int*,    \
+                                         const int*, const int*, const P*, const P*, const P*, const P*, double*); \
+  template void launch_fit_forward_layer<P>(cudaStream_t, int, const int*, int, int, const P*, int, const P*,   \
+                                            const P*, bool, P*, P*);                                               \
+  template void launch_fit_energy<P>(cudaStream_t, int, const int*, int, const P*, const P*, double, const int*,   \
+                                     double*);                                                                     \
+  template void launch_fit_seed<P>(cudaStream_t, int, const int*, int, const P*, const P*, P*, P*);              \
+  template void launch_fit_backward_layer<P>(cudaStream_t, int, const int*, int, int, const P*, const P*,          \
+                                             const P*, P*, const P*, P*);
+
+B200DP_INST(double)
+B200DP_INST(float)
+
+}  // namespace b200dp

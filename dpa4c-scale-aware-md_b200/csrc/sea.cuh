@@ -1,0 +1,73 @@
+// DPA4C-style (se_e2_a type) model kernels: environment matrix with smooth
+// switch, embedding net fused with the contraction T = R~^T G / N and
+// D = T^T T_<, the fitting MLP forward and analytic backward, and the
+// atomic-free force / virial assembly.
+//
+// Reference roles these kernels take over (paths in the reference project):
+//  - descriptor forward: components/deepmd-op/overlays/op/pt/dpa4c/graph_compress_kernel.cuh:78-767
+//  - fitting forward + input gradient: components/deepmd-op/overlays/op/pt/graph_fitting.cu:614-801
+//  - node/edge backward: graph_compress_kernel.cuh:909-1458, 1460-1917
+//  - force / virial assembly: components/deepmd-op/overlays/op/pt/edge_force_virial.cu:1-190
+//  - widen + reduce: components/deepmd-op/overlays/op/pt/dpa4c/graph_compress.cu:1493-1504
+// The se_e2_a math itself (switch, residual rules, 1/N normalisation) is
+// DeePMD-kit's published definition; DeePMD-kit is not vendored in the
+// reference (production/dpa4c-runtime/third_party/sources.lock.json:4-12).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+
+namespace b200dp {
+
+struct SeaDev {
+  int ntypes, nnets, type_one_side, nl;  // nl: embedding layers
+  int ed[kMaxLayers + 1];                // embedding dims, ed[0] = 1
+  int M1, M2, dim, selt, maxd;
+  int sel[kMaxTypes], off[kMaxTypes + 1];
+  double rcut, rcut_smth, inv_nnei;
+  int net_stride;  // elements per embedding net
+  int w_off[kMaxLayers], b_off[kMaxLayers];
+};
+
+constexpr int kSeaThreads = 128;
+
+template <typename P>
+size_t descriptor_fwd_smem(const SeaDev& s, int ch);
+template <typename P>
+size_t descriptor_bwd_smem(const SeaDev& s, int ch);
+
+template <typename P>
+void launch_descriptor_fwd(cudaStream_t st, const SeaDev& s, int nloc, int ch, int grid, const double* rij,
+                           const int* cnt, const int* atype, const int* perm_pos, const P* emb, P* T, P* D);
+template <typename P>
+void launch_descriptor_bwd(cudaStream_t st, const SeaDev& s, int nloc, int ch, int grid, const double* rij,
+                           const int* cnt, const int* atype, const int* perm_pos, const P* emb, const P* embT,
+                           const P* T, const P* dD, double* gslot);
+template <typename P>
+int descriptor_grid(const SeaDev& s, int ch, bool bwd, int nloc);
+
+// Fitting pieces.  Rows of one centre type are [range[0], range[1]) of the
+// type-grouped order; `range` is device memory so no host sync is needed.
+// Mmax bounds the row count for the launch grid (blocks past range exit).
+template <typename P>
+void launch_fit_forward_layer(cudaStream_t st, int Mmax, const int* range, int N, int K, const P* X, int ldx,
+                              const P* W, const P* b, bool residual, P* th, P* Y);
+template <typename P>
+void launch_fit_energy(cudaStream_t st, int Mmax, const int* range, int N, const P* Y, const P* wo,
+                       double bo_plus_bias, const int* perm_atom, double* atom_energy);
+template <typename P>
+void launch_fit_seed(cudaStream_t st, int Mmax, const int* range, int N, const P* wo, const P* th, P* dy, P* dz);
+// dX = dZ W^T (+ dY_next if residual); if th_prev: dz_prev = dX * (1 - th_prev^2).
+template <typename P>
+void launch_fit_backward_layer(cudaStream_t st, int Mmax, const int* range, int Nin, int Nout, const P* dZ,
+                               const P* W, const P* dY_next, P* dX, const P* th_prev, P* dZ_prev);
+
+void launch_assemble(cudaStream_t st, int nloc, int nall, int selt, const int* nl_j, const double* gslot,
+                     const double* rij, const int* rev_start, const int* rev_slot, double* force,
+                     double* atom_virial, double* virial_rows);
+// Deterministic column sums of rows [n][C] into out[C] (fixed reduction tree).
+void launch_reduce_rows(cudaStream_t st, int n, int C, const double* rows, double* partial, double* out);
+constexpr int kReduceBlocks = 148;
+
+}  // namespace b200dp

@@ -1,0 +1,163 @@
+/*
+ * b200dp — B200-native DPA4C-style energy / force / virial evaluation.
+ *
+ * C ABI of the force-evaluation hot path.  Plain pointers and sizes only; no
+ * C++ or torch types cross this boundary, and no exception leaves it: every
+ * call returns a b200dp_status and the engine keeps a readable message.
+ *
+ * Interfaces this header replaces (paths inside the reference project):
+ *
+ *  - DeePMD C++ API, DeepPot::compute(ener, force, virial, atom_energy,
+ *    atom_virial, coord, atype, box[, nghost, lmp_list, ago])
+ *    components/deepmd-op/overlays/api_cc/include/DeepPot.h:605-690
+ *      -> b200dp_compute_host / b200dp_compute_host_nlist
+ *  - DeepPot::compute_canonical_graph_gpu (device pointers, caller's stream)
+ *    components/deepmd-op/overlays/api_cc/include/DeepPot.h:903-915
+ *      -> b200dp_compute_device
+ *  - extern "C" dpa_direct_energy_force(atype, row_ptr, source, edge_vec,
+ *    node_count, nloc, edge_storage, energy, force, virial)
+ *    components/deepmd-op/overlays/op/pt/dpa4c/graph_compress.cu:1817-1902
+ *      -> b200dp_direct_energy_force (same argument meaning and return
+ *         convention: 1 = handled, 0 = caller must fall back)
+ *  - DeepPotPTExpt::init (model load and priming)
+ *    components/deepmd-op/overlays/api_cc/src/DeepPotPTExpt.cc:324
+ *      -> b200dp_create
+ *
+ * Units follow DeePMD/LAMMPS metal units: Angstrom, eV, eV/Angstrom.
+ * Virial: 9 components, row-major, W[a][b] = sum over edges of -g_a * r_b
+ * (g = dE/dr_ij, r_ij = x_j - x_i); the atom virial of an edge belongs to the
+ * neighbour j, as in the reference's edge assembly
+ * (components/deepmd-op/overlays/op/pt/edge_force_virial.cu:8-11).
+ */
+#ifndef B200DP_H
+#define B200DP_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum b200dp_status {
+  B200DP_OK = 0,
+  B200DP_ERR_INVALID = 1,      /* bad argument (null pointer, negative size, ...) */
+  B200DP_ERR_IO = 2,           /* model file missing or malformed */
+  B200DP_ERR_CUDA = 3,         /* a CUDA runtime call failed; see b200dp_last_error */
+  B200DP_ERR_SEL_OVERFLOW = 4, /* a type section held more neighbours than sel (only
+                                  when b200dp_options.sel_overflow_is_error != 0;
+                                  otherwise the nearest sel are kept, as DeePMD does) */
+  B200DP_ERR_CAPACITY = 5,     /* a centre had more in-cutoff candidates than the
+                                  builder's per-centre buffer */
+  B200DP_ERR_BAD_TYPE = 6,     /* an atom type outside [0, ntypes) */
+  B200DP_ERR_UNSUPPORTED = 7   /* configuration this build does not handle */
+} b200dp_status;
+
+typedef enum b200dp_precision {
+  B200DP_FP64 = 0,  /* every stage in fp64 */
+  B200DP_MIXED = 1  /* fp64 geometry and accumulation, fp32 networks */
+} b200dp_precision;
+
+typedef struct b200dp_options {
+  int precision;              /* b200dp_precision */
+  int device;                 /* CUDA device ordinal */
+  int sel_overflow_is_error;  /* 0: truncate to sel like DeePMD; 1: report B200DP_ERR_SEL_OVERFLOW */
+  int reserved[13];
+} b200dp_options;
+
+typedef struct b200dp_model_info {
+  int ntypes;
+  int sel_total;
+  int descriptor_dim;
+  int embedding_out;  /* M1 */
+  int axis;           /* M2 */
+  int n_embedding_layers;
+  int n_fitting_layers;
+  int type_one_side;
+  double rcut;
+  double rcut_smth;
+} b200dp_model_info;
+
+/* LAMMPS-style full neighbour list (DeePMD's InputNlist: inum, ilist,
+ * numneigh, firstneigh).  Candidates may include skin neighbours; the
+ * engine re-applies the cutoff and the per-type sel ordering. */
+typedef struct b200dp_nlist {
+  int inum;
+  const int* ilist;
+  const int* numneigh;
+  const int* const* firstneigh;
+} b200dp_nlist;
+
+typedef struct b200dp_engine b200dp_engine;
+
+void b200dp_options_default(b200dp_options* opt);
+
+/* Loads a model file and prepares device-resident weights. */
+b200dp_status b200dp_create(const char* model_path, const b200dp_options* opt, b200dp_engine** out);
+void b200dp_destroy(b200dp_engine* engine);
+const char* b200dp_last_error(const b200dp_engine* engine);
+b200dp_status b200dp_model_info_get(const b200dp_engine* engine, b200dp_model_info* out);
+
+/* Host buffers in and out (synchronous).  nghost == 0 with a box: periodic
+ * system, every periodic image is a neighbour candidate.  nghost > 0: atoms
+ * [nlocal, nlocal+nghost) are ghosts (LAMMPS convention), no periodic images
+ * are generated, and forces / atom virials are returned for all nlocal+nghost
+ * atoms so the caller can fold ghost forces back (reverse communication).
+ * coord [nall*3], atype [nall], box [9] (rows are cell vectors; may be NULL
+ * when nghost > 0).  force [nall*3], virial [9], atom_energy [nlocal] and
+ * atom_virial [nall*9] (both optional, may be NULL). */
+b200dp_status b200dp_compute_host(b200dp_engine* engine, int nlocal, int nghost, const double* coord,
+                                  const int* atype, const double* box, double* energy, double* force,
+                                  double* virial, double* atom_energy, double* atom_virial);
+
+/* As b200dp_compute_host, with the caller's LAMMPS full neighbour list
+ * (indices into [0, nall)); nghost atoms are ghosts.  Mirrors
+ * DeepPot::compute(..., nghost, lmp_list, ago). */
+b200dp_status b200dp_compute_host_nlist(b200dp_engine* engine, int nlocal, int nghost, const double* coord,
+                                        const int* atype, const b200dp_nlist* nlist, double* energy,
+                                        double* force, double* virial, double* atom_energy,
+                                        double* atom_virial);
+
+/* Device buffers, work enqueued on `stream` (a cudaStream_t; NULL = legacy
+ * default stream).  No host synchronisation: device-side error counters are
+ * read by b200dp_check.  box and region are HOST arrays (9 and 6 doubles):
+ * region = {lo_x, lo_y, lo_z, hi_x, hi_y, hi_z} bounds the binning grid in
+ * ghost mode (atoms outside it are still handled correctly, only slower); it
+ * may be NULL in periodic mode.  The call is capture-safe once a call of the
+ * same or larger size has run (buffers only grow outside capture). */
+b200dp_status b200dp_compute_device(b200dp_engine* engine, void* stream, int nlocal, int nghost,
+                                    const double* d_coord, const int* d_atype, const double* box,
+                                    const double* region, double* d_energy, double* d_force,
+                                    double* d_virial, double* d_atom_energy, double* d_atom_virial);
+
+/* Synchronises the engine's last stream and converts device error counters
+ * into a status (B200DP_ERR_SEL_OVERFLOW / _CAPACITY / _BAD_TYPE). */
+b200dp_status b200dp_check(b200dp_engine* engine);
+
+/* Number of neighbour candidates the last call dropped because a type
+ * section exceeded sel (synchronises). */
+long long b200dp_sel_overflow_count(b200dp_engine* engine);
+
+/* The canonical neighbour list of the last call, copied to host: nlist and
+ * image [nlocal*sel_total] (j index or -1; image code ((n0+512)<<20 |
+ * (n1+512)<<10 | (n2+512))), rij [nlocal*sel_total*3].  Any pointer may be
+ * NULL.  For parity tests and debugging. */
+b200dp_status b200dp_last_nlist(b200dp_engine* engine, int* nlist, int* image, double* rij);
+
+/* Descriptor and its energy gradient of the last call, [nlocal * descriptor_dim]
+ * in atom order, widened to fp64. */
+b200dp_status b200dp_last_descriptor(b200dp_engine* engine, double* descriptor, double* grad_descriptor);
+
+/* Per-stage device times of the last call in milliseconds (CUDA events on
+ * the launch stream): [0] neighbour build, [1] descriptor forward,
+ * [2] fitting, [3] descriptor backward, [4] force/virial assembly.
+ * Timing is enabled by b200dp_set_stage_timing(engine, 1). */
+b200dp_status b200dp_set_stage_timing(b200dp_engine* engine, int enable);
+/* Total kernels this library has launched in the process (all engines). */
+long long b200dp_kernel_launches(void);
+b200dp_status b200dp_stage_times(b200dp_engine* engine, float* ms5);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200DP_H */
