@@ -30,7 +30,7 @@ EXPORTS = [
     "b200dp_options_default", "b200dp_create", "b200dp_destroy", "b200dp_last_error", "b200dp_model_info_get",
     "b200dp_compute_host", "b200dp_compute_host_nlist", "b200dp_compute_device", "b200dp_check",
     "b200dp_sel_overflow_count", "b200dp_last_nlist", "b200dp_last_descriptor", "b200dp_set_stage_timing",
-    "b200dp_stage_times", "b200dp_kernel_launches",
+    "b200dp_stage_times", "b200dp_kernel_launches", "b200dp_selftest_mma",
 ]
 
 
@@ -42,7 +42,7 @@ class B200DPError(RuntimeError):
 
 class Options(ctypes.Structure):
     _fields_ = [("precision", ctypes.c_int), ("device", ctypes.c_int), ("sel_overflow_is_error", ctypes.c_int),
-                ("reserved", ctypes.c_int * 13)]
+                ("simt_only", ctypes.c_int), ("reserved", ctypes.c_int * 12)]
 
 
 class ModelInfo(ctypes.Structure):
@@ -91,6 +91,9 @@ def load_library(path: str = LIB_PATH):
     L.b200dp_last_descriptor.argtypes = [_vp, _dp, _dp]
     L.b200dp_set_stage_timing.argtypes = [_vp, ctypes.c_int]
     L.b200dp_stage_times.argtypes = [_vp, ctypes.POINTER(ctypes.c_float)]
+    L.b200dp_selftest_mma.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                      ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_float),
+                                      ctypes.POINTER(ctypes.c_float)]
     L.b200dp_kernel_launches.argtypes = []
     L.b200dp_kernel_launches.restype = ctypes.c_longlong
     for name in EXPORTS:
@@ -106,13 +109,15 @@ def _p(a, t):
 class DeepPot:
     """One engine = one model on one device with one precision."""
 
-    def __init__(self, model_path: str, precision: int = MIXED, device: int = 0, sel_overflow_is_error: bool = False):
+    def __init__(self, model_path: str, precision: int = MIXED, device: int = 0, sel_overflow_is_error: bool = False,
+                 simt_only: bool = False):
         L = load_library()
         o = Options()
         L.b200dp_options_default(ctypes.byref(o))
         o.precision = precision
         o.device = device
         o.sel_overflow_is_error = int(sel_overflow_is_error)
+        o.simt_only = int(simt_only)
         h = _vp()
         rc = L.b200dp_create(model_path.encode(), ctypes.byref(o), ctypes.byref(h))
         if rc != 0:
@@ -202,6 +207,21 @@ class DeepPot:
         ms = (ctypes.c_float * 5)()
         self._raise(self.L.b200dp_stage_times(self.h, ms))
         return list(ms)
+
+
+def selftest_mma(A, B, passes=3, a_mn_major=False, b_mn_major=False):
+    """C = A @ B.T on the tensor cores (bf16 split, 1 or 3 products); A [128,K], B [N,K]."""
+    A = np.ascontiguousarray(A, dtype=np.float32)
+    B = np.ascontiguousarray(B, dtype=np.float32)
+    K = A.shape[1]
+    N = B.shape[0]
+    C = np.zeros((128, N), np.float32)
+    fp = ctypes.POINTER(ctypes.c_float)
+    rc = load_library().b200dp_selftest_mma(K, N, int(a_mn_major), int(b_mn_major), passes, A.ctypes.data_as(fp),
+                                            B.ctypes.data_as(fp), C.ctypes.data_as(fp))
+    if rc != 0:
+        raise B200DPError(rc, "tcgen05 self-test failed")
+    return C
 
 
 def kernel_launches() -> int:

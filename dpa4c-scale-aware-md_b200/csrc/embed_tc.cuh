@@ -1,0 +1,55 @@
+// Tensor-core (tcgen05) embedding path of the mixed-precision mode.
+//
+// Edges are compacted into one list per embedding net (net q = neighbour type,
+// or centre type * ntypes + neighbour type for two-sided models), ordered by
+// the centre's row in the type-grouped atom order.  A tile is 128 consecutive
+// edges of one list.  Per tile the embedding layers 2 and 3 run as tcgen05
+// MMAs (bf16 hi/lo split, three products, fp32 accumulation in TMEM) and the
+// contraction T^T = G^T R~ runs as a third MMA whose B operand holds each
+// edge's environment row in the column block of its centre atom.  Partial T
+// of the atoms a tile touches are written per (net, atom, piece); a combine
+// kernel sums them in a fixed order, so results are run-to-run identical.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <vector>
+
+#include "model.hpp"
+#include "sea.cuh"
+
+namespace b200dp {
+
+// Embedding widths that have a tensor-core instantiation (three layers).
+bool tc_supported(const SeaDev& s);
+// Bytes of one packed net (B operands in UMMA layout + fp32 w1, b1, b2, b3).
+size_t tc_net_bytes(const SeaDev& s);
+// Packs one embedding net on the host.
+void tc_pack_net(const SeaDev& s, const std::vector<HostLayer>& net, std::vector<unsigned char>& out);
+// Maximum pieces a (net, atom) contraction can be split into.
+int tc_pieces(const SeaDev& s);
+
+struct TcLists {
+  int nloc, nnets, pieces;
+  const int* eoff;  // [nnets*nloc + 1] exclusive scan of per-(net,row) edge counts
+  const int* tstart;  // [nnets + 1] first global tile of each list
+  const float4* rt;   // [E] environment row (s, s x/r, s y/r, s z/r)
+  const int* row;     // [E] centre row in type-grouped order
+  const int* slot;    // [E] slot in the formatted neighbour list
+};
+
+void launch_edge_count(cudaStream_t st, const SeaDev& s, int nloc, const int* type_start, const int* perm_atom,
+                       const int* atype, const int* cnt, int* ecount);
+void launch_edge_compact(cudaStream_t st, const SeaDev& s, int nloc, const int* type_start, const int* perm_atom,
+                         const int* atype, const int* cnt, const double* rij, const int* eoff, float4* rt, int* row,
+                         int* slot);
+void launch_tile_table(cudaStream_t st, int nnets, int nloc, const int* eoff, int* tstart);
+int embed_tc_grid(const SeaDev& s);
+void launch_embed_fwd_tc(cudaStream_t st, const SeaDev& s, const TcLists& L, int grid, const unsigned char* nets,
+                         float* partial, int* err);
+void launch_t_combine(cudaStream_t st, const SeaDev& s, const TcLists& L, const int* type_start, const int* perm_atom,
+                      const float* partial, float* T, float* D);
+// Device error slot written by the tensor-core kernels when a bounded wait expires.
+constexpr int kErrTcTimeout = 3;
+
+}  // namespace b200dp

@@ -9,6 +9,7 @@
 // force / widen (components/deepmd-op/overlays/op/pt/dpa4c/graph_compress.cu:1690-1900).
 #include <algorithm>
 #include <atomic>
+#include <type_traits>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -159,6 +160,18 @@ b200dp_status Engine::init(const char* path, const b200dp_options* o) {
   }
   maxfit = 1;
   for (int v : hm.fit) maxfit = std::max(maxfit, v);
+  use_tc = !fp64 && !opt.simt_only && tc_supported(sd);
+  if (use_tc) {
+    const size_t nb = tc_net_bytes(sd);
+    std::vector<unsigned char> all(nb * sd.nnets), one;
+    for (int n = 0; n < sd.nnets; ++n) {
+      tc_pack_net(sd, hm.emb_nets[n], one);
+      std::memcpy(all.data() + n * nb, one.data(), nb);
+    }
+    B200DP_CUDA_TRY(tc_nets.ensure(all.size()));
+    B200DP_CUDA_TRY(cudaMemcpy(tc_nets.ptr, all.data(), all.size(), cudaMemcpyHostToDevice));
+    tc_pieces_n = tc_pieces(sd);
+  }
   cap = std::max(256, ((2 * s.selt + 31) / 32) * 32);
   B200DP_CUDA_TRY(cudaStreamCreateWithFlags(&own_stream, cudaStreamNonBlocking));
   for (auto& ev : events) B200DP_CUDA_TRY(cudaEventCreate(&ev));
@@ -181,7 +194,8 @@ void Engine::release() {
                     &nl_code, &nl_rij, &nl_cnt, &rev_count, &rev_start, &rev_cursor, &rev_tmp, &rev_slot,
                     &blk_counts, &type_start, &perm_pos, &perm_atom, &Tbuf, &Dbuf, &dDbuf, &atom_e, &gslot,
                     &vrows, &err_buf, &reduce_part, &scalars, &h_coord, &h_atype, &h_force, &h_aviral, &h_ae,
-                    &cand_start, &cand_list, &ilist_d})
+                    &cand_start, &cand_list, &ilist_d, &tc_nets, &ecount, &eoff, &tstart, &rec_rt, &rec_row,
+                    &rec_slot, &partial, &scan_scratch})
     b->release();
   for (auto& v : fit_w)
     for (auto& b : v) b.release();
@@ -237,6 +251,18 @@ b200dp_status Engine::ensure_buffers(int nloc, int nall, int ncells, int ncand) 
   B200DP_CUDA_TRY(gslot.ensure(sizeof(double) * 3 * S));
   B200DP_CUDA_TRY(vrows.ensure(sizeof(double) * 9 * A));
   if (ncand > 0) B200DP_CUDA_TRY(cand_list.ensure(sizeof(int) * (size_t)ncand));
+  const size_t nscan = std::max({(size_t)C, A, (size_t)sd.nnets * L}) + 1;
+  B200DP_CUDA_TRY(scan_scratch.ensure(sizeof(int) * scan_scratch_ints((int)nscan)));
+  if (use_tc) {
+    const size_t NL = (size_t)sd.nnets * L;
+    B200DP_CUDA_TRY(ecount.ensure(sizeof(int) * (NL + 1)));
+    B200DP_CUDA_TRY(eoff.ensure(sizeof(int) * (NL + 1)));
+    B200DP_CUDA_TRY(tstart.ensure(sizeof(int) * (sd.nnets + 1)));
+    B200DP_CUDA_TRY(rec_rt.ensure(sizeof(float4) * S));
+    B200DP_CUDA_TRY(rec_row.ensure(sizeof(int) * S));
+    B200DP_CUDA_TRY(rec_slot.ensure(sizeof(int) * S));
+    B200DP_CUDA_TRY(partial.ensure(sizeof(float) * NL * tc_pieces_n * 4 * sd.M1));
+  }
   return B200DP_OK;
 }
 
@@ -322,13 +348,29 @@ b200dp_status Engine::run_model(cudaStream_t st, int nloc, int nall, const int* 
                                 double* d_atom_energy, double* d_atom_virial, double* d_energy, double* d_virial) {
   int* err_d = static_cast<int*>(err_buf.ptr);
   launch_reverse_index(st, nloc, nall, sd.selt, nl_j.as<int>(), rev_count.as<int>(), rev_start.as<int>(),
-                       rev_cursor.as<int>(), rev_tmp.as<int>(), rev_slot.as<int>());
+                       rev_cursor.as<int>(), rev_tmp.as<int>(), rev_slot.as<int>(), scan_scratch.as<int>());
   launch_type_partition(st, nloc, hm.ntypes, d_atype, blk_counts.as<int>(), type_start.as<int>(),
                         perm_pos.as<int>(), perm_atom.as<int>(), err_d);
   mark(st, 1);
-  const int gf = descriptor_grid<P>(sd, ch_fwd, false, nloc);
-  launch_descriptor_fwd<P>(st, sd, nloc, ch_fwd, gf, nl_rij.as<double>(), nl_cnt.as<int>(), d_atype,
-                           perm_pos.as<int>(), w_emb.as<P>(), Tbuf.as<P>(), Dbuf.as<P>());
+  if (std::is_same<P, float>::value && use_tc) {
+    const int NL = sd.nnets * nloc;
+    launch_edge_count(st, sd, nloc, type_start.as<int>(), perm_atom.as<int>(), d_atype, nl_cnt.as<int>(),
+                      ecount.as<int>());
+    launch_exclusive_scan(st, NL, ecount.as<int>(), eoff.as<int>(), scan_scratch.as<int>());
+    launch_edge_compact(st, sd, nloc, type_start.as<int>(), perm_atom.as<int>(), d_atype, nl_cnt.as<int>(),
+                        nl_rij.as<double>(), eoff.as<int>(), rec_rt.as<float4>(), rec_row.as<int>(),
+                        rec_slot.as<int>());
+    launch_tile_table(st, sd.nnets, nloc, eoff.as<int>(), tstart.as<int>());
+    TcLists Lst{nloc, sd.nnets, tc_pieces_n, eoff.as<int>(), tstart.as<int>(), rec_rt.as<float4>(),
+                rec_row.as<int>(), rec_slot.as<int>()};
+    launch_embed_fwd_tc(st, sd, Lst, embed_tc_grid(sd), tc_nets.as<unsigned char>(), partial.as<float>(), err_d);
+    launch_t_combine(st, sd, Lst, type_start.as<int>(), perm_atom.as<int>(), partial.as<float>(),
+                     reinterpret_cast<float*>(Tbuf.ptr), reinterpret_cast<float*>(Dbuf.ptr));
+  } else {
+    const int gf = descriptor_grid<P>(sd, ch_fwd, false, nloc);
+    launch_descriptor_fwd<P>(st, sd, nloc, ch_fwd, gf, nl_rij.as<double>(), nl_cnt.as<int>(), d_atype,
+                             perm_pos.as<int>(), w_emb.as<P>(), Tbuf.as<P>(), Dbuf.as<P>());
+  }
   mark(st, 2);
   // fitting, per centre type over its row range [type_start[t], type_start[t+1])
   const int nfl = (int)hm.fit.size();
@@ -416,7 +458,7 @@ b200dp_status Engine::compute_device(cudaStream_t st, int nloc, int nghost, cons
   B200DP_CUDA_TRY(cudaMemsetAsync(cell_count.ptr, 0, sizeof(int) * g.ncells, st));
   B200DP_CUDA_TRY(cudaMemsetAsync(cell_cursor.ptr, 0, sizeof(int) * g.ncells, st));
   launch_bin(st, nall, d_coord, g, xw.as<double>(), cell_of.as<int>(), cell_count.as<int>());
-  launch_exclusive_scan(st, g.ncells, cell_count.as<int>(), cell_start.as<int>());
+  launch_exclusive_scan(st, g.ncells, cell_count.as<int>(), cell_start.as<int>(), scan_scratch.as<int>());
   launch_fill_cells(st, nall, cell_of.as<int>(), cell_start.as<int>(), cell_cursor.as<int>(), cell_atoms.as<int>());
   launch_format(st, format_spec(nloc, nall), g, xw.as<double>(), d_atype, cell_of.as<int>(), cell_start.as<int>(),
                 cell_atoms.as<int>(), nl_j.as<int>(), nl_code.as<int>(), nl_rij.as<double>(), nl_cnt.as<int>(), err_d);
@@ -438,6 +480,10 @@ b200dp_status Engine::check() {
   if (h[kErrBadType]) {
     err = "atom type outside [0, ntypes)";
     return B200DP_ERR_BAD_TYPE;
+  }
+  if (h[kErrTcTimeout]) {
+    err = "a tensor-core stage gave up waiting for its MMA (bounded wait expired)";
+    return B200DP_ERR_CUDA;
   }
   if (h[kErrCandCapacity]) {
     err = "a centre had more in-cutoff candidates than the builder buffer";

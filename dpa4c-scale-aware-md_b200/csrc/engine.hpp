@@ -8,6 +8,7 @@
 #include <vector>
 
 #include "../../include/b200dp.h"
+#include "embed_tc.cuh"
 #include "model.hpp"
 #include "nlist.cuh"
 #include "sea.cuh"
@@ -49,6 +50,10 @@ struct Engine {
   DevBuf rev_count, rev_start, rev_cursor, rev_tmp, rev_slot;
   DevBuf blk_counts, type_start, perm_pos, perm_atom;
   DevBuf cand_start, cand_list, ilist_d;
+  // tensor-core embedding path (mixed mode)
+  bool use_tc = false;
+  int tc_pieces_n = 0;
+  DevBuf tc_nets, ecount, eoff, tstart, rec_rt, rec_row, rec_slot, partial, scan_scratch;
   // model activations
   DevBuf Tbuf, Dbuf, dDbuf;
   std::vector<DevBuf> th_l, y_l;

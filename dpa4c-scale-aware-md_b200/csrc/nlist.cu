@@ -130,9 +130,71 @@ __global__ void __launch_bounds__(1024) k_exclusive_scan(int n, const int* __res
   if (tid == 0) out[n] = carry;
 }
 
-void launch_exclusive_scan(cudaStream_t st, int n, const int* in, int* out) {
+// Multi-block exclusive scan: tile sums, a single-block scan of the sums, and
+// a per-tile scan that adds the tile's offset (fixed order, deterministic).
+constexpr int kScanTile = 4096;
+
+__global__ void __launch_bounds__(1024) k_scan_tile_sums(int n, const int* __restrict__ in, int* __restrict__ sums) {
+  __shared__ int warp_tot[32];
+  const int base = blockIdx.x * kScanTile;
+  int local = 0;
+  for (int i = base + threadIdx.x; i < min(n, base + kScanTile); i += 1024) local += in[i];
+  local = warp_sum(local);
+  if ((threadIdx.x & 31) == 0) warp_tot[threadIdx.x >> 5] = local;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    int v = warp_sum(warp_tot[threadIdx.x]);
+    if (threadIdx.x == 0) sums[blockIdx.x] = v;
+  }
+}
+
+__global__ void __launch_bounds__(1024) k_scan_tile_apply(int n, const int* __restrict__ in,
+                                                          const int* __restrict__ offs, int* __restrict__ out) {
+  __shared__ int warp_ex[32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int i0 = blockIdx.x * kScanTile + tid * 4;
+  int v[4], local = 0;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    v[q] = (i0 + q < n) ? in[i0 + q] : 0;
+    local += v[q];
+  }
+  int wt;
+  const int ex = warp_exclusive_scan(local, lane, wt);
+  if (lane == 0) warp_ex[warp] = wt;
+  __syncthreads();
+  if (warp == 0) {
+    const int mine = warp_ex[lane];
+    int tot;
+    warp_ex[lane] = warp_exclusive_scan(mine, lane, tot);
+  }
+  __syncthreads();
+  int run = offs[blockIdx.x] + warp_ex[warp] + ex;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    if (i0 + q < n) out[i0 + q] = run;
+    run += v[q];
+  }
+  if (blockIdx.x == gridDim.x - 1 && tid == 0) out[n] = offs[gridDim.x];
+}
+
+size_t scan_scratch_ints(int n) { return 2 * ((size_t)n / kScanTile + 2); }
+
+void launch_exclusive_scan(cudaStream_t st, int n, const int* in, int* out, int* scratch) {
+  const int nb = (n + kScanTile - 1) / kScanTile;
+  if (nb <= 8 || scratch == nullptr) {
+    count_launch();
+    k_exclusive_scan<<<1, 1024, 0, st>>>(n, in, out);
+    return;
+  }
+  int* sums = scratch;
+  int* offs = scratch + nb + 1;
   count_launch();
-  k_exclusive_scan<<<1, 1024, 0, st>>>(n, in, out);
+  k_scan_tile_sums<<<nb, 1024, 0, st>>>(n, in, sums);
+  count_launch();
+  k_exclusive_scan<<<1, 1024, 0, st>>>(nb, sums, offs);
+  count_launch();
+  k_scan_tile_apply<<<nb, 1024, 0, st>>>(n, in, offs, out);
 }
 
 __global__ void k_fill_cells(int nall, const int* __restrict__ cell_of, const int* __restrict__ cell_start,
@@ -465,7 +527,7 @@ __global__ void __launch_bounds__(kRevWarps * 32)
 }
 
 void launch_reverse_index(cudaStream_t st, int nloc, int nall, int selt, const int* nl_j, int* rev_count,
-                          int* rev_start, int* rev_cursor, int* rev_tmp, int* rev_slot) {
+                          int* rev_start, int* rev_cursor, int* rev_tmp, int* rev_slot, int* scan_scratch) {
   const long long nslots = (long long)nloc * selt;
   cudaMemsetAsync(rev_count, 0, sizeof(int) * (size_t)nall, st);
   cudaMemsetAsync(rev_cursor, 0, sizeof(int) * (size_t)nall, st);
@@ -473,11 +535,11 @@ void launch_reverse_index(cudaStream_t st, int nloc, int nall, int selt, const i
     const int blocks = (int)std::min<long long>((nslots + 255) / 256, 148 * 16);
     count_launch();
     k_rev_count<<<blocks, 256, 0, st>>>(nslots, nl_j, rev_count);
-    launch_exclusive_scan(st, nall, rev_count, rev_start);
+    launch_exclusive_scan(st, nall, rev_count, rev_start, scan_scratch);
     count_launch();
     k_rev_fill<<<blocks, 256, 0, st>>>(nslots, nl_j, rev_start, rev_cursor, rev_tmp);
   } else {
-    launch_exclusive_scan(st, nall, rev_count, rev_start);
+    launch_exclusive_scan(st, nall, rev_count, rev_start, scan_scratch);
   }
   if (nall > 0) {
     count_launch();

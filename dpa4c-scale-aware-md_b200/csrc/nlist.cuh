@@ -40,7 +40,10 @@ void make_box_inverse(const double* box, double* Binv, double* width);
 // Launchers; all enqueue on `st`.
 void launch_bin(cudaStream_t st, int nall, const double* coord, const GridSpec& g, double* xw, int* cell_of,
                 int* cell_count);
-void launch_exclusive_scan(cudaStream_t st, int n, const int* in, int* out);
+// Exclusive scan of n ints into out[0..n] (out[n] = total).  scratch holds
+// scan_scratch_ints(n) ints; with scratch == nullptr a single block is used.
+void launch_exclusive_scan(cudaStream_t st, int n, const int* in, int* out, int* scratch);
+size_t scan_scratch_ints(int n);
 void launch_fill_cells(cudaStream_t st, int nall, const int* cell_of, const int* cell_start, int* cursor,
                        int* cell_atoms);
 size_t format_smem_bytes(int cap);
@@ -52,7 +55,7 @@ void launch_format_candidates(cudaStream_t st, const FormatSpec& f, const double
                               const int* ilist, const int* cand_start, const int* cand, int* nl_j, int* nl_code,
                               double* nl_rij, int* nl_cnt, int* err);
 void launch_reverse_index(cudaStream_t st, int nloc, int nall, int selt, const int* nl_j, int* rev_count,
-                          int* rev_start, int* rev_cursor, int* rev_tmp, int* rev_slot);
+                          int* rev_start, int* rev_cursor, int* rev_tmp, int* rev_slot, int* scan_scratch);
 void launch_type_partition(cudaStream_t st, int nloc, int ntypes, const int* atype, int* blk_counts,
                            int* type_start, int* perm_pos, int* perm_atom, int* err);
 size_t type_partition_blocks(int nloc);

@@ -61,7 +61,8 @@ typedef struct b200dp_options {
   int precision;              /* b200dp_precision */
   int device;                 /* CUDA device ordinal */
   int sel_overflow_is_error;  /* 0: truncate to sel like DeePMD; 1: report B200DP_ERR_SEL_OVERFLOW */
-  int reserved[13];
+  int simt_only;              /* 1: never use the tensor-core kernels (mixed mode uses SIMT fp32) */
+  int reserved[12];
 } b200dp_options;
 
 typedef struct b200dp_model_info {
@@ -152,6 +153,12 @@ b200dp_status b200dp_last_descriptor(b200dp_engine* engine, double* descriptor, 
  * [2] fitting, [3] descriptor backward, [4] force/virial assembly.
  * Timing is enabled by b200dp_set_stage_timing(engine, 1). */
 b200dp_status b200dp_set_stage_timing(b200dp_engine* engine, int enable);
+/* Self-test of the tensor-core (tcgen05) layer: C[128 x N] = A[128 x K] *
+ * B[N x K]^T from host fp32 arrays, bf16 split with 1 or 3 products,
+ * operands in K-major or MN-major layout.  K, N multiples of 16, K <= 256,
+ * 16 <= N <= 256.  Synchronous; allocates its own device buffers. */
+b200dp_status b200dp_selftest_mma(int K, int N, int a_mn_major, int b_mn_major, int passes, const float* A,
+                                  const float* B, float* C);
 /* Total kernels this library has launched in the process (all engines). */
 long long b200dp_kernel_launches(void);
 b200dp_status b200dp_stage_times(b200dp_engine* engine, float* ms5);

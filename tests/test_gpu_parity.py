@@ -235,3 +235,22 @@ def test_device_entry_on_torch_stream(engines, model_dir):
     dp.check()
     assert float(e.item()) == host["energy"]
     np.testing.assert_array_equal(f.cpu().numpy(), host["force"])
+
+
+@pytest.mark.parametrize("name", ["water192", "cu108", "alloy128", "water192_two_side"])
+def test_tensor_core_descriptor_matches_simt(model_dir, name):
+    """The tcgen05 embedding path and the SIMT fp32 path give the same descriptor."""
+    g, meta = golden(name)
+    path = golden_model_path(model_dir, meta)
+    tc = b200dp.DeepPot(path, precision=b200dp.MIXED)
+    simt = b200dp.DeepPot(path, precision=b200dp.MIXED, simt_only=True)
+    n = len(g["atype"])
+    rt = tc.compute(g["coord"], g["atype"], g["box"])
+    rs = simt.compute(g["coord"], g["atype"], g["box"])
+    d_tc, _ = tc.last_descriptor(n)
+    d_s, _ = simt.last_descriptor(n)
+    assert rel(d_tc, d_s) < 2e-5
+    assert abs(rt["energy"] - rs["energy"]) <= 2e-5 * abs(rs["energy"])
+    assert rel(rt["force"], rs["force"]) < 2e-4
+    tc.close()
+    simt.close()
