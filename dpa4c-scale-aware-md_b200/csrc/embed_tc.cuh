@@ -49,6 +49,13 @@ void launch_embed_fwd_tc(cudaStream_t st, const SeaDev& s, const TcLists& L, int
                          float* partial, int* err);
 void launch_t_combine(cudaStream_t st, const SeaDev& s, const TcLists& L, const int* type_start, const int* perm_atom,
                       const float* partial, float* T, float* D);
+// dE/dT per centre row (scaled by 1/N) from T (atom order) and dE/dD (row order).
+void launch_dT(cudaStream_t st, const SeaDev& s, int nloc, const int* type_start, const int* perm_atom, const float* T,
+               const float* dD, float* dT);
+// Embedding backward: recomputes the forward per tile, then dG, dR~, the
+// layer backprop on tensor cores and the chain rule to r_ij (fp64) -> gslot.
+void launch_embed_bwd_tc(cudaStream_t st, const SeaDev& s, const TcLists& L, int grid, const unsigned char* nets,
+                         const float* dT, const double* rij, double* gslot, int* err);
 // Device error slot written by the tensor-core kernels when a bounded wait expires.
 constexpr int kErrTcTimeout = 3;
 

@@ -195,7 +195,7 @@ void Engine::release() {
                     &blk_counts, &type_start, &perm_pos, &perm_atom, &Tbuf, &Dbuf, &dDbuf, &atom_e, &gslot,
                     &vrows, &err_buf, &reduce_part, &scalars, &h_coord, &h_atype, &h_force, &h_aviral, &h_ae,
                     &cand_start, &cand_list, &ilist_d, &tc_nets, &ecount, &eoff, &tstart, &rec_rt, &rec_row,
-                    &rec_slot, &partial, &scan_scratch})
+                    &rec_slot, &partial, &scan_scratch, &dTbuf})
     b->release();
   for (auto& v : fit_w)
     for (auto& b : v) b.release();
@@ -262,6 +262,7 @@ b200dp_status Engine::ensure_buffers(int nloc, int nall, int ncells, int ncand) 
     B200DP_CUDA_TRY(rec_row.ensure(sizeof(int) * S));
     B200DP_CUDA_TRY(rec_slot.ensure(sizeof(int) * S));
     B200DP_CUDA_TRY(partial.ensure(sizeof(float) * NL * tc_pieces_n * 4 * sd.M1));
+    B200DP_CUDA_TRY(dTbuf.ensure(sizeof(float) * L * 4 * sd.M1));
   }
   return B200DP_OK;
 }
@@ -409,10 +410,19 @@ b200dp_status Engine::run_model(cudaStream_t st, int nloc, int nall, const int* 
     }
   }
   mark(st, 3);
-  const int gb = descriptor_grid<P>(sd, ch_bwd, true, nloc);
-  launch_descriptor_bwd<P>(st, sd, nloc, ch_bwd, gb, nl_rij.as<double>(), nl_cnt.as<int>(), d_atype,
-                           perm_pos.as<int>(), w_emb.as<P>(), w_embT.as<P>(), Tbuf.as<P>(), dDbuf.as<P>(),
-                           gslot.as<double>());
+  if (std::is_same<P, float>::value && use_tc) {
+    TcLists Lst{nloc, sd.nnets, tc_pieces_n, eoff.as<int>(), tstart.as<int>(), rec_rt.as<float4>(),
+                rec_row.as<int>(), rec_slot.as<int>()};
+    launch_dT(st, sd, nloc, type_start.as<int>(), perm_atom.as<int>(), reinterpret_cast<const float*>(Tbuf.ptr),
+              reinterpret_cast<const float*>(dDbuf.ptr), dTbuf.as<float>());
+    launch_embed_bwd_tc(st, sd, Lst, embed_tc_grid(sd), tc_nets.as<unsigned char>(), dTbuf.as<float>(),
+                        nl_rij.as<double>(), gslot.as<double>(), err_d);
+  } else {
+    const int gb = descriptor_grid<P>(sd, ch_bwd, true, nloc);
+    launch_descriptor_bwd<P>(st, sd, nloc, ch_bwd, gb, nl_rij.as<double>(), nl_cnt.as<int>(), d_atype,
+                             perm_pos.as<int>(), w_emb.as<P>(), w_embT.as<P>(), Tbuf.as<P>(), dDbuf.as<P>(),
+                             gslot.as<double>());
+  }
   mark(st, 4);
   launch_assemble(st, nloc, nall, sd.selt, nl_j.as<int>(), gslot.as<double>(), nl_rij.as<double>(),
                   rev_start.as<int>(), rev_slot.as<int>(), d_force, d_atom_virial, vrows.as<double>());

@@ -53,7 +53,7 @@ struct Engine {
   // tensor-core embedding path (mixed mode)
   bool use_tc = false;
   int tc_pieces_n = 0;
-  DevBuf tc_nets, ecount, eoff, tstart, rec_rt, rec_row, rec_slot, partial, scan_scratch;
+  DevBuf tc_nets, ecount, eoff, tstart, rec_rt, rec_row, rec_slot, partial, scan_scratch, dTbuf;
   // model activations
   DevBuf Tbuf, Dbuf, dDbuf;
   std::vector<DevBuf> th_l, y_l;

@@ -87,6 +87,7 @@ extern "C" b200dp_status b200dp_selftest_mma(int K, int N, int a_mn_major, int b
   using namespace b200dp;
   if (K < 16 || K > 256 || K % 16 || N < 16 || N > 256 || N % 16 || (passes != 1 && passes != 3) || !A || !B || !C)
     return B200DP_ERR_INVALID;
+  if ((size_t)4 * K * (128 + N) > 200 * 1024) return B200DP_ERR_INVALID;  // operands must fit in shared memory
   float *dA = nullptr, *dB = nullptr, *dC = nullptr;
   int* dErr = nullptr;
   b200dp_status st = B200DP_OK;

@@ -156,7 +156,8 @@ b200dp_status b200dp_set_stage_timing(b200dp_engine* engine, int enable);
 /* Self-test of the tensor-core (tcgen05) layer: C[128 x N] = A[128 x K] *
  * B[N x K]^T from host fp32 arrays, bf16 split with 1 or 3 products,
  * operands in K-major or MN-major layout.  K, N multiples of 16, K <= 256,
- * 16 <= N <= 256.  Synchronous; allocates its own device buffers. */
+ * 16 <= N <= 256, 4*K*(128+N) <= 200 KiB.  Synchronous; allocates its own
+ * device buffers. */
 b200dp_status b200dp_selftest_mma(int K, int N, int a_mn_major, int b_mn_major, int passes, const float* A,
                                   const float* B, float* C);
 /* Total kernels this library has launched in the process (all engines). */
