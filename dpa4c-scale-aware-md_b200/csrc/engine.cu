@@ -171,6 +171,56 @@ b200dp_status Engine::init(const char* path, const b200dp_options* o) {
     B200DP_CUDA_TRY(tc_nets.ensure(all.size()));
     B200DP_CUDA_TRY(cudaMemcpy(tc_nets.ptr, all.data(), all.size(), cudaMemcpyHostToDevice));
     tc_pieces_n = tc_pieces(sd);
+    fplan = fit_tc_plan(hm);
+    use_fit_tc = fplan.ok;
+  }
+  if (use_fit_tc) {
+    fitw.resize(hm.ntypes);
+    fit_dev.reserve((size_t)hm.ntypes * (4 * kFitMaxLayers + kFitMaxLayers + 1));
+    auto up_bytes = [&](const std::vector<unsigned char>& v) -> const unsigned char* {
+      fit_dev.emplace_back();
+      DevBuf& d = fit_dev.back();
+      if (d.ensure(v.size()) != cudaSuccess) return nullptr;
+      cudaMemcpy(d.ptr, v.data(), v.size(), cudaMemcpyHostToDevice);
+      return static_cast<const unsigned char*>(d.ptr);
+    };
+    auto up_f = [&](const std::vector<double>& v) -> const float* {
+      std::vector<float> f(v.begin(), v.end());
+      fit_dev.emplace_back();
+      DevBuf& d = fit_dev.back();
+      if (d.ensure(f.size() * 4) != cudaSuccess) return nullptr;
+      cudaMemcpy(d.ptr, f.data(), f.size() * 4, cudaMemcpyHostToDevice);
+      return static_cast<const float*>(d.ptr);
+    };
+    for (int t = 0; t < hm.ntypes; ++t) {
+      const auto& net = hm.fit_nets[t];
+      FitTcWeights& W = fitw[t];
+      std::vector<unsigned char> hi, lo;
+      for (int l = 0; l < fplan.L; ++l) {
+        const HostLayer& Lr = net[l];
+        const int din = Lr.din, dout = Lr.dout;
+        fit_pack_B(dout, fplan.kpad[l], dout,
+                   [&](int n, int k) { return k < din ? Lr.w[(size_t)k * dout + n] : 0.0; }, hi, lo);
+        W.fB_hi[l] = up_bytes(hi);
+        W.fB_lo[l] = up_bytes(lo);
+        const int kp = (dout + 31) / 32 * 32;
+        fit_pack_B(din, kp, l == 0 ? fplan.bn_out : din,
+                   [&](int n, int k) { return k < dout ? Lr.w[(size_t)n * dout + k] : 0.0; }, hi, lo);
+        W.bB_hi[l] = up_bytes(hi);
+        W.bB_lo[l] = up_bytes(lo);
+        W.bias[l] = up_f(Lr.b);
+        if (!W.fB_hi[l] || !W.fB_lo[l] || !W.bB_hi[l] || !W.bB_lo[l] || !W.bias[l]) {
+          err = "cannot upload fitting weights";
+          return B200DP_ERR_CUDA;
+        }
+      }
+      W.wo = up_f(net[fplan.L].w);
+      W.bo = net[fplan.L].b[0] + hm.bias_atom_e[t];
+      if (!W.wo) {
+        err = "cannot upload fitting weights";
+        return B200DP_ERR_CUDA;
+      }
+    }
   }
   cap = std::max(256, ((2 * s.selt + 31) / 32) * 32);
   B200DP_CUDA_TRY(cudaStreamCreateWithFlags(&own_stream, cudaStreamNonBlocking));
@@ -195,12 +245,17 @@ void Engine::release() {
                     &blk_counts, &type_start, &perm_pos, &perm_atom, &Tbuf, &Dbuf, &dDbuf, &atom_e, &gslot,
                     &vrows, &err_buf, &reduce_part, &scalars, &h_coord, &h_atype, &h_force, &h_aviral, &h_ae,
                     &cand_start, &cand_list, &ilist_d, &tc_nets, &ecount, &eoff, &tstart, &rec_rt, &rec_row,
-                    &rec_slot, &partial, &scan_scratch, &dTbuf})
+                    &rec_slot, &partial, &scan_scratch, &dTbuf, &ftile})
     b->release();
   for (auto& v : fit_w)
     for (auto& b : v) b.release();
   for (auto& v : fit_b)
     for (auto& b : v) b.release();
+  for (auto& b : fit_dev) b.release();
+  for (auto* arr : {&At_hi, &At_lo, &THf, &Yf})
+    for (auto& b : *arr) b.release();
+  for (auto* arr : {&Z_hi, &Z_lo, &DYf})
+    for (auto& b : *arr) b.release();
   for (auto& b : th_l) b.release();
   for (auto& b : y_l) b.release();
   for (auto& b : dy_l) b.release();
@@ -263,6 +318,29 @@ b200dp_status Engine::ensure_buffers(int nloc, int nall, int ncells, int ncand) 
     B200DP_CUDA_TRY(rec_slot.ensure(sizeof(int) * S));
     B200DP_CUDA_TRY(partial.ensure(sizeof(float) * NL * tc_pieces_n * 4 * sd.M1));
     B200DP_CUDA_TRY(dTbuf.ensure(sizeof(float) * L * 4 * sd.M1));
+  }
+  if (use_fit_tc) {
+    const size_t rp = 128 * ((L + 127) / 128 + sd.ntypes);
+    B200DP_CUDA_TRY(ftile.ensure(sizeof(int) * (sd.ntypes + 1)));
+    auto grow_zero = [&](DevBuf& b, size_t bytes) -> cudaError_t {
+      void* before = b.ptr;
+      cudaError_t e = b.ensure(bytes);
+      if (e == cudaSuccess && b.ptr != before) e = cudaMemset(b.ptr, 0, b.bytes);  // zero K padding once
+      return e;
+    };
+    for (int l = 0; l < fplan.L; ++l) {
+      const size_t tb = tiled_bytes(rp, fplan.kpad[l]);
+      B200DP_CUDA_TRY(grow_zero(At_hi[l], tb));
+      B200DP_CUDA_TRY(grow_zero(At_lo[l], tb));
+      B200DP_CUDA_TRY(THf[l].ensure(sizeof(float) * rp * fplan.width[l]));
+      B200DP_CUDA_TRY(Yf[l].ensure(sizeof(float) * rp * fplan.width[l]));
+    }
+    for (int q = 0; q < 2; ++q) {
+      B200DP_CUDA_TRY(grow_zero(Z_hi[q], tiled_bytes(rp, 256)));
+      B200DP_CUDA_TRY(grow_zero(Z_lo[q], tiled_bytes(rp, 256)));
+      B200DP_CUDA_TRY(DYf[q].ensure(sizeof(float) * rp * 256));
+    }
+    fit_rows_padded = rp;
   }
   return B200DP_OK;
 }
@@ -373,40 +451,62 @@ b200dp_status Engine::run_model(cudaStream_t st, int nloc, int nall, const int* 
                              perm_pos.as<int>(), w_emb.as<P>(), Tbuf.as<P>(), Dbuf.as<P>());
   }
   mark(st, 2);
-  // fitting, per centre type over its row range [type_start[t], type_start[t+1])
-  const int nfl = (int)hm.fit.size();
-  for (int t = 0; t < hm.ntypes; ++t) {
-    const int* range = type_start.as<int>() + t;
-    const P* x = Dbuf.as<P>();
-    int dx = sd.dim;
-    for (int l = 0; l < nfl; ++l) {
-      const int dout = hm.fit[l];
-      const bool res = (l >= 1 && dout == dx);
-      launch_fit_forward_layer<P>(st, nloc, range, dout, dx, x, dx, fit_w[t][l].as<P>(), fit_b[t][l].as<P>(), res,
-                                  th_l[l].as<P>(), y_l[l].as<P>());
-      x = y_l[l].as<P>();
-      dx = dout;
+  if (std::is_same<P, float>::value && use_fit_tc) {
+    FitTcBuffers fb;
+    std::memset(&fb, 0, sizeof(fb));
+    fb.rows_padded = fit_rows_padded;
+    for (int l = 0; l < fplan.L; ++l) {
+      fb.At_hi[l] = At_hi[l].as<unsigned char>();
+      fb.At_lo[l] = At_lo[l].as<unsigned char>();
+      fb.TH[l] = THf[l].as<float>();
+      fb.Y[l] = Yf[l].as<float>();
     }
-    launch_fit_energy<P>(st, nloc, range, dx, x, fit_w[t][nfl].as<P>(), fit_bo[t], perm_atom.as<int>(),
-                         atom_e.as<double>());
-    // backward: dy_L = w_out, dz_{L-1} = w_out * (1 - th^2)
-    int cur = 0;
-    launch_fit_seed<P>(st, nloc, range, dx, fit_w[t][nfl].as<P>(), th_l[nfl - 1].as<P>(), dy_l[cur].as<P>(),
-                       dz_l[cur].as<P>());
-    for (int l = nfl - 1; l >= 0; --l) {
-      const int din = (l == 0) ? sd.dim : hm.fit[l - 1];
-      const int dout = hm.fit[l];
-      const bool res = (l >= 1 && dout == din);
-      const int nxt = cur ^ 1;
-      if (l == 0) {
-        launch_fit_backward_layer<P>(st, nloc, range, din, dout, dz_l[cur].as<P>(), fit_w[t][l].as<P>(),
-                                     res ? dy_l[cur].as<P>() : nullptr, dDbuf.as<P>(), nullptr, nullptr);
-      } else {
-        launch_fit_backward_layer<P>(st, nloc, range, din, dout, dz_l[cur].as<P>(), fit_w[t][l].as<P>(),
-                                     res ? dy_l[cur].as<P>() : nullptr, dy_l[nxt].as<P>(), th_l[l - 1].as<P>(),
-                                     dz_l[nxt].as<P>());
+    for (int q = 0; q < 2; ++q) {
+      fb.Z_hi[q] = Z_hi[q].as<unsigned char>();
+      fb.Z_lo[q] = Z_lo[q].as<unsigned char>();
+      fb.DY[q] = DYf[q].as<float>();
+    }
+    launch_fit_tile_table(st, hm.ntypes, type_start.as<int>(), ftile.as<int>());
+    launch_fit_tile_D(st, nloc, hm.ntypes, sd.dim, type_start.as<int>(), ftile.as<int>(),
+                      reinterpret_cast<const float*>(Dbuf.ptr), fb.At_hi[0], fb.At_lo[0]);
+    launch_fit_tc(st, fplan, hm.ntypes, nloc, type_start.as<int>(), ftile.as<int>(), perm_atom.as<int>(),
+                  fitw.data(), fb, atom_e.as<double>(), reinterpret_cast<float*>(dDbuf.ptr), err_d);
+  } else {
+    // fitting, per centre type over its row range [type_start[t], type_start[t+1])
+    const int nfl = (int)hm.fit.size();
+    for (int t = 0; t < hm.ntypes; ++t) {
+      const int* range = type_start.as<int>() + t;
+      const P* x = Dbuf.as<P>();
+      int dx = sd.dim;
+      for (int l = 0; l < nfl; ++l) {
+        const int dout = hm.fit[l];
+        const bool res = (l >= 1 && dout == dx);
+        launch_fit_forward_layer<P>(st, nloc, range, dout, dx, x, dx, fit_w[t][l].as<P>(), fit_b[t][l].as<P>(), res,
+                                    th_l[l].as<P>(), y_l[l].as<P>());
+        x = y_l[l].as<P>();
+        dx = dout;
       }
-      cur = nxt;
+      launch_fit_energy<P>(st, nloc, range, dx, x, fit_w[t][nfl].as<P>(), fit_bo[t], perm_atom.as<int>(),
+                           atom_e.as<double>());
+      // backward: dy_L = w_out, dz_{L-1} = w_out * (1 - th^2)
+      int cur = 0;
+      launch_fit_seed<P>(st, nloc, range, dx, fit_w[t][nfl].as<P>(), th_l[nfl - 1].as<P>(), dy_l[cur].as<P>(),
+                         dz_l[cur].as<P>());
+      for (int l = nfl - 1; l >= 0; --l) {
+        const int din = (l == 0) ? sd.dim : hm.fit[l - 1];
+        const int dout = hm.fit[l];
+        const bool res = (l >= 1 && dout == din);
+        const int nxt = cur ^ 1;
+        if (l == 0) {
+          launch_fit_backward_layer<P>(st, nloc, range, din, dout, dz_l[cur].as<P>(), fit_w[t][l].as<P>(),
+                                       res ? dy_l[cur].as<P>() : nullptr, dDbuf.as<P>(), nullptr, nullptr);
+        } else {
+          launch_fit_backward_layer<P>(st, nloc, range, din, dout, dz_l[cur].as<P>(), fit_w[t][l].as<P>(),
+                                       res ? dy_l[cur].as<P>() : nullptr, dy_l[nxt].as<P>(), th_l[l - 1].as<P>(),
+                                       dz_l[nxt].as<P>());
+        }
+        cur = nxt;
+      }
     }
   }
   mark(st, 3);

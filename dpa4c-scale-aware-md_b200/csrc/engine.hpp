@@ -9,6 +9,7 @@
 
 #include "../../include/b200dp.h"
 #include "embed_tc.cuh"
+#include "fit_tc.cuh"
 #include "model.hpp"
 #include "nlist.cuh"
 #include "sea.cuh"
@@ -54,6 +55,15 @@ struct Engine {
   bool use_tc = false;
   int tc_pieces_n = 0;
   DevBuf tc_nets, ecount, eoff, tstart, rec_rt, rec_row, rec_slot, partial, scan_scratch, dTbuf;
+  // tensor-core fitting (mixed mode)
+  bool use_fit_tc = false;
+  FitTcPlan fplan;
+  std::vector<FitTcWeights> fitw;
+  std::vector<DevBuf> fit_dev;  // owns every pre-tiled weight array
+  DevBuf ftile;
+  std::array<DevBuf, kFitMaxLayers> At_hi, At_lo, THf, Yf;
+  std::array<DevBuf, 2> Z_hi, Z_lo, DYf;
+  size_t fit_rows_padded = 0;
   // model activations
   DevBuf Tbuf, Dbuf, dDbuf;
   std::vector<DevBuf> th_l, y_l;

@@ -1,0 +1,425 @@
+// Tensor-core fitting net (see fit_tc.cuh).
+#include <algorithm>
+#include <cstring>
+#include <functional>
+
+#include "common.cuh"
+#include "fit_tc.cuh"
+#include "umma.cuh"
+
+namespace b200dp {
+
+namespace {
+
+constexpr int kStages = 4;
+constexpr uint32_t kABlock = 128 * kFitBK * 2;  // one half of a 128 x 32 activation block (8 KB)
+constexpr uint32_t kSbo = (kFitBK / 8) * 128;    // K-major SBO inside a block (512 B)
+constexpr long long kWaitLimit = 1LL << 26;
+
+__device__ __forceinline__ float tanh_fast(float x) { return 1.0f - __fdividef(2.0f, __expf(2.0f * x) + 1.0f); }
+
+// Byte offset of element (row, k) of a tiled activation with kpad columns.
+__device__ __forceinline__ size_t tiled_off(int prow, int k, int kpad) {
+  const int rt = prow >> 7, r = prow & 127;
+  return ((size_t)rt * (kpad / kFitBK) + k / kFitBK) * kABlock + (uint32_t)(r >> 3) * kSbo +
+         (uint32_t)((k % kFitBK) >> 3) * 128 + (uint32_t)(r & 7) * 16 + (uint32_t)(k & 7) * 2;
+}
+
+__device__ __forceinline__ void store8_split(unsigned char* hi, unsigned char* lo, const float* v) {
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    __nv_bfloat16 h0, l0, h1, l1;
+    umma::split_bf16(v[2 * j], h0, l0);
+    umma::split_bf16(v[2 * j + 1], h1, l1);
+    h[j] = umma::pack2(h0, h1);
+    l[j] = umma::pack2(l0, l1);
+  }
+  *reinterpret_cast<uint4*>(hi) = make_uint4(h[0], h[1], h[2], h[3]);
+  *reinterpret_cast<uint4*>(lo) = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+enum Mode : int { kFwd = 0, kBwd = 1, kBwdFinal = 2 };
+
+struct GemmArgs {
+  int ntypes;
+  const int* type_start;
+  const int* ftile;
+  int nk;  // K chunks of 32
+  const unsigned char* A_hi;
+  const unsigned char* A_lo;
+  const unsigned char* B_hi[kMaxTypes];
+  const unsigned char* B_lo[kMaxTypes];
+  int BN, N;
+  int mode;
+  // forward
+  const float* bias[kMaxTypes];
+  const float* Yprev;
+  int ldprev;
+  float* TH;
+  float* Y;
+  unsigned char* Anext_hi;
+  unsigned char* Anext_lo;
+  int kpad_next;
+  int last;
+  const float* wo[kMaxTypes];
+  double bo[kMaxTypes];
+  const int* perm_atom;
+  double* atom_e;
+  unsigned char* Z_hi;
+  unsigned char* Z_lo;
+  int kpad_z;
+  // backward
+  const float* DYnext;
+  int dy_is_wo;
+  float* DYout;
+  const float* THprev;
+  float* dD;
+  int* err;
+};
+
+__global__ void __launch_bounds__(128, 1) k_fit_gemm(GemmArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem[];
+  __shared__ uint64_t full[kStages], empty[kStages], done;
+  __shared__ uint32_t tbase;
+  __shared__ int s_ok;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int g = blockIdx.x, nt = blockIdx.y;
+  if (g >= a.ftile[a.ntypes]) return;  // CTA-uniform, before any TMEM allocation
+  int t = 0;
+  while (t + 1 < a.ntypes && a.ftile[t + 1] <= g) ++t;
+  const int row0 = a.type_start[t] + 128 * (g - a.ftile[t]);
+  const int nrows = min(128, a.type_start[t + 1] - row0);
+  const uint32_t BB = (uint32_t)a.BN * kFitBK * 2;
+  const uint32_t SB = 2 * kABlock + 2 * BB;
+  if (warp == 0) umma::tmem_alloc(&tbase, 256);
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      umma::mbar_init(&full[s], 1);
+      umma::mbar_init(&empty[s], 1);
+    }
+    umma::mbar_init(&done, 1);
+    umma::fence_mbar_init();
+    s_ok = 1;
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tm = tbase;
+  if (tid == 0) {
+    const uint32_t idesc = umma::idesc_bf16(128, a.BN, false, false);
+    const unsigned char* Ah = a.A_hi + (size_t)g * a.nk * kABlock;
+    const unsigned char* Al = a.A_lo + (size_t)g * a.nk * kABlock;
+    const unsigned char* Bh = a.B_hi[t] + (size_t)nt * a.nk * BB;
+    const unsigned char* Bl = a.B_lo[t] + (size_t)nt * a.nk * BB;
+    auto load = [&](int kc) {
+      const int s = kc % kStages;
+      unsigned char* st = smem + s * SB;
+      umma::mbar_expect_tx(&full[s], SB);
+      umma::bulk_g2s(st, Ah + (size_t)kc * kABlock, kABlock, &full[s]);
+      umma::bulk_g2s(st + kABlock, Al + (size_t)kc * kABlock, kABlock, &full[s]);
+      umma::bulk_g2s(st + 2 * kABlock, Bh + (size_t)kc * BB, BB, &full[s]);
+      umma::bulk_g2s(st + 2 * kABlock + BB, Bl + (size_t)kc * BB, BB, &full[s]);
+    };
+    for (int kc = 0; kc < min(kStages, a.nk); ++kc) load(kc);
+    bool ok = true;
+    for (int kc = 0; kc < a.nk && ok; ++kc) {
+      const int s = kc % kStages;
+      ok = umma::mbar_wait(&full[s], (kc / kStages) & 1, kWaitLimit);
+      if (!ok) break;
+      umma::fence_after_sync();
+      const uint32_t st = umma::smem_u32(smem + s * SB);
+      const uint32_t ah = st, al = st + kABlock, bh = st + 2 * kABlock, bl = st + 2 * kABlock + BB;
+#pragma unroll
+      for (int ks = 0; ks < kFitBK / 16; ++ks) {
+        const uint32_t o = ks * 256;
+        umma::mma(tm, umma::desc(ah + o, 128, kSbo), umma::desc(bh + o, 128, kSbo), idesc, (kc | ks) ? 1u : 0u);
+        umma::mma(tm, umma::desc(ah + o, 128, kSbo), umma::desc(bl + o, 128, kSbo), idesc, 1u);
+        umma::mma(tm, umma::desc(al + o, 128, kSbo), umma::desc(bh + o, 128, kSbo), idesc, 1u);
+      }
+      umma::commit(&empty[s]);
+      if (kc >= 1) {
+        const int j = kc - 1 + kStages;
+        if (j < a.nk) {
+          const int sp = (kc - 1) % kStages;
+          ok = umma::mbar_wait(&empty[sp], ((kc - 1) / kStages) & 1, kWaitLimit);
+          if (ok) load(j);
+        }
+      }
+    }
+    umma::commit(&done);
+    if (!ok) s_ok = 0;
+  }
+  const bool ok = umma::mbar_wait(&done, 0, kWaitLimit);
+  if (__syncthreads_or(!ok || !s_ok)) {
+    if (tid == 0) atomicAdd(a.err + 3, 1);
+  } else {
+    umma::fence_after_sync();
+    const int r = tid;  // row within the tile (TMEM lane)
+    const bool valid = r < nrows;
+    const int prow = g * 128 + r;     // padded row
+    const int urow = row0 + r;        // row in type-grouped order
+    const uint32_t lb = (uint32_t)(warp * 32) << 16;
+    double e_acc = 0.0;
+    for (int c = 0; c < a.BN / 16; ++c) {
+      float v[16];
+      umma::ld16(tm + lb + c * 16, v);
+      umma::wait_ld();
+      if (!valid) continue;
+      const int col0 = nt * a.BN + c * 16;
+      if (a.mode == kFwd) {
+        float y[16], zs[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int col = col0 + j;
+          const float th = tanh_fast(v[j] + a.bias[t][col]);
+          float yy = th;
+          if (a.Yprev) yy += a.Yprev[(size_t)prow * a.ldprev + col];
+          a.TH[(size_t)prow * a.N + col] = th;
+          a.Y[(size_t)prow * a.N + col] = yy;
+          y[j] = yy;
+          if (a.last) {
+            const float w = a.wo[t][col];
+            e_acc += (double)(yy * w);
+            zs[j] = w * (1.f - th * th);
+          }
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int k = col0 + 8 * h;
+          if (a.last) {
+            const size_t o = tiled_off(prow, k, a.kpad_z);
+            store8_split(a.Z_hi + o, a.Z_lo + o, zs + 8 * h);
+          } else {
+            const size_t o = tiled_off(prow, k, a.kpad_next);
+            store8_split(a.Anext_hi + o, a.Anext_lo + o, y + 8 * h);
+          }
+        }
+      } else if (a.mode == kBwd) {
+        float z[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int col = col0 + j;
+          float d = v[j];
+          if (a.dy_is_wo)
+            d += a.wo[t][col];
+          else if (a.DYnext)
+            d += a.DYnext[(size_t)prow * a.N + col];
+          if (a.DYout) a.DYout[(size_t)prow * a.N + col] = d;
+          const float th = a.THprev[(size_t)prow * a.N + col];
+          z[j] = d * (1.f - th * th);
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const size_t o = tiled_off(prow, col0 + 8 * h, a.kpad_z);
+          store8_split(a.Z_hi + o, a.Z_lo + o, z + 8 * h);
+        }
+      } else {
+        float* dst = a.dD + (size_t)urow * a.N + col0;
+#pragma unroll
+        for (int j = 0; j < 16; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+      }
+    }
+    if (a.mode == kFwd && a.last && valid) a.atom_e[a.perm_atom[urow]] = e_acc + a.bo[t];
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) umma::tmem_dealloc(tm, 256);
+}
+
+__global__ void k_fit_tile_table(int ntypes, const int* __restrict__ type_start, int* __restrict__ ftile) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  int acc = 0;
+  ftile[0] = 0;
+  for (int t = 0; t < ntypes; ++t) {
+    acc += (type_start[t + 1] - type_start[t] + 127) / 128;
+    ftile[t + 1] = acc;
+  }
+}
+
+// One thread per (row, 8-column group) of D.
+__global__ void k_fit_tile_D(int nloc, int ntypes, int dim, const int* __restrict__ type_start,
+                             const int* __restrict__ ftile, const float* __restrict__ D, unsigned char* __restrict__ hi,
+                             unsigned char* __restrict__ lo) {
+  const int groups = dim / 8;
+  const size_t total = (size_t)type_start[ntypes] * groups;
+  for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total; idx += (size_t)gridDim.x * blockDim.x) {
+    const int r = (int)(idx / groups), kg = (int)(idx % groups);
+    int t = 0;
+    while (t + 1 < ntypes && type_start[t + 1] <= r) ++t;
+    const int prow = 128 * ftile[t] + (r - type_start[t]);
+    const float4* src = reinterpret_cast<const float4*>(D + (size_t)r * dim + kg * 8);
+    const float4 x0 = src[0], x1 = src[1];
+    const float v[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+    const size_t o = tiled_off(prow, kg * 8, dim);
+    store8_split(hi + o, lo + o, v);
+  }
+}
+
+int round32(int x) { return (x + 31) / 32 * 32; }
+
+}  // namespace
+
+FitTcPlan fit_tc_plan(const HostModel& m) {
+  FitTcPlan p;
+  p.L = (int)m.fit.size();
+  p.dim = m.dim();
+  if (p.L < 1 || p.L > kFitMaxLayers || p.dim % kFitBK != 0 || m.ntypes > kMaxTypes) return p;
+  int din = p.dim;
+  for (int l = 0; l < p.L; ++l) {
+    const int w = m.fit[l];
+    if (w % 16 != 0 || w > 256) return p;
+    p.width[l] = w;
+    p.kpad[l] = l == 0 ? p.dim : round32(m.fit[l - 1]);
+    p.res[l] = (l >= 1 && w == din) ? 1 : 0;
+    din = w;
+  }
+  p.bn_out = 0;
+  for (int bn = 256; bn >= 16; bn -= 16)
+    if (p.dim % bn == 0) {
+      p.bn_out = bn;
+      break;
+    }
+  p.ok = p.bn_out > 0;
+  return p;
+}
+
+void fit_pack_B(int N, int Kp, int BN, const std::function<double(int, int)>& val, std::vector<unsigned char>& hi,
+                std::vector<unsigned char>& lo) {
+  const int nkc = Kp / kFitBK;
+  const size_t bytes = (size_t)N * Kp * 2;
+  hi.assign(bytes, 0);
+  lo.assign(bytes, 0);
+  auto to_bf16 = [](float f) {
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    const uint32_t rnd = 0x7FFFu + ((u >> 16) & 1u);
+    return (uint16_t)((u + rnd) >> 16);
+  };
+  auto from_bf16 = [](uint16_t h) {
+    uint32_t u = (uint32_t)h << 16;
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+  };
+  for (int n = 0; n < N; ++n)
+    for (int k = 0; k < Kp; ++k) {
+      const float x = (float)val(n, k);
+      const uint16_t h = to_bf16(x);
+      const uint16_t l = to_bf16(x - from_bf16(h));
+      const int nt = n / BN, nn = n % BN;
+      const size_t o = ((size_t)nt * nkc + k / kFitBK) * ((size_t)BN * kFitBK * 2) + (size_t)(nn >> 3) * kSbo +
+                       (size_t)((k % kFitBK) >> 3) * 128 + (nn & 7) * 16 + (k & 7) * 2;
+      std::memcpy(&hi[o], &h, 2);
+      std::memcpy(&lo[o], &l, 2);
+    }
+}
+
+void launch_fit_tile_table(cudaStream_t st, int ntypes, const int* type_start, int* ftile) {
+  count_launch();
+  k_fit_tile_table<<<1, 32, 0, st>>>(ntypes, type_start, ftile);
+}
+
+void launch_fit_tile_D(cudaStream_t st, int nloc, int ntypes, int dim, const int* type_start, const int* ftile,
+                       const float* D, unsigned char* hi, unsigned char* lo) {
+  if (nloc <= 0) return;
+  const size_t total = (size_t)nloc * (dim / 8);
+  const int blocks = (int)std::min<size_t>((total + 255) / 256, 148 * 16);
+  count_launch();
+  k_fit_tile_D<<<blocks, 256, 0, st>>>(nloc, ntypes, dim, type_start, ftile, D, hi, lo);
+}
+
+static void run_gemm(cudaStream_t st, GemmArgs& a, int row_tiles, int ntn) {
+  const size_t smem = (size_t)kStages * (2 * kABlock + 2 * (size_t)a.BN * kFitBK * 2);
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k_fit_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    attr = true;
+  }
+  count_launch();
+  k_fit_gemm<<<dim3(row_tiles, ntn), 128, smem, st>>>(a);
+}
+
+void launch_fit_tc(cudaStream_t st, const FitTcPlan& p, int ntypes, int nloc, const int* type_start,
+                   const int* ftile, const int* perm_atom, const FitTcWeights* w, const FitTcBuffers& b,
+                   double* atom_energy, float* dD, int* err) {
+  if (nloc <= 0) return;
+  const int row_tiles = (nloc + 127) / 128 + ntypes;
+  const int L = p.L;
+  for (int l = 0; l < L; ++l) {
+    GemmArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.ntypes = ntypes;
+    a.type_start = type_start;
+    a.ftile = ftile;
+    a.nk = p.kpad[l] / kFitBK;
+    a.A_hi = b.At_hi[l];
+    a.A_lo = b.At_lo[l];
+    for (int t = 0; t < ntypes; ++t) {
+      a.B_hi[t] = w[t].fB_hi[l];
+      a.B_lo[t] = w[t].fB_lo[l];
+      a.bias[t] = w[t].bias[l];
+      a.wo[t] = w[t].wo;
+      a.bo[t] = w[t].bo;
+    }
+    a.BN = p.width[l];
+    a.N = p.width[l];
+    a.mode = kFwd;
+    a.Yprev = p.res[l] ? b.Y[l - 1] : nullptr;
+    a.ldprev = l > 0 ? p.width[l - 1] : 0;
+    a.TH = b.TH[l];
+    a.Y = b.Y[l];
+    a.last = (l == L - 1);
+    if (!a.last) {
+      a.Anext_hi = b.At_hi[l + 1];
+      a.Anext_lo = b.At_lo[l + 1];
+      a.kpad_next = p.kpad[l + 1];
+    } else {
+      a.Z_hi = b.Z_hi[0];
+      a.Z_lo = b.Z_lo[0];
+      a.kpad_z = round32(p.width[l]);
+      a.perm_atom = perm_atom;
+      a.atom_e = atom_energy;
+    }
+    a.err = err;
+    run_gemm(st, a, row_tiles, 1);
+  }
+  for (int s = 0; s < L; ++s) {
+    const int l = L - 1 - s;
+    GemmArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.ntypes = ntypes;
+    a.type_start = type_start;
+    a.ftile = ftile;
+    a.nk = round32(p.width[l]) / kFitBK;
+    a.A_hi = b.Z_hi[s & 1];
+    a.A_lo = b.Z_lo[s & 1];
+    for (int t = 0; t < ntypes; ++t) {
+      a.B_hi[t] = w[t].bB_hi[l];
+      a.B_lo[t] = w[t].bB_lo[l];
+      a.wo[t] = w[t].wo;
+    }
+    a.err = err;
+    if (l >= 1) {
+      a.BN = p.width[l - 1];
+      a.N = p.width[l - 1];
+      a.mode = kBwd;
+      a.dy_is_wo = (p.res[l] && l == L - 1) ? 1 : 0;
+      a.DYnext = (p.res[l] && l < L - 1) ? b.DY[s & 1] : nullptr;
+      a.DYout = p.res[l - 1] ? b.DY[(s + 1) & 1] : nullptr;
+      a.THprev = b.TH[l - 1];
+      a.Z_hi = b.Z_hi[(s + 1) & 1];
+      a.Z_lo = b.Z_lo[(s + 1) & 1];
+      a.kpad_z = round32(p.width[l - 1]);
+      run_gemm(st, a, row_tiles, 1);
+    } else {
+      a.BN = p.bn_out;
+      a.N = p.dim;
+      a.mode = kBwdFinal;
+      a.dD = dD;
+      run_gemm(st, a, row_tiles, p.dim / p.bn_out);
+    }
+  }
+}
+
+}  // namespace b200dp
