@@ -1,4 +1,4 @@
-// Tensor-core embedding forward (see embed_tc.cuh).
+// Tensor-core embedding forward and backward (see embed_tc.cuh).
 #include <algorithm>
 #include <cstring>
 
@@ -14,45 +14,31 @@ namespace {
 // saturates correctly at both ends (exp overflow -> 1, underflow -> -1).
 __device__ __forceinline__ float tanh_fast(float x) { return 1.0f - __fdividef(2.0f, __expf(2.0f * x) + 1.0f); }
 
+constexpr long long kWaitLimit = 1LL << 26;
+
+// Packed net blob (global memory and the front of shared memory):
+// [w2 hi|lo][w3 hi|lo][w1 b1 b2 b3 fp32].  W2 and W3 are stored as K-major B
+// operands of the forward MMAs: element (n, k) = W[k][n].
 template <int D1, int D2, int D3>
 struct TcShape {
   static constexpr int D1p = (D1 + 15) / 16 * 16;
   static constexpr int D2p = (D2 + 15) / 16 * 16;
   static constexpr int D3p = (D3 + 15) / 16 * 16;
-  static constexpr int NT = 32;  // contraction MMA columns: 8 atoms x 4 environment components
   static constexpr uint32_t W2B = D2p * D1p * 2;
   static constexpr uint32_t W3B = D3p * D2p * 2;
-  static constexpr uint32_t BUFB = 128 * 128 * 2;  // largest view: G^T, 128 (a) x 128 (edges)
-  static constexpr uint32_t RB = NT * 128 * 2;
-  static constexpr uint32_t NF = 2 * D1 + D2 + D3;  // w1, b1, b2, b3
-  // shared memory map (bytes); every block is a multiple of 16
+  static constexpr uint32_t NF = 2 * D1 + D2 + D3;
   static constexpr uint32_t O_W2 = 0;
   static constexpr uint32_t O_W3 = O_W2 + 2 * W2B;
   static constexpr uint32_t O_F = O_W3 + 2 * W3B;
-  static constexpr uint32_t O_BUF = ((O_F + NF * 4 + 1023) / 1024) * 1024;
-  static constexpr uint32_t O_R = O_BUF + 2 * BUFB;
-  static constexpr uint32_t SMEM = O_R + 2 * RB;
-  // packed net blob in global memory: [w2 hi|lo][w3 hi|lo][floats]
   static constexpr uint32_t BLOB = O_F + NF * 4;
-  // canonical no-swizzle layouts
-  static constexpr uint32_t SBO_A1 = (D1p / 8) * 128;  // K-major, K = D1p
-  static constexpr uint32_t SBO_A2 = (D2p / 8) * 128;  // K-major, K = D2p
+  static constexpr uint32_t O_END = ((BLOB + 1023) / 1024) * 1024;
   static constexpr uint32_t SBO_W2 = (D1p / 8) * 128;
   static constexpr uint32_t SBO_W3 = (D2p / 8) * 128;
-  static constexpr uint32_t LBO_G = (128 / 8) * 128, SBO_G = 128;  // MN-major, M = 128, K = 128
-  static constexpr uint32_t LBO_R = (NT / 8) * 128, SBO_R = 128;   // MN-major, N = NT, K = 128
-  // TMEM columns
-  static constexpr uint32_t C_D2 = 0, C_D3 = D2p, C_T = D2p + D3p, NCOLS = 256;
-  static_assert(C_T + NT <= NCOLS, "TMEM budget");
+  static constexpr uint32_t SBO_A1 = (D1p / 8) * 128;  // K-major activations, K = D1p
+  static constexpr uint32_t SBO_A2 = (D2p / 8) * 128;  // K-major activations, K = D2p
   static_assert(D1 > 2, "layer-1 residual is not handled by the tensor-core path");
+  static_assert(D1p <= 32 && D2p <= 64 && D3p <= 128, "widths of the tensor-core instantiations");
 };
-
-constexpr long long kWaitLimit = 1LL << 26;
-
-template <int D2>
-__host__ __device__ constexpr int D2p_of() {
-  return (D2 + 15) / 16 * 16;
-}
 
 template <int D2, int D1>
 __device__ __forceinline__ float resid_of(const float* x, int n) {
@@ -61,62 +47,100 @@ __device__ __forceinline__ float resid_of(const float* x, int n) {
   return 0.0f;
 }
 
-// Writes 8 consecutive fp32 values as bf16 hi and lo 16-byte chunks.
+// Writes 8 consecutive fp32 values as bf16 hi and lo 16-byte chunks (packed
+// round-to-nearest conversions, two values per instruction).
 __device__ __forceinline__ void store8_split(unsigned char* hi, unsigned char* lo, const float* v) {
   uint32_t h[4], l[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    __nv_bfloat16 h0, l0, h1, l1;
-    umma::split_bf16(v[2 * j], h0, l0);
-    umma::split_bf16(v[2 * j + 1], h1, l1);
-    h[j] = umma::pack2(h0, h1);
-    l[j] = umma::pack2(l0, l1);
+    const __nv_bfloat162 hh = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+    const float2 hf = __bfloat1622float2(hh);
+    const __nv_bfloat162 ll = __floats2bfloat162_rn(v[2 * j] - hf.x, v[2 * j + 1] - hf.y);
+    h[j] = *reinterpret_cast<const uint32_t*>(&hh);
+    l[j] = *reinterpret_cast<const uint32_t*>(&ll);
   }
   *reinterpret_cast<uint4*>(hi) = make_uint4(h[0], h[1], h[2], h[3]);
   *reinterpret_cast<uint4*>(lo) = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
-struct FwdArgs {
-  TcLists L;
-  const unsigned char* nets;
-  size_t net_bytes;
-  float* partial;
-  int* err;
-  int M1;
-};
-
-// Issues the three split products of one K=16 step pair (hi*hi, hi*lo, lo*hi).
+// The three split products of `steps` K=16 steps (hi*hi, hi*lo, lo*hi).
 __device__ __forceinline__ void mma3(uint32_t d, uint32_t a_hi, uint32_t a_lo, uint32_t b_hi, uint32_t b_lo,
                                      uint32_t lbo_a, uint32_t sbo_a, uint32_t lbo_b, uint32_t sbo_b, uint32_t idesc,
-                                     int steps, uint32_t step_a, uint32_t step_b) {
+                                     int steps, uint32_t step_a, uint32_t step_b, bool accumulate) {
   for (int s = 0; s < steps; ++s) {
     const uint32_t oa = s * step_a, ob = s * step_b;
-    umma::mma(d, umma::desc(a_hi + oa, lbo_a, sbo_a), umma::desc(b_hi + ob, lbo_b, sbo_b), idesc, s > 0 ? 1u : 0u);
+    umma::mma(d, umma::desc(a_hi + oa, lbo_a, sbo_a), umma::desc(b_hi + ob, lbo_b, sbo_b), idesc,
+              (accumulate || s > 0) ? 1u : 0u);
     umma::mma(d, umma::desc(a_hi + oa, lbo_a, sbo_a), umma::desc(b_lo + ob, lbo_b, sbo_b), idesc, 1u);
     umma::mma(d, umma::desc(a_lo + oa, lbo_a, sbo_a), umma::desc(b_hi + ob, lbo_b, sbo_b), idesc, 1u);
   }
 }
 
+// Work item -> (net, first row, end row) and its edge range.
+struct Item {
+  int q, rb, re, e0, e1;
+};
+__device__ __forceinline__ Item item_of(const TcLists& L, int it) {
+  Item r;
+  int q = 0;
+  while (q + 1 < L.nnets && L.istart[q + 1] <= it) ++q;
+  r.q = q;
+  int rb0 = 0, re0 = L.type_start[L.ntypes];
+  if (!L.type_one_side) {
+    const int ti = q / L.ntypes;
+    rb0 = L.type_start[ti];
+    re0 = L.type_start[ti + 1];
+  }
+  r.rb = rb0 + kItemRows * (it - L.istart[q]);
+  r.re = min(r.rb + kItemRows, re0);
+  r.e0 = L.eoff[(size_t)q * L.nloc + r.rb];
+  r.e1 = L.eoff[(size_t)q * L.nloc + r.re];
+  return r;
+}
+
+// ---------------------------------------------------------------- forward
 template <int D1, int D2, int D3>
-__global__ void __launch_bounds__(128, 1) k_embed_fwd_tc(FwdArgs a) {
-  using S = TcShape<D1, D2, D3>;
+struct Fwd {
+  using F = TcShape<D1, D2, D3>;
+  static constexpr int NT = 4 * kItemRows;           // contraction columns
+  static constexpr uint32_t A1B = 128 * F::D1p * 2;  // one bf16 half
+  static constexpr uint32_t XB = 128 * 64 * 2;       // A2 (K <= 64) or G^T half (M = 128 a, K = 64 edges)
+  static constexpr uint32_t RB = NT * 64 * 2;        // R~ half (N = 32, K = 64 edges)
+  static constexpr uint32_t O_A1 = F::O_END;
+  static constexpr uint32_t O_X = O_A1 + 2 * A1B;
+  static constexpr uint32_t O_R = O_X + 2 * XB;
+  static constexpr uint32_t SMEM = O_R + 2 * RB;
+  static constexpr uint32_t LBO_G = (128 / 8) * 128, SBO_G = 128;  // MN-major
+  static constexpr uint32_t LBO_R = (NT / 8) * 128, SBO_R = 128;   // MN-major
+  static constexpr uint32_t C_D2 = 0, C_D3 = 64, C_T = 192, NCOLS = 256;
+};
+
+struct FwdArgs {
+  TcLists L;
+  const unsigned char* nets;
+  size_t net_bytes;
+  float* Tq;
+  int* err;
+};
+
+template <int D1, int D2, int D3>
+__global__ void __launch_bounds__(128, 2) k_embed_fwd_tc(FwdArgs a) {
+  using F = TcShape<D1, D2, D3>;
+  using S = Fwd<D1, D2, D3>;
   extern __shared__ __align__(1024) unsigned char smem[];
   __shared__ uint64_t bar;
   __shared__ uint32_t tbase;
-  __shared__ int s_row[128];
-  __shared__ int s_lrow[128];
-  __shared__ int s_wcnt[4];
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const float* w1 = reinterpret_cast<const float*>(smem + S::O_F);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const float* w1 = reinterpret_cast<const float*>(smem + F::O_F);
   const float* b1 = w1 + D1;
   const float* b2 = b1 + D1;
   const float* b3 = b2 + D2;
-  unsigned char* w2h = smem + S::O_W2;
-  unsigned char* w2l = w2h + S::W2B;
-  unsigned char* w3h = smem + S::O_W3;
-  unsigned char* w3l = w3h + S::W3B;
-  unsigned char* bufh = smem + S::O_BUF;
-  unsigned char* bufl = bufh + S::BUFB;
+  const uint32_t w2h = umma::smem_u32(smem + F::O_W2), w2l = w2h + F::W2B;
+  const uint32_t w3h = umma::smem_u32(smem + F::O_W3), w3l = w3h + F::W3B;
+  unsigned char* a1h = smem + S::O_A1;
+  unsigned char* a1l = a1h + S::A1B;
+  unsigned char* xh = smem + S::O_X;
+  unsigned char* xl = xh + S::XB;
   unsigned char* rh = smem + S::O_R;
   unsigned char* rl = rh + S::RB;
   if (warp == 0) umma::tmem_alloc(&tbase, S::NCOLS);
@@ -128,179 +152,165 @@ __global__ void __launch_bounds__(128, 1) k_embed_fwd_tc(FwdArgs a) {
   __syncthreads();
   umma::fence_after_sync();
   const uint32_t tm = tbase;
-  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+  const uint32_t lb = (uint32_t)(warp * 32) << 16;
   uint32_t phase = 0;
   int loaded = -1;
   const TcLists& L = a.L;
-  const int ntiles = L.tstart[L.nnets];
-  const uint32_t idesc2 = umma::idesc_bf16(128, S::D2p, false, false);
-  const uint32_t idesc3 = umma::idesc_bf16(128, S::D3p, false, false);
-  const uint32_t idescT = umma::idesc_bf16(128, S::NT, true, true);
+  const int nitems = L.istart[L.nnets];
+  const uint32_t id2 = umma::idesc_bf16(128, F::D2p, false, false);
+  const uint32_t id3 = umma::idesc_bf16(128, F::D3p, false, false);
+  const uint32_t idT = umma::idesc_bf16(128, S::NT, true, true);
   bool aborted = false;
-  for (int g = blockIdx.x; g < ntiles && !aborted; g += gridDim.x) {
-    int q = 0;
-    while (q + 1 < L.nnets && L.tstart[q + 1] <= g) ++q;
-    const int kt = g - L.tstart[q];
-    const int lbase = L.eoff[(size_t)q * L.nloc];
-    const int lend = L.eoff[(size_t)(q + 1) * L.nloc];
-    const int e0 = lbase + kt * 128;
-    const int ne = min(128, lend - e0);
-    if (q != loaded) {
+  auto sync_mma = [&]() {
+    umma::fence_proxy_async();
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+  };
+  auto wait_mma = [&]() -> bool {
+    const bool ok = umma::mbar_wait(&bar, phase, kWaitLimit);
+    phase ^= 1;
+    if (__syncthreads_or(!ok)) return false;
+    umma::fence_after_sync();
+    return true;
+  };
+  for (int it = blockIdx.x; it < nitems && !aborted; it += gridDim.x) {
+    const Item I = item_of(L, it);
+    if (I.q != loaded) {
       __syncthreads();
-      const uint4* src = reinterpret_cast<const uint4*>(a.nets + (size_t)q * a.net_bytes);
+      const uint4* src = reinterpret_cast<const uint4*>(a.nets + (size_t)I.q * a.net_bytes);
       uint4* dst = reinterpret_cast<uint4*>(smem);
-      for (uint32_t i = tid; i < S::BLOB / 16; i += 128) dst[i] = src[i];
-      loaded = q;
+      for (uint32_t i = tid; i < F::BLOB / 16; i += 128) dst[i] = src[i];
+      loaded = I.q;
+      __syncthreads();
     }
-    // environment rows of this tile and the local rank of each edge's centre
-    const bool valid = tid < ne;
-    const float4 rt = valid ? L.rt[e0 + tid] : make_float4(0.f, 0.f, 0.f, 0.f);
-    const int row = valid ? L.row[e0 + tid] : -1;
-    s_row[tid] = row;
-    __syncthreads();
-    const bool first = valid && (tid == 0 || s_row[tid - 1] != row);
-    const unsigned fm = __ballot_sync(0xffffffffu, first);
-    if (lane == 0) s_wcnt[warp] = __popc(fm);
-    __syncthreads();
-    int before = 0;
-    for (int w = 0; w < warp; ++w) before += s_wcnt[w];
-    const int na = s_wcnt[0] + s_wcnt[1] + s_wcnt[2] + s_wcnt[3];
-    const unsigned le_mask = (lane == 31) ? 0xffffffffu : ((2u << lane) - 1u);
-    const int lr = valid ? before + __popc(fm & le_mask) - 1 : -1;
-    if (first) s_lrow[lr] = row;
-    // layer 1 (scalar input, elementwise) -> A1
-    float h1[D1];
+    bool first = true;
+    for (int sub = I.e0; sub < I.e1 && !aborted; sub += 128) {
+      const int ne = min(128, I.e1 - sub);
+      const bool valid = tid < ne;
+      const float4 rt = valid ? L.rt[sub + tid] : make_float4(0.f, 0.f, 0.f, 0.f);
+      const int rl_ = valid ? L.row[sub + tid] - I.rb : -1;
+      float h1[D1];
 #pragma unroll
-    for (int n = 0; n < D1; ++n) h1[n] = valid ? tanh_fast(rt.x * w1[n] + b1[n]) : 0.f;
+      for (int n = 0; n < D1; ++n) h1[n] = valid ? tanh_fast(rt.x * w1[n] + b1[n]) : 0.f;
 #pragma unroll
-    for (int kg = 0; kg < S::D1p / 8; ++kg) {
-      float v[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = (kg * 8 + j < D1) ? h1[kg * 8 + j] : 0.f;
-      const uint32_t o = (tid >> 3) * S::SBO_A1 + kg * 128 + (tid & 7) * 16;
-      store8_split(bufh + o, bufl + o, v);
-    }
-    umma::fence_proxy_async();
-    umma::fence_before_sync();
-    __syncthreads();
-    umma::fence_after_sync();
-    if (tid == 0) {
-      mma3(tm + S::C_D2, umma::smem_u32(bufh), umma::smem_u32(bufl), umma::smem_u32(w2h), umma::smem_u32(w2l), 128,
-           S::SBO_A1, 128, S::SBO_W2, idesc2, S::D1p / 16, 256, 256);
-      umma::commit(&bar);
-    }
-    bool ok = umma::mbar_wait(&bar, phase, kWaitLimit);
-    phase ^= 1;
-    if (__syncthreads_or(!ok)) {
-      aborted = true;
-      break;
-    }
-    umma::fence_after_sync();
-    // layer 2 epilogue -> A2 (overwrites A1; the MMA that read it has completed)
-    float h2[D2];
-#pragma unroll
-    for (int c = 0; c < S::D2p / 16; ++c) {
-      float v[16];
-      umma::ld16(tm + lane_base + S::C_D2 + c * 16, v);
-      umma::wait_ld();
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int n = c * 16 + j;
-        if (n < D2) h2[n] = valid ? tanh_fast(v[j] + b2[n]) + resid_of<D2, D1>(h1, n) : 0.f;
-      }
-    }
-#pragma unroll
-    for (int kg = 0; kg < S::D2p / 8; ++kg) {
-      float v[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = (kg * 8 + j < D2) ? h2[kg * 8 + j] : 0.f;
-      const uint32_t o = (tid >> 3) * S::SBO_A2 + kg * 128 + (tid & 7) * 16;
-      store8_split(bufh + o, bufl + o, v);
-    }
-    umma::fence_proxy_async();
-    umma::fence_before_sync();
-    __syncthreads();
-    umma::fence_after_sync();
-    if (tid == 0) {
-      mma3(tm + S::C_D3, umma::smem_u32(bufh), umma::smem_u32(bufl), umma::smem_u32(w3h), umma::smem_u32(w3l), 128,
-           S::SBO_A2, 128, S::SBO_W3, idesc3, S::D2p / 16, 256, 256);
-      umma::commit(&bar);
-    }
-    ok = umma::mbar_wait(&bar, phase, kWaitLimit);
-    phase ^= 1;
-    if (__syncthreads_or(!ok)) {
-      aborted = true;
-      break;
-    }
-    umma::fence_after_sync();
-    // layer 3 epilogue: G -> G^T (MN-major A operand of the contraction)
-#pragma unroll
-    for (int c = 0; c < S::D3p / 16; ++c) {
-      float v[16];
-      umma::ld16(tm + lane_base + S::C_D3 + c * 16, v);
-      umma::wait_ld();
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int n = c * 16 + j;
-        v[j] = (n < D3 && valid) ? tanh_fast(v[j] + b3[n]) + resid_of<D3, D2>(h2, n) : 0.f;
-      }
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const uint32_t o = (2 * c + h) * S::SBO_G + (tid >> 3) * S::LBO_G + (tid & 7) * 16;
-        store8_split(bufh + o, bufl + o, v + 8 * h);
-      }
-    }
-    // contraction T^T[a][4r+k] = sum_e G_e[a] rt_e[k] over the edges of local atom r
-    for (int ch = 0; ch * 8 < na; ++ch) {
-      const int rr = lr - 8 * ch;
-      const float rv[4] = {rt.x, rt.y, rt.z, rt.w};
-#pragma unroll
-      for (int ng = 0; ng < S::NT / 8; ++ng) {
+      for (int kg = 0; kg < F::D1p / 8; ++kg) {
         float v[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int n = ng * 8 + j;
-          v[j] = (valid && rr == (n >> 2)) ? rv[n & 3] : 0.f;
-        }
-        const uint32_t o = ng * S::SBO_R + (tid >> 3) * S::LBO_R + (tid & 7) * 16;
-        store8_split(rh + o, rl + o, v);
+        for (int j = 0; j < 8; ++j) v[j] = (kg * 8 + j < D1) ? h1[kg * 8 + j] : 0.f;
+        const uint32_t o = (tid >> 3) * F::SBO_A1 + kg * 128 + (tid & 7) * 16;
+        store8_split(a1h + o, a1l + o, v);
       }
-      umma::fence_proxy_async();
-      umma::fence_before_sync();
-      __syncthreads();
-      umma::fence_after_sync();
+      sync_mma();
       if (tid == 0) {
-        mma3(tm + S::C_T, umma::smem_u32(bufh), umma::smem_u32(bufl), umma::smem_u32(rh), umma::smem_u32(rl),
-             S::LBO_G, S::SBO_G, S::LBO_R, S::SBO_R, idescT, 128 / 16, 2 * S::LBO_G, 2 * S::LBO_R);
+        mma3(tm + S::C_D2, umma::smem_u32(a1h), umma::smem_u32(a1l), w2h, w2l, 128, F::SBO_A1, 128, F::SBO_W2, id2,
+             F::D1p / 16, 256, 256, false);
         umma::commit(&bar);
       }
-      ok = umma::mbar_wait(&bar, phase, kWaitLimit);
-      phase ^= 1;
-      if (__syncthreads_or(!ok)) {
+      if (!wait_mma()) {
         aborted = true;
         break;
       }
-      umma::fence_after_sync();
-      float v[32];
-      umma::ld16(tm + lane_base + S::C_T, v);
-      umma::ld16(tm + lane_base + S::C_T + 16, v + 16);
-      umma::wait_ld();
-      if (tid < D3) {
-        for (int r8 = 0; r8 < 8; ++r8) {
-          const int r = 8 * ch + r8;
-          if (r >= na) break;
-          const int prow = s_lrow[r];
-          const int lo = L.eoff[(size_t)q * L.nloc + prow] - lbase;
-          const int piece = kt - lo / 128;
-          float* dst = a.partial + (((size_t)q * L.nloc + prow) * L.pieces + piece) * 4 * D3;
+      float h2[D2];
 #pragma unroll
-          for (int k = 0; k < 4; ++k) dst[k * D3 + tid] = v[4 * r8 + k];
+      for (int c = 0; c < F::D2p / 16; ++c) {
+        float v[16];
+        umma::ld16(tm + lb + S::C_D2 + c * 16, v);
+        umma::wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int n = c * 16 + j;
+          if (n < D2) h2[n] = valid ? tanh_fast(v[j] + b2[n]) + resid_of<D2, D1>(h1, n) : 0.f;
         }
       }
-      umma::fence_before_sync();
-      __syncthreads();
-      umma::fence_after_sync();
+#pragma unroll
+      for (int kg = 0; kg < F::D2p / 8; ++kg) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = (kg * 8 + j < D2) ? h2[kg * 8 + j] : 0.f;
+        const uint32_t o = (tid >> 3) * F::SBO_A2 + kg * 128 + (tid & 7) * 16;
+        store8_split(xh + o, xl + o, v);
+      }
+      sync_mma();
+      if (tid == 0) {
+        mma3(tm + S::C_D3, umma::smem_u32(xh), umma::smem_u32(xl), w3h, w3l, 128, F::SBO_A2, 128, F::SBO_W3, id3,
+             F::D2p / 16, 256, 256, false);
+        umma::commit(&bar);
+      }
+      if (!wait_mma()) {
+        aborted = true;
+        break;
+      }
+      // contraction in two halves of 64 edges: G^T and R~ of half h, then one MMA
+      const int nh = ne > 64 ? 2 : 1;
+      for (int h = 0; h < nh; ++h) {
+        if ((tid >> 6) == h) {
+          const int ep = tid & 63;
+#pragma unroll
+          for (int c = 0; c < F::D3p / 16; ++c) {
+            float v[16];
+            umma::ld16(tm + lb + S::C_D3 + c * 16, v);
+            umma::wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int n = c * 16 + j;
+              v[j] = (n < D3 && valid) ? tanh_fast(v[j] + b3[n]) + resid_of<D3, D2>(h2, n) : 0.f;
+            }
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              const uint32_t o = (2 * c + hh) * S::SBO_G + (ep >> 3) * S::LBO_G + (ep & 7) * 16;
+              store8_split(xh + o, xl + o, v + 8 * hh);
+            }
+          }
+          const float rv[4] = {rt.x, rt.y, rt.z, rt.w};
+#pragma unroll
+          for (int ng = 0; ng < S::NT / 8; ++ng) {
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int n = ng * 8 + j;
+              v[j] = (rl_ == (n >> 2)) ? rv[n & 3] : 0.f;
+            }
+            const uint32_t o = ng * S::SBO_R + (ep >> 3) * S::LBO_R + (ep & 7) * 16;
+            store8_split(rh + o, rl + o, v);
+          }
+        }
+        sync_mma();
+        if (tid == 0) {
+          mma3(tm + S::C_T, umma::smem_u32(xh), umma::smem_u32(xl), umma::smem_u32(rh), umma::smem_u32(rl), S::LBO_G,
+               S::SBO_G, S::LBO_R, S::SBO_R, idT, 64 / 16, 2 * S::LBO_G, 2 * S::LBO_R, !first);
+          umma::commit(&bar);
+        }
+        first = false;
+        if (!wait_mma()) {
+          aborted = true;
+          break;
+        }
+      }
     }
+    if (aborted) break;
+    if (I.e1 > I.e0) {
+      float v[32];
+      umma::ld16(tm + lb + S::C_T, v);
+      umma::ld16(tm + lb + S::C_T + 16, v + 16);
+      umma::wait_ld();
+      if (tid < D3) {
+        for (int r = 0; r < I.re - I.rb; ++r) {
+          float* dst = a.Tq + (((size_t)I.q * L.nloc + I.rb + r) * 4) * D3;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) dst[k * D3 + tid] = v[4 * r + k];
+        }
+      }
+    } else if (tid < D3) {
+      for (int r = 0; r < I.re - I.rb; ++r) {
+        float* dst = a.Tq + (((size_t)I.q * L.nloc + I.rb + r) * 4) * D3;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) dst[k * D3 + tid] = 0.f;
+      }
+    }
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
   }
   if (aborted && tid == 0) atomicAdd(a.err + kErrTcTimeout, 1);
   umma::fence_before_sync();
@@ -309,36 +319,34 @@ __global__ void __launch_bounds__(128, 1) k_embed_fwd_tc(FwdArgs a) {
 }
 
 // ---------------------------------------------------------------- backward
-// Shared-memory map of the backward tile kernel.  The forward weight blobs
-// double as the backward B operands: read with MN-major descriptors they are
-// W3 and W2 themselves (LBO and SBO swapped), so no transposed copy is kept.
+// The forward blobs double as the backward B operands: read with MN-major
+// descriptors they are W3 and W2 themselves, so no transposed copy is kept.
 template <int D1, int D2, int D3>
-struct TcBwd {
+struct Bwd {
   using F = TcShape<D1, D2, D3>;
-  static constexpr int D1p = F::D1p, D2p = F::D2p, D3p = F::D3p, NT = 32;
-  static constexpr uint32_t XB = 128 * D2p * 2;   // A1 / A2 / dz2 (one half)
-  static constexpr uint32_t GB = 128 * D3p * 2;   // G, then dz3, K-major [edge][a]
-  static constexpr uint32_t RB = 128 * NT * 2;    // environment rows, K-major [edge][n]
-  static constexpr uint32_t TB = NT * D3p * 2;    // dT chunk stored [n][a]
-  static constexpr uint32_t O_X = ((F::O_F + F::NF * 4 + 1023) / 1024) * 1024;
-  static constexpr uint32_t O_G = O_X + 2 * XB;
-  static constexpr uint32_t O_R = O_G + 2 * GB;
+  static constexpr int NT = 4 * kItemRows;
+  static constexpr uint32_t A1B = 128 * F::D1p * 2;
+  static constexpr uint32_t XB = 128 * 64 * 2;     // A2 / G half / dz2, K-major K = 64
+  static constexpr uint32_t YB = 128 * 64 * 2;     // dz3 half, K-major K = 64
+  static constexpr uint32_t RB = 128 * NT * 2;     // R~ rows, K-major [edge][n]
+  static constexpr uint32_t TB = NT * F::D3p * 2;  // dT of the item's rows, stored [n][a]
+  static constexpr uint32_t O_A1 = F::O_END;
+  static constexpr uint32_t O_X = O_A1 + 2 * A1B;
+  static constexpr uint32_t O_Y = O_X + 2 * XB;
+  static constexpr uint32_t O_R = O_Y + 2 * YB;
   static constexpr uint32_t O_T = O_R + 2 * RB;
   static constexpr uint32_t SMEM = O_T + 2 * TB;
-  static constexpr uint32_t SBO_A1 = (D1p / 8) * 128, SBO_A2 = (D2p / 8) * 128, SBO_G = (D3p / 8) * 128;
-  static constexpr uint32_t SBO_R = (NT / 8) * 128, SBO_T = (D3p / 8) * 128;
-  // TMEM columns (512 allocated: one CTA per SM)
+  static constexpr uint32_t SBO_H = (64 / 8) * 128, SBO_R = (NT / 8) * 128, SBO_T = (F::D3p / 8) * 128;
   static constexpr uint32_t C_D2 = 0, C_D3 = 64, C_DG = 192, C_DR = 320, C_DH1 = 352, NCOLS = 512;
-  static_assert(D2p <= 64 && D3p <= 128 && D1p <= 32, "TMEM column plan");
 };
 
 struct BwdArgs {
   TcLists L;
   const unsigned char* nets;
   size_t net_bytes;
-  const float* dT;     // [row][4][D3], already scaled by 1/N
-  const double* rij;   // formatted neighbour list vectors
-  double* gslot;       // dE/dr per slot
+  const float* dT;    // [row][4][D3], already scaled by 1/N
+  const double* rij;  // formatted neighbour list vectors
+  double* gslot;      // dE/dr per slot
   int* err;
   double rcut, rcut_smth;
 };
@@ -346,26 +354,23 @@ struct BwdArgs {
 template <int D1, int D2, int D3>
 __global__ void __launch_bounds__(128, 1) k_embed_bwd_tc(BwdArgs a) {
   using F = TcShape<D1, D2, D3>;
-  using B = TcBwd<D1, D2, D3>;
+  using B = Bwd<D1, D2, D3>;
   extern __shared__ __align__(1024) unsigned char smem[];
   __shared__ uint64_t bar;
   __shared__ uint32_t tbase;
-  __shared__ int s_row[128];
-  __shared__ int s_lrow[128];
-  __shared__ int s_wcnt[4];
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tid = threadIdx.x, warp = tid >> 5;
   const float* w1 = reinterpret_cast<const float*>(smem + F::O_F);
   const float* b1 = w1 + D1;
   const float* b2 = b1 + D1;
   const float* b3 = b2 + D2;
-  unsigned char* w2h = smem + F::O_W2;
-  unsigned char* w2l = w2h + F::W2B;
-  unsigned char* w3h = smem + F::O_W3;
-  unsigned char* w3l = w3h + F::W3B;
+  const uint32_t w2h = umma::smem_u32(smem + F::O_W2), w2l = w2h + F::W2B;
+  const uint32_t w3h = umma::smem_u32(smem + F::O_W3), w3l = w3h + F::W3B;
+  unsigned char* a1h = smem + B::O_A1;
+  unsigned char* a1l = a1h + B::A1B;
   unsigned char* xh = smem + B::O_X;
   unsigned char* xl = xh + B::XB;
-  unsigned char* gh = smem + B::O_G;
-  unsigned char* gl = gh + B::GB;
+  unsigned char* yh = smem + B::O_Y;
+  unsigned char* yl = yh + B::YB;
   unsigned char* rh = smem + B::O_R;
   unsigned char* rl = rh + B::RB;
   unsigned char* th = smem + B::O_T;
@@ -383,13 +388,13 @@ __global__ void __launch_bounds__(128, 1) k_embed_bwd_tc(BwdArgs a) {
   uint32_t phase = 0;
   int loaded = -1;
   const TcLists& L = a.L;
-  const int ntiles = L.tstart[L.nnets];
-  const uint32_t id_2 = umma::idesc_bf16(128, D2p_of<D2>(), false, false);
-  const uint32_t id_3 = umma::idesc_bf16(128, B::D3p, false, false);
-  const uint32_t id_dg = umma::idesc_bf16(128, B::D3p, false, true);
+  const int nitems = L.istart[L.nnets];
+  const uint32_t id2 = umma::idesc_bf16(128, F::D2p, false, false);
+  const uint32_t id3 = umma::idesc_bf16(128, F::D3p, false, false);
+  const uint32_t id_dg = umma::idesc_bf16(128, F::D3p, false, true);
   const uint32_t id_dr = umma::idesc_bf16(128, B::NT, false, false);
-  const uint32_t id_h2 = umma::idesc_bf16(128, B::D2p, false, true);
-  const uint32_t id_h1 = umma::idesc_bf16(128, B::D1p, false, true);
+  const uint32_t id_h2 = umma::idesc_bf16(128, F::D2p, false, true);
+  const uint32_t id_h1 = umma::idesc_bf16(128, F::D1p, false, true);
   bool aborted = false;
   auto sync_mma = [&]() {
     umma::fence_proxy_async();
@@ -404,309 +409,248 @@ __global__ void __launch_bounds__(128, 1) k_embed_bwd_tc(BwdArgs a) {
     umma::fence_after_sync();
     return true;
   };
-  for (int g = blockIdx.x; g < ntiles && !aborted; g += gridDim.x) {
-    int q = 0;
-    while (q + 1 < L.nnets && L.tstart[q + 1] <= g) ++q;
-    const int kt = g - L.tstart[q];
-    const int lbase = L.eoff[(size_t)q * L.nloc];
-    const int lend = L.eoff[(size_t)(q + 1) * L.nloc];
-    const int e0 = lbase + kt * 128;
-    const int ne = min(128, lend - e0);
-    if (q != loaded) {
+  for (int it = blockIdx.x; it < nitems && !aborted; it += gridDim.x) {
+    const Item I = item_of(L, it);
+    if (I.e1 <= I.e0) continue;  // CTA-uniform
+    if (I.q != loaded) {
       __syncthreads();
-      const uint4* src = reinterpret_cast<const uint4*>(a.nets + (size_t)q * a.net_bytes);
+      const uint4* src = reinterpret_cast<const uint4*>(a.nets + (size_t)I.q * a.net_bytes);
       uint4* dst = reinterpret_cast<uint4*>(smem);
       for (uint32_t i = tid; i < F::BLOB / 16; i += 128) dst[i] = src[i];
-      loaded = q;
+      loaded = I.q;
     }
-    const bool valid = tid < ne;
-    const float4 rt = valid ? L.rt[e0 + tid] : make_float4(0.f, 0.f, 0.f, 0.f);
-    const int row = valid ? L.row[e0 + tid] : -1;
-    const int slot = valid ? L.slot[e0 + tid] : -1;
-    s_row[tid] = row;
-    __syncthreads();
-    const bool first = valid && (tid == 0 || s_row[tid - 1] != row);
-    const unsigned fm = __ballot_sync(0xffffffffu, first);
-    if (lane == 0) s_wcnt[warp] = __popc(fm);
-    __syncthreads();
-    int before = 0;
-    for (int w = 0; w < warp; ++w) before += s_wcnt[w];
-    const int na = s_wcnt[0] + s_wcnt[1] + s_wcnt[2] + s_wcnt[3];
-    const unsigned le_mask = (lane == 31) ? 0xffffffffu : ((2u << lane) - 1u);
-    const int lr = valid ? before + __popc(fm & le_mask) - 1 : -1;
-    if (first) s_lrow[lr] = row;
-    __syncthreads();
-    const float rv[4] = {rt.x, rt.y, rt.z, rt.w};
-    float dR[4] = {0.f, 0.f, 0.f, 0.f};
-    // layer 1 recompute -> A1 (X)
-    float h1[D1];
-#pragma unroll
-    for (int n = 0; n < D1; ++n) h1[n] = valid ? tanh_fast(rt.x * w1[n] + b1[n]) : 0.f;
-#pragma unroll
-    for (int kg = 0; kg < B::D1p / 8; ++kg) {
+    // dT of the item's rows as a [n][a] operand (n = 4 * local row + k)
+    for (int idx = tid; idx < B::NT * (F::D3p / 8); idx += 128) {
+      const int n = idx / (F::D3p / 8), ag = idx - n * (F::D3p / 8);
+      const int row = I.rb + (n >> 2), k = n & 3;
       float v[8];
+      const float* src = (row < I.re) ? a.dT + ((size_t)row * 4 + k) * D3 : nullptr;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = (kg * 8 + j < D1) ? h1[kg * 8 + j] : 0.f;
-      const uint32_t o = (tid >> 3) * B::SBO_A1 + kg * 128 + (tid & 7) * 16;
-      store8_split(xh + o, xl + o, v);
-    }
-    sync_mma();
-    if (tid == 0) {
-      mma3(tm + B::C_D2, umma::smem_u32(xh), umma::smem_u32(xl), umma::smem_u32(w2h), umma::smem_u32(w2l), 128,
-           B::SBO_A1, 128, F::SBO_W2, id_2, B::D1p / 16, 256, 256);
-      umma::commit(&bar);
-    }
-    if (!wait_mma()) {
-      aborted = true;
-      break;
-    }
-    // layer 2 recompute -> A2 (X)
-    float h2[D2];
-#pragma unroll
-    for (int c = 0; c < B::D2p / 16; ++c) {
-      float v[16];
-      umma::ld16(tm + lb + B::C_D2 + c * 16, v);
-      umma::wait_ld();
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int n = c * 16 + j;
-        if (n < D2) h2[n] = valid ? tanh_fast(v[j] + b2[n]) + resid_of<D2, D1>(h1, n) : 0.f;
+      for (int j = 0; j < 8; ++j) {
+        const int aa = ag * 8 + j;
+        v[j] = (src && aa < D3) ? src[aa] : 0.f;
       }
+      const uint32_t o = (n >> 3) * B::SBO_T + ag * 128 + (n & 7) * 16;
+      store8_split(th + o, tl + o, v);
     }
-#pragma unroll
-    for (int kg = 0; kg < B::D2p / 8; ++kg) {
-      float v[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = (kg * 8 + j < D2) ? h2[kg * 8 + j] : 0.f;
-      const uint32_t o = (tid >> 3) * B::SBO_A2 + kg * 128 + (tid & 7) * 16;
-      store8_split(xh + o, xl + o, v);
-    }
-    sync_mma();
-    if (tid == 0) {
-      mma3(tm + B::C_D3, umma::smem_u32(xh), umma::smem_u32(xl), umma::smem_u32(w3h), umma::smem_u32(w3l), 128,
-           B::SBO_A2, 128, F::SBO_W3, id_3, B::D2p / 16, 256, 256);
-      umma::commit(&bar);
-    }
-    if (!wait_mma()) {
-      aborted = true;
-      break;
-    }
-    // layer 3 recompute: G -> K-major [edge][a] (A operand of dR = G dT^T)
-#pragma unroll
-    for (int c = 0; c < B::D3p / 16; ++c) {
-      float v[16];
-      umma::ld16(tm + lb + B::C_D3 + c * 16, v);
-      umma::wait_ld();
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int n = c * 16 + j;
-        v[j] = (n < D3 && valid) ? tanh_fast(v[j] + b3[n]) + resid_of<D3, D2>(h2, n) : 0.f;
-      }
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const uint32_t o = (tid >> 3) * B::SBO_G + (2 * c + h) * 128 + (tid & 7) * 16;
-        store8_split(gh + o, gl + o, v + 8 * h);
-      }
-    }
-    // dG = R dT (accumulated over atom chunks) and dR = G dT^T (per chunk)
-    for (int ch = 0; ch * 8 < na; ++ch) {
-      const int rr = lr - 8 * ch;
+    for (int sub = I.e0; sub < I.e1; sub += 128) {
+      const int ne = min(128, I.e1 - sub);
+      const bool valid = tid < ne;
+      const float4 rt = valid ? L.rt[sub + tid] : make_float4(0.f, 0.f, 0.f, 0.f);
+      const int rl_ = valid ? L.row[sub + tid] - I.rb : -1;
+      const int slot = valid ? L.slot[sub + tid] : -1;
+      const float rv[4] = {rt.x, rt.y, rt.z, rt.w};
 #pragma unroll
       for (int ng = 0; ng < B::NT / 8; ++ng) {
         float v[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const int n = ng * 8 + j;
-          v[j] = (valid && rr == (n >> 2)) ? rv[n & 3] : 0.f;
+          v[j] = (rl_ == (n >> 2)) ? rv[n & 3] : 0.f;
         }
         const uint32_t o = (tid >> 3) * B::SBO_R + ng * 128 + (tid & 7) * 16;
         store8_split(rh + o, rl + o, v);
       }
-      for (int idx = tid; idx < B::NT * (B::D3p / 8); idx += 128) {
-        const int n = idx / (B::D3p / 8), ag = idx - n * (B::D3p / 8);
-        const int r = 8 * ch + (n >> 2), k = n & 3;
-        float v[8];
-        const float* src = (r < na) ? a.dT + ((size_t)s_lrow[r] * 4 + k) * D3 : nullptr;
+      float h1[D1];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int aa = ag * 8 + j;
-          v[j] = (src && aa < D3) ? src[aa] : 0.f;
-        }
-        const uint32_t o = (n >> 3) * B::SBO_T + ag * 128 + (n & 7) * 16;
-        store8_split(th + o, tl + o, v);
+      for (int n = 0; n < D1; ++n) h1[n] = valid ? tanh_fast(rt.x * w1[n] + b1[n]) : 0.f;
+#pragma unroll
+      for (int kg = 0; kg < F::D1p / 8; ++kg) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = (kg * 8 + j < D1) ? h1[kg * 8 + j] : 0.f;
+        const uint32_t o = (tid >> 3) * F::SBO_A1 + kg * 128 + (tid & 7) * 16;
+        store8_split(a1h + o, a1l + o, v);
       }
       sync_mma();
       if (tid == 0) {
-        // dG[e][a] += sum_n R[e][n] dT(a, n): B read MN-major from the [n][a] store
-        for (int s = 0; s < B::NT / 16; ++s) {
-          const uint32_t oa = s * 256, ob = s * 2 * B::SBO_T;
-          const uint32_t ra = umma::smem_u32(rh) + oa, rla = umma::smem_u32(rl) + oa;
-          const uint32_t tb = umma::smem_u32(th) + ob, tlb = umma::smem_u32(tl) + ob;
-          umma::mma(tm + B::C_DG, umma::desc(ra, 128, B::SBO_R), umma::desc(tb, B::SBO_T, 128), id_dg,
-                    (ch > 0 || s > 0) ? 1u : 0u);
-          umma::mma(tm + B::C_DG, umma::desc(ra, 128, B::SBO_R), umma::desc(tlb, B::SBO_T, 128), id_dg, 1u);
-          umma::mma(tm + B::C_DG, umma::desc(rla, 128, B::SBO_R), umma::desc(tb, B::SBO_T, 128), id_dg, 1u);
-        }
-        // dR[e][n] = sum_a G[e][a] dT(n, a): B read K-major from the same store
-        mma3(tm + B::C_DR, umma::smem_u32(gh), umma::smem_u32(gl), umma::smem_u32(th), umma::smem_u32(tl), 128,
-             B::SBO_G, 128, B::SBO_T, id_dr, B::D3p / 16, 256, 256);
+        mma3(tm + B::C_D2, umma::smem_u32(a1h), umma::smem_u32(a1l), w2h, w2l, 128, F::SBO_A1, 128, F::SBO_W2, id2,
+             F::D1p / 16, 256, 256, false);
+        // dG[e][a] = sum_n R~[e][n] dT(a, n); the [n][a] store read MN-major
+        mma3(tm + B::C_DG, umma::smem_u32(rh), umma::smem_u32(rl), umma::smem_u32(th), umma::smem_u32(tl), 128,
+             B::SBO_R, B::SBO_T, 128, id_dg, B::NT / 16, 256, 2 * B::SBO_T, false);
         umma::commit(&bar);
       }
       if (!wait_mma()) {
         aborted = true;
         break;
       }
-      float v[32];
-      umma::ld16(tm + lb + B::C_DR, v);
-      umma::ld16(tm + lb + B::C_DR + 16, v + 16);
-      umma::wait_ld();
-      if (rr >= 0 && rr < 8) {
+      float h2[D2];
 #pragma unroll
-        for (int r8 = 0; r8 < 8; ++r8)
-          if (r8 == rr) {
+      for (int c = 0; c < F::D2p / 16; ++c) {
+        float v[16];
+        umma::ld16(tm + lb + B::C_D2 + c * 16, v);
+        umma::wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int n = c * 16 + j;
+          if (n < D2) h2[n] = valid ? tanh_fast(v[j] + b2[n]) + resid_of<D2, D1>(h1, n) : 0.f;
+        }
+      }
+#pragma unroll
+      for (int kg = 0; kg < F::D2p / 8; ++kg) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = (kg * 8 + j < D2) ? h2[kg * 8 + j] : 0.f;
+        const uint32_t o = (tid >> 3) * F::SBO_A2 + kg * 128 + (tid & 7) * 16;
+        store8_split(xh + o, xl + o, v);
+      }
+      sync_mma();
+      if (tid == 0) {
+        mma3(tm + B::C_D3, umma::smem_u32(xh), umma::smem_u32(xl), w3h, w3l, 128, F::SBO_A2, 128, F::SBO_W3, id3,
+             F::D2p / 16, 256, 256, false);
+        umma::commit(&bar);
+      }
+      if (!wait_mma()) {
+        aborted = true;
+        break;
+      }
+      // layer 3 with its gradient, in halves of 64 columns of a:
+      // G -> X (A of dR~ = G dT^T), dz3 = dG (1 - th3^2) -> Y (A of dh2 = dz3 W3)
+      float racc[D2];
+#pragma unroll
+      for (int n = 0; n < D2; ++n) racc[n] = 0.f;
+#pragma unroll
+      for (int c = 0; c < F::D3p / 16; ++c) {
+        const int h = c / 4, cc = c % 4;
+        float z[16], dg[16];
+        umma::ld16(tm + lb + B::C_D3 + c * 16, z);
+        umma::ld16(tm + lb + B::C_DG + c * 16, dg);
+        umma::wait_ld();
+        float gv[16], zv[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int n = c * 16 + j;
+          if (n < D3 && valid) {
+            const float t3 = tanh_fast(z[j] + b3[n]);
+            gv[j] = t3 + resid_of<D3, D2>(h2, n);
+            zv[j] = dg[j] * (1.f - t3 * t3);
+            if constexpr (D3 == D2) racc[n] += dg[j];
+            if constexpr (D3 == 2 * D2) racc[n < D2 ? n : n - D2] += dg[j];
+          } else {
+            gv[j] = 0.f;
+            zv[j] = 0.f;
+          }
+        }
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const uint32_t o = (tid >> 3) * B::SBO_H + (2 * cc + hh) * 128 + (tid & 7) * 16;
+          store8_split(xh + o, xl + o, gv + 8 * hh);
+          store8_split(yh + o, yl + o, zv + 8 * hh);
+        }
+        if (cc == 3 || c == F::D3p / 16 - 1) {
+          const int steps = cc + 1;
+          sync_mma();
+          if (tid == 0) {
+            // dR~[e][n] += sum_a G[e][a] dT(n, a) over this half of a
+            mma3(tm + B::C_DR, umma::smem_u32(xh), umma::smem_u32(xl), umma::smem_u32(th) + 1024u * h,
+                 umma::smem_u32(tl) + 1024u * h, 128, B::SBO_H, 128, B::SBO_T, id_dr, steps, 256, 256, h > 0);
+            // dh2[e][k] += sum_a dz3[e][a] W3[k][a] over this half; W3 blob read MN-major
+            mma3(tm + B::C_D2, umma::smem_u32(yh), umma::smem_u32(yl), w3h + 8u * h * F::SBO_W3,
+                 w3l + 8u * h * F::SBO_W3, 128, B::SBO_H, F::SBO_W3, 128, id_h2, steps, 256, 2 * F::SBO_W3, h > 0);
+            umma::commit(&bar);
+          }
+          if (!wait_mma()) {
+            aborted = true;
+            break;
+          }
+        }
+      }
+      if (aborted) break;
+      float dR[4] = {0.f, 0.f, 0.f, 0.f};
+      {
+        float v[32];
+        umma::ld16(tm + lb + B::C_DR, v);
+        umma::ld16(tm + lb + B::C_DR + 16, v + 16);
+        umma::wait_ld();
+#pragma unroll
+        for (int r8 = 0; r8 < kItemRows; ++r8)
+          if (r8 == rl_) {
 #pragma unroll
             for (int k = 0; k < 4; ++k) dR[k] = v[4 * r8 + k];
           }
+      }
+      // dh2 = MMA + residual gradient; dz2 = dh2 (1 - th2^2) -> X
+      float dh2[D2];
+#pragma unroll
+      for (int c = 0; c < F::D2p / 16; ++c) {
+        float v[16];
+        umma::ld16(tm + lb + B::C_D2 + c * 16, v);
+        umma::wait_ld();
+        float zz[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int n = c * 16 + j;
+          if (n < D2) {
+            dh2[n] = valid ? v[j] + racc[n] : 0.f;
+            const float t2 = h2[n] - resid_of<D2, D1>(h1, n);
+            zz[j] = dh2[n] * (1.f - t2 * t2);
+          } else {
+            zz[j] = 0.f;
+          }
+        }
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const uint32_t o = (tid >> 3) * F::SBO_A2 + (2 * c + hh) * 128 + (tid & 7) * 16;
+          store8_split(xh + o, xl + o, zz + 8 * hh);
+        }
+      }
+      sync_mma();
+      if (tid == 0) {
+        // dh1[e][k1] = sum_n dz2[e][n] W2[k1][n]; W2 blob read MN-major
+        mma3(tm + B::C_DH1, umma::smem_u32(xh), umma::smem_u32(xl), w2h, w2l, 128, F::SBO_A2, F::SBO_W2, 128, id_h1,
+             F::D2p / 16, 256, 2 * F::SBO_W2, false);
+        umma::commit(&bar);
+      }
+      if (!wait_mma()) {
+        aborted = true;
+        break;
+      }
+      float ds = 0.f;
+#pragma unroll
+      for (int c = 0; c < F::D1p / 16; ++c) {
+        float v[16];
+        umma::ld16(tm + lb + B::C_DH1 + c * 16, v);
+        umma::wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int n = c * 16 + j;
+          if (n < D1) {
+            float r = v[j];
+            if constexpr (D2 == D1) r += dh2[n];
+            if constexpr (D2 == 2 * D1) r += dh2[n] + dh2[n + D1];
+            ds += r * (1.f - h1[n] * h1[n]) * w1[n];
+          }
+        }
+      }
+      if (valid) {
+        // chain rule to r_ij in fp64
+        const double* rp = a.rij + 3 * (size_t)slot;
+        const double x = rp[0], y = rp[1], zc = rp[2];
+        const double r2 = x * x + y * y + zc * zc, rr = sqrt(r2);
+        double sw, dsw;
+        smooth_switch(rr, a.rcut_smth, a.rcut, sw, dsw);
+        const double ir = 1.0 / rr, ir2 = ir * ir;
+        const double d0 = dsw * ir - sw * ir2;
+        const double rvec[3] = {x, y, zc};
+        const double g0 = (double)dR[0] + (double)ds;
+        double* go = a.gslot + 3 * (size_t)slot;
+#pragma unroll
+        for (int cc = 0; cc < 3; ++cc) {
+          double acc = g0 * d0 * rvec[cc] * ir;
+#pragma unroll
+          for (int aa = 0; aa < 3; ++aa) {
+            const double J = dsw * rvec[cc] * ir * rvec[aa] * ir2 +
+                             sw * ((aa == cc ? ir2 : 0.0) - 2.0 * rvec[aa] * rvec[cc] * ir2 * ir2);
+            acc += (double)dR[1 + aa] * J;
+          }
+          go[cc] = acc;
+        }
       }
       umma::fence_before_sync();
       __syncthreads();
       umma::fence_after_sync();
     }
-    if (aborted) break;
-    // dz3 = dG (1 - th3^2), th3 = G - residual; written over G (own row only)
-#pragma unroll
-    for (int c = 0; c < B::D3p / 16; ++c) {
-      float dg[16];
-      umma::ld16(tm + lb + B::C_DG + c * 16, dg);
-      umma::wait_ld();
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const uint32_t o = (tid >> 3) * B::SBO_G + (2 * c + h) * 128 + (tid & 7) * 16;
-        const uint4 uh = *reinterpret_cast<const uint4*>(gh + o);
-        const uint4 ul = *reinterpret_cast<const uint4*>(gl + o);
-        const uint32_t hw[4] = {uh.x, uh.y, uh.z, uh.w}, lw[4] = {ul.x, ul.y, ul.z, ul.w};
-        float z[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int n = c * 16 + 8 * h + j;
-          const uint32_t hb = (j & 1) ? (hw[j >> 1] & 0xFFFF0000u) : (hw[j >> 1] << 16);
-          const uint32_t lbits = (j & 1) ? (lw[j >> 1] & 0xFFFF0000u) : (lw[j >> 1] << 16);
-          const float gval = __uint_as_float(hb) + __uint_as_float(lbits);
-          const float t3 = gval - resid_of<D3, D2>(h2, n);
-          z[j] = (n < D3 && valid) ? dg[8 * h + j] * (1.f - t3 * t3) : 0.f;
-        }
-        store8_split(gh + o, gl + o, z);
-      }
-    }
-    sync_mma();
-    if (tid == 0) {
-      // dh2[e][k2] = sum_a dz3[e][a] W3[k2][a]; W3 blob read MN-major
-      mma3(tm + B::C_D2, umma::smem_u32(gh), umma::smem_u32(gl), umma::smem_u32(w3h), umma::smem_u32(w3l), 128,
-           B::SBO_G, F::SBO_W3, 128, id_h2, B::D3p / 16, 256, 2 * F::SBO_W3);
-      umma::commit(&bar);
-    }
-    if (!wait_mma()) {
-      aborted = true;
-      break;
-    }
-    // dh2 = MMA + residual gradient from dG; dz2 = dh2 (1 - th2^2) -> X.
-    // TMEM is read in aligned 16-column chunks; the chunk holding dG[n + D2]
-    // is known at compile time, so every register index below is static.
-    float dh2[D2];
-#pragma unroll
-    for (int c = 0; c < B::D2p / 16; ++c) {
-      float v[16], ga[16], gb[16], gc[16];
-      umma::ld16(tm + lb + B::C_D2 + c * 16, v);
-      umma::ld16(tm + lb + B::C_DG + c * 16, ga);
-      constexpr int kShift = (D3 == 2 * D2) ? D2 : 0;
-      const int cb = (c * 16 + kShift) / 16;
-      umma::ld16(tm + lb + B::C_DG + min(cb, B::D3p / 16 - 1) * 16, gb);
-      umma::ld16(tm + lb + B::C_DG + min(cb + 1, B::D3p / 16 - 1) * 16, gc);
-      umma::wait_ld();
-      float z[16];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int n = c * 16 + j;
-        float r = v[j];
-        if constexpr (D3 == D2) r += ga[j];
-        if constexpr (D3 == 2 * D2) {
-          const int m = n + D2;
-          const int off = m - cb * 16;  // 0..31, static after unrolling
-          r += ga[j] + (off < 16 ? gb[off & 15] : gc[off & 15]);
-        }
-        if (n < D2) {
-          dh2[n] = valid ? r : 0.f;
-          const float t2 = h2[n] - resid_of<D2, D1>(h1, n);
-          z[j] = dh2[n] * (1.f - t2 * t2);
-        } else {
-          z[j] = 0.f;
-        }
-      }
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const uint32_t o = (tid >> 3) * B::SBO_A2 + (2 * c + h) * 128 + (tid & 7) * 16;
-        store8_split(xh + o, xl + o, z + 8 * h);
-      }
-    }
-    sync_mma();
-    if (tid == 0) {
-      // dh1[e][k1] = sum_n dz2[e][n] W2[k1][n]; W2 blob read MN-major
-      mma3(tm + B::C_DH1, umma::smem_u32(xh), umma::smem_u32(xl), umma::smem_u32(w2h), umma::smem_u32(w2l), 128,
-           B::SBO_A2, F::SBO_W2, 128, id_h1, B::D2p / 16, 256, 2 * F::SBO_W2);
-      umma::commit(&bar);
-    }
-    if (!wait_mma()) {
-      aborted = true;
-      break;
-    }
-    float ds = 0.f;
-#pragma unroll
-    for (int c = 0; c < B::D1p / 16; ++c) {
-      float v[16];
-      umma::ld16(tm + lb + B::C_DH1 + c * 16, v);
-      umma::wait_ld();
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int n = c * 16 + j;
-        if (n < D1) {
-          float r = v[j];
-          if constexpr (D2 == D1) r += dh2[n];
-          if constexpr (D2 == 2 * D1) r += dh2[n] + dh2[n + D1];
-          ds += r * (1.f - h1[n] * h1[n]) * w1[n];
-        }
-      }
-    }
-    if (valid) {
-      // chain rule to r_ij in fp64
-      const double* rp = a.rij + 3 * (size_t)slot;
-      const double x = rp[0], y = rp[1], z = rp[2];
-      const double r2 = x * x + y * y + z * z, rr = sqrt(r2);
-      double sw, dsw;
-      smooth_switch(rr, a.rcut_smth, a.rcut, sw, dsw);
-      const double ir = 1.0 / rr, ir2 = ir * ir;
-      const double d0 = dsw * ir - sw * ir2;
-      const double rvec[3] = {x, y, z};
-      const double g0 = (double)dR[0] + (double)ds;
-      double gout[3];
-#pragma unroll
-      for (int cc = 0; cc < 3; ++cc) {
-        double acc = g0 * d0 * rvec[cc] * ir;
-#pragma unroll
-        for (int aa = 0; aa < 3; ++aa) {
-          const double J = dsw * rvec[cc] * ir * rvec[aa] * ir2 +
-                           sw * ((aa == cc ? ir2 : 0.0) - 2.0 * rvec[aa] * rvec[cc] * ir2 * ir2);
-          acc += (double)dR[1 + aa] * J;
-        }
-        gout[cc] = acc;
-      }
-      double* go = a.gslot + 3 * (size_t)slot;
-      go[0] = gout[0];
-      go[1] = gout[1];
-      go[2] = gout[2];
-    }
-    umma::fence_before_sync();
-    __syncthreads();
-    umma::fence_after_sync();
   }
   if (aborted && tid == 0) atomicAdd(a.err + kErrTcTimeout, 1);
   umma::fence_before_sync();
@@ -716,18 +660,19 @@ __global__ void __launch_bounds__(128, 1) k_embed_bwd_tc(BwdArgs a) {
 
 // dT[row][k][a] = (sum_b dD[a][b] T[k][b] + [a < M2] sum_c dD[c][a] T[k][c]) / N
 template <int D3>
-__global__ void __launch_bounds__(128) k_dT(int nloc, int ntypes, int M2, double inv_nnei,
+__global__ void __launch_bounds__(128) k_dT(int nloc, int ntypes, int M2, float inv_nnei,
                                             const int* __restrict__ type_start, const int* __restrict__ perm_atom,
                                             const float* __restrict__ T, const float* __restrict__ dD,
                                             float* __restrict__ dT) {
   extern __shared__ float sm[];
-  float* sT = sm;             // 4 * D3
-  float* sdD = sm + 4 * D3;   // D3 * M2
+  float* sT = sm;            // 4 * D3
+  float* sdD = sm + 4 * D3;  // D3 * M2
   const int r = blockIdx.x;
   if (r >= type_start[ntypes]) return;
   const int atom = perm_atom[r];
   for (int i = threadIdx.x; i < 4 * D3; i += blockDim.x) sT[i] = T[(size_t)atom * 4 * D3 + i];
-  for (int i = threadIdx.x; i < D3 * M2; i += blockDim.x) sdD[i] = dD[(size_t)r * D3 * M2 + i];
+  const float4* src = reinterpret_cast<const float4*>(dD + (size_t)r * D3 * M2);
+  for (int i = threadIdx.x; i < D3 * M2 / 4; i += blockDim.x) reinterpret_cast<float4*>(sdD)[i] = src[i];
   __syncthreads();
   for (int idx = threadIdx.x; idx < 4 * D3; idx += blockDim.x) {
     const int k = idx / D3, aa = idx - k * D3;
@@ -736,51 +681,60 @@ __global__ void __launch_bounds__(128) k_dT(int nloc, int ntypes, int M2, double
     for (int b = 0; b < M2; ++b) acc += sdD[aa * M2 + b] * tk[b];
     if (aa < M2)
       for (int c = 0; c < D3; ++c) acc += sdD[c * M2 + aa] * tk[c];
-    dT[(size_t)r * 4 * D3 + idx] = (float)(acc * inv_nnei);
+    dT[(size_t)r * 4 * D3 + idx] = acc * inv_nnei;
   }
 }
 
-// T_i = (sum over nets and pieces, fixed order) / N; D = T^T T_< .
+// T_i = sum over nets (fixed order) / N; D = T^T T_< written as fp32 rows and,
+// when requested, pre-tiled bf16 hi/lo for the fitting GEMMs.
 template <int D3>
-__global__ void __launch_bounds__(128) k_t_combine(TcLists L, int ntypes, int M2, double inv_nnei,
-                                                    const int* __restrict__ type_start,
-                                                    const int* __restrict__ perm_atom,
-                                                    const float* __restrict__ partial, float* __restrict__ T,
-                                                    float* __restrict__ D) {
+__global__ void __launch_bounds__(128) k_t_combine(TcLists L, int M2, float inv_nnei, const int* __restrict__ perm_atom,
+                                                    const int* __restrict__ ftile, const float* __restrict__ Tq,
+                                                    float* __restrict__ T, float* __restrict__ D,
+                                                    unsigned char* __restrict__ Dt_hi,
+                                                    unsigned char* __restrict__ Dt_lo) {
   __shared__ float sT[4 * D3];
   const int r = blockIdx.x;
-  if (r >= type_start[ntypes]) return;
+  if (r >= L.type_start[L.ntypes]) return;
+  int t = 0;
+  while (t + 1 < L.ntypes && L.type_start[t + 1] <= r) ++t;
   const int tid = threadIdx.x;
   if (tid < D3) {
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int q = 0; q < L.nnets; ++q) {
-      const size_t idx = (size_t)q * L.nloc + r;
-      const int beg = L.eoff[idx], cnt = L.eoff[idx + 1] - beg;
-      if (cnt <= 0) continue;
-      const int base = L.eoff[(size_t)q * L.nloc];
-      const int np = (beg + cnt - 1 - base) / 128 - (beg - base) / 128 + 1;
-      for (int p = 0; p < np; ++p) {
-        const float* src = partial + (idx * L.pieces + p) * 4 * D3;
+    const int q0 = L.type_one_side ? 0 : t * L.ntypes;
+    const int q1 = L.type_one_side ? L.nnets : q0 + L.ntypes;
+    for (int q = q0; q < q1; ++q) {
+      const float* src = Tq + (((size_t)q * L.nloc + r) * 4) * D3;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) acc[k] += src[k * D3 + tid];
-      }
+      for (int k = 0; k < 4; ++k) acc[k] += src[k * D3 + tid];
     }
     const int atom = perm_atom[r];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const float v = (float)(acc[k] * inv_nnei);
+      const float v = acc[k] * inv_nnei;
       sT[k * D3 + tid] = v;
       T[(size_t)atom * 4 * D3 + k * D3 + tid] = v;
     }
   }
   __syncthreads();
-  float* drow = D + (size_t)r * D3 * M2;
-  for (int idx = tid; idx < D3 * M2; idx += blockDim.x) {
-    const int aa = idx / M2, b = idx - aa * M2;
-    float acc = 0.f;
+  const int dim = D3 * M2;
+  const int prow = Dt_hi ? 128 * ftile[t] + (r - L.type_start[t]) : 0;
+  for (int g = tid; g < dim / 8; g += blockDim.x) {
+    const int k0 = g * 8;
+    float v[8];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) acc += sT[k * D3 + aa] * sT[k * D3 + b];
-    drow[idx] = acc;
+    for (int j = 0; j < 8; ++j) {
+      const int k = k0 + j, aa = k / M2, b = k - aa * M2;
+      v[j] = sT[aa] * sT[b] + sT[D3 + aa] * sT[D3 + b] + sT[2 * D3 + aa] * sT[2 * D3 + b] +
+             sT[3 * D3 + aa] * sT[3 * D3 + b];
+    }
+    float4* drow = reinterpret_cast<float4*>(D + (size_t)r * dim + k0);
+    drow[0] = make_float4(v[0], v[1], v[2], v[3]);
+    drow[1] = make_float4(v[4], v[5], v[6], v[7]);
+    if (Dt_hi) {
+      const size_t o = umma::tiled_off(prow, k0, dim);
+      store8_split(Dt_hi + o, Dt_lo + o, v);
+    }
   }
 }
 
@@ -829,14 +783,21 @@ __global__ void k_edge_compact(SeaDev s, int nloc, const int* __restrict__ type_
   }
 }
 
-__global__ void k_tile_table(int nnets, int nloc, const int* __restrict__ eoff, int* __restrict__ tstart) {
+__global__ void k_item_table(int nnets, int ntypes, int tos, const int* __restrict__ type_start,
+                             int* __restrict__ istart) {
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
-  int t = 0;
-  tstart[0] = 0;
+  int acc = 0;
+  istart[0] = 0;
   for (int q = 0; q < nnets; ++q) {
-    const int e = eoff[(size_t)(q + 1) * nloc] - eoff[(size_t)q * nloc];
-    t += (e + 127) / 128;
-    tstart[q + 1] = t;
+    int rows;
+    if (tos) {
+      rows = type_start[ntypes];
+    } else {
+      const int ti = q / ntypes;
+      rows = type_start[ti + 1] - type_start[ti];
+    }
+    acc += (rows + kItemRows - 1) / kItemRows;
+    istart[q + 1] = acc;
   }
 }
 
@@ -844,23 +805,22 @@ template <int D1, int D2, int D3>
 void pack_net(const std::vector<HostLayer>& net, std::vector<unsigned char>& out) {
   using S = TcShape<D1, D2, D3>;
   out.assign(S::BLOB, 0);
+  auto to_bf16 = [](float f) {
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    const uint32_t rnd = 0x7FFFu + ((u >> 16) & 1u);
+    return (uint16_t)((u + rnd) >> 16);
+  };
+  auto from_bf16 = [](uint16_t h) {
+    uint32_t u = (uint32_t)h << 16;
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+  };
   auto put = [&](uint32_t base, uint32_t half, int rows, int K, auto val) {
     for (int r = 0; r < rows; ++r)
       for (int k = 0; k < K; ++k) {
         const float x = val(r, k);
-        // round-to-nearest-even bf16 split on the host
-        auto to_bf16 = [](float f) {
-          uint32_t u;
-          std::memcpy(&u, &f, 4);
-          const uint32_t rnd = 0x7FFFu + ((u >> 16) & 1u);
-          return (uint16_t)((u + rnd) >> 16);
-        };
-        auto from_bf16 = [](uint16_t h) {
-          uint32_t u = (uint32_t)h << 16;
-          float f;
-          std::memcpy(&f, &u, 4);
-          return f;
-        };
         const uint16_t hi = to_bf16(x);
         const uint16_t lo = to_bf16(x - from_bf16(hi));
         const uint32_t o = (uint32_t)(r >> 3) * ((K / 8) * 128) + (uint32_t)(k >> 3) * 128 + (r & 7) * 16 + (k & 7) * 2;
@@ -890,6 +850,33 @@ Inst which(const SeaDev& s) {
   return Inst::None;
 }
 
+template <int D1, int D2, int D3>
+void launch_fwd(cudaStream_t st, const TcLists& L, int grid, const unsigned char* nets, float* Tq, int* err) {
+  using S = Fwd<D1, D2, D3>;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k_embed_fwd_tc<D1, D2, D3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::SMEM);
+    attr = true;
+  }
+  FwdArgs a{L, nets, TcShape<D1, D2, D3>::BLOB, Tq, err};
+  count_launch();
+  k_embed_fwd_tc<D1, D2, D3><<<grid, 128, S::SMEM, st>>>(a);
+}
+
+template <int D1, int D2, int D3>
+void launch_bwd(cudaStream_t st, const TcLists& L, int grid, const unsigned char* nets, const float* dT,
+                const double* rij, double* gslot, int* err, double rcut, double rs) {
+  using Bw = Bwd<D1, D2, D3>;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k_embed_bwd_tc<D1, D2, D3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Bw::SMEM);
+    attr = true;
+  }
+  BwdArgs a{L, nets, TcShape<D1, D2, D3>::BLOB, dT, rij, gslot, err, rcut, rs};
+  count_launch();
+  k_embed_bwd_tc<D1, D2, D3><<<grid, 128, Bw::SMEM, st>>>(a);
+}
+
 }  // namespace
 
 bool tc_supported(const SeaDev& s) { return which(s) != Inst::None; }
@@ -908,12 +895,6 @@ size_t tc_net_bytes(const SeaDev& s) {
 void tc_pack_net(const SeaDev& s, const std::vector<HostLayer>& net, std::vector<unsigned char>& out) {
   if (which(s) == Inst::W25) pack_net<25, 50, 100>(net, out);
   if (which(s) == Inst::W32) pack_net<32, 64, 128>(net, out);
-}
-
-int tc_pieces(const SeaDev& s) {
-  int mx = 0;
-  for (int t = 0; t < s.ntypes; ++t) mx = std::max(mx, s.sel[t]);
-  return (mx + 127) / 128 + 1;
 }
 
 void launch_edge_count(cudaStream_t st, const SeaDev& s, int nloc, const int* type_start, const int* perm_atom,
@@ -936,50 +917,25 @@ void launch_edge_compact(cudaStream_t st, const SeaDev& s, int nloc, const int* 
                                                                        rt, row, slot);
 }
 
-void launch_tile_table(cudaStream_t st, int nnets, int nloc, const int* eoff, int* tstart) {
+void launch_item_table(cudaStream_t st, const SeaDev& s, int nloc, const int* type_start, int* istart) {
+  (void)nloc;
   count_launch();
-  k_tile_table<<<1, 32, 0, st>>>(nnets, nloc, eoff, tstart);
+  k_item_table<<<1, 32, 0, st>>>(s.nnets, s.ntypes, s.type_one_side, type_start, istart);
 }
 
-int embed_tc_grid(const SeaDev&) {
+int embed_tc_grid(const SeaDev&, bool backward) {
   int dev = 0, nsm = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-  return nsm;  // one CTA per SM (TMEM 256 columns and ~120 KB shared memory each)
-}
-
-template <int D1, int D2, int D3>
-static void launch_fwd(cudaStream_t st, const SeaDev& s, const TcLists& L, int grid, const unsigned char* nets,
-                       float* partial, int* err) {
-  using S = TcShape<D1, D2, D3>;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(k_embed_fwd_tc<D1, D2, D3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::SMEM);
-    attr = true;
-  }
-  FwdArgs a{L, nets, S::BLOB, partial, err, s.M1};
-  count_launch();
-  k_embed_fwd_tc<D1, D2, D3><<<grid, 128, S::SMEM, st>>>(a);
+  // forward: 2 CTAs per SM (256 TMEM columns, < 100 KB shared memory each);
+  // backward: 1 CTA per SM (512 TMEM columns, ~150 KB shared memory)
+  return backward ? nsm : 2 * nsm;
 }
 
 void launch_embed_fwd_tc(cudaStream_t st, const SeaDev& s, const TcLists& L, int grid, const unsigned char* nets,
-                         float* partial, int* err) {
-  if (which(s) == Inst::W25) launch_fwd<25, 50, 100>(st, s, L, grid, nets, partial, err);
-  if (which(s) == Inst::W32) launch_fwd<32, 64, 128>(st, s, L, grid, nets, partial, err);
-}
-
-template <int D1, int D2, int D3>
-static void launch_bwd(cudaStream_t st, const TcLists& L, int grid, const unsigned char* nets, const float* dT,
-                       const double* rij, double* gslot, int* err, double rcut, double rs) {
-  using Bw = TcBwd<D1, D2, D3>;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(k_embed_bwd_tc<D1, D2, D3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Bw::SMEM);
-    attr = true;
-  }
-  BwdArgs a{L, nets, TcShape<D1, D2, D3>::BLOB, dT, rij, gslot, err, rcut, rs};
-  count_launch();
-  k_embed_bwd_tc<D1, D2, D3><<<grid, 128, Bw::SMEM, st>>>(a);
+                         float* Tq, int* err) {
+  if (which(s) == Inst::W25) launch_fwd<25, 50, 100>(st, L, grid, nets, Tq, err);
+  if (which(s) == Inst::W32) launch_fwd<32, 64, 128>(st, L, grid, nets, Tq, err);
 }
 
 void launch_embed_bwd_tc(cudaStream_t st, const SeaDev& s, const TcLists& L, int grid, const unsigned char* nets,
@@ -994,19 +950,19 @@ void launch_dT(cudaStream_t st, const SeaDev& s, int nloc, const int* type_start
   const size_t smem = sizeof(float) * (4 + s.M2) * s.M1;
   count_launch();
   if (which(s) == Inst::W25)
-    k_dT<100><<<nloc, 128, smem, st>>>(nloc, s.ntypes, s.M2, s.inv_nnei, type_start, perm_atom, T, dD, dT);
+    k_dT<100><<<nloc, 128, smem, st>>>(nloc, s.ntypes, s.M2, (float)s.inv_nnei, type_start, perm_atom, T, dD, dT);
   else
-    k_dT<128><<<nloc, 128, smem, st>>>(nloc, s.ntypes, s.M2, s.inv_nnei, type_start, perm_atom, T, dD, dT);
+    k_dT<128><<<nloc, 128, smem, st>>>(nloc, s.ntypes, s.M2, (float)s.inv_nnei, type_start, perm_atom, T, dD, dT);
 }
 
-void launch_t_combine(cudaStream_t st, const SeaDev& s, const TcLists& L, const int* type_start, const int* perm_atom,
-                      const float* partial, float* T, float* D) {
+void launch_t_combine(cudaStream_t st, const SeaDev& s, const TcLists& L, const int* perm_atom, const int* ftile,
+                      const float* Tq, float* T, float* D, unsigned char* Dt_hi, unsigned char* Dt_lo) {
   if (L.nloc <= 0) return;
   count_launch();
   if (which(s) == Inst::W25)
-    k_t_combine<100><<<L.nloc, 128, 0, st>>>(L, s.ntypes, s.M2, s.inv_nnei, type_start, perm_atom, partial, T, D);
+    k_t_combine<100><<<L.nloc, 128, 0, st>>>(L, s.M2, (float)s.inv_nnei, perm_atom, ftile, Tq, T, D, Dt_hi, Dt_lo);
   else
-    k_t_combine<128><<<L.nloc, 128, 0, st>>>(L, s.ntypes, s.M2, s.inv_nnei, type_start, perm_atom, partial, T, D);
+    k_t_combine<128><<<L.nloc, 128, 0, st>>>(L, s.M2, (float)s.inv_nnei, perm_atom, ftile, Tq, T, D, Dt_hi, Dt_lo);
 }
 
 }  // namespace b200dp

@@ -2,13 +2,15 @@
 //
 // Edges are compacted into one list per embedding net (net q = neighbour type,
 // or centre type * ntypes + neighbour type for two-sided models), ordered by
-// the centre's row in the type-grouped atom order.  A tile is 128 consecutive
-// edges of one list.  Per tile the embedding layers 2 and 3 run as tcgen05
-// MMAs (bf16 hi/lo split, three products, fp32 accumulation in TMEM) and the
+// the centre's row in the type-grouped atom order.  A work item is 8
+// consecutive centre rows of one net; its edges are processed in subtiles of
+// up to 128.  Per subtile the embedding layers 2 and 3 run as tcgen05 MMAs
+// (bf16 hi/lo split, three products, fp32 accumulation in TMEM) and the
 // contraction T^T = G^T R~ runs as a third MMA whose B operand holds each
-// edge's environment row in the column block of its centre atom.  Partial T
-// of the atoms a tile touches are written per (net, atom, piece); a combine
-// kernel sums them in a fixed order, so results are run-to-run identical.
+// edge's environment row in the column block of its centre (8 centres x 4
+// components = 32 columns), accumulated in TMEM across the item's subtiles.
+// Per-net T are summed in a fixed order by the combine kernel, so results are
+// run-to-run identical.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -26,16 +28,17 @@ bool tc_supported(const SeaDev& s);
 size_t tc_net_bytes(const SeaDev& s);
 // Packs one embedding net on the host.
 void tc_pack_net(const SeaDev& s, const std::vector<HostLayer>& net, std::vector<unsigned char>& out);
-// Maximum pieces a (net, atom) contraction can be split into.
-int tc_pieces(const SeaDev& s);
+
+constexpr int kItemRows = 8;  // centre rows per work item
 
 struct TcLists {
-  int nloc, nnets, pieces;
-  const int* eoff;  // [nnets*nloc + 1] exclusive scan of per-(net,row) edge counts
-  const int* tstart;  // [nnets + 1] first global tile of each list
-  const float4* rt;   // [E] environment row (s, s x/r, s y/r, s z/r)
-  const int* row;     // [E] centre row in type-grouped order
-  const int* slot;    // [E] slot in the formatted neighbour list
+  int nloc, nnets, ntypes, type_one_side;
+  const int* eoff;        // [nnets*nloc + 1] exclusive scan of per-(net,row) edge counts
+  const int* istart;      // [nnets + 1] first work item of each net
+  const int* type_start;  // [ntypes + 1] rows of each centre type
+  const float4* rt;       // [E] environment row (s, s x/r, s y/r, s z/r)
+  const int* row;         // [E] centre row in type-grouped order
+  const int* slot;        // [E] slot in the formatted neighbour list
 };
 
 void launch_edge_count(cudaStream_t st, const SeaDev& s, int nloc, const int* type_start, const int* perm_atom,
@@ -43,16 +46,21 @@ void launch_edge_count(cudaStream_t st, const SeaDev& s, int nloc, const int* ty
 void launch_edge_compact(cudaStream_t st, const SeaDev& s, int nloc, const int* type_start, const int* perm_atom,
                          const int* atype, const int* cnt, const double* rij, const int* eoff, float4* rt, int* row,
                          int* slot);
-void launch_tile_table(cudaStream_t st, int nnets, int nloc, const int* eoff, int* tstart);
-int embed_tc_grid(const SeaDev& s);
+void launch_item_table(cudaStream_t st, const SeaDev& s, int nloc, const int* type_start, int* istart);
+// Grid for the persistent kernels (CTAs per SM times SMs).
+int embed_tc_grid(const SeaDev& s, bool backward);
+// Forward: Tq[net][row][4][M1] = sum over the net's edges of the row of R~ (x) G.
 void launch_embed_fwd_tc(cudaStream_t st, const SeaDev& s, const TcLists& L, int grid, const unsigned char* nets,
-                         float* partial, int* err);
-void launch_t_combine(cudaStream_t st, const SeaDev& s, const TcLists& L, const int* type_start, const int* perm_atom,
-                      const float* partial, float* T, float* D);
+                         float* Tq, int* err);
+// T_i = sum over nets (fixed order) / N -> T (atom order, fp32), D (row order,
+// fp32) and, when Dt_hi != nullptr, D pre-tiled for the tensor-core fitting
+// (padded rows from ftile).
+void launch_t_combine(cudaStream_t st, const SeaDev& s, const TcLists& L, const int* perm_atom, const int* ftile,
+                      const float* Tq, float* T, float* D, unsigned char* Dt_hi, unsigned char* Dt_lo);
 // dE/dT per centre row (scaled by 1/N) from T (atom order) and dE/dD (row order).
 void launch_dT(cudaStream_t st, const SeaDev& s, int nloc, const int* type_start, const int* perm_atom, const float* T,
                const float* dD, float* dT);
-// Embedding backward: recomputes the forward per tile, then dG, dR~, the
+// Embedding backward: recomputes the forward per subtile, then dG, dR~, the
 // layer backprop on tensor cores and the chain rule to r_ij (fp64) -> gslot.
 void launch_embed_bwd_tc(cudaStream_t st, const SeaDev& s, const TcLists& L, int grid, const unsigned char* nets,
                          const float* dT, const double* rij, double* gslot, int* err);

@@ -170,7 +170,6 @@ b200dp_status Engine::init(const char* path, const b200dp_options* o) {
     }
     B200DP_CUDA_TRY(tc_nets.ensure(all.size()));
     B200DP_CUDA_TRY(cudaMemcpy(tc_nets.ptr, all.data(), all.size(), cudaMemcpyHostToDevice));
-    tc_pieces_n = tc_pieces(sd);
     fplan = fit_tc_plan(hm);
     use_fit_tc = fplan.ok;
   }
@@ -316,7 +315,7 @@ b200dp_status Engine::ensure_buffers(int nloc, int nall, int ncells, int ncand) 
     B200DP_CUDA_TRY(rec_rt.ensure(sizeof(float4) * S));
     B200DP_CUDA_TRY(rec_row.ensure(sizeof(int) * S));
     B200DP_CUDA_TRY(rec_slot.ensure(sizeof(int) * S));
-    B200DP_CUDA_TRY(partial.ensure(sizeof(float) * NL * tc_pieces_n * 4 * sd.M1));
+    B200DP_CUDA_TRY(partial.ensure(sizeof(float) * NL * 4 * sd.M1));
     B200DP_CUDA_TRY(dTbuf.ensure(sizeof(float) * L * 4 * sd.M1));
   }
   if (use_fit_tc) {
@@ -407,6 +406,21 @@ void Engine::mark(cudaStream_t st, int k) {
   if (timing) cudaEventRecord(events[k], st);
 }
 
+TcLists Engine::tc_lists(int nloc) const {
+  TcLists L;
+  L.nloc = nloc;
+  L.nnets = sd.nnets;
+  L.ntypes = sd.ntypes;
+  L.type_one_side = sd.type_one_side;
+  L.eoff = eoff.as<int>();
+  L.istart = tstart.as<int>();
+  L.type_start = type_start.as<int>();
+  L.rt = rec_rt.as<float4>();
+  L.row = rec_row.as<int>();
+  L.slot = rec_slot.as<int>();
+  return L;
+}
+
 FormatSpec Engine::format_spec(int nloc, int nall) const {
   FormatSpec f;
   std::memset(&f, 0, sizeof(f));
@@ -439,12 +453,19 @@ b200dp_status Engine::run_model(cudaStream_t st, int nloc, int nall, const int* 
     launch_edge_compact(st, sd, nloc, type_start.as<int>(), perm_atom.as<int>(), d_atype, nl_cnt.as<int>(),
                         nl_rij.as<double>(), eoff.as<int>(), rec_rt.as<float4>(), rec_row.as<int>(),
                         rec_slot.as<int>());
-    launch_tile_table(st, sd.nnets, nloc, eoff.as<int>(), tstart.as<int>());
-    TcLists Lst{nloc, sd.nnets, tc_pieces_n, eoff.as<int>(), tstart.as<int>(), rec_rt.as<float4>(),
-                rec_row.as<int>(), rec_slot.as<int>()};
-    launch_embed_fwd_tc(st, sd, Lst, embed_tc_grid(sd), tc_nets.as<unsigned char>(), partial.as<float>(), err_d);
-    launch_t_combine(st, sd, Lst, type_start.as<int>(), perm_atom.as<int>(), partial.as<float>(),
-                     reinterpret_cast<float*>(Tbuf.ptr), reinterpret_cast<float*>(Dbuf.ptr));
+    launch_item_table(st, sd, nloc, type_start.as<int>(), tstart.as<int>());
+    const TcLists Lst = tc_lists(nloc);
+    launch_embed_fwd_tc(st, sd, Lst, embed_tc_grid(sd, false), tc_nets.as<unsigned char>(), partial.as<float>(),
+                        err_d);
+    unsigned char* dth = nullptr;
+    unsigned char* dtl = nullptr;
+    if (use_fit_tc) {
+      launch_fit_tile_table(st, hm.ntypes, type_start.as<int>(), ftile.as<int>());
+      dth = At_hi[0].as<unsigned char>();
+      dtl = At_lo[0].as<unsigned char>();
+    }
+    launch_t_combine(st, sd, Lst, perm_atom.as<int>(), ftile.as<int>(), partial.as<float>(),
+                     reinterpret_cast<float*>(Tbuf.ptr), reinterpret_cast<float*>(Dbuf.ptr), dth, dtl);
   } else {
     const int gf = descriptor_grid<P>(sd, ch_fwd, false, nloc);
     launch_descriptor_fwd<P>(st, sd, nloc, ch_fwd, gf, nl_rij.as<double>(), nl_cnt.as<int>(), d_atype,
@@ -466,9 +487,6 @@ b200dp_status Engine::run_model(cudaStream_t st, int nloc, int nall, const int* 
       fb.Z_lo[q] = Z_lo[q].as<unsigned char>();
       fb.DY[q] = DYf[q].as<float>();
     }
-    launch_fit_tile_table(st, hm.ntypes, type_start.as<int>(), ftile.as<int>());
-    launch_fit_tile_D(st, nloc, hm.ntypes, sd.dim, type_start.as<int>(), ftile.as<int>(),
-                      reinterpret_cast<const float*>(Dbuf.ptr), fb.At_hi[0], fb.At_lo[0]);
     launch_fit_tc(st, fplan, hm.ntypes, nloc, type_start.as<int>(), ftile.as<int>(), perm_atom.as<int>(),
                   fitw.data(), fb, atom_e.as<double>(), reinterpret_cast<float*>(dDbuf.ptr), err_d);
   } else {
@@ -511,11 +529,10 @@ b200dp_status Engine::run_model(cudaStream_t st, int nloc, int nall, const int* 
   }
   mark(st, 3);
   if (std::is_same<P, float>::value && use_tc) {
-    TcLists Lst{nloc, sd.nnets, tc_pieces_n, eoff.as<int>(), tstart.as<int>(), rec_rt.as<float4>(),
-                rec_row.as<int>(), rec_slot.as<int>()};
+    const TcLists Lst = tc_lists(nloc);
     launch_dT(st, sd, nloc, type_start.as<int>(), perm_atom.as<int>(), reinterpret_cast<const float*>(Tbuf.ptr),
               reinterpret_cast<const float*>(dDbuf.ptr), dTbuf.as<float>());
-    launch_embed_bwd_tc(st, sd, Lst, embed_tc_grid(sd), tc_nets.as<unsigned char>(), dTbuf.as<float>(),
+    launch_embed_bwd_tc(st, sd, Lst, embed_tc_grid(sd, true), tc_nets.as<unsigned char>(), dTbuf.as<float>(),
                         nl_rij.as<double>(), gslot.as<double>(), err_d);
   } else {
     const int gb = descriptor_grid<P>(sd, ch_bwd, true, nloc);

@@ -53,7 +53,6 @@ struct Engine {
   DevBuf cand_start, cand_list, ilist_d;
   // tensor-core embedding path (mixed mode)
   bool use_tc = false;
-  int tc_pieces_n = 0;
   DevBuf tc_nets, ecount, eoff, tstart, rec_rt, rec_row, rec_slot, partial, scan_scratch, dTbuf;
   // tensor-core fitting (mixed mode)
   bool use_fit_tc = false;
@@ -85,6 +84,7 @@ struct Engine {
   b200dp_status ensure_buffers(int nloc, int nall, int ncells, int ncand);
   b200dp_status make_grid(int nall, const double* box, const double* region, bool periodic, GridSpec& g);
   FormatSpec format_spec(int nloc, int nall) const;
+  TcLists tc_lists(int nloc) const;
   void mark(cudaStream_t st, int k);
   bool last_stream_valid() const { return true; }
 

@@ -18,12 +18,7 @@ constexpr long long kWaitLimit = 1LL << 26;
 
 __device__ __forceinline__ float tanh_fast(float x) { return 1.0f - __fdividef(2.0f, __expf(2.0f * x) + 1.0f); }
 
-// Byte offset of element (row, k) of a tiled activation with kpad columns.
-__device__ __forceinline__ size_t tiled_off(int prow, int k, int kpad) {
-  const int rt = prow >> 7, r = prow & 127;
-  return ((size_t)rt * (kpad / kFitBK) + k / kFitBK) * kABlock + (uint32_t)(r >> 3) * kSbo +
-         (uint32_t)((k % kFitBK) >> 3) * 128 + (uint32_t)(r & 7) * 16 + (uint32_t)(k & 7) * 2;
-}
+using umma::tiled_off;
 
 __device__ __forceinline__ void store8_split(unsigned char* hi, unsigned char* lo, const float* v) {
   uint32_t h[4], l[4];

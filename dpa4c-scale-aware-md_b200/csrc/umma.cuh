@@ -131,6 +131,15 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                : "memory");
 }
 
+// Byte offset of element (row, k) in a pre-tiled activation operand: blocks
+// of 128 rows x 32 columns (8 KB per bf16 half), K-major no-swizzle inside,
+// kpad columns per row (a multiple of 32).
+__host__ __device__ __forceinline__ size_t tiled_off(int prow, int k, int kpad) {
+  const int rt = prow >> 7, r = prow & 127;
+  return ((size_t)rt * (kpad / 32) + k / 32) * 8192u + (uint32_t)(r >> 3) * 512u + (uint32_t)((k % 32) >> 3) * 128u +
+         (uint32_t)(r & 7) * 16u + (uint32_t)(k & 7) * 2u;
+}
+
 // bf16 split of an fp32 value: x ~= hi + lo with |x - hi - lo| <~ 2^-17 |x|.
 __device__ __forceinline__ void split_bf16(float x, __nv_bfloat16& hi, __nv_bfloat16& lo) {
   hi = __float2bfloat16_rn(x);
