@@ -15,6 +15,7 @@ namespace {
 __device__ __forceinline__ float tanh_fast(float x) { return 1.0f - __fdividef(2.0f, __expf(2.0f * x) + 1.0f); }
 
 constexpr long long kWaitLimit = 1LL << 26;
+constexpr int kFwdGroups = 3;  // groups of 4 warps per CTA in the forward kernel
 
 // Packed net blob (global memory and the front of shared memory):
 // [w2 hi|lo][w3 hi|lo][w1 b1 b2 b3 fp32].  W2 and W3 are stored as K-major B
@@ -91,7 +92,7 @@ __device__ __forceinline__ Item item_of(const TcLists& L, int it) {
     rb0 = L.type_start[ti];
     re0 = L.type_start[ti + 1];
   }
-  r.rb = rb0 + kItemRows * (it - L.istart[q]);
+  r.rb = min(rb0 + kItemRows * (it - L.istart[q]), re0);  // padded items are empty
   r.re = min(r.rb + kItemRows, re0);
   r.e0 = L.eoff[(size_t)q * L.nloc + r.rb];
   r.e1 = L.eoff[(size_t)q * L.nloc + r.re];
@@ -99,20 +100,26 @@ __device__ __forceinline__ Item item_of(const TcLists& L, int it) {
 }
 
 // ---------------------------------------------------------------- forward
-template <int D1, int D2, int D3>
+// NG independent groups of 4 warps per CTA share the current net's weights;
+// each group runs its own work item with its own TMEM slice (D2 and D3 share
+// columns, T after them), mbarrier and named barrier, so tensor-core waits of
+// one group overlap the SIMT epilogues of the others.
+template <int D1, int D2, int D3, int NG>
 struct Fwd {
   using F = TcShape<D1, D2, D3>;
   static constexpr int NT = 4 * kItemRows;           // contraction columns
   static constexpr uint32_t A1B = 128 * F::D1p * 2;  // one bf16 half
   static constexpr uint32_t XB = 128 * 64 * 2;       // A2 (K <= 64) or G^T half (M = 128 a, K = 64 edges)
   static constexpr uint32_t RB = NT * 64 * 2;        // R~ half (N = 32, K = 64 edges)
-  static constexpr uint32_t O_A1 = F::O_END;
-  static constexpr uint32_t O_X = O_A1 + 2 * A1B;
-  static constexpr uint32_t O_R = O_X + 2 * XB;
-  static constexpr uint32_t SMEM = O_R + 2 * RB;
+  static constexpr uint32_t GS = 2 * A1B + 2 * XB + 2 * RB;  // per-group bytes
+  static constexpr uint32_t O_G0 = F::O_END;
+  static constexpr uint32_t SMEM = O_G0 + NG * GS;
   static constexpr uint32_t LBO_G = (128 / 8) * 128, SBO_G = 128;  // MN-major
   static constexpr uint32_t LBO_R = (NT / 8) * 128, SBO_R = 128;   // MN-major
-  static constexpr uint32_t C_D2 = 0, C_D3 = 64, C_T = 192, NCOLS = 256;
+  static constexpr uint32_t COLS = 160;                            // per group: D2/D3 [0,128), T [128,160)
+  static constexpr uint32_t C_D = 0, C_T = 128, NCOLS = 512;
+  static_assert(NG * COLS <= NCOLS, "TMEM budget");
+  static_assert(F::D3p <= 128, "D3 must fit the shared accumulator columns");
 };
 
 struct FwdArgs {
@@ -123,35 +130,38 @@ struct FwdArgs {
   int* err;
 };
 
-template <int D1, int D2, int D3>
-__global__ void __launch_bounds__(128, 2) k_embed_fwd_tc(FwdArgs a) {
+template <int D1, int D2, int D3, int NG>
+__global__ void __launch_bounds__(128 * NG, 1) k_embed_fwd_tc(FwdArgs a) {
   using F = TcShape<D1, D2, D3>;
-  using S = Fwd<D1, D2, D3>;
+  using S = Fwd<D1, D2, D3, NG>;
   extern __shared__ __align__(1024) unsigned char smem[];
-  __shared__ uint64_t bar;
+  __shared__ uint64_t bars[NG];
   __shared__ uint32_t tbase;
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int gtid = threadIdx.x, g = gtid >> 7, tid = gtid & 127, warp = tid >> 5;
+  const int bid = 1 + g;  // named barrier of this group
   const float* w1 = reinterpret_cast<const float*>(smem + F::O_F);
   const float* b1 = w1 + D1;
   const float* b2 = b1 + D1;
   const float* b3 = b2 + D2;
   const uint32_t w2h = umma::smem_u32(smem + F::O_W2), w2l = w2h + F::W2B;
   const uint32_t w3h = umma::smem_u32(smem + F::O_W3), w3l = w3h + F::W3B;
-  unsigned char* a1h = smem + S::O_A1;
+  unsigned char* gbase = smem + S::O_G0 + g * S::GS;
+  unsigned char* a1h = gbase;
   unsigned char* a1l = a1h + S::A1B;
-  unsigned char* xh = smem + S::O_X;
+  unsigned char* xh = a1l + S::A1B;
   unsigned char* xl = xh + S::XB;
-  unsigned char* rh = smem + S::O_R;
+  unsigned char* rh = xl + S::XB;
   unsigned char* rl = rh + S::RB;
-  if (warp == 0) umma::tmem_alloc(&tbase, S::NCOLS);
+  uint64_t* bar = &bars[g];
+  if ((gtid >> 5) == 0) umma::tmem_alloc(&tbase, S::NCOLS);
   if (tid == 0) {
-    umma::mbar_init(&bar, 1);
+    umma::mbar_init(bar, 1);
     umma::fence_mbar_init();
   }
   umma::fence_before_sync();
   __syncthreads();
   umma::fence_after_sync();
-  const uint32_t tm = tbase;
+  const uint32_t tm = tbase + g * S::COLS;
   const uint32_t lb = (uint32_t)(warp * 32) << 16;
   uint32_t phase = 0;
   int loaded = -1;
@@ -164,26 +174,29 @@ __global__ void __launch_bounds__(128, 2) k_embed_fwd_tc(FwdArgs a) {
   auto sync_mma = [&]() {
     umma::fence_proxy_async();
     umma::fence_before_sync();
-    __syncthreads();
+    umma::bar_sync(bid, 128);
     umma::fence_after_sync();
   };
   auto wait_mma = [&]() -> bool {
-    const bool ok = umma::mbar_wait(&bar, phase, kWaitLimit);
+    const bool ok = umma::mbar_wait(bar, phase, kWaitLimit);
     phase ^= 1;
-    if (__syncthreads_or(!ok)) return false;
+    if (umma::bar_sync_or(bid, 128, !ok)) return false;
     umma::fence_after_sync();
     return true;
   };
-  for (int it = blockIdx.x; it < nitems && !aborted; it += gridDim.x) {
-    const Item I = item_of(L, it);
-    if (I.q != loaded) {
+  // rounds of NG consecutive items, all of one net (item counts are padded)
+  for (int base = blockIdx.x * NG; base < nitems; base += gridDim.x * NG) {
+    const int qr = item_of(L, base).q;
+    if (qr != loaded) {
       __syncthreads();
-      const uint4* src = reinterpret_cast<const uint4*>(a.nets + (size_t)I.q * a.net_bytes);
+      const uint4* src = reinterpret_cast<const uint4*>(a.nets + (size_t)qr * a.net_bytes);
       uint4* dst = reinterpret_cast<uint4*>(smem);
-      for (uint32_t i = tid; i < F::BLOB / 16; i += 128) dst[i] = src[i];
-      loaded = I.q;
+      for (uint32_t i = gtid; i < F::BLOB / 16; i += 128 * NG) dst[i] = src[i];
+      loaded = qr;
       __syncthreads();
     }
+    if (aborted) continue;  // keep taking part in the CTA-wide barriers above
+    const Item I = item_of(L, base + g);
     bool first = true;
     for (int sub = I.e0; sub < I.e1 && !aborted; sub += 128) {
       const int ne = min(128, I.e1 - sub);
@@ -203,9 +216,9 @@ __global__ void __launch_bounds__(128, 2) k_embed_fwd_tc(FwdArgs a) {
       }
       sync_mma();
       if (tid == 0) {
-        mma3(tm + S::C_D2, umma::smem_u32(a1h), umma::smem_u32(a1l), w2h, w2l, 128, F::SBO_A1, 128, F::SBO_W2, id2,
+        mma3(tm + S::C_D, umma::smem_u32(a1h), umma::smem_u32(a1l), w2h, w2l, 128, F::SBO_A1, 128, F::SBO_W2, id2,
              F::D1p / 16, 256, 256, false);
-        umma::commit(&bar);
+        umma::commit(bar);
       }
       if (!wait_mma()) {
         aborted = true;
@@ -215,7 +228,7 @@ __global__ void __launch_bounds__(128, 2) k_embed_fwd_tc(FwdArgs a) {
 #pragma unroll
       for (int c = 0; c < F::D2p / 16; ++c) {
         float v[16];
-        umma::ld16(tm + lb + S::C_D2 + c * 16, v);
+        umma::ld16(tm + lb + S::C_D + c * 16, v);
         umma::wait_ld();
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
@@ -231,11 +244,11 @@ __global__ void __launch_bounds__(128, 2) k_embed_fwd_tc(FwdArgs a) {
         const uint32_t o = (tid >> 3) * F::SBO_A2 + kg * 128 + (tid & 7) * 16;
         store8_split(xh + o, xl + o, v);
       }
-      sync_mma();
+      sync_mma();  // also orders every D2 read before MMA3 overwrites the columns
       if (tid == 0) {
-        mma3(tm + S::C_D3, umma::smem_u32(xh), umma::smem_u32(xl), w3h, w3l, 128, F::SBO_A2, 128, F::SBO_W3, id3,
+        mma3(tm + S::C_D, umma::smem_u32(xh), umma::smem_u32(xl), w3h, w3l, 128, F::SBO_A2, 128, F::SBO_W3, id3,
              F::D2p / 16, 256, 256, false);
-        umma::commit(&bar);
+        umma::commit(bar);
       }
       if (!wait_mma()) {
         aborted = true;
@@ -249,7 +262,7 @@ __global__ void __launch_bounds__(128, 2) k_embed_fwd_tc(FwdArgs a) {
 #pragma unroll
           for (int c = 0; c < F::D3p / 16; ++c) {
             float v[16];
-            umma::ld16(tm + lb + S::C_D3 + c * 16, v);
+            umma::ld16(tm + lb + S::C_D + c * 16, v);
             umma::wait_ld();
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
@@ -279,7 +292,7 @@ __global__ void __launch_bounds__(128, 2) k_embed_fwd_tc(FwdArgs a) {
         if (tid == 0) {
           mma3(tm + S::C_T, umma::smem_u32(xh), umma::smem_u32(xl), umma::smem_u32(rh), umma::smem_u32(rl), S::LBO_G,
                S::SBO_G, S::LBO_R, S::SBO_R, idT, 64 / 16, 2 * S::LBO_G, 2 * S::LBO_R, !first);
-          umma::commit(&bar);
+          umma::commit(bar);
         }
         first = false;
         if (!wait_mma()) {
@@ -288,7 +301,7 @@ __global__ void __launch_bounds__(128, 2) k_embed_fwd_tc(FwdArgs a) {
         }
       }
     }
-    if (aborted) break;
+    if (aborted) continue;
     if (I.e1 > I.e0) {
       float v[32];
       umma::ld16(tm + lb + S::C_T, v);
@@ -309,13 +322,13 @@ __global__ void __launch_bounds__(128, 2) k_embed_fwd_tc(FwdArgs a) {
       }
     }
     umma::fence_before_sync();
-    __syncthreads();
+    umma::bar_sync(bid, 128);
     umma::fence_after_sync();
   }
   if (aborted && tid == 0) atomicAdd(a.err + kErrTcTimeout, 1);
   umma::fence_before_sync();
   __syncthreads();
-  if (warp == 0) umma::tmem_dealloc(tm, S::NCOLS);
+  if ((gtid >> 5) == 0) umma::tmem_dealloc(tbase, S::NCOLS);
 }
 
 // ---------------------------------------------------------------- backward
@@ -783,6 +796,8 @@ __global__ void k_edge_compact(SeaDev s, int nloc, const int* __restrict__ type_
   }
 }
 
+// Items per net are padded to a multiple of kFwdGroups so that a round of
+// the grouped forward kernel never mixes nets (padded items are empty).
 __global__ void k_item_table(int nnets, int ntypes, int tos, const int* __restrict__ type_start,
                              int* __restrict__ istart) {
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
@@ -796,7 +811,8 @@ __global__ void k_item_table(int nnets, int ntypes, int tos, const int* __restri
       const int ti = q / ntypes;
       rows = type_start[ti + 1] - type_start[ti];
     }
-    acc += (rows + kItemRows - 1) / kItemRows;
+    const int items = (rows + kItemRows - 1) / kItemRows;
+    acc += (items + kFwdGroups - 1) / kFwdGroups * kFwdGroups;
     istart[q + 1] = acc;
   }
 }
@@ -852,15 +868,16 @@ Inst which(const SeaDev& s) {
 
 template <int D1, int D2, int D3>
 void launch_fwd(cudaStream_t st, const TcLists& L, int grid, const unsigned char* nets, float* Tq, int* err) {
-  using S = Fwd<D1, D2, D3>;
+  using S = Fwd<D1, D2, D3, kFwdGroups>;
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(k_embed_fwd_tc<D1, D2, D3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::SMEM);
+    cudaFuncSetAttribute(k_embed_fwd_tc<D1, D2, D3, kFwdGroups>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)S::SMEM);
     attr = true;
   }
   FwdArgs a{L, nets, TcShape<D1, D2, D3>::BLOB, Tq, err};
   count_launch();
-  k_embed_fwd_tc<D1, D2, D3><<<grid, 128, S::SMEM, st>>>(a);
+  k_embed_fwd_tc<D1, D2, D3, kFwdGroups><<<grid, 128 * kFwdGroups, S::SMEM, st>>>(a);
 }
 
 template <int D1, int D2, int D3>
@@ -927,9 +944,8 @@ int embed_tc_grid(const SeaDev&, bool backward) {
   int dev = 0, nsm = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-  // forward: 2 CTAs per SM (256 TMEM columns, < 100 KB shared memory each);
-  // backward: 1 CTA per SM (512 TMEM columns, ~150 KB shared memory)
-  return backward ? nsm : 2 * nsm;
+  // one CTA per SM: the forward runs kFwdGroups groups in it, the backward one
+  return nsm;
 }
 
 void launch_embed_fwd_tc(cudaStream_t st, const SeaDev& s, const TcLists& L, int grid, const unsigned char* nets,

@@ -131,6 +131,24 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                : "memory");
 }
 
+// Named barrier over `count` threads (id 1..15; id 0 is __syncthreads).
+__device__ __forceinline__ void bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+// Named barrier that also ORs a predicate over the participating threads.
+__device__ __forceinline__ bool bar_sync_or(int id, int count, bool pred) {
+  uint32_t res;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}\n"
+      : "=r"(res)
+      : "r"((uint32_t)pred), "r"(id), "r"(count)
+      : "memory");
+  return res != 0;
+}
+
 // Byte offset of element (row, k) in a pre-tiled activation operand: blocks
 // of 128 rows x 32 columns (8 KB per bf16 half), K-major no-swizzle inside,
 // kpad columns per row (a multiple of 32).
