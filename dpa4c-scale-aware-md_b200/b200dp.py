@@ -30,7 +30,7 @@ EXPORTS = [
     "b200dp_options_default", "b200dp_create", "b200dp_destroy", "b200dp_last_error", "b200dp_model_info_get",
     "b200dp_compute_host", "b200dp_compute_host_nlist", "b200dp_compute_device", "b200dp_check",
     "b200dp_sel_overflow_count", "b200dp_last_nlist", "b200dp_last_descriptor", "b200dp_set_stage_timing",
-    "b200dp_stage_times", "b200dp_kernel_launches", "b200dp_selftest_mma",
+    "b200dp_stage_times", "b200dp_kernel_launches", "b200dp_selftest_mma", "b200dp_build_nlist_noalloc",
 ]
 
 
@@ -94,6 +94,8 @@ def load_library(path: str = LIB_PATH):
     L.b200dp_selftest_mma.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                       ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_float),
                                       ctypes.POINTER(ctypes.c_float)]
+    L.b200dp_build_nlist_noalloc.argtypes = [_vp, ctypes.c_int, ctypes.c_int, _vp, _vp, _dp, _dp, ctypes.c_double,
+                                             ctypes.c_int, _ip, _vp, _vp, _vp]
     L.b200dp_kernel_launches.argtypes = []
     L.b200dp_kernel_launches.restype = ctypes.c_longlong
     for name in EXPORTS:

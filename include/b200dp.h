@@ -160,6 +160,25 @@ b200dp_status b200dp_set_stage_timing(b200dp_engine* engine, int enable);
  * device buffers. */
 b200dp_status b200dp_selftest_mma(int K, int N, int a_mn_major, int b_mn_major, int passes, const float* A,
                                   const float* B, float* C);
+/* Neighbour-list build that allocates no device memory (no counterpart in the
+ * reference; it exists for callers that must not call cudaMalloc while they
+ * run, e.g. an MD engine whose memory pool already owns the GPU, or a step
+ * loop that cannot afford the device synchronisation cudaMalloc/cudaFree may
+ * cause).  Produces the same formatted list as b200dp_compute_device (same
+ * arguments meaning; rcut, ntypes and sel[ntypes] given directly, no engine):
+ * d_nlist and d_image [nlocal*sum(sel)] int32, d_rij [nlocal*sum(sel)*3] fp64,
+ * all caller-owned device buffers.  Scratch lives in one static device array
+ * of about 4.5 MiB that every GPU loading the library keeps until exit; it
+ * limits nlocal + nghost to 65536 (larger inputs return B200DP_ERR_CAPACITY)
+ * and the binning grid to 65536 cells (coarsened automatically).  The first
+ * call on a device looks up that array's device address (cudaGetSymbolAddress)
+ * with the device current; make that first call before any stream capture.
+ * All calls share the array, so calls that overlap on the GPU (other streams,
+ * other host threads) race; the call synchronises `stream` before returning
+ * and reports bad types / candidate overflow through its status. */
+b200dp_status b200dp_build_nlist_noalloc(void* stream, int nlocal, int nghost, const double* d_coord,
+                                         const int* d_atype, const double* box, const double* region, double rcut,
+                                         int ntypes, const int* sel, int* d_nlist, int* d_image, double* d_rij);
 /* Total kernels this library has launched in the process (all engines). */
 long long b200dp_kernel_launches(void);
 b200dp_status b200dp_stage_times(b200dp_engine* engine, float* ms5);
