@@ -672,6 +672,8 @@ __global__ void __launch_bounds__(128, 1) k_embed_bwd_tc(BwdArgs a) {
 }
 
 // dT[row][k][a] = (sum_b dD[a][b] T[k][b] + [a < M2] sum_c dD[c][a] T[k][c]) / N
+// dD rows are staged with a stride of M2 + 1 floats so that threads over a
+// read distinct banks.
 template <int D3>
 __global__ void __launch_bounds__(128) k_dT(int nloc, int ntypes, int M2, float inv_nnei,
                                             const int* __restrict__ type_start, const int* __restrict__ perm_atom,
@@ -679,21 +681,25 @@ __global__ void __launch_bounds__(128) k_dT(int nloc, int ntypes, int M2, float 
                                             float* __restrict__ dT) {
   extern __shared__ float sm[];
   float* sT = sm;            // 4 * D3
-  float* sdD = sm + 4 * D3;  // D3 * M2
+  float* sdD = sm + 4 * D3;  // D3 rows of (M2 + 1)
   const int r = blockIdx.x;
   if (r >= type_start[ntypes]) return;
   const int atom = perm_atom[r];
+  const int ld = M2 + 1;
   for (int i = threadIdx.x; i < 4 * D3; i += blockDim.x) sT[i] = T[(size_t)atom * 4 * D3 + i];
-  const float4* src = reinterpret_cast<const float4*>(dD + (size_t)r * D3 * M2);
-  for (int i = threadIdx.x; i < D3 * M2 / 4; i += blockDim.x) reinterpret_cast<float4*>(sdD)[i] = src[i];
+  const float* src = dD + (size_t)r * D3 * M2;
+  for (int i = threadIdx.x; i < D3 * M2; i += blockDim.x) {
+    const int aa = i / M2, b = i - aa * M2;
+    sdD[aa * ld + b] = src[i];
+  }
   __syncthreads();
   for (int idx = threadIdx.x; idx < 4 * D3; idx += blockDim.x) {
     const int k = idx / D3, aa = idx - k * D3;
     const float* tk = sT + k * D3;
     float acc = 0.f;
-    for (int b = 0; b < M2; ++b) acc += sdD[aa * M2 + b] * tk[b];
+    for (int b = 0; b < M2; ++b) acc += sdD[aa * ld + b] * tk[b];
     if (aa < M2)
-      for (int c = 0; c < D3; ++c) acc += sdD[c * M2 + aa] * tk[c];
+      for (int c = 0; c < D3; ++c) acc += sdD[c * ld + aa] * tk[c];
     dT[(size_t)r * 4 * D3 + idx] = acc * inv_nnei;
   }
 }
@@ -963,7 +969,7 @@ void launch_embed_bwd_tc(cudaStream_t st, const SeaDev& s, const TcLists& L, int
 void launch_dT(cudaStream_t st, const SeaDev& s, int nloc, const int* type_start, const int* perm_atom, const float* T,
                const float* dD, float* dT) {
   if (nloc <= 0) return;
-  const size_t smem = sizeof(float) * (4 + s.M2) * s.M1;
+  const size_t smem = sizeof(float) * (4 + s.M2 + 1) * s.M1;
   count_launch();
   if (which(s) == Inst::W25)
     k_dT<100><<<nloc, 128, smem, st>>>(nloc, s.ntypes, s.M2, (float)s.inv_nnei, type_start, perm_atom, T, dD, dT);

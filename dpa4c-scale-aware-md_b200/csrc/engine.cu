@@ -198,12 +198,12 @@ b200dp_status Engine::init(const char* path, const b200dp_options* o) {
       for (int l = 0; l < fplan.L; ++l) {
         const HostLayer& Lr = net[l];
         const int din = Lr.din, dout = Lr.dout;
-        fit_pack_B(dout, fplan.kpad[l], dout,
+        fit_pack_B(dout, fplan.kpad[l], fplan.bnf[l],
                    [&](int n, int k) { return k < din ? Lr.w[(size_t)k * dout + n] : 0.0; }, hi, lo);
         W.fB_hi[l] = up_bytes(hi);
         W.fB_lo[l] = up_bytes(lo);
         const int kp = (dout + 31) / 32 * 32;
-        fit_pack_B(din, kp, l == 0 ? fplan.bn_out : din,
+        fit_pack_B(din, kp, l == 0 ? fplan.bn_out : fplan.bnb[l],
                    [&](int n, int k) { return k < dout ? Lr.w[(size_t)n * dout + k] : 0.0; }, hi, lo);
         W.bB_hi[l] = up_bytes(hi);
         W.bB_lo[l] = up_bytes(lo);
@@ -527,11 +527,12 @@ b200dp_status Engine::run_model(cudaStream_t st, int nloc, int nall, const int* 
       }
     }
   }
+  if (std::is_same<P, float>::value && use_tc)
+    launch_dT(st, sd, nloc, type_start.as<int>(), perm_atom.as<int>(), reinterpret_cast<const float*>(Tbuf.ptr),
+              reinterpret_cast<const float*>(dDbuf.ptr), dTbuf.as<float>());
   mark(st, 3);
   if (std::is_same<P, float>::value && use_tc) {
     const TcLists Lst = tc_lists(nloc);
-    launch_dT(st, sd, nloc, type_start.as<int>(), perm_atom.as<int>(), reinterpret_cast<const float*>(Tbuf.ptr),
-              reinterpret_cast<const float*>(dDbuf.ptr), dTbuf.as<float>());
     launch_embed_bwd_tc(st, sd, Lst, embed_tc_grid(sd, true), tc_nets.as<unsigned char>(), dTbuf.as<float>(),
                         nl_rij.as<double>(), gslot.as<double>(), err_d);
   } else {

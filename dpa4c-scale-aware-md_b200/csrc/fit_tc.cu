@@ -253,6 +253,14 @@ __global__ void k_fit_tile_D(int nloc, int ntypes, int dim, const int* __restric
 
 int round32(int x) { return (x + 31) / 32 * 32; }
 
+// Largest N tile that is a multiple of 16, at most 128 and divides w into at
+// least two tiles (more CTAs per layer); w itself when no such tile exists.
+int split_bn(int w) {
+  for (int bn = 128; bn >= 16; bn -= 16)
+    if (w % bn == 0 && w / bn >= 2) return bn;
+  return w;
+}
+
 }  // namespace
 
 FitTcPlan fit_tc_plan(const HostModel& m) {
@@ -268,6 +276,10 @@ FitTcPlan fit_tc_plan(const HostModel& m) {
     p.kpad[l] = l == 0 ? p.dim : round32(m.fit[l - 1]);
     p.res[l] = (l >= 1 && w == din) ? 1 : 0;
     din = w;
+  }
+  for (int l = 0; l < p.L; ++l) {
+    p.bnf[l] = (l == p.L - 1) ? p.width[l] : split_bn(p.width[l]);
+    p.bnb[l] = (l == 0) ? 0 : split_bn(p.width[l - 1]);
   }
   p.bn_out = 0;
   for (int bn = 256; bn >= 16; bn -= 16)
@@ -357,7 +369,7 @@ void launch_fit_tc(cudaStream_t st, const FitTcPlan& p, int ntypes, int nloc, co
       a.wo[t] = w[t].wo;
       a.bo[t] = w[t].bo;
     }
-    a.BN = p.width[l];
+    a.BN = p.bnf[l];
     a.N = p.width[l];
     a.mode = kFwd;
     a.Yprev = p.res[l] ? b.Y[l - 1] : nullptr;
@@ -377,7 +389,7 @@ void launch_fit_tc(cudaStream_t st, const FitTcPlan& p, int ntypes, int nloc, co
       a.atom_e = atom_energy;
     }
     a.err = err;
-    run_gemm(st, a, row_tiles, 1);
+    run_gemm(st, a, row_tiles, p.width[l] / p.bnf[l]);
   }
   for (int s = 0; s < L; ++s) {
     const int l = L - 1 - s;
@@ -396,7 +408,7 @@ void launch_fit_tc(cudaStream_t st, const FitTcPlan& p, int ntypes, int nloc, co
     }
     a.err = err;
     if (l >= 1) {
-      a.BN = p.width[l - 1];
+      a.BN = p.bnb[l];
       a.N = p.width[l - 1];
       a.mode = kBwd;
       a.dy_is_wo = (p.res[l] && l == L - 1) ? 1 : 0;
@@ -406,7 +418,7 @@ void launch_fit_tc(cudaStream_t st, const FitTcPlan& p, int ntypes, int nloc, co
       a.Z_hi = b.Z_hi[(s + 1) & 1];
       a.Z_lo = b.Z_lo[(s + 1) & 1];
       a.kpad_z = round32(p.width[l - 1]);
-      run_gemm(st, a, row_tiles, 1);
+      run_gemm(st, a, row_tiles, p.width[l - 1] / p.bnb[l]);
     } else {
       a.BN = p.bn_out;
       a.N = p.dim;

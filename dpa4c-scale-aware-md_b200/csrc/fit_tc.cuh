@@ -31,6 +31,8 @@ struct FitTcPlan {
   int kpad[kFitMaxLayers] = {};   // padded K of each layer's input
   int res[kFitMaxLayers] = {};    // residual on layer l
   int bn_out = 0;                 // N tile of the final dE/dD GEMM
+  int bnf[kFitMaxLayers] = {};    // N tile of each forward layer (the last one keeps whole rows)
+  int bnb[kFitMaxLayers] = {};    // N tile of each backward layer
   bool ok = false;
 };
 

@@ -218,8 +218,8 @@ constexpr int kFmtWarps = 4;
 __device__ __forceinline__ int floor_div(int a, int n) { return a >= 0 ? a / n : -((-a + n - 1) / n); }
 
 size_t format_smem_bytes(int cap) {
-  // per warp: r2 (8) + r (24) + j, code, type (12) bytes per candidate
-  return (size_t)kFmtWarps * cap * 44;
+  // per warp: r2 (8) + r (24) + j, code, type, type-grouped index (16) bytes per candidate
+  return (size_t)kFmtWarps * cap * 48;
 }
 
 struct CandBuf {
@@ -228,35 +228,67 @@ struct CandBuf {
   int* j;
   int* code;
   int* t;
+  int* grp;  // candidate indices grouped by type, stable within a type
 };
 
 __device__ __forceinline__ CandBuf cand_buf(unsigned char* smem, int warp, int cap) {
-  unsigned char* base = smem + (size_t)warp * cap * 44;
+  unsigned char* base = smem + (size_t)warp * cap * 48;
   CandBuf b;
   b.r2 = reinterpret_cast<double*>(base);
   b.r = b.r2 + cap;
   b.j = reinterpret_cast<int*>(b.r + 3 * cap);
   b.code = b.j + cap;
   b.t = b.code + cap;
+  b.grp = b.t + cap;
   return b;
 }
 
-// Rank sort of one centre's candidates and the row write.  Keys are unique
-// (j, image) pairs, so the order (type, r^2, j, image) is total and the output
-// does not depend on the order candidates were found in.
+// Orders one centre's candidates and writes its row.  Candidates are first
+// grouped by type (stable, by warp ballots), then each is ranked against the
+// candidates of its own type by (r^2, j, image).  Keys are unique (j, image)
+// pairs, so the order is total and does not depend on the order in which the
+// candidates were found.
 __device__ void emit_row(const FormatSpec& f, int i, const CandBuf& b, int ncand, int lane, int* __restrict__ nl_j,
                          int* __restrict__ nl_code, double* __restrict__ nl_rij, int* __restrict__ nl_cnt,
                          int* __restrict__ err) {
+  const unsigned lt_mask = (1u << lane) - 1u;
+  int toff[kMaxTypes + 1];
+  int tcnt[kMaxTypes];
+  // counts per type
+  toff[0] = 0;
+  for (int t = 0; t < f.ntypes; ++t) {
+    int local = 0;
+    for (int c = lane; c < ncand; c += 32) local += (b.t[c] == t);
+    tcnt[t] = warp_sum(local);
+    toff[t + 1] = toff[t] + tcnt[t];
+  }
+  // stable grouping by type
+  int run[kMaxTypes];
+  for (int t = 0; t < f.ntypes; ++t) run[t] = 0;
+  for (int base = 0; base < ncand; base += 32) {
+    const int c = base + lane;
+    const int tc = (c < ncand) ? b.t[c] : -1;
+    for (int t = 0; t < f.ntypes; ++t) {
+      const unsigned m = __ballot_sync(0xffffffffu, tc == t);
+      if (tc == t) b.grp[toff[t] + run[t] + __popc(m & lt_mask)] = c;
+      run[t] += __popc(m);
+    }
+  }
+  __syncwarp();
   for (int c = lane; c < ncand; c += 32) {
     const int t = b.t[c];
     const double r2 = b.r2[c];
     const int j = b.j[c], code = b.code[c];
     int rank = 0;
-    for (int c2 = 0; c2 < ncand; ++c2) {
-      if (b.t[c2] != t) continue;
+    for (int k = toff[t]; k < toff[t + 1]; ++k) {
+      const int c2 = b.grp[k];
       const double q = b.r2[c2];
-      const int j2 = b.j[c2];
-      rank += (q < r2) || (q == r2 && (j2 < j || (j2 == j && b.code[c2] < code)));
+      if (q < r2) {
+        ++rank;
+      } else if (q == r2 && c2 != c) {
+        const int j2 = b.j[c2];
+        rank += (j2 < j || (j2 == j && b.code[c2] < code));
+      }
     }
     if (rank < f.sel[t]) {
       const size_t slot = (size_t)i * f.selt + f.off[t] + rank;
@@ -268,9 +300,7 @@ __device__ void emit_row(const FormatSpec& f, int i, const CandBuf& b, int ncand
     }
   }
   for (int t = 0; t < f.ntypes; ++t) {
-    int local = 0;
-    for (int c = lane; c < ncand; c += 32) local += (b.t[c] == t);
-    const int nt = warp_sum(local);
+    const int nt = tcnt[t];
     const int keep = nt < f.sel[t] ? nt : f.sel[t];
     if (lane == 0) {
       nl_cnt[(size_t)i * f.ntypes + t] = keep;
