@@ -11,11 +11,17 @@ random-init weights, seed 0).  Inputs are seeded synthetic data.
 
 * ``value``: device-timed throughput, inputs resident in HBM, CUDA events on
   the launch stream around each step; L2 is flushed (256 MB write) before
-  every timed step, outside the events.  Multi-GPU: one process per GPU, each
-  rank evaluates its own replica (weak scaling), time = max over ranks.
-* ``e2e``: the same metric through the host C entry (b200dp_compute_host) with
-  pinned host buffers: H2D of coordinates and types, D2H of forces, energy
-  and virial inside the timed region.
+  every timed step, outside the events.  Multi-GPU (weak scaling): one
+  process per GPU, one global water box of 4096 H2O per GPU split by spatial
+  domain decomposition (slab for 2 GPUs, 2x2x1 for 4, 2x2x2 for 8; 8 A ghost
+  shell); a step is the forward halo of coordinates over NCCL, the force call
+  on owned + ghost atoms, the reverse fold of ghost forces and an all-reduce
+  of energy and virial; time = max over ranks.
+* ``e2e``: the same metric through the public API with pinned host buffers:
+  1 GPU, the host C entry (b200dp_compute_host), H2D of coordinates and
+  types, D2H of forces, energy and virial inside the timed region; N GPUs,
+  each rank copies its owned coordinates in and its forces, energy and
+  virial out around DistributedDeepPot.step.
 * ``roofline``: the dominant kernel (descriptor backward), algorithmic FLOPs
   per launch over its CUDA-event duration, against the measured bf16 peak.
 * ``cpu_baseline``: the CPU oracle (C++ fp64, OpenMP) on the host cores.
@@ -47,6 +53,7 @@ import systems  # noqa: E402
 METRIC = "atom-steps/s (E+F+virial)"
 WORKLOAD = "c1_water_12288"
 L2_FLUSH_BYTES = 256 << 20
+HALO = 8.0  # ghost shell: rcut 6 A + 2 A neighbour skin
 
 
 def parse():
@@ -195,6 +202,56 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+class Periodic:
+    """One GPU: the whole periodic box through b200dp_compute_device."""
+
+    def __init__(self, dp, system, dev, stream, torch):
+        self.dp, self.system, self.stream = dp, system, stream
+        self.n = self.total = system.natoms
+        self.x = torch.tensor(system.coord, device=dev)
+        self.t = torch.tensor(system.atype, device=dev)
+        self.e = torch.zeros(1, dtype=torch.float64, device=dev)
+        self.f = torch.zeros(self.n, 3, dtype=torch.float64, device=dev)
+        self.v = torch.zeros(9, dtype=torch.float64, device=dev)
+
+    def step(self):
+        self.dp.compute_device(self.stream.cuda_stream, self.n, 0, self.x.data_ptr(), self.t.data_ptr(),
+                               self.system.box, None, self.e.data_ptr(), self.f.data_ptr(), self.v.data_ptr())
+
+
+class Decomposed:
+    """N GPUs: spatial domain decomposition of one global box (domain.py)."""
+
+    def __init__(self, dp, system, grid, rank, dev, stream, torch):
+        import domain
+
+        self.dp, self.stream = dp, stream
+        dd = domain.Decomposition(system.box, grid, rank, HALO)
+        x, t, ids = domain.distribute(system.coord, system.atype, dd)
+
+        def compute(x_all, t_all, nloc, nghost, region, e, f, v):
+            dp.compute_device(stream.cuda_stream, nloc, nghost, x_all.data_ptr(), t_all.data_ptr(), None, region,
+                              e.data_ptr(), f.data_ptr(), v.data_ptr())
+
+        self.ddp = domain.DistributedDeepPot(compute, system.box, grid, rank, HALO, x, t, ids, device=dev)
+        self.n = self.ddp.nloc
+        self.total = system.natoms
+        self.nghost = self.ddp.nghost
+
+    def step(self):
+        self.ddp.step()
+
+
+def global_system(world, rank):
+    """Weak scaling: 4096 H2O per GPU, the global box grows with the rank grid."""
+    import domain
+
+    if world == 1:
+        return systems.config1(), (1, 1, 1)
+    grid = domain.rank_grid(world)
+    return systems.water(16 * grid[0], 16 * grid[1], 16 * grid[2], seed=0, name=WORKLOAD), grid
+
+
 def run_b200dp(args, world, rank, local):
     import torch
 
@@ -202,31 +259,29 @@ def run_b200dp(args, world, rank, local):
 
     torch.cuda.set_device(local)
     dist = None
+    dev = torch.device("cuda", local)
     if world > 1:
+        import datetime
+
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120))
-    system = systems.water(16, seed=rank, name=WORKLOAD) if rank else systems.config1()
-    n = system.natoms
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    system, grid = global_system(world, rank)
     mp = model_path("water")
     m = modelgen.load(mp)
     prec = b200dp.MIXED if args.precision == "mixed" else b200dp.FP64
-    dev = torch.device("cuda", local)
     stream = torch.cuda.current_stream(dev)
-    x = torch.tensor(system.coord, device=dev)
-    t = torch.tensor(system.atype, device=dev)
-    e = torch.zeros(1, dtype=torch.float64, device=dev)
-    f = torch.zeros(n, 3, dtype=torch.float64, device=dev)
-    v = torch.zeros(9, dtype=torch.float64, device=dev)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    sync = torch.zeros(1, device=dev)
 
-    def device_loop(dp, steps, warmup, stage_timing):
-        def step():
-            dp.compute_device(stream.cuda_stream, n, 0, x.data_ptr(), t.data_ptr(), system.box, None, e.data_ptr(),
-                              f.data_ptr(), v.data_ptr())
+    def workload(dp):
+        if world == 1:
+            return Periodic(dp, system, dev, stream, torch)
+        return Decomposed(dp, system, grid, rank, dev, stream, torch)
 
+    def device_loop(dp, w, steps, warmup, stage_timing):
         for _ in range(warmup):
-            step()
+            w.step()
         dp.check()
         dp.set_stage_timing(stage_timing)
         if dist:
@@ -238,8 +293,10 @@ def run_b200dp(args, world, rank, local):
         l0 = b200dp.kernel_launches()
         for k in range(steps):
             flush.fill_(k & 0xFF)
+            if dist:  # ranks enter the step together (device-side, no host sync)
+                dist.all_reduce(sync)
             starts[k].record(stream)
-            step()
+            w.step()
             ends[k].record(stream)
             if stage_timing:
                 stages.append(dp.stage_times())
@@ -251,17 +308,23 @@ def run_b200dp(args, world, rank, local):
         ms = sum(s.elapsed_time(en) for s, en in zip(starts, ends))
         return ms, launches, stages
 
+    def max_over_ranks(x):
+        if not dist:
+            return x
+        tt = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        return float(tt.item())
+
     dp = b200dp.DeepPot(mp, precision=prec, device=local)
+    w = workload(dp)
+    n = w.n
     clk_path = os.path.join(tempfile.gettempdir(), f"b200dp_clocks_{rank}.csv")
     cp, cf = start_clocks(local, clk_path)
-    ms, launches, stages = device_loop(dp, args.steps, args.warmup, True)
+    ms, launches, stages = device_loop(dp, w, args.steps, args.warmup, True)
     clocks = stop_clocks(cp, cf, clk_path)
-    if dist:
-        tt = torch.tensor([ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms = float(tt.item())
-    value = world * n * args.steps / (ms / 1e3)
-    # edges (real neighbours) of this workload for the FLOP count
+    ms = max_over_ranks(ms)
+    value = w.total * args.steps / (ms / 1e3)
+    # edges (real neighbours) of this rank's owned atoms for the FLOP count
     nl = dp.last_nlist(n)["nlist"]
     edges = int((nl >= 0).sum())
     fl = model_flops(m, n, edges)
@@ -271,41 +334,45 @@ def run_b200dp(args, world, rank, local):
     bwd_ms = float(stage_ms[3])
     achieved = fl["descriptor_bwd"] / (bwd_ms / 1e3) / 1e12 if bwd_ms > 0 else 0.0
     peak = float(pk["bf16_tflops"])
-    roofline = {"kernel": "k_descriptor_bwd", "bound": "tensor", "achieved": achieved, "peak": peak,
-                "unit": "TFLOP/s", "frac": achieved / peak, "traffic": ncu_traffic("descriptor_bwd"),
+    roofline = {"kernel": "k_embed_bwd_tc" if prec == b200dp.MIXED else "k_descriptor_bwd", "bound": "tensor",
+                "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                "traffic": ncu_traffic("descriptor_bwd"),
                 "peak_source": f"{pk_kind} bf16 burst (MEASURED_PEAKS.json)" if pk_kind == "measured"
                 else "fallback 1.59 PFLOP/s",
                 "flops_per_launch": fl["descriptor_bwd"], "avg_launch_ms": bwd_ms,
-                "note": "SIMT fp32 kernel measured against the tensor-core peak it is to be moved onto"}
-    # e2e through the host C entry with pinned buffers
+                "note": "algorithmic FLOPs of the embedding backward over the CUDA-event time of its stage"}
+    # e2e through the public API with pinned host buffers
     e2e = None
     try:
-        e2e = e2e_loop(dp, system, args.steps, max(1, min(args.warmup, 3)), torch)
+        e2e = e2e_loop(dp, w, system, args.steps, max(1, min(args.warmup, 3)), torch, dist)
     except Exception as ex:  # report, never hide
         e2e = {"error": repr(ex)}
-    if dist:
-        ev = torch.tensor([e2e.get("seconds", 0.0)], dtype=torch.float64, device=dev)
-        dist.all_reduce(ev, op=dist.ReduceOp.MAX)
-        if "seconds" in e2e:
-            e2e["value"] = world * n * args.steps / float(ev.item())
+    if "seconds" in e2e:
+        secs = max_over_ranks(e2e["seconds"])
+        e2e["value"] = w.total * args.steps / secs
+        e2e["seconds"] = secs
     # fp64 mode (secondary line item)
     fp64 = None
     if prec == b200dp.MIXED:
         dp64 = b200dp.DeepPot(mp, precision=b200dp.FP64, device=local)
+        w64 = workload(dp64)
         k64 = max(2, min(args.steps, 5))
-        ms64, _, st64 = device_loop(dp64, k64, max(1, min(args.warmup, 2)), True)
-        if dist:
-            tt = torch.tensor([ms64], dtype=torch.float64, device=dev)
-            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-            ms64 = float(tt.item())
-        fp64 = {"value": world * n * k64 / (ms64 / 1e3), "ms_per_step": ms64 / k64,
+        ms64, _, st64 = device_loop(dp64, w64, k64, max(1, min(args.warmup, 2)), True)
+        ms64 = max_over_ranks(ms64)
+        fp64 = {"value": w.total * k64 / (ms64 / 1e3), "ms_per_step": ms64 / k64,
                 "stage_ms": [round(float(q), 4) for q in np.array(st64).mean(0)]}
+        del w64
         dp64.close()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, used, dt = cpu_oracle_rate(mp, system)
         cpu = {"value": rate, "unit": "atom-steps/s", "cores": used, "kind": "port",
                "sample": f"one full evaluation of the 12,288-atom system ({dt:.2f} s), fp64 C++ oracle, OpenMP"}
+    if world > 1:
+        parallelism = f"domain decomposition {grid[0]}x{grid[1]}x{grid[2]}, halo {HALO} A, NCCL send/recv"
+        cfg_extra = {"global_atoms": w.total, "ghosts_rank0": w.nghost}
+    else:
+        parallelism, cfg_extra = "single", {}
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "atom-steps/s", "n_gpus": world, "steps": args.steps,
@@ -313,7 +380,7 @@ def run_b200dp(args, world, rank, local):
             "vs_baseline": None, "dtype": "f32-mixed" if prec == b200dp.MIXED else "f64",
             "data": "synthetic (seeded water, random-init weights)",
             "config": {"workload": WORKLOAD, "atoms": n, "edges": edges, "model": "water se_e2_a-type",
-                       "precision": args.precision, "parallelism": f"replicas x{world}" if world > 1 else "single",
+                       "precision": args.precision, "parallelism": parallelism, **cfg_extra,
                        "l2": "flushed before every timed step (256 MB write), flush outside the events"},
             "stage_ms": {k: round(float(q), 4) for k, q in
                          zip(["neighbour", "descriptor_fwd", "fitting", "descriptor_bwd", "assembly"], stage_ms)},
@@ -326,17 +393,21 @@ def run_b200dp(args, world, rank, local):
             "flops_per_step": fl["total"],
         }
         print(json.dumps(line), flush=True)
+    del w
     dp.close()
     if dist:
         dist.barrier()
         dist.destroy_process_group()
 
 
-def e2e_loop(dp, system, steps, warmup, torch):
+def e2e_loop(dp, w, system, steps, warmup, torch, dist):
+    """Host buffers in, host buffers out: coordinates H2D and forces, energy, virial D2H every step."""
     import ctypes
 
     import b200dp
 
+    if dist is not None:
+        return e2e_decomposed(w, steps, warmup, torch, dist)
     n = system.natoms
     coord = torch.tensor(system.coord).pin_memory()
     atype = torch.tensor(system.atype).pin_memory()
@@ -365,6 +436,35 @@ def e2e_loop(dp, system, steps, warmup, torch):
     return {"value": n * steps / dt, "unit": "atom-steps/s", "seconds": dt,
             "h2d_bytes_per_step": n * 3 * 8 + n * 4, "d2h_bytes_per_step": n * 3 * 8 + 8 * 10,
             "entry": "b200dp_compute_host (pinned host buffers, synchronous)"}
+
+
+def e2e_decomposed(w, steps, warmup, torch, dist):
+    """Per rank: owned coordinates from pinned host memory, owned forces and energy/virial back."""
+    ddp = w.ddp
+    n = ddp.nloc
+    x_host = ddp.x[:n].cpu().pin_memory()
+    f_host = torch.zeros(n, 3, dtype=torch.float64).pin_memory()
+    ev_host = torch.zeros(10, dtype=torch.float64).pin_memory()
+
+    def call():
+        ddp.x[:n].copy_(x_host, non_blocking=True)
+        e, f, v = ddp.step()
+        f_host.copy_(f, non_blocking=True)
+        ev_host.copy_(ddp.ev, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    for _ in range(warmup):
+        call()
+    dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        call()
+    dt = time.perf_counter() - t0
+    return {"value": None, "unit": "atom-steps/s", "seconds": dt,
+            "h2d_bytes_per_step": n * 3 * 8, "d2h_bytes_per_step": n * 3 * 8 + 8 * 10,
+            "entry": "domain.DistributedDeepPot.step over b200dp_compute_device (pinned host buffers, per rank)",
+            "bytes_rank": "rank 0's own counts"}
 
 
 def main():
