@@ -1,5 +1,6 @@
 // Tensor-core embedding forward and backward (see embed_tc.cuh).
 #include <algorithm>
+#include <cmath>
 #include <cstring>
 
 #include "common.cuh"
@@ -10,12 +11,9 @@ namespace b200dp {
 
 namespace {
 
-// tanh from the exponential: 1 - 2 / (exp(2x) + 1).  Absolute error ~1e-7,
-// saturates correctly at both ends (exp overflow -> 1, underflow -> -1).
-__device__ __forceinline__ float tanh_fast(float x) { return 1.0f - __fdividef(2.0f, __expf(2.0f * x) + 1.0f); }
 
 constexpr long long kWaitLimit = 1LL << 26;
-constexpr int kFwdGroups = 3;  // groups of 4 warps per CTA in the forward kernel
+constexpr int kFwdGroups = 2;  // groups of 8 warps per CTA in the forward kernel
 
 // Packed net blob (global memory and the front of shared memory):
 // [w2 hi|lo][w3 hi|lo][w1 b1 b2 b3 fp32].  W2 and W3 are stored as K-major B
@@ -48,18 +46,11 @@ __device__ __forceinline__ float resid_of(const float* x, int n) {
   return 0.0f;
 }
 
-// Writes 8 consecutive fp32 values as bf16 hi and lo 16-byte chunks (packed
-// round-to-nearest conversions, two values per instruction).
+// Writes 8 consecutive fp32 values as bf16 hi and lo 16-byte chunks.
 __device__ __forceinline__ void store8_split(unsigned char* hi, unsigned char* lo, const float* v) {
   uint32_t h[4], l[4];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const __nv_bfloat162 hh = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
-    const float2 hf = __bfloat1622float2(hh);
-    const __nv_bfloat162 ll = __floats2bfloat162_rn(v[2 * j] - hf.x, v[2 * j + 1] - hf.y);
-    h[j] = *reinterpret_cast<const uint32_t*>(&hh);
-    l[j] = *reinterpret_cast<const uint32_t*>(&ll);
-  }
+  for (int j = 0; j < 4; ++j) umma::split_pair(v[2 * j], v[2 * j + 1], h[j], l[j]);
   *reinterpret_cast<uint4*>(hi) = make_uint4(h[0], h[1], h[2], h[3]);
   *reinterpret_cast<uint4*>(lo) = make_uint4(l[0], l[1], l[2], l[3]);
 }
@@ -74,6 +65,18 @@ __device__ __forceinline__ void mma3(uint32_t d, uint32_t a_hi, uint32_t a_lo, u
               (accumulate || s > 0) ? 1u : 0u);
     umma::mma(d, umma::desc(a_hi + oa, lbo_a, sbo_a), umma::desc(b_lo + ob, lbo_b, sbo_b), idesc, 1u);
     umma::mma(d, umma::desc(a_lo + oa, lbo_a, sbo_a), umma::desc(b_hi + ob, lbo_b, sbo_b), idesc, 1u);
+  }
+}
+
+// Same with precomputed descriptors: K step s adds s * inc (bytes >> 4) to
+// the start-address field of the A and B descriptors.
+__device__ __forceinline__ void mma3d(uint32_t d, uint64_t a_hi, uint64_t a_lo, uint64_t b_hi, uint64_t b_lo,
+                                      uint32_t idesc, int steps, uint32_t inc_a, uint32_t inc_b, bool accumulate) {
+  for (int s = 0; s < steps; ++s) {
+    const uint64_t oa = (uint64_t)(s * inc_a), ob = (uint64_t)(s * inc_b);
+    umma::mma(d, a_hi + oa, b_hi + ob, idesc, (accumulate || s > 0) ? 1u : 0u);
+    umma::mma(d, a_hi + oa, b_lo + ob, idesc, 1u);
+    umma::mma(d, a_lo + oa, b_hi + ob, idesc, 1u);
   }
 }
 
@@ -100,61 +103,204 @@ __device__ __forceinline__ Item item_of(const TcLists& L, int it) {
 }
 
 // ---------------------------------------------------------------- forward
-// NG independent groups of 4 warps per CTA share the current net's weights;
-// each group runs its own work item with its own TMEM slice (D2 and D3 share
-// columns, T after them), mbarrier and named barrier, so tensor-core waits of
-// one group overlap the SIMT epilogues of the others.
-template <int D1, int D2, int D3, int NG>
-struct Fwd {
-  using F = TcShape<D1, D2, D3>;
-  static constexpr int NT = 4 * kItemRows;           // contraction columns
-  static constexpr uint32_t A1B = 128 * F::D1p * 2;  // one bf16 half
-  static constexpr uint32_t XB = 128 * 64 * 2;       // A2 (K <= 64) or G^T half (M = 128 a, K = 64 edges)
-  static constexpr uint32_t RB = NT * 64 * 2;        // R~ half (N = 32, K = 64 edges)
-  static constexpr uint32_t GS = 2 * A1B + 2 * XB + 2 * RB;  // per-group bytes
-  static constexpr uint32_t O_G0 = F::O_END;
-  static constexpr uint32_t SMEM = O_G0 + NG * GS;
-  static constexpr uint32_t LBO_G = (128 / 8) * 128, SBO_G = 128;  // MN-major
-  static constexpr uint32_t LBO_R = (NT / 8) * 128, SBO_R = 128;   // MN-major
-  static constexpr uint32_t COLS = 160;                            // per group: D2/D3 [0,128), T [128,160)
-  static constexpr uint32_t C_D = 0, C_T = 128, NCOLS = 512;
-  static_assert(NG * COLS <= NCOLS, "TMEM budget");
-  static_assert(F::D3p <= 128, "D3 must fit the shared accumulator columns");
+// Two threads per edge.  Every layer's output features are divided between
+// the two threads of an edge ("halves"), so that each thread owns the
+// residual sources of its own features: with DeePMD's concat rule
+// (d_out = 2 d_in, feature n uses input n mod d_in) the half that owns input
+// feature i also owns outputs i and i + d_in; with the identity rule it owns
+// output i.  The host permutes the weights into this order: positions
+// [0, H) of a layer are half 0's features, [H, 2H) half 1's, with zero
+// padding; H = 16, 32, 64 for layers 1, 2, 3.  The contraction operand G^T
+// (128 positions x 128 edges) is written by all 256 threads of a group at
+// once, and its rows stay in position order through the T accumulator; the
+// store of T maps positions back to feature indices.
+constexpr int res_kind(int dout, int din) { return dout == din ? 1 : (dout == 2 * din ? 2 : 0); }
+
+template <int D1, int D2, int D3>
+struct Split {
+  static constexpr int H1 = 16, H2 = 32, H3 = 64;  // slots per half
+  static constexpr int R2 = res_kind(D2, D1), R3 = res_kind(D3, D2);
+  static constexpr int c1(int h) { return h == 0 ? (D1 + 1) / 2 : D1 / 2; }
+  static constexpr int c2(int h) { return R2 == 1 ? c1(h) : R2 == 2 ? 2 * c1(h) : (h == 0 ? (D2 + 1) / 2 : D2 / 2); }
+  static constexpr int c3(int h) { return R3 == 1 ? c2(h) : R3 == 2 ? 2 * c2(h) : (h == 0 ? (D3 + 1) / 2 : D3 / 2); }
+  // input slot (same half) feeding the residual of output slot j, -1 for none
+  static constexpr int src2(int h, int j) { return R2 == 1 ? j : R2 == 2 ? (j < c1(h) ? j : j - c1(h)) : -1; }
+  static constexpr int src3(int h, int j) { return R3 == 1 ? j : R3 == 2 ? (j < c2(h) ? j : j - c2(h)) : -1; }
+  static_assert(c1(0) <= H1 && c2(0) <= H2 && c3(0) <= H3, "widths of the split forward kernel");
+  // A padding slot of half 0 carries a constant 1 whose weight row is the
+  // next layer's bias, so the MMA adds the bias (when such a slot exists).
+  static constexpr bool FOLD2 = c1(0) < H1, FOLD3 = c2(0) < H2;
 };
+
+// Pre-activations arrive scaled by c = 2 log2(e) (the host scales weights
+// and biases), so tanh(z) = 1 - 2 / (1 + 2^(c z)); `base` is 1 plus the
+// residual input, which turns the tanh and the residual add into one FMA.
+constexpr float kTanhScale = 2.8853900817779268f;
+__device__ __forceinline__ float tanh_scaled(float zc, float base) {
+  float e, r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(zc));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + e));
+  return fmaf(-2.0f, r, base);
+}
+
+// Host: original feature index of every position of the three layers (-1 = padding).
+template <int D1, int D2, int D3>
+void split_order(std::vector<int>& p1, std::vector<int>& p2, std::vector<int>& p3) {
+  using P = Split<D1, D2, D3>;
+  p1.assign(2 * P::H1, -1);
+  p2.assign(2 * P::H2, -1);
+  p3.assign(2 * P::H3, -1);
+  for (int h = 0; h < 2; ++h) {
+    for (int j = 0; j < P::c1(h); ++j) p1[h * P::H1 + j] = (h ? P::c1(0) : 0) + j;
+    for (int j = 0; j < P::c2(h); ++j) {
+      const int s = P::src2(h, j);
+      p2[h * P::H2 + j] = P::R2 == 0 ? (h ? P::c2(0) : 0) + j : p1[h * P::H1 + s] + (j >= P::c1(h) ? D1 : 0);
+    }
+    for (int j = 0; j < P::c3(h); ++j) {
+      const int s = P::src3(h, j);
+      p3[h * P::H3 + j] = P::R3 == 0 ? (h ? P::c3(0) : 0) + j : p2[h * P::H2 + s] + (j >= P::c2(h) ? D2 : 0);
+    }
+  }
+}
+
+// Forward blob (after the backward blob of the same net): W2 and W3 as
+// K-major B operands in position order, then fp32 w1, b1 (layer-1 positions),
+// b2, b3, and the feature index of each layer-3 position.
+struct FwdBlob {
+  static constexpr uint32_t W2B = 64 * 32 * 2, W3B = 128 * 64 * 2;
+  static constexpr uint32_t O_W2 = 0, O_W3 = 2 * W2B, O_F = O_W3 + 2 * W3B;
+  static constexpr uint32_t O_MAP = O_F + (32 + 32 + 64 + 128) * 4;
+  static constexpr uint32_t BLOB = O_MAP + 128 * 4;
+  static constexpr uint32_t O_END = (BLOB + 1023) / 1024 * 1024;
+  static constexpr uint32_t SBO_W2 = (32 / 8) * 128, SBO_W3 = (64 / 8) * 128;
+};
+
+template <int D1, int D2, int D3>
+struct NetBlob {
+  static constexpr uint32_t OFF_FWD = TcShape<D1, D2, D3>::O_END;
+  static constexpr uint32_t BYTES = OFF_FWD + FwdBlob::O_END;
+};
+
+// Shared memory of one group (256 threads): A1 (layer-2 A), X (layer-3 A),
+// then G^T (contraction A, MN-major, 128 positions x 128 edges) over both,
+// and R~ (contraction B, MN-major, 32 columns x 128 edges).
+struct FwdGroup {
+  static constexpr uint32_t A1B = 128 * 32 * 2, XB = 128 * 64 * 2, GB = 128 * 128 * 2, RB = 32 * 128 * 2;
+  static constexpr uint32_t O_A1 = 0, O_X = 2 * A1B, O_G = 0, O_R = 2 * GB;
+  static constexpr uint32_t BYTES = O_R + 2 * RB;
+  static constexpr uint32_t SBO_A1 = (32 / 8) * 128, SBO_X = (64 / 8) * 128;
+  static constexpr uint32_t SBO_G = 128, LBO_G = 16 * 128;  // MN-major, 16 position blocks per edge block
+  static constexpr uint32_t SBO_R = 128, LBO_R = 4 * 128;   // MN-major, 4 column blocks per edge block
+  static constexpr uint32_t C_D = 0, C_T = 128, COLS = 256;  // TMEM columns per group
+  static constexpr int NG = 2;
+  static constexpr uint32_t SMEM = FwdBlob::O_END + NG * BYTES;
+};
+static_assert(FwdGroup::O_X + 2 * FwdGroup::XB <= FwdGroup::O_R, "A1 and X lie inside the G^T region");
+static_assert(kFwdGroups == FwdGroup::NG, "item padding matches the groups per CTA");
 
 struct FwdArgs {
   TcLists L;
   const unsigned char* nets;
-  size_t net_bytes;
+  size_t net_bytes, fwd_off;
   float* Tq;
   int* err;
 };
 
-template <int D1, int D2, int D3, int NG>
-__global__ void __launch_bounds__(128 * NG, 1) k_embed_fwd_tc(FwdArgs a) {
-  using F = TcShape<D1, D2, D3>;
-  using S = Fwd<D1, D2, D3, NG>;
+// The per-half pieces of one subtile (H = the thread's half, compile time).
+// Rows of edges beyond the subtile compute finite values from a zero
+// environment row; their R~ rows are zero, so they add nothing to T.
+// h1 / h2 hold the activations to store, h1p / h2p hold 1 + activation for
+// the next layer's residual (or 1 where a feature has no residual).
+template <int D1, int D2, int D3, int H>
+__device__ __forceinline__ void fwd_layer1(const float* f, float s, float (&h1)[16], float (&h1p)[16]) {
+  using P = Split<D1, D2, D3>;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    if (j < P::c1(H)) {
+      const float y = tanh_scaled(fmaf(s, f[H * 16 + j], f[32 + H * 16 + j]), 1.0f);
+      h1[j] = y;
+      h1p[j] = y + 1.0f;
+    } else {
+      h1[j] = (P::FOLD2 && H == 0 && j == P::c1(0)) ? 1.0f : 0.0f;
+      h1p[j] = 1.0f;
+    }
+  }
+}
+
+template <int D1, int D2, int D3, int H>
+__device__ __forceinline__ void fwd_epi2(const float* f, uint32_t taddr, const float (&h1p)[16], float (&h2)[32],
+                                         float (&h2p)[32]) {
+  using P = Split<D1, D2, D3>;
+  float v[32];
+  umma::ld16(taddr + H * 32, v);
+  umma::ld16(taddr + H * 32 + 16, v + 16);
+  umma::wait_ld();
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if (j < P::c2(H)) {
+      const float z = P::FOLD2 ? v[j] : v[j] + f[64 + H * 32 + j];
+      const float y = tanh_scaled(z, P::R2 != 0 ? h1p[P::src2(H, j)] : 1.0f);
+      h2[j] = y;
+      h2p[j] = y + 1.0f;
+    } else {
+      h2[j] = (P::FOLD3 && H == 0 && j == P::c2(0)) ? 1.0f : 0.0f;
+      h2p[j] = 1.0f;
+    }
+  }
+}
+
+template <int D1, int D2, int D3, int H>
+__device__ __forceinline__ void fwd_epi3(const float* f, uint32_t taddr, const float (&h2p)[32], unsigned char* gh,
+                                         unsigned char* gl, int e) {
+  using P = Split<D1, D2, D3>;
+  using S = FwdGroup;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    float v[16];
+    umma::ld16(taddr + H * 64 + c * 16, v);
+    umma::wait_ld();
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int j = c * 16 + i;
+      if (j < P::c3(H)) {
+        const float z = P::FOLD3 ? v[i] : v[i] + f[128 + H * 64 + j];
+        v[i] = tanh_scaled(z, P::R3 != 0 ? h2p[P::src3(H, j)] : 1.0f);
+      } else {
+        v[i] = 0.f;
+      }
+    }
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int mb = H * 8 + 2 * c + hh;
+      const uint32_t o = mb * S::SBO_G + (e >> 3) * S::LBO_G + (e & 7) * 16;
+      store8_split(gh + o, gl + o, v + 8 * hh);
+    }
+  }
+}
+
+template <int D1, int D2, int D3>
+__global__ void __launch_bounds__(256 * FwdGroup::NG, 1) k_embed_fwd_tc(FwdArgs a) {
+  using S = FwdGroup;
+  using B = FwdBlob;
   extern __shared__ __align__(1024) unsigned char smem[];
-  __shared__ uint64_t bars[NG];
+  __shared__ uint64_t bars[S::NG];
   __shared__ uint32_t tbase;
-  const int gtid = threadIdx.x, g = gtid >> 7, tid = gtid & 127, warp = tid >> 5;
+  const int gtid = threadIdx.x, g = gtid >> 8, t = gtid & 255, hf = t >> 7, e = t & 127;
   const int bid = 1 + g;  // named barrier of this group
-  const float* w1 = reinterpret_cast<const float*>(smem + F::O_F);
-  const float* b1 = w1 + D1;
-  const float* b2 = b1 + D1;
-  const float* b3 = b2 + D2;
-  const uint32_t w2h = umma::smem_u32(smem + F::O_W2), w2l = w2h + F::W2B;
-  const uint32_t w3h = umma::smem_u32(smem + F::O_W3), w3l = w3h + F::W3B;
-  unsigned char* gbase = smem + S::O_G0 + g * S::GS;
-  unsigned char* a1h = gbase;
+  const float* f = reinterpret_cast<const float*>(smem + B::O_F);
+  const int* pmap = reinterpret_cast<const int*>(smem + B::O_MAP);
+  unsigned char* gbase = smem + B::O_END + g * S::BYTES;
+  unsigned char* a1h = gbase + S::O_A1;
   unsigned char* a1l = a1h + S::A1B;
-  unsigned char* xh = a1l + S::A1B;
+  unsigned char* xh = gbase + S::O_X;
   unsigned char* xl = xh + S::XB;
-  unsigned char* rh = xl + S::XB;
+  unsigned char* gh = gbase + S::O_G;
+  unsigned char* gl = gh + S::GB;
+  unsigned char* rh = gbase + S::O_R;
   unsigned char* rl = rh + S::RB;
   uint64_t* bar = &bars[g];
-  if ((gtid >> 5) == 0) umma::tmem_alloc(&tbase, S::NCOLS);
-  if (tid == 0) {
+  if ((gtid >> 5) == 0) umma::tmem_alloc(&tbase, 512);
+  if (t == 0) {
     umma::mbar_init(bar, 1);
     umma::fence_mbar_init();
   }
@@ -162,173 +308,162 @@ __global__ void __launch_bounds__(128 * NG, 1) k_embed_fwd_tc(FwdArgs a) {
   __syncthreads();
   umma::fence_after_sync();
   const uint32_t tm = tbase + g * S::COLS;
-  const uint32_t lb = (uint32_t)(warp * 32) << 16;
+  const uint32_t lane_base = (uint32_t)((e >> 5) * 32) << 16;
   uint32_t phase = 0;
   int loaded = -1;
   const TcLists& L = a.L;
   const int nitems = L.istart[L.nnets];
-  const uint32_t id2 = umma::idesc_bf16(128, F::D2p, false, false);
-  const uint32_t id3 = umma::idesc_bf16(128, F::D3p, false, false);
-  const uint32_t idT = umma::idesc_bf16(128, S::NT, true, true);
+  // descriptors of the fixed operands (later K steps add (bytes >> 4))
+  const uint64_t dw2h = umma::desc(umma::smem_u32(smem + B::O_W2), 128, B::SBO_W2);
+  const uint64_t dw2l = umma::desc(umma::smem_u32(smem + B::O_W2 + B::W2B), 128, B::SBO_W2);
+  const uint64_t dw3h = umma::desc(umma::smem_u32(smem + B::O_W3), 128, B::SBO_W3);
+  const uint64_t dw3l = umma::desc(umma::smem_u32(smem + B::O_W3 + B::W3B), 128, B::SBO_W3);
+  const uint64_t da1h = umma::desc(umma::smem_u32(a1h), 128, S::SBO_A1);
+  const uint64_t da1l = umma::desc(umma::smem_u32(a1l), 128, S::SBO_A1);
+  const uint64_t dxh = umma::desc(umma::smem_u32(xh), 128, S::SBO_X);
+  const uint64_t dxl = umma::desc(umma::smem_u32(xl), 128, S::SBO_X);
+  const uint64_t dgh = umma::desc(umma::smem_u32(gh), S::LBO_G, S::SBO_G);
+  const uint64_t dgl = umma::desc(umma::smem_u32(gl), S::LBO_G, S::SBO_G);
+  const uint64_t drh = umma::desc(umma::smem_u32(rh), S::LBO_R, S::SBO_R);
+  const uint64_t drl = umma::desc(umma::smem_u32(rl), S::LBO_R, S::SBO_R);
+  const uint32_t id2 = umma::idesc_bf16(128, 64, false, false);
+  const uint32_t id3 = umma::idesc_bf16(128, 128, false, false);
+  const uint32_t idT = umma::idesc_bf16(128, 32, true, true);
   bool aborted = false;
   auto sync_mma = [&]() {
     umma::fence_proxy_async();
     umma::fence_before_sync();
-    umma::bar_sync(bid, 128);
+    umma::bar_sync(bid, 256);
     umma::fence_after_sync();
   };
   auto wait_mma = [&]() -> bool {
     const bool ok = umma::mbar_wait(bar, phase, kWaitLimit);
     phase ^= 1;
-    if (umma::bar_sync_or(bid, 128, !ok)) return false;
+    if (umma::bar_sync_or(bid, 256, !ok)) return false;
     umma::fence_after_sync();
     return true;
   };
-  // rounds of NG consecutive items, all of one net (item counts are padded)
-  for (int base = blockIdx.x * NG; base < nitems; base += gridDim.x * NG) {
+  for (int base = blockIdx.x * S::NG; base < nitems; base += gridDim.x * S::NG) {
     const int qr = item_of(L, base).q;
     if (qr != loaded) {
       __syncthreads();
-      const uint4* src = reinterpret_cast<const uint4*>(a.nets + (size_t)qr * a.net_bytes);
+      const uint4* src = reinterpret_cast<const uint4*>(a.nets + (size_t)qr * a.net_bytes + a.fwd_off);
       uint4* dst = reinterpret_cast<uint4*>(smem);
-      for (uint32_t i = gtid; i < F::BLOB / 16; i += 128 * NG) dst[i] = src[i];
+      for (uint32_t i = gtid; i < B::BLOB / 16; i += 256 * S::NG) dst[i] = src[i];
       loaded = qr;
       __syncthreads();
     }
     if (aborted) continue;  // keep taking part in the CTA-wide barriers above
     const Item I = item_of(L, base + g);
-    bool first = true;
-    for (int sub = I.e0; sub < I.e1 && !aborted; sub += 128) {
+    bool first = true, pending = false;
+    for (int sub = I.e0; sub < I.e1; sub += 128) {
       const int ne = min(128, I.e1 - sub);
-      const bool valid = tid < ne;
-      const float4 rt = valid ? L.rt[sub + tid] : make_float4(0.f, 0.f, 0.f, 0.f);
-      const int rl_ = valid ? L.row[sub + tid] - I.rb : -1;
-      float h1[D1];
-#pragma unroll
-      for (int n = 0; n < D1; ++n) h1[n] = valid ? tanh_fast(rt.x * w1[n] + b1[n]) : 0.f;
-#pragma unroll
-      for (int kg = 0; kg < F::D1p / 8; ++kg) {
-        float v[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = (kg * 8 + j < D1) ? h1[kg * 8 + j] : 0.f;
-        const uint32_t o = (tid >> 3) * F::SBO_A1 + kg * 128 + (tid & 7) * 16;
-        store8_split(a1h + o, a1l + o, v);
-      }
-      sync_mma();
-      if (tid == 0) {
-        mma3(tm + S::C_D, umma::smem_u32(a1h), umma::smem_u32(a1l), w2h, w2l, 128, F::SBO_A1, 128, F::SBO_W2, id2,
-             F::D1p / 16, 256, 256, false);
-        umma::commit(bar);
-      }
-      if (!wait_mma()) {
-        aborted = true;
-        break;
-      }
-      float h2[D2];
-#pragma unroll
-      for (int c = 0; c < F::D2p / 16; ++c) {
-        float v[16];
-        umma::ld16(tm + lb + S::C_D + c * 16, v);
-        umma::wait_ld();
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int n = c * 16 + j;
-          if (n < D2) h2[n] = valid ? tanh_fast(v[j] + b2[n]) + resid_of<D2, D1>(h1, n) : 0.f;
-        }
-      }
-#pragma unroll
-      for (int kg = 0; kg < F::D2p / 8; ++kg) {
-        float v[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = (kg * 8 + j < D2) ? h2[kg * 8 + j] : 0.f;
-        const uint32_t o = (tid >> 3) * F::SBO_A2 + kg * 128 + (tid & 7) * 16;
-        store8_split(xh + o, xl + o, v);
-      }
-      sync_mma();  // also orders every D2 read before MMA3 overwrites the columns
-      if (tid == 0) {
-        mma3(tm + S::C_D, umma::smem_u32(xh), umma::smem_u32(xl), w3h, w3l, 128, F::SBO_A2, 128, F::SBO_W3, id3,
-             F::D2p / 16, 256, 256, false);
-        umma::commit(bar);
-      }
-      if (!wait_mma()) {
-        aborted = true;
-        break;
-      }
-      // contraction in two halves of 64 edges: G^T and R~ of half h, then one MMA
-      const int nh = ne > 64 ? 2 : 1;
-      for (int h = 0; h < nh; ++h) {
-        if ((tid >> 6) == h) {
-          const int ep = tid & 63;
-#pragma unroll
-          for (int c = 0; c < F::D3p / 16; ++c) {
-            float v[16];
-            umma::ld16(tm + lb + S::C_D + c * 16, v);
-            umma::wait_ld();
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int n = c * 16 + j;
-              v[j] = (n < D3 && valid) ? tanh_fast(v[j] + b3[n]) + resid_of<D3, D2>(h2, n) : 0.f;
-            }
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-              const uint32_t o = (2 * c + hh) * S::SBO_G + (ep >> 3) * S::LBO_G + (ep & 7) * 16;
-              store8_split(xh + o, xl + o, v + 8 * hh);
-            }
-          }
-          const float rv[4] = {rt.x, rt.y, rt.z, rt.w};
-#pragma unroll
-          for (int ng = 0; ng < S::NT / 8; ++ng) {
-            float v[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const int n = ng * 8 + j;
-              v[j] = (rl_ == (n >> 2)) ? rv[n & 3] : 0.f;
-            }
-            const uint32_t o = ng * S::SBO_R + (ep >> 3) * S::LBO_R + (ep & 7) * 16;
-            store8_split(rh + o, rl + o, v);
-          }
-        }
-        sync_mma();
-        if (tid == 0) {
-          mma3(tm + S::C_T, umma::smem_u32(xh), umma::smem_u32(xl), umma::smem_u32(rh), umma::smem_u32(rl), S::LBO_G,
-               S::SBO_G, S::LBO_R, S::SBO_R, idT, 64 / 16, 2 * S::LBO_G, 2 * S::LBO_R, !first);
-          umma::commit(bar);
-        }
-        first = false;
+      const bool valid = e < ne;
+      const float4 rt = valid ? L.rt[sub + e] : make_float4(0.f, 0.f, 0.f, 0.f);
+      const int rloc = valid ? L.row[sub + e] - I.rb : -1;
+      float h1[16], h1p[16], h2[32], h2p[32];
+      if (hf == 0)
+        fwd_layer1<D1, D2, D3, 0>(f, rt.x, h1, h1p);
+      else
+        fwd_layer1<D1, D2, D3, 1>(f, rt.x, h1, h1p);
+      if (pending) {  // the previous contraction still reads G^T (over A1) and R~
         if (!wait_mma()) {
           aborted = true;
           break;
         }
+        pending = false;
       }
-    }
-    if (aborted) continue;
-    if (I.e1 > I.e0) {
-      float v[32];
-      umma::ld16(tm + lb + S::C_T, v);
-      umma::ld16(tm + lb + S::C_T + 16, v + 16);
-      umma::wait_ld();
-      if (tid < D3) {
-        for (int r = 0; r < I.re - I.rb; ++r) {
-          float* dst = a.Tq + (((size_t)I.q * L.nloc + I.rb + r) * 4) * D3;
 #pragma unroll
-          for (int k = 0; k < 4; ++k) dst[k * D3 + tid] = v[4 * r + k];
+      for (int kk = 0; kk < 2; ++kk) {
+        const uint32_t o = (e >> 3) * S::SBO_A1 + (2 * hf + kk) * 128 + (e & 7) * 16;
+        store8_split(a1h + o, a1l + o, h1 + 8 * kk);
+      }
+      {  // environment row in the column block of its centre; this half writes centres 4 hf .. 4 hf + 3
+        const float rv[4] = {rt.x, rt.y, rt.z, rt.w};
+#pragma unroll
+        for (int nn = 0; nn < 2; ++nn) {
+          float v[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int n = 16 * hf + 8 * nn + j;
+            v[j] = (rloc == (n >> 2)) ? rv[j & 3] : 0.f;
+          }
+          const int nb = 2 * hf + nn;
+          const uint32_t o = nb * S::SBO_R + (e >> 3) * S::LBO_R + (e & 7) * 16;
+          store8_split(rh + o, rl + o, v);
         }
       }
-    } else if (tid < D3) {
-      for (int r = 0; r < I.re - I.rb; ++r) {
-        float* dst = a.Tq + (((size_t)I.q * L.nloc + I.rb + r) * 4) * D3;
+      sync_mma();
+      if (t == 0) {
+        mma3d(tm + S::C_D, da1h, da1l, dw2h, dw2l, id2, 2, 256 >> 4, 256 >> 4, false);
+        umma::commit(bar);
+      }
+      if (!wait_mma()) {
+        aborted = true;
+        break;
+      }
+      if (hf == 0)
+        fwd_epi2<D1, D2, D3, 0>(f, tm + lane_base + S::C_D, h1p, h2, h2p);
+      else
+        fwd_epi2<D1, D2, D3, 1>(f, tm + lane_base + S::C_D, h1p, h2, h2p);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) dst[k * D3 + tid] = 0.f;
+      for (int kk = 0; kk < 4; ++kk) {
+        const uint32_t o = (e >> 3) * S::SBO_X + (4 * hf + kk) * 128 + (e & 7) * 16;
+        store8_split(xh + o, xl + o, h2 + 8 * kk);
+      }
+      sync_mma();  // also orders every D2 read before MMA3 overwrites the columns
+      if (t == 0) {
+        mma3d(tm + S::C_D, dxh, dxl, dw3h, dw3l, id3, 4, 256 >> 4, 256 >> 4, false);
+        umma::commit(bar);
+      }
+      if (!wait_mma()) {
+        aborted = true;
+        break;
+      }
+      if (hf == 0)
+        fwd_epi3<D1, D2, D3, 0>(f, tm + lane_base + S::C_D, h2p, gh, gl, e);
+      else
+        fwd_epi3<D1, D2, D3, 1>(f, tm + lane_base + S::C_D, h2p, gh, gl, e);
+      sync_mma();
+      if (t == 0) {
+        mma3d(tm + S::C_T, dgh, dgl, drh, drl, idT, (ne + 15) / 16, (2 * S::LBO_G) >> 4, (2 * S::LBO_R) >> 4, !first);
+        umma::commit(bar);
+      }
+      first = false;
+      pending = true;
+    }
+    if (aborted) continue;
+    if (pending && !wait_mma()) {
+      aborted = true;
+      continue;
+    }
+    // T[position][4 r + k] -> Tq[net][row][k][feature]; half hf stores centres 4 hf .. 4 hf + 3
+    const int a_idx = pmap[e];
+    float v[16];
+    if (I.e1 > I.e0) {
+      umma::ld16(tm + lane_base + S::C_T + 16 * hf, v);
+      umma::wait_ld();
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] = 0.f;
+    }
+    if (a_idx >= 0) {
+      for (int rr = 0; rr < 4; ++rr) {
+        const int r = 4 * hf + rr;
+        if (r >= I.re - I.rb) break;
+        float* dst = a.Tq + (((size_t)I.q * L.nloc + I.rb + r) * 4) * D3 + a_idx;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) dst[k * D3] = v[4 * rr + k];
       }
     }
     umma::fence_before_sync();
-    umma::bar_sync(bid, 128);
+    umma::bar_sync(bid, 256);
     umma::fence_after_sync();
   }
-  if (aborted && tid == 0) atomicAdd(a.err + kErrTcTimeout, 1);
+  if (aborted && t == 0) atomicAdd(a.err + kErrTcTimeout, 1);
   umma::fence_before_sync();
   __syncthreads();
-  if ((gtid >> 5) == 0) umma::tmem_dealloc(tbase, S::NCOLS);
+  if ((gtid >> 5) == 0) umma::tmem_dealloc(tbase, 512);
 }
 
 // ---------------------------------------------------------------- backward
@@ -466,7 +601,7 @@ __global__ void __launch_bounds__(128, 1) k_embed_bwd_tc(BwdArgs a) {
       }
       float h1[D1];
 #pragma unroll
-      for (int n = 0; n < D1; ++n) h1[n] = valid ? tanh_fast(rt.x * w1[n] + b1[n]) : 0.f;
+      for (int n = 0; n < D1; ++n) h1[n] = valid ? umma::tanh_fast(rt.x * w1[n] + b1[n]) : 0.f;
 #pragma unroll
       for (int kg = 0; kg < F::D1p / 8; ++kg) {
         float v[8];
@@ -497,7 +632,7 @@ __global__ void __launch_bounds__(128, 1) k_embed_bwd_tc(BwdArgs a) {
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int n = c * 16 + j;
-          if (n < D2) h2[n] = valid ? tanh_fast(v[j] + b2[n]) + resid_of<D2, D1>(h1, n) : 0.f;
+          if (n < D2) h2[n] = valid ? umma::tanh_fast(v[j] + b2[n]) + resid_of<D2, D1>(h1, n) : 0.f;
         }
       }
 #pragma unroll
@@ -535,7 +670,7 @@ __global__ void __launch_bounds__(128, 1) k_embed_bwd_tc(BwdArgs a) {
         for (int j = 0; j < 16; ++j) {
           const int n = c * 16 + j;
           if (n < D3 && valid) {
-            const float t3 = tanh_fast(z[j] + b3[n]);
+            const float t3 = umma::tanh_fast(z[j] + b3[n]);
             gv[j] = t3 + resid_of<D3, D2>(h2, n);
             zv[j] = dg[j] * (1.f - t3 * t3);
             if constexpr (D3 == D2) racc[n] += dg[j];
@@ -826,7 +961,7 @@ __global__ void k_item_table(int nnets, int ntypes, int tos, const int* __restri
 template <int D1, int D2, int D3>
 void pack_net(const std::vector<HostLayer>& net, std::vector<unsigned char>& out) {
   using S = TcShape<D1, D2, D3>;
-  out.assign(S::BLOB, 0);
+  out.assign(NetBlob<D1, D2, D3>::BYTES, 0);
   auto to_bf16 = [](float f) {
     uint32_t u;
     std::memcpy(&u, &f, 4);
@@ -862,6 +997,44 @@ void pack_net(const std::vector<HostLayer>& net, std::vector<unsigned char>& out
   for (int n = 0; n < D1; ++n) f[D1 + n] = (float)L1.b[n];
   for (int n = 0; n < D2; ++n) f[2 * D1 + n] = (float)L2.b[n];
   for (int n = 0; n < D3; ++n) f[2 * D1 + D2 + n] = (float)L3.b[n];
+  // forward blob: the same weights in the split kernel's position order
+  using FB = FwdBlob;
+  const uint32_t fo = NetBlob<D1, D2, D3>::OFF_FWD;
+  std::vector<int> p1, p2, p3;
+  split_order<D1, D2, D3>(p1, p2, p3);
+  auto putf = [&](uint32_t base, uint32_t half, int rows, int K, auto val) {
+    for (int r = 0; r < rows; ++r)
+      for (int k = 0; k < K; ++k) {
+        const float x = val(r, k);
+        const uint16_t hi = to_bf16(x);
+        const uint16_t lo = to_bf16(x - from_bf16(hi));
+        const uint32_t o = (uint32_t)(r >> 3) * ((K / 8) * 128) + (uint32_t)(k >> 3) * 128 + (r & 7) * 16 + (k & 7) * 2;
+        std::memcpy(&out[fo + base + o], &hi, 2);
+        std::memcpy(&out[fo + base + half + o], &lo, 2);
+      }
+  };
+  // weights and biases scaled by 2 log2(e) (the kernel's tanh takes scaled
+  // pre-activations); folded biases sit in the weight row of the constant slot
+  using P = Split<D1, D2, D3>;
+  const double c = 2.0 / std::log(2.0);
+  const int one1 = P::FOLD2 ? P::c1(0) : -1, one2 = P::FOLD3 ? P::c2(0) : -1;
+  putf(FB::O_W2, FB::W2B, 64, 32, [&](int n, int k) {
+    if (p2[n] < 0) return 0.f;
+    if (k == one1) return (float)(c * L2.b[p2[n]]);
+    return p1[k] >= 0 ? (float)(c * L2.w[(size_t)p1[k] * D2 + p2[n]]) : 0.f;
+  });
+  putf(FB::O_W3, FB::W3B, 128, 64, [&](int n, int k) {
+    if (p3[n] < 0) return 0.f;
+    if (k == one2) return (float)(c * L3.b[p3[n]]);
+    return p2[k] >= 0 ? (float)(c * L3.w[(size_t)p2[k] * D3 + p3[n]]) : 0.f;
+  });
+  float* ff = reinterpret_cast<float*>(&out[fo + FB::O_F]);
+  for (int j = 0; j < 32; ++j) ff[j] = p1[j] >= 0 ? (float)(c * L1.w[p1[j]]) : 0.f;
+  for (int j = 0; j < 32; ++j) ff[32 + j] = p1[j] >= 0 ? (float)(c * L1.b[p1[j]]) : 0.f;
+  for (int j = 0; j < 64; ++j) ff[64 + j] = p2[j] >= 0 ? (float)(c * L2.b[p2[j]]) : 0.f;
+  for (int j = 0; j < 128; ++j) ff[128 + j] = p3[j] >= 0 ? (float)(c * L3.b[p3[j]]) : 0.f;
+  int* map = reinterpret_cast<int*>(&out[fo + FB::O_MAP]);
+  for (int j = 0; j < 128; ++j) map[j] = p3[j];
 }
 
 enum class Inst { None, W25, W32 };
@@ -874,16 +1047,15 @@ Inst which(const SeaDev& s) {
 
 template <int D1, int D2, int D3>
 void launch_fwd(cudaStream_t st, const TcLists& L, int grid, const unsigned char* nets, float* Tq, int* err) {
-  using S = Fwd<D1, D2, D3, kFwdGroups>;
+  using S = FwdGroup;
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(k_embed_fwd_tc<D1, D2, D3, kFwdGroups>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)S::SMEM);
+    cudaFuncSetAttribute(k_embed_fwd_tc<D1, D2, D3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::SMEM);
     attr = true;
   }
-  FwdArgs a{L, nets, TcShape<D1, D2, D3>::BLOB, Tq, err};
+  FwdArgs a{L, nets, NetBlob<D1, D2, D3>::BYTES, NetBlob<D1, D2, D3>::OFF_FWD, Tq, err};
   count_launch();
-  k_embed_fwd_tc<D1, D2, D3, kFwdGroups><<<grid, 128 * kFwdGroups, S::SMEM, st>>>(a);
+  k_embed_fwd_tc<D1, D2, D3><<<grid, 256 * S::NG, S::SMEM, st>>>(a);
 }
 
 template <int D1, int D2, int D3>
@@ -895,7 +1067,7 @@ void launch_bwd(cudaStream_t st, const TcLists& L, int grid, const unsigned char
     cudaFuncSetAttribute(k_embed_bwd_tc<D1, D2, D3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Bw::SMEM);
     attr = true;
   }
-  BwdArgs a{L, nets, TcShape<D1, D2, D3>::BLOB, dT, rij, gslot, err, rcut, rs};
+  BwdArgs a{L, nets, NetBlob<D1, D2, D3>::BYTES, dT, rij, gslot, err, rcut, rs};
   count_launch();
   k_embed_bwd_tc<D1, D2, D3><<<grid, 128, Bw::SMEM, st>>>(a);
 }
@@ -907,9 +1079,9 @@ bool tc_supported(const SeaDev& s) { return which(s) != Inst::None; }
 size_t tc_net_bytes(const SeaDev& s) {
   switch (which(s)) {
     case Inst::W25:
-      return TcShape<25, 50, 100>::BLOB;
+      return NetBlob<25, 50, 100>::BYTES;
     case Inst::W32:
-      return TcShape<32, 64, 128>::BLOB;
+      return NetBlob<32, 64, 128>::BYTES;
     default:
       return 0;
   }
@@ -950,7 +1122,7 @@ int embed_tc_grid(const SeaDev&, bool backward) {
   int dev = 0, nsm = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-  // one CTA per SM: the forward runs kFwdGroups groups in it, the backward one
+  // one CTA per SM: the forward runs kFwdGroups groups of 8 warps in it, the backward one group of 4
   return nsm;
 }
 

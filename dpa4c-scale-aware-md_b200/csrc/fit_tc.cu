@@ -16,20 +16,13 @@ constexpr uint32_t kABlock = 128 * kFitBK * 2;  // one half of a 128 x 32 activa
 constexpr uint32_t kSbo = (kFitBK / 8) * 128;    // K-major SBO inside a block (512 B)
 constexpr long long kWaitLimit = 1LL << 26;
 
-__device__ __forceinline__ float tanh_fast(float x) { return 1.0f - __fdividef(2.0f, __expf(2.0f * x) + 1.0f); }
 
 using umma::tiled_off;
 
 __device__ __forceinline__ void store8_split(unsigned char* hi, unsigned char* lo, const float* v) {
   uint32_t h[4], l[4];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    __nv_bfloat16 h0, l0, h1, l1;
-    umma::split_bf16(v[2 * j], h0, l0);
-    umma::split_bf16(v[2 * j + 1], h1, l1);
-    h[j] = umma::pack2(h0, h1);
-    l[j] = umma::pack2(l0, l1);
-  }
+  for (int j = 0; j < 4; ++j) umma::split_pair(v[2 * j], v[2 * j + 1], h[j], l[j]);
   *reinterpret_cast<uint4*>(hi) = make_uint4(h[0], h[1], h[2], h[3]);
   *reinterpret_cast<uint4*>(lo) = make_uint4(l[0], l[1], l[2], l[3]);
 }
@@ -167,7 +160,7 @@ __global__ void __launch_bounds__(128, 1) k_fit_gemm(GemmArgs a) {
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int col = col0 + j;
-          const float th = tanh_fast(v[j] + a.bias[t][col]);
+          const float th = umma::tanh_fast(v[j] + a.bias[t][col]);
           float yy = th;
           if (a.Yprev) yy += a.Yprev[(size_t)prow * a.ldprev + col];
           a.TH[(size_t)prow * a.N + col] = th;
