@@ -15,37 +15,6 @@ namespace {
 constexpr long long kWaitLimit = 1LL << 26;
 constexpr int kFwdGroups = 2;  // groups of 8 warps per CTA in the forward kernel
 
-// Packed net blob (global memory and the front of shared memory):
-// [w2 hi|lo][w3 hi|lo][w1 b1 b2 b3 fp32].  W2 and W3 are stored as K-major B
-// operands of the forward MMAs: element (n, k) = W[k][n].
-template <int D1, int D2, int D3>
-struct TcShape {
-  static constexpr int D1p = (D1 + 15) / 16 * 16;
-  static constexpr int D2p = (D2 + 15) / 16 * 16;
-  static constexpr int D3p = (D3 + 15) / 16 * 16;
-  static constexpr uint32_t W2B = D2p * D1p * 2;
-  static constexpr uint32_t W3B = D3p * D2p * 2;
-  static constexpr uint32_t NF = 2 * D1 + D2 + D3;
-  static constexpr uint32_t O_W2 = 0;
-  static constexpr uint32_t O_W3 = O_W2 + 2 * W2B;
-  static constexpr uint32_t O_F = O_W3 + 2 * W3B;
-  static constexpr uint32_t BLOB = O_F + NF * 4;
-  static constexpr uint32_t O_END = ((BLOB + 1023) / 1024) * 1024;
-  static constexpr uint32_t SBO_W2 = (D1p / 8) * 128;
-  static constexpr uint32_t SBO_W3 = (D2p / 8) * 128;
-  static constexpr uint32_t SBO_A1 = (D1p / 8) * 128;  // K-major activations, K = D1p
-  static constexpr uint32_t SBO_A2 = (D2p / 8) * 128;  // K-major activations, K = D2p
-  static_assert(D1 > 2, "layer-1 residual is not handled by the tensor-core path");
-  static_assert(D1p <= 32 && D2p <= 64 && D3p <= 128, "widths of the tensor-core instantiations");
-};
-
-template <int D2, int D1>
-__device__ __forceinline__ float resid_of(const float* x, int n) {
-  if constexpr (D2 == D1) return x[n];
-  if constexpr (D2 == 2 * D1) return x[n < D1 ? n : n - D1];
-  return 0.0f;
-}
-
 // Writes 8 consecutive fp32 values as bf16 hi and lo 16-byte chunks.
 __device__ __forceinline__ void store8_split(unsigned char* hi, unsigned char* lo, const float* v) {
   uint32_t h[4], l[4];
@@ -55,21 +24,9 @@ __device__ __forceinline__ void store8_split(unsigned char* hi, unsigned char* l
   *reinterpret_cast<uint4*>(lo) = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
-// The three split products of `steps` K=16 steps (hi*hi, hi*lo, lo*hi).
-__device__ __forceinline__ void mma3(uint32_t d, uint32_t a_hi, uint32_t a_lo, uint32_t b_hi, uint32_t b_lo,
-                                     uint32_t lbo_a, uint32_t sbo_a, uint32_t lbo_b, uint32_t sbo_b, uint32_t idesc,
-                                     int steps, uint32_t step_a, uint32_t step_b, bool accumulate) {
-  for (int s = 0; s < steps; ++s) {
-    const uint32_t oa = s * step_a, ob = s * step_b;
-    umma::mma(d, umma::desc(a_hi + oa, lbo_a, sbo_a), umma::desc(b_hi + ob, lbo_b, sbo_b), idesc,
-              (accumulate || s > 0) ? 1u : 0u);
-    umma::mma(d, umma::desc(a_hi + oa, lbo_a, sbo_a), umma::desc(b_lo + ob, lbo_b, sbo_b), idesc, 1u);
-    umma::mma(d, umma::desc(a_lo + oa, lbo_a, sbo_a), umma::desc(b_hi + ob, lbo_b, sbo_b), idesc, 1u);
-  }
-}
-
-// Same with precomputed descriptors: K step s adds s * inc (bytes >> 4) to
-// the start-address field of the A and B descriptors.
+// The three split products (hi*hi, hi*lo, lo*hi) of `steps` K = 16 steps from
+// precomputed descriptors: K step s adds s * inc (bytes >> 4) to the
+// start-address field of the A and B descriptors.
 __device__ __forceinline__ void mma3d(uint32_t d, uint64_t a_hi, uint64_t a_lo, uint64_t b_hi, uint64_t b_lo,
                                       uint32_t idesc, int steps, uint32_t inc_a, uint32_t inc_b, bool accumulate) {
   for (int s = 0; s < steps; ++s) {
@@ -163,9 +120,11 @@ void split_order(std::vector<int>& p1, std::vector<int>& p2, std::vector<int>& p
   }
 }
 
-// Forward blob (after the backward blob of the same net): W2 and W3 as
-// K-major B operands in position order, then fp32 w1, b1 (layer-1 positions),
-// b2, b3, and the feature index of each layer-3 position.
+// Packed net (global memory and the front of shared memory), shared by the
+// forward and backward kernels: W2 and W3 as K-major B operands in position
+// order (element (n, k) = W[k][n], bf16 hi then lo), then fp32 w1, b1
+// (layer-1 positions), b2, b3, and the feature index of each layer-3
+// position.  Weights and biases are scaled by c = 2 log2(e).
 struct FwdBlob {
   static constexpr uint32_t W2B = 64 * 32 * 2, W3B = 128 * 64 * 2;
   static constexpr uint32_t O_W2 = 0, O_W3 = 2 * W2B, O_F = O_W3 + 2 * W3B;
@@ -177,8 +136,9 @@ struct FwdBlob {
 
 template <int D1, int D2, int D3>
 struct NetBlob {
-  static constexpr uint32_t OFF_FWD = TcShape<D1, D2, D3>::O_END;
-  static constexpr uint32_t BYTES = OFF_FWD + FwdBlob::O_END;
+  static_assert(D1 > 2, "a layer-1 residual is not handled by the tensor-core path");
+  static constexpr uint32_t OFF_FWD = 0;
+  static constexpr uint32_t BYTES = FwdBlob::O_END;
 };
 
 // Shared memory of one group (256 threads): A1 (layer-2 A), X (layer-3 A),
@@ -467,31 +427,31 @@ __global__ void __launch_bounds__(256 * FwdGroup::NG, 1) k_embed_fwd_tc(FwdArgs 
 }
 
 // ---------------------------------------------------------------- backward
-// The forward blobs double as the backward B operands: read with MN-major
-// descriptors they are W3 and W2 themselves, so no transposed copy is kept.
-template <int D1, int D2, int D3>
-struct Bwd {
-  using F = TcShape<D1, D2, D3>;
-  static constexpr int NT = 4 * kItemRows;
-  static constexpr uint32_t A1B = 128 * F::D1p * 2;
-  static constexpr uint32_t XB = 128 * 64 * 2;     // A2 / G half / dz2, K-major K = 64
-  static constexpr uint32_t YB = 128 * 64 * 2;     // dz3 half, K-major K = 64
-  static constexpr uint32_t RB = 128 * NT * 2;     // R~ rows, K-major [edge][n]
-  static constexpr uint32_t TB = NT * F::D3p * 2;  // dT of the item's rows, stored [n][a]
-  static constexpr uint32_t O_A1 = F::O_END;
-  static constexpr uint32_t O_X = O_A1 + 2 * A1B;
-  static constexpr uint32_t O_Y = O_X + 2 * XB;
-  static constexpr uint32_t O_R = O_Y + 2 * YB;
-  static constexpr uint32_t O_T = O_R + 2 * RB;
-  static constexpr uint32_t SMEM = O_T + 2 * TB;
-  static constexpr uint32_t SBO_H = (64 / 8) * 128, SBO_R = (NT / 8) * 128, SBO_T = (F::D3p / 8) * 128;
-  static constexpr uint32_t C_D2 = 0, C_D3 = 64, C_DG = 192, C_DR = 320, C_DH1 = 352, NCOLS = 512;
+// Same split as the forward: two threads per edge, each owning half of the
+// positions of every layer (and the residual sources of its own positions).
+// Per subtile the forward is recomputed with the same MMAs; then
+//   dG[e][p] = sum_k R~[e][k] dT[row][k][p]    (rank 4: CUDA cores)
+//   dR~[e][k] = sum_p G[e][p] dT[row][k][p]   (rank 4: CUDA cores)
+//   dh2 = dz3 W3^T, dh1 = dz2 W2^T             (tcgen05 MMAs)
+// dz3 is written back into the TMEM columns of the layer-3 pre-activations
+// (bf16 hi and lo halves per K step) and read from there as the A operand;
+// dz2 goes to the shared-memory slot of the layer-3 A operand.  The weights
+// are the forward blob (scaled by c = 2 log2(e)); dT is staged scaled by 1/c,
+// so the MMAs with scaled weights return true gradients.
+struct BwdGroup {
+  static constexpr uint32_t A1B = 128 * 32 * 2, XB = 128 * 64 * 2, DTB = kItemRows * 128 * 16;
+  static constexpr uint32_t O_A1 = 0, O_X = 2 * A1B, O_DT = O_X + 2 * XB, BYTES = O_DT + DTB;
+  static constexpr uint32_t SBO_A1 = (32 / 8) * 128, SBO_X = (64 / 8) * 128;
+  static constexpr uint32_t C_D2 = 0, C_D3 = 64, C_DH1 = 192, COLS = 256;  // TMEM columns per group
+  static constexpr int NG = 2;
+  static constexpr uint32_t SMEM = FwdBlob::O_END + NG * BYTES;
 };
+static_assert(kFwdGroups == BwdGroup::NG, "item padding matches the groups per CTA");
 
 struct BwdArgs {
   TcLists L;
   const unsigned char* nets;
-  size_t net_bytes;
+  size_t net_bytes, fwd_off;
   const float* dT;    // [row][4][D3], already scaled by 1/N
   const double* rij;  // formatted neighbour list vectors
   double* gslot;      // dE/dr per slot
@@ -499,279 +459,348 @@ struct BwdArgs {
   double rcut, rcut_smth;
 };
 
+constexpr float kInvTanhScale = 0.34657359027997264f;  // 1 / c
+
+// r = 1 / (1 + 2^zc): tanh(z) = 1 - 2 r for the scaled pre-activation zc = c z.
+__device__ __forceinline__ float tanh_r(float zc) {
+  float e, r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(zc));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + e));
+  return r;
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// D[tmem] (+)= A[tmem] * B^T: the A operand is read from tensor memory.
+__device__ __forceinline__ void mma_ta(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+template <int D1, int D2, int D3, int H>
+__device__ __forceinline__ void bwd_epi2(const float* f, uint32_t taddr, const float (&h1p)[16], float (&h2)[32],
+                                         float (&t2)[32]) {
+  using P = Split<D1, D2, D3>;
+  float v[32];
+  umma::ld16(taddr + H * 32, v);
+  umma::ld16(taddr + H * 32 + 16, v + 16);
+  umma::wait_ld();
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if (j < P::c2(H)) {
+      const float r = tanh_r(P::FOLD2 ? v[j] : v[j] + f[64 + H * 32 + j]);
+      t2[j] = fmaf(-2.0f, r, 1.0f);
+      h2[j] = fmaf(-2.0f, r, P::R2 != 0 ? h1p[P::src2(H, j)] : 1.0f);  // t2 + h1 (1 + h1 - 2 r)
+    } else {
+      t2[j] = 0.f;
+      h2[j] = (P::FOLD3 && H == 0 && j == P::c2(0)) ? 1.0f : 0.0f;
+    }
+  }
+}
+
+// Layer 3 with its gradient for the 64 positions of half H.  Returns the
+// partial dR~' (over this half's positions) and accumulates racc' (residual
+// gradient into layer 2, scaled by 1/c); writes dz3' into TMEM in place.
+template <int D1, int D2, int D3, int H>
+__device__ __forceinline__ void bwd_epi3(const float* f, uint32_t taddr, const float4* dts, float4 rt,
+                                         const float (&h1p)[16], const float (&t2)[32], float (&racc)[32],
+                                         float4& dR) {
+  using P = Split<D1, D2, D3>;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    float z[16];
+    umma::ld16(taddr + H * 64 + c * 16, z);
+    umma::wait_ld();
+    float v[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int j = c * 16 + i;
+      if (j < P::c3(H)) {
+        const float4 d4 = dts[H * 64 + j];
+        const float dg = fmaf(rt.x, d4.x, fmaf(rt.y, d4.y, fmaf(rt.z, d4.z, rt.w * d4.w)));
+        const float r = tanh_r(P::FOLD3 ? z[i] : z[i] + f[128 + H * 64 + j]);
+        const float t3 = fmaf(-2.0f, r, 1.0f);
+        float gv = t3;
+        if constexpr (P::R3 != 0) {
+          const int s = P::src3(H, j);
+          float h2s = t2[s];
+          if constexpr (P::R2 != 0) h2s += h1p[P::src2(H, s)] - 1.0f;
+          gv += h2s;
+          racc[s] += dg;
+        }
+        dR.x = fmaf(gv, d4.x, dR.x);
+        dR.y = fmaf(gv, d4.y, dR.y);
+        dR.z = fmaf(gv, d4.z, dR.z);
+        dR.w = fmaf(gv, d4.w, dR.w);
+        v[i] = dg * fmaf(-t3, t3, 1.0f);
+      } else {
+        v[i] = 0.f;
+      }
+    }
+    uint32_t pk[16];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) umma::split_pair(v[2 * q], v[2 * q + 1], pk[q], pk[8 + q]);
+    tmem_st16(taddr + H * 64 + c * 16, pk);
+  }
+  tmem_wait_st();
+}
+
+// dh2 total = MMA + layer-3 residual gradient; dz2' = dh2 (1 - t2^2) / c;
+// racc1 collects the layer-2 residual gradient into layer 1.
+template <int D1, int D2, int D3, int H>
+__device__ __forceinline__ void bwd_epi_dh2(uint32_t taddr, const float (&t2)[32], const float (&racc)[32],
+                                            float (&racc1)[16], float (&zz)[32]) {
+  using P = Split<D1, D2, D3>;
+  float v[32];
+  umma::ld16(taddr + H * 32, v);
+  umma::ld16(taddr + H * 32 + 16, v + 16);
+  umma::wait_ld();
+#pragma unroll
+  for (int j = 0; j < 16; ++j) racc1[j] = 0.f;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if (j < P::c2(H)) {
+      const float dh = fmaf(kTanhScale, racc[j], v[j]);
+      if constexpr (P::R2 != 0) racc1[P::src2(H, j)] += dh;
+      zz[j] = dh * kInvTanhScale * fmaf(-t2[j], t2[j], 1.0f);
+    } else {
+      zz[j] = 0.f;
+    }
+  }
+}
+
+// dE/ds of this half: sum over its layer-1 positions of (dh1 + residual) (1 - t1^2) w1.
+template <int D1, int D2, int D3, int H>
+__device__ __forceinline__ float bwd_ds(const float* f, uint32_t taddr, const float (&h1p)[16],
+                                        const float (&racc1)[16]) {
+  using P = Split<D1, D2, D3>;
+  float v[16];
+  umma::ld16(taddr + H * 16, v);
+  umma::wait_ld();
+  float ds = 0.f;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    if (j < P::c1(H)) {
+      const float t1 = h1p[j] - 1.0f;
+      ds = fmaf((v[j] + racc1[j]) * fmaf(-t1, t1, 1.0f), f[H * 16 + j], ds);
+    }
+  }
+  return ds * kInvTanhScale;
+}
+
 template <int D1, int D2, int D3>
-__global__ void __launch_bounds__(128, 1) k_embed_bwd_tc(BwdArgs a) {
-  using F = TcShape<D1, D2, D3>;
-  using B = Bwd<D1, D2, D3>;
+__global__ void __launch_bounds__(256 * BwdGroup::NG, 1) k_embed_bwd_tc(BwdArgs a) {
+  using S = BwdGroup;
+  using B = FwdBlob;
+  using P = Split<D1, D2, D3>;
   extern __shared__ __align__(1024) unsigned char smem[];
-  __shared__ uint64_t bar;
+  __shared__ uint64_t bars[S::NG];
   __shared__ uint32_t tbase;
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const float* w1 = reinterpret_cast<const float*>(smem + F::O_F);
-  const float* b1 = w1 + D1;
-  const float* b2 = b1 + D1;
-  const float* b3 = b2 + D2;
-  const uint32_t w2h = umma::smem_u32(smem + F::O_W2), w2l = w2h + F::W2B;
-  const uint32_t w3h = umma::smem_u32(smem + F::O_W3), w3l = w3h + F::W3B;
-  unsigned char* a1h = smem + B::O_A1;
-  unsigned char* a1l = a1h + B::A1B;
-  unsigned char* xh = smem + B::O_X;
-  unsigned char* xl = xh + B::XB;
-  unsigned char* yh = smem + B::O_Y;
-  unsigned char* yl = yh + B::YB;
-  unsigned char* rh = smem + B::O_R;
-  unsigned char* rl = rh + B::RB;
-  unsigned char* th = smem + B::O_T;
-  unsigned char* tl = th + B::TB;
-  if (warp == 0) umma::tmem_alloc(&tbase, B::NCOLS);
-  if (tid == 0) {
-    umma::mbar_init(&bar, 1);
+  __shared__ float4 xdr[S::NG][128];
+  __shared__ float xds[S::NG][128];
+  const int gtid = threadIdx.x, g = gtid >> 8, t = gtid & 255, hf = t >> 7, e = t & 127;
+  const int bid = 1 + g;
+  const float* f = reinterpret_cast<const float*>(smem + B::O_F);
+  const int* pmap = reinterpret_cast<const int*>(smem + B::O_MAP);
+  unsigned char* gbase = smem + B::O_END + g * S::BYTES;
+  unsigned char* a1h = gbase + S::O_A1;
+  unsigned char* a1l = a1h + S::A1B;
+  unsigned char* xh = gbase + S::O_X;
+  unsigned char* xl = xh + S::XB;
+  float4* dts = reinterpret_cast<float4*>(gbase + S::O_DT);
+  uint64_t* bar = &bars[g];
+  if ((gtid >> 5) == 0) umma::tmem_alloc(&tbase, 512);
+  if (t == 0) {
+    umma::mbar_init(bar, 1);
     umma::fence_mbar_init();
   }
   umma::fence_before_sync();
   __syncthreads();
   umma::fence_after_sync();
-  const uint32_t tm = tbase;
-  const uint32_t lb = (uint32_t)(warp * 32) << 16;
+  const uint32_t tm = tbase + g * S::COLS;
+  const uint32_t lane_base = (uint32_t)((e >> 5) * 32) << 16;
   uint32_t phase = 0;
   int loaded = -1;
   const TcLists& L = a.L;
   const int nitems = L.istart[L.nnets];
-  const uint32_t id2 = umma::idesc_bf16(128, F::D2p, false, false);
-  const uint32_t id3 = umma::idesc_bf16(128, F::D3p, false, false);
-  const uint32_t id_dg = umma::idesc_bf16(128, F::D3p, false, true);
-  const uint32_t id_dr = umma::idesc_bf16(128, B::NT, false, false);
-  const uint32_t id_h2 = umma::idesc_bf16(128, F::D2p, false, true);
-  const uint32_t id_h1 = umma::idesc_bf16(128, F::D1p, false, true);
+  const uint64_t dw2h = umma::desc(umma::smem_u32(smem + B::O_W2), 128, B::SBO_W2);
+  const uint64_t dw2l = umma::desc(umma::smem_u32(smem + B::O_W2 + B::W2B), 128, B::SBO_W2);
+  const uint64_t dw3h = umma::desc(umma::smem_u32(smem + B::O_W3), 128, B::SBO_W3);
+  const uint64_t dw3l = umma::desc(umma::smem_u32(smem + B::O_W3 + B::W3B), 128, B::SBO_W3);
+  // the same blobs read MN-major: W3 as B of dh2 (N = layer-2 positions, K = layer-3
+  // positions), W2 as B of dh1 (N = layer-1 positions, K = layer-2 positions)
+  const uint64_t dw3th = umma::desc(umma::smem_u32(smem + B::O_W3), B::SBO_W3, 128);
+  const uint64_t dw3tl = umma::desc(umma::smem_u32(smem + B::O_W3 + B::W3B), B::SBO_W3, 128);
+  const uint64_t dw2th = umma::desc(umma::smem_u32(smem + B::O_W2), B::SBO_W2, 128);
+  const uint64_t dw2tl = umma::desc(umma::smem_u32(smem + B::O_W2 + B::W2B), B::SBO_W2, 128);
+  const uint64_t da1h = umma::desc(umma::smem_u32(a1h), 128, S::SBO_A1);
+  const uint64_t da1l = umma::desc(umma::smem_u32(a1l), 128, S::SBO_A1);
+  const uint64_t dxh = umma::desc(umma::smem_u32(xh), 128, S::SBO_X);
+  const uint64_t dxl = umma::desc(umma::smem_u32(xl), 128, S::SBO_X);
+  const uint32_t id2 = umma::idesc_bf16(128, 64, false, false);
+  const uint32_t id3 = umma::idesc_bf16(128, 128, false, false);
+  const uint32_t id_h2 = umma::idesc_bf16(128, 64, false, true);
+  const uint32_t id_h1 = umma::idesc_bf16(128, 32, false, true);
   bool aborted = false;
   auto sync_mma = [&]() {
     umma::fence_proxy_async();
     umma::fence_before_sync();
-    __syncthreads();
+    umma::bar_sync(bid, 256);
     umma::fence_after_sync();
   };
   auto wait_mma = [&]() -> bool {
-    const bool ok = umma::mbar_wait(&bar, phase, kWaitLimit);
+    const bool ok = umma::mbar_wait(bar, phase, kWaitLimit);
     phase ^= 1;
-    if (__syncthreads_or(!ok)) return false;
+    if (umma::bar_sync_or(bid, 256, !ok)) return false;
     umma::fence_after_sync();
     return true;
   };
-  for (int it = blockIdx.x; it < nitems && !aborted; it += gridDim.x) {
-    const Item I = item_of(L, it);
-    if (I.e1 <= I.e0) continue;  // CTA-uniform
-    if (I.q != loaded) {
+  for (int base = blockIdx.x * S::NG; base < nitems; base += gridDim.x * S::NG) {
+    const int qr = item_of(L, base).q;
+    if (qr != loaded) {
       __syncthreads();
-      const uint4* src = reinterpret_cast<const uint4*>(a.nets + (size_t)I.q * a.net_bytes);
+      const uint4* src = reinterpret_cast<const uint4*>(a.nets + (size_t)qr * a.net_bytes + a.fwd_off);
       uint4* dst = reinterpret_cast<uint4*>(smem);
-      for (uint32_t i = tid; i < F::BLOB / 16; i += 128) dst[i] = src[i];
-      loaded = I.q;
+      for (uint32_t i = gtid; i < B::BLOB / 16; i += 256 * S::NG) dst[i] = src[i];
+      loaded = qr;
+      __syncthreads();
     }
-    // dT of the item's rows as a [n][a] operand (n = 4 * local row + k)
-    for (int idx = tid; idx < B::NT * (F::D3p / 8); idx += 128) {
-      const int n = idx / (F::D3p / 8), ag = idx - n * (F::D3p / 8);
-      const int row = I.rb + (n >> 2), k = n & 3;
-      float v[8];
-      const float* src = (row < I.re) ? a.dT + ((size_t)row * 4 + k) * D3 : nullptr;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int aa = ag * 8 + j;
-        v[j] = (src && aa < D3) ? src[aa] : 0.f;
+    if (aborted) continue;  // keep taking part in the CTA-wide barriers above
+    const Item I = item_of(L, base + g);
+    if (I.e1 <= I.e0) continue;  // uniform over the group
+    // dT of the item's rows in position order, [row][position] float4 over k, scaled by 1/c
+    for (int idx = t; idx < kItemRows * 128; idx += 256) {
+      const int r = idx >> 7, p = idx & 127, fa = pmap[p], row = I.rb + r;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (fa >= 0 && row < I.re) {
+        const float* src = a.dT + (size_t)row * 4 * D3 + fa;
+        v = make_float4(src[0] * kInvTanhScale, src[D3] * kInvTanhScale, src[2 * D3] * kInvTanhScale,
+                        src[3 * D3] * kInvTanhScale);
       }
-      const uint32_t o = (n >> 3) * B::SBO_T + ag * 128 + (n & 7) * 16;
-      store8_split(th + o, tl + o, v);
+      dts[idx] = v;
     }
+    umma::bar_sync(bid, 256);
     for (int sub = I.e0; sub < I.e1; sub += 128) {
       const int ne = min(128, I.e1 - sub);
-      const bool valid = tid < ne;
-      const float4 rt = valid ? L.rt[sub + tid] : make_float4(0.f, 0.f, 0.f, 0.f);
-      const int rl_ = valid ? L.row[sub + tid] - I.rb : -1;
-      const int slot = valid ? L.slot[sub + tid] : -1;
-      const float rv[4] = {rt.x, rt.y, rt.z, rt.w};
+      const bool valid = e < ne;
+      const float4 rt = valid ? L.rt[sub + e] : make_float4(0.f, 0.f, 0.f, 0.f);
+      const int rloc = valid ? L.row[sub + e] - I.rb : 0;
+      float h1[16], h1p[16], h2[32], t2[32];
+      if (hf == 0)
+        fwd_layer1<D1, D2, D3, 0>(f, rt.x, h1, h1p);
+      else
+        fwd_layer1<D1, D2, D3, 1>(f, rt.x, h1, h1p);
 #pragma unroll
-      for (int ng = 0; ng < B::NT / 8; ++ng) {
-        float v[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int n = ng * 8 + j;
-          v[j] = (rl_ == (n >> 2)) ? rv[n & 3] : 0.f;
-        }
-        const uint32_t o = (tid >> 3) * B::SBO_R + ng * 128 + (tid & 7) * 16;
-        store8_split(rh + o, rl + o, v);
-      }
-      float h1[D1];
-#pragma unroll
-      for (int n = 0; n < D1; ++n) h1[n] = valid ? umma::tanh_fast(rt.x * w1[n] + b1[n]) : 0.f;
-#pragma unroll
-      for (int kg = 0; kg < F::D1p / 8; ++kg) {
-        float v[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = (kg * 8 + j < D1) ? h1[kg * 8 + j] : 0.f;
-        const uint32_t o = (tid >> 3) * F::SBO_A1 + kg * 128 + (tid & 7) * 16;
-        store8_split(a1h + o, a1l + o, v);
+      for (int kk = 0; kk < 2; ++kk) {
+        const uint32_t o = (e >> 3) * S::SBO_A1 + (2 * hf + kk) * 128 + (e & 7) * 16;
+        store8_split(a1h + o, a1l + o, h1 + 8 * kk);
       }
       sync_mma();
-      if (tid == 0) {
-        mma3(tm + B::C_D2, umma::smem_u32(a1h), umma::smem_u32(a1l), w2h, w2l, 128, F::SBO_A1, 128, F::SBO_W2, id2,
-             F::D1p / 16, 256, 256, false);
-        // dG[e][a] = sum_n R~[e][n] dT(a, n); the [n][a] store read MN-major
-        mma3(tm + B::C_DG, umma::smem_u32(rh), umma::smem_u32(rl), umma::smem_u32(th), umma::smem_u32(tl), 128,
-             B::SBO_R, B::SBO_T, 128, id_dg, B::NT / 16, 256, 2 * B::SBO_T, false);
-        umma::commit(&bar);
+      if (t == 0) {
+        mma3d(tm + S::C_D2, da1h, da1l, dw2h, dw2l, id2, 2, 256 >> 4, 256 >> 4, false);
+        umma::commit(bar);
       }
       if (!wait_mma()) {
         aborted = true;
         break;
       }
-      float h2[D2];
+      if (hf == 0)
+        bwd_epi2<D1, D2, D3, 0>(f, tm + lane_base + S::C_D2, h1p, h2, t2);
+      else
+        bwd_epi2<D1, D2, D3, 1>(f, tm + lane_base + S::C_D2, h1p, h2, t2);
 #pragma unroll
-      for (int c = 0; c < F::D2p / 16; ++c) {
-        float v[16];
-        umma::ld16(tm + lb + B::C_D2 + c * 16, v);
-        umma::wait_ld();
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int n = c * 16 + j;
-          if (n < D2) h2[n] = valid ? umma::tanh_fast(v[j] + b2[n]) + resid_of<D2, D1>(h1, n) : 0.f;
-        }
-      }
-#pragma unroll
-      for (int kg = 0; kg < F::D2p / 8; ++kg) {
-        float v[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = (kg * 8 + j < D2) ? h2[kg * 8 + j] : 0.f;
-        const uint32_t o = (tid >> 3) * F::SBO_A2 + kg * 128 + (tid & 7) * 16;
-        store8_split(xh + o, xl + o, v);
+      for (int kk = 0; kk < 4; ++kk) {
+        const uint32_t o = (e >> 3) * S::SBO_X + (4 * hf + kk) * 128 + (e & 7) * 16;
+        store8_split(xh + o, xl + o, h2 + 8 * kk);
       }
       sync_mma();
-      if (tid == 0) {
-        mma3(tm + B::C_D3, umma::smem_u32(xh), umma::smem_u32(xl), w3h, w3l, 128, F::SBO_A2, 128, F::SBO_W3, id3,
-             F::D2p / 16, 256, 256, false);
-        umma::commit(&bar);
+      if (t == 0) {
+        mma3d(tm + S::C_D3, dxh, dxl, dw3h, dw3l, id3, 4, 256 >> 4, 256 >> 4, false);
+        umma::commit(bar);
       }
       if (!wait_mma()) {
         aborted = true;
         break;
       }
-      // layer 3 with its gradient, in halves of 64 columns of a:
-      // G -> X (A of dR~ = G dT^T), dz3 = dG (1 - th3^2) -> Y (A of dh2 = dz3 W3)
-      float racc[D2];
+      float racc[32];
 #pragma unroll
-      for (int n = 0; n < D2; ++n) racc[n] = 0.f;
+      for (int j = 0; j < 32; ++j) racc[j] = 0.f;
+      float4 dR = make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4* drow = dts + rloc * 128;
+      if (hf == 0)
+        bwd_epi3<D1, D2, D3, 0>(f, tm + lane_base + S::C_D3, drow, rt, h1p, t2, racc, dR);
+      else
+        bwd_epi3<D1, D2, D3, 1>(f, tm + lane_base + S::C_D3, drow, rt, h1p, t2, racc, dR);
+      umma::fence_before_sync();
+      umma::bar_sync(bid, 256);
+      umma::fence_after_sync();
+      if (t == 0) {
+        // dh2[e][q] = sum_p dz3'[e][p] W3s[q][p]; A = dz3' in TMEM (hi at +16 s, lo at +16 s + 8)
+        const uint32_t az = tm + S::C_D3;
 #pragma unroll
-      for (int c = 0; c < F::D3p / 16; ++c) {
-        const int h = c / 4, cc = c % 4;
-        float z[16], dg[16];
-        umma::ld16(tm + lb + B::C_D3 + c * 16, z);
-        umma::ld16(tm + lb + B::C_DG + c * 16, dg);
-        umma::wait_ld();
-        float gv[16], zv[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int n = c * 16 + j;
-          if (n < D3 && valid) {
-            const float t3 = umma::tanh_fast(z[j] + b3[n]);
-            gv[j] = t3 + resid_of<D3, D2>(h2, n);
-            zv[j] = dg[j] * (1.f - t3 * t3);
-            if constexpr (D3 == D2) racc[n] += dg[j];
-            if constexpr (D3 == 2 * D2) racc[n < D2 ? n : n - D2] += dg[j];
-          } else {
-            gv[j] = 0.f;
-            zv[j] = 0.f;
-          }
+        for (int s = 0; s < 8; ++s) {
+          const uint64_t ob = (uint64_t)(s * ((2 * B::SBO_W3) >> 4));
+          mma_ta(tm + S::C_D2, az + 16 * s, dw3th + ob, id_h2, s > 0 ? 1u : 0u);
+          mma_ta(tm + S::C_D2, az + 16 * s, dw3tl + ob, id_h2, 1u);
+          mma_ta(tm + S::C_D2, az + 16 * s + 8, dw3th + ob, id_h2, 1u);
         }
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const uint32_t o = (tid >> 3) * B::SBO_H + (2 * cc + hh) * 128 + (tid & 7) * 16;
-          store8_split(xh + o, xl + o, gv + 8 * hh);
-          store8_split(yh + o, yl + o, zv + 8 * hh);
-        }
-        if (cc == 3 || c == F::D3p / 16 - 1) {
-          const int steps = cc + 1;
-          sync_mma();
-          if (tid == 0) {
-            // dR~[e][n] += sum_a G[e][a] dT(n, a) over this half of a
-            mma3(tm + B::C_DR, umma::smem_u32(xh), umma::smem_u32(xl), umma::smem_u32(th) + 1024u * h,
-                 umma::smem_u32(tl) + 1024u * h, 128, B::SBO_H, 128, B::SBO_T, id_dr, steps, 256, 256, h > 0);
-            // dh2[e][k] += sum_a dz3[e][a] W3[k][a] over this half; W3 blob read MN-major
-            mma3(tm + B::C_D2, umma::smem_u32(yh), umma::smem_u32(yl), w3h + 8u * h * F::SBO_W3,
-                 w3l + 8u * h * F::SBO_W3, 128, B::SBO_H, F::SBO_W3, 128, id_h2, steps, 256, 2 * F::SBO_W3, h > 0);
-            umma::commit(&bar);
-          }
-          if (!wait_mma()) {
-            aborted = true;
-            break;
-          }
-        }
+        umma::commit(bar);
       }
-      if (aborted) break;
-      float dR[4] = {0.f, 0.f, 0.f, 0.f};
+      if (!wait_mma()) {
+        aborted = true;
+        break;
+      }
+      // dh2 total -> dz2' into the X slot (the A operand of dh1)
+      float racc1[16];
       {
-        float v[32];
-        umma::ld16(tm + lb + B::C_DR, v);
-        umma::ld16(tm + lb + B::C_DR + 16, v + 16);
-        umma::wait_ld();
+        float zz[32];
+        if (hf == 0)
+          bwd_epi_dh2<D1, D2, D3, 0>(tm + lane_base + S::C_D2, t2, racc, racc1, zz);
+        else
+          bwd_epi_dh2<D1, D2, D3, 1>(tm + lane_base + S::C_D2, t2, racc, racc1, zz);
 #pragma unroll
-        for (int r8 = 0; r8 < kItemRows; ++r8)
-          if (r8 == rl_) {
-#pragma unroll
-            for (int k = 0; k < 4; ++k) dR[k] = v[4 * r8 + k];
-          }
-      }
-      // dh2 = MMA + residual gradient; dz2 = dh2 (1 - th2^2) -> X
-      float dh2[D2];
-#pragma unroll
-      for (int c = 0; c < F::D2p / 16; ++c) {
-        float v[16];
-        umma::ld16(tm + lb + B::C_D2 + c * 16, v);
-        umma::wait_ld();
-        float zz[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int n = c * 16 + j;
-          if (n < D2) {
-            dh2[n] = valid ? v[j] + racc[n] : 0.f;
-            const float t2 = h2[n] - resid_of<D2, D1>(h1, n);
-            zz[j] = dh2[n] * (1.f - t2 * t2);
-          } else {
-            zz[j] = 0.f;
-          }
-        }
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const uint32_t o = (tid >> 3) * F::SBO_A2 + (2 * c + hh) * 128 + (tid & 7) * 16;
-          store8_split(xh + o, xl + o, zz + 8 * hh);
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint32_t o = (e >> 3) * S::SBO_X + (4 * hf + kk) * 128 + (e & 7) * 16;
+          store8_split(xh + o, xl + o, zz + 8 * kk);
         }
       }
       sync_mma();
-      if (tid == 0) {
-        // dh1[e][k1] = sum_n dz2[e][n] W2[k1][n]; W2 blob read MN-major
-        mma3(tm + B::C_DH1, umma::smem_u32(xh), umma::smem_u32(xl), w2h, w2l, 128, F::SBO_A2, F::SBO_W2, 128, id_h1,
-             F::D2p / 16, 256, 2 * F::SBO_W2, false);
-        umma::commit(&bar);
+      if (t == 0) {
+        // dh1[e][l] = sum_q dz2'[e][q] W2s[l][q]
+        mma3d(tm + S::C_DH1, dxh, dxl, dw2th, dw2tl, id_h1, 4, 256 >> 4, (2 * B::SBO_W2) >> 4, false);
+        umma::commit(bar);
       }
       if (!wait_mma()) {
         aborted = true;
         break;
       }
-      float ds = 0.f;
-#pragma unroll
-      for (int c = 0; c < F::D1p / 16; ++c) {
-        float v[16];
-        umma::ld16(tm + lb + B::C_DH1 + c * 16, v);
-        umma::wait_ld();
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int n = c * 16 + j;
-          if (n < D1) {
-            float r = v[j];
-            if constexpr (D2 == D1) r += dh2[n];
-            if constexpr (D2 == 2 * D1) r += dh2[n] + dh2[n + D1];
-            ds += r * (1.f - h1[n] * h1[n]) * w1[n];
-          }
-        }
+      const float ds = hf == 0 ? bwd_ds<D1, D2, D3, 0>(f, tm + lane_base + S::C_DH1, h1p, racc1)
+                               : bwd_ds<D1, D2, D3, 1>(f, tm + lane_base + S::C_DH1, h1p, racc1);
+      if (hf == 1) {
+        xdr[g][e] = dR;
+        xds[g][e] = ds;
       }
-      if (valid) {
+      umma::fence_before_sync();
+      umma::bar_sync(bid, 256);
+      umma::fence_after_sync();
+      if (hf == 0 && valid) {
+        const float4 o4 = xdr[g][e];
+        const double dR0 = kTanhScale * ((double)dR.x + o4.x), dR1 = kTanhScale * ((double)dR.y + o4.y);
+        const double dR2 = kTanhScale * ((double)dR.z + o4.z), dR3 = kTanhScale * ((double)dR.w + o4.w);
+        const double dRv[3] = {dR1, dR2, dR3};
+        const double dsum = (double)ds + xds[g][e];
+        const int slot = L.slot[sub + e];
         // chain rule to r_ij in fp64
         const double* rp = a.rij + 3 * (size_t)slot;
         const double x = rp[0], y = rp[1], zc = rp[2];
@@ -781,7 +810,7 @@ __global__ void __launch_bounds__(128, 1) k_embed_bwd_tc(BwdArgs a) {
         const double ir = 1.0 / rr, ir2 = ir * ir;
         const double d0 = dsw * ir - sw * ir2;
         const double rvec[3] = {x, y, zc};
-        const double g0 = (double)dR[0] + (double)ds;
+        const double g0 = dR0 + dsum;
         double* go = a.gslot + 3 * (size_t)slot;
 #pragma unroll
         for (int cc = 0; cc < 3; ++cc) {
@@ -790,20 +819,19 @@ __global__ void __launch_bounds__(128, 1) k_embed_bwd_tc(BwdArgs a) {
           for (int aa = 0; aa < 3; ++aa) {
             const double J = dsw * rvec[cc] * ir * rvec[aa] * ir2 +
                              sw * ((aa == cc ? ir2 : 0.0) - 2.0 * rvec[aa] * rvec[cc] * ir2 * ir2);
-            acc += (double)dR[1 + aa] * J;
+            acc += dRv[aa] * J;
           }
           go[cc] = acc;
         }
       }
-      umma::fence_before_sync();
-      __syncthreads();
-      umma::fence_after_sync();
     }
+    if (aborted) continue;
+    umma::bar_sync(bid, 256);  // every reader of dts is done before the next item restages it
   }
-  if (aborted && tid == 0) atomicAdd(a.err + kErrTcTimeout, 1);
+  if (aborted && t == 0) atomicAdd(a.err + kErrTcTimeout, 1);
   umma::fence_before_sync();
   __syncthreads();
-  if (warp == 0) umma::tmem_dealloc(tm, B::NCOLS);
+  if ((gtid >> 5) == 0) umma::tmem_dealloc(tbase, 512);
 }
 
 // dT[row][k][a] = (sum_b dD[a][b] T[k][b] + [a < M2] sum_c dD[c][a] T[k][c]) / N
@@ -960,7 +988,6 @@ __global__ void k_item_table(int nnets, int ntypes, int tos, const int* __restri
 
 template <int D1, int D2, int D3>
 void pack_net(const std::vector<HostLayer>& net, std::vector<unsigned char>& out) {
-  using S = TcShape<D1, D2, D3>;
   out.assign(NetBlob<D1, D2, D3>::BYTES, 0);
   auto to_bf16 = [](float f) {
     uint32_t u;
@@ -974,30 +1001,9 @@ void pack_net(const std::vector<HostLayer>& net, std::vector<unsigned char>& out
     std::memcpy(&f, &u, 4);
     return f;
   };
-  auto put = [&](uint32_t base, uint32_t half, int rows, int K, auto val) {
-    for (int r = 0; r < rows; ++r)
-      for (int k = 0; k < K; ++k) {
-        const float x = val(r, k);
-        const uint16_t hi = to_bf16(x);
-        const uint16_t lo = to_bf16(x - from_bf16(hi));
-        const uint32_t o = (uint32_t)(r >> 3) * ((K / 8) * 128) + (uint32_t)(k >> 3) * 128 + (r & 7) * 16 + (k & 7) * 2;
-        std::memcpy(&out[base + o], &hi, 2);
-        std::memcpy(&out[base + half + o], &lo, 2);
-      }
-  };
   const HostLayer& L1 = net[0];
   const HostLayer& L2 = net[1];
   const HostLayer& L3 = net[2];
-  put(S::O_W2, S::W2B, S::D2p, S::D1p,
-      [&](int n, int k) { return (n < D2 && k < D1) ? (float)L2.w[(size_t)k * D2 + n] : 0.f; });
-  put(S::O_W3, S::W3B, S::D3p, S::D2p,
-      [&](int n, int k) { return (n < D3 && k < D2) ? (float)L3.w[(size_t)k * D3 + n] : 0.f; });
-  float* f = reinterpret_cast<float*>(&out[S::O_F]);
-  for (int n = 0; n < D1; ++n) f[n] = (float)L1.w[n];
-  for (int n = 0; n < D1; ++n) f[D1 + n] = (float)L1.b[n];
-  for (int n = 0; n < D2; ++n) f[2 * D1 + n] = (float)L2.b[n];
-  for (int n = 0; n < D3; ++n) f[2 * D1 + D2 + n] = (float)L3.b[n];
-  // forward blob: the same weights in the split kernel's position order
   using FB = FwdBlob;
   const uint32_t fo = NetBlob<D1, D2, D3>::OFF_FWD;
   std::vector<int> p1, p2, p3;
@@ -1061,15 +1067,15 @@ void launch_fwd(cudaStream_t st, const TcLists& L, int grid, const unsigned char
 template <int D1, int D2, int D3>
 void launch_bwd(cudaStream_t st, const TcLists& L, int grid, const unsigned char* nets, const float* dT,
                 const double* rij, double* gslot, int* err, double rcut, double rs) {
-  using Bw = Bwd<D1, D2, D3>;
+  using S = BwdGroup;
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(k_embed_bwd_tc<D1, D2, D3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Bw::SMEM);
+    cudaFuncSetAttribute(k_embed_bwd_tc<D1, D2, D3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::SMEM);
     attr = true;
   }
-  BwdArgs a{L, nets, NetBlob<D1, D2, D3>::BYTES, dT, rij, gslot, err, rcut, rs};
+  BwdArgs a{L, nets, NetBlob<D1, D2, D3>::BYTES, NetBlob<D1, D2, D3>::OFF_FWD, dT, rij, gslot, err, rcut, rs};
   count_launch();
-  k_embed_bwd_tc<D1, D2, D3><<<grid, 128, Bw::SMEM, st>>>(a);
+  k_embed_bwd_tc<D1, D2, D3><<<grid, 256 * S::NG, S::SMEM, st>>>(a);
 }
 
 }  // namespace

@@ -4,13 +4,16 @@
 // or centre type * ntypes + neighbour type for two-sided models), ordered by
 // the centre's row in the type-grouped atom order.  A work item is 8
 // consecutive centre rows of one net; its edges are processed in subtiles of
-// up to 128.  Per subtile the embedding layers 2 and 3 run as tcgen05 MMAs
+// up to 128, two threads per edge (each owns half of every layer's
+// features).  Per subtile the embedding layers 2 and 3 run as tcgen05 MMAs
 // (bf16 hi/lo split, three products, fp32 accumulation in TMEM) and the
 // contraction T^T = G^T R~ runs as a third MMA whose B operand holds each
 // edge's environment row in the column block of its centre (8 centres x 4
 // components = 32 columns), accumulated in TMEM across the item's subtiles.
-// Per-net T are summed in a fixed order by the combine kernel, so results are
-// run-to-run identical.
+// The backward recomputes layers 1-3 the same way, forms dG and dR~ (rank-4
+// contractions with dT) on the CUDA cores and runs the layer backprop
+// (dz3 W3^T, dz2 W2^T) as MMAs.  Per-net T are summed in a fixed order by
+// the combine kernel, so results are run-to-run identical.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -60,8 +63,9 @@ void launch_t_combine(cudaStream_t st, const SeaDev& s, const TcLists& L, const 
 // dE/dT per centre row (scaled by 1/N) from T (atom order) and dE/dD (row order).
 void launch_dT(cudaStream_t st, const SeaDev& s, int nloc, const int* type_start, const int* perm_atom, const float* T,
                const float* dD, float* dT);
-// Embedding backward: recomputes the forward per subtile, then dG, dR~, the
-// layer backprop on tensor cores and the chain rule to r_ij (fp64) -> gslot.
+// Embedding backward: recomputes the forward per subtile, then dG, dR~ (CUDA
+// cores), the layer backprop (tensor cores) and the chain rule to r_ij (fp64)
+// -> gslot.
 void launch_embed_bwd_tc(cudaStream_t st, const SeaDev& s, const TcLists& L, int grid, const unsigned char* nets,
                          const float* dT, const double* rij, double* gslot, int* err);
 // Device error slot written by the tensor-core kernels when a bounded wait expires.
