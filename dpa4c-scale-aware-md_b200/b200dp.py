@@ -42,7 +42,7 @@ class B200DPError(RuntimeError):
 
 class Options(ctypes.Structure):
     _fields_ = [("precision", ctypes.c_int), ("device", ctypes.c_int), ("sel_overflow_is_error", ctypes.c_int),
-                ("simt_only", ctypes.c_int), ("reserved", ctypes.c_int * 12)]
+                ("simt_only", ctypes.c_int), ("keep_descriptor", ctypes.c_int), ("reserved", ctypes.c_int * 11)]
 
 
 class ModelInfo(ctypes.Structure):
@@ -112,7 +112,7 @@ class DeepPot:
     """One engine = one model on one device with one precision."""
 
     def __init__(self, model_path: str, precision: int = MIXED, device: int = 0, sel_overflow_is_error: bool = False,
-                 simt_only: bool = False):
+                 simt_only: bool = False, keep_descriptor: bool = False):
         L = load_library()
         o = Options()
         L.b200dp_options_default(ctypes.byref(o))
@@ -120,6 +120,7 @@ class DeepPot:
         o.device = device
         o.sel_overflow_is_error = int(sel_overflow_is_error)
         o.simt_only = int(simt_only)
+        o.keep_descriptor = int(keep_descriptor)
         h = _vp()
         rc = L.b200dp_create(model_path.encode(), ctypes.byref(o), ctypes.byref(h))
         if rc != 0:

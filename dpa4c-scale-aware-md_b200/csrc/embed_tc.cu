@@ -910,9 +910,11 @@ __global__ void __launch_bounds__(128) k_t_combine(TcLists L, int M2, float inv_
       v[j] = sT[aa] * sT[b] + sT[D3 + aa] * sT[D3 + b] + sT[2 * D3 + aa] * sT[2 * D3 + b] +
              sT[3 * D3 + aa] * sT[3 * D3 + b];
     }
-    float4* drow = reinterpret_cast<float4*>(D + (size_t)r * dim + k0);
-    drow[0] = make_float4(v[0], v[1], v[2], v[3]);
-    drow[1] = make_float4(v[4], v[5], v[6], v[7]);
+    if (D) {
+      float4* drow = reinterpret_cast<float4*>(D + (size_t)r * dim + k0);
+      drow[0] = make_float4(v[0], v[1], v[2], v[3]);
+      drow[1] = make_float4(v[4], v[5], v[6], v[7]);
+    }
     if (Dt_hi) {
       const size_t o = umma::tiled_off(prow, k0, dim);
       store8_split(Dt_hi + o, Dt_lo + o, v);

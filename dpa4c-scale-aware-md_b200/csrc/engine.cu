@@ -464,8 +464,10 @@ b200dp_status Engine::run_model(cudaStream_t st, int nloc, int nall, const int* 
       dth = At_hi[0].as<unsigned char>();
       dtl = At_lo[0].as<unsigned char>();
     }
+    // fp32 D rows feed the SIMT fitting; the tensor-core fitting reads the tiled copy only
+    float* Drows = (!use_fit_tc || opt.keep_descriptor) ? reinterpret_cast<float*>(Dbuf.ptr) : nullptr;
     launch_t_combine(st, sd, Lst, perm_atom.as<int>(), ftile.as<int>(), partial.as<float>(),
-                     reinterpret_cast<float*>(Tbuf.ptr), reinterpret_cast<float*>(Dbuf.ptr), dth, dtl);
+                     reinterpret_cast<float*>(Tbuf.ptr), Drows, dth, dtl);
   } else {
     const int gf = descriptor_grid<P>(sd, ch_fwd, false, nloc);
     launch_descriptor_fwd<P>(st, sd, nloc, ch_fwd, gf, nl_rij.as<double>(), nl_cnt.as<int>(), d_atype,
@@ -488,7 +490,9 @@ b200dp_status Engine::run_model(cudaStream_t st, int nloc, int nall, const int* 
       fb.DY[q] = DYf[q].as<float>();
     }
     launch_fit_tc(st, fplan, hm.ntypes, nloc, type_start.as<int>(), ftile.as<int>(), perm_atom.as<int>(),
-                  fitw.data(), fb, atom_e.as<double>(), reinterpret_cast<float*>(dDbuf.ptr), err_d);
+                  fitw.data(), fb, atom_e.as<double>(), reinterpret_cast<const float*>(Tbuf.ptr),
+                  (float)sd.inv_nnei, dTbuf.as<float>(),
+                  opt.keep_descriptor ? reinterpret_cast<float*>(dDbuf.ptr) : nullptr, err_d);
   } else {
     // fitting, per centre type over its row range [type_start[t], type_start[t+1])
     const int nfl = (int)hm.fit.size();
@@ -527,7 +531,7 @@ b200dp_status Engine::run_model(cudaStream_t st, int nloc, int nall, const int* 
       }
     }
   }
-  if (std::is_same<P, float>::value && use_tc)
+  if (std::is_same<P, float>::value && use_tc && !use_fit_tc)
     launch_dT(st, sd, nloc, type_start.as<int>(), perm_atom.as<int>(), reinterpret_cast<const float*>(Tbuf.ptr),
               reinterpret_cast<const float*>(dDbuf.ptr), dTbuf.as<float>());
   mark(st, 3);
@@ -857,6 +861,10 @@ b200dp_status b200dp_last_descriptor(b200dp_engine* engine, double* descriptor, 
   std::vector<int> perm(n);
   B200DP_CUDA_TRY(cudaMemcpy(perm.data(), e.perm_pos.ptr, sizeof(int) * n, cudaMemcpyDeviceToHost));
   const bool fp64 = e.opt.precision == B200DP_FP64;
+  if (e.use_fit_tc && !e.opt.keep_descriptor) {
+    e.err = "descriptor not kept: create the engine with keep_descriptor = 1";
+    return B200DP_ERR_INVALID;
+  }
   for (int which = 0; which < 2; ++which) {
     double* out = which ? grad_descriptor : descriptor;
     if (!out) continue;

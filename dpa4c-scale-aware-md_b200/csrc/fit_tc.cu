@@ -19,6 +19,13 @@ constexpr long long kWaitLimit = 1LL << 26;
 
 using umma::tiled_off;
 
+// fp32 activations of the fitting (tanh outputs, layer outputs, residual
+// gradients) are stored per 128-row tile column by column, so the epilogue
+// threads (one per row) read and write consecutive addresses.
+__device__ __forceinline__ size_t colmajor_off(int prow, int col, int ncols) {
+  return ((size_t)(prow >> 7) * ncols + col) * 128 + (prow & 127);
+}
+
 __device__ __forceinline__ void store8_split(unsigned char* hi, unsigned char* lo, const float* v) {
   uint32_t h[4], l[4];
 #pragma unroll
@@ -27,7 +34,7 @@ __device__ __forceinline__ void store8_split(unsigned char* hi, unsigned char* l
   *reinterpret_cast<uint4*>(lo) = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
-enum Mode : int { kFwd = 0, kBwd = 1, kBwdFinal = 2 };
+enum Mode : int { kFwd = 0, kBwd = 1 };
 
 struct GemmArgs {
   int ntypes;
@@ -62,7 +69,6 @@ struct GemmArgs {
   int dy_is_wo;
   float* DYout;
   const float* THprev;
-  float* dD;
   int* err;
 };
 
@@ -162,9 +168,9 @@ __global__ void __launch_bounds__(128, 1) k_fit_gemm(GemmArgs a) {
           const int col = col0 + j;
           const float th = umma::tanh_fast(v[j] + a.bias[t][col]);
           float yy = th;
-          if (a.Yprev) yy += a.Yprev[(size_t)prow * a.ldprev + col];
-          a.TH[(size_t)prow * a.N + col] = th;
-          a.Y[(size_t)prow * a.N + col] = yy;
+          if (a.Yprev) yy += a.Yprev[colmajor_off(prow, col, a.ldprev)];
+          a.TH[colmajor_off(prow, col, a.N)] = th;
+          a.Y[colmajor_off(prow, col, a.N)] = yy;
           y[j] = yy;
           if (a.last) {
             const float w = a.wo[t][col];
@@ -192,9 +198,9 @@ __global__ void __launch_bounds__(128, 1) k_fit_gemm(GemmArgs a) {
           if (a.dy_is_wo)
             d += a.wo[t][col];
           else if (a.DYnext)
-            d += a.DYnext[(size_t)prow * a.N + col];
-          if (a.DYout) a.DYout[(size_t)prow * a.N + col] = d;
-          const float th = a.THprev[(size_t)prow * a.N + col];
+            d += a.DYnext[colmajor_off(prow, col, a.N)];
+          if (a.DYout) a.DYout[colmajor_off(prow, col, a.N)] = d;
+          const float th = a.THprev[colmajor_off(prow, col, a.N)];
           z[j] = d * (1.f - th * th);
         }
 #pragma unroll
@@ -202,10 +208,6 @@ __global__ void __launch_bounds__(128, 1) k_fit_gemm(GemmArgs a) {
           const size_t o = tiled_off(prow, col0 + 8 * h, a.kpad_z);
           store8_split(a.Z_hi + o, a.Z_lo + o, z + 8 * h);
         }
-      } else {
-        float* dst = a.dD + (size_t)urow * a.N + col0;
-#pragma unroll
-        for (int j = 0; j < 16; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
       }
     }
     if (a.mode == kFwd && a.last && valid) a.atom_e[a.perm_atom[urow]] = e_acc + a.bo[t];
@@ -213,6 +215,205 @@ __global__ void __launch_bounds__(128, 1) k_fit_gemm(GemmArgs a) {
   umma::fence_before_sync();
   __syncthreads();
   if (warp == 0) umma::tmem_dealloc(tm, 256);
+}
+
+// ------------------------------------------------------------ final backward
+// dD = dz0 W0^T fused with the descriptor contraction (D = T^T T_<, with T
+// already divided by N):
+//   dT[k][a] = (sum_b dD[a][b] T[k][b] + [a < M2] sum_c dD[c][a] T[k][c]) / N
+// One CTA per 128-row tile.  The whole dz0 tile stays in shared memory; dD is
+// produced in N chunks of BN = 16 NA columns (NA descriptor rows a) into two
+// TMEM buffers, so the epilogue of chunk j overlaps the MMAs of chunk j + 1.
+// Warps 0-7 run the epilogue (two warps per TMEM lane quadrant, each taking
+// half of the chunk's a values); warp 8 streams W0 and issues the MMAs.  dD
+// itself is written only when requested (descriptor inspection).
+constexpr int kDtStages = 3;
+constexpr int kDtThreads = 288;
+
+struct DtArgs {
+  int ntypes;
+  const int* type_start;
+  const int* ftile;
+  int nk;  // K chunks of dz0 (32 columns each)
+  const unsigned char* A_hi;
+  const unsigned char* A_lo;
+  const unsigned char* B_hi[kMaxTypes];
+  const unsigned char* B_lo[kMaxTypes];
+  int BN, nchunks, M1;
+  float inv_nnei;
+  const float* T;  // [atom][4][M1]
+  const int* perm_atom;
+  float* dT;  // [row][4][M1]
+  float* dD;  // [row][16 M1] or null
+  int* err;
+};
+
+__global__ void __launch_bounds__(kDtThreads, 1) k_fit_dT(DtArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem[];
+  __shared__ uint64_t a_full, b_full[kDtStages], b_empty[kDtStages], acc_full[2], acc_empty[2];
+  __shared__ uint32_t tbase;
+  __shared__ int s_fail;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = blockIdx.x;
+  if (g >= a.ftile[a.ntypes]) return;  // CTA-uniform, before any TMEM allocation
+  int t = 0;
+  while (t + 1 < a.ntypes && a.ftile[t + 1] <= g) ++t;
+  const int row0 = a.type_start[t] + 128 * (g - a.ftile[t]);
+  const int nrows = min(128, a.type_start[t + 1] - row0);
+  const uint32_t AH = (uint32_t)a.nk * kABlock;  // one half of the dz0 tile
+  const uint32_t BB = (uint32_t)a.BN * kFitBK * 2;
+  unsigned char* sA = smem;
+  unsigned char* sB = smem + 2 * AH;
+  if (warp == 0) umma::tmem_alloc(&tbase, 512);
+  if (tid == 0) {
+    umma::mbar_init(&a_full, 1);
+    for (int s = 0; s < kDtStages; ++s) {
+      umma::mbar_init(&b_full[s], 1);
+      umma::mbar_init(&b_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      umma::mbar_init(&acc_full[i], 1);
+      umma::mbar_init(&acc_empty[i], 256);
+    }
+    umma::fence_mbar_init();
+    s_fail = 0;
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+  const int total = a.nchunks * a.nk;
+  if (warp == 8) {
+    if (lane == 0) {
+      const unsigned char* Ah = a.A_hi + (size_t)g * AH;
+      const unsigned char* Al = a.A_lo + (size_t)g * AH;
+      umma::mbar_expect_tx(&a_full, 2 * AH);
+      for (int kc = 0; kc < a.nk; ++kc) {
+        umma::bulk_g2s(sA + kc * kABlock, Ah + (size_t)kc * kABlock, kABlock, &a_full);
+        umma::bulk_g2s(sA + AH + kc * kABlock, Al + (size_t)kc * kABlock, kABlock, &a_full);
+      }
+      const unsigned char* Bh = a.B_hi[t];
+      const unsigned char* Bl = a.B_lo[t];
+      // B blocks are ordered (N chunk, K chunk): iteration it is block it
+      auto load = [&](int it) {
+        const int s = it % kDtStages;
+        unsigned char* st = sB + s * 2 * BB;
+        umma::mbar_expect_tx(&b_full[s], 2 * BB);
+        umma::bulk_g2s(st, Bh + (size_t)it * BB, BB, &b_full[s]);
+        umma::bulk_g2s(st + BB, Bl + (size_t)it * BB, BB, &b_full[s]);
+      };
+      for (int it = 0; it < min(kDtStages, total); ++it) load(it);
+      bool ok = umma::mbar_wait(&a_full, 0, kWaitLimit);
+      umma::fence_after_sync();
+      const uint32_t idesc = umma::idesc_bf16(128, a.BN, false, false);
+      const uint32_t a0 = umma::smem_u32(sA);
+      for (int j = 0; j < a.nchunks && ok; ++j) {
+        const int buf = j & 1;
+        if (j >= 2) {
+          ok = umma::mbar_wait(&acc_empty[buf], ((j - 2) >> 1) & 1, kWaitLimit);
+          if (!ok) break;
+          umma::fence_after_sync();
+        }
+        const uint32_t d = tbase + buf * 256;
+        for (int kc = 0; kc < a.nk && ok; ++kc) {
+          const int it = j * a.nk + kc, s = it % kDtStages;
+          ok = umma::mbar_wait(&b_full[s], (it / kDtStages) & 1, kWaitLimit);
+          if (!ok) break;
+          umma::fence_after_sync();
+          const uint32_t ah = a0 + kc * kABlock, al = ah + AH;
+          const uint32_t bh = umma::smem_u32(sB + s * 2 * BB), bl = bh + BB;
+#pragma unroll
+          for (int ks = 0; ks < kFitBK / 16; ++ks) {
+            const uint32_t o = ks * 256;
+            umma::mma(d, umma::desc(ah + o, 128, kSbo), umma::desc(bh + o, 128, kSbo), idesc, (kc | ks) ? 1u : 0u);
+            umma::mma(d, umma::desc(ah + o, 128, kSbo), umma::desc(bl + o, 128, kSbo), idesc, 1u);
+            umma::mma(d, umma::desc(al + o, 128, kSbo), umma::desc(bh + o, 128, kSbo), idesc, 1u);
+          }
+          umma::commit(&b_empty[s]);
+          if (it >= 1 && it - 1 + kDtStages < total) {
+            const int sp = (it - 1) % kDtStages;
+            ok = umma::mbar_wait(&b_empty[sp], ((it - 1) / kDtStages) & 1, kWaitLimit);
+            if (ok) load(it - 1 + kDtStages);
+          }
+        }
+        umma::commit(&acc_full[buf]);
+      }
+      if (!ok) s_fail = 1;
+    }
+  } else {
+    const int h = warp >> 2, q = warp & 3, r = q * 32 + lane;
+    const bool valid = r < nrows;
+    const int urow = row0 + r;
+    const int M1 = a.M1;
+    const float* Trow = a.T + (size_t)(valid ? a.perm_atom[urow] : 0) * 4 * M1;
+    float* dTrow = a.dT + (size_t)urow * 4 * M1;
+    const uint32_t lb = (uint32_t)(q * 32) << 16;
+    float Tb[4][16], acc2[4][16];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+      for (int b = 0; b < 16; ++b) {
+        Tb[k][b] = valid ? Trow[k * M1 + b] : 0.f;
+        acc2[k][b] = 0.f;
+      }
+    const int NA = a.BN / 16, NAh = NA / 2;
+    bool ok = true;
+    for (int j = 0; j < a.nchunks; ++j) {
+      const int buf = j & 1;
+      if (ok) ok = umma::mbar_wait(&acc_full[buf], (j >> 1) & 1, kWaitLimit);
+      umma::fence_after_sync();
+      if (ok) {
+        for (int i = 0; i < NAh; ++i) {
+          const int ai = h * NAh + i, aa = j * NA + ai;
+          float dv[16];
+          umma::ld16(tbase + lb + buf * 256 + ai * 16, dv);
+          umma::wait_ld();
+          if (valid) {
+            float Ta[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) Ta[k] = Trow[k * M1 + aa];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              float s = 0.f;
+#pragma unroll
+              for (int b = 0; b < 16; ++b) {
+                s = fmaf(dv[b], Tb[k][b], s);
+                acc2[k][b] = fmaf(dv[b], Ta[k], acc2[k][b]);
+              }
+              dTrow[k * M1 + aa] = s * a.inv_nnei;
+            }
+            if (a.dD) {
+              float4* dst = reinterpret_cast<float4*>(a.dD + (size_t)urow * 16 * M1 + aa * 16);
+#pragma unroll
+              for (int b = 0; b < 16; b += 4) dst[b / 4] = make_float4(dv[b], dv[b + 1], dv[b + 2], dv[b + 3]);
+            }
+          }
+        }
+      }
+      umma::fence_before_sync();
+      umma::mbar_arrive(&acc_empty[buf]);
+    }
+    // every MMA has completed (the last acc_full), so the dz0 tile is free for the exchange
+    float* xs = reinterpret_cast<float*>(smem);
+    if (h == 1) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+#pragma unroll
+        for (int b = 0; b < 16; ++b) xs[(k * 16 + b) * 128 + r] = acc2[k][b];
+    }
+    umma::bar_sync(1, 256);  // also orders the dT stores of both halves
+    if (h == 0 && valid && ok) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+#pragma unroll
+        for (int b = 0; b < 16; ++b)
+          dTrow[k * M1 + b] += (acc2[k][b] + xs[(k * 16 + b) * 128 + r]) * a.inv_nnei;
+    }
+    if (!ok) s_fail = 1;
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  if (tid == 0 && s_fail) atomicAdd(a.err + 3, 1);
+  if (warp == 0) umma::tmem_dealloc(tbase, 512);
 }
 
 __global__ void k_fit_tile_table(int ntypes, const int* __restrict__ type_start, int* __restrict__ ftile) {
@@ -274,12 +475,15 @@ FitTcPlan fit_tc_plan(const HostModel& m) {
     p.bnf[l] = (l == p.L - 1) ? p.width[l] : split_bn(p.width[l]);
     p.bnb[l] = (l == 0) ? 0 : split_bn(p.width[l - 1]);
   }
+  // final backward: N chunks of whole descriptor rows (16 columns each), an
+  // even number of rows per chunk (two epilogue halves)
   p.bn_out = 0;
-  for (int bn = 256; bn >= 16; bn -= 16)
-    if (p.dim % bn == 0) {
-      p.bn_out = bn;
-      break;
-    }
+  if (m.axis == 16)
+    for (int bn = 256; bn >= 32; bn -= 32)
+      if (p.dim % bn == 0) {
+        p.bn_out = bn;
+        break;
+      }
   p.ok = p.bn_out > 0;
   return p;
 }
@@ -342,7 +546,7 @@ static void run_gemm(cudaStream_t st, GemmArgs& a, int row_tiles, int ntn) {
 
 void launch_fit_tc(cudaStream_t st, const FitTcPlan& p, int ntypes, int nloc, const int* type_start,
                    const int* ftile, const int* perm_atom, const FitTcWeights* w, const FitTcBuffers& b,
-                   double* atom_energy, float* dD, int* err) {
+                   double* atom_energy, const float* T, float inv_nnei, float* dT, float* dD, int* err) {
   if (nloc <= 0) return;
   const int row_tiles = (nloc + 127) / 128 + ntypes;
   const int L = p.L;
@@ -413,11 +617,35 @@ void launch_fit_tc(cudaStream_t st, const FitTcPlan& p, int ntypes, int nloc, co
       a.kpad_z = round32(p.width[l - 1]);
       run_gemm(st, a, row_tiles, p.width[l - 1] / p.bnb[l]);
     } else {
-      a.BN = p.bn_out;
-      a.N = p.dim;
-      a.mode = kBwdFinal;
-      a.dD = dD;
-      run_gemm(st, a, row_tiles, p.dim / p.bn_out);
+      DtArgs d;
+      std::memset(&d, 0, sizeof(d));
+      d.ntypes = ntypes;
+      d.type_start = type_start;
+      d.ftile = ftile;
+      d.nk = a.nk;
+      d.A_hi = a.A_hi;
+      d.A_lo = a.A_lo;
+      for (int t = 0; t < ntypes; ++t) {
+        d.B_hi[t] = a.B_hi[t];
+        d.B_lo[t] = a.B_lo[t];
+      }
+      d.BN = p.bn_out;
+      d.nchunks = p.dim / p.bn_out;
+      d.M1 = p.dim / 16;
+      d.inv_nnei = inv_nnei;
+      d.T = T;
+      d.perm_atom = perm_atom;
+      d.dT = dT;
+      d.dD = dD;
+      d.err = err;
+      const size_t smem = 2 * (size_t)d.nk * kABlock + kDtStages * 2 * (size_t)d.BN * kFitBK * 2;
+      static size_t attr = 0;
+      if (smem > attr) {
+        cudaFuncSetAttribute(k_fit_dT, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        attr = smem;
+      }
+      count_launch();
+      k_fit_dT<<<row_tiles, kDtThreads, smem, st>>>(d);
     }
   }
 }

@@ -30,7 +30,7 @@ struct FitTcPlan {
   int width[kFitMaxLayers] = {};  // hidden widths
   int kpad[kFitMaxLayers] = {};   // padded K of each layer's input
   int res[kFitMaxLayers] = {};    // residual on layer l
-  int bn_out = 0;                 // N tile of the final dE/dD GEMM
+  int bn_out = 0;                 // N chunk of the final dE/dD GEMM (fused with dE/dT)
   int bnf[kFitMaxLayers] = {};    // N tile of each forward layer (the last one keeps whole rows)
   int bnb[kFitMaxLayers] = {};    // N tile of each backward layer
   bool ok = false;
@@ -60,7 +60,7 @@ struct FitTcBuffers {
   size_t rows_padded;
   unsigned char* At_hi[kFitMaxLayers];  // tiled input of each forward layer
   unsigned char* At_lo[kFitMaxLayers];
-  float* TH[kFitMaxLayers];             // tanh outputs [rows_padded x width]
+  float* TH[kFitMaxLayers];             // tanh outputs, rows_padded x width (per 128-row tile, column-major)
   float* Y[kFitMaxLayers];              // layer outputs
   unsigned char* Z_hi[2];               // tiled dz ping-pong
   unsigned char* Z_lo[2];
@@ -72,10 +72,12 @@ void launch_fit_tile_table(cudaStream_t st, int ntypes, const int* type_start, i
 // Writes D (fp32 rows in type-grouped order) into the tiled layer-0 input.
 void launch_fit_tile_D(cudaStream_t st, int nloc, int ntypes, int dim, const int* type_start, const int* ftile,
                        const float* D, unsigned char* hi, unsigned char* lo);
-// Whole fitting forward + backward; energies to atom_energy (atom order), dE/dD
-// to dD (fp32 rows in type-grouped order).
+// Whole fitting forward + backward; energies to atom_energy (atom order) and
+// dE/dT (rows in type-grouped order, [row][4][M1], through D = T^T T_< with T
+// in atom order already divided by N) to dT; dE/dD to dD only when dD is not
+// null.
 void launch_fit_tc(cudaStream_t st, const FitTcPlan& p, int ntypes, int nloc, const int* type_start,
                    const int* ftile, const int* perm_atom, const FitTcWeights* w, const FitTcBuffers& b,
-                   double* atom_energy, float* dD, int* err);
+                   double* atom_energy, const float* T, float inv_nnei, float* dT, float* dD, int* err);
 
 }  // namespace b200dp

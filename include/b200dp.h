@@ -62,7 +62,9 @@ typedef struct b200dp_options {
   int device;                 /* CUDA device ordinal */
   int sel_overflow_is_error;  /* 0: truncate to sel like DeePMD; 1: report B200DP_ERR_SEL_OVERFLOW */
   int simt_only;              /* 1: never use the tensor-core kernels (mixed mode uses SIMT fp32) */
-  int reserved[12];
+  int keep_descriptor;        /* 1: keep D and dE/dD of the last call for b200dp_last_descriptor (the
+                                 tensor-core mixed path otherwise never materialises them) */
+  int reserved[11];
 } b200dp_options;
 
 typedef struct b200dp_model_info {
@@ -145,7 +147,9 @@ long long b200dp_sel_overflow_count(b200dp_engine* engine);
 b200dp_status b200dp_last_nlist(b200dp_engine* engine, int* nlist, int* image, double* rij);
 
 /* Descriptor and its energy gradient of the last call, [nlocal * descriptor_dim]
- * in atom order, widened to fp64. */
+ * in atom order, widened to fp64.  In mixed precision with the tensor-core
+ * path this needs an engine created with keep_descriptor = 1 (else
+ * B200DP_ERR_INVALID). */
 b200dp_status b200dp_last_descriptor(b200dp_engine* engine, double* descriptor, double* grad_descriptor);
 
 /* Per-stage device times of the last call in milliseconds (CUDA events on

@@ -242,15 +242,26 @@ def test_tensor_core_descriptor_matches_simt(model_dir, name):
     """The tcgen05 embedding path and the SIMT fp32 path give the same descriptor."""
     g, meta = golden(name)
     path = golden_model_path(model_dir, meta)
-    tc = b200dp.DeepPot(path, precision=b200dp.MIXED)
+    tc = b200dp.DeepPot(path, precision=b200dp.MIXED, keep_descriptor=True)
     simt = b200dp.DeepPot(path, precision=b200dp.MIXED, simt_only=True)
     n = len(g["atype"])
     rt = tc.compute(g["coord"], g["atype"], g["box"])
     rs = simt.compute(g["coord"], g["atype"], g["box"])
-    d_tc, _ = tc.last_descriptor(n)
-    d_s, _ = simt.last_descriptor(n)
+    d_tc, dd_tc = tc.last_descriptor(n)
+    d_s, dd_s = simt.last_descriptor(n)
     assert rel(d_tc, d_s) < 2e-5
+    assert rel(dd_tc, dd_s) < 2e-4
     assert abs(rt["energy"] - rs["energy"]) <= 2e-5 * abs(rs["energy"])
     assert rel(rt["force"], rs["force"]) < 2e-4
     tc.close()
     simt.close()
+
+
+def test_descriptor_not_kept_is_an_error(model_dir):
+    """The tensor-core mixed path never materialises D and dE/dD unless asked to."""
+    s = systems.config0()
+    dp = b200dp.DeepPot(str(model_dir / "water.b2dp"), precision=b200dp.MIXED)
+    dp.compute(s.coord, s.atype, s.box)
+    with pytest.raises(b200dp.B200DPError):
+        dp.last_descriptor(s.natoms)
+    dp.close()
