@@ -11,7 +11,7 @@ namespace b200dp {
 
 namespace {
 
-constexpr int kStages = 4;
+constexpr int kMaxStages = 8;
 constexpr uint32_t kABlock = 128 * kFitBK * 2;  // one half of a 128 x 32 activation block (8 KB)
 constexpr uint32_t kSbo = (kFitBK / 8) * 128;    // K-major SBO inside a block (512 B)
 constexpr long long kWaitLimit = 1LL << 26;
@@ -47,6 +47,7 @@ struct GemmArgs {
   const unsigned char* B_lo[kMaxTypes];
   int BN, N;
   int mode;
+  int stages;  // K-chunk pipeline depth
   // forward
   const float* bias[kMaxTypes];
   const float* Yprev;
@@ -72,12 +73,21 @@ struct GemmArgs {
   int* err;
 };
 
-__global__ void __launch_bounds__(128, 1) k_fit_gemm(GemmArgs a) {
+// Warps 0-15 run the epilogue (4 warps per TMEM lane quadrant share a
+// tile's columns); warp 16 streams the K chunks of A and B into a ring of
+// shared-memory stages, warp 17 issues the MMAs, so loads, MMAs and their
+// bookkeeping proceed independently.  Ring indices advance by increments
+// (no runtime division in the issue loops).
+constexpr int kFitEpiThreads = 512;
+constexpr int kFitThreads = kFitEpiThreads + 64;
+
+__global__ void __launch_bounds__(kFitThreads, 1) k_fit_gemm(GemmArgs a) {
   extern __shared__ __align__(1024) unsigned char smem[];
-  __shared__ uint64_t full[kStages], empty[kStages], done;
+  __shared__ uint64_t full[kMaxStages], empty[kMaxStages], done;
   __shared__ uint32_t tbase;
   __shared__ int s_ok;
-  const int tid = threadIdx.x, warp = tid >> 5;
+  __shared__ double s_e[kFitEpiThreads / 128][128];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = blockIdx.x, nt = blockIdx.y;
   if (g >= a.ftile[a.ntypes]) return;  // CTA-uniform, before any TMEM allocation
   int t = 0;
@@ -87,8 +97,9 @@ __global__ void __launch_bounds__(128, 1) k_fit_gemm(GemmArgs a) {
   const uint32_t BB = (uint32_t)a.BN * kFitBK * 2;
   const uint32_t SB = 2 * kABlock + 2 * BB;
   if (warp == 0) umma::tmem_alloc(&tbase, 256);
+  const int S = a.stages;
   if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < S; ++s) {
       umma::mbar_init(&full[s], 1);
       umma::mbar_init(&empty[s], 1);
     }
@@ -100,62 +111,69 @@ __global__ void __launch_bounds__(128, 1) k_fit_gemm(GemmArgs a) {
   __syncthreads();
   umma::fence_after_sync();
   const uint32_t tm = tbase;
-  if (tid == 0) {
-    const uint32_t idesc = umma::idesc_bf16(128, a.BN, false, false);
+  if (warp == kFitEpiThreads / 32 && lane == 0) {  // loader
     const unsigned char* Ah = a.A_hi + (size_t)g * a.nk * kABlock;
     const unsigned char* Al = a.A_lo + (size_t)g * a.nk * kABlock;
     const unsigned char* Bh = a.B_hi[t] + (size_t)nt * a.nk * BB;
     const unsigned char* Bl = a.B_lo[t] + (size_t)nt * a.nk * BB;
-    auto load = [&](int kc) {
-      const int s = kc % kStages;
+    int s = 0, round = 0;
+    for (int kc = 0; kc < a.nk; ++kc) {
+      if (round > 0 && !umma::mbar_wait(&empty[s], (round - 1) & 1, kWaitLimit)) {
+        s_ok = 0;
+        break;
+      }
       unsigned char* st = smem + s * SB;
       umma::mbar_expect_tx(&full[s], SB);
       umma::bulk_g2s(st, Ah + (size_t)kc * kABlock, kABlock, &full[s]);
       umma::bulk_g2s(st + kABlock, Al + (size_t)kc * kABlock, kABlock, &full[s]);
       umma::bulk_g2s(st + 2 * kABlock, Bh + (size_t)kc * BB, BB, &full[s]);
       umma::bulk_g2s(st + 2 * kABlock + BB, Bl + (size_t)kc * BB, BB, &full[s]);
-    };
-    for (int kc = 0; kc < min(kStages, a.nk); ++kc) load(kc);
+      if (++s == S) {
+        s = 0;
+        ++round;
+      }
+    }
+  } else if (warp == kFitEpiThreads / 32 + 1 && lane == 0) {  // MMA issuer
+    const uint32_t idesc = umma::idesc_bf16(128, a.BN, false, false);
+    const uint64_t d0 = umma::desc(umma::smem_u32(smem), 128, kSbo);
+    const uint64_t sstep = SB >> 4, o_al = kABlock >> 4, o_bh = (2 * kABlock) >> 4, o_bl = (2 * kABlock + BB) >> 4;
+    int s = 0, round = 0;
     bool ok = true;
-    for (int kc = 0; kc < a.nk && ok; ++kc) {
-      const int s = kc % kStages;
-      ok = umma::mbar_wait(&full[s], (kc / kStages) & 1, kWaitLimit);
+    for (int kc = 0; kc < a.nk; ++kc) {
+      ok = umma::mbar_wait(&full[s], round & 1, kWaitLimit);
       if (!ok) break;
       umma::fence_after_sync();
-      const uint32_t st = umma::smem_u32(smem + s * SB);
-      const uint32_t ah = st, al = st + kABlock, bh = st + 2 * kABlock, bl = st + 2 * kABlock + BB;
+      const uint64_t ah = d0 + (uint64_t)s * sstep;
 #pragma unroll
       for (int ks = 0; ks < kFitBK / 16; ++ks) {
-        const uint32_t o = ks * 256;
-        umma::mma(tm, umma::desc(ah + o, 128, kSbo), umma::desc(bh + o, 128, kSbo), idesc, (kc | ks) ? 1u : 0u);
-        umma::mma(tm, umma::desc(ah + o, 128, kSbo), umma::desc(bl + o, 128, kSbo), idesc, 1u);
-        umma::mma(tm, umma::desc(al + o, 128, kSbo), umma::desc(bh + o, 128, kSbo), idesc, 1u);
+        const uint64_t o = (uint64_t)(ks * (256 >> 4));
+        umma::mma(tm, ah + o, ah + o_bh + o, idesc, (kc | ks) ? 1u : 0u);
+        umma::mma(tm, ah + o, ah + o_bl + o, idesc, 1u);
+        umma::mma(tm, ah + o_al + o, ah + o_bh + o, idesc, 1u);
       }
       umma::commit(&empty[s]);
-      if (kc >= 1) {
-        const int j = kc - 1 + kStages;
-        if (j < a.nk) {
-          const int sp = (kc - 1) % kStages;
-          ok = umma::mbar_wait(&empty[sp], ((kc - 1) / kStages) & 1, kWaitLimit);
-          if (ok) load(j);
-        }
+      if (++s == S) {
+        s = 0;
+        ++round;
       }
     }
     umma::commit(&done);
     if (!ok) s_ok = 0;
   }
   const bool ok = umma::mbar_wait(&done, 0, kWaitLimit);
+  const int q = warp & 3, part = warp >> 2;  // lane quadrant, column part
+  const int r = q * 32 + lane;               // row within the tile (TMEM lane)
+  const bool valid = r < nrows;
+  const int prow = g * 128 + r;  // padded row
+  const int urow = row0 + r;     // row in type-grouped order
+  const int nparts = warp < kFitEpiThreads / 32 ? kFitEpiThreads / 128 : 0;
   if (__syncthreads_or(!ok || !s_ok)) {
     if (tid == 0) atomicAdd(a.err + 3, 1);
   } else {
     umma::fence_after_sync();
-    const int r = tid;  // row within the tile (TMEM lane)
-    const bool valid = r < nrows;
-    const int prow = g * 128 + r;     // padded row
-    const int urow = row0 + r;        // row in type-grouped order
-    const uint32_t lb = (uint32_t)(warp * 32) << 16;
+    const uint32_t lb = (uint32_t)(q * 32) << 16;
     double e_acc = 0.0;
-    for (int c = 0; c < a.BN / 16; ++c) {
+    for (int c = part; nparts && c < a.BN / 16; c += nparts) {
       float v[16];
       umma::ld16(tm + lb + c * 16, v);
       umma::wait_ld();
@@ -189,7 +207,7 @@ __global__ void __launch_bounds__(128, 1) k_fit_gemm(GemmArgs a) {
             store8_split(a.Anext_hi + o, a.Anext_lo + o, y + 8 * h);
           }
         }
-      } else if (a.mode == kBwd) {
+      } else {
         float z[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
@@ -210,7 +228,15 @@ __global__ void __launch_bounds__(128, 1) k_fit_gemm(GemmArgs a) {
         }
       }
     }
-    if (a.mode == kFwd && a.last && valid) a.atom_e[a.perm_atom[urow]] = e_acc + a.bo[t];
+    if (a.mode == kFwd && a.last) {  // partial energies of the column parts, summed in a fixed order
+      if (nparts) s_e[part][r] = e_acc;
+      __syncthreads();
+      if (nparts && part == 0 && valid) {
+        double e = a.bo[t];
+        for (int p2 = 0; p2 < kFitEpiThreads / 128; ++p2) e += s_e[p2][r];
+        a.atom_e[a.perm_atom[urow]] = e;
+      }
+    }
   }
   umma::fence_before_sync();
   __syncthreads();
@@ -224,11 +250,14 @@ __global__ void __launch_bounds__(128, 1) k_fit_gemm(GemmArgs a) {
 // One CTA per 128-row tile.  The whole dz0 tile stays in shared memory; dD is
 // produced in N chunks of BN = 16 NA columns (NA descriptor rows a) into two
 // TMEM buffers, so the epilogue of chunk j overlaps the MMAs of chunk j + 1.
-// Warps 0-7 run the epilogue (two warps per TMEM lane quadrant, each taking
-// half of the chunk's a values); warp 8 streams W0 and issues the MMAs.  dD
-// itself is written only when requested (descriptor inspection).
-constexpr int kDtStages = 3;
-constexpr int kDtThreads = 288;
+// Warps 0-15 run the epilogue: four warps per TMEM lane quadrant, one per
+// environment component k, each reading the whole chunk of its rows; warp 16
+// streams W0 through a ring of shared-memory stages and warp 17 issues the
+// MMAs.  dD itself is written only when requested
+// (descriptor inspection).
+constexpr int kDtMaxStages = 16;
+constexpr int kDtThreads = 576;
+constexpr size_t kDtSmemMax = 227 * 1024 - 2048;  // dynamic shared memory budget of k_fit_dT
 
 struct DtArgs {
   int ntypes;
@@ -239,7 +268,7 @@ struct DtArgs {
   const unsigned char* A_lo;
   const unsigned char* B_hi[kMaxTypes];
   const unsigned char* B_lo[kMaxTypes];
-  int BN, nchunks, M1;
+  int BN, nchunks, M1, stages;
   float inv_nnei;
   const float* T;  // [atom][4][M1]
   const int* perm_atom;
@@ -250,7 +279,7 @@ struct DtArgs {
 
 __global__ void __launch_bounds__(kDtThreads, 1) k_fit_dT(DtArgs a) {
   extern __shared__ __align__(1024) unsigned char smem[];
-  __shared__ uint64_t a_full, b_full[kDtStages], b_empty[kDtStages], acc_full[2], acc_empty[2];
+  __shared__ uint64_t a_full, b_full[kDtMaxStages], b_empty[kDtMaxStages], acc_full[2], acc_empty[2];
   __shared__ uint32_t tbase;
   __shared__ int s_fail;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -267,13 +296,13 @@ __global__ void __launch_bounds__(kDtThreads, 1) k_fit_dT(DtArgs a) {
   if (warp == 0) umma::tmem_alloc(&tbase, 512);
   if (tid == 0) {
     umma::mbar_init(&a_full, 1);
-    for (int s = 0; s < kDtStages; ++s) {
+    for (int s = 0; s < a.stages; ++s) {
       umma::mbar_init(&b_full[s], 1);
       umma::mbar_init(&b_empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       umma::mbar_init(&acc_full[i], 1);
-      umma::mbar_init(&acc_empty[i], 256);
+      umma::mbar_init(&acc_empty[i], 512);
     }
     umma::fence_mbar_init();
     s_fail = 0;
@@ -282,106 +311,114 @@ __global__ void __launch_bounds__(kDtThreads, 1) k_fit_dT(DtArgs a) {
   __syncthreads();
   umma::fence_after_sync();
   const int total = a.nchunks * a.nk;
-  if (warp == 8) {
-    if (lane == 0) {
-      const unsigned char* Ah = a.A_hi + (size_t)g * AH;
-      const unsigned char* Al = a.A_lo + (size_t)g * AH;
-      umma::mbar_expect_tx(&a_full, 2 * AH);
-      for (int kc = 0; kc < a.nk; ++kc) {
-        umma::bulk_g2s(sA + kc * kABlock, Ah + (size_t)kc * kABlock, kABlock, &a_full);
-        umma::bulk_g2s(sA + AH + kc * kABlock, Al + (size_t)kc * kABlock, kABlock, &a_full);
-      }
-      const unsigned char* Bh = a.B_hi[t];
-      const unsigned char* Bl = a.B_lo[t];
-      // B blocks are ordered (N chunk, K chunk): iteration it is block it
-      auto load = [&](int it) {
-        const int s = it % kDtStages;
-        unsigned char* st = sB + s * 2 * BB;
-        umma::mbar_expect_tx(&b_full[s], 2 * BB);
-        umma::bulk_g2s(st, Bh + (size_t)it * BB, BB, &b_full[s]);
-        umma::bulk_g2s(st + BB, Bl + (size_t)it * BB, BB, &b_full[s]);
-      };
-      for (int it = 0; it < min(kDtStages, total); ++it) load(it);
-      bool ok = umma::mbar_wait(&a_full, 0, kWaitLimit);
-      umma::fence_after_sync();
-      const uint32_t idesc = umma::idesc_bf16(128, a.BN, false, false);
-      const uint32_t a0 = umma::smem_u32(sA);
-      for (int j = 0; j < a.nchunks && ok; ++j) {
-        const int buf = j & 1;
-        if (j >= 2) {
-          ok = umma::mbar_wait(&acc_empty[buf], ((j - 2) >> 1) & 1, kWaitLimit);
-          if (!ok) break;
-          umma::fence_after_sync();
-        }
-        const uint32_t d = tbase + buf * 256;
-        for (int kc = 0; kc < a.nk && ok; ++kc) {
-          const int it = j * a.nk + kc, s = it % kDtStages;
-          ok = umma::mbar_wait(&b_full[s], (it / kDtStages) & 1, kWaitLimit);
-          if (!ok) break;
-          umma::fence_after_sync();
-          const uint32_t ah = a0 + kc * kABlock, al = ah + AH;
-          const uint32_t bh = umma::smem_u32(sB + s * 2 * BB), bl = bh + BB;
-#pragma unroll
-          for (int ks = 0; ks < kFitBK / 16; ++ks) {
-            const uint32_t o = ks * 256;
-            umma::mma(d, umma::desc(ah + o, 128, kSbo), umma::desc(bh + o, 128, kSbo), idesc, (kc | ks) ? 1u : 0u);
-            umma::mma(d, umma::desc(ah + o, 128, kSbo), umma::desc(bl + o, 128, kSbo), idesc, 1u);
-            umma::mma(d, umma::desc(al + o, 128, kSbo), umma::desc(bh + o, 128, kSbo), idesc, 1u);
-          }
-          umma::commit(&b_empty[s]);
-          if (it >= 1 && it - 1 + kDtStages < total) {
-            const int sp = (it - 1) % kDtStages;
-            ok = umma::mbar_wait(&b_empty[sp], ((it - 1) / kDtStages) & 1, kWaitLimit);
-            if (ok) load(it - 1 + kDtStages);
-          }
-        }
-        umma::commit(&acc_full[buf]);
-      }
-      if (!ok) s_fail = 1;
+  const int S = a.stages;
+  if (warp == 16 && lane == 0) {  // loader: the dz0 tile once, then the W0 blocks through the ring
+    const unsigned char* Ah = a.A_hi + (size_t)g * AH;
+    const unsigned char* Al = a.A_lo + (size_t)g * AH;
+    umma::mbar_expect_tx(&a_full, 2 * AH);
+    for (int kc = 0; kc < a.nk; ++kc) {
+      umma::bulk_g2s(sA + kc * kABlock, Ah + (size_t)kc * kABlock, kABlock, &a_full);
+      umma::bulk_g2s(sA + AH + kc * kABlock, Al + (size_t)kc * kABlock, kABlock, &a_full);
     }
-  } else {
-    const int h = warp >> 2, q = warp & 3, r = q * 32 + lane;
+    const unsigned char* Bh = a.B_hi[t];
+    const unsigned char* Bl = a.B_lo[t];
+    int s = 0, round = 0;
+    for (int it = 0; it < total; ++it) {  // B blocks are ordered (N chunk, K chunk)
+      if (round > 0 && !umma::mbar_wait(&b_empty[s], (round - 1) & 1, kWaitLimit)) {
+        s_fail = 1;
+        break;
+      }
+      unsigned char* st = sB + s * 2 * BB;
+      umma::mbar_expect_tx(&b_full[s], 2 * BB);
+      umma::bulk_g2s(st, Bh + (size_t)it * BB, BB, &b_full[s]);
+      umma::bulk_g2s(st + BB, Bl + (size_t)it * BB, BB, &b_full[s]);
+      if (++s == S) {
+        s = 0;
+        ++round;
+      }
+    }
+  } else if (warp == 17 && lane == 0) {  // MMA issuer
+    bool ok = umma::mbar_wait(&a_full, 0, kWaitLimit);
+    umma::fence_after_sync();
+    const uint32_t idesc = umma::idesc_bf16(128, a.BN, false, false);
+    const uint64_t dah = umma::desc(umma::smem_u32(sA), 128, kSbo);
+    const uint64_t dal = umma::desc(umma::smem_u32(sA + AH), 128, kSbo);
+    const uint64_t db0 = umma::desc(umma::smem_u32(sB), 128, kSbo);
+    const uint64_t sstep = (2 * BB) >> 4, o_bl = BB >> 4, kstep = kABlock >> 4;
+    int s = 0, round = 0;
+    for (int j = 0; j < a.nchunks && ok; ++j) {
+      const int buf = j & 1;
+      if (j >= 2) {
+        ok = umma::mbar_wait(&acc_empty[buf], ((j - 2) >> 1) & 1, kWaitLimit);
+        if (!ok) break;
+        umma::fence_after_sync();
+      }
+      const uint32_t d = tbase + buf * 256;
+      for (int kc = 0; kc < a.nk; ++kc) {
+        ok = umma::mbar_wait(&b_full[s], round & 1, kWaitLimit);
+        if (!ok) break;
+        umma::fence_after_sync();
+        const uint64_t ah = dah + (uint64_t)kc * kstep, al = dal + (uint64_t)kc * kstep;
+        const uint64_t bh = db0 + (uint64_t)s * sstep, bl = bh + o_bl;
+#pragma unroll
+        for (int ks = 0; ks < kFitBK / 16; ++ks) {
+          const uint64_t o = (uint64_t)(ks * (256 >> 4));
+          umma::mma(d, ah + o, bh + o, idesc, (kc | ks) ? 1u : 0u);
+          umma::mma(d, ah + o, bl + o, idesc, 1u);
+          umma::mma(d, al + o, bh + o, idesc, 1u);
+        }
+        umma::commit(&b_empty[s]);
+        if (++s == S) {
+          s = 0;
+          ++round;
+        }
+      }
+      if (ok) umma::commit(&acc_full[buf]);
+    }
+    if (!ok) s_fail = 1;
+  } else if (warp < 16) {  // epilogue
+    const int k = warp >> 2, q = warp & 3, r = q * 32 + lane;
     const bool valid = r < nrows;
     const int urow = row0 + r;
     const int M1 = a.M1;
-    const float* Trow = a.T + (size_t)(valid ? a.perm_atom[urow] : 0) * 4 * M1;
-    float* dTrow = a.dT + (size_t)urow * 4 * M1;
+    const float* Tk = a.T + (size_t)(valid ? a.perm_atom[urow] : 0) * 4 * M1 + k * M1;
+    float* dTk = a.dT + (size_t)urow * 4 * M1 + k * M1;
     const uint32_t lb = (uint32_t)(q * 32) << 16;
-    float Tb[4][16], acc2[4][16];
+    float Tb[16], acc2[16];
 #pragma unroll
-    for (int k = 0; k < 4; ++k)
-#pragma unroll
-      for (int b = 0; b < 16; ++b) {
-        Tb[k][b] = valid ? Trow[k * M1 + b] : 0.f;
-        acc2[k][b] = 0.f;
-      }
-    const int NA = a.BN / 16, NAh = NA / 2;
+    for (int b = 0; b < 16; ++b) {
+      Tb[b] = valid ? Tk[b] : 0.f;
+      acc2[b] = 0.f;
+    }
+    const int NA = a.BN / 16;  // at most 16
     bool ok = true;
     for (int j = 0; j < a.nchunks; ++j) {
       const int buf = j & 1;
+      float tav[16];  // T[k][a] of the chunk's rows a, loaded before waiting for the MMA
+#pragma unroll
+      for (int i = 0; i < 16; ++i) tav[i] = (valid && i < NA) ? Tk[j * NA + i] : 0.f;
       if (ok) ok = umma::mbar_wait(&acc_full[buf], (j >> 1) & 1, kWaitLimit);
       umma::fence_after_sync();
       if (ok) {
-        for (int i = 0; i < NAh; ++i) {
-          const int ai = h * NAh + i, aa = j * NA + ai;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          if (i >= NA) break;
+          const int aa = j * NA + i;
           float dv[16];
-          umma::ld16(tbase + lb + buf * 256 + ai * 16, dv);
+          umma::ld16(tbase + lb + buf * 256 + i * 16, dv);
           umma::wait_ld();
           if (valid) {
-            float Ta[4];
+            const float ta = tav[i];
+            float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-            for (int k = 0; k < 4; ++k) Ta[k] = Trow[k * M1 + aa];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              float s = 0.f;
-#pragma unroll
-              for (int b = 0; b < 16; ++b) {
-                s = fmaf(dv[b], Tb[k][b], s);
-                acc2[k][b] = fmaf(dv[b], Ta[k], acc2[k][b]);
-              }
-              dTrow[k * M1 + aa] = s * a.inv_nnei;
+            for (int b = 0; b < 16; b += 2) {
+              s0 = fmaf(dv[b], Tb[b], s0);
+              s1 = fmaf(dv[b + 1], Tb[b + 1], s1);
+              acc2[b] = fmaf(dv[b], ta, acc2[b]);
+              acc2[b + 1] = fmaf(dv[b + 1], ta, acc2[b + 1]);
             }
-            if (a.dD) {
+            dTk[aa] = (s0 + s1) * a.inv_nnei;
+            if (a.dD && k == 0) {
               float4* dst = reinterpret_cast<float4*>(a.dD + (size_t)urow * 16 * M1 + aa * 16);
 #pragma unroll
               for (int b = 0; b < 16; b += 4) dst[b / 4] = make_float4(dv[b], dv[b + 1], dv[b + 2], dv[b + 3]);
@@ -392,21 +429,10 @@ __global__ void __launch_bounds__(kDtThreads, 1) k_fit_dT(DtArgs a) {
       umma::fence_before_sync();
       umma::mbar_arrive(&acc_empty[buf]);
     }
-    // every MMA has completed (the last acc_full), so the dz0 tile is free for the exchange
-    float* xs = reinterpret_cast<float*>(smem);
-    if (h == 1) {
+    // second term for a < 16: this thread wrote the first term itself
+    if (valid && ok) {
 #pragma unroll
-      for (int k = 0; k < 4; ++k)
-#pragma unroll
-        for (int b = 0; b < 16; ++b) xs[(k * 16 + b) * 128 + r] = acc2[k][b];
-    }
-    umma::bar_sync(1, 256);  // also orders the dT stores of both halves
-    if (h == 0 && valid && ok) {
-#pragma unroll
-      for (int k = 0; k < 4; ++k)
-#pragma unroll
-        for (int b = 0; b < 16; ++b)
-          dTrow[k * M1 + b] += (acc2[k][b] + xs[(k * 16 + b) * 128 + r]) * a.inv_nnei;
+      for (int b = 0; b < 16; ++b) dTk[b] += acc2[b] * a.inv_nnei;
     }
     if (!ok) s_fail = 1;
   }
@@ -476,7 +502,8 @@ FitTcPlan fit_tc_plan(const HostModel& m) {
     p.bnb[l] = (l == 0) ? 0 : split_bn(p.width[l - 1]);
   }
   // final backward: N chunks of whole descriptor rows (16 columns each), an
-  // even number of rows per chunk (two epilogue halves)
+  // even number of them, at most 256 columns; three W0 stages must fit beside
+  // the resident dz0 tile
   p.bn_out = 0;
   if (m.axis == 16)
     for (int bn = 256; bn >= 32; bn -= 32)
@@ -484,6 +511,9 @@ FitTcPlan fit_tc_plan(const HostModel& m) {
         p.bn_out = bn;
         break;
       }
+  if (p.L >= 1 && 2 * (size_t)(round32(p.width[0]) / kFitBK) * kABlock + 3 * 2 * (size_t)p.bn_out * kFitBK * 2 >
+                      kDtSmemMax)
+    p.bn_out = 0;
   p.ok = p.bn_out > 0;
   return p;
 }
@@ -534,14 +564,19 @@ void launch_fit_tile_D(cudaStream_t st, int nloc, int ntypes, int dim, const int
 }
 
 static void run_gemm(cudaStream_t st, GemmArgs& a, int row_tiles, int ntn) {
-  const size_t smem = (size_t)kStages * (2 * kABlock + 2 * (size_t)a.BN * kFitBK * 2);
+  // K chunks stream from L2: a deep pipeline hides its latency.  With several
+  // N tiles two CTAs share an SM (4 stages each), else one CTA takes up to 8.
+  const size_t sb = 2 * kABlock + 2 * (size_t)a.BN * kFitBK * 2;
+  a.stages = ntn > 1 ? 4 : (int)std::min<size_t>(kMaxStages, (200 * 1024) / sb);
+  a.stages = std::max(2, std::min(a.stages, a.nk));
+  const size_t smem = (size_t)a.stages * sb;
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(k_fit_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     attr = true;
   }
   count_launch();
-  k_fit_gemm<<<dim3(row_tiles, ntn), 128, smem, st>>>(a);
+  k_fit_gemm<<<dim3(row_tiles, ntn), kFitThreads, smem, st>>>(a);
 }
 
 void launch_fit_tc(cudaStream_t st, const FitTcPlan& p, int ntypes, int nloc, const int* type_start,
@@ -638,7 +673,10 @@ void launch_fit_tc(cudaStream_t st, const FitTcPlan& p, int ntypes, int nloc, co
       d.dT = dT;
       d.dD = dD;
       d.err = err;
-      const size_t smem = 2 * (size_t)d.nk * kABlock + kDtStages * 2 * (size_t)d.BN * kFitBK * 2;
+      // as many W0 stages as fit beside the resident dz0 tile: the stream is L2-latency bound
+      const size_t abytes = 2 * (size_t)d.nk * kABlock, sbytes = 2 * (size_t)d.BN * kFitBK * 2;
+      d.stages = (int)std::min<size_t>(kDtMaxStages, (kDtSmemMax - abytes) / sbytes);
+      const size_t smem = abytes + d.stages * sbytes;
       static size_t attr = 0;
       if (smem > attr) {
         cudaFuncSetAttribute(k_fit_dT, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
