@@ -336,7 +336,7 @@ def run_b200dp(args, world, rank, local):
     peak = float(pk["bf16_tflops"])
     roofline = {"kernel": "k_embed_bwd_tc" if prec == b200dp.MIXED else "k_descriptor_bwd", "bound": "tensor",
                 "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                "traffic": ncu_traffic("descriptor_bwd"),
+                "traffic": ncu_traffic("embed_bwd_tc" if prec == b200dp.MIXED else "descriptor_bwd"),
                 "peak_source": f"{pk_kind} bf16 burst (MEASURED_PEAKS.json)" if pk_kind == "measured"
                 else "fallback 1.59 PFLOP/s",
                 "flops_per_launch": fl["descriptor_bwd"], "avg_launch_ms": bwd_ms,
