@@ -31,6 +31,7 @@ EXPORTS = [
     "b200dp_compute_host", "b200dp_compute_host_nlist", "b200dp_compute_device", "b200dp_check",
     "b200dp_sel_overflow_count", "b200dp_last_nlist", "b200dp_last_descriptor", "b200dp_set_stage_timing",
     "b200dp_stage_times", "b200dp_kernel_launches", "b200dp_selftest_mma", "b200dp_build_nlist_noalloc",
+    "b200dp_direct_bind", "b200dp_direct_energy_force",
 ]
 
 
@@ -98,6 +99,10 @@ def load_library(path: str = LIB_PATH):
                                              ctypes.c_int, _ip, _vp, _vp, _vp]
     L.b200dp_kernel_launches.argtypes = []
     L.b200dp_kernel_launches.restype = ctypes.c_longlong
+    L.b200dp_direct_bind.argtypes = [_vp, _vp]
+    L.b200dp_direct_energy_force.restype = ctypes.c_int
+    L.b200dp_direct_energy_force.argtypes = [_vp, _vp, _vp, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                             _vp, _vp, _vp]
     for name in EXPORTS:
         getattr(L, name)  # every declared symbol must resolve
     _L = L
@@ -225,6 +230,19 @@ def selftest_mma(A, B, passes=3, a_mn_major=False, b_mn_major=False):
     if rc != 0:
         raise B200DPError(rc, "tcgen05 self-test failed")
     return C
+
+
+def direct_bind(engine, stream: int = 0):
+    """Binds `engine` (a DeepPot, or None) and a CUDA stream to direct_energy_force."""
+    load_library().b200dp_direct_bind(engine.h if engine is not None else None, stream or None)
+
+
+def direct_energy_force(atype_ptr, row_ptr_ptr, source_ptr, edge_vec_ptr, node_count, nloc, edge_storage,
+                        energy_ptr, force_ptr, virial_ptr) -> int:
+    """dpa_direct_energy_force on device pointers: 1 = handled, 0 = caller must fall back."""
+    return int(load_library().b200dp_direct_energy_force(atype_ptr or None, row_ptr_ptr or None, source_ptr or None,
+                                                         edge_vec_ptr or None, node_count, nloc, edge_storage,
+                                                         energy_ptr or None, force_ptr or None, virial_ptr or None))
 
 
 def kernel_launches() -> int:

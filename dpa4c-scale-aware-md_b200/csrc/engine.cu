@@ -738,6 +738,34 @@ b200dp_status Engine::compute_with_nlist(cudaStream_t st, int nloc, int nall, co
   return B200DP_OK;
 }
 
+b200dp_status Engine::compute_graph(cudaStream_t st, int n, const int64_t* d_atype64, const int64_t* d_row_ptr,
+                                    const uint32_t* d_source, const float* d_edge_vec, double* d_atom_energy,
+                                    double* d_force, double* d_atom_virial) {
+  g_err_sink = &err;
+  B200DP_CUDA_TRY(cudaSetDevice(opt.device));
+  last_stream = st;
+  last_nloc = n;
+  last_nall = n;
+  b200dp_status rc = ensure_buffers(n, n, 1, 0);
+  if (rc != B200DP_OK) return rc;
+  B200DP_CUDA_TRY(graph_atype.ensure(sizeof(int) * std::max(n, 1)));
+  mark(st, 0);
+  int* err_d = err_buf.as<int>();
+  B200DP_CUDA_TRY(cudaMemsetAsync(err_d, 0, sizeof(int) * kErrCount, st));
+  launch_format_graph(st, format_spec(n, n), d_atype64, d_row_ptr, d_source, d_edge_vec, graph_atype.as<int>(),
+                      nl_j.as<int>(), nl_code.as<int>(), nl_rij.as<double>(), nl_cnt.as<int>(), err_d);
+  B200DP_CUDA_TRY(cudaGetLastError());
+  double* d_scal = scalars.as<double>();
+  rc = (opt.precision == B200DP_FP64)
+           ? run_model<double>(st, n, n, graph_atype.as<int>(), d_force, d_atom_energy, d_atom_virial, d_scal,
+                               d_scal + 1)
+           : run_model<float>(st, n, n, graph_atype.as<int>(), d_force, d_atom_energy, d_atom_virial, d_scal,
+                              d_scal + 1);
+  if (rc != B200DP_OK) return rc;
+  B200DP_CUDA_TRY(cudaGetLastError());
+  return B200DP_OK;
+}
+
 }  // namespace b200dp
 
 // ============================================================== C ABI
@@ -883,6 +911,30 @@ b200dp_status b200dp_last_descriptor(b200dp_engine* engine, double* descriptor, 
 }
 
 long long b200dp_kernel_launches(void) { return b200dp::launch_count(); }
+
+// Engine and stream used by b200dp_direct_energy_force (process-wide, like the
+// reference's primed direct-engine cache).
+static std::atomic<b200dp_engine*> g_direct_engine{nullptr};
+static std::atomic<void*> g_direct_stream{nullptr};
+
+b200dp_status b200dp_direct_bind(b200dp_engine* engine, void* stream) {
+  g_direct_engine.store(engine);
+  g_direct_stream.store(stream);
+  return B200DP_OK;
+}
+
+int b200dp_direct_energy_force(const int64_t* atype, const int64_t* row_ptr, const uint32_t* source,
+                               const float* edge_vec, int64_t node_count, int64_t nloc, int64_t edge_storage,
+                               double* energy_out, double* force_out, double* virial_out) {
+  b200dp_engine* eng = g_direct_engine.load();
+  if (!eng || nloc != node_count || node_count <= 0 || node_count > INT32_MAX || edge_storage < 0) return 0;
+  if (!atype || !row_ptr || !energy_out || !force_out || !virial_out || (edge_storage > 0 && (!source || !edge_vec)))
+    return 0;
+  const b200dp_status rc =
+      eng->e.compute_graph(static_cast<cudaStream_t>(g_direct_stream.load()), (int)node_count, atype, row_ptr, source,
+                           edge_vec, energy_out, force_out, virial_out);
+  return rc == B200DP_OK ? 1 : 0;
+}
 
 b200dp_status b200dp_set_stage_timing(b200dp_engine* engine, int enable) {
   if (!engine) return B200DP_ERR_INVALID;

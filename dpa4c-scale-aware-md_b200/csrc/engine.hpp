@@ -53,6 +53,7 @@ struct Engine {
   DevBuf cand_start, cand_list, ilist_d;
   // tensor-core embedding path (mixed mode)
   bool use_tc = false;
+  DevBuf graph_atype;
   DevBuf tc_nets, ecount, eoff, tstart, rec_rt, rec_row, rec_slot, partial, scan_scratch, dTbuf;
   // tensor-core fitting (mixed mode)
   bool use_fit_tc = false;
@@ -94,6 +95,10 @@ struct Engine {
   b200dp_status compute_device(cudaStream_t st, int nloc, int nghost, const double* d_coord, const int* d_atype,
                                const double* box, const double* region, double* d_energy, double* d_force,
                                double* d_virial, double* d_atom_energy, double* d_atom_virial);
+  // Canonical destination-major graph (n nodes, all local), device pointers.
+  b200dp_status compute_graph(cudaStream_t st, int n, const int64_t* d_atype64, const int64_t* d_row_ptr,
+                              const uint32_t* d_source, const float* d_edge_vec, double* d_atom_energy,
+                              double* d_force, double* d_atom_virial);
   b200dp_status compute_with_nlist(cudaStream_t st, int nloc, int nall, const double* d_coord, const int* d_atype,
                                    const b200dp_nlist* nl, double* d_energy, double* d_force, double* d_virial,
                                    double* d_atom_energy, double* d_atom_virial);

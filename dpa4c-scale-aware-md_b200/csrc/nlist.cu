@@ -499,6 +499,83 @@ __global__ void __launch_bounds__(kFmtWarps * 32)
   emit_row(f, i, b, ncand, lane, nl_j, nl_code, nl_rij, nl_cnt, err);
 }
 
+// Canonical destination-major graph (the reference's direct-engine input):
+// node i's edges are [row_ptr[i], row_ptr[i+1]), each with a source node j and
+// the fp32 vector x_j - x_i.  Every edge is a candidate; periodic images are
+// separate edges of the same source, told apart by their position in the
+// row (the tie-break key in place of the image code).  Also writes the int32
+// type of every node.
+__global__ void __launch_bounds__(kFmtWarps * 32)
+    k_format_graph(FormatSpec f, const int64_t* __restrict__ atype64, const int64_t* __restrict__ row_ptr,
+                   const uint32_t* __restrict__ source, const float* __restrict__ edge_vec, int* __restrict__ atype32,
+                   int* __restrict__ nl_j, int* __restrict__ nl_code, double* __restrict__ nl_rij,
+                   int* __restrict__ nl_cnt, int* __restrict__ err) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int i = blockIdx.x * kFmtWarps + warp;
+  if (i >= f.nloc) return;
+  if (lane == 0) {
+    const int64_t ti = atype64[i];
+    atype32[i] = (ti >= 0 && ti < f.ntypes) ? (int)ti : -1;
+    if (ti < 0 || ti >= f.ntypes) atomicAdd(err + kErrBadType, 1);
+  }
+  CandBuf b = cand_buf(smem, warp, f.cap);
+  const unsigned lt_mask = (1u << lane) - 1u;
+  const int64_t beg = row_ptr[i], end = row_ptr[i + 1];
+  int ncand = 0;
+  for (int64_t k = beg + lane; k - lane < end; k += 32) {
+    bool valid = false;
+    int j = -1, tj = 0;
+    double r[3] = {0, 0, 0}, r2 = 0;
+    if (k < end) {
+      const uint32_t src = source[k];
+      if (src < (uint32_t)f.nall) {
+        j = (int)src;
+#pragma unroll
+        for (int c = 0; c < 3; ++c) r[c] = (double)edge_vec[3 * k + c];
+        r2 = dadd(dadd(dmul(r[0], r[0]), dmul(r[1], r[1])), dmul(r[2], r[2]));
+        const int64_t t64 = atype64[j];
+        const bool type_ok = (t64 >= 0 && t64 < f.ntypes);
+        tj = type_ok ? (int)t64 : 0;
+        if (!type_ok && r2 < f.rc2) atomicAdd(err + kErrBadType, 1);
+        valid = type_ok && r2 > 0.0 && r2 < f.rc2;
+      }
+    }
+    const unsigned m = __ballot_sync(0xffffffffu, valid);
+    const int pos = ncand + __popc(m & lt_mask);
+    if (valid && pos < f.cap) {
+      b.r2[pos] = r2;
+      b.r[3 * pos] = r[0];
+      b.r[3 * pos + 1] = r[1];
+      b.r[3 * pos + 2] = r[2];
+      b.j[pos] = j;
+      b.code[pos] = (int)(k - beg);
+      b.t[pos] = tj;
+    }
+    ncand += __popc(m);
+  }
+  if (ncand > f.cap) {
+    if (lane == 0) atomicAdd(err + kErrCandCapacity, 1);
+    ncand = f.cap;
+  }
+  __syncwarp();
+  emit_row(f, i, b, ncand, lane, nl_j, nl_code, nl_rij, nl_cnt, err);
+}
+
+void launch_format_graph(cudaStream_t st, const FormatSpec& f, const int64_t* atype64, const int64_t* row_ptr,
+                         const uint32_t* source, const float* edge_vec, int* atype32, int* nl_j, int* nl_code,
+                         double* nl_rij, int* nl_cnt, int* err) {
+  if (f.nloc <= 0) return;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(k_format_graph, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    attr_set = true;
+  }
+  count_launch();
+  k_format_graph<<<(f.nloc + kFmtWarps - 1) / kFmtWarps, kFmtWarps * 32, format_smem_bytes(f.cap), st>>>(
+      f, atype64, row_ptr, source, edge_vec, atype32, nl_j, nl_code, nl_rij, nl_cnt, err);
+}
+
 void launch_format_candidates(cudaStream_t st, const FormatSpec& f, const double* coord, const int* atype,
                               const int* ilist, const int* cand_start, const int* cand, int* nl_j, int* nl_code,
                               double* nl_rij, int* nl_cnt, int* err) {

@@ -51,6 +51,11 @@ void launch_format(cudaStream_t st, const FormatSpec& f, const GridSpec& g, cons
                    const int* cell_of, const int* cell_start, const int* cell_atoms, int* nl_j, int* nl_code,
                    double* nl_rij, int* nl_cnt, int* err);
 // Formats a caller-provided candidate list (LAMMPS full list in CSR form).
+// Formats a canonical destination-major edge graph (fp32 edge vectors) and
+// converts the int64 node types to int32 (invalid types become -1).
+void launch_format_graph(cudaStream_t st, const FormatSpec& f, const int64_t* atype64, const int64_t* row_ptr,
+                         const uint32_t* source, const float* edge_vec, int* atype32, int* nl_j, int* nl_code,
+                         double* nl_rij, int* nl_cnt, int* err);
 void launch_format_candidates(cudaStream_t st, const FormatSpec& f, const double* coord, const int* atype,
                               const int* ilist, const int* cand_start, const int* cand, int* nl_j, int* nl_code,
                               double* nl_rij, int* nl_cnt, int* err);

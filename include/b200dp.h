@@ -183,6 +183,31 @@ b200dp_status b200dp_selftest_mma(int K, int N, int a_mn_major, int b_mn_major, 
 b200dp_status b200dp_build_nlist_noalloc(void* stream, int nlocal, int nghost, const double* d_coord,
                                          const int* d_atype, const double* box, const double* region, double rcut,
                                          int ntypes, const int* sel, int* d_nlist, int* d_image, double* d_rij);
+/* Engine and CUDA stream used by b200dp_direct_energy_force (process-wide;
+ * the reference's counterpart is the direct-engine cache primed at model load,
+ * components/deepmd-op/overlays/op/pt/dpa4c/graph_compress.cu:1451-1476).
+ * NULL engine unbinds. */
+b200dp_status b200dp_direct_bind(b200dp_engine* engine, void* stream);
+
+/* Replaces extern "C" dpa_direct_energy_force
+ * (components/deepmd-op/overlays/op/pt/dpa4c/graph_compress.cu:1817-1902),
+ * called from DeepPotPTExpt::compute_canonical_graph_gpu
+ * (components/deepmd-op/overlays/api_cc/src/DeepPotPTExpt.cc:2893-2907).
+ * Device pointers, canonical destination-major graph of node_count nodes:
+ * atype [node_count] int64; row_ptr [node_count + 1] int64, node i's edges are
+ * [row_ptr[i], row_ptr[i+1]); source [edge_storage] uint32 neighbour node;
+ * edge_vec [edge_storage][3] fp32, x_source - x_node in Angstrom (periodic
+ * images are separate edges).  Outputs are overwritten: energy_out
+ * [nloc] per-atom energies, force_out [node_count][3], virial_out
+ * [node_count][9] per-atom virials (fp64).  Runs on the bound stream without
+ * synchronising; device-side errors are reported by b200dp_check.  Returns 1
+ * when handled, 0 when the caller must run its fallback: no engine bound,
+ * nloc != node_count (ghost nodes), node_count <= 0, a null pointer, or a
+ * launch failure (message in b200dp_last_error of the bound engine). */
+int b200dp_direct_energy_force(const int64_t* atype, const int64_t* row_ptr, const uint32_t* source,
+                               const float* edge_vec, int64_t node_count, int64_t nloc, int64_t edge_storage,
+                               double* energy_out, double* force_out, double* virial_out);
+
 /* Total kernels this library has launched in the process (all engines). */
 long long b200dp_kernel_launches(void);
 b200dp_status b200dp_stage_times(b200dp_engine* engine, float* ms5);
