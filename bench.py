@@ -363,6 +363,26 @@ def run_b200dp(args, world, rank, local):
                 "stage_ms": [round(float(q), 4) for q in np.array(st64).mean(0)]}
         del w64
         dp64.close()
+    # MD loop (N = 1): the same force call inside the device MD driver (NVT Nose-Hoover chain,
+    # velocity Verlet), reported beside the force-call metric
+    md_loop = None
+    if world == 1 and prec == b200dp.MIXED:
+        try:
+            md = b200dp.MD(dp, system.coord, system.atype, system.box, [15.9994, 1.00794], dt=0.0005,
+                           ensemble=b200dp.NVT, t_init=300.0, t_target=300.0, t_damp=0.05, seed=1)
+            md.run(max(3, args.warmup))
+            md.thermo()
+            k_md = max(10, args.steps)
+            t0 = time.perf_counter()
+            md.run(k_md)
+            th = md.thermo()
+            dt_md = time.perf_counter() - t0
+            md_loop = {"ms_per_step": 1e3 * dt_md / k_md, "value": n * k_md / dt_md, "unit": "atom-steps/s",
+                       "steps": k_md, "ensemble": "NVT (Nose-Hoover chain 3, 300 K, dt 0.5 fs)",
+                       "temperature_K": th["temp"], "timing": "host wall clock around the enqueued steps + sync"}
+            md.close()
+        except Exception as ex:  # report, never hide
+            md_loop = {"error": repr(ex)}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, used, dt = cpu_oracle_rate(mp, system)
@@ -388,6 +408,7 @@ def run_b200dp(args, world, rank, local):
             "roofline": roofline,
             "e2e": e2e,
             "fp64": fp64,
+            "md_loop": md_loop,
             "cpu_baseline": cpu,
             "clocks": clocks,
             "flops_per_step": fl["total"],

@@ -31,8 +31,17 @@ EXPORTS = [
     "b200dp_compute_host", "b200dp_compute_host_nlist", "b200dp_compute_device", "b200dp_check",
     "b200dp_sel_overflow_count", "b200dp_last_nlist", "b200dp_last_descriptor", "b200dp_set_stage_timing",
     "b200dp_stage_times", "b200dp_kernel_launches", "b200dp_selftest_mma", "b200dp_build_nlist_noalloc",
-    "b200dp_direct_bind", "b200dp_direct_energy_force",
+    "b200dp_direct_bind", "b200dp_direct_energy_force", "b200dp_md_params_default", "b200dp_md_create",
+    "b200dp_md_run", "b200dp_md_thermo", "b200dp_md_state", "b200dp_md_destroy",
 ]
+
+NVE, NVT = 0, 1
+
+
+class MDParams(ctypes.Structure):
+    _fields_ = [("dt", ctypes.c_double), ("ensemble", ctypes.c_int), ("chain", ctypes.c_int),
+                ("t_target", ctypes.c_double), ("t_damp", ctypes.c_double), ("t_init", ctypes.c_double),
+                ("seed", ctypes.c_ulonglong), ("mass", ctypes.c_double * 8), ("reserved", ctypes.c_int * 16)]
 
 
 class B200DPError(RuntimeError):
@@ -100,6 +109,11 @@ def load_library(path: str = LIB_PATH):
     L.b200dp_kernel_launches.argtypes = []
     L.b200dp_kernel_launches.restype = ctypes.c_longlong
     L.b200dp_direct_bind.argtypes = [_vp, _vp]
+    L.b200dp_md_create.argtypes = [_vp, ctypes.c_int, _dp, _dp, _ip, _dp, ctypes.c_void_p, ctypes.POINTER(_vp)]
+    L.b200dp_md_run.argtypes = [_vp, ctypes.c_int]
+    L.b200dp_md_thermo.argtypes = [_vp, _dp]
+    L.b200dp_md_state.argtypes = [_vp, _dp, _dp, _dp]
+    L.b200dp_md_destroy.argtypes = [_vp]
     L.b200dp_direct_energy_force.restype = ctypes.c_int
     L.b200dp_direct_energy_force.argtypes = [_vp, _vp, _vp, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                              _vp, _vp, _vp]
@@ -230,6 +244,65 @@ def selftest_mma(A, B, passes=3, a_mn_major=False, b_mn_major=False):
     if rc != 0:
         raise B200DPError(rc, "tcgen05 self-test failed")
     return C
+
+
+class MD:
+    """Device-resident MD driver (velocity Verlet, optional Nose-Hoover chain) around a DeepPot engine."""
+
+    THERMO = ("step", "pe", "ke", "temp", "conserved", "press", "volume", "e_thermostat")
+
+    def __init__(self, dp: DeepPot, coord, atype, box, masses, dt=0.0005, ensemble=NVE, vel=None, t_init=0.0,
+                 t_target=300.0, t_damp=0.05, chain=3, seed=0):
+        L = load_library()
+        p = MDParams()
+        L.b200dp_md_params_default(ctypes.byref(p))
+        p.dt, p.ensemble, p.chain = dt, ensemble, chain
+        p.t_target, p.t_damp, p.t_init, p.seed = t_target, t_damp, t_init, seed
+        for t, m in enumerate(masses):
+            p.mass[t] = m
+        coord = np.ascontiguousarray(coord, dtype=np.float64).reshape(-1, 3)
+        atype = np.ascontiguousarray(atype, dtype=np.int32)
+        box = np.ascontiguousarray(box, dtype=np.float64).reshape(9)
+        v = None if vel is None else np.ascontiguousarray(vel, dtype=np.float64).reshape(-1, 3)
+        self.n = coord.shape[0]
+        self.L = L
+        self.dp = dp
+        h = _vp()
+        rc = L.b200dp_md_create(dp.h, self.n, _p(coord, _dp), _p(v, _dp), _p(atype, _ip), _p(box, _dp),
+                                ctypes.byref(p), ctypes.byref(h))
+        if rc != 0:
+            raise B200DPError(rc, dp.L.b200dp_last_error(dp.h).decode())
+        self.h = h
+
+    def run(self, nsteps: int):
+        rc = self.L.b200dp_md_run(self.h, int(nsteps))
+        if rc != 0:
+            raise B200DPError(rc, self.dp.L.b200dp_last_error(self.dp.h).decode())
+
+    def thermo(self) -> dict:
+        t = np.zeros(8)
+        rc = self.L.b200dp_md_thermo(self.h, _p(t, _dp))
+        if rc != 0:
+            raise B200DPError(rc, self.dp.L.b200dp_last_error(self.dp.h).decode())
+        return dict(zip(self.THERMO, t))
+
+    def state(self):
+        x, v, f = (np.zeros((self.n, 3)) for _ in range(3))
+        rc = self.L.b200dp_md_state(self.h, _p(x, _dp), _p(v, _dp), _p(f, _dp))
+        if rc != 0:
+            raise B200DPError(rc, self.dp.L.b200dp_last_error(self.dp.h).decode())
+        return x, v, f
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.L.b200dp_md_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def direct_bind(engine, stream: int = 0):

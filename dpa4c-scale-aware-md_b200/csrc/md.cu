@@ -1,0 +1,423 @@
+// Molecular-dynamics driver around the force engine: velocity Verlet with an
+// optional Nose-Hoover chain thermostat (NVT), state resident on the device.
+//
+// Semantics follow LAMMPS `fix nve` / `fix nvt` in metal units (the reference
+// drives its force call from LAMMPS' Kokkos Verlet with `fix nh`,
+// components/lammps/overlays/src/KOKKOS/fix_nh_kokkos.cpp:863-1001, and keeps
+// the chain recurrence on the device,
+// components/lammps/overlays/src/KOKKOS/dpa_fast_step_kokkos.h:307-400):
+//   initial half: [NVT] chain update from the current temperature, v *= s;
+//                 v += dt/2 F/m; x += dt v
+//   force call (b200dp_compute_device, periodic box)
+//   final half:   v += dt/2 F/m; temperature; [NVT] chain update, v *= s
+// The chain follows the Martyna-Tuckerman-Klein integration of LAMMPS' FixNH
+// (one Suzuki-Yoshida stage, chain length M, masses Q0 = dof kB T0 / w^2,
+// Qi = kB T0 / w^2 with w = 1 / t_damp).  Every step is enqueued on one stream
+// with no host synchronisation; reductions use a fixed grid and order, so a
+// trajectory is bitwise reproducible.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/b200dp.h"
+#include "common.cuh"
+
+namespace b200dp {
+namespace {
+
+constexpr double kMvv2e = 1.0364269e-4;  // (g/mol) (A/ps)^2 -> eV
+constexpr double kFtm2v = 1.0 / 1.0364269e-4;
+constexpr double kBoltz = 8.617343e-5;  // eV / K
+constexpr double kNktv2p = 1.6021765e6;  // eV / A^3 -> bar
+constexpr int kMaxChain = 8;
+constexpr int kRedBlocks = 148;
+constexpr int kMdThreads = 256;
+
+struct Chain {
+  double eta[kMaxChain], eta_dot[kMaxChain + 1], eta_dotdot[kMaxChain];
+  double t_current, factor;
+};
+
+struct ChainParams {
+  int M;
+  double dof_boltz, ke_target, boltz_t, dt4, dt8, dthalf;
+  double mass[kMaxChain];
+};
+
+// v = v * s + dtf F / m ; x += dt v   (s = chain factor, 1 without a thermostat)
+__global__ void k_md_first(int n, double* __restrict__ x, double* __restrict__ v, const double* __restrict__ f,
+                           const double* __restrict__ minv, const Chain* __restrict__ ch, double dtf, double dt) {
+  const double s = ch ? ch->factor : 1.0;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const double w = dtf * minv[i];
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+      const double vv = v[3 * i + c] * s + w * f[3 * i + c];
+      v[3 * i + c] = vv;
+      x[3 * i + c] += dt * vv;
+    }
+  }
+}
+
+// v += dtf F / m, and per-block partial sums of m v^2 (fixed grid, fixed order)
+__global__ void __launch_bounds__(kMdThreads) k_md_second(int n, double* __restrict__ v, const double* __restrict__ f,
+                                                          const double* __restrict__ minv,
+                                                          const double* __restrict__ mass, double dtf,
+                                                          double* __restrict__ part) {
+  __shared__ double sh[kMdThreads / 32];
+  double acc = 0.0;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const double w = dtf * minv[i];
+    double s2 = 0.0;
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+      const double vv = v[3 * i + c] + w * f[3 * i + c];
+      v[3 * i + c] = vv;
+      s2 += vv * vv;
+    }
+    acc += mass[i] * s2;
+  }
+  acc = warp_sum(acc);
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double b = 0.0;
+    for (int w = 0; w < kMdThreads / 32; ++w) b += sh[w];
+    part[blockIdx.x] = b;
+  }
+}
+
+// sum of the partials in a fixed order (one warp)
+__device__ double sum_parts(const double* part, int nparts) {
+  const int lane = threadIdx.x & 31;
+  double a = 0.0;
+  for (int k = lane; k < nparts; k += 32) a += part[k];
+  return warp_sum(a);
+}
+
+// One half-step of the chain (LAMMPS FixNH::nhc_temp_integrate with one
+// Suzuki-Yoshida stage).  With `part` the current temperature comes from the
+// kinetic-energy partials, else from the state.  Writes the velocity factor.
+__global__ void k_md_chain(ChainParams p, Chain* __restrict__ st, const double* __restrict__ part, int nparts,
+                           double* __restrict__ ke_out) {
+  double mv2 = 0.0;
+  if (part) mv2 = sum_parts(part, nparts);
+  if (threadIdx.x != 0) return;
+  double t_current = part ? mv2 * kMvv2e / p.dof_boltz : st->t_current;
+  if (ke_out && part) *ke_out = 0.5 * mv2 * kMvv2e;
+  const int M = p.M;
+  double eta_dot[kMaxChain + 1], eta_dotdot[kMaxChain];
+  for (int i = 0; i <= M; ++i) eta_dot[i] = st->eta_dot[i];
+  for (int i = 0; i < M; ++i) eta_dotdot[i] = st->eta_dotdot[i];
+  double ke = p.dof_boltz * t_current;
+  eta_dotdot[0] = (ke - p.ke_target) / p.mass[0];
+  double expfac = 1.0;
+  for (int i = M - 1; i > 0; --i) {
+    expfac = exp(-p.dt8 * eta_dot[i + 1]);
+    eta_dot[i] = (eta_dot[i] * expfac + eta_dotdot[i] * p.dt4) * expfac;
+  }
+  expfac = exp(-p.dt8 * eta_dot[1]);
+  eta_dot[0] = (eta_dot[0] * expfac + eta_dotdot[0] * p.dt4) * expfac;
+  const double factor = exp(-p.dthalf * eta_dot[0]);
+  t_current *= factor * factor;
+  ke = p.dof_boltz * t_current;
+  eta_dotdot[0] = (ke - p.ke_target) / p.mass[0];
+  for (int i = 0; i < M; ++i) st->eta[i] += p.dthalf * eta_dot[i];
+  eta_dot[0] = (eta_dot[0] * expfac + eta_dotdot[0] * p.dt4) * expfac;
+  for (int i = 1; i < M; ++i) {
+    expfac = exp(-p.dt8 * eta_dot[i + 1]);
+    eta_dotdot[i] = (p.mass[i - 1] * eta_dot[i - 1] * eta_dot[i - 1] - p.boltz_t) / p.mass[i];
+    eta_dot[i] = (eta_dot[i] * expfac + eta_dotdot[i] * p.dt4) * expfac;
+  }
+  for (int i = 0; i <= M; ++i) st->eta_dot[i] = eta_dot[i];
+  for (int i = 0; i < M; ++i) st->eta_dotdot[i] = eta_dotdot[i];
+  st->t_current = t_current;
+  st->factor = factor;
+}
+
+__global__ void k_md_scale(int n, double* __restrict__ v, const Chain* __restrict__ ch) {
+  const double s = ch->factor;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < 3 * n; i += gridDim.x * blockDim.x) v[i] *= s;
+}
+
+// kinetic-energy partials only (thermo after creation)
+__global__ void __launch_bounds__(kMdThreads) k_md_ke(int n, const double* __restrict__ v,
+                                                      const double* __restrict__ mass, double* __restrict__ part) {
+  __shared__ double sh[kMdThreads / 32];
+  double acc = 0.0;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    acc += mass[i] * (v[3 * i] * v[3 * i] + v[3 * i + 1] * v[3 * i + 1] + v[3 * i + 2] * v[3 * i + 2]);
+  acc = warp_sum(acc);
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double b = 0.0;
+    for (int w = 0; w < kMdThreads / 32; ++w) b += sh[w];
+    part[blockIdx.x] = b;
+  }
+}
+
+template <class T>
+struct Dev {
+  T* p = nullptr;
+  cudaError_t alloc(size_t n) { return cudaMalloc(&p, sizeof(T) * std::max<size_t>(n, 1)); }
+  ~Dev() {
+    if (p) cudaFree(p);
+  }
+};
+
+// splitmix64 + Box-Muller: seeded Gaussian draws for the initial velocities
+struct Rng {
+  uint64_t s;
+  uint64_t next() {
+    uint64_t z = (s += 0x9E3779B97F4A7C15ull);
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+  }
+  double uniform() { return ((next() >> 11) + 0.5) * (1.0 / 9007199254740992.0); }
+  double gauss() { return std::sqrt(-2.0 * std::log(uniform())) * std::cos(6.283185307179586 * uniform()); }
+};
+
+}  // namespace
+}  // namespace b200dp
+
+using namespace b200dp;
+
+struct b200dp_md {
+  b200dp_engine* engine = nullptr;
+  b200dp_md_params p{};
+  int n = 0, ensemble = 0;
+  double box[9] = {0}, volume = 0, dof = 0;
+  long long step = 0;
+  cudaStream_t stream = nullptr;
+  Dev<double> x, v, f, minv, mass, e, vir, part, ke;
+  Dev<int> atype;
+  Dev<Chain> chain;
+  ChainParams cp{};
+  std::string err;
+};
+
+extern "C" {
+
+b200dp_status b200dp_md_params_default(b200dp_md_params* p) {
+  if (!p) return B200DP_ERR_INVALID;
+  std::memset(p, 0, sizeof(*p));
+  p->dt = 0.0005;  // 0.5 fs
+  p->ensemble = B200DP_MD_NVE;
+  p->chain = 3;
+  p->t_target = 300.0;
+  p->t_damp = 0.05;  // 100 steps of 0.5 fs
+  return B200DP_OK;
+}
+
+b200dp_status b200dp_md_create(b200dp_engine* engine, int natoms, const double* coord, const double* vel,
+                               const int* atype, const double* box, const b200dp_md_params* params,
+                               b200dp_md** out) {
+  if (!engine || !out || natoms <= 0 || !coord || !atype || !box || !params) return B200DP_ERR_INVALID;
+  const b200dp_md_params& p = *params;
+  if (!(p.dt > 0) || (p.ensemble != B200DP_MD_NVE && p.ensemble != B200DP_MD_NVT)) return B200DP_ERR_INVALID;
+  if (p.ensemble == B200DP_MD_NVT && (p.chain < 1 || p.chain > kMaxChain || !(p.t_target > 0) || !(p.t_damp > 0)))
+    return B200DP_ERR_INVALID;
+  if (!vel && !(p.t_init > 0)) return B200DP_ERR_INVALID;
+  b200dp_model_info info;
+  if (b200dp_model_info_get(engine, &info) != B200DP_OK) return B200DP_ERR_INVALID;
+  std::vector<double> mass(natoms), minv(natoms);
+  for (int i = 0; i < natoms; ++i) {
+    if (atype[i] < 0 || atype[i] >= info.ntypes || atype[i] >= 8 || !(p.mass[atype[i]] > 0)) return B200DP_ERR_BAD_TYPE;
+    mass[i] = p.mass[atype[i]];
+    minv[i] = 1.0 / mass[i];
+  }
+  auto* md = new b200dp_md();
+  md->engine = engine;
+  md->p = p;
+  md->n = natoms;
+  md->ensemble = p.ensemble;
+  std::memcpy(md->box, box, sizeof(md->box));
+  md->volume = std::fabs(box[0] * (box[4] * box[8] - box[5] * box[7]) - box[1] * (box[3] * box[8] - box[5] * box[6]) +
+                         box[2] * (box[3] * box[7] - box[4] * box[6]));
+  md->dof = 3.0 * natoms - 3.0;  // centre-of-mass motion removed, as LAMMPS' default temperature compute
+  // velocities: given, or seeded Gaussian at t_init with zero total momentum, scaled to t_init exactly
+  std::vector<double> v(3 * (size_t)natoms);
+  if (vel) {
+    std::copy(vel, vel + 3 * (size_t)natoms, v.begin());
+  } else {
+    Rng rng{p.seed ? p.seed : 0x5EEDull};
+    double pc[3] = {0, 0, 0}, mt = 0;
+    for (int i = 0; i < natoms; ++i) {
+      const double sd = std::sqrt(kBoltz * p.t_init / (mass[i] * kMvv2e));
+      for (int c = 0; c < 3; ++c) {
+        v[3 * i + c] = sd * rng.gauss();
+        pc[c] += mass[i] * v[3 * i + c];
+      }
+      mt += mass[i];
+    }
+    double mv2 = 0;
+    for (int i = 0; i < natoms; ++i)
+      for (int c = 0; c < 3; ++c) {
+        v[3 * i + c] -= pc[c] / mt;
+        mv2 += mass[i] * v[3 * i + c] * v[3 * i + c];
+      }
+    const double t_now = mv2 * kMvv2e / (md->dof * kBoltz);
+    const double s = t_now > 0 ? std::sqrt(p.t_init / t_now) : 0.0;
+    for (double& x : v) x *= s;
+  }
+  double mv2 = 0;
+  for (int i = 0; i < natoms; ++i)
+    for (int c = 0; c < 3; ++c) mv2 += mass[i] * v[3 * i + c] * v[3 * i + c];
+  // chain parameters and state
+  ChainParams& cp = md->cp;
+  Chain ch;
+  std::memset(&ch, 0, sizeof(ch));
+  ch.factor = 1.0;
+  ch.t_current = mv2 * kMvv2e / (md->dof * kBoltz);
+  if (p.ensemble == B200DP_MD_NVT) {
+    const double w = 1.0 / p.t_damp;
+    cp.M = p.chain;
+    cp.dof_boltz = md->dof * kBoltz;
+    cp.ke_target = md->dof * kBoltz * p.t_target;
+    cp.boltz_t = kBoltz * p.t_target;
+    cp.dt4 = 0.25 * p.dt;
+    cp.dt8 = 0.125 * p.dt;
+    cp.dthalf = 0.5 * p.dt;
+    cp.mass[0] = cp.ke_target / (w * w);
+    for (int i = 1; i < cp.M; ++i) cp.mass[i] = cp.boltz_t / (w * w);
+    for (int i = 1; i < cp.M; ++i)
+      ch.eta_dotdot[i] = (cp.mass[i - 1] * ch.eta_dot[i - 1] * ch.eta_dot[i - 1] - cp.boltz_t) / cp.mass[i];
+  }
+  const size_t n3 = 3 * (size_t)natoms;
+  cudaError_t ce = cudaSuccess;
+  auto chk = [&](cudaError_t e) {
+    if (ce == cudaSuccess) ce = e;
+  };
+  chk(cudaStreamCreateWithFlags(&md->stream, cudaStreamNonBlocking));
+  chk(md->x.alloc(n3));
+  chk(md->v.alloc(n3));
+  chk(md->f.alloc(n3));
+  chk(md->minv.alloc(natoms));
+  chk(md->mass.alloc(natoms));
+  chk(md->e.alloc(1));
+  chk(md->vir.alloc(9));
+  chk(md->part.alloc(kRedBlocks));
+  chk(md->ke.alloc(1));
+  chk(md->atype.alloc(natoms));
+  chk(md->chain.alloc(1));
+  if (ce == cudaSuccess) {
+    chk(cudaMemcpy(md->x.p, coord, sizeof(double) * n3, cudaMemcpyHostToDevice));
+    chk(cudaMemcpy(md->v.p, v.data(), sizeof(double) * n3, cudaMemcpyHostToDevice));
+    chk(cudaMemcpy(md->minv.p, minv.data(), sizeof(double) * natoms, cudaMemcpyHostToDevice));
+    chk(cudaMemcpy(md->mass.p, mass.data(), sizeof(double) * natoms, cudaMemcpyHostToDevice));
+    chk(cudaMemcpy(md->atype.p, atype, sizeof(int) * natoms, cudaMemcpyHostToDevice));
+    chk(cudaMemcpy(md->chain.p, &ch, sizeof(ch), cudaMemcpyHostToDevice));
+  }
+  if (ce != cudaSuccess) {
+    if (md->stream) cudaStreamDestroy(md->stream);
+    delete md;
+    return B200DP_ERR_CUDA;
+  }
+  // forces of the initial configuration
+  const b200dp_status rc = b200dp_compute_device(engine, md->stream, natoms, 0, md->x.p, md->atype.p, md->box, nullptr,
+                                                 md->e.p, md->f.p, md->vir.p, nullptr, nullptr);
+  if (rc != B200DP_OK) {
+    cudaStreamDestroy(md->stream);
+    delete md;
+    return rc;
+  }
+  count_launch();
+  k_md_ke<<<kRedBlocks, kMdThreads, 0, md->stream>>>(natoms, md->v.p, md->mass.p, md->part.p);
+  *out = md;
+  return cudaGetLastError() == cudaSuccess ? B200DP_OK : B200DP_ERR_CUDA;
+}
+
+b200dp_status b200dp_md_run(b200dp_md* md, int nsteps) {
+  if (!md || nsteps < 0) return B200DP_ERR_INVALID;
+  const int n = md->n;
+  const double dtf = 0.5 * md->p.dt * kFtm2v, dt = md->p.dt;
+  const int grid = std::min(kRedBlocks * 4, (n + kMdThreads - 1) / kMdThreads);
+  const bool nvt = md->ensemble == B200DP_MD_NVT;
+  cudaStream_t st = md->stream;
+  for (int s = 0; s < nsteps; ++s) {
+    if (nvt) {
+      count_launch();
+      k_md_chain<<<1, 32, 0, st>>>(md->cp, md->chain.p, nullptr, 0, nullptr);
+    }
+    count_launch();
+    k_md_first<<<grid, kMdThreads, 0, st>>>(n, md->x.p, md->v.p, md->f.p, md->minv.p, nvt ? md->chain.p : nullptr,
+                                            dtf, dt);
+    const b200dp_status rc = b200dp_compute_device(md->engine, st, n, 0, md->x.p, md->atype.p, md->box, nullptr,
+                                                   md->e.p, md->f.p, md->vir.p, nullptr, nullptr);
+    if (rc != B200DP_OK) return rc;
+    count_launch();
+    k_md_second<<<kRedBlocks, kMdThreads, 0, st>>>(n, md->v.p, md->f.p, md->minv.p, md->mass.p, dtf, md->part.p);
+    if (nvt) {
+      count_launch();
+      k_md_chain<<<1, 32, 0, st>>>(md->cp, md->chain.p, md->part.p, kRedBlocks, nullptr);
+      count_launch();
+      k_md_scale<<<grid, kMdThreads, 0, st>>>(n, md->v.p, md->chain.p);
+      count_launch();
+      k_md_ke<<<kRedBlocks, kMdThreads, 0, st>>>(n, md->v.p, md->mass.p, md->part.p);
+    }
+    ++md->step;
+  }
+  return cudaGetLastError() == cudaSuccess ? B200DP_OK : B200DP_ERR_CUDA;
+}
+
+b200dp_status b200dp_md_thermo(b200dp_md* md, double* thermo) {
+  if (!md || !thermo) return B200DP_ERR_INVALID;
+  double e = 0, vir[9], part[kRedBlocks];
+  Chain ch;
+  if (cudaMemcpyAsync(&e, md->e.p, sizeof(double), cudaMemcpyDeviceToHost, md->stream) != cudaSuccess ||
+      cudaMemcpyAsync(vir, md->vir.p, sizeof(vir), cudaMemcpyDeviceToHost, md->stream) != cudaSuccess ||
+      cudaMemcpyAsync(part, md->part.p, sizeof(part), cudaMemcpyDeviceToHost, md->stream) != cudaSuccess ||
+      cudaMemcpyAsync(&ch, md->chain.p, sizeof(ch), cudaMemcpyDeviceToHost, md->stream) != cudaSuccess ||
+      cudaStreamSynchronize(md->stream) != cudaSuccess)
+    return B200DP_ERR_CUDA;
+  const b200dp_status rc = b200dp_check(md->engine);
+  if (rc != B200DP_OK) return rc;
+  double mv2 = 0;
+  for (int k = 0; k < kRedBlocks; ++k) mv2 += part[k];
+  const double ke = 0.5 * mv2 * kMvv2e;
+  const double temp = 2.0 * ke / (md->dof * kBoltz);
+  double e_chain = 0;
+  if (md->ensemble == B200DP_MD_NVT) {
+    const ChainParams& cp = md->cp;
+    e_chain = cp.ke_target * ch.eta[0];
+    for (int i = 1; i < cp.M; ++i) e_chain += cp.boltz_t * ch.eta[i];
+    for (int i = 0; i < cp.M; ++i) e_chain += 0.5 * cp.mass[i] * ch.eta_dot[i] * ch.eta_dot[i];
+  }
+  thermo[0] = (double)md->step;
+  thermo[1] = e;
+  thermo[2] = ke;
+  thermo[3] = temp;
+  thermo[4] = e + ke + e_chain;
+  thermo[5] = (md->dof * kBoltz * temp + vir[0] + vir[4] + vir[8]) / (3.0 * md->volume) * kNktv2p;
+  thermo[6] = md->volume;
+  thermo[7] = e_chain;
+  return B200DP_OK;
+}
+
+b200dp_status b200dp_md_state(b200dp_md* md, double* coord, double* vel, double* force) {
+  if (!md) return B200DP_ERR_INVALID;
+  const size_t b = sizeof(double) * 3 * (size_t)md->n;
+  if ((coord && cudaMemcpyAsync(coord, md->x.p, b, cudaMemcpyDeviceToHost, md->stream) != cudaSuccess) ||
+      (vel && cudaMemcpyAsync(vel, md->v.p, b, cudaMemcpyDeviceToHost, md->stream) != cudaSuccess) ||
+      (force && cudaMemcpyAsync(force, md->f.p, b, cudaMemcpyDeviceToHost, md->stream) != cudaSuccess) ||
+      cudaStreamSynchronize(md->stream) != cudaSuccess)
+    return B200DP_ERR_CUDA;
+  return b200dp_check(md->engine);
+}
+
+b200dp_status b200dp_md_destroy(b200dp_md* md) {
+  if (!md) return B200DP_OK;
+  cudaStreamSynchronize(md->stream);
+  cudaStreamDestroy(md->stream);
+  delete md;
+  return B200DP_OK;
+}
+
+}  // extern "C"

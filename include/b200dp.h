@@ -208,6 +208,50 @@ int b200dp_direct_energy_force(const int64_t* atype, const int64_t* row_ptr, con
                                const float* edge_vec, int64_t node_count, int64_t nloc, int64_t edge_storage,
                                double* energy_out, double* force_out, double* virial_out);
 
+/* ------------------------------------------------------------------ MD
+ * Molecular-dynamics driver around an engine (metal units: Angstrom, ps,
+ * g/mol, eV, K, bar).  Velocity Verlet (NVE) or velocity Verlet with a
+ * Nose-Hoover chain thermostat (NVT) in the integration order of LAMMPS'
+ * fix nve / fix nvt, which drives the reference's force call
+ * (components/lammps/overlays/src/KOKKOS/fix_nh_kokkos.cpp:863-1001; device
+ * chain: components/lammps/overlays/src/KOKKOS/dpa_fast_step_kokkos.h:307-400).
+ * Positions, velocities, forces and the chain state stay on the device; a
+ * run enqueues its steps on the driver's stream without host
+ * synchronisation.  The box is fixed and periodic; positions are not
+ * wrapped (the engine images them). */
+typedef enum b200dp_md_ensemble { B200DP_MD_NVE = 0, B200DP_MD_NVT = 1 } b200dp_md_ensemble;
+
+typedef struct b200dp_md_params {
+  double dt;        /* time step, ps (default 0.0005) */
+  int ensemble;     /* b200dp_md_ensemble */
+  int chain;        /* Nose-Hoover chain length (NVT, 1..8, default 3) */
+  double t_target;  /* K (NVT) */
+  double t_damp;    /* thermostat period, ps (NVT, default 0.05) */
+  double t_init;    /* K: > 0 draws seeded Gaussian velocities at this temperature (zero momentum) */
+  unsigned long long seed;
+  double mass[8];   /* g/mol per atom type */
+  int reserved[16];
+} b200dp_md_params;
+
+typedef struct b200dp_md b200dp_md;
+
+b200dp_status b200dp_md_params_default(b200dp_md_params* params);
+/* Host arrays: coord [natoms*3], vel [natoms*3] or NULL (then t_init > 0),
+ * atype [natoms], box [9].  Computes the initial forces. */
+b200dp_status b200dp_md_create(b200dp_engine* engine, int natoms, const double* coord, const double* vel,
+                               const int* atype, const double* box, const b200dp_md_params* params,
+                               b200dp_md** out);
+/* Enqueues nsteps steps; returns without waiting for them. */
+b200dp_status b200dp_md_run(b200dp_md* md, int nsteps);
+/* Waits for the driver's stream.  thermo[8]: step, potential energy, kinetic
+ * energy, temperature (dof = 3N - 3), conserved energy (potential + kinetic +
+ * thermostat), pressure (bar), volume, thermostat energy. */
+b200dp_status b200dp_md_thermo(b200dp_md* md, double* thermo);
+/* Waits for the driver's stream and copies positions / velocities / forces
+ * (host arrays of natoms*3, any may be NULL). */
+b200dp_status b200dp_md_state(b200dp_md* md, double* coord, double* vel, double* force);
+b200dp_status b200dp_md_destroy(b200dp_md* md);
+
 /* Total kernels this library has launched in the process (all engines). */
 long long b200dp_kernel_launches(void);
 b200dp_status b200dp_stage_times(b200dp_engine* engine, float* ms5);

@@ -1,0 +1,110 @@
+"""The device MD driver (velocity Verlet, Nose-Hoover chain) against a numpy
+restatement of LAMMPS' fix nve / fix nvt driven by the CPU oracle's forces,
+plus conservation, determinism and the seeded initial velocities."""
+import numpy as np
+import pytest
+
+import b200dp
+import oracle
+import systems
+from md_reference import BOLTZ, MVV2E, Chain, run, temperature
+
+pytestmark = pytest.mark.gpu
+
+MASS = [15.9994, 1.00794]  # O, H (g/mol)
+
+
+def start(seed=7, t=300.0):
+    s = systems.config0()
+    m = np.array([MASS[k] for k in s.atype])
+    rng = np.random.default_rng(seed)
+    v = rng.normal(size=(s.natoms, 3)) * np.sqrt(BOLTZ * t / (m[:, None] * MVV2E))
+    v -= (m[:, None] * v).sum(0) / m.sum()
+    return s, m, v
+
+
+def oracle_force(model, box):
+    o = oracle.Oracle(model)
+
+    def force(x):
+        r = o.compute(x, force.atype, box, atomic=False)
+        return r["energy"], r["force"]
+
+    return force
+
+
+@pytest.mark.parametrize("ensemble", [b200dp.NVE, b200dp.NVT])
+def test_trajectory_matches_reference(model_dir, ensemble):
+    model = str(model_dir / "water.b2dp")
+    s, m, v0 = start()
+    dt, nsteps = 0.0005, 20
+    dp = b200dp.DeepPot(model, precision=b200dp.FP64)
+    md = b200dp.MD(dp, s.coord, s.atype, s.box, MASS, dt=dt, ensemble=ensemble, vel=v0, t_target=330.0,
+                   t_damp=0.01, chain=3)
+    md.run(nsteps)
+    x, v, f = md.state()
+    th = md.thermo()
+    force = oracle_force(model, s.box)
+    force.atype = s.atype
+    chain = Chain(3 * s.natoms - 3, 330.0, 0.01, 3, dt) if ensemble == b200dp.NVT else None
+    xr, vr, er = run(s.coord, v0, m, force, dt, nsteps, chain)
+    assert np.abs(x - xr).max() < 1e-9
+    assert np.abs(v - vr).max() < 1e-7 * np.abs(vr).max()
+    assert abs(th["pe"] - er) < 1e-9 * abs(er)
+    assert abs(th["temp"] - temperature(vr, m)) < 1e-8 * th["temp"]
+    if chain is not None:
+        assert abs(th["e_thermostat"] - chain.energy()) < 1e-7 * max(abs(chain.energy()), 1e-3)
+    md.close()
+    dp.close()
+
+
+def energy_error(dp, s, v0, masses, dt, ens, nsteps, every):
+    md = b200dp.MD(dp, s.coord, s.atype, s.box, masses, dt=dt, ensemble=ens, vel=v0, t_target=300.0, t_damp=0.025)
+    e0 = md.thermo()["conserved"]
+    err = 0.0
+    for _ in range(nsteps // every):
+        md.run(every)
+        err = max(err, abs(md.thermo()["conserved"] - e0))
+    md.close()
+    return err
+
+
+@pytest.mark.parametrize("precision", [b200dp.FP64, b200dp.MIXED])
+def test_conserved_energy(model_dir, precision):
+    """The random test model has no bonds, so atoms are given the oxygen mass
+    (no free-flying hydrogens reaching the 1/r part of the environment rows);
+    the conserved energy then stays within a small fraction of kT per degree
+    of freedom and its error falls ~4x when the step is halved (Verlet, dt^2)."""
+    s, m, _ = start(seed=3)
+    masses = [15.9994, 15.9994]
+    mh = np.full(s.natoms, 15.9994)
+    rng = np.random.default_rng(4)
+    v0 = rng.normal(size=(s.natoms, 3)) * np.sqrt(BOLTZ * 300.0 / (mh[:, None] * MVV2E))
+    v0 -= v0.mean(0)
+    dp = b200dp.DeepPot(str(model_dir / "water.b2dp"), precision=precision)
+    kt = BOLTZ * 300.0
+    for ens in (b200dp.NVE, b200dp.NVT):
+        e1 = energy_error(dp, s, v0, masses, 0.001, ens, 200, 10)
+        assert e1 < 0.05 * kt * s.natoms / 100, (ens, e1)
+        if precision == b200dp.FP64:
+            e2 = energy_error(dp, s, v0, masses, 0.0005, ens, 400, 20)
+            assert e2 < 0.5 * e1, (ens, e1, e2)
+    dp.close()
+
+
+def test_deterministic_and_seeded_start(model_dir):
+    s, m, _ = start()
+    dp = b200dp.DeepPot(str(model_dir / "water.b2dp"), precision=b200dp.MIXED)
+    runs = []
+    for _ in range(2):
+        md = b200dp.MD(dp, s.coord, s.atype, s.box, MASS, ensemble=b200dp.NVT, t_init=250.0, seed=11)
+        th0 = md.thermo()
+        assert abs(th0["temp"] - 250.0) < 1e-9 * 250.0
+        _, v, _ = md.state()
+        assert np.abs((m[:, None] * v).sum(0)).max() < 1e-9
+        md.run(50)
+        runs.append(md.state())
+        md.close()
+    for a, b in zip(*runs):
+        assert np.array_equal(a, b)
+    dp.close()
