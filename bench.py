@@ -59,7 +59,7 @@ HALO = 8.0  # ghost shell: rcut 6 A + 2 A neighbour skin
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200dp", choices=["b200dp", "reference"])
     ap.add_argument("--precision", default="mixed", choices=["mixed", "fp64"])
@@ -91,7 +91,7 @@ def start_clocks(gpu: int, path: str):
     try:
         f = open(path, "w")
         p = subprocess.Popen(["nvidia-smi", "-i", str(gpu), f"--query-gpu={q}", "--format=csv,noheader,nounits",
-                              "-lms", "200"], stdout=f, stderr=subprocess.DEVNULL)
+                              "-lms", "25"], stdout=f, stderr=subprocess.DEVNULL)
         return p, f
     except OSError:
         return None, None

@@ -41,7 +41,7 @@ __device__ __forceinline__ void mma3d(uint32_t d, uint64_t a_hi, uint64_t a_lo, 
 struct Item {
   int q, rb, re, e0, e1;
 };
-__device__ __forceinline__ Item item_of(const TcLists& L, int it) {
+__device__ __forceinline__ Item item_compute(const TcLists& L, int it) {
   Item r;
   int q = 0;
   while (q + 1 < L.nnets && L.istart[q + 1] <= it) ++q;
@@ -57,6 +57,12 @@ __device__ __forceinline__ Item item_of(const TcLists& L, int it) {
   r.e0 = L.eoff[(size_t)q * L.nloc + r.rb];
   r.e1 = L.eoff[(size_t)q * L.nloc + r.re];
   return r;
+}
+// The kernels read the precomputed record (two 16-byte loads instead of a
+// chain of dependent lookups).
+__device__ __forceinline__ Item item_of(const TcLists& L, int it) {
+  const int4 a = L.items[2 * it], b = L.items[2 * it + 1];
+  return Item{a.x, a.y, a.z, a.w, b.x};
 }
 
 // ---------------------------------------------------------------- forward
@@ -967,6 +973,15 @@ __global__ void k_edge_compact(SeaDev s, int nloc, const int* __restrict__ type_
   }
 }
 
+__global__ void k_item_records(TcLists L, int cap, int4* __restrict__ items) {
+  const int n = min(L.istart[L.nnets], cap);
+  for (int it = blockIdx.x * blockDim.x + threadIdx.x; it < n; it += gridDim.x * blockDim.x) {
+    const Item I = item_compute(L, it);
+    items[2 * it] = make_int4(I.q, I.rb, I.re, I.e0);
+    items[2 * it + 1] = make_int4(I.e1, 0, 0, 0);
+  }
+}
+
 // Items per net are padded to a multiple of kFwdGroups so that a round of
 // the grouped forward kernel never mixes nets (padded items are empty).
 __global__ void k_item_table(int nnets, int ntypes, int tos, const int* __restrict__ type_start,
@@ -1118,6 +1133,16 @@ void launch_edge_compact(cudaStream_t st, const SeaDev& s, int nloc, const int* 
   count_launch();
   k_edge_compact<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(s, nloc, type_start, perm_atom, atype, rij, eoff,
                                                                        rt, row, slot);
+}
+
+int tc_item_capacity(const SeaDev& s, int nloc) {
+  return s.nnets * ((nloc + kItemRows - 1) / kItemRows + kFwdGroups) + kFwdGroups;
+}
+
+void launch_item_records(cudaStream_t st, const SeaDev& s, const TcLists& L, int4* items) {
+  const int cap = tc_item_capacity(s, L.nloc);
+  count_launch();
+  k_item_records<<<std::max(1, std::min(148 * 4, (cap + 255) / 256)), 256, 0, st>>>(L, cap, items);
 }
 
 void launch_item_table(cudaStream_t st, const SeaDev& s, int nloc, const int* type_start, int* istart) {

@@ -42,7 +42,14 @@ struct TcLists {
   const float4* rt;       // [E] environment row (s, s x/r, s y/r, s z/r)
   const int* row;         // [E] centre row in type-grouped order
   const int* slot;        // [E] slot in the formatted neighbour list
+  const int4* items;      // [2 * item capacity] per work item {net, first row, end row, first edge}, {end edge, -, -, -}
 };
+
+// Work items per embedding net are padded to whole rounds of the grouped
+// kernels; this bounds the item count for buffer sizing.
+int tc_item_capacity(const SeaDev& s, int nloc);
+// Fills TcLists::items from istart / type_start / eoff (one thread per item).
+void launch_item_records(cudaStream_t st, const SeaDev& s, const TcLists& L, int4* items);
 
 void launch_edge_count(cudaStream_t st, const SeaDev& s, int nloc, const int* type_start, const int* perm_atom,
                        const int* atype, const int* cnt, int* ecount);

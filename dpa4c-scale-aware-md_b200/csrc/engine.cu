@@ -244,7 +244,7 @@ void Engine::release() {
                     &blk_counts, &type_start, &perm_pos, &perm_atom, &Tbuf, &Dbuf, &dDbuf, &atom_e, &gslot,
                     &vrows, &err_buf, &reduce_part, &scalars, &h_coord, &h_atype, &h_force, &h_aviral, &h_ae,
                     &cand_start, &cand_list, &ilist_d, &tc_nets, &ecount, &eoff, &tstart, &rec_rt, &rec_row,
-                    &rec_slot, &partial, &scan_scratch, &dTbuf, &ftile})
+                    &rec_slot, &partial, &scan_scratch, &dTbuf, &ftile, &graph_atype, &item_rec})
     b->release();
   for (auto& v : fit_w)
     for (auto& b : v) b.release();
@@ -312,6 +312,7 @@ b200dp_status Engine::ensure_buffers(int nloc, int nall, int ncells, int ncand) 
     B200DP_CUDA_TRY(ecount.ensure(sizeof(int) * (NL + 1)));
     B200DP_CUDA_TRY(eoff.ensure(sizeof(int) * (NL + 1)));
     B200DP_CUDA_TRY(tstart.ensure(sizeof(int) * (sd.nnets + 1)));
+    B200DP_CUDA_TRY(item_rec.ensure(sizeof(int) * 8 * (size_t)tc_item_capacity(sd, L)));
     B200DP_CUDA_TRY(rec_rt.ensure(sizeof(float4) * S));
     B200DP_CUDA_TRY(rec_row.ensure(sizeof(int) * S));
     B200DP_CUDA_TRY(rec_slot.ensure(sizeof(int) * S));
@@ -418,6 +419,7 @@ TcLists Engine::tc_lists(int nloc) const {
   L.rt = rec_rt.as<float4>();
   L.row = rec_row.as<int>();
   L.slot = rec_slot.as<int>();
+  L.items = reinterpret_cast<const int4*>(item_rec.ptr);
   return L;
 }
 
@@ -455,6 +457,7 @@ b200dp_status Engine::run_model(cudaStream_t st, int nloc, int nall, const int* 
                         rec_slot.as<int>());
     launch_item_table(st, sd, nloc, type_start.as<int>(), tstart.as<int>());
     const TcLists Lst = tc_lists(nloc);
+    launch_item_records(st, sd, Lst, reinterpret_cast<int4*>(item_rec.ptr));
     launch_embed_fwd_tc(st, sd, Lst, embed_tc_grid(sd, false), tc_nets.as<unsigned char>(), partial.as<float>(),
                         err_d);
     unsigned char* dth = nullptr;

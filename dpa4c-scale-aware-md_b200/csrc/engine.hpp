@@ -53,7 +53,7 @@ struct Engine {
   DevBuf cand_start, cand_list, ilist_d;
   // tensor-core embedding path (mixed mode)
   bool use_tc = false;
-  DevBuf graph_atype;
+  DevBuf graph_atype, item_rec;
   DevBuf tc_nets, ecount, eoff, tstart, rec_rt, rec_row, rec_slot, partial, scan_scratch, dTbuf;
   // tensor-core fitting (mixed mode)
   bool use_fit_tc = false;
