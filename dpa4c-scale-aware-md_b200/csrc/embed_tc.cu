@@ -220,11 +220,16 @@ __device__ __forceinline__ void fwd_epi3(const float* f, uint32_t taddr, const f
                                          unsigned char* gl, int e) {
   using P = Split<D1, D2, D3>;
   using S = FwdGroup;
+  // TMEM loads one chunk ahead: the load of chunk c + 1 overlaps the tanh of chunk c
+  float nxt[16];
+  umma::ld16(taddr + H * 64, nxt);
+  umma::wait_ld();
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
     float v[16];
-    umma::ld16(taddr + H * 64 + c * 16, v);
-    umma::wait_ld();
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = nxt[i];
+    if (c + 1 < 4) umma::ld16(taddr + H * 64 + (c + 1) * 16, nxt);
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       const int j = c * 16 + i;
@@ -241,6 +246,7 @@ __device__ __forceinline__ void fwd_epi3(const float* f, uint32_t taddr, const f
       const uint32_t o = mb * S::SBO_G + (e >> 3) * S::LBO_G + (e & 7) * 16;
       store8_split(gh + o, gl + o, v + 8 * hh);
     }
+    if (c + 1 < 4) umma::wait_ld();
   }
 }
 
