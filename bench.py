@@ -230,13 +230,19 @@ class Decomposed:
         x, t, ids = domain.distribute(system.coord, system.atype, dd)
 
         def compute(x_all, t_all, nloc, nghost, region, e, f, v):
-            dp.compute_device(stream.cuda_stream, nloc, nghost, x_all.data_ptr(), t_all.data_ptr(), None, region,
-                              e.data_ptr(), f.data_ptr(), v.data_ptr())
+            dp.compute_device(torch.cuda.current_stream(dev).cuda_stream, nloc, nghost, x_all.data_ptr(),
+                              t_all.data_ptr(), None, region, e.data_ptr(), f.data_ptr(), v.data_ptr())
 
         self.ddp = domain.DistributedDeepPot(compute, system.box, grid, rank, HALO, x, t, ids, device=dev)
         self.n = self.ddp.nloc
         self.total = system.natoms
         self.nghost = self.ddp.nghost
+
+    def capture(self):
+        self.ddp.capture()
+
+    def release(self):
+        self.ddp.release()
 
     def step(self):
         self.ddp.step()
@@ -279,17 +285,24 @@ def run_b200dp(args, world, rank, local):
             return Periodic(dp, system, dev, stream, torch)
         return Decomposed(dp, system, grid, rank, dev, stream, torch)
 
-    def device_loop(dp, w, steps, warmup, stage_timing):
+    def device_loop(dp, w, steps, warmup):
+        """Timed steps: CUDA events around each step on the launch stream, L2 flushed before each,
+        no host synchronisation inside the loop.  N > 1 replays the decomposed step as a CUDA graph;
+        its kernel count per step is the number the capture recorded."""
         for _ in range(warmup):
             w.step()
         dp.check()
-        dp.set_stage_timing(stage_timing)
+        dp.set_stage_timing(False)
+        per_step = None
+        if hasattr(w, "capture"):
+            l0 = b200dp.kernel_launches()
+            w.capture()
+            per_step = (b200dp.kernel_launches() - l0) // 2  # the capture runs one eager step, then records one
         if dist:
             dist.barrier()
         torch.cuda.synchronize()
         starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
         ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-        stages = []
         l0 = b200dp.kernel_launches()
         for k in range(steps):
             flush.fill_(k & 0xFF)
@@ -298,15 +311,29 @@ def run_b200dp(args, world, rank, local):
             starts[k].record(stream)
             w.step()
             ends[k].record(stream)
-            if stage_timing:
-                stages.append(dp.stage_times())
         torch.cuda.synchronize()
-        launches = b200dp.kernel_launches() - l0
+        launches = b200dp.kernel_launches() - l0 if per_step is None else per_step * steps
         if dist:
             dist.barrier()
         dp.check()
+        if hasattr(w, "release"):
+            w.release()
         ms = sum(s.elapsed_time(en) for s, en in zip(starts, ends))
-        return ms, launches, stages
+        return ms, launches
+
+    def stage_pass(dp, w, nsteps):
+        """Per-stage device times from the engine's stage events (a host sync per step, so this
+        runs apart from the timed loop)."""
+        dp.set_stage_timing(True)
+        stages = []
+        for k in range(nsteps):
+            flush.fill_(k & 0xFF)
+            if dist:
+                dist.all_reduce(sync)
+            w.step()
+            stages.append(dp.stage_times())
+        dp.set_stage_timing(False)
+        return np.array(stages).mean(0)
 
     def max_over_ranks(x):
         if not dist:
@@ -320,16 +347,15 @@ def run_b200dp(args, world, rank, local):
     n = w.n
     clk_path = os.path.join(tempfile.gettempdir(), f"b200dp_clocks_{rank}.csv")
     cp, cf = start_clocks(local, clk_path)
-    ms, launches, stages = device_loop(dp, w, args.steps, args.warmup, True)
+    ms, launches = device_loop(dp, w, args.steps, args.warmup)
     clocks = stop_clocks(cp, cf, clk_path)
+    stage_ms = stage_pass(dp, w, max(5, min(args.steps, 20)))
     ms = max_over_ranks(ms)
     value = w.total * args.steps / (ms / 1e3)
     # edges (real neighbours) of this rank's owned atoms for the FLOP count
     nl = dp.last_nlist(n)["nlist"]
     edges = int((nl >= 0).sum())
     fl = model_flops(m, n, edges)
-    st = np.array(stages)  # [steps, 5]
-    stage_ms = st.mean(0) if len(st) else np.zeros(5)
     pk, pk_kind = peaks()
     bwd_ms = float(stage_ms[3])
     achieved = fl["descriptor_bwd"] / (bwd_ms / 1e3) / 1e12 if bwd_ms > 0 else 0.0
@@ -357,10 +383,11 @@ def run_b200dp(args, world, rank, local):
         dp64 = b200dp.DeepPot(mp, precision=b200dp.FP64, device=local)
         w64 = workload(dp64)
         k64 = max(2, min(args.steps, 5))
-        ms64, _, st64 = device_loop(dp64, w64, k64, max(1, min(args.warmup, 2)), True)
+        ms64, _ = device_loop(dp64, w64, k64, max(1, min(args.warmup, 2)))
         ms64 = max_over_ranks(ms64)
+        st64 = stage_pass(dp64, w64, 2)
         fp64 = {"value": w.total * k64 / (ms64 / 1e3), "ms_per_step": ms64 / k64,
-                "stage_ms": [round(float(q), 4) for q in np.array(st64).mean(0)]}
+                "stage_ms": [round(float(q), 4) for q in st64]}
         del w64
         dp64.close()
     # MD loop (N = 1): the same force call inside the device MD driver (NVT Nose-Hoover chain,
@@ -389,7 +416,8 @@ def run_b200dp(args, world, rank, local):
         cpu = {"value": rate, "unit": "atom-steps/s", "cores": used, "kind": "port",
                "sample": f"one full evaluation of the 12,288-atom system ({dt:.2f} s), fp64 C++ oracle, OpenMP"}
     if world > 1:
-        parallelism = f"domain decomposition {grid[0]}x{grid[1]}x{grid[2]}, halo {HALO} A, NCCL send/recv"
+        parallelism = (f"domain decomposition {grid[0]}x{grid[1]}x{grid[2]}, halo {HALO} A, NCCL send/recv, "
+                       "step replayed as one CUDA graph")
         cfg_extra = {"global_atoms": w.total, "ghosts_rank0": w.nghost}
     else:
         parallelism, cfg_extra = "single", {}
@@ -404,6 +432,7 @@ def run_b200dp(args, world, rank, local):
                        "l2": "flushed before every timed step (256 MB write), flush outside the events"},
             "stage_ms": {k: round(float(q), 4) for k, q in
                          zip(["neighbour", "descriptor_fwd", "fitting", "descriptor_bwd", "assembly"], stage_ms)},
+            "stage_note": "stage times from a separate pass with the engine's stage events (rank 0)",
             "gpu_launches": int(launches),
             "roofline": roofline,
             "e2e": e2e,
@@ -476,15 +505,17 @@ def e2e_decomposed(w, steps, warmup, torch, dist):
 
     for _ in range(warmup):
         call()
+    ddp.capture()
     dist.barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for _ in range(steps):
         call()
     dt = time.perf_counter() - t0
+    ddp.release()
     return {"value": None, "unit": "atom-steps/s", "seconds": dt,
             "h2d_bytes_per_step": n * 3 * 8, "d2h_bytes_per_step": n * 3 * 8 + 8 * 10,
-            "entry": "domain.DistributedDeepPot.step over b200dp_compute_device (pinned host buffers, per rank)",
+            "entry": "domain.DistributedDeepPot.step (captured CUDA graph) over b200dp_compute_device (pinned host buffers, per rank)",
             "bytes_rank": "rank 0's own counts"}
 
 

@@ -105,6 +105,26 @@ def _exchange(send: torch.Tensor, peer_send: int, recv: torch.Tensor, peer_recv:
             req.wait()
 
 
+def _exchange_many(items, rank: int) -> None:
+    """Several (send, peer_send, recv, peer_recv) exchanges in one batch.
+
+    Every rank posts the same sequence, so point-to-point messages between a
+    pair of ranks match in posting order; self-exchanges are local copies.
+    """
+    ops = []
+    for send, peer_send, recv, peer_recv in items:
+        if peer_send == rank and peer_recv == rank:
+            recv.copy_(send)
+            continue
+        if recv.numel():
+            ops.append(dist.P2POp(dist.irecv, recv, peer_recv))
+        if send.numel():
+            ops.append(dist.P2POp(dist.isend, send.contiguous(), peer_send))
+    if ops:
+        for req in dist.batch_isend_irecv(ops):
+            req.wait()
+
+
 def _exchange_counts(n_send: int, peer_send: int, peer_recv: int, rank: int, device) -> int:
     s = torch.tensor([n_send], dtype=torch.int64, device=device)
     r = torch.zeros(1, dtype=torch.int64, device=device)
@@ -171,20 +191,32 @@ class HaloExchange:
         return self.nall - self.nloc
 
     def forward(self, x_all: torch.Tensor) -> None:
-        """Refreshes the ghost rows of x_all ([nall, 3]) from the owners' rows."""
-        for p in self.passes:
-            sp = x_all.index_select(0, p.send_idx)
-            if p.shift:
-                sp[:, p.dim] += p.shift
-            _exchange(sp, p.peer_send, x_all[p.recv_off:p.recv_off + p.n_recv], p.peer_recv, self.rank)
+        """Refreshes the ghost rows of x_all ([nall, 3]) from the owners' rows.
+
+        Dimensions go in order (a later one forwards ghosts of an earlier one);
+        the two directions of a dimension are independent and share one batch.
+        """
+        for d in range(3):
+            items = []
+            for p in self.passes[2 * d:2 * d + 2]:
+                sp = x_all.index_select(0, p.send_idx)
+                if p.shift:
+                    sp[:, p.dim] += p.shift
+                items.append((sp, p.peer_send, x_all[p.recv_off:p.recv_off + p.n_recv], p.peer_recv))
+            _exchange_many(items, self.rank)
 
     def reverse(self, f_all: torch.Tensor) -> None:
-        """Folds ghost forces back onto the atoms they were copied from."""
-        for p in reversed(self.passes):
-            back = torch.empty((p.send_idx.numel(), f_all.shape[1]), dtype=f_all.dtype, device=self.device)
-            _exchange(f_all[p.recv_off:p.recv_off + p.n_recv].contiguous(), p.peer_recv, back, p.peer_send,
-                      self.rank)
-            f_all.index_add_(0, p.send_idx, back)
+        """Folds ghost forces back onto the atoms they were copied from
+        (dimensions in reverse order, both directions of one in one batch)."""
+        for d in (2, 1, 0):
+            items, backs = [], []
+            for p in reversed(self.passes[2 * d:2 * d + 2]):
+                back = torch.empty((p.send_idx.numel(), f_all.shape[1]), dtype=f_all.dtype, device=self.device)
+                items.append((f_all[p.recv_off:p.recv_off + p.n_recv].contiguous(), p.peer_recv, back, p.peer_send))
+                backs.append((p, back))
+            _exchange_many(items, self.rank)
+            for p, back in backs:
+                f_all.index_add_(0, p.send_idx, back)
 
 
 def wrap(coord: np.ndarray, L: np.ndarray) -> np.ndarray:
@@ -218,6 +250,7 @@ class DistributedDeepPot:
         self.dd = Decomposition(box, grid, rank, halo)
         self.compute = compute
         dev = torch.device(device)
+        self.device = dev
         x = torch.as_tensor(np.asarray(x_owned, dtype=np.float64), device=dev)
         t = torch.as_tensor(np.asarray(t_owned, dtype=np.int32), device=dev)
         ids = None if ids_owned is None else torch.as_tensor(np.asarray(ids_owned, dtype=np.int64), device=dev)
@@ -239,6 +272,9 @@ class DistributedDeepPot:
 
     def step(self):
         """Returns (energy [1], force of owned atoms [nloc, 3], virial [9]) summed over ranks."""
+        if self._graph is not None:
+            self._graph.replay()
+            return self.ev[0:1], self.force[: self.nloc], self.ev[1:10]
         self.plan.forward(self.x)
         self.compute(self.x, self.types, self.nloc, self.nghost, self.region, self.ev[0:1], self.force,
                      self.ev[1:10])
@@ -246,3 +282,29 @@ class DistributedDeepPot:
         if dist.is_initialized():
             dist.all_reduce(self.ev, op=dist.ReduceOp.SUM)
         return self.ev[0:1], self.force[: self.nloc], self.ev[1:10]
+
+    _graph = None
+
+    def capture(self) -> None:
+        """Records one whole step (halo exchange, force call, reverse fold,
+        all-reduce) as a CUDA graph; later step() calls replay it.  The many
+        small exchange launches then cost no host time.  Every rank captures
+        together; `compute` must launch on torch's current stream; positions
+        change through `set_positions` (same buffer).  Call release() before
+        the process group is destroyed."""
+        if self.device.type != "cuda":
+            return
+        cur = torch.cuda.current_stream(self.device)
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(cur)
+        with torch.cuda.stream(side):
+            self.step()  # warm-up on the capturing stream
+        cur.wait_stream(side)
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.step()
+        self._graph = g
+
+    def release(self) -> None:
+        self._graph = None
