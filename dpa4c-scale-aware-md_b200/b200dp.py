@@ -35,13 +35,14 @@ EXPORTS = [
     "b200dp_md_run", "b200dp_md_thermo", "b200dp_md_state", "b200dp_md_destroy",
 ]
 
-NVE, NVT = 0, 1
+NVE, NVT, NPT = 0, 1, 2
 
 
 class MDParams(ctypes.Structure):
     _fields_ = [("dt", ctypes.c_double), ("ensemble", ctypes.c_int), ("chain", ctypes.c_int),
                 ("t_target", ctypes.c_double), ("t_damp", ctypes.c_double), ("t_init", ctypes.c_double),
-                ("seed", ctypes.c_ulonglong), ("mass", ctypes.c_double * 8), ("reserved", ctypes.c_int * 16)]
+                ("seed", ctypes.c_ulonglong), ("mass", ctypes.c_double * 8), ("p_target", ctypes.c_double),
+                ("p_damp", ctypes.c_double), ("pchain", ctypes.c_int), ("reserved", ctypes.c_int * 11)]
 
 
 class B200DPError(RuntimeError):
@@ -252,12 +253,13 @@ class MD:
     THERMO = ("step", "pe", "ke", "temp", "conserved", "press", "volume", "e_thermostat")
 
     def __init__(self, dp: DeepPot, coord, atype, box, masses, dt=0.0005, ensemble=NVE, vel=None, t_init=0.0,
-                 t_target=300.0, t_damp=0.05, chain=3, seed=0):
+                 t_target=300.0, t_damp=0.05, chain=3, seed=0, p_target=1.0, p_damp=0.5, pchain=3):
         L = load_library()
         p = MDParams()
         L.b200dp_md_params_default(ctypes.byref(p))
         p.dt, p.ensemble, p.chain = dt, ensemble, chain
         p.t_target, p.t_damp, p.t_init, p.seed = t_target, t_damp, t_init, seed
+        p.p_target, p.p_damp, p.pchain = p_target, p_damp, pchain
         for t, m in enumerate(masses):
             p.mass[t] = m
         coord = np.ascontiguousarray(coord, dtype=np.float64).reshape(-1, 3)

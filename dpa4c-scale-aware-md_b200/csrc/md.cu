@@ -1,5 +1,6 @@
 // Molecular-dynamics driver around the force engine: velocity Verlet with an
-// optional Nose-Hoover chain thermostat (NVT), state resident on the device.
+// optional Nose-Hoover chain thermostat (NVT) or thermostat + isotropic MTK
+// barostat (NPT), state resident on the device.
 //
 // Semantics follow LAMMPS `fix nve` / `fix nvt` in metal units (the reference
 // drives its force call from LAMMPS' Kokkos Verlet with `fix nh`,
@@ -15,6 +16,19 @@
 // Qi = kB T0 / w^2 with w = 1 / t_damp).  Every step is enqueued on one stream
 // with no host synchronisation; reductions use a fixed grid and order, so a
 // trajectory is bitwise reproducible.
+//
+// NPT follows LAMMPS' fix npt iso with the MTK terms (FixNH: nhc_press_integrate,
+// nhc_temp_integrate, nh_omega_dot, nh_v_press, remap):
+//   initial: barostat chain; thermostat chain (v *= s); pressure from the last
+//            virial; omega_dot += dt/2 F_omega; v *= exp(-dt/2 (omega_dot + mtk2));
+//            v += dt/2 F/m; x *= exp(dt omega_dot) around the drift x += dt v
+//            (two half remaps), box scaled the same way
+//   force call in the new box
+//   final:   v += dt/2 F/m; v *= exp(-dt/2 (omega_dot + mtk2)); temperature and
+//            pressure; omega_dot += dt/2 F_omega; thermostat chain; barostat chain
+// The scalar chains run on the host (one 12-number read per step); every
+// per-atom operation is a device kernel.  The box is scaled about the origin
+// (LAMMPS scales about the box centre; the two differ by a uniform translation).
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -162,6 +176,118 @@ __global__ void __launch_bounds__(kMdThreads) k_md_ke(int n, const double* __res
   }
 }
 
+// v = v * sv + dtf F / m ; x = e (e x + dt v)   (NPT first half: remap, drift, remap)
+__global__ void k_npt_first(int n, double* __restrict__ x, double* __restrict__ v, const double* __restrict__ f,
+                            const double* __restrict__ minv, double sv, double dtf, double dt, double e) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const double w = dtf * minv[i];
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+      const double vv = v[3 * i + c] * sv + w * f[3 * i + c];
+      v[3 * i + c] = vv;
+      x[3 * i + c] = e * (e * x[3 * i + c] + dt * vv);
+    }
+  }
+}
+
+// v = (v + dtf F / m) * sv, with per-block partial sums of m v^2
+__global__ void __launch_bounds__(kMdThreads) k_npt_second(int n, double* __restrict__ v,
+                                                           const double* __restrict__ f,
+                                                           const double* __restrict__ minv,
+                                                           const double* __restrict__ mass, double dtf, double sv,
+                                                           double* __restrict__ part) {
+  __shared__ double sh[kMdThreads / 32];
+  double acc = 0.0;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const double w = dtf * minv[i];
+    double s2 = 0.0;
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+      const double vv = (v[3 * i + c] + w * f[3 * i + c]) * sv;
+      v[3 * i + c] = vv;
+      s2 += vv * vv;
+    }
+    acc += mass[i] * s2;
+  }
+  acc = warp_sum(acc);
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double b = 0.0;
+    for (int w = 0; w < kMdThreads / 32; ++w) b += sh[w];
+    part[blockIdx.x] = b;
+  }
+}
+
+__global__ void k_md_scale_by(int n, double* __restrict__ v, double s) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < 3 * n; i += gridDim.x * blockDim.x) v[i] *= s;
+}
+
+// Host Nose-Hoover chain (same recurrence as k_md_chain) for the NPT path.
+struct HostChain {
+  int M = 0;
+  double eta[kMaxChain] = {0}, eta_dot[kMaxChain + 1] = {0}, eta_dotdot[kMaxChain] = {0}, mass[kMaxChain] = {0};
+  void init(int m, double q0, double qi, double boltz_t) {
+    M = m;
+    mass[0] = q0;
+    for (int i = 1; i < M; ++i) mass[i] = qi;
+    for (int i = 1; i < M; ++i) eta_dotdot[i] = (mass[i - 1] * eta_dot[i - 1] * eta_dot[i - 1] - boltz_t) / mass[i];
+  }
+  // Thermostat half-step for kinetic energy `ke` (target ke_target); returns the velocity factor.
+  double thermostat(double& t_current, double dof_boltz, double ke_target, double boltz_t, double dt) {
+    const double dt4 = 0.25 * dt, dt8 = 0.125 * dt, dthalf = 0.5 * dt;
+    eta_dotdot[0] = (dof_boltz * t_current - ke_target) / mass[0];
+    double expfac = 1.0;
+    for (int i = M - 1; i > 0; --i) {
+      expfac = std::exp(-dt8 * eta_dot[i + 1]);
+      eta_dot[i] = (eta_dot[i] * expfac + eta_dotdot[i] * dt4) * expfac;
+    }
+    expfac = std::exp(-dt8 * eta_dot[1]);
+    eta_dot[0] = (eta_dot[0] * expfac + eta_dotdot[0] * dt4) * expfac;
+    const double factor = std::exp(-dthalf * eta_dot[0]);
+    t_current *= factor * factor;
+    eta_dotdot[0] = (dof_boltz * t_current - ke_target) / mass[0];
+    for (int i = 0; i < M; ++i) eta[i] += dthalf * eta_dot[i];
+    eta_dot[0] = (eta_dot[0] * expfac + eta_dotdot[0] * dt4) * expfac;
+    for (int i = 1; i < M; ++i) {
+      expfac = std::exp(-dt8 * eta_dot[i + 1]);
+      eta_dotdot[i] = (mass[i - 1] * eta_dot[i - 1] * eta_dot[i - 1] - boltz_t) / mass[i];
+      eta_dot[i] = (eta_dot[i] * expfac + eta_dotdot[i] * dt4) * expfac;
+    }
+    return factor;
+  }
+  // Barostat-chain half-step (FixNH::nhc_press_integrate, isotropic): scales
+  // omega_dot; kinetic energy 3 W omega_dot^2 against kB T0.
+  void barostat(double& omega_dot, double w_mass, double kt, double dt) {
+    const double dt4 = 0.25 * dt, dt8 = 0.125 * dt, dthalf = 0.5 * dt;
+    double ke = 3.0 * w_mass * omega_dot * omega_dot;
+    eta_dotdot[0] = (ke - kt) / mass[0];
+    double expfac = 1.0;
+    for (int i = M - 1; i > 0; --i) {
+      expfac = std::exp(-dt8 * eta_dot[i + 1]);
+      eta_dot[i] = (eta_dot[i] * expfac + eta_dotdot[i] * dt4) * expfac;
+    }
+    expfac = std::exp(-dt8 * eta_dot[1]);
+    eta_dot[0] = (eta_dot[0] * expfac + eta_dotdot[0] * dt4) * expfac;
+    for (int i = 0; i < M; ++i) eta[i] += dthalf * eta_dot[i];
+    omega_dot *= std::exp(-dthalf * eta_dot[0]);
+    ke = 3.0 * w_mass * omega_dot * omega_dot;
+    eta_dotdot[0] = (ke - kt) / mass[0];
+    eta_dot[0] = (eta_dot[0] * expfac + eta_dotdot[0] * dt4) * expfac;
+    for (int i = 1; i < M; ++i) {
+      expfac = std::exp(-dt8 * eta_dot[i + 1]);
+      eta_dotdot[i] = (mass[i - 1] * eta_dot[i - 1] * eta_dot[i - 1] - kt) / mass[i];
+      eta_dot[i] = (eta_dot[i] * expfac + eta_dotdot[i] * dt4) * expfac;
+    }
+  }
+  double energy(double first_kt, double kt) const {
+    double e = first_kt * eta[0];
+    for (int i = 1; i < M; ++i) e += kt * eta[i];
+    for (int i = 0; i < M; ++i) e += 0.5 * mass[i] * eta_dot[i] * eta_dot[i];
+    return e;
+  }
+};
+
 template <class T>
 struct Dev {
   T* p = nullptr;
@@ -200,6 +326,9 @@ struct b200dp_md {
   Dev<int> atype;
   Dev<Chain> chain;
   ChainParams cp{};
+  // NPT (host-side scalars)
+  HostChain tch, pch;
+  double omega_dot = 0, w_mass = 0, vol0 = 0, t_current = 0, vir_trace = 0, epot = 0;
   std::string err;
 };
 
@@ -213,6 +342,9 @@ b200dp_status b200dp_md_params_default(b200dp_md_params* p) {
   p->chain = 3;
   p->t_target = 300.0;
   p->t_damp = 0.05;  // 100 steps of 0.5 fs
+  p->p_target = 1.0;
+  p->p_damp = 0.5;
+  p->pchain = 3;
   return B200DP_OK;
 }
 
@@ -221,9 +353,14 @@ b200dp_status b200dp_md_create(b200dp_engine* engine, int natoms, const double* 
                                b200dp_md** out) {
   if (!engine || !out || natoms <= 0 || !coord || !atype || !box || !params) return B200DP_ERR_INVALID;
   const b200dp_md_params& p = *params;
-  if (!(p.dt > 0) || (p.ensemble != B200DP_MD_NVE && p.ensemble != B200DP_MD_NVT)) return B200DP_ERR_INVALID;
-  if (p.ensemble == B200DP_MD_NVT && (p.chain < 1 || p.chain > kMaxChain || !(p.t_target > 0) || !(p.t_damp > 0)))
+  if (!(p.dt > 0) || (p.ensemble != B200DP_MD_NVE && p.ensemble != B200DP_MD_NVT && p.ensemble != B200DP_MD_NPT))
     return B200DP_ERR_INVALID;
+  if (p.ensemble != B200DP_MD_NVE && (p.chain < 1 || p.chain > kMaxChain || !(p.t_target > 0) || !(p.t_damp > 0)))
+    return B200DP_ERR_INVALID;
+  if (p.ensemble == B200DP_MD_NPT &&
+      (p.pchain < 1 || p.pchain > kMaxChain || !(p.p_damp > 0) || box[1] != 0 || box[2] != 0 || box[3] != 0 ||
+       box[5] != 0 || box[6] != 0 || box[7] != 0))
+    return B200DP_ERR_INVALID;  // isotropic barostat on an orthorhombic box
   if (!vel && !(p.t_init > 0)) return B200DP_ERR_INVALID;
   b200dp_model_info info;
   if (b200dp_model_info_get(engine, &info) != B200DP_OK) return B200DP_ERR_INVALID;
@@ -276,7 +413,7 @@ b200dp_status b200dp_md_create(b200dp_engine* engine, int natoms, const double* 
   std::memset(&ch, 0, sizeof(ch));
   ch.factor = 1.0;
   ch.t_current = mv2 * kMvv2e / (md->dof * kBoltz);
-  if (p.ensemble == B200DP_MD_NVT) {
+  if (p.ensemble != B200DP_MD_NVE) {
     const double w = 1.0 / p.t_damp;
     cp.M = p.chain;
     cp.dof_boltz = md->dof * kBoltz;
@@ -320,6 +457,15 @@ b200dp_status b200dp_md_create(b200dp_engine* engine, int natoms, const double* 
     delete md;
     return B200DP_ERR_CUDA;
   }
+  if (p.ensemble == B200DP_MD_NPT) {
+    const double w = 1.0 / p.t_damp, wp = 1.0 / p.p_damp, kt = kBoltz * p.t_target;
+    md->tch.init(p.chain, cp.mass[0], p.chain > 1 ? cp.mass[1] : 0.0, cp.boltz_t);
+    md->pch.init(p.pchain, kt / (wp * wp), kt / (wp * wp), kt);
+    md->w_mass = (natoms + 1) * kt / (wp * wp);
+    md->vol0 = md->volume;
+    md->t_current = ch.t_current;
+    (void)w;
+  }
   // forces of the initial configuration
   const b200dp_status rc = b200dp_compute_device(engine, md->stream, natoms, 0, md->x.p, md->atype.p, md->box, nullptr,
                                                  md->e.p, md->f.p, md->vir.p, nullptr, nullptr);
@@ -334,8 +480,76 @@ b200dp_status b200dp_md_create(b200dp_engine* engine, int natoms, const double* 
   return cudaGetLastError() == cudaSuccess ? B200DP_OK : B200DP_ERR_CUDA;
 }
 
+// One NPT step (host-side scalars, device kernels), LAMMPS fix npt iso order.
+static b200dp_status npt_step(b200dp_md* md, int grid) {
+  const int n = md->n;
+  const double dt = md->p.dt, dthalf = 0.5 * dt, dtf = 0.5 * dt * kFtm2v;
+  const double kt = kBoltz * md->p.t_target, dof_boltz = md->dof * kBoltz;
+  const double ke_target = dof_boltz * md->p.t_target, p_hydro = md->p.p_target;
+  cudaStream_t st = md->stream;
+  auto omega_force = [&](double t_cur, double vir_tr) {
+    const double vol = md->box[0] * md->box[4] * md->box[8];
+    const double p_cur = (dof_boltz * t_cur + vir_tr) / (3.0 * vol) * kNktv2p;
+    const double mtk1 = dof_boltz * t_cur / (3.0 * md->n);
+    md->omega_dot += ((p_cur - p_hydro) * vol / (md->w_mass * kNktv2p) + mtk1 / md->w_mass) * dthalf;
+  };
+  // ---- initial half
+  md->pch.barostat(md->omega_dot, md->w_mass, kt, dt);
+  const double s_t = md->tch.thermostat(md->t_current, dof_boltz, ke_target, kt, dt);
+  omega_force(md->t_current, md->vir_trace);
+  const double mtk2 = 3.0 * md->omega_dot / (3.0 * md->n);
+  const double fp = std::exp(-0.25 * dt * (md->omega_dot + mtk2));
+  const double e = std::exp(dthalf * md->omega_dot);
+  count_launch();
+  k_npt_first<<<grid, kMdThreads, 0, st>>>(n, md->x.p, md->v.p, md->f.p, md->minv.p, s_t * fp * fp, dtf, dt, e);
+  for (int d = 0; d < 3; ++d) md->box[4 * d] *= e * e;
+  md->volume = md->box[0] * md->box[4] * md->box[8];
+  b200dp_status rc = b200dp_compute_device(md->engine, st, n, 0, md->x.p, md->atype.p, md->box, nullptr, md->e.p,
+                                           md->f.p, md->vir.p, nullptr, nullptr);
+  if (rc != B200DP_OK) return rc;
+  // ---- final half
+  count_launch();
+  k_npt_second<<<kRedBlocks, kMdThreads, 0, st>>>(n, md->v.p, md->f.p, md->minv.p, md->mass.p, dtf, fp * fp,
+                                                  md->part.p);
+  double part[kRedBlocks], vir[9], epot = 0;
+  if (cudaMemcpyAsync(part, md->part.p, sizeof(part), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaMemcpyAsync(vir, md->vir.p, sizeof(vir), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaMemcpyAsync(&epot, md->e.p, sizeof(double), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return B200DP_ERR_CUDA;
+  double mv2 = 0;
+  for (int k = 0; k < kRedBlocks; ++k) mv2 += part[k];
+  md->t_current = mv2 * kMvv2e / dof_boltz;
+  md->vir_trace = vir[0] + vir[4] + vir[8];
+  md->epot = epot;
+  omega_force(md->t_current, md->vir_trace);
+  const double s_t2 = md->tch.thermostat(md->t_current, dof_boltz, ke_target, kt, dt);
+  count_launch();
+  k_md_scale_by<<<grid, kMdThreads, 0, st>>>(n, md->v.p, s_t2);
+  md->pch.barostat(md->omega_dot, md->w_mass, kt, dt);
+  count_launch();
+  k_md_ke<<<kRedBlocks, kMdThreads, 0, st>>>(n, md->v.p, md->mass.p, md->part.p);
+  return cudaGetLastError() == cudaSuccess ? B200DP_OK : B200DP_ERR_CUDA;
+}
+
 b200dp_status b200dp_md_run(b200dp_md* md, int nsteps) {
   if (!md || nsteps < 0) return B200DP_ERR_INVALID;
+  if (md->ensemble == B200DP_MD_NPT) {
+    const int grid = std::min(kRedBlocks * 4, (md->n + kMdThreads - 1) / kMdThreads);
+    if (md->step == 0 && md->vir_trace == 0) {  // virial of the initial forces (computed at creation)
+      double vir[9];
+      if (cudaMemcpyAsync(vir, md->vir.p, sizeof(vir), cudaMemcpyDeviceToHost, md->stream) != cudaSuccess ||
+          cudaStreamSynchronize(md->stream) != cudaSuccess)
+        return B200DP_ERR_CUDA;
+      md->vir_trace = vir[0] + vir[4] + vir[8];
+    }
+    for (int s = 0; s < nsteps; ++s) {
+      const b200dp_status rc = npt_step(md, grid);
+      if (rc != B200DP_OK) return rc;
+      ++md->step;
+    }
+    return B200DP_OK;
+  }
   const int n = md->n;
   const double dtf = 0.5 * md->p.dt * kFtm2v, dt = md->p.dt;
   const int grid = std::min(kRedBlocks * 4, (n + kMdThreads - 1) / kMdThreads);
@@ -384,7 +598,11 @@ b200dp_status b200dp_md_thermo(b200dp_md* md, double* thermo) {
   const double ke = 0.5 * mv2 * kMvv2e;
   const double temp = 2.0 * ke / (md->dof * kBoltz);
   double e_chain = 0;
-  if (md->ensemble == B200DP_MD_NVT) {
+  if (md->ensemble == B200DP_MD_NPT) {
+    const double kt = kBoltz * md->p.t_target;
+    e_chain = md->tch.energy(md->cp.ke_target, kt) + md->pch.energy(kt, kt) +
+              1.5 * md->w_mass * md->omega_dot * md->omega_dot + md->p.p_target * (md->volume - md->vol0) / kNktv2p;
+  } else if (md->ensemble == B200DP_MD_NVT) {
     const ChainParams& cp = md->cp;
     e_chain = cp.ke_target * ch.eta[0];
     for (int i = 1; i < cp.M; ++i) e_chain += cp.boltz_t * ch.eta[i];

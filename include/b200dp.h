@@ -210,16 +210,18 @@ int b200dp_direct_energy_force(const int64_t* atype, const int64_t* row_ptr, con
 
 /* ------------------------------------------------------------------ MD
  * Molecular-dynamics driver around an engine (metal units: Angstrom, ps,
- * g/mol, eV, K, bar).  Velocity Verlet (NVE) or velocity Verlet with a
- * Nose-Hoover chain thermostat (NVT) in the integration order of LAMMPS'
- * fix nve / fix nvt, which drives the reference's force call
+ * g/mol, eV, K, bar).  Velocity Verlet (NVE), with a Nose-Hoover chain
+ * thermostat (NVT), or with the thermostat and an isotropic
+ * Martyna-Tobias-Klein barostat with its own chain (NPT, orthorhombic box
+ * scaled about the origin), in the integration order of LAMMPS'
+ * fix nve / fix nvt / fix npt iso, which drives the reference's force call
  * (components/lammps/overlays/src/KOKKOS/fix_nh_kokkos.cpp:863-1001; device
  * chain: components/lammps/overlays/src/KOKKOS/dpa_fast_step_kokkos.h:307-400).
  * Positions, velocities, forces and the chain state stay on the device; a
  * run enqueues its steps on the driver's stream without host
- * synchronisation.  The box is fixed and periodic; positions are not
- * wrapped (the engine images them). */
-typedef enum b200dp_md_ensemble { B200DP_MD_NVE = 0, B200DP_MD_NVT = 1 } b200dp_md_ensemble;
+ * synchronisation (NPT reads 12 numbers back per step for the barostat).
+ * The box is periodic; positions are not wrapped (the engine images them). */
+typedef enum b200dp_md_ensemble { B200DP_MD_NVE = 0, B200DP_MD_NVT = 1, B200DP_MD_NPT = 2 } b200dp_md_ensemble;
 
 typedef struct b200dp_md_params {
   double dt;        /* time step, ps (default 0.0005) */
@@ -230,7 +232,10 @@ typedef struct b200dp_md_params {
   double t_init;    /* K: > 0 draws seeded Gaussian velocities at this temperature (zero momentum) */
   unsigned long long seed;
   double mass[8];   /* g/mol per atom type */
-  int reserved[16];
+  double p_target;  /* bar (NPT, isotropic) */
+  double p_damp;    /* barostat period, ps (NPT, default 0.5) */
+  int pchain;       /* barostat Nose-Hoover chain length (NPT, 1..8, default 3) */
+  int reserved[11];
 } b200dp_md_params;
 
 typedef struct b200dp_md b200dp_md;

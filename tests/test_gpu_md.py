@@ -108,3 +108,53 @@ def test_deterministic_and_seeded_start(model_dir):
     for a, b in zip(*runs):
         assert np.array_equal(a, b)
     dp.close()
+
+
+def test_npt_matches_reference(model_dir):
+    """fix npt iso: positions, velocities and box after 20 steps against the numpy restatement."""
+    from md_reference import run_npt
+
+    model = str(model_dir / "cu.b2dp")
+    s = systems.fcc(3, name="cu_108")
+    m = np.full(s.natoms, 63.546)
+    rng = np.random.default_rng(9)
+    v0 = rng.normal(size=(s.natoms, 3)) * np.sqrt(BOLTZ * 800.0 / (m[:, None] * MVV2E))
+    v0 -= v0.mean(0)
+    dt, nsteps = 0.001, 20
+    dp = b200dp.DeepPot(model, precision=b200dp.FP64)
+    md = b200dp.MD(dp, s.coord, s.atype, s.box, [63.546], dt=dt, ensemble=b200dp.NPT, vel=v0, t_target=800.0,
+                   t_damp=0.1, p_target=1.0, p_damp=0.2)
+    md.run(nsteps)
+    x, v, _ = md.state()
+    th = md.thermo()
+    o = oracle.Oracle(model)
+
+    def force(xx, box):
+        r = o.compute(xx, s.atype, box, atomic=False)
+        return r["energy"], r["force"], r["virial"]
+
+    xr, vr, boxr, er = run_npt(s.coord, v0, m, force, s.box, dt, nsteps, 800.0, 0.1, 3, 1.0, 0.2, 3)
+    assert abs(th["volume"] - np.prod(np.diag(boxr))) < 1e-9 * th["volume"]
+    assert np.abs(x - xr).max() < 1e-8
+    assert np.abs(v - vr).max() < 1e-7 * np.abs(vr).max()
+    assert abs(th["pe"] - er) < 1e-8 * abs(er)
+    md.close()
+    dp.close()
+
+
+def test_npt_conserved_energy(model_dir):
+    s = systems.fcc(3, name="cu_108")
+    m = np.full(s.natoms, 63.546)
+    rng = np.random.default_rng(10)
+    v0 = rng.normal(size=(s.natoms, 3)) * np.sqrt(BOLTZ * 800.0 / (m[:, None] * MVV2E))
+    v0 -= v0.mean(0)
+    dp = b200dp.DeepPot(str(model_dir / "cu.b2dp"), precision=b200dp.FP64)
+    md = b200dp.MD(dp, s.coord, s.atype, s.box, [63.546], dt=0.001, ensemble=b200dp.NPT, vel=v0, t_target=800.0,
+                   t_damp=0.1, p_target=1.0, p_damp=0.5)
+    e0 = md.thermo()["conserved"]
+    md.run(300)
+    th = md.thermo()
+    assert abs(th["conserved"] - e0) < 0.02 * BOLTZ * 800.0 * s.natoms / 100, th["conserved"] - e0
+    assert th["volume"] > 0
+    md.close()
+    dp.close()
