@@ -222,6 +222,10 @@ b200dp_status Engine::init(const char* path, const b200dp_options* o) {
     }
   }
   cap = std::max(256, ((2 * s.selt + 31) / 32) * 32);
+  if (format_smem_bytes(cap) > 200 * 1024) {
+    err = "neighbour selection too large for the list-format kernel";
+    return B200DP_ERR_UNSUPPORTED;
+  }
   B200DP_CUDA_TRY(cudaStreamCreateWithFlags(&own_stream, cudaStreamNonBlocking));
   for (auto& ev : events) B200DP_CUDA_TRY(cudaEventCreate(&ev));
   B200DP_CUDA_TRY(err_buf.ensure(sizeof(int) * kErrCount));
@@ -239,7 +243,7 @@ b200dp_status Engine::init(const char* path, const b200dp_options* o) {
 }
 
 void Engine::release() {
-  for (DevBuf* b : {&w_emb, &w_embT, &xw, &cell_of, &cell_count, &cell_start, &cell_cursor, &cell_atoms, &nl_j,
+  for (DevBuf* b : {&w_emb, &w_embT, &xw, &cell_of, &cell_count, &cell_start, &cell_cursor, &cell_rec, &nl_j,
                     &nl_code, &nl_rij, &nl_cnt, &rev_count, &rev_start, &rev_cursor, &rev_tmp, &rev_slot,
                     &blk_counts, &type_start, &perm_pos, &perm_atom, &Tbuf, &Dbuf, &dDbuf, &atom_e, &gslot,
                     &vrows, &err_buf, &reduce_part, &scalars, &h_coord, &h_atype, &h_force, &h_aviral, &h_ae,
@@ -275,7 +279,7 @@ b200dp_status Engine::ensure_buffers(int nloc, int nall, int ncells, int ncand) 
   B200DP_CUDA_TRY(cell_count.ensure(sizeof(int) * C));
   B200DP_CUDA_TRY(cell_start.ensure(sizeof(int) * (C + 1)));
   B200DP_CUDA_TRY(cell_cursor.ensure(sizeof(int) * C));
-  B200DP_CUDA_TRY(cell_atoms.ensure(sizeof(int) * A));
+  B200DP_CUDA_TRY(cell_rec.ensure(sizeof(CellRec) * A));
   B200DP_CUDA_TRY(nl_j.ensure(sizeof(int) * S));
   B200DP_CUDA_TRY(nl_code.ensure(sizeof(int) * S));
   B200DP_CUDA_TRY(nl_rij.ensure(sizeof(double) * 3 * S));
@@ -346,61 +350,19 @@ b200dp_status Engine::ensure_buffers(int nloc, int nall, int ncells, int ncand) 
 }
 
 // Grid set-up on the host: cell counts and stencil reach from the box (periodic)
-// or the region (open).  Cells are at least rcut wide in every direction.
+// or the region (open).
 b200dp_status Engine::make_grid(int nall, const double* box, const double* region, bool periodic, GridSpec& g) {
-  std::memset(&g, 0, sizeof(g));
-  const double rc = hm.rcut;
   const long long max_cells = std::max<long long>(4096, 4LL * nall);
-  g.periodic = periodic ? 1 : 0;
-  if (periodic) {
-    double width[3];
-    for (int k = 0; k < 9; ++k) g.B[k] = box[k];
-    make_box_inverse(box, g.Binv, width);
-    for (int d = 0; d < 3; ++d)
-      if (!(width[d] > 0) || !std::isfinite(width[d])) {
-        err = "degenerate box";
-        return B200DP_ERR_INVALID;
-      }
-    double scale = 1.0;
-    for (;;) {
-      long long tot = 1;
-      for (int d = 0; d < 3; ++d) {
-        g.n[d] = std::max(1, (int)std::floor(width[d] / (rc * scale)));
-        tot *= g.n[d];
-      }
-      if (tot <= max_cells) break;
-      scale *= 1.25;
-    }
-    for (int d = 0; d < 3; ++d) {
-      g.reach[d] = (int)std::ceil(rc * g.n[d] / width[d] * (1.0 + 1e-12));
-      if (2 * g.reach[d] + 1 > 32) {
-        err = "box narrower than rcut/15 along a cell vector";
-        return B200DP_ERR_UNSUPPORTED;
-      }
-    }
-  } else {
-    double scale = 1.0;
-    double ext[3];
-    for (int d = 0; d < 3; ++d) {
-      g.lo[d] = region[d];
-      ext[d] = std::max(region[3 + d] - region[d], 1e-9);
-    }
-    for (;;) {
-      long long tot = 1;
-      for (int d = 0; d < 3; ++d) {
-        g.n[d] = std::max(1, (int)std::floor(ext[d] / (rc * scale)));
-        tot *= g.n[d];
-      }
-      if (tot <= max_cells) break;
-      scale *= 1.25;
-    }
-    for (int d = 0; d < 3; ++d) {
-      g.inv_h[d] = g.n[d] / ext[d];
-      g.reach[d] = 1;
-    }
+  switch (b200dp::make_grid(periodic, box, region, hm.rcut, max_cells, g)) {
+    case 0:
+      return B200DP_OK;
+    case 1:
+      err = "degenerate box";
+      return B200DP_ERR_INVALID;
+    default:
+      err = "box narrower than rcut/15 along a cell vector";
+      return B200DP_ERR_UNSUPPORTED;
   }
-  g.ncells = g.n[0] * g.n[1] * g.n[2];
-  return B200DP_OK;
 }
 
 void Engine::mark(cudaStream_t st, int k) {
@@ -594,9 +556,11 @@ b200dp_status Engine::compute_device(cudaStream_t st, int nloc, int nghost, cons
   B200DP_CUDA_TRY(cudaMemsetAsync(cell_cursor.ptr, 0, sizeof(int) * g.ncells, st));
   launch_bin(st, nall, d_coord, g, xw.as<double>(), cell_of.as<int>(), cell_count.as<int>());
   launch_exclusive_scan(st, g.ncells, cell_count.as<int>(), cell_start.as<int>(), scan_scratch.as<int>());
-  launch_fill_cells(st, nall, cell_of.as<int>(), cell_start.as<int>(), cell_cursor.as<int>(), cell_atoms.as<int>());
-  launch_format(st, format_spec(nloc, nall), g, xw.as<double>(), d_atype, cell_of.as<int>(), cell_start.as<int>(),
-                cell_atoms.as<int>(), nl_j.as<int>(), nl_code.as<int>(), nl_rij.as<double>(), nl_cnt.as<int>(), err_d);
+  launch_fill_cells(st, nall, xw.as<double>(), d_atype, cell_of.as<int>(), cell_start.as<int>(),
+                    cell_cursor.as<int>(), cell_rec.as<CellRec>());
+  launch_format(st, format_spec(nloc, nall), g, xw.as<double>(), cell_of.as<int>(), cell_start.as<int>(),
+                cell_rec.as<CellRec>(), nl_j.as<int>(), nl_code.as<int>(), nl_rij.as<double>(), nl_cnt.as<int>(),
+                err_d);
   B200DP_CUDA_TRY(cudaGetLastError());
   rc = (opt.precision == B200DP_FP64)
            ? run_model<double>(st, nloc, nall, d_atype, d_force, d_atom_energy, d_atom_virial, d_energy, d_virial)

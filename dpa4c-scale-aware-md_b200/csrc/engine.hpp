@@ -46,7 +46,7 @@ struct Engine {
   std::vector<double> fit_bo;                     // output bias + bias_atom_e per type
 
   // neighbour graph
-  DevBuf xw, cell_of, cell_count, cell_start, cell_cursor, cell_atoms;
+  DevBuf xw, cell_of, cell_count, cell_start, cell_cursor, cell_rec;
   DevBuf nl_j, nl_code, nl_rij, nl_cnt;
   DevBuf rev_count, rev_start, rev_cursor, rev_tmp, rev_slot;
   DevBuf blk_counts, type_start, perm_pos, perm_atom;

@@ -1,5 +1,7 @@
 // Neighbour-graph builder kernels (see nlist.cuh).
+#include <algorithm>
 #include <cmath>
+#include <cstring>
 
 #include "nlist.cuh"
 
@@ -36,6 +38,47 @@ void make_box_inverse(const double* box, double* Binv, double* width) {
     double x = u[1] * v[2] - u[2] * v[1], y = u[2] * v[0] - u[0] * v[2], z = u[0] * v[1] - u[1] * v[0];
     width[d] = vol / std::sqrt(x * x + y * y + z * z);
   }
+}
+
+int make_grid(bool periodic, const double* box, const double* region, double rcut, long long max_cells, GridSpec& g) {
+  std::memset(&g, 0, sizeof(g));
+  g.periodic = periodic ? 1 : 0;
+  double width[3], ext[3];
+  if (periodic) {
+    for (int k = 0; k < 9; ++k) g.B[k] = box[k];
+    make_box_inverse(box, g.Binv, width);
+    for (int d = 0; d < 3; ++d)
+      if (!(width[d] > 0) || !std::isfinite(width[d])) return 1;
+  } else {
+    for (int d = 0; d < 3; ++d) {
+      g.lo[d] = region[d];
+      ext[d] = std::max(region[3 + d] - region[d], 1e-9);
+      width[d] = ext[d];
+    }
+  }
+  double scale = 1.0;
+  for (;;) {
+    long long tot = 1;
+    for (int d = 0; d < 3; ++d) {
+      g.n[d] = std::max(1, (int)std::floor(width[d] * kCellsPerCut / (rcut * scale)));
+      tot *= g.n[d];
+    }
+    if (tot <= max_cells) break;
+    scale *= 1.25;
+  }
+  for (int d = 0; d < 3; ++d) {
+    // cells are width / n wide; reach = ceil(rcut / cell width)
+    g.reach[d] = (int)std::ceil(rcut * g.n[d] / width[d] * (1.0 + 1e-12));
+    if (!periodic) {
+      // open grid: atoms outside the region are clamped into the edge cells,
+      // and nothing lies beyond the grid
+      g.inv_h[d] = g.n[d] / ext[d];
+      g.reach[d] = std::min(g.reach[d], g.n[d] - 1);
+    }
+    if (2 * g.reach[d] + 1 > 31) return 2;
+  }
+  g.ncells = g.n[0] * g.n[1] * g.n[2];
+  return 0;
 }
 
 // ---------------------------------------------------------------- binning
@@ -197,19 +240,28 @@ void launch_exclusive_scan(cudaStream_t st, int n, const int* in, int* out, int*
   k_scan_tile_apply<<<nb, 1024, 0, st>>>(n, in, offs, out);
 }
 
-__global__ void k_fill_cells(int nall, const int* __restrict__ cell_of, const int* __restrict__ cell_start,
-                             int* __restrict__ cursor, int* __restrict__ cell_atoms) {
+// Order within a cell follows the atomics and is not fixed; the list kernel's
+// ranking does not depend on it.
+__global__ void k_fill_cells(int nall, const double* __restrict__ xw, const int* __restrict__ atype,
+                             const int* __restrict__ cell_of, const int* __restrict__ cell_start,
+                             int* __restrict__ cursor, CellRec* __restrict__ cell_rec) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= nall) return;
   const int c = cell_of[i];
-  cell_atoms[cell_start[c] + atomicAdd(cursor + c, 1)] = i;
+  CellRec r;
+  r.x = xw[3 * i];
+  r.y = xw[3 * i + 1];
+  r.z = xw[3 * i + 2];
+  r.j = i;
+  r.t = atype[i];
+  cell_rec[cell_start[c] + atomicAdd(cursor + c, 1)] = r;
 }
 
-void launch_fill_cells(cudaStream_t st, int nall, const int* cell_of, const int* cell_start, int* cursor,
-                       int* cell_atoms) {
+void launch_fill_cells(cudaStream_t st, int nall, const double* xw, const int* atype, const int* cell_of,
+                       const int* cell_start, int* cursor, CellRec* cell_rec) {
   if (nall <= 0) return;
   count_launch();
-  k_fill_cells<<<(nall + 255) / 256, 256, 0, st>>>(nall, cell_of, cell_start, cursor, cell_atoms);
+  k_fill_cells<<<(nall + 255) / 256, 256, 0, st>>>(nall, xw, atype, cell_of, cell_start, cursor, cell_rec);
 }
 
 // ---------------------------------------------------------------- format
@@ -217,29 +269,33 @@ constexpr int kFmtWarps = 4;
 
 __device__ __forceinline__ int floor_div(int a, int n) { return a >= 0 ? a / n : -((-a + n - 1) / n); }
 
-size_t format_smem_bytes(int cap) {
-  // per warp: r2 (8) + r (24) + j, code, type, type-grouped index (16) bytes per candidate
-  return (size_t)kFmtWarps * cap * 48;
-}
+// per warp and candidate: r2 (8) + r (24) + grouped r2 (8) + j, code, type,
+// type-grouped index (16) bytes, plus one rank bit per candidate
+__host__ __device__ constexpr size_t cand_bytes(int cap) { return (size_t)cap * 56 + ((size_t)cap / 32 + 1) * 4; }
+size_t format_smem_bytes(int cap) { return (size_t)kFmtWarps * ((cand_bytes(cap) + 15) / 16 * 16); }
 
 struct CandBuf {
   double* r2;
-  double* r;  // [cap][3]
+  double* r;    // [cap][3]
+  double* r2g;  // r2 in type-grouped order
   int* j;
   int* code;
   int* t;
-  int* grp;  // candidate indices grouped by type, stable within a type
+  int* grp;        // candidate indices grouped by type, stable within a type
+  unsigned* seen;  // rank bitmap (tie detection)
 };
 
 __device__ __forceinline__ CandBuf cand_buf(unsigned char* smem, int warp, int cap) {
-  unsigned char* base = smem + (size_t)warp * cap * 48;
+  unsigned char* base = smem + (size_t)warp * ((cand_bytes(cap) + 15) / 16 * 16);
   CandBuf b;
   b.r2 = reinterpret_cast<double*>(base);
   b.r = b.r2 + cap;
-  b.j = reinterpret_cast<int*>(b.r + 3 * cap);
+  b.r2g = b.r + 3 * cap;
+  b.j = reinterpret_cast<int*>(b.r2g + cap);
   b.code = b.j + cap;
   b.t = b.code + cap;
   b.grp = b.t + cap;
+  b.seen = reinterpret_cast<unsigned*>(b.grp + cap);
   return b;
 }
 
@@ -275,29 +331,62 @@ __device__ void emit_row(const FormatSpec& f, int i, const CandBuf& b, int ncand
     }
   }
   __syncwarp();
-  for (int c = lane; c < ncand; c += 32) {
-    const int t = b.t[c];
-    const double r2 = b.r2[c];
-    const int j = b.j[c], code = b.code[c];
-    int rank = 0;
-    for (int k = toff[t]; k < toff[t + 1]; ++k) {
-      const int c2 = b.grp[k];
-      const double q = b.r2[c2];
-      if (q < r2) {
-        ++rank;
-      } else if (q == r2 && c2 != c) {
-        const int j2 = b.j[c2];
-        rank += (j2 < j || (j2 == j && b.code[c2] < code));
+  // Rank within each type.  r^2 alone decides almost always: count smaller r^2
+  // in the grouped copy (warp-uniform broadcast reads); two members landing on
+  // the same rank reveal a tie, and only then is the type re-ranked with the
+  // full key (r^2, j, image).
+  for (int k = lane; k < ncand; k += 32) b.r2g[k] = b.r2[b.grp[k]];
+  for (int t = 0; t < f.ntypes; ++t) {
+    const int k0 = toff[t], k1 = toff[t + 1], nt = k1 - k0;
+    if (nt == 0) continue;
+    for (int w = lane; w <= nt / 32; w += 32) b.seen[w] = 0u;
+    __syncwarp();
+    bool tie = false;
+    for (int base = k0; base < k1; base += 64) {
+      const int ma = base + lane, mb = base + 32 + lane;
+      const double ra = ma < k1 ? b.r2g[ma] : 0.0, rb = mb < k1 ? b.r2g[mb] : 0.0;
+      int ka = 0, kb = 0;
+      for (int k = k0; k < k1; ++k) {
+        const double q = b.r2g[k];
+        ka += (q < ra);
+        kb += (q < rb);
+      }
+      if (ma < k1) tie |= (atomicOr(&b.seen[ka >> 5], 1u << (ka & 31)) >> (ka & 31)) & 1u;
+      if (mb < k1) tie |= (atomicOr(&b.seen[kb >> 5], 1u << (kb & 31)) >> (kb & 31)) & 1u;
+      // provisional ranks, final unless a tie shows up
+      if (ma < k1) b.t[b.grp[ma]] = t + (ka << 4);
+      if (mb < k1) b.t[b.grp[mb]] = t + (kb << 4);
+    }
+    tie = __any_sync(0xffffffffu, tie);
+    __syncwarp();
+    for (int m = k0 + lane; m < k1; m += 32) {
+      const int c = b.grp[m];
+      int rank = b.t[c] >> 4;
+      if (tie) {  // full key (r^2, j, image)
+        const double r2 = b.r2[c];
+        const int j = b.j[c], code = b.code[c];
+        rank = 0;
+        for (int k = k0; k < k1; ++k) {
+          const int c2 = b.grp[k];
+          const double q = b.r2[c2];
+          if (q < r2) {
+            ++rank;
+          } else if (q == r2 && c2 != c) {
+            const int j2 = b.j[c2];
+            rank += (j2 < j || (j2 == j && b.code[c2] < code));
+          }
+        }
+      }
+      if (rank < f.sel[t]) {
+        const size_t slot = (size_t)i * f.selt + f.off[t] + rank;
+        nl_j[slot] = b.j[c];
+        nl_code[slot] = b.code[c];
+        nl_rij[3 * slot] = b.r[3 * c];
+        nl_rij[3 * slot + 1] = b.r[3 * c + 1];
+        nl_rij[3 * slot + 2] = b.r[3 * c + 2];
       }
     }
-    if (rank < f.sel[t]) {
-      const size_t slot = (size_t)i * f.selt + f.off[t] + rank;
-      nl_j[slot] = j;
-      nl_code[slot] = code;
-      nl_rij[3 * slot] = b.r[3 * c];
-      nl_rij[3 * slot + 1] = b.r[3 * c + 1];
-      nl_rij[3 * slot + 2] = b.r[3 * c + 2];
-    }
+    __syncwarp();
   }
   for (int t = 0; t < f.ntypes; ++t) {
     const int nt = tcnt[t];
@@ -318,92 +407,129 @@ __device__ void emit_row(const FormatSpec& f, int i, const CandBuf& b, int ncand
   }
 }
 
+// Stencil cells handled per pass: kStencilPerLane consecutive cells per lane.
+constexpr int kStencilPerLane = 4;
+constexpr int kStencilChunk = 32 * kStencilPerLane;
+constexpr int kGatherBatch = 4;  // candidate records loaded per lane before any is used
+
+// One warp per centre.  The stencil (every cell within reach, periodic images
+// included) is flattened; a warp scan over the cells' atom counts numbers the
+// candidates, and each lane takes every 32nd candidate, finds its cell by a
+// binary search over the scanned counts and loads the cell-sorted record.
 __global__ void __launch_bounds__(kFmtWarps * 32)
-    k_format(FormatSpec f, GridSpec g, const double* __restrict__ xw, const int* __restrict__ atype,
-             const int* __restrict__ cell_of, const int* __restrict__ cell_start, const int* __restrict__ cell_atoms,
-             int* __restrict__ nl_j, int* __restrict__ nl_code, double* __restrict__ nl_rij, int* __restrict__ nl_cnt,
+    k_format(FormatSpec f, GridSpec g, const double* __restrict__ xw, const int* __restrict__ cell_of,
+             const int* __restrict__ cell_start, const CellRec* __restrict__ cell_rec, int* __restrict__ nl_j,
+             int* __restrict__ nl_code, double* __restrict__ nl_rij, int* __restrict__ nl_cnt,
              int* __restrict__ err) {
   extern __shared__ __align__(16) unsigned char smem[];
-  __shared__ int rng_start[kFmtWarps][32], rng_pref[kFmtWarps][33], rng_img[kFmtWarps][32];
+  __shared__ int s_start[kFmtWarps][kStencilChunk], s_pref[kFmtWarps][kStencilChunk], s_code[kFmtWarps][kStencilChunk];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int i = blockIdx.x * kFmtWarps + warp;
   if (i >= f.nloc) return;  // warp-uniform; no block-level barrier follows
   CandBuf b = cand_buf(smem, warp, f.cap);
+  int* const c_start = s_start[warp];
+  int* const c_pref = s_pref[warp];
+  int* const c_code = s_code[warp];
   const double xi[3] = {xw[3 * i], xw[3 * i + 1], xw[3 * i + 2]};
   const int cell = cell_of[i];
   const int ci[3] = {cell / (g.n[1] * g.n[2]), (cell / g.n[2]) % g.n[1], cell % g.n[2]};
-  const int nz = 2 * g.reach[2] + 1;
+  const int sy = 2 * g.reach[1] + 1, sz = 2 * g.reach[2] + 1;
+  const int nstencil = (2 * g.reach[0] + 1) * sy * sz;
   const unsigned lt_mask = (1u << lane) - 1u;
   int ncand = 0;
-  for (int d0 = -g.reach[0]; d0 <= g.reach[0]; ++d0) {
-    int u0 = ci[0] + d0, img0 = 0;
-    if (g.periodic) {
-      img0 = floor_div(u0, g.n[0]);
-      u0 -= img0 * g.n[0];
-    } else if (u0 < 0 || u0 >= g.n[0]) {
-      continue;
-    }
-    for (int d1 = -g.reach[1]; d1 <= g.reach[1]; ++d1) {
-      int u1 = ci[1] + d1, img1 = 0;
-      if (g.periodic) {
-        img1 = floor_div(u1, g.n[1]);
-        u1 -= img1 * g.n[1];
-      } else if (u1 < 0 || u1 >= g.n[1]) {
-        continue;
-      }
-      int cnt = 0, start = 0, img2 = 0;
-      if (lane < nz) {
-        int u2 = ci[2] + lane - g.reach[2];
+  for (int s0 = 0; s0 < nstencil; s0 += kStencilChunk) {
+    // counts of this lane's cells, then a warp scan
+    int cnt[kStencilPerLane], st[kStencilPerLane], cd[kStencilPerLane];
+    int local = 0;
+#pragma unroll
+    for (int u = 0; u < kStencilPerLane; ++u) {
+      const int sidx = s0 + lane * kStencilPerLane + u;
+      cnt[u] = 0;
+      st[u] = 0;
+      cd[u] = 0;
+      if (sidx < nstencil) {
+        const int dz = sidx % sz, dy = (sidx / sz) % sy, dx = sidx / (sz * sy);
+        int uu[3] = {ci[0] + dx - g.reach[0], ci[1] + dy - g.reach[1], ci[2] + dz - g.reach[2]};
+        int img[3] = {0, 0, 0};
         bool ok = true;
-        if (g.periodic) {
-          img2 = floor_div(u2, g.n[2]);
-          u2 -= img2 * g.n[2];
-        } else {
-          ok = (u2 >= 0 && u2 < g.n[2]);
+#pragma unroll
+        for (int d = 0; d < 3; ++d) {
+          if (g.periodic) {
+            img[d] = floor_div(uu[d], g.n[d]);
+            uu[d] -= img[d] * g.n[d];
+          } else {
+            ok = ok && uu[d] >= 0 && uu[d] < g.n[d];
+          }
         }
         if (ok) {
-          const int cc = (u0 * g.n[1] + u1) * g.n[2] + u2;
-          start = cell_start[cc];
-          cnt = cell_start[cc + 1] - start;
+          const int cc = (uu[0] * g.n[1] + uu[1]) * g.n[2] + uu[2];
+          st[u] = cell_start[cc];
+          cnt[u] = cell_start[cc + 1] - st[u];
+          cd[u] = image_code(img[0], img[1], img[2]);
         }
       }
-      int total;
-      const int pref = warp_exclusive_scan(cnt, lane, total);
-      rng_start[warp][lane] = start;
-      rng_pref[warp][lane] = pref;
-      rng_img[warp][lane] = img2;
-      __syncwarp();
-      double shx = 0, shy = 0, shz = 0;  // shift of (img0, img1, 0)
-      if (g.periodic) {
-        shx = dadd(dmul((double)img0, g.B[0]), dmul((double)img1, g.B[3]));
-        shy = dadd(dmul((double)img0, g.B[1]), dmul((double)img1, g.B[4]));
-        shz = dadd(dmul((double)img0, g.B[2]), dmul((double)img1, g.B[5]));
-      }
-      for (int k = lane; k - lane < total; k += 32) {
-        bool valid = false;
-        int j = -1, code = 0, tj = 0;
-        double r[3] = {0, 0, 0}, r2 = 0;
-        if (k < total) {
-          int q = 0;
-          while (q + 1 < nz && rng_pref[warp][q + 1] <= k) ++q;
-          j = cell_atoms[rng_start[warp][q] + (k - rng_pref[warp][q])];
-          const int im2 = rng_img[warp][q];
-          double s[3] = {0, 0, 0};
-          if (g.periodic) {
-            const double m2 = (double)im2;
-            s[0] = dadd(shx, dmul(m2, g.B[6]));
-            s[1] = dadd(shy, dmul(m2, g.B[7]));
-            s[2] = dadd(shz, dmul(m2, g.B[8]));
-          }
+      local += cnt[u];
+    }
+    int total;
+    int run = warp_exclusive_scan(local, lane, total);
 #pragma unroll
-          for (int c = 0; c < 3; ++c) r[c] = dsub(dadd(xw[3 * j + c], s[c]), xi[c]);
+    for (int u = 0; u < kStencilPerLane; ++u) {
+      const int q = lane * kStencilPerLane + u;
+      c_start[q] = st[u];
+      c_pref[q] = run;  // cells past the stencil get pref == total and are never chosen
+      c_code[q] = cd[u];
+      run += cnt[u];
+    }
+    __syncwarp();
+    for (int k0 = 0; k0 < total; k0 += 32 * kGatherBatch) {
+      CellRec rec[kGatherBatch];
+      int rcode[kGatherBatch];
+#pragma unroll
+      for (int u = 0; u < kGatherBatch; ++u) {
+        const int k = k0 + 32 * u + lane;
+        rcode[u] = -1;
+        if (k < total) {
+          int q = 0;  // last cell with c_pref[q] <= k (that cell holds k)
+#pragma unroll
+          for (int step = kStencilChunk / 2; step > 0; step >>= 1)
+            if (c_pref[q + step] <= k) q += step;
+          const CellRec* src = cell_rec + c_start[q] + (k - c_pref[q]);
+          const double2 a = __ldg(reinterpret_cast<const double2*>(src));
+          const double2 c = __ldg(reinterpret_cast<const double2*>(src) + 1);
+          const long long jt = __double_as_longlong(c.y);  // {int j, int t}, little-endian
+          rec[u].x = a.x;
+          rec[u].y = a.y;
+          rec[u].z = c.x;
+          rec[u].j = (int)(unsigned)(jt & 0xffffffffll);
+          rec[u].t = (int)(jt >> 32);
+          rcode[u] = c_code[q];
+        } else {
+          rec[u].x = rec[u].y = rec[u].z = 0.0;
+          rec[u].j = rec[u].t = 0;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kGatherBatch; ++u) {
+        bool valid = false;
+        double r[3] = {0, 0, 0}, r2 = 0;
+        const int j = rec[u].j, tj = rec[u].t, code = rcode[u];
+        if (code >= 0) {
+          const int im0 = ((code >> 20) & 1023) - kImageBias, im1 = ((code >> 10) & 1023) - kImageBias,
+                    im2 = (code & 1023) - kImageBias;
+          double sh[3] = {0, 0, 0};
+          if (g.periodic) {
+            const double m0 = (double)im0, m1 = (double)im1, m2 = (double)im2;
+#pragma unroll
+            for (int c = 0; c < 3; ++c) sh[c] = dadd(dadd(dmul(m0, g.B[c]), dmul(m1, g.B[3 + c])), dmul(m2, g.B[6 + c]));
+          }
+          const double xj[3] = {rec[u].x, rec[u].y, rec[u].z};
+#pragma unroll
+          for (int c = 0; c < 3; ++c) r[c] = dsub(dadd(xj[c], sh[c]), xi[c]);
           r2 = dadd(dadd(dmul(r[0], r[0]), dmul(r[1], r[1])), dmul(r[2], r[2]));
-          const bool self = (j == i) && img0 == 0 && img1 == 0 && im2 == 0;
-          tj = atype[j];
+          const bool self = (j == i) && im0 == 0 && im1 == 0 && im2 == 0;
           const bool type_ok = (tj >= 0 && tj < f.ntypes);
           if (!type_ok && !self && r2 < f.rc2) atomicAdd(err + kErrBadType, 1);
           valid = !self && type_ok && (r2 < f.rc2);
-          code = image_code(img0, img1, im2);
         }
         const unsigned m = __ballot_sync(0xffffffffu, valid);
         const int pos = ncand + __popc(m & lt_mask);
@@ -418,8 +544,8 @@ __global__ void __launch_bounds__(kFmtWarps * 32)
         }
         ncand += __popc(m);
       }
-      __syncwarp();
     }
+    __syncwarp();
   }
   if (ncand > f.cap) {
     if (lane == 0) atomicAdd(err + kErrCandCapacity, 1);
@@ -429,9 +555,9 @@ __global__ void __launch_bounds__(kFmtWarps * 32)
   emit_row(f, i, b, ncand, lane, nl_j, nl_code, nl_rij, nl_cnt, err);
 }
 
-void launch_format(cudaStream_t st, const FormatSpec& f, const GridSpec& g, const double* xw, const int* atype,
-                   const int* cell_of, const int* cell_start, const int* cell_atoms, int* nl_j, int* nl_code,
-                   double* nl_rij, int* nl_cnt, int* err) {
+void launch_format(cudaStream_t st, const FormatSpec& f, const GridSpec& g, const double* xw, const int* cell_of,
+                   const int* cell_start, const CellRec* cell_rec, int* nl_j, int* nl_code, double* nl_rij,
+                   int* nl_cnt, int* err) {
   if (f.nloc <= 0) return;
   const size_t smem = format_smem_bytes(f.cap);
   static bool attr_set = false;
@@ -440,8 +566,9 @@ void launch_format(cudaStream_t st, const FormatSpec& f, const GridSpec& g, cons
     attr_set = true;
   }
   count_launch();
-  k_format<<<(f.nloc + kFmtWarps - 1) / kFmtWarps, kFmtWarps * 32, smem, st>>>(
-      f, g, xw, atype, cell_of, cell_start, cell_atoms, nl_j, nl_code, nl_rij, nl_cnt, err);
+  k_format<<<(f.nloc + kFmtWarps - 1) / kFmtWarps, kFmtWarps * 32, smem, st>>>(f, g, xw, cell_of, cell_start,
+                                                                               cell_rec, nl_j, nl_code, nl_rij,
+                                                                               nl_cnt, err);
 }
 
 // Caller-provided candidates (LAMMPS full list): cand_start is a CSR over

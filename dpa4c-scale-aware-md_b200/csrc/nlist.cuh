@@ -27,6 +27,21 @@ struct GridSpec {
   int ncells;
 };
 
+// Cell-sorted atom record written by the fill kernel: the wrapped position
+// and the atom's index and type, so the list kernel reaches a candidate's
+// data with one 32-byte load.
+struct __align__(32) CellRec {
+  double x, y, z;
+  int j, t;
+};
+
+// Binning grid: cells at least rcut / kCellsPerCut wide (coarsened until there
+// are at most max_cells), stencil reach covering every cell within rcut.
+// Returns 0, or 1 for a degenerate box / region, or 2 for a box so narrow
+// that the stencil would exceed 31 cells along a cell vector.
+constexpr int kCellsPerCut = 2;
+int make_grid(bool periodic, const double* box, const double* region, double rcut, long long max_cells, GridSpec& g);
+
 struct FormatSpec {
   int nloc, nall, ntypes, selt, cap;
   int sel[kMaxTypes];
@@ -44,12 +59,12 @@ void launch_bin(cudaStream_t st, int nall, const double* coord, const GridSpec& 
 // scan_scratch_ints(n) ints; with scratch == nullptr a single block is used.
 void launch_exclusive_scan(cudaStream_t st, int n, const int* in, int* out, int* scratch);
 size_t scan_scratch_ints(int n);
-void launch_fill_cells(cudaStream_t st, int nall, const int* cell_of, const int* cell_start, int* cursor,
-                       int* cell_atoms);
+void launch_fill_cells(cudaStream_t st, int nall, const double* xw, const int* atype, const int* cell_of,
+                       const int* cell_start, int* cursor, CellRec* cell_rec);
 size_t format_smem_bytes(int cap);
-void launch_format(cudaStream_t st, const FormatSpec& f, const GridSpec& g, const double* xw, const int* atype,
-                   const int* cell_of, const int* cell_start, const int* cell_atoms, int* nl_j, int* nl_code,
-                   double* nl_rij, int* nl_cnt, int* err);
+void launch_format(cudaStream_t st, const FormatSpec& f, const GridSpec& g, const double* xw, const int* cell_of,
+                   const int* cell_start, const CellRec* cell_rec, int* nl_j, int* nl_code, double* nl_rij,
+                   int* nl_cnt, int* err);
 // Formats a caller-provided candidate list (LAMMPS full list in CSR form).
 // Formats a canonical destination-major edge graph (fp32 edge vectors) and
 // converts the int64 node types to int32 (invalid types become -1).

@@ -32,10 +32,10 @@ constexpr size_t kOffCellOf = kOffXw + align256(sizeof(double) * 3 * kNoAllocMax
 constexpr size_t kOffCellCount = kOffCellOf + align256(sizeof(int) * kNoAllocMaxAtoms);
 constexpr size_t kOffCellStart = kOffCellCount + align256(sizeof(int) * kNoAllocMaxCells);
 constexpr size_t kOffCursor = kOffCellStart + align256(sizeof(int) * (kNoAllocMaxCells + 1));
-constexpr size_t kOffCellAtoms = kOffCursor + align256(sizeof(int) * kNoAllocMaxCells);
-constexpr size_t kOffCounts = kOffCellAtoms + align256(sizeof(int) * kNoAllocMaxAtoms);
+constexpr size_t kOffCellRec = kOffCursor + align256(sizeof(int) * kNoAllocMaxCells);
+constexpr size_t kOffCounts = kOffCellRec + align256(sizeof(CellRec) * kNoAllocMaxAtoms);
 constexpr size_t kOffErr = kOffCounts + align256(sizeof(int) * kNoAllocMaxAtoms * kNoAllocMaxTypes);
-constexpr size_t kScratchBytes = kOffErr + align256(sizeof(int) * kErrCount);  // about 4.5 MiB
+constexpr size_t kScratchBytes = kOffErr + align256(sizeof(int) * kErrCount);  // about 6.5 MiB
 
 // The scratch itself.  In host code this name is only a stand-in for the
 // device symbol: its device address comes from cudaGetSymbolAddress below.
@@ -80,48 +80,21 @@ extern "C" b200dp_status b200dp_build_nlist_noalloc(void* stream, int nlocal, in
   int* cell_count = reinterpret_cast<int*>(base + kOffCellCount);
   int* cell_start = reinterpret_cast<int*>(base + kOffCellStart);
   int* cursor = reinterpret_cast<int*>(base + kOffCursor);
-  int* cell_atoms = reinterpret_cast<int*>(base + kOffCellAtoms);
+  CellRec* cell_rec = reinterpret_cast<CellRec*>(base + kOffCellRec);
   int* counts = reinterpret_cast<int*>(base + kOffCounts);
   int* err = reinterpret_cast<int*>(base + kOffErr);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 
-  // Binning grid (host arithmetic only), cells of at least rcut, coarsened to fit.
+  // Binning grid (host arithmetic only), coarsened to fit the static scratch.
   GridSpec g;
-  std::memset(&g, 0, sizeof(g));
-  g.periodic = periodic ? 1 : 0;
-  double width[3], ext[3];
-  if (periodic) {
-    for (int k = 0; k < 9; ++k) g.B[k] = box[k];
-    make_box_inverse(box, g.Binv, width);
-    for (int d = 0; d < 3; ++d)
-      if (!(width[d] > 0) || !std::isfinite(width[d])) return B200DP_ERR_INVALID;
-  } else {
-    for (int d = 0; d < 3; ++d) {
-      g.lo[d] = region[d];
-      ext[d] = std::max(region[3 + d] - region[d], 1e-9);
-      width[d] = ext[d];
-    }
+  switch (make_grid(periodic, box, region, rcut, kNoAllocMaxCells, g)) {
+    case 0:
+      break;
+    case 1:
+      return B200DP_ERR_INVALID;
+    default:
+      return B200DP_ERR_UNSUPPORTED;
   }
-  double scale = 1.0;
-  for (;;) {
-    long long tot = 1;
-    for (int d = 0; d < 3; ++d) {
-      g.n[d] = std::max(1, (int)std::floor(width[d] / (rcut * scale)));
-      tot *= g.n[d];
-    }
-    if (tot <= kNoAllocMaxCells) break;
-    scale *= 1.25;
-  }
-  for (int d = 0; d < 3; ++d) {
-    if (periodic) {
-      g.reach[d] = (int)std::ceil(rcut * g.n[d] / width[d] * (1.0 + 1e-12));
-      if (2 * g.reach[d] + 1 > 32) return B200DP_ERR_UNSUPPORTED;
-    } else {
-      g.inv_h[d] = g.n[d] / ext[d];
-      g.reach[d] = 1;
-    }
-  }
-  g.ncells = g.n[0] * g.n[1] * g.n[2];
 
   FormatSpec f;
   std::memset(&f, 0, sizeof(f));
@@ -145,8 +118,8 @@ extern "C" b200dp_status b200dp_build_nlist_noalloc(void* stream, int nlocal, in
       return B200DP_ERR_CUDA;
     launch_bin(st, nall, d_coord, g, xw, cell_of, cell_count);
     launch_exclusive_scan(st, g.ncells, cell_count, cell_start, nullptr);
-    launch_fill_cells(st, nall, cell_of, cell_start, cursor, cell_atoms);
-    launch_format(st, f, g, xw, d_atype, cell_of, cell_start, cell_atoms, d_nlist, d_image, d_rij, counts, err);
+    launch_fill_cells(st, nall, xw, d_atype, cell_of, cell_start, cursor, cell_rec);
+    launch_format(st, f, g, xw, cell_of, cell_start, cell_rec, d_nlist, d_image, d_rij, counts, err);
   }
   if (cudaGetLastError() != cudaSuccess) return B200DP_ERR_CUDA;
   if (cudaStreamSynchronize(st) != cudaSuccess) return B200DP_ERR_CUDA;

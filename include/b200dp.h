@@ -172,7 +172,7 @@ b200dp_status b200dp_selftest_mma(int K, int N, int a_mn_major, int b_mn_major, 
  * arguments meaning; rcut, ntypes and sel[ntypes] given directly, no engine):
  * d_nlist and d_image [nlocal*sum(sel)] int32, d_rij [nlocal*sum(sel)*3] fp64,
  * all caller-owned device buffers.  Scratch lives in one static device array
- * of about 4.5 MiB that every GPU loading the library keeps until exit; it
+ * of about 6.5 MiB that every GPU loading the library keeps until exit; it
  * limits nlocal + nghost to 65536 (larger inputs return B200DP_ERR_CAPACITY)
  * and the binning grid to 65536 cells (coarsened automatically).  The first
  * call on a device looks up that array's device address (cudaGetSymbolAddress)
