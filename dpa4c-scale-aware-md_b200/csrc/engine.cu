@@ -221,8 +221,7 @@ b200dp_status Engine::init(const char* path, const b200dp_options* o) {
       }
     }
   }
-  cap = std::max(256, ((2 * s.selt + 31) / 32) * 32);
-  if (format_smem_bytes(cap) > 200 * 1024) {
+  if (format_smem_bytes(format_spec(0, 0)) > 200 * 1024) {
     err = "neighbour selection too large for the list-format kernel";
     return B200DP_ERR_UNSUPPORTED;
   }
@@ -230,7 +229,8 @@ b200dp_status Engine::init(const char* path, const b200dp_options* o) {
   for (auto& ev : events) B200DP_CUDA_TRY(cudaEventCreate(&ev));
   B200DP_CUDA_TRY(err_buf.ensure(sizeof(int) * kErrCount));
   B200DP_CUDA_TRY(cudaMemset(err_buf.ptr, 0, sizeof(int) * kErrCount));
-  B200DP_CUDA_TRY(reduce_part.ensure(sizeof(double) * kReduceBlocks * 9));
+  B200DP_CUDA_TRY(asm_done.ensure(sizeof(unsigned)));
+  B200DP_CUDA_TRY(cudaMemset(asm_done.ptr, 0, sizeof(unsigned)));
   B200DP_CUDA_TRY(scalars.ensure(sizeof(double) * 16));
   ch_fwd = 32;
   ch_bwd = 32;
@@ -246,7 +246,7 @@ void Engine::release() {
   for (DevBuf* b : {&w_emb, &w_embT, &xw, &cell_of, &cell_count, &cell_start, &cell_cursor, &cell_rec, &nl_j,
                     &nl_code, &nl_rij, &nl_cnt, &rev_count, &rev_start, &rev_cursor, &rev_tmp, &rev_slot,
                     &blk_counts, &type_start, &perm_pos, &perm_atom, &Tbuf, &Dbuf, &dDbuf, &atom_e, &gslot,
-                    &vrows, &err_buf, &reduce_part, &scalars, &h_coord, &h_atype, &h_force, &h_aviral, &h_ae,
+                    &asm_done, &err_buf, &reduce_part, &scalars, &h_coord, &h_atype, &h_force, &h_aviral, &h_ae,
                     &cand_start, &cand_list, &ilist_d, &tc_nets, &ecount, &eoff, &tstart, &rec_rt, &rec_row,
                     &rec_slot, &partial, &scan_scratch, &dTbuf, &ftile, &graph_atype, &item_rec})
     b->release();
@@ -307,7 +307,7 @@ b200dp_status Engine::ensure_buffers(int nloc, int nall, int ncells, int ncand) 
   for (auto& b : dz_l) B200DP_CUDA_TRY(b.ensure(ps * L * maxfit));
   B200DP_CUDA_TRY(atom_e.ensure(sizeof(double) * L));
   B200DP_CUDA_TRY(gslot.ensure(sizeof(double) * 3 * S));
-  B200DP_CUDA_TRY(vrows.ensure(sizeof(double) * 9 * A));
+  B200DP_CUDA_TRY(reduce_part.ensure(sizeof(double) * 10 * assemble_blocks((int)A)));
   if (ncand > 0) B200DP_CUDA_TRY(cand_list.ensure(sizeof(int) * (size_t)ncand));
   const size_t nscan = std::max({(size_t)C, A, (size_t)sd.nnets * L}) + 1;
   B200DP_CUDA_TRY(scan_scratch.ensure(sizeof(int) * scan_scratch_ints((int)nscan)));
@@ -392,10 +392,10 @@ FormatSpec Engine::format_spec(int nloc, int nall) const {
   f.nall = nall;
   f.ntypes = hm.ntypes;
   f.selt = sd.selt;
-  f.cap = cap;
   for (int t = 0; t < hm.ntypes; ++t) f.sel[t] = sd.sel[t];
   for (int t = 0; t <= hm.ntypes; ++t) f.off[t] = sd.off[t];
   f.rc2 = hm.rcut * hm.rcut;
+  format_caps(f);
   return f;
 }
 
@@ -512,9 +512,8 @@ b200dp_status Engine::run_model(cudaStream_t st, int nloc, int nall, const int* 
   }
   mark(st, 4);
   launch_assemble(st, nloc, nall, sd.selt, nl_j.as<int>(), gslot.as<double>(), nl_rij.as<double>(),
-                  rev_start.as<int>(), rev_slot.as<int>(), d_force, d_atom_virial, vrows.as<double>());
-  launch_reduce_rows(st, nall, 9, vrows.as<double>(), reduce_part.as<double>(), d_virial);
-  launch_reduce_rows(st, nloc, 1, atom_e.as<double>(), reduce_part.as<double>(), d_energy);
+                  rev_start.as<int>(), rev_slot.as<int>(), atom_e.as<double>(), d_force, d_atom_virial,
+                  reduce_part.as<double>(), asm_done.as<unsigned>(), d_energy, d_virial);
   if (d_atom_energy)
     B200DP_CUDA_TRY(cudaMemcpyAsync(d_atom_energy, atom_e.ptr, sizeof(double) * nloc, cudaMemcpyDeviceToDevice, st));
   mark(st, 5);

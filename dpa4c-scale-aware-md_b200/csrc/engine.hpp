@@ -36,7 +36,6 @@ struct Engine {
   b200dp_options opt{};
   SeaDev sd{};
   std::string err;
-  int cap = 256;  // per-centre in-cutoff candidate buffer
   int maxfit = 1;
   int ch_fwd = 32, ch_bwd = 32;
 
@@ -68,7 +67,7 @@ struct Engine {
   DevBuf Tbuf, Dbuf, dDbuf;
   std::vector<DevBuf> th_l, y_l;
   std::array<DevBuf, 2> dy_l, dz_l;
-  DevBuf atom_e, gslot, vrows, reduce_part, scalars, err_buf;
+  DevBuf atom_e, gslot, asm_done, reduce_part, scalars, err_buf;
   // host-call staging
   DevBuf h_coord, h_atype, h_force, h_aviral, h_ae;
 

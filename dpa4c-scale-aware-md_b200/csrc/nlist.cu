@@ -1,6 +1,7 @@
 // Neighbour-graph builder kernels (see nlist.cuh).
 #include <algorithm>
 #include <cmath>
+#include <cstdint>
 #include <cstring>
 
 #include "nlist.cuh"
@@ -138,16 +139,26 @@ __global__ void __launch_bounds__(1024) k_exclusive_scan(int n, const int* __res
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (tid == 0) carry = 0;
   __syncthreads();
-  constexpr int kPer = 4;
+  constexpr int kPer = 16;  // all of a pass's loads are issued before the scan
   for (int base = 0; base < n; base += 1024 * kPer) {
     int v[kPer];
     int local = 0;
     const int i0 = base + tid * kPer;
+    if (i0 + kPer <= n && (reinterpret_cast<uintptr_t>(in) & 15) == 0) {
 #pragma unroll
-    for (int q = 0; q < kPer; ++q) {
-      v[q] = (i0 + q < n) ? in[i0 + q] : 0;
-      local += v[q];
+      for (int q = 0; q < kPer; q += 4) {
+        const int4 w = __ldg(reinterpret_cast<const int4*>(in + i0 + q));
+        v[q] = w.x;
+        v[q + 1] = w.y;
+        v[q + 2] = w.z;
+        v[q + 3] = w.w;
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < kPer; ++q) v[q] = (i0 + q < n) ? in[i0 + q] : 0;
     }
+#pragma unroll
+    for (int q = 0; q < kPer; ++q) local += v[q];
     int wt;
     const int ex = warp_exclusive_scan(local, lane, wt);
     if (lane == 0) warp_ex[warp] = wt;
@@ -265,138 +276,154 @@ void launch_fill_cells(cudaStream_t st, int nall, const double* xw, const int* a
 }
 
 // ---------------------------------------------------------------- format
-constexpr int kFmtWarps = 4;
+constexpr int kFmtWarps = 8;
 
 __device__ __forceinline__ int floor_div(int a, int n) { return a >= 0 ? a / n : -((-a + n - 1) / n); }
 
-// per warp and candidate: r2 (8) + r (24) + grouped r2 (8) + j, code, type,
-// type-grouped index (16) bytes, plus one rank bit per candidate
-__host__ __device__ constexpr size_t cand_bytes(int cap) { return (size_t)cap * 56 + ((size_t)cap / 32 + 1) * 4; }
-size_t format_smem_bytes(int cap) { return (size_t)kFmtWarps * ((cand_bytes(cap) + 15) / 16 * 16); }
+void format_caps(FormatSpec& f) {
+  f.cap_off[0] = 0;
+  f.cap_max = 0;
+  for (int t = 0; t < f.ntypes; ++t) {
+    const int c = (std::max(128, 2 * f.sel[t]) + 31) / 32 * 32;
+    f.cap_off[t + 1] = f.cap_off[t] + c;
+    f.cap_max = std::max(f.cap_max, c);
+  }
+}
+
+// Per warp: r2 (8 bytes), j, image code, source index and rank (16 bytes) per
+// candidate slot, plus a rank bitmap of the largest type region.
+__host__ __device__ inline size_t cand_bytes(int capsum, int cap_max) {
+  return ((size_t)capsum * 24 + ((size_t)cap_max / 32 + 1) * 4 + 15) / 16 * 16;
+}
+size_t format_smem_bytes(const FormatSpec& f) {
+  return (size_t)kFmtWarps * cand_bytes(f.cap_off[f.ntypes], f.cap_max);
+}
 
 struct CandBuf {
   double* r2;
-  double* r;    // [cap][3]
-  double* r2g;  // r2 in type-grouped order
   int* j;
   int* code;
-  int* t;
-  int* grp;        // candidate indices grouped by type, stable within a type
+  int* src;   // kernel-specific handle from which the centre-to-neighbour vector is recomputed
+  int* rank;
   unsigned* seen;  // rank bitmap (tie detection)
 };
 
-__device__ __forceinline__ CandBuf cand_buf(unsigned char* smem, int warp, int cap) {
-  unsigned char* base = smem + (size_t)warp * ((cand_bytes(cap) + 15) / 16 * 16);
+__device__ __forceinline__ CandBuf cand_buf(unsigned char* smem, int warp, const FormatSpec& f) {
+  const int capsum = f.cap_off[f.ntypes];
+  unsigned char* base = smem + (size_t)warp * cand_bytes(capsum, f.cap_max);
   CandBuf b;
   b.r2 = reinterpret_cast<double*>(base);
-  b.r = b.r2 + cap;
-  b.r2g = b.r + 3 * cap;
-  b.j = reinterpret_cast<int*>(b.r2g + cap);
-  b.code = b.j + cap;
-  b.t = b.code + cap;
-  b.grp = b.t + cap;
-  b.seen = reinterpret_cast<unsigned*>(b.grp + cap);
+  b.j = reinterpret_cast<int*>(b.r2 + capsum);
+  b.code = b.j + capsum;
+  b.src = b.code + capsum;
+  b.rank = b.src + capsum;
+  b.seen = reinterpret_cast<unsigned*>(b.rank + capsum);
   return b;
 }
 
-// Orders one centre's candidates and writes its row.  Candidates are first
-// grouped by type (stable, by warp ballots), then each is ranked against the
-// candidates of its own type by (r^2, j, image).  Keys are unique (j, image)
-// pairs, so the order is total and does not depend on the order in which the
-// candidates were found.
-__device__ void emit_row(const FormatSpec& f, int i, const CandBuf& b, int ncand, int lane, int* __restrict__ nl_j,
-                         int* __restrict__ nl_code, double* __restrict__ nl_rij, int* __restrict__ nl_cnt,
-                         int* __restrict__ err) {
-  const unsigned lt_mask = (1u << lane) - 1u;
-  int toff[kMaxTypes + 1];
-  int tcnt[kMaxTypes];
-  // counts per type
-  toff[0] = 0;
-  for (int t = 0; t < f.ntypes; ++t) {
-    int local = 0;
-    for (int c = lane; c < ncand; c += 32) local += (b.t[c] == t);
-    tcnt[t] = warp_sum(local);
-    toff[t + 1] = toff[t] + tcnt[t];
-  }
-  // stable grouping by type
-  int run[kMaxTypes];
-  for (int t = 0; t < f.ntypes; ++t) run[t] = 0;
-  for (int base = 0; base < ncand; base += 32) {
-    const int c = base + lane;
-    const int tc = (c < ncand) ? b.t[c] : -1;
-    for (int t = 0; t < f.ntypes; ++t) {
-      const unsigned m = __ballot_sync(0xffffffffu, tc == t);
-      if (tc == t) b.grp[toff[t] + run[t] + __popc(m & lt_mask)] = c;
-      run[t] += __popc(m);
+// Appends the valid lanes' candidates to their type regions (warp ballots per
+// type; ncnt[t] keeps counting past the capacity so overflow is seen).
+__device__ __forceinline__ void cand_push(const FormatSpec& f, const CandBuf& b, int (&ncnt)[kMaxTypes], bool valid,
+                                          int tj, double r2, int j, int code, int src, unsigned lt_mask) {
+#pragma unroll
+  for (int t = 0; t < kMaxTypes; ++t) {
+    if (t >= f.ntypes) break;
+    const bool mine = valid && tj == t;
+    const unsigned m = __ballot_sync(0xffffffffu, mine);
+    const int pos = ncnt[t] + __popc(m & lt_mask);
+    if (mine && pos < f.cap_off[t + 1] - f.cap_off[t]) {
+      const int o = f.cap_off[t] + pos;
+      b.r2[o] = r2;
+      b.j[o] = j;
+      b.code[o] = code;
+      b.src[o] = src;
     }
+    ncnt[t] += __popc(m);
   }
-  __syncwarp();
-  // Rank within each type.  r^2 alone decides almost always: count smaller r^2
-  // in the grouped copy (warp-uniform broadcast reads); two members landing on
-  // the same rank reveal a tie, and only then is the type re-ranked with the
-  // full key (r^2, j, image).
-  for (int k = lane; k < ncand; k += 32) b.r2g[k] = b.r2[b.grp[k]];
+}
+
+// Orders one centre's candidates and writes its row: each candidate is ranked
+// against the candidates of its own type by (r^2, j, image).  Keys are unique
+// (j, image) pairs, so the order is total and does not depend on the order in
+// which the candidates were found.  r^2 alone decides almost always: each
+// member counts the smaller r^2 of its type (warp-uniform broadcast reads);
+// two members landing on the same rank reveal a tie, and only then is the
+// type re-ranked with the full key.  rvec(src, code, r) recomputes the
+// centre-to-neighbour vector of a kept candidate.
+template <typename RVec>
+__device__ void emit_row(const FormatSpec& f, int i, const CandBuf& b, const int (&ncnt)[kMaxTypes], int lane,
+                         int* __restrict__ nl_j, int* __restrict__ nl_code, double* __restrict__ nl_rij,
+                         int* __restrict__ nl_cnt, int* __restrict__ err, RVec rvec) {
+  const int zero_code = image_code(0, 0, 0);
+#pragma unroll 1
   for (int t = 0; t < f.ntypes; ++t) {
-    const int k0 = toff[t], k1 = toff[t + 1], nt = k1 - k0;
-    if (nt == 0) continue;
-    for (int w = lane; w <= nt / 32; w += 32) b.seen[w] = 0u;
-    __syncwarp();
-    bool tie = false;
-    for (int base = k0; base < k1; base += 64) {
-      const int ma = base + lane, mb = base + 32 + lane;
-      const double ra = ma < k1 ? b.r2g[ma] : 0.0, rb = mb < k1 ? b.r2g[mb] : 0.0;
-      int ka = 0, kb = 0;
-      for (int k = k0; k < k1; ++k) {
-        const double q = b.r2g[k];
-        ka += (q < ra);
-        kb += (q < rb);
-      }
-      if (ma < k1) tie |= (atomicOr(&b.seen[ka >> 5], 1u << (ka & 31)) >> (ka & 31)) & 1u;
-      if (mb < k1) tie |= (atomicOr(&b.seen[kb >> 5], 1u << (kb & 31)) >> (kb & 31)) & 1u;
-      // provisional ranks, final unless a tie shows up
-      if (ma < k1) b.t[b.grp[ma]] = t + (ka << 4);
-      if (mb < k1) b.t[b.grp[mb]] = t + (kb << 4);
+    const int cap_t = f.cap_off[t + 1] - f.cap_off[t];
+    const int o = f.cap_off[t];
+    int nt = ncnt[0];
+#pragma unroll
+    for (int u = 1; u < kMaxTypes; ++u)
+      if (u == t) nt = ncnt[u];
+    if (nt > cap_t) {
+      if (lane == 0) atomicAdd(err + kErrCandCapacity, 1);
+      nt = cap_t;
     }
-    tie = __any_sync(0xffffffffu, tie);
-    __syncwarp();
-    for (int m = k0 + lane; m < k1; m += 32) {
-      const int c = b.grp[m];
-      int rank = b.t[c] >> 4;
-      if (tie) {  // full key (r^2, j, image)
-        const double r2 = b.r2[c];
-        const int j = b.j[c], code = b.code[c];
-        rank = 0;
-        for (int k = k0; k < k1; ++k) {
-          const int c2 = b.grp[k];
-          const double q = b.r2[c2];
-          if (q < r2) {
-            ++rank;
-          } else if (q == r2 && c2 != c) {
-            const int j2 = b.j[c2];
-            rank += (j2 < j || (j2 == j && b.code[c2] < code));
-          }
+    const int sel = f.sel[t];
+    const int keep = nt < sel ? nt : sel;
+    const double* r2v = b.r2 + o;
+    if (nt > 0) {
+      for (int w = lane; w <= nt / 32; w += 32) b.seen[w] = 0u;
+      __syncwarp();
+      bool tie = false;
+      for (int base = 0; base < nt; base += 64) {
+        const int ma = base + lane, mb = base + 32 + lane;
+        const double ra = ma < nt ? r2v[ma] : 0.0, rb = mb < nt ? r2v[mb] : 0.0;
+        int ka = 0, kb = 0;
+        for (int k = 0; k < nt; ++k) {
+          const double q = r2v[k];
+          ka += (q < ra);
+          kb += (q < rb);
+        }
+        if (ma < nt) {
+          tie |= (atomicOr(&b.seen[ka >> 5], 1u << (ka & 31)) >> (ka & 31)) & 1u;
+          b.rank[o + ma] = ka;
+        }
+        if (mb < nt) {
+          tie |= (atomicOr(&b.seen[kb >> 5], 1u << (kb & 31)) >> (kb & 31)) & 1u;
+          b.rank[o + mb] = kb;
         }
       }
-      if (rank < f.sel[t]) {
-        const size_t slot = (size_t)i * f.selt + f.off[t] + rank;
-        nl_j[slot] = b.j[c];
-        nl_code[slot] = b.code[c];
-        nl_rij[3 * slot] = b.r[3 * c];
-        nl_rij[3 * slot + 1] = b.r[3 * c + 1];
-        nl_rij[3 * slot + 2] = b.r[3 * c + 2];
+      tie = __any_sync(0xffffffffu, tie);
+      __syncwarp();
+      for (int m = lane; m < nt; m += 32) {
+        int rank = b.rank[o + m];
+        const int j = b.j[o + m], code = b.code[o + m];
+        if (tie) {  // full key (r^2, j, image)
+          const double r2 = r2v[m];
+          rank = 0;
+          for (int k = 0; k < nt; ++k) {
+            const double q = r2v[k];
+            if (q < r2) {
+              ++rank;
+            } else if (q == r2 && k != m) {
+              const int j2 = b.j[o + k];
+              rank += (j2 < j || (j2 == j && b.code[o + k] < code));
+            }
+          }
+        }
+        if (rank < sel) {
+          double r[3];
+          rvec(b.src[o + m], code, r);
+          const size_t slot = (size_t)i * f.selt + f.off[t] + rank;
+          nl_j[slot] = j;
+          nl_code[slot] = code;
+          nl_rij[3 * slot] = r[0];
+          nl_rij[3 * slot + 1] = r[1];
+          nl_rij[3 * slot + 2] = r[2];
+        }
       }
+      __syncwarp();
     }
-    __syncwarp();
-  }
-  for (int t = 0; t < f.ntypes; ++t) {
-    const int nt = tcnt[t];
-    const int keep = nt < f.sel[t] ? nt : f.sel[t];
-    if (lane == 0) {
-      nl_cnt[(size_t)i * f.ntypes + t] = keep;
-      if (nt > f.sel[t]) atomicAdd(err + kErrSelOverflow, nt - f.sel[t]);
-    }
-    const int zero_code = image_code(0, 0, 0);
-    for (int s = keep + lane; s < f.sel[t]; s += 32) {
+    for (int s = keep + lane; s < sel; s += 32) {
       const size_t slot = (size_t)i * f.selt + f.off[t] + s;
       nl_j[slot] = -1;
       nl_code[slot] = zero_code;
@@ -404,13 +431,43 @@ __device__ void emit_row(const FormatSpec& f, int i, const CandBuf& b, int ncand
       nl_rij[3 * slot + 1] = 0.0;
       nl_rij[3 * slot + 2] = 0.0;
     }
+    if (lane == 0) {
+      nl_cnt[(size_t)i * f.ntypes + t] = keep;
+      if (nt > sel) atomicAdd(err + kErrSelOverflow, nt - sel);
+    }
   }
+}
+
+// Shift of periodic image (n0, n1, n2) and the vector from centre xi to
+// neighbour xj in that image: (xj + shift) - xi, fp64, fixed operation order.
+__device__ __forceinline__ void image_vector(const GridSpec& g, const double (&xi)[3], double x0, double x1,
+                                             double x2, int code, double (&r)[3]) {
+  double sh[3] = {0, 0, 0};
+  if (g.periodic) {
+    const double m0 = (double)(((code >> 20) & 1023) - kImageBias), m1 = (double)(((code >> 10) & 1023) - kImageBias),
+                 m2 = (double)((code & 1023) - kImageBias);
+#pragma unroll
+    for (int c = 0; c < 3; ++c) sh[c] = dadd(dadd(dmul(m0, g.B[c]), dmul(m1, g.B[3 + c])), dmul(m2, g.B[6 + c]));
+  }
+  r[0] = dsub(dadd(x0, sh[0]), xi[0]);
+  r[1] = dsub(dadd(x1, sh[1]), xi[1]);
+  r[2] = dsub(dadd(x2, sh[2]), xi[2]);
 }
 
 // Stencil cells handled per pass: kStencilPerLane consecutive cells per lane.
 constexpr int kStencilPerLane = 4;
 constexpr int kStencilChunk = 32 * kStencilPerLane;
 constexpr int kGatherBatch = 4;  // candidate records loaded per lane before any is used
+
+template <typename K>
+static void format_attr(K kernel, size_t smem) {
+  // the attribute is raised (never lowered) as larger type capacities arrive
+  static size_t set = 48 * 1024;
+  if (smem > set) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    set = smem;
+  }
+}
 
 // One warp per centre.  The stencil (every cell within reach, periodic images
 // included) is flattened; a warp scan over the cells' atom counts numbers the
@@ -426,7 +483,7 @@ __global__ void __launch_bounds__(kFmtWarps * 32)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int i = blockIdx.x * kFmtWarps + warp;
   if (i >= f.nloc) return;  // warp-uniform; no block-level barrier follows
-  CandBuf b = cand_buf(smem, warp, f.cap);
+  const CandBuf b = cand_buf(smem, warp, f);
   int* const c_start = s_start[warp];
   int* const c_pref = s_pref[warp];
   int* const c_code = s_code[warp];
@@ -436,7 +493,9 @@ __global__ void __launch_bounds__(kFmtWarps * 32)
   const int sy = 2 * g.reach[1] + 1, sz = 2 * g.reach[2] + 1;
   const int nstencil = (2 * g.reach[0] + 1) * sy * sz;
   const unsigned lt_mask = (1u << lane) - 1u;
-  int ncand = 0;
+  int ncnt[kMaxTypes];
+#pragma unroll
+  for (int t = 0; t < kMaxTypes; ++t) ncnt[t] = 0;
   for (int s0 = 0; s0 < nstencil; s0 += kStencilChunk) {
     // counts of this lane's cells, then a warp scan
     int cnt[kStencilPerLane], st[kStencilPerLane], cd[kStencilPerLane];
@@ -482,89 +541,62 @@ __global__ void __launch_bounds__(kFmtWarps * 32)
     }
     __syncwarp();
     for (int k0 = 0; k0 < total; k0 += 32 * kGatherBatch) {
-      CellRec rec[kGatherBatch];
-      int rcode[kGatherBatch];
+      double2 ra[kGatherBatch], rc[kGatherBatch];
+      int rcode[kGatherBatch], ridx[kGatherBatch];
 #pragma unroll
       for (int u = 0; u < kGatherBatch; ++u) {
         const int k = k0 + 32 * u + lane;
         rcode[u] = -1;
+        ridx[u] = 0;
+        ra[u] = make_double2(0.0, 0.0);
+        rc[u] = make_double2(0.0, 0.0);
         if (k < total) {
           int q = 0;  // last cell with c_pref[q] <= k (that cell holds k)
 #pragma unroll
           for (int step = kStencilChunk / 2; step > 0; step >>= 1)
             if (c_pref[q + step] <= k) q += step;
-          const CellRec* src = cell_rec + c_start[q] + (k - c_pref[q]);
-          const double2 a = __ldg(reinterpret_cast<const double2*>(src));
-          const double2 c = __ldg(reinterpret_cast<const double2*>(src) + 1);
-          const long long jt = __double_as_longlong(c.y);  // {int j, int t}, little-endian
-          rec[u].x = a.x;
-          rec[u].y = a.y;
-          rec[u].z = c.x;
-          rec[u].j = (int)(unsigned)(jt & 0xffffffffll);
-          rec[u].t = (int)(jt >> 32);
+          ridx[u] = c_start[q] + (k - c_pref[q]);
+          const double2* src = reinterpret_cast<const double2*>(cell_rec + ridx[u]);
+          ra[u] = __ldg(src);
+          rc[u] = __ldg(src + 1);
           rcode[u] = c_code[q];
-        } else {
-          rec[u].x = rec[u].y = rec[u].z = 0.0;
-          rec[u].j = rec[u].t = 0;
         }
       }
 #pragma unroll
       for (int u = 0; u < kGatherBatch; ++u) {
+        const long long jt = __double_as_longlong(rc[u].y);  // {int j, int t}, little-endian
+        const int j = (int)(unsigned)(jt & 0xffffffffll), tj = (int)(jt >> 32), code = rcode[u];
         bool valid = false;
-        double r[3] = {0, 0, 0}, r2 = 0;
-        const int j = rec[u].j, tj = rec[u].t, code = rcode[u];
+        double r2 = 0;
         if (code >= 0) {
-          const int im0 = ((code >> 20) & 1023) - kImageBias, im1 = ((code >> 10) & 1023) - kImageBias,
-                    im2 = (code & 1023) - kImageBias;
-          double sh[3] = {0, 0, 0};
-          if (g.periodic) {
-            const double m0 = (double)im0, m1 = (double)im1, m2 = (double)im2;
-#pragma unroll
-            for (int c = 0; c < 3; ++c) sh[c] = dadd(dadd(dmul(m0, g.B[c]), dmul(m1, g.B[3 + c])), dmul(m2, g.B[6 + c]));
-          }
-          const double xj[3] = {rec[u].x, rec[u].y, rec[u].z};
-#pragma unroll
-          for (int c = 0; c < 3; ++c) r[c] = dsub(dadd(xj[c], sh[c]), xi[c]);
+          double r[3];
+          image_vector(g, xi, ra[u].x, ra[u].y, rc[u].x, code, r);
           r2 = dadd(dadd(dmul(r[0], r[0]), dmul(r[1], r[1])), dmul(r[2], r[2]));
-          const bool self = (j == i) && im0 == 0 && im1 == 0 && im2 == 0;
+          const bool self = (j == i) && code == image_code(0, 0, 0);
           const bool type_ok = (tj >= 0 && tj < f.ntypes);
           if (!type_ok && !self && r2 < f.rc2) atomicAdd(err + kErrBadType, 1);
           valid = !self && type_ok && (r2 < f.rc2);
         }
-        const unsigned m = __ballot_sync(0xffffffffu, valid);
-        const int pos = ncand + __popc(m & lt_mask);
-        if (valid && pos < f.cap) {
-          b.r2[pos] = r2;
-          b.r[3 * pos] = r[0];
-          b.r[3 * pos + 1] = r[1];
-          b.r[3 * pos + 2] = r[2];
-          b.j[pos] = j;
-          b.code[pos] = code;
-          b.t[pos] = tj;
-        }
-        ncand += __popc(m);
+        cand_push(f, b, ncnt, valid, tj, r2, j, code, ridx[u], lt_mask);
       }
     }
     __syncwarp();
   }
-  if (ncand > f.cap) {
-    if (lane == 0) atomicAdd(err + kErrCandCapacity, 1);
-    ncand = f.cap;
-  }
   __syncwarp();
-  emit_row(f, i, b, ncand, lane, nl_j, nl_code, nl_rij, nl_cnt, err);
+  emit_row(f, i, b, ncnt, lane, nl_j, nl_code, nl_rij, nl_cnt, err,
+           [&](int src, int code, double (&r)[3]) {
+             const double2* p = reinterpret_cast<const double2*>(cell_rec + src);
+             const double2 a = __ldg(p), c = __ldg(p + 1);
+             image_vector(g, xi, a.x, a.y, c.x, code, r);
+           });
 }
 
 void launch_format(cudaStream_t st, const FormatSpec& f, const GridSpec& g, const double* xw, const int* cell_of,
                    const int* cell_start, const CellRec* cell_rec, int* nl_j, int* nl_code, double* nl_rij,
                    int* nl_cnt, int* err) {
   if (f.nloc <= 0) return;
-  const size_t smem = format_smem_bytes(f.cap);
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(k_format, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    attr_set = true;
-  }
+  const size_t smem = format_smem_bytes(f);
+  format_attr(k_format, smem);
   count_launch();
   k_format<<<(f.nloc + kFmtWarps - 1) / kFmtWarps, kFmtWarps * 32, smem, st>>>(f, g, xw, cell_of, cell_start,
                                                                                cell_rec, nl_j, nl_code, nl_rij,
@@ -584,18 +616,21 @@ __global__ void __launch_bounds__(kFmtWarps * 32)
   if (row >= f.nloc) return;
   const int i = ilist[row];
   if (i < 0 || i >= f.nloc) return;
-  CandBuf b = cand_buf(smem, warp, f.cap);
+  const CandBuf b = cand_buf(smem, warp, f);
   const double xi[3] = {coord[3 * i], coord[3 * i + 1], coord[3 * i + 2]};
   const unsigned lt_mask = (1u << lane) - 1u;
   const int beg = cand_start[row], end = cand_start[row + 1];
-  int ncand = 0;
+  int ncnt[kMaxTypes];
+#pragma unroll
+  for (int t = 0; t < kMaxTypes; ++t) ncnt[t] = 0;
   for (int k = beg + lane; k - lane < end; k += 32) {
     bool valid = false;
     int j = -1, tj = 0;
-    double r[3] = {0, 0, 0}, r2 = 0;
+    double r2 = 0;
     if (k < end) {
       j = cand[k];
       if (j >= 0 && j < f.nall && j != i) {
+        double r[3];
 #pragma unroll
         for (int c = 0; c < 3; ++c) r[c] = dsub(coord[3 * j + c], xi[c]);
         r2 = dadd(dadd(dmul(r[0], r[0]), dmul(r[1], r[1])), dmul(r[2], r[2]));
@@ -605,25 +640,15 @@ __global__ void __launch_bounds__(kFmtWarps * 32)
         valid = type_ok && r2 < f.rc2;
       }
     }
-    const unsigned m = __ballot_sync(0xffffffffu, valid);
-    const int pos = ncand + __popc(m & lt_mask);
-    if (valid && pos < f.cap) {
-      b.r2[pos] = r2;
-      b.r[3 * pos] = r[0];
-      b.r[3 * pos + 1] = r[1];
-      b.r[3 * pos + 2] = r[2];
-      b.j[pos] = j;
-      b.code[pos] = image_code(0, 0, 0);
-      b.t[pos] = tj;
-    }
-    ncand += __popc(m);
-  }
-  if (ncand > f.cap) {
-    if (lane == 0) atomicAdd(err + kErrCandCapacity, 1);
-    ncand = f.cap;
+    cand_push(f, b, ncnt, valid, tj, r2, j, image_code(0, 0, 0), j, lt_mask);
   }
   __syncwarp();
-  emit_row(f, i, b, ncand, lane, nl_j, nl_code, nl_rij, nl_cnt, err);
+  const double xi0 = xi[0], xi1 = xi[1], xi2 = xi[2];
+  emit_row(f, i, b, ncnt, lane, nl_j, nl_code, nl_rij, nl_cnt, err, [=](int src, int, double (&r)[3]) {
+    r[0] = dsub(coord[3 * src], xi0);
+    r[1] = dsub(coord[3 * src + 1], xi1);
+    r[2] = dsub(coord[3 * src + 2], xi2);
+  });
 }
 
 // Canonical destination-major graph (the reference's direct-engine input):
@@ -646,18 +671,21 @@ __global__ void __launch_bounds__(kFmtWarps * 32)
     atype32[i] = (ti >= 0 && ti < f.ntypes) ? (int)ti : -1;
     if (ti < 0 || ti >= f.ntypes) atomicAdd(err + kErrBadType, 1);
   }
-  CandBuf b = cand_buf(smem, warp, f.cap);
+  const CandBuf b = cand_buf(smem, warp, f);
   const unsigned lt_mask = (1u << lane) - 1u;
   const int64_t beg = row_ptr[i], end = row_ptr[i + 1];
-  int ncand = 0;
+  int ncnt[kMaxTypes];
+#pragma unroll
+  for (int t = 0; t < kMaxTypes; ++t) ncnt[t] = 0;
   for (int64_t k = beg + lane; k - lane < end; k += 32) {
     bool valid = false;
     int j = -1, tj = 0;
-    double r[3] = {0, 0, 0}, r2 = 0;
+    double r2 = 0;
     if (k < end) {
       const uint32_t src = source[k];
       if (src < (uint32_t)f.nall) {
         j = (int)src;
+        double r[3];
 #pragma unroll
         for (int c = 0; c < 3; ++c) r[c] = (double)edge_vec[3 * k + c];
         r2 = dadd(dadd(dmul(r[0], r[0]), dmul(r[1], r[1])), dmul(r[2], r[2]));
@@ -668,38 +696,25 @@ __global__ void __launch_bounds__(kFmtWarps * 32)
         valid = type_ok && r2 > 0.0 && r2 < f.rc2;
       }
     }
-    const unsigned m = __ballot_sync(0xffffffffu, valid);
-    const int pos = ncand + __popc(m & lt_mask);
-    if (valid && pos < f.cap) {
-      b.r2[pos] = r2;
-      b.r[3 * pos] = r[0];
-      b.r[3 * pos + 1] = r[1];
-      b.r[3 * pos + 2] = r[2];
-      b.j[pos] = j;
-      b.code[pos] = (int)(k - beg);
-      b.t[pos] = tj;
-    }
-    ncand += __popc(m);
-  }
-  if (ncand > f.cap) {
-    if (lane == 0) atomicAdd(err + kErrCandCapacity, 1);
-    ncand = f.cap;
+    // the image code is the edge's position in the row
+    cand_push(f, b, ncnt, valid, tj, r2, j, (int)(k - beg), (int)(k - beg), lt_mask);
   }
   __syncwarp();
-  emit_row(f, i, b, ncand, lane, nl_j, nl_code, nl_rij, nl_cnt, err);
+  emit_row(f, i, b, ncnt, lane, nl_j, nl_code, nl_rij, nl_cnt, err, [&](int src, int, double (&r)[3]) {
+    const int64_t k = beg + src;
+#pragma unroll
+    for (int c = 0; c < 3; ++c) r[c] = (double)edge_vec[3 * k + c];
+  });
 }
 
 void launch_format_graph(cudaStream_t st, const FormatSpec& f, const int64_t* atype64, const int64_t* row_ptr,
                          const uint32_t* source, const float* edge_vec, int* atype32, int* nl_j, int* nl_code,
                          double* nl_rij, int* nl_cnt, int* err) {
   if (f.nloc <= 0) return;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(k_format_graph, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    attr_set = true;
-  }
+  const size_t smem = format_smem_bytes(f);
+  format_attr(k_format_graph, smem);
   count_launch();
-  k_format_graph<<<(f.nloc + kFmtWarps - 1) / kFmtWarps, kFmtWarps * 32, format_smem_bytes(f.cap), st>>>(
+  k_format_graph<<<(f.nloc + kFmtWarps - 1) / kFmtWarps, kFmtWarps * 32, smem, st>>>(
       f, atype64, row_ptr, source, edge_vec, atype32, nl_j, nl_code, nl_rij, nl_cnt, err);
 }
 
@@ -707,13 +722,10 @@ void launch_format_candidates(cudaStream_t st, const FormatSpec& f, const double
                               const int* ilist, const int* cand_start, const int* cand, int* nl_j, int* nl_code,
                               double* nl_rij, int* nl_cnt, int* err) {
   if (f.nloc <= 0) return;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(k_format_candidates, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    attr_set = true;
-  }
+  const size_t smem = format_smem_bytes(f);
+  format_attr(k_format_candidates, smem);
   count_launch();
-  k_format_candidates<<<(f.nloc + kFmtWarps - 1) / kFmtWarps, kFmtWarps * 32, format_smem_bytes(f.cap), st>>>(
+  k_format_candidates<<<(f.nloc + kFmtWarps - 1) / kFmtWarps, kFmtWarps * 32, smem, st>>>(
       f, coord, atype, ilist, cand_start, cand, nl_j, nl_code, nl_rij, nl_cnt, err);
 }
 

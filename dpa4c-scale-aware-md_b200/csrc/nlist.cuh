@@ -43,11 +43,19 @@ constexpr int kCellsPerCut = 2;
 int make_grid(bool periodic, const double* box, const double* region, double rcut, long long max_cells, GridSpec& g);
 
 struct FormatSpec {
-  int nloc, nall, ntypes, selt, cap;
+  int nloc, nall, ntypes, selt;
   int sel[kMaxTypes];
   int off[kMaxTypes + 1];
+  // per-type candidate capacity: type t's in-cutoff candidates of one centre
+  // occupy [cap_off[t], cap_off[t+1]) of the warp's buffer (set by
+  // format_caps; more than that is a capacity error)
+  int cap_off[kMaxTypes + 1];
+  int cap_max;
   double rc2;
 };
+
+// Fills cap_off / cap_max from sel: max(128, 2 sel[t]) rounded up to 32.
+void format_caps(FormatSpec& f);
 
 // Host helpers (identical arithmetic to the oracle's cell set-up).
 void make_box_inverse(const double* box, double* Binv, double* width);
@@ -61,7 +69,7 @@ void launch_exclusive_scan(cudaStream_t st, int n, const int* in, int* out, int*
 size_t scan_scratch_ints(int n);
 void launch_fill_cells(cudaStream_t st, int nall, const double* xw, const int* atype, const int* cell_of,
                        const int* cell_start, int* cursor, CellRec* cell_rec);
-size_t format_smem_bytes(int cap);
+size_t format_smem_bytes(const FormatSpec& f);
 void launch_format(cudaStream_t st, const FormatSpec& f, const GridSpec& g, const double* xw, const int* cell_of,
                    const int* cell_start, const CellRec* cell_rec, int* nl_j, int* nl_code, double* nl_rij,
                    int* nl_cnt, int* err);

@@ -102,13 +102,14 @@ extern "C" b200dp_status b200dp_build_nlist_noalloc(void* stream, int nlocal, in
   f.nall = nall;
   f.ntypes = ntypes;
   f.selt = selt;
-  f.cap = std::max(256, ((2 * selt + 31) / 32) * 32);
   f.off[0] = 0;
   for (int t = 0; t < ntypes; ++t) {
     f.sel[t] = sel[t];
     f.off[t + 1] = f.off[t] + sel[t];
   }
   f.rc2 = rcut * rcut;
+  format_caps(f);
+  if (format_smem_bytes(f) > 200 * 1024) return B200DP_ERR_UNSUPPORTED;
 
   // Calls share the scratch: the counters that must start at zero are cleared here.
   if (cudaMemsetAsync(err, 0, sizeof(int) * kErrCount, st) != cudaSuccess) return B200DP_ERR_CUDA;

@@ -571,111 +571,129 @@ void launch_fit_seed(cudaStream_t st, int Mmax, const int* range, int N, const P
 }
 
 // ---------------------------------------------------------------- assembly
-// One warp per atom j: F_j = sum_{own row} g - sum_{edges into j} g, and the
-// atom virial of j = sum_{edges into j} -g (x) r, in a fixed order (own row by
-// slot, reverse list sorted by slot id, xor-tree warp reduction).
+// One warp per atom j: F_j = sum_{own row} g - sum_{edges into j} g, in a fixed
+// order (own row by slot, reverse list sorted by slot id, xor-tree warp
+// reduction).  The total virial -sum g (x) r runs over every edge once, so it
+// is summed over the own rows, where g and r are read contiguously; the
+// per-atom virial (edges into j) is formed only when asked for.  Energy and
+// virial are reduced in the same launch: each block writes its sums, and the
+// last block to finish adds the blocks' sums in block order.
 constexpr int kAsmWarps = 8;
+constexpr int kAsmCols = 10;  // virial (9) + energy
+
+template <bool kAtomVirial>
 __global__ void __launch_bounds__(kAsmWarps * 32)
     k_assemble(int nloc, int nall, int selt, const int* __restrict__ nl_j, const double* __restrict__ gslot,
                const double* __restrict__ rij, const int* __restrict__ rev_start, const int* __restrict__ rev_slot,
-               double* __restrict__ force, double* __restrict__ atom_virial, double* __restrict__ virial_rows) {
+               const double* __restrict__ atom_e, double* __restrict__ force, double* __restrict__ atom_virial,
+               double* __restrict__ partial, unsigned* __restrict__ done, double* __restrict__ energy,
+               double* __restrict__ virial) {
+  __shared__ double s_part[kAsmWarps][kAsmCols];
+  __shared__ int s_last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int j = blockIdx.x * kAsmWarps + warp;
-  if (j >= nall) return;
   double f[3] = {0, 0, 0};
   double v[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
+  double av[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
+  double e = 0;
   if (j < nloc) {
     const size_t row = (size_t)j * selt;
     for (int s = lane; s < selt; s += 32) {
       if (nl_j[row + s] >= 0) {
         const double* g = gslot + 3 * (row + s);
-        f[0] += g[0];
-        f[1] += g[1];
-        f[2] += g[2];
+        const double* r = rij + 3 * (row + s);
+        const double g3[3] = {g[0], g[1], g[2]}, r3[3] = {r[0], r[1], r[2]};
+        f[0] += g3[0];
+        f[1] += g3[1];
+        f[2] += g3[2];
+#pragma unroll
+        for (int a = 0; a < 3; ++a)
+#pragma unroll
+          for (int b = 0; b < 3; ++b) v[3 * a + b] -= g3[a] * r3[b];
       }
     }
+    if (lane == 0) e = atom_e[j];
   }
-  for (int q = rev_start[j] + lane; q < rev_start[j + 1]; q += 32) {
-    const size_t slot = (size_t)rev_slot[q];
-    const double g[3] = {gslot[3 * slot], gslot[3 * slot + 1], gslot[3 * slot + 2]};
-    const double r[3] = {rij[3 * slot], rij[3 * slot + 1], rij[3 * slot + 2]};
-    f[0] -= g[0];
-    f[1] -= g[1];
-    f[2] -= g[2];
+  if (j < nall) {
+    for (int q = rev_start[j] + lane; q < rev_start[j + 1]; q += 32) {
+      const size_t slot = (size_t)rev_slot[q];
+      const double g[3] = {gslot[3 * slot], gslot[3 * slot + 1], gslot[3 * slot + 2]};
+      f[0] -= g[0];
+      f[1] -= g[1];
+      f[2] -= g[2];
+      if (kAtomVirial) {
+        const double r[3] = {rij[3 * slot], rij[3 * slot + 1], rij[3 * slot + 2]};
 #pragma unroll
-    for (int a = 0; a < 3; ++a)
+        for (int a = 0; a < 3; ++a)
 #pragma unroll
-      for (int b = 0; b < 3; ++b) v[3 * a + b] -= g[a] * r[b];
+          for (int b = 0; b < 3; ++b) av[3 * a + b] -= g[a] * r[b];
+      }
+    }
   }
 #pragma unroll
   for (int c = 0; c < 3; ++c) f[c] = warp_sum(f[c]);
 #pragma unroll
   for (int c = 0; c < 9; ++c) v[c] = warp_sum(v[c]);
-  if (lane == 0) {
-    force[3 * (size_t)j] = f[0];
-    force[3 * (size_t)j + 1] = f[1];
-    force[3 * (size_t)j + 2] = f[2];
+  if (kAtomVirial) {
 #pragma unroll
-    for (int c = 0; c < 9; ++c) {
-      virial_rows[9 * (size_t)j + c] = v[c];
-      if (atom_virial) atom_virial[9 * (size_t)j + c] = v[c];
+    for (int c = 0; c < 9; ++c) av[c] = warp_sum(av[c]);
+  }
+  if (lane == 0) {
+    if (j < nall) {
+      force[3 * (size_t)j] = f[0];
+      force[3 * (size_t)j + 1] = f[1];
+      force[3 * (size_t)j + 2] = f[2];
+      if (kAtomVirial) {
+#pragma unroll
+        for (int c = 0; c < 9; ++c) atom_virial[9 * (size_t)j + c] = av[c];
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < 9; ++c) s_part[warp][c] = v[c];
+    s_part[warp][9] = e;
+  }
+  __syncthreads();
+  if (threadIdx.x < kAsmCols) {
+    double acc = 0;
+#pragma unroll
+    for (int w = 0; w < kAsmWarps; ++w) acc += s_part[w][threadIdx.x];
+    partial[(size_t)blockIdx.x * kAsmCols + threadIdx.x] = acc;
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = (atomicAdd(done, 1u) == gridDim.x - 1);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int c = warp; c < kAsmCols; c += kAsmWarps) {
+    double acc = 0;
+    for (int b = lane; b < (int)gridDim.x; b += 32) acc += __ldcg(partial + (size_t)b * kAsmCols + c);
+    acc = warp_sum(acc);
+    if (lane == 0) {
+      if (c < 9)
+        virial[c] = acc;
+      else
+        energy[0] = acc;
     }
   }
+  if (threadIdx.x == 0) *done = 0u;  // ready for the next launch
 }
+
+int assemble_blocks(int nall) { return (nall + kAsmWarps - 1) / kAsmWarps; }
 
 void launch_assemble(cudaStream_t st, int nloc, int nall, int selt, const int* nl_j, const double* gslot,
-                     const double* rij, const int* rev_start, const int* rev_slot, double* force,
-                     double* atom_virial, double* virial_rows) {
+                     const double* rij, const int* rev_start, const int* rev_slot, const double* atom_e,
+                     double* force, double* atom_virial, double* partial, unsigned* done, double* energy,
+                     double* virial) {
   if (nall <= 0) return;
   count_launch();
-  k_assemble<<<(nall + kAsmWarps - 1) / kAsmWarps, kAsmWarps * 32, 0, st>>>(nloc, nall, selt, nl_j, gslot, rij,
-                                                                            rev_start, rev_slot, force, atom_virial,
-                                                                            virial_rows);
-}
-
-// Fixed-shape two-stage column reduction (kReduceBlocks x 256 threads, then
-// one block), so the result is identical from run to run.
-__global__ void __launch_bounds__(256) k_reduce_partial(int n, int C, const double* __restrict__ rows,
-                                                         double* __restrict__ partial) {
-  __shared__ double sh[256];
-  const int chunk = (n + gridDim.x - 1) / gridDim.x;
-  const int r0 = blockIdx.x * chunk, r1 = min(n, r0 + chunk);
-  for (int c = 0; c < C; ++c) {
-    double acc = 0;
-    for (int r = r0 + threadIdx.x; r < r1; r += blockDim.x) acc += rows[(size_t)r * C + c];
-    sh[threadIdx.x] = acc;
-    __syncthreads();
-    for (int o = 128; o > 0; o >>= 1) {
-      if (threadIdx.x < o) sh[threadIdx.x] += sh[threadIdx.x + o];
-      __syncthreads();
-    }
-    if (threadIdx.x == 0) partial[blockIdx.x * C + c] = sh[0];
-    __syncthreads();
-  }
-}
-
-__global__ void __launch_bounds__(256) k_reduce_final(int nb, int C, const double* __restrict__ partial,
-                                                       double* __restrict__ out) {
-  __shared__ double sh[256];
-  for (int c = 0; c < C; ++c) {
-    double acc = 0;
-    for (int b = threadIdx.x; b < nb; b += blockDim.x) acc += partial[b * C + c];
-    sh[threadIdx.x] = acc;
-    __syncthreads();
-    for (int o = 128; o > 0; o >>= 1) {
-      if (threadIdx.x < o) sh[threadIdx.x] += sh[threadIdx.x + o];
-      __syncthreads();
-    }
-    if (threadIdx.x == 0) out[c] = sh[0];
-    __syncthreads();
-  }
-}
-
-void launch_reduce_rows(cudaStream_t st, int n, int C, const double* rows, double* partial, double* out) {
-  count_launch();
-  k_reduce_partial<<<kReduceBlocks, 256, 0, st>>>(n, C, rows, partial);
-  count_launch();
-  k_reduce_final<<<1, 256, 0, st>>>(kReduceBlocks, C, partial, out);
+  const int nb = assemble_blocks(nall);
+  if (atom_virial)
+    k_assemble<true><<<nb, kAsmWarps * 32, 0, st>>>(nloc, nall, selt, nl_j, gslot, rij, rev_start, rev_slot, atom_e,
+                                                    force, atom_virial, partial, done, energy, virial);
+  else
+    k_assemble<false><<<nb, kAsmWarps * 32, 0, st>>>(nloc, nall, selt, nl_j, gslot, rij, rev_start, rev_slot,
+                                                     atom_e, force, nullptr, partial, done, energy, virial);
 }
 
 // ---------------------------------------------------------------- instantiations

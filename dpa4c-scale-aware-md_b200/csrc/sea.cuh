@@ -63,11 +63,13 @@ template <typename P>
 void launch_fit_backward_layer(cudaStream_t st, int Mmax, const int* range, int Nin, int Nout, const P* dZ,
                                const P* W, const P* dY_next, P* dX, const P* th_prev, P* dZ_prev);
 
+// Forces, optional per-atom virials, and the total energy and virial (fixed
+// summation order).  partial holds 10 doubles per assembly block; *done must
+// be zero before the first launch and is zero again after each.
 void launch_assemble(cudaStream_t st, int nloc, int nall, int selt, const int* nl_j, const double* gslot,
-                     const double* rij, const int* rev_start, const int* rev_slot, double* force,
-                     double* atom_virial, double* virial_rows);
-// Deterministic column sums of rows [n][C] into out[C] (fixed reduction tree).
-void launch_reduce_rows(cudaStream_t st, int n, int C, const double* rows, double* partial, double* out);
-constexpr int kReduceBlocks = 148;
+                     const double* rij, const int* rev_start, const int* rev_slot, const double* atom_e,
+                     double* force, double* atom_virial, double* partial, unsigned* done, double* energy,
+                     double* virial);
+int assemble_blocks(int nall);
 
 }  // namespace b200dp
