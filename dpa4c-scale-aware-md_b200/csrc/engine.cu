@@ -2,9 +2,10 @@
 // the C ABI declared in include/b200dp.h.
 //
 // Stage sequence of one evaluation (all on the caller's stream, no host sync):
-//   bin -> scan -> fill -> format (neighbour graph)  -> reverse index -> type partition
+//   bin -> scan -> fill -> format (neighbour graph) -> type partition
 //   descriptor forward -> fitting forward/backward per centre type
-//   descriptor backward (edge gradients) -> assembly -> deterministic reductions
+//   descriptor backward (edge gradients) -> assembly (own rows + fixed-point
+//   scatter, energy/virial reduction) -> accumulator conversion
 // The reference runs the same roles as forward / fitting / node VJP / edge
 // force / widen (components/deepmd-op/overlays/op/pt/dpa4c/graph_compress.cu:1690-1900).
 #include <algorithm>
@@ -239,12 +240,14 @@ b200dp_status Engine::init(const char* path, const b200dp_options* o) {
     return fp64 ? descriptor_bwd_smem<double>(sd, ch) : descriptor_bwd_smem<float>(sd, ch);
   };
   while (ch_bwd > 8 && bwd_smem(ch_bwd) > budget) ch_bwd /= 2;
+  // the legacy-stream memsets above must land before work on other streams
+  B200DP_CUDA_TRY(cudaDeviceSynchronize());
   return B200DP_OK;
 }
 
 void Engine::release() {
   for (DevBuf* b : {&w_emb, &w_embT, &xw, &cell_of, &cell_count, &cell_start, &cell_cursor, &cell_rec, &nl_j,
-                    &nl_code, &nl_rij, &nl_cnt, &rev_count, &rev_start, &rev_cursor, &rev_tmp, &rev_slot,
+                    &nl_code, &nl_rij, &nl_cnt, &acc_f, &acc_v, &nonfinite,
                     &blk_counts, &type_start, &perm_pos, &perm_atom, &Tbuf, &Dbuf, &dDbuf, &atom_e, &gslot,
                     &asm_done, &err_buf, &reduce_part, &scalars, &h_coord, &h_atype, &h_force, &h_aviral, &h_ae,
                     &cand_start, &cand_list, &ilist_d, &tc_nets, &ecount, &eoff, &tstart, &rec_rt, &rec_row,
@@ -284,11 +287,13 @@ b200dp_status Engine::ensure_buffers(int nloc, int nall, int ncells, int ncand) 
   B200DP_CUDA_TRY(nl_code.ensure(sizeof(int) * S));
   B200DP_CUDA_TRY(nl_rij.ensure(sizeof(double) * 3 * S));
   B200DP_CUDA_TRY(nl_cnt.ensure(sizeof(int) * L * sd.ntypes));
-  B200DP_CUDA_TRY(rev_count.ensure(sizeof(int) * A));
-  B200DP_CUDA_TRY(rev_start.ensure(sizeof(int) * (A + 1)));
-  B200DP_CUDA_TRY(rev_cursor.ensure(sizeof(int) * A));
-  B200DP_CUDA_TRY(rev_tmp.ensure(sizeof(int) * S));
-  B200DP_CUDA_TRY(rev_slot.ensure(sizeof(int) * S));
+  {
+    // force accumulators are cleared by each assembly; fresh memory is cleared once
+    const size_t bf = acc_f.bytes, bn = nonfinite.bytes;
+    B200DP_CUDA_TRY(acc_f.ensure(sizeof(unsigned long long) * 6 * A));
+    B200DP_CUDA_TRY(nonfinite.ensure(sizeof(unsigned) * A));
+    if (acc_f.bytes != bf || nonfinite.bytes != bn) acc_fresh = true;
+  }
   B200DP_CUDA_TRY(blk_counts.ensure(sizeof(int) * (type_partition_blocks((int)L) + 1) * sd.ntypes));
   B200DP_CUDA_TRY(type_start.ensure(sizeof(int) * (sd.ntypes + 1)));
   B200DP_CUDA_TRY(perm_pos.ensure(sizeof(int) * L));
@@ -307,7 +312,7 @@ b200dp_status Engine::ensure_buffers(int nloc, int nall, int ncells, int ncand) 
   for (auto& b : dz_l) B200DP_CUDA_TRY(b.ensure(ps * L * maxfit));
   B200DP_CUDA_TRY(atom_e.ensure(sizeof(double) * L));
   B200DP_CUDA_TRY(gslot.ensure(sizeof(double) * 3 * S));
-  B200DP_CUDA_TRY(reduce_part.ensure(sizeof(double) * 10 * assemble_blocks((int)A)));
+  B200DP_CUDA_TRY(reduce_part.ensure(sizeof(double) * 10 * assemble_blocks((int)L)));
   if (ncand > 0) B200DP_CUDA_TRY(cand_list.ensure(sizeof(int) * (size_t)ncand));
   const size_t nscan = std::max({(size_t)C, A, (size_t)sd.nnets * L}) + 1;
   B200DP_CUDA_TRY(scan_scratch.ensure(sizeof(int) * scan_scratch_ints((int)nscan)));
@@ -404,8 +409,6 @@ template <typename P>
 b200dp_status Engine::run_model(cudaStream_t st, int nloc, int nall, const int* d_atype, double* d_force,
                                 double* d_atom_energy, double* d_atom_virial, double* d_energy, double* d_virial) {
   int* err_d = static_cast<int*>(err_buf.ptr);
-  launch_reverse_index(st, nloc, nall, sd.selt, nl_j.as<int>(), rev_count.as<int>(), rev_start.as<int>(),
-                       rev_cursor.as<int>(), rev_tmp.as<int>(), rev_slot.as<int>(), scan_scratch.as<int>());
   launch_type_partition(st, nloc, hm.ntypes, d_atype, blk_counts.as<int>(), type_start.as<int>(),
                         perm_pos.as<int>(), perm_atom.as<int>(), err_d);
   mark(st, 1);
@@ -511,8 +514,19 @@ b200dp_status Engine::run_model(cudaStream_t st, int nloc, int nall, const int* 
                              gslot.as<double>());
   }
   mark(st, 4);
+  if (d_atom_virial) {
+    const size_t bv = acc_v.bytes;
+    B200DP_CUDA_TRY(acc_v.ensure(sizeof(unsigned long long) * 18 * std::max(nall, 1)));
+    if (acc_v.bytes != bv) B200DP_CUDA_TRY(cudaMemsetAsync(acc_v.ptr, 0, acc_v.bytes, st));
+  }
+  if (acc_fresh) {
+    B200DP_CUDA_TRY(cudaMemsetAsync(acc_f.ptr, 0, acc_f.bytes, st));
+    B200DP_CUDA_TRY(cudaMemsetAsync(nonfinite.ptr, 0, nonfinite.bytes, st));
+    acc_fresh = false;
+  }
   launch_assemble(st, nloc, nall, sd.selt, nl_j.as<int>(), gslot.as<double>(), nl_rij.as<double>(),
-                  rev_start.as<int>(), rev_slot.as<int>(), atom_e.as<double>(), d_force, d_atom_virial,
+                  atom_e.as<double>(), d_force, d_atom_virial, acc_f.as<unsigned long long>(),
+                  d_atom_virial ? acc_v.as<unsigned long long>() : nullptr, nonfinite.as<unsigned>(),
                   reduce_part.as<double>(), asm_done.as<unsigned>(), d_energy, d_virial);
   if (d_atom_energy)
     B200DP_CUDA_TRY(cudaMemcpyAsync(d_atom_energy, atom_e.ptr, sizeof(double) * nloc, cudaMemcpyDeviceToDevice, st));

@@ -47,7 +47,8 @@ struct Engine {
   // neighbour graph
   DevBuf xw, cell_of, cell_count, cell_start, cell_cursor, cell_rec;
   DevBuf nl_j, nl_code, nl_rij, nl_cnt;
-  DevBuf rev_count, rev_start, rev_cursor, rev_tmp, rev_slot;
+  DevBuf acc_f, acc_v, nonfinite;  // fixed-point force / atom-virial accumulators (zero between calls)
+  bool acc_fresh = false;
   DevBuf blk_counts, type_start, perm_pos, perm_atom;
   DevBuf cand_start, cand_list, ilist_d;
   // tensor-core embedding path (mixed mode)

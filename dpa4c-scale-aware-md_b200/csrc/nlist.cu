@@ -729,70 +729,6 @@ void launch_format_candidates(cudaStream_t st, const FormatSpec& f, const double
       f, coord, atype, ilist, cand_start, cand, nl_j, nl_code, nl_rij, nl_cnt, err);
 }
 
-// ---------------------------------------------------------------- reverse index
-__global__ void k_rev_count(long long nslots, const int* __restrict__ nl_j, int* __restrict__ rev_count) {
-  for (long long s = blockIdx.x * (long long)blockDim.x + threadIdx.x; s < nslots;
-       s += (long long)gridDim.x * blockDim.x) {
-    const int j = nl_j[s];
-    if (j >= 0) atomicAdd(rev_count + j, 1);
-  }
-}
-
-__global__ void k_rev_fill(long long nslots, const int* __restrict__ nl_j, const int* __restrict__ rev_start,
-                           int* __restrict__ cursor, int* __restrict__ rev_tmp) {
-  for (long long s = blockIdx.x * (long long)blockDim.x + threadIdx.x; s < nslots;
-       s += (long long)gridDim.x * blockDim.x) {
-    const int j = nl_j[s];
-    if (j >= 0) rev_tmp[rev_start[j] + atomicAdd(cursor + j, 1)] = (int)s;
-  }
-}
-
-// One warp per owner: rank-sort the owner's slot ids so the force gather
-// sums them in a fixed order (deterministic, atomic-free assembly).
-constexpr int kRevWarps = 8;
-constexpr int kRevStage = 256;
-__global__ void __launch_bounds__(kRevWarps * 32)
-    k_rev_sort(int nall, const int* __restrict__ rev_start, const int* __restrict__ rev_tmp, int* __restrict__ rev_slot) {
-  __shared__ int stage[kRevWarps][kRevStage];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int j = blockIdx.x * kRevWarps + warp;
-  if (j >= nall) return;
-  const int beg = rev_start[j], len = rev_start[j + 1] - beg;
-  const int* src = rev_tmp + beg;
-  if (len <= kRevStage) {
-    for (int e = lane; e < len; e += 32) stage[warp][e] = src[e];
-    __syncwarp();
-    src = stage[warp];
-  }
-  for (int e = lane; e < len; e += 32) {
-    const int key = src[e];
-    int rank = 0;
-    for (int e2 = 0; e2 < len; ++e2) rank += (src[e2] < key);
-    rev_slot[beg + rank] = key;
-  }
-}
-
-void launch_reverse_index(cudaStream_t st, int nloc, int nall, int selt, const int* nl_j, int* rev_count,
-                          int* rev_start, int* rev_cursor, int* rev_tmp, int* rev_slot, int* scan_scratch) {
-  const long long nslots = (long long)nloc * selt;
-  cudaMemsetAsync(rev_count, 0, sizeof(int) * (size_t)nall, st);
-  cudaMemsetAsync(rev_cursor, 0, sizeof(int) * (size_t)nall, st);
-  if (nslots > 0) {
-    const int blocks = (int)std::min<long long>((nslots + 255) / 256, 148 * 16);
-    count_launch();
-    k_rev_count<<<blocks, 256, 0, st>>>(nslots, nl_j, rev_count);
-    launch_exclusive_scan(st, nall, rev_count, rev_start, scan_scratch);
-    count_launch();
-    k_rev_fill<<<blocks, 256, 0, st>>>(nslots, nl_j, rev_start, rev_cursor, rev_tmp);
-  } else {
-    launch_exclusive_scan(st, nall, rev_count, rev_start, scan_scratch);
-  }
-  if (nall > 0) {
-    count_launch();
-    k_rev_sort<<<(nall + kRevWarps - 1) / kRevWarps, kRevWarps * 32, 0, st>>>(nall, rev_start, rev_tmp, rev_slot);
-  }
-}
-
 // ---------------------------------------------------------------- type partition
 // Stable partition of local atoms by type: perm_pos[i] is atom i's row in the
 // type-grouped order, perm_atom the inverse, type_start[t] the first row of t.

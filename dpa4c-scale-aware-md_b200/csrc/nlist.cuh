@@ -1,6 +1,6 @@
 // Neighbour-graph builder: cell binning, warp-ballot compacted candidate
-// rows, deterministic per-type (r^2, j, image) ordering, and the reverse
-// (owner-major) index used by the atomic-free force assembly.
+// rows, deterministic per-type (r^2, j, image) ordering, and the stable
+// partition of centres by type.
 //
 // Replaces the LAMMPS/Kokkos candidate list and compact canonical graph of
 // the reference (LO/KOKKOS/npair_kokkos.cpp:151-460,
@@ -82,8 +82,6 @@ void launch_format_graph(cudaStream_t st, const FormatSpec& f, const int64_t* at
 void launch_format_candidates(cudaStream_t st, const FormatSpec& f, const double* coord, const int* atype,
                               const int* ilist, const int* cand_start, const int* cand, int* nl_j, int* nl_code,
                               double* nl_rij, int* nl_cnt, int* err);
-void launch_reverse_index(cudaStream_t st, int nloc, int nall, int selt, const int* nl_j, int* rev_count,
-                          int* rev_start, int* rev_cursor, int* rev_tmp, int* rev_slot, int* scan_scratch);
 void launch_type_partition(cudaStream_t st, int nloc, int ntypes, const int* atype, int* blk_counts,
                            int* type_start, int* perm_pos, int* perm_atom, int* err);
 size_t type_partition_blocks(int nloc);

@@ -571,82 +571,99 @@ void launch_fit_seed(cudaStream_t st, int Mmax, const int* range, int N, const P
 }
 
 // ---------------------------------------------------------------- assembly
-// One warp per atom j: F_j = sum_{own row} g - sum_{edges into j} g, in a fixed
-// order (own row by slot, reverse list sorted by slot id, xor-tree warp
-// reduction).  The total virial -sum g (x) r runs over every edge once, so it
-// is summed over the own rows, where g and r are read contiguously; the
-// per-atom virial (edges into j) is formed only when asked for.  Energy and
-// virial are reduced in the same launch: each block writes its sums, and the
-// last block to finish adds the blocks' sums in block order.
+// F_j = sum_{own row} g - sum_{edges into j} g.  One warp per centre i sums its
+// own row in a fixed order (slot order, xor-tree warp reduction) and scatters
+// -g of every edge into the neighbour's accumulator.  The accumulators are
+// 128-bit two's-complement fixed point with 64 fractional bits, added with
+// integer atomics: integer addition is associative, so the sum does not
+// depend on the order in which edges arrive (deterministic), and it is exact
+// to 2^-64 per term.  A second pass converts each accumulator to fp64, adds
+// the own-row part and clears the accumulator for the next call.
+//
+// The total virial -sum g (x) r runs over every edge once and is summed over
+// the own rows; the per-atom virial (edges into j) is scattered the same way
+// when asked for.  Energy and virial are reduced in the first launch: each
+// block writes its sums, and the last block to finish adds the blocks' sums
+// in block order.
 constexpr int kAsmWarps = 8;
 constexpr int kAsmCols = 10;  // virial (9) + energy
 
+// v * 2^64 as (lo, hi), truncated toward -inf at 2^-64; |v| < 2^63.  For
+// |v| < 1 the high word's increment (integer part + carry) is usually zero
+// and is then not sent.
+__device__ __forceinline__ void fix_add(unsigned long long* __restrict__ p, double v) {
+  const double fl = floor(v);
+  const unsigned long long hi = (unsigned long long)(long long)fl;
+  const unsigned long long lo = (unsigned long long)((v - fl) * 0x1p64);
+  const unsigned long long old = atomicAdd(p, lo);
+  const unsigned long long inc = hi + (old + lo < old ? 1ull : 0ull);
+  if (inc) atomicAdd(p + 1, inc);
+}
+
+__device__ __forceinline__ double fix_value(unsigned long long lo, unsigned long long hi) {
+  return (double)(long long)hi + (double)lo * 0x1p-64;
+}
+
 template <bool kAtomVirial>
 __global__ void __launch_bounds__(kAsmWarps * 32)
-    k_assemble(int nloc, int nall, int selt, const int* __restrict__ nl_j, const double* __restrict__ gslot,
-               const double* __restrict__ rij, const int* __restrict__ rev_start, const int* __restrict__ rev_slot,
-               const double* __restrict__ atom_e, double* __restrict__ force, double* __restrict__ atom_virial,
-               double* __restrict__ partial, unsigned* __restrict__ done, double* __restrict__ energy,
-               double* __restrict__ virial) {
+    k_assemble(int nloc, int selt, const int* __restrict__ nl_j, const double* __restrict__ gslot,
+               const double* __restrict__ rij, const double* __restrict__ atom_e, double* __restrict__ force,
+               unsigned long long* __restrict__ acc_f, unsigned long long* __restrict__ acc_v,
+               unsigned* __restrict__ nonfinite, double* __restrict__ partial, unsigned* __restrict__ done,
+               double* __restrict__ energy, double* __restrict__ virial) {
   __shared__ double s_part[kAsmWarps][kAsmCols];
   __shared__ int s_last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int j = blockIdx.x * kAsmWarps + warp;
+  const int i = blockIdx.x * kAsmWarps + warp;
   double f[3] = {0, 0, 0};
   double v[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
-  double av[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
   double e = 0;
-  if (j < nloc) {
-    const size_t row = (size_t)j * selt;
+  if (i < nloc) {
+    const size_t row = (size_t)i * selt;
     for (int s = lane; s < selt; s += 32) {
-      if (nl_j[row + s] >= 0) {
+      const int j = nl_j[row + s];
+      if (j >= 0) {
         const double* g = gslot + 3 * (row + s);
         const double* r = rij + 3 * (row + s);
         const double g3[3] = {g[0], g[1], g[2]}, r3[3] = {r[0], r[1], r[2]};
         f[0] += g3[0];
         f[1] += g3[1];
         f[2] += g3[2];
+        double w[9];
 #pragma unroll
         for (int a = 0; a < 3; ++a)
 #pragma unroll
-          for (int b = 0; b < 3; ++b) v[3 * a + b] -= g3[a] * r3[b];
+          for (int b = 0; b < 3; ++b) {
+            w[3 * a + b] = -g3[a] * r3[b];
+            v[3 * a + b] += w[3 * a + b];
+          }
+        bool finite = isfinite(g3[0]) && isfinite(g3[1]) && isfinite(g3[2]);
+        if (finite) {
+#pragma unroll
+          for (int c = 0; c < 3; ++c) fix_add(acc_f + 2 * (3 * (size_t)j + c), -g3[c]);
+          if (kAtomVirial) {
+#pragma unroll
+            for (int c = 0; c < 9; ++c) finite = finite && isfinite(w[c]);
+            if (finite) {
+#pragma unroll
+              for (int c = 0; c < 9; ++c) fix_add(acc_v + 2 * (9 * (size_t)j + c), w[c]);
+            }
+          }
+        }
+        if (!finite) atomicOr(nonfinite + j, 1u);
       }
     }
-    if (lane == 0) e = atom_e[j];
-  }
-  if (j < nall) {
-    for (int q = rev_start[j] + lane; q < rev_start[j + 1]; q += 32) {
-      const size_t slot = (size_t)rev_slot[q];
-      const double g[3] = {gslot[3 * slot], gslot[3 * slot + 1], gslot[3 * slot + 2]};
-      f[0] -= g[0];
-      f[1] -= g[1];
-      f[2] -= g[2];
-      if (kAtomVirial) {
-        const double r[3] = {rij[3 * slot], rij[3 * slot + 1], rij[3 * slot + 2]};
-#pragma unroll
-        for (int a = 0; a < 3; ++a)
-#pragma unroll
-          for (int b = 0; b < 3; ++b) av[3 * a + b] -= g[a] * r[b];
-      }
-    }
+    if (lane == 0) e = atom_e[i];
   }
 #pragma unroll
   for (int c = 0; c < 3; ++c) f[c] = warp_sum(f[c]);
 #pragma unroll
   for (int c = 0; c < 9; ++c) v[c] = warp_sum(v[c]);
-  if (kAtomVirial) {
-#pragma unroll
-    for (int c = 0; c < 9; ++c) av[c] = warp_sum(av[c]);
-  }
   if (lane == 0) {
-    if (j < nall) {
-      force[3 * (size_t)j] = f[0];
-      force[3 * (size_t)j + 1] = f[1];
-      force[3 * (size_t)j + 2] = f[2];
-      if (kAtomVirial) {
-#pragma unroll
-        for (int c = 0; c < 9; ++c) atom_virial[9 * (size_t)j + c] = av[c];
-      }
+    if (i < nloc) {
+      force[3 * (size_t)i] = f[0];
+      force[3 * (size_t)i + 1] = f[1];
+      force[3 * (size_t)i + 2] = f[2];
     }
 #pragma unroll
     for (int c = 0; c < 9; ++c) s_part[warp][c] = v[c];
@@ -679,21 +696,56 @@ __global__ void __launch_bounds__(kAsmWarps * 32)
   if (threadIdx.x == 0) *done = 0u;  // ready for the next launch
 }
 
-int assemble_blocks(int nall) { return (nall + kAsmWarps - 1) / kAsmWarps; }
+// Adds the scattered sums to the own-row forces (ghost atoms have no own row),
+// writes the per-atom virials, and clears the accumulators.
+template <bool kAtomVirial>
+__global__ void k_assemble_finish(int nloc, int nall, double* __restrict__ force, double* __restrict__ atom_virial,
+                                  unsigned long long* __restrict__ acc_f, unsigned long long* __restrict__ acc_v,
+                                  unsigned* __restrict__ nonfinite) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= nall) return;
+  const bool bad = nonfinite[j] != 0u;
+  if (bad) nonfinite[j] = 0u;
+  const double nan = __longlong_as_double(0x7ff8000000000000ll);
+#pragma unroll
+  for (int c = 0; c < 3; ++c) {
+    ulonglong2* a = reinterpret_cast<ulonglong2*>(acc_f) + 3 * (size_t)j + c;
+    const ulonglong2 q = *a;
+    const double own = j < nloc ? force[3 * (size_t)j + c] : 0.0;
+    force[3 * (size_t)j + c] = bad ? nan : own + fix_value(q.x, q.y);
+    *a = make_ulonglong2(0ull, 0ull);
+  }
+  if (kAtomVirial) {
+#pragma unroll
+    for (int c = 0; c < 9; ++c) {
+      ulonglong2* a = reinterpret_cast<ulonglong2*>(acc_v) + 9 * (size_t)j + c;
+      const ulonglong2 q = *a;
+      atom_virial[9 * (size_t)j + c] = bad ? nan : fix_value(q.x, q.y);
+      *a = make_ulonglong2(0ull, 0ull);
+    }
+  }
+}
+
+int assemble_blocks(int nloc) { return std::max(1, (nloc + kAsmWarps - 1) / kAsmWarps); }
 
 void launch_assemble(cudaStream_t st, int nloc, int nall, int selt, const int* nl_j, const double* gslot,
-                     const double* rij, const int* rev_start, const int* rev_slot, const double* atom_e,
-                     double* force, double* atom_virial, double* partial, unsigned* done, double* energy,
-                     double* virial) {
+                     const double* rij, const double* atom_e, double* force, double* atom_virial,
+                     unsigned long long* acc_f, unsigned long long* acc_v, unsigned* nonfinite, double* partial,
+                     unsigned* done, double* energy, double* virial) {
   if (nall <= 0) return;
+  const int nb = assemble_blocks(nloc);
+  const int fb = (nall + 255) / 256;
   count_launch();
-  const int nb = assemble_blocks(nall);
-  if (atom_virial)
-    k_assemble<true><<<nb, kAsmWarps * 32, 0, st>>>(nloc, nall, selt, nl_j, gslot, rij, rev_start, rev_slot, atom_e,
-                                                    force, atom_virial, partial, done, energy, virial);
-  else
-    k_assemble<false><<<nb, kAsmWarps * 32, 0, st>>>(nloc, nall, selt, nl_j, gslot, rij, rev_start, rev_slot,
-                                                     atom_e, force, nullptr, partial, done, energy, virial);
+  count_launch();
+  if (atom_virial) {
+    k_assemble<true><<<nb, kAsmWarps * 32, 0, st>>>(nloc, selt, nl_j, gslot, rij, atom_e, force, acc_f, acc_v,
+                                                    nonfinite, partial, done, energy, virial);
+    k_assemble_finish<true><<<fb, 256, 0, st>>>(nloc, nall, force, atom_virial, acc_f, acc_v, nonfinite);
+  } else {
+    k_assemble<false><<<nb, kAsmWarps * 32, 0, st>>>(nloc, selt, nl_j, gslot, rij, atom_e, force, acc_f, nullptr,
+                                                     nonfinite, partial, done, energy, virial);
+    k_assemble_finish<false><<<fb, 256, 0, st>>>(nloc, nall, force, nullptr, acc_f, nullptr, nonfinite);
+  }
 }
 
 // ---------------------------------------------------------------- instantiations

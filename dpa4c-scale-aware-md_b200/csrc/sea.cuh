@@ -63,13 +63,15 @@ template <typename P>
 void launch_fit_backward_layer(cudaStream_t st, int Mmax, const int* range, int Nin, int Nout, const P* dZ,
                                const P* W, const P* dY_next, P* dX, const P* th_prev, P* dZ_prev);
 
-// Forces, optional per-atom virials, and the total energy and virial (fixed
-// summation order).  partial holds 10 doubles per assembly block; *done must
-// be zero before the first launch and is zero again after each.
+// Forces, optional per-atom virials, and the total energy and virial
+// (deterministic).  partial holds 10 doubles per assembly block
+// (assemble_blocks(nloc)); acc_f (6 x u64 per atom), acc_v (18 x u64 per atom,
+// only with atom_virial), nonfinite (one per atom) and *done must be zero
+// before the first launch and are zero again after each.
 void launch_assemble(cudaStream_t st, int nloc, int nall, int selt, const int* nl_j, const double* gslot,
-                     const double* rij, const int* rev_start, const int* rev_slot, const double* atom_e,
-                     double* force, double* atom_virial, double* partial, unsigned* done, double* energy,
-                     double* virial);
-int assemble_blocks(int nall);
+                     const double* rij, const double* atom_e, double* force, double* atom_virial,
+                     unsigned long long* acc_f, unsigned long long* acc_v, unsigned* nonfinite, double* partial,
+                     unsigned* done, double* energy, double* virial);
+int assemble_blocks(int nloc);
 
 }  // namespace b200dp
