@@ -131,54 +131,71 @@ void launch_bin(cudaStream_t st, int nall, const double* coord, const GridSpec& 
   k_bin<<<(nall + 255) / 256, 256, 0, st>>>(nall, coord, g, xw, cell_of, cell_count);
 }
 
-// Single-block exclusive scan; out has n+1 entries (out[n] = total).
+// Single-block exclusive scan; out has n+1 entries (out[n] = total).  Each
+// pass stages 8192 values through shared memory so that global loads and
+// stores are coalesced 16-byte vectors while every thread scans 8
+// consecutive values.
+constexpr int kScanPer = 8;
+constexpr int kScanPass = 1024 * kScanPer;
+
 __global__ void __launch_bounds__(1024) k_exclusive_scan(int n, const int* __restrict__ in, int* __restrict__ out) {
+  __shared__ __align__(16) int stage[kScanPass];
   __shared__ int warp_ex[32];
   __shared__ int block_total;
-  __shared__ int carry;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid == 0) carry = 0;
-  __syncthreads();
-  constexpr int kPer = 16;  // all of a pass's loads are issued before the scan
-  for (int base = 0; base < n; base += 1024 * kPer) {
-    int v[kPer];
-    int local = 0;
-    const int i0 = base + tid * kPer;
-    if (i0 + kPer <= n && (reinterpret_cast<uintptr_t>(in) & 15) == 0) {
+  const bool vec_in = (reinterpret_cast<uintptr_t>(in) & 15) == 0;
+  const bool vec_out = (reinterpret_cast<uintptr_t>(out) & 15) == 0;
+  int carry = 0;
+  for (int base = 0; base < n; base += kScanPass) {
+    const int m = min(kScanPass, n - base);
+    if (vec_in && m == kScanPass) {
 #pragma unroll
-      for (int q = 0; q < kPer; q += 4) {
-        const int4 w = __ldg(reinterpret_cast<const int4*>(in + i0 + q));
-        v[q] = w.x;
-        v[q + 1] = w.y;
-        v[q + 2] = w.z;
-        v[q + 3] = w.w;
+      for (int k = 0; k < kScanPer / 4; ++k) {
+        const int q = tid + 1024 * k;
+        reinterpret_cast<int4*>(stage)[q] = __ldg(reinterpret_cast<const int4*>(in + base) + q);
       }
     } else {
-#pragma unroll
-      for (int q = 0; q < kPer; ++q) v[q] = (i0 + q < n) ? in[i0 + q] : 0;
+      for (int q = tid; q < kScanPass; q += 1024) stage[q] = q < m ? in[base + q] : 0;
     }
+    __syncthreads();
+    int v[kScanPer];
+    const int4 a = reinterpret_cast<const int4*>(stage)[2 * tid];
+    const int4 b = reinterpret_cast<const int4*>(stage)[2 * tid + 1];
+    v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+    int local = 0;
 #pragma unroll
-    for (int q = 0; q < kPer; ++q) local += v[q];
+    for (int q = 0; q < kScanPer; ++q) local += v[q];
     int wt;
     const int ex = warp_exclusive_scan(local, lane, wt);
     if (lane == 0) warp_ex[warp] = wt;
     __syncthreads();
     if (warp == 0) {
-      const int mine = warp_ex[lane];
       int tot;
-      const int e = warp_exclusive_scan(mine, lane, tot);
+      const int e = warp_exclusive_scan(warp_ex[lane], lane, tot);
       warp_ex[lane] = e;
       if (lane == 0) block_total = tot;
     }
     __syncthreads();
     int run = carry + warp_ex[warp] + ex;
+    int w[kScanPer];
 #pragma unroll
-    for (int q = 0; q < kPer; ++q) {
-      if (i0 + q < n) out[i0 + q] = run;
+    for (int q = 0; q < kScanPer; ++q) {
+      w[q] = run;
       run += v[q];
     }
+    reinterpret_cast<int4*>(stage)[2 * tid] = make_int4(w[0], w[1], w[2], w[3]);
+    reinterpret_cast<int4*>(stage)[2 * tid + 1] = make_int4(w[4], w[5], w[6], w[7]);
+    carry += block_total;
     __syncthreads();
-    if (tid == 0) carry += block_total;
+    if (vec_out && m == kScanPass) {
+#pragma unroll
+      for (int k = 0; k < kScanPer / 4; ++k) {
+        const int q = tid + 1024 * k;
+        reinterpret_cast<int4*>(out + base)[q] = reinterpret_cast<const int4*>(stage)[q];
+      }
+    } else {
+      for (int q = tid; q < m; q += 1024) out[base + q] = stage[q];
+    }
     __syncthreads();
   }
   if (tid == 0) out[n] = carry;
