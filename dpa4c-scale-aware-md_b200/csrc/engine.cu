@@ -71,6 +71,7 @@ static cudaError_t upload(DevBuf& dst, const std::vector<double>& src) {
 
 b200dp_status Engine::init(const char* path, const b200dp_options* o) {
   if (o) opt = *o;
+  if (is_c8_model(path)) return init_c8(path);
   std::string msg = load_model(path, hm);
   if (!msg.empty()) {
     err = msg;
@@ -222,6 +223,95 @@ b200dp_status Engine::init(const char* path, const b200dp_options* o) {
       }
     }
   }
+  return init_tail();
+}
+
+// C8L2 model: shapes for the neighbour list, device copies of every tensor in
+// the engine's arithmetic type (fp64 mode: double, mixed mode: float, which is
+// the reference's own precision for this profile).
+b200dp_status Engine::init_c8(const char* path) {
+  std::string msg = load_c8_model(path, c8h);
+  if (!msg.empty()) {
+    err = msg;
+    return B200DP_ERR_IO;
+  }
+  if (opt.precision != B200DP_FP64 && opt.precision != B200DP_MIXED) {
+    err = "unknown precision";
+    return B200DP_ERR_INVALID;
+  }
+  c8 = true;
+  B200DP_CUDA_TRY(cudaSetDevice(opt.device));
+  hm.ntypes = c8h.ntypes;
+  hm.sel = c8h.sel;
+  hm.rcut = c8h.rcut;
+  hm.rcut_smth = 0;
+  hm.bias_atom_e = c8h.bias;
+  std::memset(&sd, 0, sizeof(sd));
+  sd.ntypes = c8h.ntypes;
+  sd.off[0] = 0;
+  for (int t = 0; t < c8h.ntypes; ++t) {
+    sd.sel[t] = c8h.sel[t];
+    sd.off[t + 1] = sd.off[t] + c8h.sel[t];
+  }
+  sd.selt = sd.off[c8h.ntypes];
+  sd.dim = kC8Dim;
+  sd.rcut = c8h.rcut;
+  const bool fp64 = opt.precision == B200DP_FP64;
+  c8_dev.reserve(16);
+  auto up = [&](const std::vector<double>& v) -> const void* {
+    c8_dev.emplace_back();
+    DevBuf& d = c8_dev.back();
+    const size_t n = std::max<size_t>(v.size(), 1);
+    cudaError_t e;
+    if (fp64) {
+      e = d.ensure(n * sizeof(double));
+      if (e == cudaSuccess && !v.empty()) e = cudaMemcpy(d.ptr, v.data(), v.size() * 8, cudaMemcpyHostToDevice);
+    } else {
+      std::vector<float> f(v.begin(), v.end());
+      e = d.ensure(n * sizeof(float));
+      if (e == cudaSuccess && !f.empty()) e = cudaMemcpy(d.ptr, f.data(), f.size() * 4, cudaMemcpyHostToDevice);
+    }
+    return e == cudaSuccess ? d.ptr : nullptr;
+  };
+  C8Dev& m = c8m;
+  m.ntypes = c8h.ntypes;
+  m.nint = c8h.nint;
+  m.nfit = (int)c8h.layers.size();
+  m.act = c8h.act;
+  m.stride = c8h.stride;
+  m.rcut = c8h.rcut;
+  m.eps = c8h.eps;
+  m.floor_ = c8h.floor_;
+  m.b_head = c8h.b_head;
+  m.table = up(c8h.table);
+  m.film = up(c8h.film);
+  m.temb = up(c8h.temb);
+  m.readout = up(c8h.readout);
+  m.mean = up(c8h.mean);
+  m.istd = up(c8h.istd);
+  for (int l = 0; l < m.nfit; ++l) {
+    m.fw[l] = up(c8h.layers[l].w);
+    m.fb[l] = up(c8h.layers[l].b);
+    m.fdin[l] = c8h.layers[l].din;
+    m.fdout[l] = c8h.layers[l].dout;
+    m.fres[l] = c8h.res[l];
+  }
+  m.w_head = up(c8h.w_head);
+  c8_dev.emplace_back();
+  B200DP_CUDA_TRY(c8_dev.back().ensure(sizeof(double) * c8h.ntypes));
+  B200DP_CUDA_TRY(cudaMemcpy(c8_dev.back().ptr, c8h.bias.data(), sizeof(double) * c8h.ntypes,
+                             cudaMemcpyHostToDevice));
+  m.bias = c8_dev.back().as<double>();
+  for (const DevBuf& b : c8_dev)
+    if (!b.ptr) {
+      err = "cannot upload the C8L2 model";
+      return B200DP_ERR_CUDA;
+    }
+  return init_tail();
+}
+
+b200dp_status Engine::init_tail() {
+  const bool fp64 = opt.precision == B200DP_FP64;
   if (format_smem_bytes(format_spec(0, 0)) > 200 * 1024) {
     err = "neighbour selection too large for the list-format kernel";
     return B200DP_ERR_UNSUPPORTED;
@@ -258,6 +348,12 @@ void Engine::release() {
   for (auto& v : fit_b)
     for (auto& b : v) b.release();
   for (auto& b : fit_dev) b.release();
+  for (auto& b : c8_dev) b.release();
+  for (DevBuf* b : {&c8_state, &c8_q}) b->release();
+  for (auto* arr : {&c8_Z, &c8_H})
+    for (auto& b : *arr) b.release();
+  for (auto* arr : {&c8_dH, &c8_dZ})
+    for (auto& b : *arr) b.release();
   for (auto* arr : {&At_hi, &At_lo, &THf, &Yf})
     for (auto& b : *arr) b.release();
   for (auto* arr : {&Z_hi, &Z_lo, &DYf})
@@ -310,6 +406,19 @@ b200dp_status Engine::ensure_buffers(int nloc, int nall, int ncells, int ncand) 
   }
   for (auto& b : dy_l) B200DP_CUDA_TRY(b.ensure(ps * L * maxfit));
   for (auto& b : dz_l) B200DP_CUDA_TRY(b.ensure(ps * L * maxfit));
+  if (c8) {
+    // descriptor and its gradient reuse Dbuf / dDbuf (rows in atom order)
+    int wmax = 1;
+    for (int l = 0; l < c8m.nfit; ++l) {
+      B200DP_CUDA_TRY(c8_Z[l].ensure(ps * L * c8m.fdout[l]));
+      B200DP_CUDA_TRY(c8_H[l].ensure(ps * L * c8m.fdout[l]));
+      wmax = std::max(wmax, c8m.fdout[l]);
+    }
+    for (auto& b : c8_dH) B200DP_CUDA_TRY(b.ensure(ps * L * wmax));
+    for (auto& b : c8_dZ) B200DP_CUDA_TRY(b.ensure(ps * L * wmax));
+    B200DP_CUDA_TRY(c8_state.ensure(ps * L * kC8State));
+    B200DP_CUDA_TRY(c8_q.ensure(ps * L * kC8State));
+  }
   B200DP_CUDA_TRY(atom_e.ensure(sizeof(double) * L));
   B200DP_CUDA_TRY(gslot.ensure(sizeof(double) * 3 * S));
   B200DP_CUDA_TRY(reduce_part.ensure(sizeof(double) * 10 * assemble_blocks((int)L)));
@@ -406,8 +515,49 @@ FormatSpec Engine::format_spec(int nloc, int nall) const {
 
 // Model stages after the neighbour list is formatted.
 template <typename P>
+C8Work<P> Engine::c8_work() const {
+  C8Work<P> w;
+  w.desc = Dbuf.as<P>();
+  w.dD = dDbuf.as<P>();
+  w.state = c8_state.as<P>();
+  w.q = c8_q.as<P>();
+  for (int l = 0; l < kC8MaxFit; ++l) {
+    w.Z[l] = c8_Z[l].as<P>();
+    w.H[l] = c8_H[l].as<P>();
+  }
+  for (int k = 0; k < 2; ++k) {
+    w.dH[k] = c8_dH[k].as<P>();
+    w.dZ[k] = c8_dZ[k].as<P>();
+  }
+  return w;
+}
+
+// C8L2 stages: descriptor forward (edge moments + node readout), fitting
+// forward and backward, node readout VJP, edge recomputation, assembly.
+template <typename P>
+b200dp_status Engine::run_c8(cudaStream_t st, int nloc, int nall, const int* d_atype, double* d_force,
+                             double* d_atom_energy, double* d_atom_virial, double* d_energy, double* d_virial) {
+  int* err_d = static_cast<int*>(err_buf.ptr);
+  // reports centre types outside [0, ntypes) (neighbours are checked by the list builder)
+  launch_type_partition(st, nloc, hm.ntypes, d_atype, blk_counts.as<int>(), type_start.as<int>(),
+                        perm_pos.as<int>(), perm_atom.as<int>(), err_d);
+  mark(st, 1);
+  const C8Work<P> w = c8_work<P>();
+  launch_c8_forward<P>(st, c8m, nloc, sd.selt, nl_j.as<int>(), nl_rij.as<double>(), d_atype, w);
+  mark(st, 2);
+  launch_c8_fitting<P>(st, c8m, nloc, d_atype, w, atom_e.as<double>());
+  mark(st, 3);
+  launch_c8_node_backward<P>(st, c8m, nloc, w);
+  launch_c8_edge_backward<P>(st, c8m, nloc, sd.selt, nl_j.as<int>(), nl_rij.as<double>(), d_atype, w,
+                             gslot.as<double>());
+  mark(st, 4);
+  return finish_assembly(st, nloc, nall, d_force, d_atom_energy, d_atom_virial, d_energy, d_virial);
+}
+
+template <typename P>
 b200dp_status Engine::run_model(cudaStream_t st, int nloc, int nall, const int* d_atype, double* d_force,
                                 double* d_atom_energy, double* d_atom_virial, double* d_energy, double* d_virial) {
+  if (c8) return run_c8<P>(st, nloc, nall, d_atype, d_force, d_atom_energy, d_atom_virial, d_energy, d_virial);
   int* err_d = static_cast<int*>(err_buf.ptr);
   launch_type_partition(st, nloc, hm.ntypes, d_atype, blk_counts.as<int>(), type_start.as<int>(),
                         perm_pos.as<int>(), perm_atom.as<int>(), err_d);
@@ -514,6 +664,13 @@ b200dp_status Engine::run_model(cudaStream_t st, int nloc, int nall, const int* 
                              gslot.as<double>());
   }
   mark(st, 4);
+  return finish_assembly(st, nloc, nall, d_force, d_atom_energy, d_atom_virial, d_energy, d_virial);
+}
+
+// Force / virial assembly over the slot gradients in gslot and the energy
+// reduction of atom_e (shared by both model profiles).
+b200dp_status Engine::finish_assembly(cudaStream_t st, int nloc, int nall, double* d_force, double* d_atom_energy,
+                                      double* d_atom_virial, double* d_energy, double* d_virial) {
   if (d_atom_virial) {
     const size_t bv = acc_v.bytes;
     B200DP_CUDA_TRY(acc_v.ensure(sizeof(unsigned long long) * 18 * std::max(nall, 1)));
@@ -809,6 +966,10 @@ b200dp_status b200dp_model_info_get(const b200dp_engine* engine, b200dp_model_in
   out->type_one_side = m.type_one_side;
   out->rcut = m.rcut;
   out->rcut_smth = m.rcut_smth;
+  if (engine->e.c8) {  // C8L2: 70 invariants, shared fitting net, no embedding nets
+    out->descriptor_dim = b200dp::kC8Dim;
+    out->n_fitting_layers = engine->e.c8m.nfit;
+  }
   return B200DP_OK;
 }
 
@@ -867,7 +1028,11 @@ b200dp_status b200dp_last_descriptor(b200dp_engine* engine, double* descriptor, 
   const int n = e.last_nloc, dim = e.sd.dim;
   if (n <= 0) return B200DP_OK;
   std::vector<int> perm(n);
-  B200DP_CUDA_TRY(cudaMemcpy(perm.data(), e.perm_pos.ptr, sizeof(int) * n, cudaMemcpyDeviceToHost));
+  if (e.c8) {  // C8L2 rows are in atom order
+    for (int i = 0; i < n; ++i) perm[i] = i;
+  } else {
+    B200DP_CUDA_TRY(cudaMemcpy(perm.data(), e.perm_pos.ptr, sizeof(int) * n, cudaMemcpyDeviceToHost));
+  }
   const bool fp64 = e.opt.precision == B200DP_FP64;
   if (e.use_fit_tc && !e.opt.keep_descriptor) {
     e.err = "descriptor not kept: create the engine with keep_descriptor = 1";

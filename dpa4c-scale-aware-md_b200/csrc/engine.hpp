@@ -8,6 +8,7 @@
 #include <vector>
 
 #include "../../include/b200dp.h"
+#include "c8l2.cuh"
 #include "embed_tc.cuh"
 #include "fit_tc.cuh"
 #include "model.hpp"
@@ -69,6 +70,14 @@ struct Engine {
   std::vector<DevBuf> th_l, y_l;
   std::array<DevBuf, 2> dy_l, dz_l;
   DevBuf atom_e, gslot, asm_done, reduce_part, scalars, err_buf;
+  // C8L2 profile (the reference's production descriptor)
+  bool c8 = false;
+  C8Host c8h;
+  C8Dev c8m;
+  std::vector<DevBuf> c8_dev;  // owns the device copies of the model tensors
+  DevBuf c8_state, c8_q;
+  std::array<DevBuf, kC8MaxFit> c8_Z, c8_H;
+  std::array<DevBuf, 2> c8_dH, c8_dZ;
   // host-call staging
   DevBuf h_coord, h_atype, h_force, h_aviral, h_ae;
 
@@ -81,6 +90,13 @@ struct Engine {
   std::array<cudaEvent_t, 6> events{};
 
   b200dp_status init(const char* path, const b200dp_options* o);
+  b200dp_status init_c8(const char* path);
+  b200dp_status init_tail();
+  template <typename P>
+  C8Work<P> c8_work() const;
+  template <typename P>
+  b200dp_status run_c8(cudaStream_t st, int nloc, int nall, const int* d_atype, double* d_force,
+                       double* d_atom_energy, double* d_atom_virial, double* d_energy, double* d_virial);
   void release();
   b200dp_status ensure_buffers(int nloc, int nall, int ncells, int ncand);
   b200dp_status make_grid(int nall, const double* box, const double* region, bool periodic, GridSpec& g);
@@ -92,6 +108,8 @@ struct Engine {
   template <typename P>
   b200dp_status run_model(cudaStream_t st, int nloc, int nall, const int* d_atype, double* d_force,
                           double* d_atom_energy, double* d_atom_virial, double* d_energy, double* d_virial);
+  b200dp_status finish_assembly(cudaStream_t st, int nloc, int nall, double* d_force, double* d_atom_energy,
+                                double* d_atom_virial, double* d_energy, double* d_virial);
   b200dp_status compute_device(cudaStream_t st, int nloc, int nghost, const double* d_coord, const int* d_atype,
                                const double* box, const double* region, double* d_energy, double* d_force,
                                double* d_virial, double* d_atom_energy, double* d_atom_virial);

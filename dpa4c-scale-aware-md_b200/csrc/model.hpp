@@ -116,4 +116,98 @@ inline std::string load_model(const char* path, HostModel& m) {
   return "";
 }
 
+// C8L2 model file (magic "B2DPC8L2"; layout written by modelgen.py's
+// save_c8): int32 version, ntypes, channels, lmax, interval_count,
+// table_width, n_fit, fit[n_fit], resnets[n_fit], activation, sel[ntypes];
+// fp64 table_stride, table_max, rcut, eps, degree_floor, b_head,
+// bias_atom_e[ntypes]; fp64 table [interval_count][6 * table_width],
+// pair_film [ntypes^2][channels][2], type_embedding [ntypes][channels],
+// readout [8][4][4], output_mean [70], output_inv_std [70]; fitting layers
+// (W [d_in][d_out], b [d_out]) from the 70-wide descriptor; w_head.
+struct C8Host {
+  int ntypes = 0, channels = 0, lmax = 0, nint = 0, width = 0, act = 1;
+  std::vector<int> fit, res, sel;
+  double stride = 0, tmax = 0, rcut = 0, eps = 0, floor_ = 0, b_head = 0;
+  std::vector<double> bias, table, film, temb, readout, mean, istd, w_head;
+  std::vector<HostLayer> layers;
+};
+
+inline bool is_c8_model(const char* path) {
+  std::ifstream f(path, std::ios::binary);
+  char magic[8] = {};
+  return f && f.read(magic, 8) && std::memcmp(magic, "B2DPC8L2", 8) == 0;
+}
+
+inline std::string load_c8_model(const char* path, C8Host& m) {
+  std::ifstream f(path, std::ios::binary);
+  if (!f) return std::string("cannot open model file ") + path;
+  std::vector<char> buf((std::istreambuf_iterator<char>(f)), std::istreambuf_iterator<char>());
+  size_t off = 0;
+  bool short_read = false;
+  auto rd = [&](void* dst, size_t n) {
+    if (off + n > buf.size()) {
+      short_read = true;
+      std::memset(dst, 0, n);
+    } else {
+      std::memcpy(dst, buf.data() + off, n);
+    }
+    off += n;
+  };
+  auto rd_i = [&]() {
+    int32_t v;
+    rd(&v, 4);
+    return (int)v;
+  };
+  auto rd_v = [&](std::vector<double>& v, size_t n) {
+    v.resize(n);
+    if (n) rd(v.data(), 8 * n);
+  };
+  if (buf.size() < 8 || std::memcmp(buf.data(), "B2DPC8L2", 8) != 0) return "model file: bad magic";
+  off = 8;
+  if (rd_i() != 1) return "model file: unsupported version";
+  m.ntypes = rd_i();
+  m.channels = rd_i();
+  m.lmax = rd_i();
+  m.nint = rd_i();
+  m.width = rd_i();
+  const int nf = rd_i();
+  if (m.ntypes <= 0 || m.ntypes > 8) return "model file: ntypes out of range (1..8)";
+  if (m.channels != 8 || m.lmax != 2 || m.width != 8)
+    return "model file: only the C8 L2 profile (8 channels, lmax 2, table width 8) is supported";
+  if (nf <= 0 || nf > 4 || m.nint <= 0) return "model file: bad C8L2 header";
+  for (int i = 0; i < nf; ++i) m.fit.push_back(rd_i());
+  for (int i = 0; i < nf; ++i) m.res.push_back(rd_i());
+  m.act = rd_i();
+  for (int t = 0; t < m.ntypes; ++t) m.sel.push_back(rd_i());
+  double d[6];
+  rd(d, sizeof(d));
+  m.stride = d[0], m.tmax = d[1], m.rcut = d[2], m.eps = d[3], m.floor_ = d[4], m.b_head = d[5];
+  rd_v(m.bias, m.ntypes);
+  if (short_read) return "model file: truncated header";
+  for (int v : m.fit)
+    if (v <= 0 || v > 256) return "model file: fitting width out of range (1..256)";
+  if (m.act != 0 && m.act != 1) return "model file: activation must be 0 (tanh) or 1 (SiLU)";
+  if (!(m.rcut > 0) || !(m.stride > 0) || !(m.floor_ >= 0)) return "model file: bad radial parameters";
+  rd_v(m.table, (size_t)m.nint * 6 * m.width);
+  rd_v(m.film, (size_t)m.ntypes * m.ntypes * m.channels * 2);
+  rd_v(m.temb, (size_t)m.ntypes * m.channels);
+  rd_v(m.readout, 8 * 16);
+  rd_v(m.mean, 70);
+  rd_v(m.istd, 70);
+  int din = 70;
+  for (int l = 0; l < nf; ++l) {
+    HostLayer L;
+    L.din = din;
+    L.dout = m.fit[l];
+    rd_v(L.w, (size_t)L.din * L.dout);
+    rd_v(L.b, L.dout);
+    m.layers.push_back(std::move(L));
+    din = m.fit[l];
+  }
+  rd_v(m.w_head, din);
+  if (short_read) return "model file: truncated weights";
+  if (off != buf.size()) return "model file: trailing bytes";
+  return "";
+}
+
 }  // namespace b200dp
