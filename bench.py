@@ -77,7 +77,10 @@ def dist_env():
 def model_path(kind="water"):
     d = tempfile.mkdtemp(prefix="b200dp_bench_")
     p = os.path.join(d, f"{kind}.b2dp")
-    modelgen.save(modelgen.random_model(kind, seed=0), p)
+    if kind == "c8l2":
+        modelgen.save_c8(modelgen.random_c8_model(seed=0), p)
+    else:
+        modelgen.save(modelgen.random_model(kind, seed=0), p)
     return p
 
 
@@ -410,6 +413,30 @@ def run_b200dp(args, world, rank, local):
             md.close()
         except Exception as ex:  # report, never hide
             md_loop = {"error": repr(ex)}
+    # C8L2 profile (the reference's production descriptor), secondary line item at N = 1:
+    # the same device loop on the headline water system and on a 98,304-atom water box
+    c8 = None
+    if world == 1 and prec == b200dp.MIXED:
+        try:
+            c8 = {"model": "C8L2: 8 channels, lmax 2, 70 invariants, 70-96-96-96 SiLU fitting (random-init)",
+                  "dtype": "f32 (the reference's precision for this model)", "unit": "atom-steps/s"}
+            cp8 = model_path("c8l2")
+            for label, sysf in (("c1_water_12288", systems.config1), ("c4_water_98k", lambda: systems.config4("98k"))):
+                s8 = sysf()
+                dp8 = b200dp.DeepPot(cp8, precision=b200dp.MIXED, device=local)
+                w8 = Periodic(dp8, s8, dev, stream, torch)
+                k8 = max(5, min(args.steps, 20))
+                ms8, l8 = device_loop(dp8, w8, k8, max(3, min(args.warmup, 3)))
+                st8 = stage_pass(dp8, w8, 3)
+                c8[label] = {"value": s8.natoms * k8 / (ms8 / 1e3), "ms_per_step": ms8 / k8, "atoms": s8.natoms,
+                             "steps": k8, "gpu_launches_per_step": int(l8 // k8),
+                             "stage_ms": {k: round(float(q), 4) for k, q in
+                                          zip(["neighbour", "descriptor_fwd", "fitting", "backward", "assembly"],
+                                              st8)}}
+                del w8
+                dp8.close()
+        except Exception as ex:  # report, never hide
+            c8 = {"error": repr(ex)}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, used, dt = cpu_oracle_rate(mp, system)
@@ -438,6 +465,7 @@ def run_b200dp(args, world, rank, local):
             "e2e": e2e,
             "fp64": fp64,
             "md_loop": md_loop,
+            "c8l2": c8,
             "cpu_baseline": cpu,
             "clocks": clocks,
             "flops_per_step": fl["total"],
