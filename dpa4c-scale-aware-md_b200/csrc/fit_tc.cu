@@ -73,15 +73,17 @@ struct GemmArgs {
   int* err;
 };
 
-// Warps 0-15 run the epilogue (4 warps per TMEM lane quadrant share a
-// tile's columns); warp 16 streams the K chunks of A and B into a ring of
-// shared-memory stages, warp 17 issues the MMAs, so loads, MMAs and their
+// Warps 0-7 run the epilogue (2 warps per TMEM lane quadrant share a tile's
+// columns); warp 8 streams the K chunks of A and B into a ring of
+// shared-memory stages, warp 9 issues the MMAs, so loads, MMAs and their
 // bookkeeping proceed independently.  Ring indices advance by increments
-// (no runtime division in the issue loops).
-constexpr int kFitEpiThreads = 512;
+// (no runtime division in the issue loops).  320 threads at <= 102 registers
+// and a 4-stage ring let two CTAs share an SM, so a layer's 3 x 98 tiles run
+// as one wave.
+constexpr int kFitEpiThreads = 256;
 constexpr int kFitThreads = kFitEpiThreads + 64;
 
-__global__ void __launch_bounds__(kFitThreads, 1) k_fit_gemm(GemmArgs a) {
+__global__ void __launch_bounds__(kFitThreads, 2) k_fit_gemm(GemmArgs a) {
   extern __shared__ __align__(1024) unsigned char smem[];
   __shared__ uint64_t full[kMaxStages], empty[kMaxStages], done;
   __shared__ uint32_t tbase;
@@ -179,21 +181,29 @@ __global__ void __launch_bounds__(kFitThreads, 1) k_fit_gemm(GemmArgs a) {
       umma::wait_ld();
       if (!valid) continue;
       const int col0 = nt * a.BN + c * 16;
+      // every global operand of the chunk is loaded before any store: the
+      // stores below may alias them in the compiler's view, and loads issued
+      // behind them would each wait a full L2 round trip
       if (a.mode == kFwd) {
-        float y[16], zs[16];
+        float y[16], zs[16], bb[16], yp[16], wo[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          bb[j] = __ldg(a.bias[t] + col0 + j);
+          yp[j] = a.Yprev ? a.Yprev[colmajor_off(prow, col0 + j, a.ldprev)] : 0.f;
+          wo[j] = a.last ? __ldg(a.wo[t] + col0 + j) : 0.f;
+        }
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int col = col0 + j;
-          const float th = umma::tanh_fast(v[j] + a.bias[t][col]);
+          const float th = umma::tanh_fast(v[j] + bb[j]);
           float yy = th;
-          if (a.Yprev) yy += a.Yprev[colmajor_off(prow, col, a.ldprev)];
+          if (a.Yprev) yy += yp[j];
           a.TH[colmajor_off(prow, col, a.N)] = th;
           a.Y[colmajor_off(prow, col, a.N)] = yy;
           y[j] = yy;
           if (a.last) {
-            const float w = a.wo[t][col];
-            e_acc += (double)(yy * w);
-            zs[j] = w * (1.f - th * th);
+            e_acc += (double)(yy * wo[j]);
+            zs[j] = wo[j] * (1.f - th * th);
           }
         }
 #pragma unroll
@@ -208,18 +218,19 @@ __global__ void __launch_bounds__(kFitThreads, 1) k_fit_gemm(GemmArgs a) {
           }
         }
       } else {
-        float z[16];
+        float z[16], dn[16], thp[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int col = col0 + j;
-          float d = v[j];
-          if (a.dy_is_wo)
-            d += a.wo[t][col];
-          else if (a.DYnext)
-            d += a.DYnext[colmajor_off(prow, col, a.N)];
+          dn[j] = a.dy_is_wo ? __ldg(a.wo[t] + col) : (a.DYnext ? a.DYnext[colmajor_off(prow, col, a.N)] : 0.f);
+          thp[j] = a.THprev[colmajor_off(prow, col, a.N)];
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int col = col0 + j;
+          const float d = v[j] + dn[j];
           if (a.DYout) a.DYout[colmajor_off(prow, col, a.N)] = d;
-          const float th = a.THprev[colmajor_off(prow, col, a.N)];
-          z[j] = d * (1.f - th * th);
+          z[j] = d * (1.f - thp[j] * thp[j]);
         }
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
