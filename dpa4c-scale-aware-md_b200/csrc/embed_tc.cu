@@ -880,47 +880,64 @@ __global__ void __launch_bounds__(128) k_dT(int nloc, int ntypes, int M2, float 
 }
 
 // T_i = sum over nets (fixed order) / N; D = T^T T_< written as fp32 rows and,
-// when requested, pre-tiled bf16 hi/lo for the fitting GEMMs.
+// when requested, pre-tiled bf16 hi/lo for the fitting GEMMs.  A block takes
+// kCombRows consecutive rows: in the tiled layout the same 8-column group of 8
+// consecutive rows of a tile is one contiguous 128-byte line, so consecutive
+// threads take consecutive rows and every line is written whole.
+constexpr int kCombRows = 8;
+
 template <int D3>
-__global__ void __launch_bounds__(128) k_t_combine(TcLists L, int M2, float inv_nnei, const int* __restrict__ perm_atom,
+__global__ void __launch_bounds__(256) k_t_combine(TcLists L, int M2, float inv_nnei, const int* __restrict__ perm_atom,
                                                     const int* __restrict__ ftile, const float* __restrict__ Tq,
                                                     float* __restrict__ T, float* __restrict__ D,
                                                     unsigned char* __restrict__ Dt_hi,
                                                     unsigned char* __restrict__ Dt_lo) {
-  __shared__ float sT[4 * D3];
-  const int r = blockIdx.x;
-  if (r >= L.type_start[L.ntypes]) return;
-  int t = 0;
-  while (t + 1 < L.ntypes && L.type_start[t + 1] <= r) ++t;
+  __shared__ float sT[kCombRows][4 * D3 + 1];  // odd row stride: the 8 rows of a warp read distinct banks
+  __shared__ int s_type[kCombRows];
+  const int nrows = L.type_start[L.ntypes];
+  const int r0 = blockIdx.x * kCombRows;
+  if (r0 >= nrows) return;
   const int tid = threadIdx.x;
-  if (tid < D3) {
+  if (tid < kCombRows) {
+    int t = 0;
+    const int r = min(r0 + tid, nrows - 1);
+    while (t + 1 < L.ntypes && L.type_start[t + 1] <= r) ++t;
+    s_type[tid] = t;
+  }
+  __syncthreads();
+  for (int idx = tid; idx < kCombRows * D3; idx += blockDim.x) {
+    const int rr = idx / D3, c = idx - rr * D3, r = r0 + rr;
+    if (r >= nrows) continue;
+    const int t = s_type[rr];
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     const int q0 = L.type_one_side ? 0 : t * L.ntypes;
     const int q1 = L.type_one_side ? L.nnets : q0 + L.ntypes;
     for (int q = q0; q < q1; ++q) {
       const float* src = Tq + (((size_t)q * L.nloc + r) * 4) * D3;
 #pragma unroll
-      for (int k = 0; k < 4; ++k) acc[k] += src[k * D3 + tid];
+      for (int k = 0; k < 4; ++k) acc[k] += src[k * D3 + c];
     }
     const int atom = perm_atom[r];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const float v = acc[k] * inv_nnei;
-      sT[k * D3 + tid] = v;
-      T[(size_t)atom * 4 * D3 + k * D3 + tid] = v;
+      sT[rr][k * D3 + c] = v;
+      T[(size_t)atom * 4 * D3 + k * D3 + c] = v;
     }
   }
   __syncthreads();
   const int dim = D3 * M2;
-  const int prow = Dt_hi ? 128 * ftile[t] + (r - L.type_start[t]) : 0;
-  for (int g = tid; g < dim / 8; g += blockDim.x) {
+  for (int idx = tid; idx < kCombRows * (dim / 8); idx += blockDim.x) {
+    const int rr = idx % kCombRows, g = idx / kCombRows, r = r0 + rr;
+    if (r >= nrows) continue;
+    const float* st = sT[rr];
     const int k0 = g * 8;
     float v[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int k = k0 + j, aa = k / M2, b = k - aa * M2;
-      v[j] = sT[aa] * sT[b] + sT[D3 + aa] * sT[D3 + b] + sT[2 * D3 + aa] * sT[2 * D3 + b] +
-             sT[3 * D3 + aa] * sT[3 * D3 + b];
+      v[j] = st[aa] * st[b] + st[D3 + aa] * st[D3 + b] + st[2 * D3 + aa] * st[2 * D3 + b] +
+             st[3 * D3 + aa] * st[3 * D3 + b];
     }
     if (D) {
       float4* drow = reinterpret_cast<float4*>(D + (size_t)r * dim + k0);
@@ -928,6 +945,8 @@ __global__ void __launch_bounds__(128) k_t_combine(TcLists L, int M2, float inv_
       drow[1] = make_float4(v[4], v[5], v[6], v[7]);
     }
     if (Dt_hi) {
+      const int t = s_type[rr];
+      const int prow = 128 * ftile[t] + (r - L.type_start[t]);
       const size_t o = umma::tiled_off(prow, k0, dim);
       store8_split(Dt_hi + o, Dt_lo + o, v);
     }
@@ -1193,9 +1212,11 @@ void launch_t_combine(cudaStream_t st, const SeaDev& s, const TcLists& L, const 
   if (L.nloc <= 0) return;
   count_launch();
   if (which(s) == Inst::W25)
-    k_t_combine<100><<<L.nloc, 128, 0, st>>>(L, s.M2, (float)s.inv_nnei, perm_atom, ftile, Tq, T, D, Dt_hi, Dt_lo);
+    k_t_combine<100><<<(L.nloc + kCombRows - 1) / kCombRows, 256, 0, st>>>(L, s.M2, (float)s.inv_nnei, perm_atom,
+                                                                            ftile, Tq, T, D, Dt_hi, Dt_lo);
   else
-    k_t_combine<128><<<L.nloc, 128, 0, st>>>(L, s.M2, (float)s.inv_nnei, perm_atom, ftile, Tq, T, D, Dt_hi, Dt_lo);
+    k_t_combine<128><<<(L.nloc + kCombRows - 1) / kCombRows, 256, 0, st>>>(L, s.M2, (float)s.inv_nnei, perm_atom,
+                                                                            ftile, Tq, T, D, Dt_hi, Dt_lo);
 }
 
 }  // namespace b200dp
