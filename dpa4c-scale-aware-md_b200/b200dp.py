@@ -30,6 +30,7 @@ EXPORTS = [
     "b200dp_options_default", "b200dp_create", "b200dp_destroy", "b200dp_last_error", "b200dp_model_info_get",
     "b200dp_compute_host", "b200dp_compute_host_nlist", "b200dp_compute_device", "b200dp_check",
     "b200dp_sel_overflow_count", "b200dp_last_nlist", "b200dp_last_descriptor", "b200dp_set_stage_timing",
+    "b200dp_set_neighbor_reuse",
     "b200dp_stage_times", "b200dp_kernel_launches", "b200dp_selftest_mma", "b200dp_build_nlist_noalloc",
     "b200dp_direct_bind", "b200dp_direct_energy_force", "b200dp_md_params_default", "b200dp_md_create",
     "b200dp_md_run", "b200dp_md_thermo", "b200dp_md_state", "b200dp_md_destroy",
@@ -42,7 +43,8 @@ class MDParams(ctypes.Structure):
     _fields_ = [("dt", ctypes.c_double), ("ensemble", ctypes.c_int), ("chain", ctypes.c_int),
                 ("t_target", ctypes.c_double), ("t_damp", ctypes.c_double), ("t_init", ctypes.c_double),
                 ("seed", ctypes.c_ulonglong), ("mass", ctypes.c_double * 8), ("p_target", ctypes.c_double),
-                ("p_damp", ctypes.c_double), ("pchain", ctypes.c_int), ("reserved", ctypes.c_int * 11)]
+                ("p_damp", ctypes.c_double), ("pchain", ctypes.c_int), ("rebuild_every", ctypes.c_int),
+                ("skin", ctypes.c_double), ("reserved", ctypes.c_int * 8)]
 
 
 class B200DPError(RuntimeError):
@@ -101,6 +103,7 @@ def load_library(path: str = LIB_PATH):
     L.b200dp_last_nlist.argtypes = [_vp, _ip, _ip, _dp]
     L.b200dp_last_descriptor.argtypes = [_vp, _dp, _dp]
     L.b200dp_set_stage_timing.argtypes = [_vp, ctypes.c_int]
+    L.b200dp_set_neighbor_reuse.argtypes = [_vp, ctypes.c_double, ctypes.c_int]
     L.b200dp_stage_times.argtypes = [_vp, ctypes.POINTER(ctypes.c_float)]
     L.b200dp_selftest_mma.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                       ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_float),
@@ -223,6 +226,10 @@ class DeepPot:
         self._raise(self.L.b200dp_last_descriptor(self.h, _p(d, _dp), _p(dd, _dp)))
         return d, dd
 
+    def set_neighbor_reuse(self, skin: float, every: int):
+        """Periodic calls reuse rcut + skin candidates for `every` calls (0: off)."""
+        self._raise(self.L.b200dp_set_neighbor_reuse(self.h, float(skin), int(every)))
+
     def set_stage_timing(self, on: bool):
         self._raise(self.L.b200dp_set_stage_timing(self.h, int(on)))
 
@@ -253,13 +260,15 @@ class MD:
     THERMO = ("step", "pe", "ke", "temp", "conserved", "press", "volume", "e_thermostat")
 
     def __init__(self, dp: DeepPot, coord, atype, box, masses, dt=0.0005, ensemble=NVE, vel=None, t_init=0.0,
-                 t_target=300.0, t_damp=0.05, chain=3, seed=0, p_target=1.0, p_damp=0.5, pchain=3):
+                 t_target=300.0, t_damp=0.05, chain=3, seed=0, p_target=1.0, p_damp=0.5, pchain=3, skin=2.0,
+                 rebuild_every=10):
         L = load_library()
         p = MDParams()
         L.b200dp_md_params_default(ctypes.byref(p))
         p.dt, p.ensemble, p.chain = dt, ensemble, chain
         p.t_target, p.t_damp, p.t_init, p.seed = t_target, t_damp, t_init, seed
         p.p_target, p.p_damp, p.pchain = p_target, p_damp, pchain
+        p.skin, p.rebuild_every = skin, rebuild_every
         for t, m in enumerate(masses):
             p.mass[t] = m
         coord = np.ascontiguousarray(coord, dtype=np.float64).reshape(-1, 3)

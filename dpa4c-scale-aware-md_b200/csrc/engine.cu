@@ -349,6 +349,7 @@ void Engine::release() {
     for (auto& b : v) b.release();
   for (auto& b : fit_dev) b.release();
   for (auto& b : c8_dev) b.release();
+  for (DevBuf* b : {&vl_cj, &vl_cc, &vl_cnt, &vl_xref, &vl_ls, &vl_stale}) b->release();
   for (DevBuf* b : {&c8_state, &c8_q}) b->release();
   for (auto* arr : {&c8_Z, &c8_H})
     for (auto& b : *arr) b.release();
@@ -722,15 +723,63 @@ b200dp_status Engine::compute_device(cudaStream_t st, int nloc, int nghost, cons
     B200DP_CUDA_TRY(cudaMemsetAsync(d_virial, 0, 9 * sizeof(double), st));
     return B200DP_OK;
   }
-  B200DP_CUDA_TRY(cudaMemsetAsync(cell_count.ptr, 0, sizeof(int) * g.ncells, st));
-  B200DP_CUDA_TRY(cudaMemsetAsync(cell_cursor.ptr, 0, sizeof(int) * g.ncells, st));
-  launch_bin(st, nall, d_coord, g, xw.as<double>(), cell_of.as<int>(), cell_count.as<int>());
-  launch_exclusive_scan(st, g.ncells, cell_count.as<int>(), cell_start.as<int>(), scan_scratch.as<int>());
-  launch_fill_cells(st, nall, xw.as<double>(), d_atype, cell_of.as<int>(), cell_start.as<int>(),
-                    cell_cursor.as<int>(), cell_rec.as<CellRec>());
-  launch_format(st, format_spec(nloc, nall), g, xw.as<double>(), cell_of.as<int>(), cell_start.as<int>(),
-                cell_rec.as<CellRec>(), nl_j.as<int>(), nl_code.as<int>(), nl_rij.as<double>(), nl_cnt.as<int>(),
-                err_d);
+  if (vl_every > 0 && periodic) {
+    // neighbour reuse: skin candidates rebuilt every vl_every calls (or when
+    // the atom count changes), rows formed from them on every call
+    if (!vl_valid || vl_age >= vl_every || vl_n != nall) {
+      GridSpec gc;
+      switch (b200dp::make_grid(true, box, nullptr, hm.rcut + vl_skin, std::max<long long>(4096, 4LL * nall), gc)) {
+        case 0:
+          break;
+        case 1:
+          err = "degenerate box";
+          return B200DP_ERR_INVALID;
+        default:
+          err = "box narrower than (rcut + skin)/15 along a cell vector";
+          return B200DP_ERR_UNSUPPORTED;
+      }
+      rc = ensure_buffers(nloc, nall, gc.ncells, 0);
+      if (rc != B200DP_OK) return rc;
+      const double grow = (hm.rcut + vl_skin) / hm.rcut;
+      vl_cap = std::max(64, ((int)std::ceil(2.0 * sd.selt * grow * grow * grow) + 31) / 32 * 32);
+      B200DP_CUDA_TRY(vl_cj.ensure(sizeof(int) * (size_t)std::max(nloc, 1) * vl_cap));
+      B200DP_CUDA_TRY(vl_cc.ensure(sizeof(int) * (size_t)std::max(nloc, 1) * vl_cap));
+      B200DP_CUDA_TRY(vl_cnt.ensure(sizeof(int) * std::max(nloc, 1)));
+      B200DP_CUDA_TRY(vl_xref.ensure(sizeof(double) * 3 * std::max(nall, 1)));
+      B200DP_CUDA_TRY(vl_ls.ensure(sizeof(int) * 3 * std::max(nall, 1)));
+      if (!vl_stale.ptr) {
+        B200DP_CUDA_TRY(vl_stale.ensure(sizeof(int)));
+        B200DP_CUDA_TRY(cudaMemsetAsync(vl_stale.ptr, 0, sizeof(int), st));
+      }
+      B200DP_CUDA_TRY(cudaMemsetAsync(cell_count.ptr, 0, sizeof(int) * gc.ncells, st));
+      B200DP_CUDA_TRY(cudaMemsetAsync(cell_cursor.ptr, 0, sizeof(int) * gc.ncells, st));
+      launch_bin(st, nall, d_coord, gc, xw.as<double>(), cell_of.as<int>(), cell_count.as<int>(), vl_ls.as<int>());
+      launch_exclusive_scan(st, gc.ncells, cell_count.as<int>(), cell_start.as<int>(), scan_scratch.as<int>());
+      launch_fill_cells(st, nall, xw.as<double>(), d_atype, cell_of.as<int>(), cell_start.as<int>(),
+                        cell_cursor.as<int>(), cell_rec.as<CellRec>());
+      launch_verlet_build(st, format_spec(nloc, nall), gc, hm.rcut + vl_skin, vl_cap, xw.as<double>(),
+                          cell_of.as<int>(), cell_start.as<int>(), cell_rec.as<CellRec>(), vl_cj.as<int>(),
+                          vl_cc.as<int>(), vl_cnt.as<int>(), err_d);
+      B200DP_CUDA_TRY(cudaMemcpyAsync(vl_xref.ptr, d_coord, sizeof(double) * 3 * nall, cudaMemcpyDeviceToDevice, st));
+      vl_valid = true;
+      vl_age = 0;
+      vl_n = nall;
+    }
+    launch_format_verlet(st, format_spec(nloc, nall), g, vl_cap, vl_skin, d_coord, d_atype, vl_ls.as<int>(),
+                         vl_xref.as<double>(), vl_cj.as<int>(), vl_cc.as<int>(), vl_cnt.as<int>(), nl_j.as<int>(),
+                         nl_code.as<int>(), nl_rij.as<double>(), nl_cnt.as<int>(), err_d, vl_stale.as<int>());
+    ++vl_age;
+  } else {
+    B200DP_CUDA_TRY(cudaMemsetAsync(cell_count.ptr, 0, sizeof(int) * g.ncells, st));
+    B200DP_CUDA_TRY(cudaMemsetAsync(cell_cursor.ptr, 0, sizeof(int) * g.ncells, st));
+    launch_bin(st, nall, d_coord, g, xw.as<double>(), cell_of.as<int>(), cell_count.as<int>());
+    launch_exclusive_scan(st, g.ncells, cell_count.as<int>(), cell_start.as<int>(), scan_scratch.as<int>());
+    launch_fill_cells(st, nall, xw.as<double>(), d_atype, cell_of.as<int>(), cell_start.as<int>(),
+                      cell_cursor.as<int>(), cell_rec.as<CellRec>());
+    launch_format(st, format_spec(nloc, nall), g, xw.as<double>(), cell_of.as<int>(), cell_start.as<int>(),
+                  cell_rec.as<CellRec>(), nl_j.as<int>(), nl_code.as<int>(), nl_rij.as<double>(), nl_cnt.as<int>(),
+                  err_d);
+  }
   B200DP_CUDA_TRY(cudaGetLastError());
   rc = (opt.precision == B200DP_FP64)
            ? run_model<double>(st, nloc, nall, d_atype, d_force, d_atom_energy, d_atom_virial, d_energy, d_virial)
@@ -762,6 +811,28 @@ b200dp_status Engine::check() {
     err = "neighbour count exceeded sel";
     return B200DP_ERR_SEL_OVERFLOW;
   }
+  if (vl_stale.ptr) {  // sticky until reported
+    int stale = 0;
+    B200DP_CUDA_TRY(cudaMemcpy(&stale, vl_stale.ptr, sizeof(int), cudaMemcpyDeviceToHost));
+    if (stale) {
+      B200DP_CUDA_TRY(cudaMemset(vl_stale.ptr, 0, sizeof(int)));
+      vl_valid = false;
+      err = "neighbour candidates went stale: an atom moved more than skin / 2 between rebuilds "
+            "(rebuild more often or use a larger skin)";
+      return B200DP_ERR_CAPACITY;
+    }
+  }
+  return B200DP_OK;
+}
+
+b200dp_status Engine::set_neighbor_reuse(double skin, int every) {
+  if (every < 0 || (every > 0 && !(skin > 0))) {
+    err = "neighbour reuse needs skin > 0 and every >= 1 (every = 0 turns it off)";
+    return B200DP_ERR_INVALID;
+  }
+  vl_skin = skin;
+  vl_every = every;
+  vl_valid = false;
   return B200DP_OK;
 }
 
@@ -1056,6 +1127,11 @@ b200dp_status b200dp_last_descriptor(b200dp_engine* engine, double* descriptor, 
 }
 
 long long b200dp_kernel_launches(void) { return b200dp::launch_count(); }
+
+b200dp_status b200dp_set_neighbor_reuse(b200dp_engine* engine, double skin, int every) {
+  if (!engine) return B200DP_ERR_INVALID;
+  return engine->e.set_neighbor_reuse(skin, every);
+}
 
 // Engine and stream used by b200dp_direct_energy_force (process-wide, like the
 // reference's primed direct-engine cache).

@@ -78,6 +78,11 @@ struct Engine {
   DevBuf c8_state, c8_q;
   std::array<DevBuf, kC8MaxFit> c8_Z, c8_H;
   std::array<DevBuf, 2> c8_dH, c8_dZ;
+  // neighbour reuse (skin candidates kept for `vl_every` periodic calls)
+  double vl_skin = 0;
+  int vl_every = 0, vl_age = 0, vl_n = -1, vl_cap = 0;
+  bool vl_valid = false;
+  DevBuf vl_cj, vl_cc, vl_cnt, vl_xref, vl_ls, vl_stale;
   // host-call staging
   DevBuf h_coord, h_atype, h_force, h_aviral, h_ae;
 
@@ -124,6 +129,7 @@ struct Engine {
                              const b200dp_nlist* nlist, double* energy, double* force, double* virial,
                              double* atom_energy, double* atom_virial);
   b200dp_status check();
+  b200dp_status set_neighbor_reuse(double skin, int every);
 };
 
 }  // namespace b200dp

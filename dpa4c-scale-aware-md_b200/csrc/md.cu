@@ -345,6 +345,8 @@ b200dp_status b200dp_md_params_default(b200dp_md_params* p) {
   p->p_target = 1.0;
   p->p_damp = 0.5;
   p->pchain = 3;
+  p->rebuild_every = 10;
+  p->skin = 2.0;
   return B200DP_OK;
 }
 
@@ -362,6 +364,7 @@ b200dp_status b200dp_md_create(b200dp_engine* engine, int natoms, const double* 
        box[5] != 0 || box[6] != 0 || box[7] != 0))
     return B200DP_ERR_INVALID;  // isotropic barostat on an orthorhombic box
   if (!vel && !(p.t_init > 0)) return B200DP_ERR_INVALID;
+  if (p.rebuild_every < 0 || (p.rebuild_every > 1 && !(p.skin > 0))) return B200DP_ERR_INVALID;
   b200dp_model_info info;
   if (b200dp_model_info_get(engine, &info) != B200DP_OK) return B200DP_ERR_INVALID;
   std::vector<double> mass(natoms), minv(natoms);
@@ -372,6 +375,11 @@ b200dp_status b200dp_md_create(b200dp_engine* engine, int natoms, const double* 
   }
   auto* md = new b200dp_md();
   md->engine = engine;
+  // skin candidates rebuilt every rebuild_every steps (0 or 1: every step from scratch)
+  if (b200dp_set_neighbor_reuse(engine, p.skin, p.rebuild_every > 1 ? p.rebuild_every : 0) != B200DP_OK) {
+    delete md;
+    return B200DP_ERR_INVALID;
+  }
   md->p = p;
   md->n = natoms;
   md->ensemble = p.ensemble;
@@ -634,6 +642,7 @@ b200dp_status b200dp_md_destroy(b200dp_md* md) {
   if (!md) return B200DP_OK;
   cudaStreamSynchronize(md->stream);
   cudaStreamDestroy(md->stream);
+  b200dp_set_neighbor_reuse(md->engine, 0.0, 0);  // the engine's other callers bin from scratch again
   delete md;
   return B200DP_OK;
 }

@@ -84,7 +84,7 @@ int make_grid(bool periodic, const double* box, const double* region, double rcu
 
 // ---------------------------------------------------------------- binning
 __global__ void k_bin(int nall, const double* __restrict__ coord, GridSpec g, double* __restrict__ xw,
-                      int* __restrict__ cell_of, int* __restrict__ cell_count) {
+                      int* __restrict__ cell_of, int* __restrict__ cell_count, int* __restrict__ lshift) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= nall) return;
   const double x[3] = {coord[3 * i], coord[3 * i + 1], coord[3 * i + 2]};
@@ -96,6 +96,7 @@ __global__ void k_bin(int nall, const double* __restrict__ coord, GridSpec g, do
     for (int d = 0; d < 3; ++d) {
       const double s = dadd(dadd(dmul(x[0], g.Binv[d]), dmul(x[1], g.Binv[3 + d])), dmul(x[2], g.Binv[6 + d]));
       f[d] = floor(s);
+      if (lshift) lshift[3 * i + d] = (int)f[d];
     }
 #pragma unroll
     for (int k = 0; k < 3; ++k)
@@ -125,10 +126,10 @@ __global__ void k_bin(int nall, const double* __restrict__ coord, GridSpec g, do
 }
 
 void launch_bin(cudaStream_t st, int nall, const double* coord, const GridSpec& g, double* xw, int* cell_of,
-                int* cell_count) {
+                int* cell_count, int* lshift) {
   if (nall <= 0) return;
   count_launch();
-  k_bin<<<(nall + 255) / 256, 256, 0, st>>>(nall, coord, g, xw, cell_of, cell_count);
+  k_bin<<<(nall + 255) / 256, 256, 0, st>>>(nall, coord, g, xw, cell_of, cell_count, lshift);
 }
 
 // Single-block exclusive scan; out has n+1 entries (out[n] = total).  Each
@@ -486,33 +487,21 @@ static void format_attr(K kernel, size_t smem) {
   }
 }
 
-// One warp per centre.  The stencil (every cell within reach, periodic images
-// included) is flattened; a warp scan over the cells' atom counts numbers the
-// candidates, and each lane takes every 32nd candidate, finds its cell by a
-// binary search over the scanned counts and loads the cell-sorted record.
-__global__ void __launch_bounds__(kFmtWarps * 32)
-    k_format(FormatSpec f, GridSpec g, const double* __restrict__ xw, const int* __restrict__ cell_of,
-             const int* __restrict__ cell_start, const CellRec* __restrict__ cell_rec, int* __restrict__ nl_j,
-             int* __restrict__ nl_code, double* __restrict__ nl_rij, int* __restrict__ nl_cnt,
-             int* __restrict__ err) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  __shared__ int s_start[kFmtWarps][kStencilChunk], s_pref[kFmtWarps][kStencilChunk], s_code[kFmtWarps][kStencilChunk];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int i = blockIdx.x * kFmtWarps + warp;
-  if (i >= f.nloc) return;  // warp-uniform; no block-level barrier follows
-  const CandBuf b = cand_buf(smem, warp, f);
-  int* const c_start = s_start[warp];
-  int* const c_pref = s_pref[warp];
-  int* const c_code = s_code[warp];
-  const double xi[3] = {xw[3 * i], xw[3 * i + 1], xw[3 * i + 2]};
-  const int cell = cell_of[i];
+// Candidates of centre i (one warp): the stencil (every cell within reach,
+// periodic images included) is flattened; a warp scan over the cells' atom
+// counts numbers the candidates, and each lane takes every 32nd candidate,
+// finds its cell by a binary search over the scanned counts and loads the
+// cell-sorted record.  push(valid, tj, r2, j, code, ridx) is called by all
+// lanes together for each batch slot (r2 < rc2, not the centre itself, type
+// in range).
+template <typename Push>
+__device__ __forceinline__ void gather_stencil(const FormatSpec& f, const GridSpec& g, const double (&xi)[3], int i,
+                                               int cell, double rc2, const int* __restrict__ cell_start,
+                                               const CellRec* __restrict__ cell_rec, int* __restrict__ err,
+                                               int* c_start, int* c_pref, int* c_code, int lane, Push push) {
   const int ci[3] = {cell / (g.n[1] * g.n[2]), (cell / g.n[2]) % g.n[1], cell % g.n[2]};
   const int sy = 2 * g.reach[1] + 1, sz = 2 * g.reach[2] + 1;
   const int nstencil = (2 * g.reach[0] + 1) * sy * sz;
-  const unsigned lt_mask = (1u << lane) - 1u;
-  int ncnt[kMaxTypes];
-#pragma unroll
-  for (int t = 0; t < kMaxTypes; ++t) ncnt[t] = 0;
   for (int s0 = 0; s0 < nstencil; s0 += kStencilChunk) {
     // counts of this lane's cells, then a warp scan
     int cnt[kStencilPerLane], st[kStencilPerLane], cd[kStencilPerLane];
@@ -591,14 +580,36 @@ __global__ void __launch_bounds__(kFmtWarps * 32)
           r2 = dadd(dadd(dmul(r[0], r[0]), dmul(r[1], r[1])), dmul(r[2], r[2]));
           const bool self = (j == i) && code == image_code(0, 0, 0);
           const bool type_ok = (tj >= 0 && tj < f.ntypes);
-          if (!type_ok && !self && r2 < f.rc2) atomicAdd(err + kErrBadType, 1);
-          valid = !self && type_ok && (r2 < f.rc2);
+          if (!type_ok && !self && r2 < rc2) atomicAdd(err + kErrBadType, 1);
+          valid = !self && type_ok && (r2 < rc2);
         }
-        cand_push(f, b, ncnt, valid, tj, r2, j, code, ridx[u], lt_mask);
+        push(valid, tj, r2, j, code, ridx[u]);
       }
     }
     __syncwarp();
   }
+}
+
+__global__ void __launch_bounds__(kFmtWarps * 32)
+    k_format(FormatSpec f, GridSpec g, const double* __restrict__ xw, const int* __restrict__ cell_of,
+             const int* __restrict__ cell_start, const CellRec* __restrict__ cell_rec, int* __restrict__ nl_j,
+             int* __restrict__ nl_code, double* __restrict__ nl_rij, int* __restrict__ nl_cnt,
+             int* __restrict__ err) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ int s_start[kFmtWarps][kStencilChunk], s_pref[kFmtWarps][kStencilChunk], s_code[kFmtWarps][kStencilChunk];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int i = blockIdx.x * kFmtWarps + warp;
+  if (i >= f.nloc) return;  // warp-uniform; no block-level barrier follows
+  const CandBuf b = cand_buf(smem, warp, f);
+  const double xi[3] = {xw[3 * i], xw[3 * i + 1], xw[3 * i + 2]};
+  const unsigned lt_mask = (1u << lane) - 1u;
+  int ncnt[kMaxTypes];
+#pragma unroll
+  for (int t = 0; t < kMaxTypes; ++t) ncnt[t] = 0;
+  gather_stencil(f, g, xi, i, cell_of[i], f.rc2, cell_start, cell_rec, err, s_start[warp], s_pref[warp],
+                 s_code[warp], lane, [&](bool valid, int tj, double r2, int j, int code, int ridx) {
+                   cand_push(f, b, ncnt, valid, tj, r2, j, code, ridx, lt_mask);
+                 });
   __syncwarp();
   emit_row(f, i, b, ncnt, lane, nl_j, nl_code, nl_rij, nl_cnt, err,
            [&](int src, int code, double (&r)[3]) {
@@ -606,6 +617,130 @@ __global__ void __launch_bounds__(kFmtWarps * 32)
              const double2 a = __ldg(p), c = __ldg(p + 1);
              image_vector(g, xi, a.x, a.y, c.x, code, r);
            });
+}
+
+// ---------------------------------------------------------------- neighbour reuse
+// Skin (Verlet) candidates: every (j, image) within rc + skin of a centre,
+// kept for several evaluations.  The rows are then formed from the candidates
+// with the positions of each call, shifted by the lattice vectors each atom
+// was wrapped by when the candidates were built (so the image codes stay
+// valid as atoms cross the cell boundary, and under a changing cell).
+__global__ void __launch_bounds__(kFmtWarps * 32)
+    k_verlet_build(FormatSpec f, GridSpec g, double rcand2, int capS, const double* __restrict__ xw,
+                   const int* __restrict__ cell_of, const int* __restrict__ cell_start,
+                   const CellRec* __restrict__ cell_rec, int* __restrict__ cand_j, int* __restrict__ cand_code,
+                   int* __restrict__ cand_cnt, int* __restrict__ err) {
+  __shared__ int s_start[kFmtWarps][kStencilChunk], s_pref[kFmtWarps][kStencilChunk], s_code[kFmtWarps][kStencilChunk];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int i = blockIdx.x * kFmtWarps + warp;
+  if (i >= f.nloc) return;
+  const double xi[3] = {xw[3 * i], xw[3 * i + 1], xw[3 * i + 2]};
+  const unsigned lt_mask = (1u << lane) - 1u;
+  int n = 0;
+  int* cj = cand_j + (size_t)i * capS;
+  int* cc = cand_code + (size_t)i * capS;
+  gather_stencil(f, g, xi, i, cell_of[i], rcand2, cell_start, cell_rec, err, s_start[warp], s_pref[warp],
+                 s_code[warp], lane, [&](bool valid, int, double, int j, int code, int) {
+                   const unsigned m = __ballot_sync(0xffffffffu, valid);
+                   const int pos = n + __popc(m & lt_mask);
+                   if (valid && pos < capS) {
+                     cj[pos] = j;
+                     cc[pos] = code;
+                   }
+                   n += __popc(m);
+                 });
+  if (lane == 0) {
+    if (n > capS) atomicAdd(err + kErrCandCapacity, 1);
+    cand_cnt[i] = n < capS ? n : capS;
+  }
+}
+
+// Position of atom j shifted by its build-time lattice shift, with the
+// arithmetic of k_bin's wrap (so a call right after a build sees the wrapped
+// coordinates bit for bit).
+__device__ __forceinline__ void shifted(const GridSpec& g, const double* __restrict__ x, const int* __restrict__ ls,
+                                        int j, double (&w)[3]) {
+  const double f0 = (double)ls[3 * j], f1 = (double)ls[3 * j + 1], f2 = (double)ls[3 * j + 2];
+#pragma unroll
+  for (int k = 0; k < 3; ++k)
+    w[k] = dsub(x[3 * j + k], dadd(dadd(dmul(f0, g.B[k]), dmul(f1, g.B[3 + k])), dmul(f2, g.B[6 + k])));
+}
+
+__global__ void __launch_bounds__(kFmtWarps * 32)
+    k_format_verlet(FormatSpec f, GridSpec g, int capS, double half_skin2, const double* __restrict__ x,
+                    const int* __restrict__ atype, const int* __restrict__ lshift, const double* __restrict__ xref,
+                    const int* __restrict__ cand_j, const int* __restrict__ cand_code,
+                    const int* __restrict__ cand_cnt, int* __restrict__ nl_j, int* __restrict__ nl_code,
+                    double* __restrict__ nl_rij, int* __restrict__ nl_cnt, int* __restrict__ err,
+                    int* __restrict__ stale) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int i = blockIdx.x * kFmtWarps + warp;
+  if (i >= f.nloc) return;
+  const CandBuf b = cand_buf(smem, warp, f);
+  double xi[3];
+  shifted(g, x, lshift, i, xi);
+  if (lane == 0) {
+    double d2 = 0;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      const double d = x[3 * i + k] - xref[3 * i + k];
+      d2 += d * d;
+    }
+    if (d2 > half_skin2) atomicOr(stale, 1);
+  }
+  const unsigned lt_mask = (1u << lane) - 1u;
+  int ncnt[kMaxTypes];
+#pragma unroll
+  for (int t = 0; t < kMaxTypes; ++t) ncnt[t] = 0;
+  const int n = cand_cnt[i];
+  const int* cj = cand_j + (size_t)i * capS;
+  const int* cc = cand_code + (size_t)i * capS;
+  for (int k0 = 0; k0 < n; k0 += 32) {
+    const int k = k0 + lane;
+    bool valid = false;
+    int j = 0, code = 0, tj = 0;
+    double r2 = 0;
+    if (k < n) {
+      j = cj[k];
+      code = cc[k];
+      tj = atype[j];
+      double xj[3], r[3];
+      shifted(g, x, lshift, j, xj);
+      image_vector(g, xi, xj[0], xj[1], xj[2], code, r);
+      r2 = dadd(dadd(dmul(r[0], r[0]), dmul(r[1], r[1])), dmul(r[2], r[2]));
+      valid = (tj >= 0 && tj < f.ntypes) && r2 < f.rc2;
+    }
+    cand_push(f, b, ncnt, valid, tj, r2, j, code, k, lt_mask);
+  }
+  __syncwarp();
+  emit_row(f, i, b, ncnt, lane, nl_j, nl_code, nl_rij, nl_cnt, err, [&](int src, int code, double (&r)[3]) {
+    double xj[3];
+    shifted(g, x, lshift, cj[src], xj);
+    image_vector(g, xi, xj[0], xj[1], xj[2], code, r);
+  });
+}
+
+void launch_verlet_build(cudaStream_t st, const FormatSpec& f, const GridSpec& g, double rcand, int capS,
+                         const double* xw, const int* cell_of, const int* cell_start, const CellRec* cell_rec,
+                         int* cand_j, int* cand_code, int* cand_cnt, int* err) {
+  if (f.nloc <= 0) return;
+  count_launch();
+  k_verlet_build<<<(f.nloc + kFmtWarps - 1) / kFmtWarps, kFmtWarps * 32, 0, st>>>(
+      f, g, rcand * rcand, capS, xw, cell_of, cell_start, cell_rec, cand_j, cand_code, cand_cnt, err);
+}
+
+void launch_format_verlet(cudaStream_t st, const FormatSpec& f, const GridSpec& g, int capS, double skin,
+                          const double* x, const int* atype, const int* lshift, const double* xref,
+                          const int* cand_j, const int* cand_code, const int* cand_cnt, int* nl_j, int* nl_code,
+                          double* nl_rij, int* nl_cnt, int* err, int* stale) {
+  if (f.nloc <= 0) return;
+  const size_t smem = format_smem_bytes(f);
+  format_attr(k_format_verlet, smem);
+  count_launch();
+  k_format_verlet<<<(f.nloc + kFmtWarps - 1) / kFmtWarps, kFmtWarps * 32, smem, st>>>(
+      f, g, capS, 0.25 * skin * skin, x, atype, lshift, xref, cand_j, cand_code, cand_cnt, nl_j, nl_code, nl_rij,
+      nl_cnt, err, stale);
 }
 
 void launch_format(cudaStream_t st, const FormatSpec& f, const GridSpec& g, const double* xw, const int* cell_of,

@@ -61,8 +61,10 @@ void format_caps(FormatSpec& f);
 void make_box_inverse(const double* box, double* Binv, double* width);
 
 // Launchers; all enqueue on `st`.
+// lshift (optional, periodic): the integer lattice shift f of each atom's
+// wrap, x_wrapped = x - f . cell.
 void launch_bin(cudaStream_t st, int nall, const double* coord, const GridSpec& g, double* xw, int* cell_of,
-                int* cell_count);
+                int* cell_count, int* lshift = nullptr);
 // Exclusive scan of n ints into out[0..n] (out[n] = total).  scratch holds
 // scan_scratch_ints(n) ints; with scratch == nullptr a single block is used.
 void launch_exclusive_scan(cudaStream_t st, int n, const int* in, int* out, int* scratch);
@@ -73,6 +75,18 @@ size_t format_smem_bytes(const FormatSpec& f);
 void launch_format(cudaStream_t st, const FormatSpec& f, const GridSpec& g, const double* xw, const int* cell_of,
                    const int* cell_start, const CellRec* cell_rec, int* nl_j, int* nl_code, double* nl_rij,
                    int* nl_cnt, int* err);
+// Neighbour reuse: skin candidates (every (j, image) within rcand of a centre,
+// at most capS per centre, built on the grid of a rcand cutoff), and the rows
+// formed from them with the current positions x and the build-time lattice
+// shifts.  An atom farther than skin / 2 from its build-time position xref
+// sets *stale.
+void launch_verlet_build(cudaStream_t st, const FormatSpec& f, const GridSpec& g, double rcand, int capS,
+                         const double* xw, const int* cell_of, const int* cell_start, const CellRec* cell_rec,
+                         int* cand_j, int* cand_code, int* cand_cnt, int* err);
+void launch_format_verlet(cudaStream_t st, const FormatSpec& f, const GridSpec& g, int capS, double skin,
+                          const double* x, const int* atype, const int* lshift, const double* xref,
+                          const int* cand_j, const int* cand_code, const int* cand_cnt, int* nl_j, int* nl_code,
+                          double* nl_rij, int* nl_cnt, int* err, int* stale);
 // Formats a caller-provided candidate list (LAMMPS full list in CSR form).
 // Formats a canonical destination-major edge graph (fp32 edge vectors) and
 // converts the int64 node types to int32 (invalid types become -1).

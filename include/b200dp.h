@@ -223,6 +223,18 @@ int b200dp_direct_energy_force(const int64_t* atype, const int64_t* row_ptr, con
  * The box is periodic; positions are not wrapped (the engine images them). */
 typedef enum b200dp_md_ensemble { B200DP_MD_NVE = 0, B200DP_MD_NVT = 1, B200DP_MD_NPT = 2 } b200dp_md_ensemble;
 
+/* Neighbour reuse for periodic calls (nghost == 0, box given) of
+ * b200dp_compute_device / b200dp_compute_host: candidate pairs within
+ * rcut + skin are built on one call and reused by the next every - 1 calls,
+ * whose neighbour rows are formed from them with the new positions (like a
+ * LAMMPS skin list rebuilt every `every` steps; the rows themselves stay the
+ * exact per-type rcut rows).  An atom that moves more than skin / 2 between
+ * rebuilds makes b200dp_check return B200DP_ERR_CAPACITY and forces a
+ * rebuild.  every = 0 turns reuse off (the default: every call bins from
+ * scratch).  Replaces the LAMMPS skin neighbour list and its rebuild cadence
+ * (LO/KOKKOS/npair_kokkos.cpp:151-460 with neigh_modify every / check). */
+b200dp_status b200dp_set_neighbor_reuse(b200dp_engine* engine, double skin, int every);
+
 typedef struct b200dp_md_params {
   double dt;        /* time step, ps (default 0.0005) */
   int ensemble;     /* b200dp_md_ensemble */
@@ -235,7 +247,9 @@ typedef struct b200dp_md_params {
   double p_target;  /* bar (NPT, isotropic) */
   double p_damp;    /* barostat period, ps (NPT, default 0.5) */
   int pchain;       /* barostat Nose-Hoover chain length (NPT, 1..8, default 3) */
-  int reserved[11];
+  int rebuild_every; /* neighbour candidates rebuilt every this many steps (default 10; 0 = every step) */
+  double skin;       /* Angstrom, neighbour skin for the reuse (default 2.0) */
+  int reserved[8];
 } b200dp_md_params;
 
 typedef struct b200dp_md b200dp_md;
