@@ -11,6 +11,7 @@
 // as (value - mean) * inv_std.
 #include <algorithm>
 #include <cmath>
+#include <type_traits>
 
 #include "c8l2.cuh"
 #include "common.cuh"
@@ -650,6 +651,204 @@ __global__ void k_c8_head(int nloc, int width, int act, const P* __restrict__ H,
   }
 }
 
+// Fused fitting (fp32): one persistent block per SM holds every weight in
+// shared memory and runs forward, head and backward for 32-row tiles with the
+// activations on chip.  Activations are K-major [k][row] with a row stride of
+// 36 floats (float4-aligned: each warp's 4 rows arrive in one broadcast
+// load); weights keep W[k][c] with an odd row stride so that both the forward
+// (lanes over c) and the transposed backward (lanes over k) read distinct
+// banks.  Warp w owns rows 4w..4w+3 of a tile, lane l output columns
+// l, l + 32, ... ; sums run over k in order, so results do not depend on the
+// launch shape.
+constexpr int kFT = 32;      // rows per tile
+constexpr int kFLD = 36;     // activation row stride
+constexpr int kFMaxW = 128;  // widest layer the fused kernel takes
+
+struct FusedFit {
+  int L, din0, width;
+  int din[kC8MaxFit], dout[kC8MaxFit], res[kC8MaxFit], ws[kC8MaxFit];
+  int w_off[kC8MaxFit], b_off[kC8MaxFit];
+  int wh_off, x_off, z_off[kC8MaxFit], h_off[2], dz_off[2];
+  int total;  // floats of shared memory
+};
+
+FusedFit fused_fit_layout(const C8Dev& m) {
+  FusedFit f{};
+  f.L = m.nfit;
+  f.din0 = kC8Dim;
+  int o = 0, maxw = 1;
+  for (int l = 0; l < f.L; ++l) {
+    f.din[l] = m.fdin[l];
+    f.dout[l] = m.fdout[l];
+    f.res[l] = m.fres[l] && m.fdin[l] == m.fdout[l];
+    f.ws[l] = m.fdout[l] | 1;
+    f.w_off[l] = o;
+    o += (f.din[l] * f.ws[l] + 3) / 4 * 4;  // every region starts 16-byte aligned
+    f.b_off[l] = o;
+    o += (f.dout[l] + 3) / 4 * 4;
+    maxw = std::max(maxw, m.fdout[l]);
+  }
+  f.width = m.fdout[f.L - 1];
+  f.wh_off = o;
+  o += (f.width + 3) / 4 * 4;
+  f.x_off = o;
+  o += kC8Dim * kFLD;
+  for (int l = 0; l < f.L; ++l) {
+    f.z_off[l] = o;
+    o += f.dout[l] * kFLD;
+  }
+  for (int k = 0; k < 2; ++k) {
+    f.h_off[k] = o;
+    o += maxw * kFLD;
+  }
+  for (int k = 0; k < 2; ++k) {
+    f.dz_off[k] = o;
+    o += maxw * kFLD;
+  }
+  f.total = o;
+  return f;
+}
+
+// out[c][r] (c < N) = sum_k A[k][r] W(k, c), A K-major (ld kFLD), W(k, c) =
+// T ? W[c * ws + k] : W[k * ws + c]; the epilogue sees (row, column, sum).
+template <bool T, class Epi>
+__device__ __forceinline__ void fit_tile_gemm(const float* A, int K, const float* W, int ws, int N, int warp,
+                                              int lane, Epi epi) {
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+  const int nj = (N + 31) >> 5;
+  for (int k = 0; k < K; ++k) {
+    const float4 a = *reinterpret_cast<const float4*>(A + k * kFLD + 4 * warp);
+    float b[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int c = lane + 32 * j;
+      b[j] = (j < nj && c < N) ? (T ? W[c * ws + k] : W[k * ws + c]) : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      acc[0][j] = fmaf(a.x, b[j], acc[0][j]);
+      acc[1][j] = fmaf(a.y, b[j], acc[1][j]);
+      acc[2][j] = fmaf(a.z, b[j], acc[2][j]);
+      acc[3][j] = fmaf(a.w, b[j], acc[3][j]);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int c = lane + 32 * j;
+    if (j < nj && c < N) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) epi(4 * warp + i, c, acc[i][j]);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256, 1)
+    k_c8_fit_fused(C8Dev m, FusedFit F, int n, const int* __restrict__ atype, const float* __restrict__ desc,
+                   float* __restrict__ dD, double* __restrict__ atom_e) {
+  extern __shared__ __align__(16) float fs[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int act = m.act;
+  for (int l = 0; l < F.L; ++l) {
+    const float* w = static_cast<const float*>(m.fw[l]);
+    const float* b = static_cast<const float*>(m.fb[l]);
+    for (int idx = tid; idx < F.din[l] * F.dout[l]; idx += blockDim.x) {
+      const int k = idx / F.dout[l], c = idx - k * F.dout[l];
+      fs[F.w_off[l] + k * F.ws[l] + c] = w[idx];
+    }
+    for (int c = tid; c < F.dout[l]; c += blockDim.x) fs[F.b_off[l] + c] = b[c];
+  }
+  for (int c = tid; c < F.width; c += blockDim.x) fs[F.wh_off + c] = static_cast<const float*>(m.w_head)[c];
+  __syncthreads();
+  float* X = fs + F.x_off;
+  const int ntiles = (n + kFT - 1) / kFT;
+  for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    const int r0 = tile * kFT, rows = min(kFT, n - r0);
+    for (int idx = tid; idx < kFT * kC8Dim; idx += blockDim.x) {
+      const int r = idx / kC8Dim, k = idx - r * kC8Dim;
+      X[k * kFLD + r] = r < rows ? desc[(size_t)(r0 + r) * kC8Dim + k] : 0.f;
+    }
+    __syncthreads();
+    // forward
+    const float* in = X;
+    int K = kC8Dim, hb = 0;
+    for (int l = 0; l < F.L; ++l) {
+      float* Z = fs + F.z_off[l];
+      float* H = fs + F.h_off[hb];
+      const float* bias = fs + F.b_off[l];
+      const bool res = F.res[l];
+      fit_tile_gemm<false>(in, K, fs + F.w_off[l], F.ws[l], F.dout[l], warp, lane, [&](int r, int c, float s) {
+        const float z = s + bias[c];
+        Z[c * kFLD + r] = z;
+        const float h = act_v(act, z);
+        H[c * kFLD + r] = res ? in[c * kFLD + r] + h : h;
+      });
+      __syncthreads();
+      in = H;
+      K = F.dout[l];
+      hb ^= 1;
+    }
+    // head (8 lanes per row, fixed-order reduction) and the backward seed
+    {
+      const float* H = in;
+      const float* wh = fs + F.wh_off;
+      const int r = 4 * warp + (lane >> 3);
+      float e = 0.f;
+      for (int c = lane & 7; c < F.width; c += 8) e = fmaf(H[c * kFLD + r], wh[c], e);
+      e += __shfl_xor_sync(0xffffffffu, e, 1);
+      e += __shfl_xor_sync(0xffffffffu, e, 2);
+      e += __shfl_xor_sync(0xffffffffu, e, 4);
+      if ((lane & 7) == 0 && r < rows) {
+        const int t = atype[r0 + r];
+        atom_e[r0 + r] = (double)e + m.b_head + ((t >= 0 && t < m.ntypes) ? m.bias[t] : 0.0);
+      }
+    }
+    __syncthreads();  // the last H is dead: its buffer and the other one now carry dH
+    float* dH = fs + F.h_off[0];
+    float* dZ = fs + F.dz_off[0];
+    {
+      const float* Zl = fs + F.z_off[F.L - 1];
+      const float* wh = fs + F.wh_off;
+      for (int idx = tid; idx < F.width * kFT; idx += blockDim.x) {
+        const int c = idx / kFT, r = idx - c * kFT;
+        dH[c * kFLD + r] = wh[c];
+        dZ[c * kFLD + r] = wh[c] * act_d(act, Zl[c * kFLD + r]);
+      }
+    }
+    __syncthreads();
+    int cur = 0;
+    for (int l = F.L - 1; l >= 0; --l) {
+      const float* dZc = fs + F.dz_off[cur];
+      const float* dHc = fs + F.h_off[cur];
+      float* dZn = fs + F.dz_off[cur ^ 1];
+      float* dHn = fs + F.h_off[cur ^ 1];
+      const float* Zp = l > 0 ? fs + F.z_off[l - 1] : nullptr;
+      const bool res = F.res[l];
+      fit_tile_gemm<true>(dZc, F.dout[l], fs + F.w_off[l], F.ws[l], F.din[l], warp, lane, [&](int r, int c, float s) {
+        const float v = res ? s + dHc[c * kFLD + r] : s;
+        if (Zp) {
+          dHn[c * kFLD + r] = v;
+          dZn[c * kFLD + r] = v * act_d(act, Zp[c * kFLD + r]);
+        } else if (r < rows) {
+          dD[(size_t)(r0 + r) * kC8Dim + c] = v;
+        }
+      });
+      __syncthreads();
+      cur ^= 1;
+    }
+  }
+}
+
+bool fused_fit_ok(const C8Dev& m, const FusedFit& F) {
+  if (m.nfit < 1 || m.nfit > kC8MaxFit) return false;
+  for (int l = 0; l < m.nfit; ++l)
+    if (m.fdin[l] > kFMaxW || m.fdout[l] > kFMaxW) return false;
+  return (size_t)F.total * sizeof(float) <= 220 * 1024;
+}
+
 }  // namespace
 
 template <typename P>
@@ -665,6 +864,27 @@ template <typename P>
 void launch_c8_fitting(cudaStream_t st, const C8Dev& m, int nloc, const int* atype, const C8Work<P>& w,
                        double* atom_e) {
   if (nloc <= 0) return;
+  if constexpr (std::is_same<P, float>::value) {
+    const FusedFit F = fused_fit_layout(m);
+    if (fused_fit_ok(m, F)) {
+      static int nsm = 0;
+      const size_t smem = (size_t)F.total * sizeof(float);
+      static size_t attr = 0;
+      if (!nsm) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+      }
+      if (smem > attr) {
+        cudaFuncSetAttribute(k_c8_fit_fused, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        attr = smem;
+      }
+      const int ntiles = (nloc + kFT - 1) / kFT;
+      count_launch();
+      k_c8_fit_fused<<<std::min(ntiles, std::max(nsm, 1)), 256, smem, st>>>(m, F, nloc, atype, w.desc, w.dD, atom_e);
+      return;
+    }
+  }
   const int L = m.nfit;
   const P* X = w.desc;
   for (int l = 0; l < L; ++l) {
