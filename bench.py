@@ -15,8 +15,11 @@ random-init weights, seed 0).  Inputs are seeded synthetic data.
   process per GPU, one global water box of 4096 H2O per GPU split by spatial
   domain decomposition (slab for 2 GPUs, 2x2x1 for 4, 2x2x2 for 8; 8 A ghost
   shell); a step is the forward halo of coordinates over NCCL, the force call
-  on owned + ghost atoms, the reverse fold of ghost forces and an all-reduce
-  of energy and virial; time = max over ranks.
+  on owned + ghost atoms whose assembly adds every ghost contribution straight
+  into the owner's force accumulator through NVLink peer memory (CUDA IPC;
+  ``--reverse nccl`` instead folds ghost forces back by NCCL send/recv), an
+  all-reduce of energy and virial and the owners' conversion of their
+  accumulators; time = max over ranks.
 * ``e2e``: the same metric through the public API with pinned host buffers:
   1 GPU, the host C entry (b200dp_compute_host), H2D of coordinates and
   types, D2H of forces, energy and virial inside the timed region; N GPUs,
@@ -64,6 +67,8 @@ def parse():
     ap.add_argument("--impl", default="b200dp", choices=["b200dp", "reference"])
     ap.add_argument("--precision", default="mixed", choices=["mixed", "fp64"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--reverse", default="peer", choices=["peer", "nccl"],
+                    help="N > 1: ghost forces to their owners by peer-memory atomics or by NCCL send/recv")
     return ap.parse_args()
 
 
@@ -225,7 +230,7 @@ class Periodic:
 class Decomposed:
     """N GPUs: spatial domain decomposition of one global box (domain.py)."""
 
-    def __init__(self, dp, system, grid, rank, dev, stream, torch):
+    def __init__(self, dp, system, grid, rank, dev, stream, torch, peer_fold=True):
         import domain
 
         self.dp, self.stream = dp, stream
@@ -236,7 +241,8 @@ class Decomposed:
             dp.compute_device(torch.cuda.current_stream(dev).cuda_stream, nloc, nghost, x_all.data_ptr(),
                               t_all.data_ptr(), None, region, e.data_ptr(), f.data_ptr(), v.data_ptr())
 
-        self.ddp = domain.DistributedDeepPot(compute, system.box, grid, rank, HALO, x, t, ids, device=dev)
+        fold = domain.PeerFold(dp, dev) if peer_fold else None
+        self.ddp = domain.DistributedDeepPot(compute, system.box, grid, rank, HALO, x, t, ids, device=dev, fold=fold)
         self.n = self.ddp.nloc
         self.total = system.natoms
         self.nghost = self.ddp.nghost
@@ -286,7 +292,7 @@ def run_b200dp(args, world, rank, local):
     def workload(dp):
         if world == 1:
             return Periodic(dp, system, dev, stream, torch)
-        return Decomposed(dp, system, grid, rank, dev, stream, torch)
+        return Decomposed(dp, system, grid, rank, dev, stream, torch, peer_fold=args.reverse == "peer")
 
     def device_loop(dp, w, steps, warmup):
         """Timed steps: CUDA events around each step on the launch stream, L2 flushed before each,
@@ -443,8 +449,10 @@ def run_b200dp(args, world, rank, local):
         cpu = {"value": rate, "unit": "atom-steps/s", "cores": used, "kind": "port",
                "sample": f"one full evaluation of the 12,288-atom system ({dt:.2f} s), fp64 C++ oracle, OpenMP"}
     if world > 1:
-        parallelism = (f"domain decomposition {grid[0]}x{grid[1]}x{grid[2]}, halo {HALO} A, NCCL send/recv, "
-                       "step replayed as one CUDA graph")
+        rev = ("ghost forces added into the owners' accumulators over NVLink peer memory"
+               if args.reverse == "peer" else "ghost forces folded back by NCCL send/recv")
+        parallelism = (f"domain decomposition {grid[0]}x{grid[1]}x{grid[2]}, halo {HALO} A, coordinate halo by "
+                       f"NCCL send/recv, {rev}, step replayed as one CUDA graph")
         cfg_extra = {"global_atoms": w.total, "ghosts_rank0": w.nghost}
     else:
         parallelism, cfg_extra = "single", {}
@@ -543,7 +551,9 @@ def e2e_decomposed(w, steps, warmup, torch, dist):
     ddp.release()
     return {"value": None, "unit": "atom-steps/s", "seconds": dt,
             "h2d_bytes_per_step": n * 3 * 8, "d2h_bytes_per_step": n * 3 * 8 + 8 * 10,
-            "entry": "domain.DistributedDeepPot.step (captured CUDA graph) over b200dp_compute_device (pinned host buffers, per rank)",
+            "entry": "domain.DistributedDeepPot.step (captured CUDA graph) over "
+                     + ("b200dp_compute_device_fold + b200dp_fold_finish" if ddp.fold is not None
+                        else "b200dp_compute_device") + " (pinned host buffers, per rank)",
             "bytes_rank": "rank 0's own counts"}
 
 

@@ -30,7 +30,8 @@ EXPORTS = [
     "b200dp_options_default", "b200dp_create", "b200dp_destroy", "b200dp_last_error", "b200dp_model_info_get",
     "b200dp_compute_host", "b200dp_compute_host_nlist", "b200dp_compute_device", "b200dp_check",
     "b200dp_sel_overflow_count", "b200dp_last_nlist", "b200dp_last_descriptor", "b200dp_set_stage_timing",
-    "b200dp_set_neighbor_reuse",
+    "b200dp_set_neighbor_reuse", "b200dp_fold_export", "b200dp_fold_connect", "b200dp_fold_origins",
+    "b200dp_compute_device_fold", "b200dp_fold_finish", "b200dp_halo_publish", "b200dp_halo_gather",
     "b200dp_stage_times", "b200dp_kernel_launches", "b200dp_selftest_mma", "b200dp_build_nlist_noalloc",
     "b200dp_direct_bind", "b200dp_direct_energy_force", "b200dp_md_params_default", "b200dp_md_create",
     "b200dp_md_run", "b200dp_md_thermo", "b200dp_md_state", "b200dp_md_destroy",
@@ -104,6 +105,13 @@ def load_library(path: str = LIB_PATH):
     L.b200dp_last_descriptor.argtypes = [_vp, _dp, _dp]
     L.b200dp_set_stage_timing.argtypes = [_vp, ctypes.c_int]
     L.b200dp_set_neighbor_reuse.argtypes = [_vp, ctypes.c_double, ctypes.c_int]
+    L.b200dp_fold_export.argtypes = [_vp, ctypes.c_int, _vp]
+    L.b200dp_fold_connect.argtypes = [_vp, ctypes.c_int, ctypes.c_int, _vp]
+    L.b200dp_fold_origins.argtypes = [_vp, ctypes.c_int, _vp, _vp]
+    L.b200dp_halo_publish.argtypes = [_vp, _vp, ctypes.c_int, _vp]
+    L.b200dp_halo_gather.argtypes = [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp]
+    L.b200dp_compute_device_fold.argtypes = [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp, _vp, _dp, _vp, _vp, _vp]
+    L.b200dp_fold_finish.argtypes = [_vp, _vp, ctypes.c_int, _vp]
     L.b200dp_stage_times.argtypes = [_vp, ctypes.POINTER(ctypes.c_float)]
     L.b200dp_selftest_mma.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                       ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_float),
@@ -229,6 +237,38 @@ class DeepPot:
     def set_neighbor_reuse(self, skin: float, every: int):
         """Periodic calls reuse rcut + skin candidates for `every` calls (0: off)."""
         self._raise(self.L.b200dp_set_neighbor_reuse(self.h, float(skin), int(every)))
+
+    # peer fold (domain decomposition over NVLink peers; see domain.PeerFold)
+    def fold_export(self, capacity: int) -> bytes:
+        """Allocates the owned-atom accumulator; returns its 64-byte CUDA IPC handle."""
+        h = ctypes.create_string_buffer(64)
+        self._raise(self.L.b200dp_fold_export(self.h, int(capacity), h))
+        return h.raw
+
+    def fold_connect(self, rank: int, handles) -> None:
+        buf = b"".join(bytes(h) for h in handles)
+        if len(buf) != 64 * len(handles):
+            raise ValueError("every handle is 64 bytes")
+        cbuf = ctypes.create_string_buffer(buf, len(buf))
+        self._raise(self.L.b200dp_fold_connect(self.h, len(handles), int(rank), cbuf))
+
+    def fold_origins(self, nghost: int, origin_ptr: int, shift_ptr: int = 0) -> None:
+        self._raise(self.L.b200dp_fold_origins(self.h, int(nghost), origin_ptr or None, shift_ptr or None))
+
+    def halo_publish(self, stream: int, nloc: int, coord_ptr: int) -> None:
+        self._raise(self.L.b200dp_halo_publish(self.h, stream or None, int(nloc), coord_ptr))
+
+    def halo_gather(self, stream: int, nloc: int, nghost: int, coord_ptr: int) -> None:
+        self._raise(self.L.b200dp_halo_gather(self.h, stream or None, int(nloc), int(nghost), coord_ptr))
+
+    def compute_device_fold(self, stream: int, nloc: int, nghost: int, coord_ptr: int, atype_ptr: int, region,
+                            energy_ptr: int, force_ptr: int, virial_ptr: int):
+        r = np.ascontiguousarray(region, dtype=np.float64).reshape(6)
+        self._raise(self.L.b200dp_compute_device_fold(self.h, stream or None, nloc, nghost, coord_ptr, atype_ptr,
+                                                      _p(r, _dp), energy_ptr, force_ptr, virial_ptr))
+
+    def fold_finish(self, stream: int, nloc: int, force_ptr: int) -> None:
+        self._raise(self.L.b200dp_fold_finish(self.h, stream or None, int(nloc), force_ptr))
 
     def set_stage_timing(self, on: bool):
         self._raise(self.L.b200dp_set_stage_timing(self.h, int(on)))

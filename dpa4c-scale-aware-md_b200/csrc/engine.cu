@@ -349,6 +349,13 @@ void Engine::release() {
     for (auto& b : v) b.release();
   for (auto& b : fit_dev) b.release();
   for (auto& b : c8_dev) b.release();
+  for (void* q : pf_opened) cudaIpcCloseMemHandle(q);
+  pf_opened.clear();
+  if (pf_buf) cudaFree(pf_buf);
+  pf_buf = nullptr;
+  pf_ptrs.release();
+  pf_origin.release();
+  pf_shift.release();
   for (DevBuf* b : {&vl_cj, &vl_cc, &vl_cnt, &vl_xref, &vl_ls, &vl_stale}) b->release();
   for (DevBuf* b : {&c8_state, &c8_q}) b->release();
   for (auto* arr : {&c8_Z, &c8_H})
@@ -672,15 +679,26 @@ b200dp_status Engine::run_model(cudaStream_t st, int nloc, int nall, const int* 
 // reduction of atom_e (shared by both model profiles).
 b200dp_status Engine::finish_assembly(cudaStream_t st, int nloc, int nall, double* d_force, double* d_atom_energy,
                                       double* d_atom_virial, double* d_energy, double* d_virial) {
-  if (d_atom_virial) {
-    const size_t bv = acc_v.bytes;
-    B200DP_CUDA_TRY(acc_v.ensure(sizeof(unsigned long long) * 18 * std::max(nall, 1)));
-    if (acc_v.bytes != bv) B200DP_CUDA_TRY(cudaMemsetAsync(acc_v.ptr, 0, acc_v.bytes, st));
-  }
   if (acc_fresh) {
     B200DP_CUDA_TRY(cudaMemsetAsync(acc_f.ptr, 0, acc_f.bytes, st));
     B200DP_CUDA_TRY(cudaMemsetAsync(nonfinite.ptr, 0, nonfinite.bytes, st));
     acc_fresh = false;
+  }
+  if (pf_active) {  // reverse contributions go to the owners' accumulators; converted by fold_finish
+    launch_assemble_fold(st, nloc, nall, sd.selt, nl_j.as<int>(), gslot.as<double>(), nl_rij.as<double>(),
+                         atom_e.as<double>(), d_force, acc_f.as<unsigned long long>(), nonfinite.as<unsigned>(),
+                         reinterpret_cast<unsigned long long*>(pf_buf), reinterpret_cast<unsigned*>(pf_buf + pf_off_nf),
+                         peer_set(), pf_origin.as<int2>(), reduce_part.as<double>(), asm_done.as<unsigned>(),
+                         d_energy, d_virial);
+    if (d_atom_energy)
+      B200DP_CUDA_TRY(cudaMemcpyAsync(d_atom_energy, atom_e.ptr, sizeof(double) * nloc, cudaMemcpyDeviceToDevice, st));
+    mark(st, 5);
+    return B200DP_OK;
+  }
+  if (d_atom_virial) {
+    const size_t bv = acc_v.bytes;
+    B200DP_CUDA_TRY(acc_v.ensure(sizeof(unsigned long long) * 18 * std::max(nall, 1)));
+    if (acc_v.bytes != bv) B200DP_CUDA_TRY(cudaMemsetAsync(acc_v.ptr, 0, acc_v.bytes, st));
   }
   launch_assemble(st, nloc, nall, sd.selt, nl_j.as<int>(), gslot.as<double>(), nl_rij.as<double>(),
                   atom_e.as<double>(), d_force, d_atom_virial, acc_f.as<unsigned long long>(),
@@ -822,6 +840,132 @@ b200dp_status Engine::check() {
       return B200DP_ERR_CAPACITY;
     }
   }
+  return B200DP_OK;
+}
+
+b200dp_status Engine::fold_export(int cap, void* handle) {
+  g_err_sink = &err;
+  if (cap <= 0 || !handle) {
+    err = "fold_export needs a capacity and a handle buffer";
+    return B200DP_ERR_INVALID;
+  }
+  if (pf_buf && cap != pf_cap) {
+    err = "the exported buffer is fixed once peers hold it (same capacity on every call and every rank)";
+    return B200DP_ERR_INVALID;
+  }
+  B200DP_CUDA_TRY(cudaSetDevice(opt.device));
+  if (!pf_buf) {
+    const size_t acc = sizeof(unsigned long long) * 6 * (size_t)cap;
+    const size_t nf = (sizeof(unsigned) * (size_t)cap + 255) & ~(size_t)255;
+    const size_t xb = sizeof(double) * 3 * (size_t)cap;
+    B200DP_CUDA_TRY(cudaMalloc(&pf_buf, acc + nf + xb));
+    B200DP_CUDA_TRY(cudaMemset(pf_buf, 0, acc + nf + xb));
+    B200DP_CUDA_TRY(cudaDeviceSynchronize());
+    pf_off_nf = acc;
+    pf_off_x = acc + nf;
+    pf_cap = cap;
+  }
+  cudaIpcMemHandle_t h;
+  B200DP_CUDA_TRY(cudaIpcGetMemHandle(&h, pf_buf));
+  std::memcpy(handle, &h, sizeof(h));
+  return B200DP_OK;
+}
+
+b200dp_status Engine::fold_connect(int nranks, int rank, const void* handles) {
+  g_err_sink = &err;
+  if (!pf_buf || nranks <= 0 || rank < 0 || rank >= nranks || !handles) {
+    err = "fold_connect needs fold_export first and every rank's handle";
+    return B200DP_ERR_INVALID;
+  }
+  B200DP_CUDA_TRY(cudaSetDevice(opt.device));
+  for (void* q : pf_opened) cudaIpcCloseMemHandle(q);
+  pf_opened.clear();
+  std::vector<unsigned char*> ptrs(nranks);
+  const auto* hs = static_cast<const cudaIpcMemHandle_t*>(handles);
+  for (int r = 0; r < nranks; ++r) {
+    if (r == rank) {
+      ptrs[r] = pf_buf;
+      continue;
+    }
+    void* q = nullptr;
+    B200DP_CUDA_TRY(cudaIpcOpenMemHandle(&q, hs[r], cudaIpcMemLazyEnablePeerAccess));
+    pf_opened.push_back(q);
+    ptrs[r] = static_cast<unsigned char*>(q);
+  }
+  B200DP_CUDA_TRY(pf_ptrs.ensure(sizeof(void*) * nranks));
+  B200DP_CUDA_TRY(cudaMemcpy(pf_ptrs.ptr, ptrs.data(), sizeof(void*) * nranks, cudaMemcpyHostToDevice));
+  pf_nranks = nranks;
+  pf_rank = rank;
+  return B200DP_OK;
+}
+
+b200dp_status Engine::fold_origins(int nghost, const int* d_origin, const double* d_shift) {
+  g_err_sink = &err;
+  if (nghost < 0 || (nghost > 0 && !d_origin)) {
+    err = "fold_origins: bad arguments";
+    return B200DP_ERR_INVALID;
+  }
+  B200DP_CUDA_TRY(cudaSetDevice(opt.device));
+  B200DP_CUDA_TRY(pf_origin.ensure(sizeof(int2) * std::max(nghost, 1)));
+  if (nghost) B200DP_CUDA_TRY(cudaMemcpy(pf_origin.ptr, d_origin, sizeof(int2) * nghost, cudaMemcpyDeviceToDevice));
+  pf_has_shift = d_shift != nullptr;
+  if (d_shift) {
+    B200DP_CUDA_TRY(pf_shift.ensure(sizeof(double) * 3 * std::max(nghost, 1)));
+    if (nghost)
+      B200DP_CUDA_TRY(cudaMemcpy(pf_shift.ptr, d_shift, sizeof(double) * 3 * nghost, cudaMemcpyDeviceToDevice));
+  }
+  pf_nghost = nghost;
+  return B200DP_OK;
+}
+
+b200dp_status Engine::halo_publish(cudaStream_t st, int nloc, const double* d_coord) {
+  g_err_sink = &err;
+  if (!pf_buf || nloc < 0 || nloc > pf_cap || (nloc && !d_coord)) {
+    err = "halo_publish: export first; nloc <= capacity";
+    return B200DP_ERR_INVALID;
+  }
+  if (nloc)
+    B200DP_CUDA_TRY(cudaMemcpyAsync(pf_buf + pf_off_x, d_coord, sizeof(double) * 3 * nloc, cudaMemcpyDeviceToDevice,
+                                    st));
+  return B200DP_OK;
+}
+
+b200dp_status Engine::halo_gather(cudaStream_t st, int nloc, int nghost, double* d_coord) {
+  g_err_sink = &err;
+  if (!pf_ptrs.ptr || !pf_has_shift || nghost != pf_nghost || !d_coord) {
+    err = "halo_gather: connect and set the ghost origins with their shifts first (nghost as given there)";
+    return B200DP_ERR_INVALID;
+  }
+  launch_halo_gather(st, nloc, nghost, d_coord, peer_set(), pf_origin.as<int2>(), pf_shift.as<double>());
+  B200DP_CUDA_TRY(cudaGetLastError());
+  return B200DP_OK;
+}
+
+b200dp_status Engine::compute_device_fold(cudaStream_t st, int nloc, int nghost, const double* d_coord,
+                                          const int* d_atype, const double* region, double* d_energy,
+                                          double* d_force, double* d_virial) {
+  g_err_sink = &err;
+  if (!pf_buf || !pf_ptrs.ptr || nloc > pf_cap || nghost != pf_nghost || !region) {
+    err = "compute_device_fold: export, connect and set the ghost origins first (nloc <= capacity, "
+          "nghost as given to fold_origins, ghost mode with a region)";
+    return B200DP_ERR_INVALID;
+  }
+  pf_active = true;
+  const b200dp_status rc = compute_device(st, nloc, nghost, d_coord, d_atype, nullptr, region, d_energy, d_force,
+                                          d_virial, nullptr, nullptr);
+  pf_active = false;
+  return rc;
+}
+
+b200dp_status Engine::fold_finish(cudaStream_t st, int nloc, double* d_force) {
+  g_err_sink = &err;
+  if (!pf_buf || nloc > pf_cap || !d_force) {
+    err = "fold_finish: bad arguments";
+    return B200DP_ERR_INVALID;
+  }
+  launch_fold_finish(st, nloc, d_force, reinterpret_cast<unsigned long long*>(pf_buf),
+                     reinterpret_cast<unsigned*>(pf_buf + pf_off_nf));
+  B200DP_CUDA_TRY(cudaGetLastError());
   return B200DP_OK;
 }
 
@@ -1127,6 +1271,44 @@ b200dp_status b200dp_last_descriptor(b200dp_engine* engine, double* descriptor, 
 }
 
 long long b200dp_kernel_launches(void) { return b200dp::launch_count(); }
+
+b200dp_status b200dp_fold_export(b200dp_engine* engine, int capacity, void* handle) {
+  if (!engine) return B200DP_ERR_INVALID;
+  return engine->e.fold_export(capacity, handle);
+}
+
+b200dp_status b200dp_fold_connect(b200dp_engine* engine, int nranks, int rank, const void* handles) {
+  if (!engine) return B200DP_ERR_INVALID;
+  return engine->e.fold_connect(nranks, rank, handles);
+}
+
+b200dp_status b200dp_fold_origins(b200dp_engine* engine, int nghost, const int* d_origin, const double* d_shift) {
+  if (!engine) return B200DP_ERR_INVALID;
+  return engine->e.fold_origins(nghost, d_origin, d_shift);
+}
+
+b200dp_status b200dp_halo_publish(b200dp_engine* engine, void* stream, int nlocal, const double* d_coord) {
+  if (!engine) return B200DP_ERR_INVALID;
+  return engine->e.halo_publish(static_cast<cudaStream_t>(stream), nlocal, d_coord);
+}
+
+b200dp_status b200dp_halo_gather(b200dp_engine* engine, void* stream, int nlocal, int nghost, double* d_coord) {
+  if (!engine) return B200DP_ERR_INVALID;
+  return engine->e.halo_gather(static_cast<cudaStream_t>(stream), nlocal, nghost, d_coord);
+}
+
+b200dp_status b200dp_compute_device_fold(b200dp_engine* engine, void* stream, int nlocal, int nghost,
+                                         const double* d_coord, const int* d_atype, const double* region,
+                                         double* d_energy, double* d_force, double* d_virial) {
+  if (!engine) return B200DP_ERR_INVALID;
+  return engine->e.compute_device_fold(static_cast<cudaStream_t>(stream), nlocal, nghost, d_coord, d_atype, region,
+                                       d_energy, d_force, d_virial);
+}
+
+b200dp_status b200dp_fold_finish(b200dp_engine* engine, void* stream, int nlocal, double* d_force) {
+  if (!engine) return B200DP_ERR_INVALID;
+  return engine->e.fold_finish(static_cast<cudaStream_t>(stream), nlocal, d_force);
+}
 
 b200dp_status b200dp_set_neighbor_reuse(b200dp_engine* engine, double skin, int every) {
   if (!engine) return B200DP_ERR_INVALID;

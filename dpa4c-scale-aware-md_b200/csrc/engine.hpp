@@ -83,6 +83,18 @@ struct Engine {
   int vl_every = 0, vl_age = 0, vl_n = -1, vl_cap = 0;
   bool vl_valid = false;
   DevBuf vl_cj, vl_cc, vl_cnt, vl_xref, vl_ls, vl_stale;
+  // peer fold (domain decomposition): this rank's owned-atom accumulator is
+  // exported by CUDA IPC; peers add their ghost edges' reverse contributions
+  // into it over NVLink
+  unsigned char* pf_buf = nullptr;  // [accumulator | flags | positions] of `pf_cap` owned atoms
+  size_t pf_off_nf = 0, pf_off_x = 0;
+  int pf_cap = 0, pf_nranks = 0, pf_rank = 0, pf_nghost = 0;
+  bool pf_active = false, pf_has_shift = false;
+  std::vector<void*> pf_opened;
+  DevBuf pf_ptrs, pf_origin, pf_shift;
+  PeerSet peer_set() const {
+    return PeerSet{pf_ptrs.as<unsigned char*>(), 0, pf_off_nf, pf_off_x};
+  }
   // host-call staging
   DevBuf h_coord, h_atype, h_force, h_aviral, h_ae;
 
@@ -130,6 +142,15 @@ struct Engine {
                              double* atom_energy, double* atom_virial);
   b200dp_status check();
   b200dp_status set_neighbor_reuse(double skin, int every);
+  b200dp_status fold_export(int cap, void* handle);
+  b200dp_status fold_connect(int nranks, int rank, const void* handles);
+  b200dp_status fold_origins(int nghost, const int* d_origin, const double* d_shift);
+  b200dp_status halo_publish(cudaStream_t st, int nloc, const double* d_coord);
+  b200dp_status halo_gather(cudaStream_t st, int nloc, int nghost, double* d_coord);
+  b200dp_status compute_device_fold(cudaStream_t st, int nloc, int nghost, const double* d_coord,
+                                    const int* d_atype, const double* region, double* d_energy, double* d_force,
+                                    double* d_virial);
+  b200dp_status fold_finish(cudaStream_t st, int nloc, double* d_force);
 };
 
 }  // namespace b200dp

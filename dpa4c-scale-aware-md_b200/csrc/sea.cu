@@ -544,13 +544,28 @@ __device__ __forceinline__ double fix_value(unsigned long long lo, unsigned long
   return (double)(long long)hi + (double)lo * 0x1p-64;
 }
 
+// (lo, hi) added to the 128-bit accumulator at p.
+__device__ __forceinline__ void fix_add128(unsigned long long* p, unsigned long long lo, unsigned long long hi) {
+  const unsigned long long old = atomicAdd(p, lo);
+  const unsigned long long inc = hi + (old + lo < old ? 1ull : 0ull);
+  if (inc) atomicAdd(p + 1, inc);
+}
+
+// Peer fold (domain decomposition): owned neighbours' contributions go to
+// this rank's exported accumulator (own, own_nf) instead of acc_f, ghost rows
+// stay in acc_f for k_fold_push.
+struct FoldTargets {
+  unsigned long long* own;
+  unsigned* own_nf;
+};
+
 template <bool kAtomVirial>
 __global__ void __launch_bounds__(kAsmWarps * 32)
     k_assemble(int nloc, int selt, const int* __restrict__ nl_j, const double* __restrict__ gslot,
                const double* __restrict__ rij, const double* __restrict__ atom_e, double* __restrict__ force,
                unsigned long long* __restrict__ acc_f, unsigned long long* __restrict__ acc_v,
                unsigned* __restrict__ nonfinite, double* __restrict__ partial, unsigned* __restrict__ done,
-               double* __restrict__ energy, double* __restrict__ virial) {
+               double* __restrict__ energy, double* __restrict__ virial, FoldTargets fold) {
   __shared__ double s_part[kAsmWarps][kAsmCols];
   __shared__ int s_last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -579,8 +594,9 @@ __global__ void __launch_bounds__(kAsmWarps * 32)
           }
         bool finite = isfinite(g3[0]) && isfinite(g3[1]) && isfinite(g3[2]);
         if (finite) {
+          unsigned long long* dst = (fold.own && j < nloc ? fold.own : acc_f) + 6 * (size_t)j;
 #pragma unroll
-          for (int c = 0; c < 3; ++c) fix_add(acc_f + 2 * (3 * (size_t)j + c), -g3[c]);
+          for (int c = 0; c < 3; ++c) fix_add(dst + 2 * c, -g3[c]);
           if (kAtomVirial) {
 #pragma unroll
             for (int c = 0; c < 9; ++c) finite = finite && isfinite(w[c]);
@@ -590,7 +606,7 @@ __global__ void __launch_bounds__(kAsmWarps * 32)
             }
           }
         }
-        if (!finite) atomicOr(nonfinite + j, 1u);
+        if (!finite) atomicOr((fold.own && j < nloc ? fold.own_nf : nonfinite) + j, 1u);
       }
     }
     if (lane == 0) e = atom_e[i];
@@ -677,15 +693,85 @@ void launch_assemble(cudaStream_t st, int nloc, int nall, int selt, const int* n
   const int fb = (nall + 255) / 256;
   count_launch();
   count_launch();
+  const FoldTargets none{nullptr, nullptr};
   if (atom_virial) {
     k_assemble<true><<<nb, kAsmWarps * 32, 0, st>>>(nloc, selt, nl_j, gslot, rij, atom_e, force, acc_f, acc_v,
-                                                    nonfinite, partial, done, energy, virial);
+                                                    nonfinite, partial, done, energy, virial, none);
     k_assemble_finish<true><<<fb, 256, 0, st>>>(nloc, nall, force, atom_virial, acc_f, acc_v, nonfinite);
   } else {
     k_assemble<false><<<nb, kAsmWarps * 32, 0, st>>>(nloc, selt, nl_j, gslot, rij, atom_e, force, acc_f, nullptr,
-                                                     nonfinite, partial, done, energy, virial);
+                                                     nonfinite, partial, done, energy, virial, none);
     k_assemble_finish<false><<<fb, 256, 0, st>>>(nloc, nall, force, nullptr, acc_f, nullptr, nonfinite);
   }
+}
+
+// Each ghost row's sums (acc_f rows nloc..nall) are added to its owner's
+// accumulator in the owner's memory (one 128-bit addition per component), and
+// the local rows are cleared for the next call.
+__global__ void k_fold_push(int nloc, int nghost, unsigned long long* __restrict__ acc_f,
+                            unsigned* __restrict__ nonfinite, PeerSet peers, const int2* __restrict__ origin) {
+  const int g = blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= nghost) return;
+  const size_t j = (size_t)nloc + g;
+  const int2 o = origin[g];
+  unsigned char* base = peers.base[o.x];
+  unsigned long long* dst = reinterpret_cast<unsigned long long*>(base + peers.off_acc) + 6 * (size_t)o.y;
+  ulonglong2* a = reinterpret_cast<ulonglong2*>(acc_f) + 3 * j;
+#pragma unroll
+  for (int c = 0; c < 3; ++c) {
+    const ulonglong2 q = a[c];
+    if (q.x | q.y) fix_add128(dst + 2 * c, q.x, q.y);
+    a[c] = make_ulonglong2(0ull, 0ull);
+  }
+  if (nonfinite[j]) {
+    nonfinite[j] = 0u;
+    atomicOr(reinterpret_cast<unsigned*>(base + peers.off_nf) + o.y, 1u);
+  }
+  __threadfence_system();  // the additions are visible to the owner before this kernel completes
+}
+
+// Ghost rows of x from the owners' published positions plus the periodic shift
+// (each component a sum of whole box lengths, applied as one addition, as the
+// staged exchange does).
+__global__ void k_halo_gather(int nloc, int nghost, double* __restrict__ x, PeerSet peers,
+                              const int2* __restrict__ origin, const double* __restrict__ shift) {
+  const int g = blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= nghost) return;
+  const int2 o = origin[g];
+  const double* src = reinterpret_cast<const double*>(peers.base[o.x] + peers.off_x) + 3 * (size_t)o.y;
+  const double s0 = src[0], s1 = src[1], s2 = src[2];
+  double* dst = x + 3 * ((size_t)nloc + g);
+  dst[0] = s0 + shift[3 * (size_t)g];
+  dst[1] = s1 + shift[3 * (size_t)g + 1];
+  dst[2] = s2 + shift[3 * (size_t)g + 2];
+}
+
+void launch_assemble_fold(cudaStream_t st, int nloc, int nall, int selt, const int* nl_j, const double* gslot,
+                          const double* rij, const double* atom_e, double* force, unsigned long long* acc_f,
+                          unsigned* nonfinite, unsigned long long* own_acc, unsigned* own_nf, const PeerSet& peers,
+                          const int2* origin, double* partial, unsigned* done, double* energy, double* virial) {
+  count_launch();
+  const FoldTargets fold{own_acc, own_nf};
+  k_assemble<false><<<assemble_blocks(nloc), kAsmWarps * 32, 0, st>>>(
+      nloc, selt, nl_j, gslot, rij, atom_e, force, acc_f, nullptr, nonfinite, partial, done, energy, virial, fold);
+  const int nghost = nall - nloc;
+  if (nghost > 0) {
+    count_launch();
+    k_fold_push<<<(nghost + 255) / 256, 256, 0, st>>>(nloc, nghost, acc_f, nonfinite, peers, origin);
+  }
+}
+
+void launch_fold_finish(cudaStream_t st, int nloc, double* force, unsigned long long* acc, unsigned* nonfinite) {
+  if (nloc <= 0) return;
+  count_launch();
+  k_assemble_finish<false><<<(nloc + 255) / 256, 256, 0, st>>>(nloc, nloc, force, nullptr, acc, nullptr, nonfinite);
+}
+
+void launch_halo_gather(cudaStream_t st, int nloc, int nghost, double* x, const PeerSet& peers, const int2* origin,
+                        const double* shift) {
+  if (nghost <= 0) return;
+  count_launch();
+  k_halo_gather<<<(nghost + 255) / 256, 256, 0, st>>>(nloc, nghost, x, peers, origin, shift);
 }
 
 // ---------------------------------------------------------------- instantiations

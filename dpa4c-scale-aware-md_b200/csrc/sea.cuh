@@ -73,5 +73,27 @@ void launch_assemble(cudaStream_t st, int nloc, int nall, int selt, const int* n
                      unsigned long long* acc_f, unsigned long long* acc_v, unsigned* nonfinite, double* partial,
                      unsigned* done, double* energy, double* virial);
 int assemble_blocks(int nloc);
+// Domain decomposition over NVLink peers.  Every rank exports one device
+// buffer (CUDA IPC) holding its owned atoms' fixed-point force accumulator
+// ([cap][3][lo, hi] u64 at off_acc), their non-finite flags (u32 at off_nf)
+// and their published positions ([cap][3] f64 at off_x); base[r] is rank r's
+// buffer as mapped in this process.
+struct PeerSet {
+  unsigned char* const* base;
+  size_t off_acc, off_nf, off_x;
+};
+// The assembly with owned neighbours' contributions added to this rank's
+// exported accumulator (own_acc, own_nf) and ghost rows (acc_f rows
+// nloc..nall) then pushed to their owners' accumulators, origin[g] = (owner
+// rank, owner's row) -- no conversion; launch_fold_finish converts this rank's
+// accumulator into the owned forces once every rank's push has completed.
+void launch_assemble_fold(cudaStream_t st, int nloc, int nall, int selt, const int* nl_j, const double* gslot,
+                          const double* rij, const double* atom_e, double* force, unsigned long long* acc_f,
+                          unsigned* nonfinite, unsigned long long* own_acc, unsigned* own_nf, const PeerSet& peers,
+                          const int2* origin, double* partial, unsigned* done, double* energy, double* virial);
+void launch_fold_finish(cudaStream_t st, int nloc, double* force, unsigned long long* acc, unsigned* nonfinite);
+// x rows nloc..nloc+nghost from the owners' published positions (+ shift [nghost][3]).
+void launch_halo_gather(cudaStream_t st, int nloc, int nghost, double* x, const PeerSet& peers, const int2* origin,
+                        const double* shift);
 
 }  // namespace b200dp

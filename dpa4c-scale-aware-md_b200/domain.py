@@ -17,6 +17,16 @@ The exchanges use torch.distributed point-to-point calls (NCCL on GPUs, gloo
 on CPUs), so the same code runs the CPU tests and the GPU benchmark.  Within
 one pass the atoms sent in one direction are distinct, so the reverse fold is
 a plain indexed add with no colliding indices (deterministic).
+
+With GPUs that are NVLink peers both exchanges can be left out (PeerFold):
+the plan also records every ghost's origin (owner rank, owner's row) and its
+periodic shift.  Each step every rank publishes its owned positions into a
+buffer the others map (CUDA IPC), a one-element all-reduce orders the
+publishes before any read, and one kernel fills the ghost rows from the
+owners' buffers over NVLink.  After the force call the engine adds each ghost
+row's reverse contribution directly into the owner's fixed-point force
+accumulator in the owner's memory; the all-reduce of energy and virial orders
+every rank's additions before any rank converts its accumulator into forces.
 """
 from __future__ import annotations
 
@@ -147,6 +157,10 @@ class HaloExchange:
         x = x_owned.clone()
         t = types_owned.clone()
         ids = ids_owned.clone() if ids_owned is not None else None
+        # origin of every row: (owner rank, owner's row); forwarded like the ids
+        org = torch.stack([torch.full((x.shape[0],), self.rank, dtype=torch.int32, device=dev),
+                           torch.arange(x.shape[0], dtype=torch.int32, device=dev)], dim=1)
+        sh = torch.zeros_like(x)  # periodic shift of every row from its owner's position
         self.nloc = x.shape[0]
         self.passes: list[Pass] = []
         for dim in range(3):
@@ -174,17 +188,29 @@ class HaloExchange:
                     _exchange(ids[idx].clone(), peer_send, ri, peer_recv, self.rank)
                 else:
                     ri = None
+                ro = torch.empty((n_recv, 2), dtype=org.dtype, device=dev)
+                _exchange(org[idx].contiguous(), peer_send, ro, peer_recv, self.rank)
+                ssh = sh[idx].clone()
+                ssh[:, dim] += shift
+                rsh = torch.empty((n_recv, 3), dtype=sh.dtype, device=dev)
+                _exchange(ssh, peer_send, rsh, peer_recv, self.rank)
                 off = x.shape[0] + sum(b[0].shape[0] for b in blocks)
                 self.passes.append(Pass(dim, direction, peer_send, peer_recv, shift, idx, off, n_recv))
-                blocks.append((rp, rt, ri))
+                blocks.append((rp, rt, ri, ro, rsh))
             x = torch.cat([x] + [b[0] for b in blocks])
             t = torch.cat([t] + [b[1] for b in blocks])
+            org = torch.cat([org] + [b[3] for b in blocks])
+            sh = torch.cat([sh] + [b[4] for b in blocks])
             if ids is not None:
                 ids = torch.cat([ids] + [b[2] for b in blocks])
         self.nall = x.shape[0]
         self.x = x
         self.types = t
         self.ids = ids
+        self.origin = org[self.nloc:].contiguous()  # [nghost, 2] int32: owner rank, owner's row
+        # [nghost, 3]: each component is one pass's shift (or 0), so owner + shift is the
+        # same single addition the staged exchange makes
+        self.shift = sh[self.nloc:].contiguous()
 
     @property
     def nghost(self) -> int:
@@ -233,6 +259,69 @@ def distribute(coord: np.ndarray, atype: np.ndarray, dd: Decomposition):
     return w[mask], np.asarray(atype)[mask], ids
 
 
+class PeerFold:
+    """Halo exchange and reverse pass through peer memory for a b200dp engine
+    (b200dp_fold_* / b200dp_halo_*).
+
+    Each rank exports one buffer (CUDA IPC handle) holding its owned atoms'
+    published positions and fixed-point force accumulator, and opens every
+    other rank's.  `publish` + `gather` replace the forward exchange: the
+    ghost rows are read from the owners' positions (plus the periodic shift)
+    by one kernel, after a barrier that orders every rank's publish before
+    any read.  The force call adds the reverse contribution of every ghost
+    row straight into the owner's accumulator (integer atomics over NVLink,
+    order-independent sums) instead of returning ghost forces; `finish`
+    converts this rank's accumulator into the owned rows' forces and must run
+    after every rank's force call has completed, which the all-reduce of
+    energy and virial on the same stream guarantees.  Ranks that share one
+    GPU work too (the handles then map the same device's memory).
+    """
+
+    gathers = True
+
+    def __init__(self, dp, device, stream=None, capacity_margin: float = 2.0):
+        self.dp = dp
+        self.device = torch.device(device)
+        self.stream = stream
+        self.margin = capacity_margin
+        self.origin = self.shift = None
+
+    def _stream(self) -> int:
+        if self.stream is not None:
+            return self.stream.cuda_stream
+        return torch.cuda.current_stream(self.device).cuda_stream
+
+    def setup(self, rank: int, nranks: int, nloc: int, origin: torch.Tensor, shift: torch.Tensor) -> None:
+        """Collective over all ranks: export (one capacity for all), exchange handles, open them,
+        upload the ghost origins and shifts."""
+        nlocs = [nloc]
+        if dist.is_initialized():
+            nlocs = [None] * nranks
+            dist.all_gather_object(nlocs, nloc)
+        h = self.dp.fold_export(int(self.margin * max(nlocs)) + 1024)
+        handles = [h]
+        if dist.is_initialized():
+            handles = [None] * nranks
+            dist.all_gather_object(handles, h)
+        self.dp.fold_connect(rank, handles)
+        self.origin = origin.to(device=self.device, dtype=torch.int32).contiguous()
+        self.shift = shift.to(device=self.device, dtype=torch.float64).contiguous()
+        self.dp.fold_origins(self.origin.shape[0], self.origin.data_ptr(), self.shift.data_ptr())
+
+    def publish(self, x_all, nloc) -> None:
+        self.dp.halo_publish(self._stream(), nloc, x_all.data_ptr())
+
+    def gather(self, x_all, nloc, nghost) -> None:
+        self.dp.halo_gather(self._stream(), nloc, nghost, x_all.data_ptr())
+
+    def compute(self, x_all, t_all, nloc, nghost, region, e, f, v):
+        self.dp.compute_device_fold(self._stream(), nloc, nghost, x_all.data_ptr(), t_all.data_ptr(), region,
+                                    e.data_ptr(), f.data_ptr(), v.data_ptr())
+
+    def finish(self, f, nloc) -> None:
+        self.dp.fold_finish(self._stream(), nloc, f.data_ptr())
+
+
 class DistributedDeepPot:
     """Energy, forces and virial of a periodic system split over the ranks.
 
@@ -243,12 +332,17 @@ class DistributedDeepPot:
     of the owned atoms' edges into v [9].  With the b200dp engine this is
     b200dp_compute_device on the rank's stream; the tests pass the CPU oracle.
     Per step: forward halo of coordinates, the force call, reverse fold of the
-    ghost forces, one all-reduce of energy and virial (10 fp64).
+    ghost forces, one all-reduce of energy and virial (10 fp64).  With
+    `fold` (a PeerFold, or anything with its methods) the ghost rows come
+    from fold.publish / barrier / fold.gather (or the staged forward exchange
+    when fold.gathers is false), the force call is fold.compute, the reverse
+    exchange is left out and fold.finish follows the all-reduce.
     """
 
-    def __init__(self, compute, box, grid, rank, halo, x_owned, t_owned, ids_owned=None, device="cpu"):
+    def __init__(self, compute, box, grid, rank, halo, x_owned, t_owned, ids_owned=None, device="cpu", fold=None):
         self.dd = Decomposition(box, grid, rank, halo)
         self.compute = compute
+        self.fold = fold
         dev = torch.device(device)
         self.device = dev
         x = torch.as_tensor(np.asarray(x_owned, dtype=np.float64), device=dev)
@@ -265,6 +359,10 @@ class DistributedDeepPot:
         self.force = torch.zeros((self.plan.nall, 3), dtype=torch.float64, device=dev)
         self.ev = torch.zeros(10, dtype=torch.float64, device=dev)  # energy, virial[9]
         self.region = self.dd.region()
+        if fold is not None:
+            nranks = dist.get_world_size() if dist.is_initialized() else 1
+            fold.setup(rank, nranks, self.nloc, self.plan.origin, self.plan.shift)
+        self._bar = torch.zeros(1, dtype=torch.float32, device=dev)
 
     def set_positions(self, x_owned: torch.Tensor) -> None:
         """New owned positions (same atoms, same owner; migration needs a new plan)."""
@@ -275,7 +373,20 @@ class DistributedDeepPot:
         if self._graph is not None:
             self._graph.replay()
             return self.ev[0:1], self.force[: self.nloc], self.ev[1:10]
-        self.plan.forward(self.x)
+        if self.fold is not None and self.fold.gathers:
+            self.fold.publish(self.x, self.nloc)
+            if dist.is_initialized():  # every rank's positions are published before any is read
+                dist.all_reduce(self._bar)
+            self.fold.gather(self.x, self.nloc, self.nghost)
+        else:
+            self.plan.forward(self.x)
+        if self.fold is not None:
+            self.fold.compute(self.x, self.types, self.nloc, self.nghost, self.region, self.ev[0:1], self.force,
+                              self.ev[1:10])
+            if dist.is_initialized():  # every rank's additions are done once this completes
+                dist.all_reduce(self.ev, op=dist.ReduceOp.SUM)
+            self.fold.finish(self.force, self.nloc)
+            return self.ev[0:1], self.force[: self.nloc], self.ev[1:10]
         self.compute(self.x, self.types, self.nloc, self.nghost, self.region, self.ev[0:1], self.force,
                      self.ev[1:10])
         self.plan.reverse(self.force)

@@ -235,6 +235,46 @@ typedef enum b200dp_md_ensemble { B200DP_MD_NVE = 0, B200DP_MD_NVT = 1, B200DP_M
  * (LO/KOKKOS/npair_kokkos.cpp:151-460 with neigh_modify every / check). */
 b200dp_status b200dp_set_neighbor_reuse(b200dp_engine* engine, double skin, int every);
 
+/* Halo exchange and reverse fold for spatial domain decomposition, one
+ * process per GPU on NVLink peers, through one device buffer per rank that
+ * every other rank maps (CUDA IPC): the owned atoms' positions, published
+ * every step, and their fixed-point force accumulator.
+ *   b200dp_fold_export   allocates this rank's buffer for `capacity` owned
+ *                        atoms (the same capacity on every rank) and writes
+ *                        its CUDA IPC handle (64 bytes) to `handle`;
+ *   b200dp_fold_connect  opens every other rank's handle (handles: nranks
+ *                        x 64 bytes, rank order);
+ *   b200dp_fold_origins  d_origin [nghost][2] int: owner rank and owner's
+ *                        atom index of every ghost row; d_shift [nghost][3]
+ *                        f64 (may be NULL without halo_gather): the periodic
+ *                        shift added to the owner's position (device memory);
+ *   b200dp_halo_publish  copies the owned positions into this rank's buffer;
+ *   b200dp_halo_gather   writes the ghost rows nlocal.. of d_coord from the
+ *                        owners' published positions (+ shift) -- only after
+ *                        every rank's publish of this step has completed
+ *                        (e.g. after a one-element all-reduce on the stream);
+ *   b200dp_compute_device_fold  the ghost-mode force call: energy and virial
+ *                        of the owned atoms' edges as usual; the ghost rows'
+ *                        reverse contributions are added into the owners'
+ *                        accumulators (128-bit integer atomics over NVLink:
+ *                        order-independent sums) and d_force is not complete
+ *                        yet;
+ *   b200dp_fold_finish   after EVERY rank's compute_device_fold has completed
+ *                        (e.g. after the all-reduce of energy and virial on
+ *                        the same stream), writes the owned rows of d_force
+ *                        and clears the accumulator.
+ * Replaces the pair style's forward and reverse ghost communication
+ * (PL/pair_deepmd_kokkos.cpp:931, comm->reverse_comm; LAMMPS comm->forward_comm). */
+b200dp_status b200dp_fold_export(b200dp_engine* engine, int capacity, void* handle);
+b200dp_status b200dp_fold_connect(b200dp_engine* engine, int nranks, int rank, const void* handles);
+b200dp_status b200dp_fold_origins(b200dp_engine* engine, int nghost, const int* d_origin, const double* d_shift);
+b200dp_status b200dp_halo_publish(b200dp_engine* engine, void* stream, int nlocal, const double* d_coord);
+b200dp_status b200dp_halo_gather(b200dp_engine* engine, void* stream, int nlocal, int nghost, double* d_coord);
+b200dp_status b200dp_compute_device_fold(b200dp_engine* engine, void* stream, int nlocal, int nghost,
+                                         const double* d_coord, const int* d_atype, const double* region,
+                                         double* d_energy, double* d_force, double* d_virial);
+b200dp_status b200dp_fold_finish(b200dp_engine* engine, void* stream, int nlocal, double* d_force);
+
 typedef struct b200dp_md_params {
   double dt;        /* time step, ps (default 0.0005) */
   int ensemble;     /* b200dp_md_ensemble */

@@ -6,6 +6,11 @@
   cuda:0 (every rank on the same GPU, each with its own engine; nothing on
   the GPU waits for another rank), the exchange over gloo on CPU tensors.
 --engine b200dp --backend nccl: one GPU per rank, exchange over NCCL.
+--fold: the reverse exchange is replaced by the engine's peer fold (ghost
+  contributions added into the owners' accumulators through CUDA IPC); with
+  gloo the ranks share cuda:0 and the host synchronises before the all-reduce.
+The rank also records its ghost origins (owner rank, owner's row) and the
+global ids of its ghost rows.
 The rank writes its owned atoms' global ids and forces plus the all-reduced
 energy and virial to an .npz for the parent test.
 """
@@ -70,6 +75,47 @@ def b200dp_compute(model, precision, device, staged):
     return compute
 
 
+class StagedFold:
+    """PeerFold for ranks that exchange CPU tensors over gloo and share one GPU
+    (the host synchronises after every device step, so no rank's kernel waits
+    for another's)."""
+
+    gathers = True
+
+    def __init__(self, dp, device):
+        self.pf = domain.PeerFold(dp, device)
+        self.dev = torch.device(device)
+        self.dp = dp
+
+    def setup(self, rank, nranks, nloc, origin, shift):
+        self.pf.setup(rank, nranks, nloc, origin, shift)
+
+    def publish(self, x_all, nloc):
+        self.xp = x_all.to(self.dev)
+        self.pf.publish(self.xp, nloc)
+        torch.cuda.synchronize(self.dev)
+
+    def gather(self, x_all, nloc, nghost):
+        xd = x_all.to(self.dev)
+        self.pf.gather(xd, nloc, nghost)
+        x_all[nloc:].copy_(xd[nloc:].cpu())
+
+    def compute(self, x_all, t_all, nloc, nghost, region, e, f, v):
+        self.xd, self.td = x_all.to(self.dev), t_all.to(self.dev)
+        self.fd = torch.zeros_like(self.xd)
+        ed = torch.zeros(1, dtype=torch.float64, device=self.dev)
+        vd = torch.zeros(9, dtype=torch.float64, device=self.dev)
+        self.pf.compute(self.xd, self.td, nloc, nghost, region, ed, self.fd, vd)
+        e.copy_(ed.cpu())  # host sync: this rank's additions into the peers are complete
+        v.copy_(vd.cpu())
+        self.dp.check()
+
+    def finish(self, f, nloc):
+        self.pf.finish(self.fd, nloc)
+        f[:nloc].copy_(self.fd[:nloc].cpu())
+        self.dp.check()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--model", required=True)
@@ -80,6 +126,8 @@ def main():
     ap.add_argument("--engine", default="oracle", choices=["oracle", "b200dp"])
     ap.add_argument("--backend", default="gloo", choices=["gloo", "nccl"])
     ap.add_argument("--precision", default="fp64", choices=["fp64", "mixed"])
+    ap.add_argument("--fold", action="store_true")
+    ap.add_argument("--capture", action="store_true", help="replay the step as a CUDA graph (nccl)")
     ap.add_argument("--out", required=True)
     a = ap.parse_args()
     rank = int(os.environ["RANK"])
@@ -94,16 +142,28 @@ def main():
     s = systems.water(*a.mol, seed=3)
     dd = domain.Decomposition(s.box, a.grid, rank, a.halo)
     x, t, ids = domain.distribute(s.coord, s.atype, dd)
+    fold = None
     if a.engine == "oracle":
         compute = oracle_compute(a.model)
     else:
         compute = b200dp_compute(a.model, a.precision, device if a.backend == "nccl" else "cuda:0",
                                  staged=a.backend == "gloo")
-    ddp = domain.DistributedDeepPot(compute, s.box, a.grid, rank, a.halo, x, t, ids, device=device)
+        if a.fold:
+            fold = domain.PeerFold(compute.engine, device) if a.backend == "nccl" else \
+                StagedFold(compute.engine, "cuda:0")
+    ddp = domain.DistributedDeepPot(compute, s.box, a.grid, rank, a.halo, x, t, ids, device=device, fold=fold)
+    if a.capture:
+        ddp.capture()
     for _ in range(a.steps):  # the plan is replayed: each step must give the same answer
         e, f, v = ddp.step()
+    if a.engine == "b200dp":
+        torch.cuda.synchronize()
+        compute.engine.check()
     np.savez(a.out, ids=ids, force=f.cpu().numpy(), energy=e.cpu().numpy(), virial=v.cpu().numpy(),
-             nghost=ddp.nghost)
+             nghost=ddp.nghost, origin=ddp.plan.origin.cpu().numpy(),
+             ghost_ids=ddp.plan.ids[ddp.nloc:].cpu().numpy(), shift=ddp.plan.shift.cpu().numpy(),
+             x_owned=ddp.x[: ddp.nloc].cpu().numpy(), x_ghost=ddp.x[ddp.nloc:].cpu().numpy())
+    ddp.release()  # the graph holds NCCL calls: release it before the group goes
     dist.barrier()
     dist.destroy_process_group()
 

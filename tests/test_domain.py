@@ -114,6 +114,19 @@ def test_decomposition_geometry():
     assert (w >= 0).all() and (w < 40).all()
 
 
+def check_origins(parts):
+    """Every ghost row's recorded origin (owner rank, owner's row) is the atom it
+    copies, and the owner's position plus the recorded shift is the ghost's
+    position bit for bit (what the peer gather computes)."""
+    for p in parts:
+        o = p["origin"]
+        assert o.shape == (int(p["nghost"]), 2)
+        owner_ids = np.array([parts[r]["ids"][k] for r, k in o])
+        np.testing.assert_array_equal(owner_ids, p["ghost_ids"])
+        xo = np.array([parts[r]["x_owned"][k] for r, k in o])
+        np.testing.assert_array_equal(xo + p["shift"], p["x_ghost"])
+
+
 @pytest.mark.parametrize("grid,mol,halo", [((2, 1, 1), (8, 4, 4), 6.0), ((2, 1, 1), (8, 4, 4), 6.2),
                                            ((2, 2, 1), (8, 8, 4), 6.0)])
 def test_gloo_ranks_equal_periodic(tmp_path, model_dir, grid, mol, halo):
@@ -122,3 +135,4 @@ def test_gloo_ranks_equal_periodic(tmp_path, model_dir, grid, mol, halo):
     parts = run_ranks(tmp_path, model, mol, grid, halo)
     assert all(int(p["nghost"]) > 0 for p in parts)
     check(s, ref, parts)
+    check_origins(parts)
