@@ -29,6 +29,15 @@ random-init weights, seed 0).  Inputs are seeded synthetic data.
   per launch over its CUDA-event duration, against the measured bf16 peak.
 * ``cpu_baseline``: the CPU oracle (C++ fp64, OpenMP) on the host cores.
 
+``--sweep`` measures the five configurations instead of the headline (one JSON
+line per configuration and mode): on 1 GPU the force call on every system
+(C0 fp64 and mixed, C1 fp64 and mixed, C2, C3, the C4 water sizes 1.5k-3.1M
+and the 786k slab, mixed) and the device MD driver over the configuration's
+steps (C1 NVT 1000, C2 NPT 500, C3 NVT 200, C4 NVT 100; neighbour candidates
+rebuilt every 10 steps with a 2 A skin); on N > 1 GPUs the domain-decomposed
+force call of the systems the configurations run there (C2 on 2, C3 and the
+C4 786k / 3.1M / slab on 2, 4, 8; strong scaling: the global system is fixed).
+
 ``--impl reference`` times the reference arm: the reference ships no CPU (or
 NVIDIA) implementation of this path, so it is the CPU restatement (oracle)
 run with all host threads on the same configuration.
@@ -67,6 +76,8 @@ def parse():
     ap.add_argument("--impl", default="b200dp", choices=["b200dp", "reference"])
     ap.add_argument("--precision", default="mixed", choices=["mixed", "fp64"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sweep", action="store_true", help="measure the five configurations (see module doc)")
+    ap.add_argument("--only", default="", help="--sweep: comma-separated labels to run")
     ap.add_argument("--reverse", default="peer", choices=["peer", "nccl"],
                     help="N > 1: ghost forces to their owners by peer-memory atomics or by NCCL send/recv")
     return ap.parse_args()
@@ -557,11 +568,166 @@ def e2e_decomposed(w, steps, warmup, torch, dist):
             "bytes_rank": "rank 0's own counts"}
 
 
+# ----------------------------------------------------------------- configuration sweep
+MASSES = {"water": [15.9994, 1.00794], "cu": [63.546], "alloy": [55.845, 51.996, 58.693, 58.933]}
+
+
+def sweep_table():
+    """(label, system factory, model kind, force-call precisions, MD (ensemble, steps, T), GPU counts)."""
+    c4 = lambda size: (lambda: systems.config4(size))  # noqa: E731
+    return [
+        ("c0_water_192", systems.config0, "water", ("fp64", "mixed"), None, (1,)),
+        ("c1_water_12288", systems.config1, "water", ("fp64", "mixed"), ("nvt", 1000, 300.0), (1,)),
+        ("c2_cu_131072", systems.config2, "cu", ("mixed",), ("npt", 500, 800.0), (1, 2)),
+        ("c3_bcc_524288", systems.config3, "alloy", ("mixed",), ("nvt", 200, 300.0), (1, 2, 4, 8)),
+        ("c4_water_1.5k", c4("1.5k"), "water", ("mixed",), ("nvt", 100, 300.0), (1,)),
+        ("c4_water_12k", c4("12k"), "water", ("mixed",), ("nvt", 100, 300.0), (1,)),
+        ("c4_water_98k", c4("98k"), "water", ("mixed",), ("nvt", 100, 300.0), (1,)),
+        ("c4_water_786k", c4("786k"), "water", ("mixed",), ("nvt", 100, 300.0), (1, 2, 4, 8)),
+        ("c4_water_3.1M", c4("3.1M"), "water", ("mixed",), ("nvt", 100, 300.0), (1, 2, 4, 8)),
+        ("c4_water_786k-slab", c4("786k-slab"), "water", ("mixed",), ("nvt", 100, 300.0), (1, 2, 4, 8)),
+    ]
+
+
+def sweep_grid(label, world):
+    """The slab's vacuum half holds no atoms: it is never split along z."""
+    import domain
+
+    if "slab" in label:
+        return {1: (1, 1, 1), 2: (2, 1, 1), 4: (2, 2, 1), 8: (4, 2, 1)}.get(world, (world, 1, 1))
+    return domain.rank_grid(world)
+
+
+def timed_steps(torch, w, steps, warmup, dist, flush, stream, sync):
+    """Device time of `steps` force calls (CUDA events on the launch stream, L2 flushed before each)."""
+    for _ in range(warmup):
+        w.step()
+    if hasattr(w, "capture"):
+        w.capture()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    for k in range(steps):
+        flush.fill_(k & 0xFF)
+        if dist:
+            dist.all_reduce(sync)
+        starts[k].record(stream)
+        w.step()
+        ends[k].record(stream)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    if hasattr(w, "release"):
+        w.release()
+    return sum(a.elapsed_time(b) for a, b in zip(starts, ends))
+
+
+def run_sweep(args, world, rank, local):
+    import datetime
+
+    import torch
+
+    import b200dp
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    sync = torch.zeros(1, device=dev)
+    models = {}
+    only = set(filter(None, args.only.split(",")))
+    for label, sysf, kind, precisions, md_cfg, gpus in sweep_table():
+        if world not in gpus or (only and label not in only):
+            continue
+        if kind not in models:
+            models[kind] = model_path(kind)
+        system = sysf()
+        for prec_name in precisions:
+            prec = b200dp.MIXED if prec_name == "mixed" else b200dp.FP64
+            line = {"sweep": label, "n_gpus": world, "atoms": system.natoms, "precision": prec_name,
+                    "model": kind, "unit": "atom-steps/s", "data": "synthetic (seeded system, random-init weights)"}
+            try:
+                dp = b200dp.DeepPot(models[kind], precision=prec, device=local)
+                if world == 1:
+                    w = Periodic(dp, system, dev, stream, torch)
+                else:
+                    grid = sweep_grid(label, world)
+                    w = Decomposed(dp, system, grid, rank, dev, stream, torch, peer_fold=args.reverse == "peer")
+                    line["parallelism"] = f"domain decomposition {grid[0]}x{grid[1]}x{grid[2]}, peer fold"
+                # about 2 s of timed work, at least 3 steps
+                w.step()
+                torch.cuda.synchronize()
+                t0 = time.perf_counter()
+                w.step()
+                torch.cuda.synchronize()
+                one = time.perf_counter() - t0
+                k = int(min(max(3, 2.0 / max(one, 1e-4)), 50))
+                if dist:  # every rank runs the same number of steps
+                    kk = torch.tensor([k], device=dev)
+                    dist.all_reduce(kk, op=dist.ReduceOp.MIN)
+                    k = int(kk.item())
+                ms = timed_steps(torch, w, k, 3, dist, flush, stream, sync)
+                if dist:
+                    tt = torch.tensor([ms], dtype=torch.float64, device=dev)
+                    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+                    ms = float(tt.item())
+                dp.check()
+                line.update({"mode": "force call", "value": system.natoms * k / (ms / 1e3), "ms_per_step": ms / k,
+                             "steps": k, "timing": "CUDA events per step, max over ranks, L2 flushed before each"})
+                del w
+                dp.close()
+            except Exception as ex:  # report, never hide
+                line["error"] = repr(ex)[:400]
+            if rank == 0:
+                print(json.dumps(line), flush=True)
+            torch.cuda.empty_cache()
+        if md_cfg and world == 1:
+            ens, nsteps, temp = md_cfg
+            line = {"sweep": label, "n_gpus": 1, "atoms": system.natoms, "precision": "mixed", "model": kind,
+                    "unit": "atom-steps/s", "mode": f"MD {ens.upper()} {nsteps} steps, dt 0.5 fs, {temp:g} K"
+                    + (", 1 bar" if ens == "npt" else "") + ", candidates rebuilt every 10 steps (2 A skin)"}
+            try:
+                dp = b200dp.DeepPot(models[kind], precision=b200dp.MIXED, device=local)
+                kw = dict(dt=0.0005, ensemble=b200dp.NPT if ens == "npt" else b200dp.NVT, t_init=temp,
+                          t_target=temp, t_damp=0.05, seed=1, skin=2.0, rebuild_every=10)
+                if ens == "npt":
+                    kw.update(p_target=1.0, p_damp=0.5)
+                md = b200dp.MD(dp, system.coord, system.atype, system.box, MASSES[kind], **kw)
+                md.run(3)
+                md.thermo()
+                t0 = time.perf_counter()
+                md.run(nsteps)
+                th = md.thermo()
+                dt = time.perf_counter() - t0
+                line.update({"value": system.natoms * nsteps / dt, "ms_per_step": 1e3 * dt / nsteps,
+                             "steps": nsteps, "temperature_K": th["temp"], "conserved": th["conserved"],
+                             "timing": "host wall clock around the enqueued steps + final read"})
+                md.close()
+                dp.close()
+            except Exception as ex:  # report, never hide
+                line["error"] = repr(ex)[:400]
+            print(json.dumps(line), flush=True)
+            torch.cuda.empty_cache()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     world, rank, local = dist_env()
     if args.impl == "reference":
         run_reference(args, world, rank)
+        return
+    if args.sweep:
+        run_sweep(args, world, rank, local)
         return
     run_b200dp(args, world, rank, local)
 

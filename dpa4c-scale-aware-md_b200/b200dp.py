@@ -30,7 +30,7 @@ EXPORTS = [
     "b200dp_options_default", "b200dp_create", "b200dp_destroy", "b200dp_last_error", "b200dp_model_info_get",
     "b200dp_compute_host", "b200dp_compute_host_nlist", "b200dp_compute_device", "b200dp_check",
     "b200dp_sel_overflow_count", "b200dp_last_nlist", "b200dp_last_descriptor", "b200dp_set_stage_timing",
-    "b200dp_set_neighbor_reuse", "b200dp_fold_export", "b200dp_fold_connect", "b200dp_fold_origins",
+    "b200dp_set_neighbor_reuse", "b200dp_neighbor_stats", "b200dp_fold_export", "b200dp_fold_connect", "b200dp_fold_origins",
     "b200dp_compute_device_fold", "b200dp_fold_finish", "b200dp_halo_publish", "b200dp_halo_gather",
     "b200dp_stage_times", "b200dp_kernel_launches", "b200dp_selftest_mma", "b200dp_build_nlist_noalloc",
     "b200dp_direct_bind", "b200dp_direct_energy_force", "b200dp_md_params_default", "b200dp_md_create",
@@ -105,6 +105,7 @@ def load_library(path: str = LIB_PATH):
     L.b200dp_last_descriptor.argtypes = [_vp, _dp, _dp]
     L.b200dp_set_stage_timing.argtypes = [_vp, ctypes.c_int]
     L.b200dp_set_neighbor_reuse.argtypes = [_vp, ctypes.c_double, ctypes.c_int]
+    L.b200dp_neighbor_stats.argtypes = [_vp, ctypes.POINTER(ctypes.c_longlong)]
     L.b200dp_fold_export.argtypes = [_vp, ctypes.c_int, _vp]
     L.b200dp_fold_connect.argtypes = [_vp, ctypes.c_int, ctypes.c_int, _vp]
     L.b200dp_fold_origins.argtypes = [_vp, ctypes.c_int, _vp, _vp]
@@ -235,7 +236,8 @@ class DeepPot:
         return d, dd
 
     def set_neighbor_reuse(self, skin: float, every: int):
-        """Periodic calls reuse rcut + skin candidates for `every` calls (0: off)."""
+        """Periodic calls reuse rcut + skin candidates, built at least every `every` calls and
+        whenever an atom moved more than skin / 2 (0: off)."""
         self._raise(self.L.b200dp_set_neighbor_reuse(self.h, float(skin), int(every)))
 
     # peer fold (domain decomposition over NVLink peers; see domain.PeerFold)
@@ -269,6 +271,12 @@ class DeepPot:
 
     def fold_finish(self, stream: int, nloc: int, force_ptr: int) -> None:
         self._raise(self.L.b200dp_fold_finish(self.h, stream or None, int(nloc), force_ptr))
+
+    def neighbor_stats(self) -> dict:
+        """Candidate builds so far: scheduled and triggered by the displacement check."""
+        b = (ctypes.c_longlong * 2)()
+        self._raise(self.L.b200dp_neighbor_stats(self.h, b))
+        return {"scheduled": int(b[0]), "triggered": int(b[1])}
 
     def set_stage_timing(self, on: bool):
         self._raise(self.L.b200dp_set_stage_timing(self.h, int(on)))

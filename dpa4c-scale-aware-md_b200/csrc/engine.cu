@@ -403,17 +403,25 @@ b200dp_status Engine::ensure_buffers(int nloc, int nall, int ncells, int ncand) 
   B200DP_CUDA_TRY(perm_pos.ensure(sizeof(int) * L));
   B200DP_CUDA_TRY(perm_atom.ensure(sizeof(int) * L));
   B200DP_CUDA_TRY(Tbuf.ensure(ps * L * 4 * sd.M1));
-  B200DP_CUDA_TRY(Dbuf.ensure(ps * L * sd.dim));
-  B200DP_CUDA_TRY(dDbuf.ensure(ps * L * sd.dim));
-  const int nfl = (int)hm.fit.size();
-  th_l.resize(nfl);
-  y_l.resize(nfl);
-  for (int l = 0; l < nfl; ++l) {
-    B200DP_CUDA_TRY(th_l[l].ensure(ps * L * hm.fit[l]));
-    B200DP_CUDA_TRY(y_l[l].ensure(ps * L * hm.fit[l]));
+  // the tensor-core fitting reads its own tiled operands: descriptor rows only
+  // when they are kept, and no per-layer SIMT activations (about 22 KB an atom
+  // for the water model, which is what lets 3 M atoms fit on one GPU)
+  const bool tc_fit = !fp64 && !c8 && use_tc && use_fit_tc;
+  if (!tc_fit || opt.keep_descriptor || c8) {
+    B200DP_CUDA_TRY(Dbuf.ensure(ps * L * sd.dim));
+    B200DP_CUDA_TRY(dDbuf.ensure(ps * L * sd.dim));
   }
-  for (auto& b : dy_l) B200DP_CUDA_TRY(b.ensure(ps * L * maxfit));
-  for (auto& b : dz_l) B200DP_CUDA_TRY(b.ensure(ps * L * maxfit));
+  if (!tc_fit) {
+    const int nfl = (int)hm.fit.size();
+    th_l.resize(nfl);
+    y_l.resize(nfl);
+    for (int l = 0; l < nfl; ++l) {
+      B200DP_CUDA_TRY(th_l[l].ensure(ps * L * hm.fit[l]));
+      B200DP_CUDA_TRY(y_l[l].ensure(ps * L * hm.fit[l]));
+    }
+    for (auto& b : dy_l) B200DP_CUDA_TRY(b.ensure(ps * L * maxfit));
+    for (auto& b : dz_l) B200DP_CUDA_TRY(b.ensure(ps * L * maxfit));
+  }
   if (c8) {
     // descriptor and its gradient reuse Dbuf / dDbuf (rows in atom order)
     int wmax = 1;
@@ -742,22 +750,26 @@ b200dp_status Engine::compute_device(cudaStream_t st, int nloc, int nghost, cons
     return B200DP_OK;
   }
   if (vl_every > 0 && periodic) {
-    // neighbour reuse: skin candidates rebuilt every vl_every calls (or when
-    // the atom count changes), rows formed from them on every call
-    if (!vl_valid || vl_age >= vl_every || vl_n != nall) {
-      GridSpec gc;
-      switch (b200dp::make_grid(true, box, nullptr, hm.rcut + vl_skin, std::max<long long>(4096, 4LL * nall), gc)) {
-        case 0:
-          break;
-        case 1:
-          err = "degenerate box";
-          return B200DP_ERR_INVALID;
-        default:
-          err = "box narrower than (rcut + skin)/15 along a cell vector";
-          return B200DP_ERR_UNSUPPORTED;
-      }
-      rc = ensure_buffers(nloc, nall, gc.ncells, 0);
-      if (rc != B200DP_OK) return rc;
+    // neighbour reuse: skin candidates built at least every vl_every calls (or
+    // when the atom count changes) and, between those, again on the device
+    // whenever an atom moved more than skin / 2 from the build positions
+    // (the rebuild kernels are gated by the device-side check, so no host
+    // round trip); the rows are formed from the candidates on every call
+    GridSpec gc;
+    switch (b200dp::make_grid(true, box, nullptr, hm.rcut + vl_skin, std::max<long long>(4096, 4LL * nall), gc)) {
+      case 0:
+        break;
+      case 1:
+        err = "degenerate box";
+        return B200DP_ERR_INVALID;
+      default:
+        err = "box narrower than (rcut + skin)/15 along a cell vector";
+        return B200DP_ERR_UNSUPPORTED;
+    }
+    rc = ensure_buffers(nloc, nall, gc.ncells, 0);
+    if (rc != B200DP_OK) return rc;
+    const bool sched = !vl_valid || vl_age >= vl_every || vl_n != nall;
+    if (sched) {
       const double grow = (hm.rcut + vl_skin) / hm.rcut;
       vl_cap = std::max(64, ((int)std::ceil(2.0 * sd.selt * grow * grow * grow) + 31) / 32 * 32);
       B200DP_CUDA_TRY(vl_cj.ensure(sizeof(int) * (size_t)std::max(nloc, 1) * vl_cap));
@@ -769,20 +781,39 @@ b200dp_status Engine::compute_device(cudaStream_t st, int nloc, int nghost, cons
         B200DP_CUDA_TRY(vl_stale.ensure(sizeof(int)));
         B200DP_CUDA_TRY(cudaMemsetAsync(vl_stale.ptr, 0, sizeof(int), st));
       }
-      B200DP_CUDA_TRY(cudaMemsetAsync(cell_count.ptr, 0, sizeof(int) * gc.ncells, st));
-      B200DP_CUDA_TRY(cudaMemsetAsync(cell_cursor.ptr, 0, sizeof(int) * gc.ncells, st));
-      launch_bin(st, nall, d_coord, gc, xw.as<double>(), cell_of.as<int>(), cell_count.as<int>(), vl_ls.as<int>());
-      launch_exclusive_scan(st, gc.ncells, cell_count.as<int>(), cell_start.as<int>(), scan_scratch.as<int>());
-      launch_fill_cells(st, nall, xw.as<double>(), d_atype, cell_of.as<int>(), cell_start.as<int>(),
-                        cell_cursor.as<int>(), cell_rec.as<CellRec>());
-      launch_verlet_build(st, format_spec(nloc, nall), gc, hm.rcut + vl_skin, vl_cap, xw.as<double>(),
-                          cell_of.as<int>(), cell_start.as<int>(), cell_rec.as<CellRec>(), vl_cj.as<int>(),
-                          vl_cc.as<int>(), vl_cnt.as<int>(), err_d);
+      if (!vl_trig.ptr) {
+        B200DP_CUDA_TRY(vl_trig.ensure(16));
+        B200DP_CUDA_TRY(cudaMemsetAsync(vl_trig.ptr, 0, 16, st));
+      }
+      B200DP_CUDA_TRY(cudaMemsetAsync(vl_trig.ptr, 0, 2 * sizeof(int), st));  // both flags
+    }
+    int* trig = vl_trig.as<int>() + (vl_calls & 1);
+    const int* gate = nullptr;
+    if (!sched) {
+      launch_skin_check(st, nall, d_coord, vl_xref.as<double>(), vl_skin, trig, vl_trig.as<int>() + ((vl_calls + 1) & 1));
+      gate = trig;
+    }
+    B200DP_CUDA_TRY(cudaMemsetAsync(cell_count.ptr, 0, sizeof(int) * gc.ncells, st));
+    B200DP_CUDA_TRY(cudaMemsetAsync(cell_cursor.ptr, 0, sizeof(int) * gc.ncells, st));
+    launch_bin(st, nall, d_coord, gc, xw.as<double>(), cell_of.as<int>(), cell_count.as<int>(), vl_ls.as<int>(),
+               gate);
+    launch_exclusive_scan(st, gc.ncells, cell_count.as<int>(), cell_start.as<int>(), scan_scratch.as<int>(), gate);
+    launch_fill_cells(st, nall, xw.as<double>(), d_atype, cell_of.as<int>(), cell_start.as<int>(),
+                      cell_cursor.as<int>(), cell_rec.as<CellRec>(), gate);
+    launch_verlet_build(st, format_spec(nloc, nall), gc, hm.rcut + vl_skin, vl_cap, xw.as<double>(),
+                        cell_of.as<int>(), cell_start.as<int>(), cell_rec.as<CellRec>(), vl_cj.as<int>(),
+                        vl_cc.as<int>(), vl_cnt.as<int>(), err_d, gate);
+    if (sched) {
       B200DP_CUDA_TRY(cudaMemcpyAsync(vl_xref.ptr, d_coord, sizeof(double) * 3 * nall, cudaMemcpyDeviceToDevice, st));
       vl_valid = true;
       vl_age = 0;
       vl_n = nall;
+      ++vl_sched;
+    } else {
+      launch_xref_update(st, nall, d_coord, vl_xref.as<double>(), gate,
+                         reinterpret_cast<unsigned long long*>(vl_trig.as<unsigned char>() + 8));
     }
+    ++vl_calls;
     launch_format_verlet(st, format_spec(nloc, nall), g, vl_cap, vl_skin, d_coord, d_atype, vl_ls.as<int>(),
                          vl_xref.as<double>(), vl_cj.as<int>(), vl_cc.as<int>(), vl_cnt.as<int>(), nl_j.as<int>(),
                          nl_code.as<int>(), nl_rij.as<double>(), nl_cnt.as<int>(), err_d, vl_stale.as<int>());
@@ -835,8 +866,8 @@ b200dp_status Engine::check() {
     if (stale) {
       B200DP_CUDA_TRY(cudaMemset(vl_stale.ptr, 0, sizeof(int)));
       vl_valid = false;
-      err = "neighbour candidates went stale: an atom moved more than skin / 2 between rebuilds "
-            "(rebuild more often or use a larger skin)";
+      err = "neighbour candidates went stale: an atom moved more than skin / 2 from the positions of the "
+            "last build";
       return B200DP_ERR_CAPACITY;
     }
   }
@@ -966,6 +997,19 @@ b200dp_status Engine::fold_finish(cudaStream_t st, int nloc, double* d_force) {
   launch_fold_finish(st, nloc, d_force, reinterpret_cast<unsigned long long*>(pf_buf),
                      reinterpret_cast<unsigned*>(pf_buf + pf_off_nf));
   B200DP_CUDA_TRY(cudaGetLastError());
+  return B200DP_OK;
+}
+
+b200dp_status Engine::neighbor_stats(long long* out) {
+  g_err_sink = &err;
+  if (!out) return B200DP_ERR_INVALID;
+  unsigned long long trig = 0;
+  if (vl_trig.ptr) {
+    if (last_stream_valid()) B200DP_CUDA_TRY(cudaStreamSynchronize(last_stream));
+    B200DP_CUDA_TRY(cudaMemcpy(&trig, vl_trig.as<unsigned char>() + 8, sizeof(trig), cudaMemcpyDeviceToHost));
+  }
+  out[0] = vl_sched;
+  out[1] = (long long)trig;
   return B200DP_OK;
 }
 
@@ -1308,6 +1352,11 @@ b200dp_status b200dp_compute_device_fold(b200dp_engine* engine, void* stream, in
 b200dp_status b200dp_fold_finish(b200dp_engine* engine, void* stream, int nlocal, double* d_force) {
   if (!engine) return B200DP_ERR_INVALID;
   return engine->e.fold_finish(static_cast<cudaStream_t>(stream), nlocal, d_force);
+}
+
+b200dp_status b200dp_neighbor_stats(b200dp_engine* engine, long long* builds) {
+  if (!engine) return B200DP_ERR_INVALID;
+  return engine->e.neighbor_stats(builds);
 }
 
 b200dp_status b200dp_set_neighbor_reuse(b200dp_engine* engine, double skin, int every) {

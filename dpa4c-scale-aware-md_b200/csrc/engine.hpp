@@ -80,9 +80,12 @@ struct Engine {
   std::array<DevBuf, 2> c8_dH, c8_dZ;
   // neighbour reuse (skin candidates kept for `vl_every` periodic calls)
   double vl_skin = 0;
-  int vl_every = 0, vl_age = 0, vl_n = -1, vl_cap = 0;
+  int vl_every = 0, vl_age = 0, vl_n = -1, vl_cap = 0, vl_calls = 0;
+  long long vl_sched = 0;  // scheduled candidate builds
   bool vl_valid = false;
-  DevBuf vl_cj, vl_cc, vl_cnt, vl_xref, vl_ls, vl_stale;
+  // vl_trig: two per-call displacement flags (ints 0, 1) and the count of
+  // displacement-triggered rebuilds (u64 at byte 8)
+  DevBuf vl_cj, vl_cc, vl_cnt, vl_xref, vl_ls, vl_stale, vl_trig;
   // peer fold (domain decomposition): this rank's owned-atom accumulator is
   // exported by CUDA IPC; peers add their ghost edges' reverse contributions
   // into it over NVLink
@@ -142,6 +145,7 @@ struct Engine {
                              double* atom_energy, double* atom_virial);
   b200dp_status check();
   b200dp_status set_neighbor_reuse(double skin, int every);
+  b200dp_status neighbor_stats(long long* out);
   b200dp_status fold_export(int cap, void* handle);
   b200dp_status fold_connect(int nranks, int rank, const void* handles);
   b200dp_status fold_origins(int nghost, const int* d_origin, const double* d_shift);

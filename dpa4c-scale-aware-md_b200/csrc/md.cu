@@ -375,7 +375,8 @@ b200dp_status b200dp_md_create(b200dp_engine* engine, int natoms, const double* 
   }
   auto* md = new b200dp_md();
   md->engine = engine;
-  // skin candidates rebuilt every rebuild_every steps (0 or 1: every step from scratch)
+  // skin candidates rebuilt at least every rebuild_every steps and on any step where an atom moved more
+  // than skin / 2 (decided on the device); 0 or 1: every step from scratch
   if (b200dp_set_neighbor_reuse(engine, p.skin, p.rebuild_every > 1 ? p.rebuild_every : 0) != B200DP_OK) {
     delete md;
     return B200DP_ERR_INVALID;

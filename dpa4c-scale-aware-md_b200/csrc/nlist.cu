@@ -84,7 +84,9 @@ int make_grid(bool periodic, const double* box, const double* region, double rcu
 
 // ---------------------------------------------------------------- binning
 __global__ void k_bin(int nall, const double* __restrict__ coord, GridSpec g, double* __restrict__ xw,
-                      int* __restrict__ cell_of, int* __restrict__ cell_count, int* __restrict__ lshift) {
+                      int* __restrict__ cell_of, int* __restrict__ cell_count, int* __restrict__ lshift,
+                      const int* __restrict__ gate) {
+  if (gate && *gate == 0) return;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= nall) return;
   const double x[3] = {coord[3 * i], coord[3 * i + 1], coord[3 * i + 2]};
@@ -126,10 +128,10 @@ __global__ void k_bin(int nall, const double* __restrict__ coord, GridSpec g, do
 }
 
 void launch_bin(cudaStream_t st, int nall, const double* coord, const GridSpec& g, double* xw, int* cell_of,
-                int* cell_count, int* lshift) {
+                int* cell_count, int* lshift, const int* gate) {
   if (nall <= 0) return;
   count_launch();
-  k_bin<<<(nall + 255) / 256, 256, 0, st>>>(nall, coord, g, xw, cell_of, cell_count, lshift);
+  k_bin<<<(nall + 255) / 256, 256, 0, st>>>(nall, coord, g, xw, cell_of, cell_count, lshift, gate);
 }
 
 // Single-block exclusive scan; out has n+1 entries (out[n] = total).  Each
@@ -139,7 +141,9 @@ void launch_bin(cudaStream_t st, int nall, const double* coord, const GridSpec& 
 constexpr int kScanPer = 8;
 constexpr int kScanPass = 1024 * kScanPer;
 
-__global__ void __launch_bounds__(1024) k_exclusive_scan(int n, const int* __restrict__ in, int* __restrict__ out) {
+__global__ void __launch_bounds__(1024) k_exclusive_scan(int n, const int* __restrict__ in, int* __restrict__ out,
+                                                         const int* __restrict__ gate) {
+  if (gate && *gate == 0) return;
   __shared__ __align__(16) int stage[kScanPass];
   __shared__ int warp_ex[32];
   __shared__ int block_total;
@@ -206,7 +210,9 @@ __global__ void __launch_bounds__(1024) k_exclusive_scan(int n, const int* __res
 // a per-tile scan that adds the tile's offset (fixed order, deterministic).
 constexpr int kScanTile = 4096;
 
-__global__ void __launch_bounds__(1024) k_scan_tile_sums(int n, const int* __restrict__ in, int* __restrict__ sums) {
+__global__ void __launch_bounds__(1024) k_scan_tile_sums(int n, const int* __restrict__ in, int* __restrict__ sums,
+                                                         const int* __restrict__ gate) {
+  if (gate && *gate == 0) return;
   __shared__ int warp_tot[32];
   const int base = blockIdx.x * kScanTile;
   int local = 0;
@@ -221,7 +227,9 @@ __global__ void __launch_bounds__(1024) k_scan_tile_sums(int n, const int* __res
 }
 
 __global__ void __launch_bounds__(1024) k_scan_tile_apply(int n, const int* __restrict__ in,
-                                                          const int* __restrict__ offs, int* __restrict__ out) {
+                                                          const int* __restrict__ offs, int* __restrict__ out,
+                                                          const int* __restrict__ gate) {
+  if (gate && *gate == 0) return;
   __shared__ int warp_ex[32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int i0 = blockIdx.x * kScanTile + tid * 4;
@@ -252,28 +260,29 @@ __global__ void __launch_bounds__(1024) k_scan_tile_apply(int n, const int* __re
 
 size_t scan_scratch_ints(int n) { return 2 * ((size_t)n / kScanTile + 2); }
 
-void launch_exclusive_scan(cudaStream_t st, int n, const int* in, int* out, int* scratch) {
+void launch_exclusive_scan(cudaStream_t st, int n, const int* in, int* out, int* scratch, const int* gate) {
   const int nb = (n + kScanTile - 1) / kScanTile;
   if (nb <= 8 || scratch == nullptr) {
     count_launch();
-    k_exclusive_scan<<<1, 1024, 0, st>>>(n, in, out);
+    k_exclusive_scan<<<1, 1024, 0, st>>>(n, in, out, gate);
     return;
   }
   int* sums = scratch;
   int* offs = scratch + nb + 1;
   count_launch();
-  k_scan_tile_sums<<<nb, 1024, 0, st>>>(n, in, sums);
+  k_scan_tile_sums<<<nb, 1024, 0, st>>>(n, in, sums, gate);
   count_launch();
-  k_exclusive_scan<<<1, 1024, 0, st>>>(nb, sums, offs);
+  k_exclusive_scan<<<1, 1024, 0, st>>>(nb, sums, offs, gate);
   count_launch();
-  k_scan_tile_apply<<<nb, 1024, 0, st>>>(n, in, offs, out);
+  k_scan_tile_apply<<<nb, 1024, 0, st>>>(n, in, offs, out, gate);
 }
 
 // Order within a cell follows the atomics and is not fixed; the list kernel's
 // ranking does not depend on it.
 __global__ void k_fill_cells(int nall, const double* __restrict__ xw, const int* __restrict__ atype,
                              const int* __restrict__ cell_of, const int* __restrict__ cell_start,
-                             int* __restrict__ cursor, CellRec* __restrict__ cell_rec) {
+                             int* __restrict__ cursor, CellRec* __restrict__ cell_rec, const int* __restrict__ gate) {
+  if (gate && *gate == 0) return;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= nall) return;
   const int c = cell_of[i];
@@ -287,10 +296,10 @@ __global__ void k_fill_cells(int nall, const double* __restrict__ xw, const int*
 }
 
 void launch_fill_cells(cudaStream_t st, int nall, const double* xw, const int* atype, const int* cell_of,
-                       const int* cell_start, int* cursor, CellRec* cell_rec) {
+                       const int* cell_start, int* cursor, CellRec* cell_rec, const int* gate) {
   if (nall <= 0) return;
   count_launch();
-  k_fill_cells<<<(nall + 255) / 256, 256, 0, st>>>(nall, xw, atype, cell_of, cell_start, cursor, cell_rec);
+  k_fill_cells<<<(nall + 255) / 256, 256, 0, st>>>(nall, xw, atype, cell_of, cell_start, cursor, cell_rec, gate);
 }
 
 // ---------------------------------------------------------------- format
@@ -629,7 +638,8 @@ __global__ void __launch_bounds__(kFmtWarps * 32)
     k_verlet_build(FormatSpec f, GridSpec g, double rcand2, int capS, const double* __restrict__ xw,
                    const int* __restrict__ cell_of, const int* __restrict__ cell_start,
                    const CellRec* __restrict__ cell_rec, int* __restrict__ cand_j, int* __restrict__ cand_code,
-                   int* __restrict__ cand_cnt, int* __restrict__ err) {
+                   int* __restrict__ cand_cnt, int* __restrict__ err, const int* __restrict__ gate) {
+  if (gate && *gate == 0) return;
   __shared__ int s_start[kFmtWarps][kStencilChunk], s_pref[kFmtWarps][kStencilChunk], s_code[kFmtWarps][kStencilChunk];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int i = blockIdx.x * kFmtWarps + warp;
@@ -723,11 +733,54 @@ __global__ void __launch_bounds__(kFmtWarps * 32)
 
 void launch_verlet_build(cudaStream_t st, const FormatSpec& f, const GridSpec& g, double rcand, int capS,
                          const double* xw, const int* cell_of, const int* cell_start, const CellRec* cell_rec,
-                         int* cand_j, int* cand_code, int* cand_cnt, int* err) {
+                         int* cand_j, int* cand_code, int* cand_cnt, int* err, const int* gate) {
   if (f.nloc <= 0) return;
   count_launch();
   k_verlet_build<<<(f.nloc + kFmtWarps - 1) / kFmtWarps, kFmtWarps * 32, 0, st>>>(
-      f, g, rcand * rcand, capS, xw, cell_of, cell_start, cell_rec, cand_j, cand_code, cand_cnt, err);
+      f, g, rcand * rcand, capS, xw, cell_of, cell_start, cell_rec, cand_j, cand_code, cand_cnt, err, gate);
+}
+
+// Displacement check of every atom against the positions the candidates were
+// built from: sets *trig when one moved more than skin / 2, and clears the
+// other call's flag (its readers have completed: same stream).
+__global__ void k_skin_check(int n, const double* __restrict__ x, const double* __restrict__ xref, double half_skin2,
+                             int* __restrict__ trig, int* __restrict__ trig_prev) {
+  if (blockIdx.x == 0 && threadIdx.x == 0) *trig_prev = 0;
+  bool moved = false;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    double d2 = 0;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      const double d = x[3 * i + k] - xref[3 * i + k];
+      d2 += d * d;
+    }
+    moved |= d2 > half_skin2;
+  }
+  if (__syncthreads_or(moved) && threadIdx.x == 0) atomicOr(trig, 1);
+}
+
+// When *gate: the reference positions become x and the rebuild is counted.
+__global__ void k_xref_update(int n, const double* __restrict__ x, double* __restrict__ xref,
+                              const int* __restrict__ gate, unsigned long long* __restrict__ count) {
+  if (*gate == 0) return;
+  if (blockIdx.x == 0 && threadIdx.x == 0) ++*count;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < 3 * n; i += gridDim.x * blockDim.x) xref[i] = x[i];
+}
+
+void launch_skin_check(cudaStream_t st, int n, const double* x, const double* xref, double skin, int* trig,
+                       int* trig_prev) {
+  if (n <= 0) return;
+  count_launch();
+  const int blocks = std::min((n + 255) / 256, 148 * 8);
+  k_skin_check<<<blocks, 256, 0, st>>>(n, x, xref, 0.25 * skin * skin, trig, trig_prev);
+}
+
+void launch_xref_update(cudaStream_t st, int n, const double* x, double* xref, const int* gate,
+                        unsigned long long* count) {
+  if (n <= 0) return;
+  count_launch();
+  const int blocks = std::min((3 * n + 255) / 256, 148 * 8);
+  k_xref_update<<<blocks, 256, 0, st>>>(n, x, xref, gate, count);
 }
 
 void launch_format_verlet(cudaStream_t st, const FormatSpec& f, const GridSpec& g, int capS, double skin,

@@ -60,17 +60,20 @@ void format_caps(FormatSpec& f);
 // Host helpers (identical arithmetic to the oracle's cell set-up).
 void make_box_inverse(const double* box, double* Binv, double* width);
 
-// Launchers; all enqueue on `st`.
+// Launchers; all enqueue on `st`.  `gate` (optional, device int): the
+// kernels do nothing when *gate == 0, so a rebuild can be decided on the
+// device without a host round trip.
 // lshift (optional, periodic): the integer lattice shift f of each atom's
 // wrap, x_wrapped = x - f . cell.
 void launch_bin(cudaStream_t st, int nall, const double* coord, const GridSpec& g, double* xw, int* cell_of,
-                int* cell_count, int* lshift = nullptr);
+                int* cell_count, int* lshift = nullptr, const int* gate = nullptr);
 // Exclusive scan of n ints into out[0..n] (out[n] = total).  scratch holds
 // scan_scratch_ints(n) ints; with scratch == nullptr a single block is used.
-void launch_exclusive_scan(cudaStream_t st, int n, const int* in, int* out, int* scratch);
+void launch_exclusive_scan(cudaStream_t st, int n, const int* in, int* out, int* scratch,
+                           const int* gate = nullptr);
 size_t scan_scratch_ints(int n);
 void launch_fill_cells(cudaStream_t st, int nall, const double* xw, const int* atype, const int* cell_of,
-                       const int* cell_start, int* cursor, CellRec* cell_rec);
+                       const int* cell_start, int* cursor, CellRec* cell_rec, const int* gate = nullptr);
 size_t format_smem_bytes(const FormatSpec& f);
 void launch_format(cudaStream_t st, const FormatSpec& f, const GridSpec& g, const double* xw, const int* cell_of,
                    const int* cell_start, const CellRec* cell_rec, int* nl_j, int* nl_code, double* nl_rij,
@@ -82,7 +85,13 @@ void launch_format(cudaStream_t st, const FormatSpec& f, const GridSpec& g, cons
 // sets *stale.
 void launch_verlet_build(cudaStream_t st, const FormatSpec& f, const GridSpec& g, double rcand, int capS,
                          const double* xw, const int* cell_of, const int* cell_start, const CellRec* cell_rec,
-                         int* cand_j, int* cand_code, int* cand_cnt, int* err);
+                         int* cand_j, int* cand_code, int* cand_cnt, int* err, const int* gate = nullptr);
+// *trig |= (some atom moved more than skin / 2 from xref); *trig_prev = 0.
+void launch_skin_check(cudaStream_t st, int n, const double* x, const double* xref, double skin, int* trig,
+                       int* trig_prev);
+// If *gate: xref = x and ++*count.
+void launch_xref_update(cudaStream_t st, int n, const double* x, double* xref, const int* gate,
+                        unsigned long long* count);
 void launch_format_verlet(cudaStream_t st, const FormatSpec& f, const GridSpec& g, int capS, double skin,
                           const double* x, const int* atype, const int* lshift, const double* xref,
                           const int* cand_j, const int* cand_code, const int* cand_cnt, int* nl_j, int* nl_code,

@@ -569,11 +569,12 @@ __global__ void __launch_bounds__(kAsmWarps * 32)
   __shared__ double s_part[kAsmWarps][kAsmCols];
   __shared__ int s_last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int i = blockIdx.x * kAsmWarps + warp;
-  double f[3] = {0, 0, 0};
   double v[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
   double e = 0;
-  if (i < nloc) {
+  // a fixed grid strides over the atoms: the same atoms land in the same
+  // block's sums on every call, and the final reduction stays short
+  for (int i = blockIdx.x * kAsmWarps + warp; i < nloc; i += gridDim.x * kAsmWarps) {
+    double f[3] = {0, 0, 0};
     const size_t row = (size_t)i * selt;
     for (int s = lane; s < selt; s += 32) {
       const int j = nl_j[row + s];
@@ -609,18 +610,18 @@ __global__ void __launch_bounds__(kAsmWarps * 32)
         if (!finite) atomicOr((fold.own && j < nloc ? fold.own_nf : nonfinite) + j, 1u);
       }
     }
-    if (lane == 0) e = atom_e[i];
-  }
+    if (lane == 0) e += atom_e[i];
 #pragma unroll
-  for (int c = 0; c < 3; ++c) f[c] = warp_sum(f[c]);
-#pragma unroll
-  for (int c = 0; c < 9; ++c) v[c] = warp_sum(v[c]);
-  if (lane == 0) {
-    if (i < nloc) {
+    for (int c = 0; c < 3; ++c) f[c] = warp_sum(f[c]);
+    if (lane == 0) {
       force[3 * (size_t)i] = f[0];
       force[3 * (size_t)i + 1] = f[1];
       force[3 * (size_t)i + 2] = f[2];
     }
+  }
+#pragma unroll
+  for (int c = 0; c < 9; ++c) v[c] = warp_sum(v[c]);
+  if (lane == 0) {
 #pragma unroll
     for (int c = 0; c < 9; ++c) s_part[warp][c] = v[c];
     s_part[warp][9] = e;
@@ -682,7 +683,7 @@ __global__ void k_assemble_finish(int nloc, int nall, double* __restrict__ force
   }
 }
 
-int assemble_blocks(int nloc) { return std::max(1, (nloc + kAsmWarps - 1) / kAsmWarps); }
+int assemble_blocks(int nloc) { return std::max(1, std::min((nloc + kAsmWarps - 1) / kAsmWarps, 148 * 8)); }
 
 void launch_assemble(cudaStream_t st, int nloc, int nall, int selt, const int* nl_j, const double* gslot,
                      const double* rij, const double* atom_e, double* force, double* atom_virial,

@@ -225,15 +225,20 @@ typedef enum b200dp_md_ensemble { B200DP_MD_NVE = 0, B200DP_MD_NVT = 1, B200DP_M
 
 /* Neighbour reuse for periodic calls (nghost == 0, box given) of
  * b200dp_compute_device / b200dp_compute_host: candidate pairs within
- * rcut + skin are built on one call and reused by the next every - 1 calls,
- * whose neighbour rows are formed from them with the new positions (like a
- * LAMMPS skin list rebuilt every `every` steps; the rows themselves stay the
- * exact per-type rcut rows).  An atom that moves more than skin / 2 between
- * rebuilds makes b200dp_check return B200DP_ERR_CAPACITY and forces a
- * rebuild.  every = 0 turns reuse off (the default: every call bins from
- * scratch).  Replaces the LAMMPS skin neighbour list and its rebuild cadence
- * (LO/KOKKOS/npair_kokkos.cpp:151-460 with neigh_modify every / check). */
+ * rcut + skin are built on one call and reused by the following calls, whose
+ * neighbour rows are formed from them with the new positions (the rows
+ * themselves stay the exact per-type rcut rows).  The candidates are built
+ * again at least every `every` calls, and on any call where an atom has moved
+ * more than skin / 2 from the positions of the last build -- that check and
+ * the rebuild run on the device inside the call, with no host round trip
+ * (LAMMPS neigh_modify every N check yes, with the check on every step).
+ * every = 0 turns reuse off (the default: every call bins from scratch).
+ * Replaces the LAMMPS skin neighbour list and its rebuild decision
+ * (LO/KOKKOS/npair_kokkos.cpp:151-460; neighbor->decide()). */
 b200dp_status b200dp_set_neighbor_reuse(b200dp_engine* engine, double skin, int every);
+/* builds[0] = scheduled candidate builds, builds[1] = builds triggered by the
+ * displacement check (synchronises the engine's last stream). */
+b200dp_status b200dp_neighbor_stats(b200dp_engine* engine, long long* builds);
 
 /* Halo exchange and reverse fold for spatial domain decomposition, one
  * process per GPU on NVLink peers, through one device buffer per rank that
@@ -287,7 +292,8 @@ typedef struct b200dp_md_params {
   double p_target;  /* bar (NPT, isotropic) */
   double p_damp;    /* barostat period, ps (NPT, default 0.5) */
   int pchain;       /* barostat Nose-Hoover chain length (NPT, 1..8, default 3) */
-  int rebuild_every; /* neighbour candidates rebuilt every this many steps (default 10; 0 = every step) */
+  int rebuild_every; /* neighbour candidates rebuilt at least every this many steps and whenever an atom
+                        moved more than skin / 2 (default 10; 0 = every step from scratch) */
   double skin;       /* Angstrom, neighbour skin for the reuse (default 2.0) */
   int reserved[8];
 } b200dp_md_params;

@@ -120,7 +120,7 @@ def test_fold_self_exchange_on_one_gpu(model_dir):
     dp.close()
 
 
-@pytest.mark.parametrize("grid,mol", [((2, 1, 1), (8, 4, 4)), ((2, 2, 1), (8, 8, 4))])
+@pytest.mark.parametrize("grid,mol", [((2, 1, 1), (8, 4, 4)), ((2, 2, 1), (8, 8, 4)), ((2, 2, 2), (8, 8, 8))])
 def test_fold_gloo_ranks_sharing_one_gpu(tmp_path, model_dir, grid, mol):
     model = str(model_dir / "water.b2dp")
     s, ref = periodic(model, mol, b200dp.FP64)
