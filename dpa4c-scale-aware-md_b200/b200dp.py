@@ -34,7 +34,8 @@ EXPORTS = [
     "b200dp_compute_device_fold", "b200dp_fold_finish", "b200dp_halo_publish", "b200dp_halo_gather",
     "b200dp_stage_times", "b200dp_kernel_launches", "b200dp_selftest_mma", "b200dp_build_nlist_noalloc",
     "b200dp_direct_bind", "b200dp_direct_energy_force", "b200dp_md_params_default", "b200dp_md_create",
-    "b200dp_md_run", "b200dp_md_thermo", "b200dp_md_state", "b200dp_md_destroy",
+    "b200dp_md_run", "b200dp_md_thermo", "b200dp_md_state", "b200dp_md_destroy", "b200dp_md_snapshot_bytes",
+    "b200dp_md_snapshot", "b200dp_md_restore", "b200dp_md_write_restart", "b200dp_md_read_restart",
 ]
 
 NVE, NVT, NPT = 0, 1, 2
@@ -127,6 +128,11 @@ def load_library(path: str = LIB_PATH):
     L.b200dp_md_thermo.argtypes = [_vp, _dp]
     L.b200dp_md_state.argtypes = [_vp, _dp, _dp, _dp]
     L.b200dp_md_destroy.argtypes = [_vp]
+    L.b200dp_md_snapshot_bytes.argtypes = [_vp, ctypes.POINTER(ctypes.c_size_t)]
+    L.b200dp_md_snapshot.argtypes = [_vp, _vp]
+    L.b200dp_md_restore.argtypes = [_vp, _vp]
+    L.b200dp_md_write_restart.argtypes = [_vp, ctypes.c_char_p]
+    L.b200dp_md_read_restart.argtypes = [_vp, ctypes.c_char_p]
     L.b200dp_direct_energy_force.restype = ctypes.c_int
     L.b200dp_direct_energy_force.argtypes = [_vp, _vp, _vp, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                              _vp, _vp, _vp]
@@ -351,6 +357,28 @@ class MD:
         if rc != 0:
             raise B200DPError(rc, self.dp.L.b200dp_last_error(self.dp.h).decode())
         return x, v, f
+
+    def _check(self, rc):
+        if rc != 0:
+            raise B200DPError(rc, self.dp.L.b200dp_last_error(self.dp.h).decode())
+
+    def snapshot_bytes(self) -> int:
+        n = ctypes.c_size_t()
+        self._check(self.L.b200dp_md_snapshot_bytes(self.h, ctypes.byref(n)))
+        return int(n.value)
+
+    def snapshot(self, buf_ptr: int) -> None:
+        """Enqueues a copy of the whole integrator state into device memory at buf_ptr."""
+        self._check(self.L.b200dp_md_snapshot(self.h, buf_ptr))
+
+    def restore(self, buf_ptr: int) -> None:
+        self._check(self.L.b200dp_md_restore(self.h, buf_ptr))
+
+    def write_restart(self, path: str) -> None:
+        self._check(self.L.b200dp_md_write_restart(self.h, os.fsencode(path)))
+
+    def read_restart(self, path: str) -> None:
+        self._check(self.L.b200dp_md_read_restart(self.h, os.fsencode(path)))
 
     def close(self):
         if getattr(self, "h", None):

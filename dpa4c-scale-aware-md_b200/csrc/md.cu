@@ -34,6 +34,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
+#include <cstdio>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -315,6 +316,42 @@ struct Rng {
 
 using namespace b200dp;
 
+namespace b200dp {
+namespace {
+// Restart snapshot: this header (host scalars of the integrator), then the
+// device state, each section 256-byte aligned.  Device-resident snapshots
+// are taken on the MD stream without a host round trip; a restart file is the
+// same byte image.
+struct SnapHeader {
+  char magic[8];
+  int n, ensemble;
+  long long step;
+  double box[9], volume, dof;
+  HostChain tch, pch;
+  ChainParams cp;
+  double omega_dot, w_mass, vol0, t_current, vir_trace, epot;
+  double dt;
+  unsigned long long bytes;
+};
+constexpr char kSnapMagic[8] = {'B', '2', 'D', 'P', 'M', 'D', 'S', '1'};
+constexpr size_t snap_align(size_t b) { return (b + 255) & ~(size_t)255; }
+struct SnapLayout {
+  size_t x, v, f, e, vir, part, chain, total;
+  explicit SnapLayout(int n) {
+    const size_t n3 = sizeof(double) * 3 * (size_t)n;
+    x = snap_align(sizeof(SnapHeader));
+    v = x + snap_align(n3);
+    f = v + snap_align(n3);
+    e = f + snap_align(n3);
+    vir = e + snap_align(sizeof(double));
+    part = vir + snap_align(9 * sizeof(double));
+    chain = part + snap_align(kRedBlocks * sizeof(double));
+    total = chain + snap_align(sizeof(Chain));
+  }
+};
+}  // namespace
+}  // namespace b200dp
+
 struct b200dp_md {
   b200dp_engine* engine = nullptr;
   b200dp_md_params p{};
@@ -330,6 +367,7 @@ struct b200dp_md {
   HostChain tch, pch;
   double omega_dot = 0, w_mass = 0, vol0 = 0, t_current = 0, vir_trace = 0, epot = 0;
   std::string err;
+  SnapHeader snap_stage{};
 };
 
 extern "C" {
@@ -637,6 +675,128 @@ b200dp_status b200dp_md_state(b200dp_md* md, double* coord, double* vel, double*
       cudaStreamSynchronize(md->stream) != cudaSuccess)
     return B200DP_ERR_CUDA;
   return b200dp_check(md->engine);
+}
+
+b200dp_status b200dp_md_snapshot_bytes(const b200dp_md* md, size_t* bytes) {
+  if (!md || !bytes) return B200DP_ERR_INVALID;
+  *bytes = SnapLayout(md->n).total;
+  return B200DP_OK;
+}
+
+b200dp_status b200dp_md_snapshot(b200dp_md* md, void* d_buf) {
+  if (!md || !d_buf) return B200DP_ERR_INVALID;
+  const SnapLayout L(md->n);
+  SnapHeader& h = md->snap_stage;
+  std::memset(&h, 0, sizeof(h));
+  std::memcpy(h.magic, kSnapMagic, sizeof(h.magic));
+  h.n = md->n;
+  h.ensemble = md->ensemble;
+  h.step = md->step;
+  std::memcpy(h.box, md->box, sizeof(h.box));
+  h.volume = md->volume;
+  h.dof = md->dof;
+  h.tch = md->tch;
+  h.pch = md->pch;
+  h.cp = md->cp;
+  h.omega_dot = md->omega_dot;
+  h.w_mass = md->w_mass;
+  h.vol0 = md->vol0;
+  h.t_current = md->t_current;
+  h.vir_trace = md->vir_trace;
+  h.epot = md->epot;
+  h.dt = md->p.dt;
+  h.bytes = L.total;
+  auto* b = static_cast<unsigned char*>(d_buf);
+  const size_t n3 = sizeof(double) * 3 * (size_t)md->n;
+  cudaStream_t st = md->stream;
+  const auto d2d = cudaMemcpyDeviceToDevice;
+  if (cudaMemcpyAsync(b, &h, sizeof(h), cudaMemcpyHostToDevice, st) != cudaSuccess ||
+      cudaMemcpyAsync(b + L.x, md->x.p, n3, d2d, st) != cudaSuccess ||
+      cudaMemcpyAsync(b + L.v, md->v.p, n3, d2d, st) != cudaSuccess ||
+      cudaMemcpyAsync(b + L.f, md->f.p, n3, d2d, st) != cudaSuccess ||
+      cudaMemcpyAsync(b + L.e, md->e.p, sizeof(double), d2d, st) != cudaSuccess ||
+      cudaMemcpyAsync(b + L.vir, md->vir.p, 9 * sizeof(double), d2d, st) != cudaSuccess ||
+      cudaMemcpyAsync(b + L.part, md->part.p, kRedBlocks * sizeof(double), d2d, st) != cudaSuccess ||
+      cudaMemcpyAsync(b + L.chain, md->chain.p, sizeof(Chain), d2d, st) != cudaSuccess)
+    return B200DP_ERR_CUDA;
+  return B200DP_OK;
+}
+
+b200dp_status b200dp_md_restore(b200dp_md* md, const void* d_buf) {
+  if (!md || !d_buf) return B200DP_ERR_INVALID;
+  const SnapLayout L(md->n);
+  const auto* b = static_cast<const unsigned char*>(d_buf);
+  SnapHeader h;
+  cudaStream_t st = md->stream;
+  if (cudaMemcpyAsync(&h, b, sizeof(h), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return B200DP_ERR_CUDA;
+  if (std::memcmp(h.magic, kSnapMagic, sizeof(h.magic)) != 0 || h.n != md->n || h.ensemble != md->ensemble ||
+      h.bytes != L.total || h.dt != md->p.dt)
+    return B200DP_ERR_INVALID;  // not a snapshot of this system and integrator
+  const size_t n3 = sizeof(double) * 3 * (size_t)md->n;
+  const auto d2d = cudaMemcpyDeviceToDevice;
+  if (cudaMemcpyAsync(md->x.p, b + L.x, n3, d2d, st) != cudaSuccess ||
+      cudaMemcpyAsync(md->v.p, b + L.v, n3, d2d, st) != cudaSuccess ||
+      cudaMemcpyAsync(md->f.p, b + L.f, n3, d2d, st) != cudaSuccess ||
+      cudaMemcpyAsync(md->e.p, b + L.e, sizeof(double), d2d, st) != cudaSuccess ||
+      cudaMemcpyAsync(md->vir.p, b + L.vir, 9 * sizeof(double), d2d, st) != cudaSuccess ||
+      cudaMemcpyAsync(md->part.p, b + L.part, kRedBlocks * sizeof(double), d2d, st) != cudaSuccess ||
+      cudaMemcpyAsync(md->chain.p, b + L.chain, sizeof(Chain), d2d, st) != cudaSuccess)
+    return B200DP_ERR_CUDA;
+  md->step = h.step;
+  std::memcpy(md->box, h.box, sizeof(md->box));
+  md->volume = h.volume;
+  md->dof = h.dof;
+  md->tch = h.tch;
+  md->pch = h.pch;
+  md->cp = h.cp;
+  md->omega_dot = h.omega_dot;
+  md->w_mass = h.w_mass;
+  md->vol0 = h.vol0;
+  md->t_current = h.t_current;
+  md->vir_trace = h.vir_trace;
+  md->epot = h.epot;
+  // candidates are rebuilt from the restored positions on the next step
+  return b200dp_set_neighbor_reuse(md->engine, md->p.skin, md->p.rebuild_every > 1 ? md->p.rebuild_every : 0);
+}
+
+b200dp_status b200dp_md_write_restart(b200dp_md* md, const char* path) {
+  if (!md || !path) return B200DP_ERR_INVALID;
+  const SnapLayout L(md->n);
+  void* d = nullptr;
+  if (cudaMalloc(&d, L.total) != cudaSuccess) return B200DP_ERR_CUDA;
+  std::vector<unsigned char> host(L.total);
+  b200dp_status rc = b200dp_md_snapshot(md, d);
+  if (rc == B200DP_OK && (cudaMemcpyAsync(host.data(), d, L.total, cudaMemcpyDeviceToHost, md->stream) != cudaSuccess ||
+                          cudaStreamSynchronize(md->stream) != cudaSuccess))
+    rc = B200DP_ERR_CUDA;
+  cudaFree(d);
+  if (rc != B200DP_OK) return rc;
+  FILE* fp = std::fopen(path, "wb");
+  if (!fp) return B200DP_ERR_IO;
+  const bool ok = std::fwrite(host.data(), 1, host.size(), fp) == host.size();
+  if (std::fclose(fp) != 0 || !ok) return B200DP_ERR_IO;
+  return b200dp_check(md->engine);
+}
+
+b200dp_status b200dp_md_read_restart(b200dp_md* md, const char* path) {
+  if (!md || !path) return B200DP_ERR_INVALID;
+  const SnapLayout L(md->n);
+  std::vector<unsigned char> host(L.total);
+  FILE* fp = std::fopen(path, "rb");
+  if (!fp) return B200DP_ERR_IO;
+  const bool ok = std::fread(host.data(), 1, host.size(), fp) == host.size() && std::fgetc(fp) == EOF;
+  std::fclose(fp);
+  if (!ok) return B200DP_ERR_IO;
+  void* d = nullptr;
+  if (cudaMalloc(&d, L.total) != cudaSuccess) return B200DP_ERR_CUDA;
+  b200dp_status rc = B200DP_OK;
+  if (cudaMemcpyAsync(d, host.data(), L.total, cudaMemcpyHostToDevice, md->stream) != cudaSuccess) rc = B200DP_ERR_CUDA;
+  if (rc == B200DP_OK) rc = b200dp_md_restore(md, d);
+  if (cudaStreamSynchronize(md->stream) != cudaSuccess && rc == B200DP_OK) rc = B200DP_ERR_CUDA;
+  cudaFree(d);
+  return rc;
 }
 
 b200dp_status b200dp_md_destroy(b200dp_md* md) {

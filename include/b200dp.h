@@ -32,6 +32,7 @@
 #ifndef B200DP_H
 #define B200DP_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -315,6 +316,23 @@ b200dp_status b200dp_md_thermo(b200dp_md* md, double* thermo);
 /* Waits for the driver's stream and copies positions / velocities / forces
  * (host arrays of natoms*3, any may be NULL). */
 b200dp_status b200dp_md_state(b200dp_md* md, double* coord, double* vel, double* force);
+/* Restart.  A snapshot is the run's complete integrator state (positions,
+ * velocities, forces, energy and virial of the last force call, thermostat
+ * and barostat chains, box, step) in one device buffer of
+ * b200dp_md_snapshot_bytes bytes: b200dp_md_snapshot enqueues the copies on
+ * the MD stream (no host synchronisation: the run continues while the buffer
+ * is kept in HBM or copied out); b200dp_md_restore puts a snapshot of the
+ * same system and integrator settings back (B200DP_ERR_INVALID otherwise),
+ * after which b200dp_md_run continues the trajectory -- bitwise with
+ * rebuild_every <= 1, within fp64 round-off of the neighbour vectors with
+ * skin reuse (the candidates are rebuilt from the restored positions).  The
+ * restart file is the snapshot's byte image.  Replaces the reference's
+ * device-side restart packing (src/runtime/device_restart.cu). */
+b200dp_status b200dp_md_snapshot_bytes(const b200dp_md* md, size_t* bytes);
+b200dp_status b200dp_md_snapshot(b200dp_md* md, void* d_buf);
+b200dp_status b200dp_md_restore(b200dp_md* md, const void* d_buf);
+b200dp_status b200dp_md_write_restart(b200dp_md* md, const char* path);
+b200dp_status b200dp_md_read_restart(b200dp_md* md, const char* path);
 b200dp_status b200dp_md_destroy(b200dp_md* md);
 
 /* Total kernels this library has launched in the process (all engines). */

@@ -10,8 +10,10 @@ the reference, so these checks use properties that hold at any size:
   * a rigid translation of every atom leaves energy and forces unchanged up to
     round-off of the shifted coordinates.
 Config 2 is FCC copper 32^3 cells (131,072 atoms), config 3 the 4-type BCC
-alloy 64^3 x 2 (524,288 atoms), config 4 water at 98,304 atoms (the 786 k and
-3.1 M water systems and the slab run in the benchmark path only).
+alloy 64^3 x 2 (524,288 atoms), config 4 water at 98,304 and 786,432 atoms and
+the 786,432-atom slab with 50 % vacuum.  The 3,145,728-atom water box does not
+fit the fp64 engine on one GPU; it is held to the mixed-mode properties (total
+force, determinism, rigid translation, no sel overflow).
 """
 import numpy as np
 import pytest
@@ -22,7 +24,9 @@ from conftest import TOLERANCES
 
 pytestmark = [pytest.mark.gpu, pytest.mark.slow]
 
-CASES = [("c2", systems.config2, "cu"), ("c3", systems.config3, "alloy"), ("c4_98k", lambda: systems.config4("98k"), "water")]
+CASES = [("c2", systems.config2, "cu"), ("c3", systems.config3, "alloy"), ("c4_98k", lambda: systems.config4("98k"), "water"),
+         ("c4_786k", lambda: systems.config4("786k"), "water"),
+         ("c4_786k_slab", lambda: systems.config4("786k-slab"), "water")]
 
 
 @pytest.mark.parametrize("name,make,kind", CASES)
@@ -57,3 +61,23 @@ def test_full_size_properties(model_dir, name, make, kind):
     for dp in (d64, dmx):
         assert dp.sel_overflow_count() == 0
         dp.close()
+
+
+def test_3m_water_mixed_properties(model_dir):
+    s = systems.config4("3.1M")
+    dp = b200dp.DeepPot(str(model_dir / "water.b2dp"), precision=b200dp.MIXED)
+    r = dp.compute(s.coord, s.atype, s.box)
+    n = s.natoms
+    fscale = np.abs(r["force"]).max()
+    assert np.isfinite(r["force"]).all() and np.isfinite(r["energy"])
+    # every edge's gradient enters its two atoms with opposite signs (fixed-point sums)
+    assert np.abs(r["force"].sum(0)).max() < 1e-9 * fscale * np.sqrt(n)
+    again = dp.compute(s.coord, s.atype, s.box)
+    assert again["energy"] == r["energy"]
+    assert np.array_equal(again["force"], r["force"])
+    shifted = dp.compute(s.coord + np.array([0.37, -1.11, 2.03]), s.atype, s.box)
+    assert abs(shifted["energy"] - r["energy"]) / n < TOLERANCES["energy_per_atom"]
+    err = shifted["force"] - r["force"]
+    assert np.sqrt((err ** 2).mean()) < TOLERANCES["force_rmse"]
+    assert dp.sel_overflow_count() == 0
+    dp.close()

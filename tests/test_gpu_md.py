@@ -158,3 +158,74 @@ def test_npt_conserved_energy(model_dir):
     assert th["volume"] > 0
     md.close()
     dp.close()
+
+
+def _md(model, ensemble, every, s=None):
+    s = s or systems.config0()
+    dp = b200dp.DeepPot(model, precision=b200dp.FP64)
+    md = b200dp.MD(dp, s.coord, s.atype, s.box, [m * 4 for m in MASS], dt=0.0005, ensemble=ensemble, t_init=300.0,
+                   t_target=300.0, seed=5, p_target=1.0, rebuild_every=every, skin=2.0)
+    return dp, md
+
+
+@pytest.mark.parametrize("ensemble,every", [(b200dp.NVT, 0), (b200dp.NPT, 0), (b200dp.NVT, 10)])
+def test_snapshot_restore_continues_the_run(model_dir, ensemble, every):
+    """Snapshot into device memory, run on, restore, run again: the same trajectory
+    (bitwise with every-step neighbour builds; with skin reuse the candidates are
+    rebuilt from the restored positions, so to fp64 round-off)."""
+    import torch
+
+    model = str(model_dir / "water.b2dp")
+    dp, md = _md(model, ensemble, every)
+    md.run(7)
+    buf = torch.empty(md.snapshot_bytes(), dtype=torch.uint8, device="cuda:0")
+    md.snapshot(buf.data_ptr())
+    md.run(15)
+    ta = md.thermo()
+    xa, va, fa = md.state()
+    md.restore(buf.data_ptr())
+    assert md.thermo()["step"] == 7
+    md.run(15)
+    tb = md.thermo()
+    xb, vb, fb = md.state()
+    dp.check()
+    if every == 0:
+        assert np.array_equal(xa, xb) and np.array_equal(va, vb) and np.array_equal(fa, fb)
+        assert ta == tb
+    else:
+        assert np.abs(xa - xb).max() < 1e-10
+        assert np.abs(va - vb).max() < 1e-10
+        assert abs(ta["conserved"] - tb["conserved"]) <= 1e-10 * abs(ta["conserved"])
+    md.close()
+    dp.close()
+
+
+def test_restart_file_in_a_new_run(model_dir, tmp_path):
+    model = str(model_dir / "water.b2dp")
+    dp, md = _md(model, b200dp.NPT, 0)
+    md.run(9)
+    path = str(tmp_path / "md.restart")
+    md.write_restart(path)
+    md.run(12)
+    ref = md.thermo(), md.state()
+    md.close()
+    dp.close()
+    dp2, md2 = _md(model, b200dp.NPT, 0)  # a fresh process would build the same object
+    md2.read_restart(path)
+    md2.run(12)
+    th, st = md2.thermo(), md2.state()
+    assert th == ref[0]
+    for a, b in zip(st, ref[1]):
+        assert np.array_equal(a, b)
+    # a snapshot of another system or a damaged file is refused
+    dp3, md3 = _md(model, b200dp.NPT, 0, s=systems.water(3))
+    with pytest.raises(b200dp.B200DPError) as e:
+        md3.read_restart(path)
+    assert e.value.status in (1, 2)  # INVALID (other system) or IO (size differs)
+    with open(path, "r+b") as f:
+        f.truncate(100)
+    with pytest.raises(b200dp.B200DPError) as e:
+        md2.read_restart(path)
+    assert e.value.status == 2  # B200DP_ERR_IO
+    for o in (md2, md3, dp2, dp3):
+        o.close()
