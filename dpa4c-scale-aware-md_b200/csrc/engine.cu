@@ -349,6 +349,8 @@ void Engine::release() {
     for (auto& b : v) b.release();
   for (auto& b : fit_dev) b.release();
   for (auto& b : c8_dev) b.release();
+  if (pin) cudaFreeHost(pin);
+  pin = nullptr;
   for (void* q : pf_opened) cudaIpcCloseMemHandle(q);
   pf_opened.clear();
   if (pf_buf) cudaFree(pf_buf);
@@ -843,6 +845,14 @@ b200dp_status Engine::check() {
   if (last_stream_valid()) B200DP_CUDA_TRY(cudaStreamSynchronize(last_stream));
   int h[kErrCount] = {0};
   B200DP_CUDA_TRY(cudaMemcpy(h, err_buf.ptr, sizeof(h), cudaMemcpyDeviceToHost));
+  int stale = 0;
+  if (vl_stale.ptr) B200DP_CUDA_TRY(cudaMemcpy(&stale, vl_stale.ptr, sizeof(int), cudaMemcpyDeviceToHost));
+  return check_flags(h, stale);
+}
+
+// The device error flags of the last call (h) and the sticky stale flag, as
+// copied to the host after the call's stream has completed.
+b200dp_status Engine::check_flags(const int* h, int stale) {
   last_overflow = h[kErrSelOverflow];
   if (h[kErrBadType]) {
     err = "atom type outside [0, ntypes)";
@@ -861,8 +871,6 @@ b200dp_status Engine::check() {
     return B200DP_ERR_SEL_OVERFLOW;
   }
   if (vl_stale.ptr) {  // sticky until reported
-    int stale = 0;
-    B200DP_CUDA_TRY(cudaMemcpy(&stale, vl_stale.ptr, sizeof(int), cudaMemcpyDeviceToHost));
     if (stale) {
       B200DP_CUDA_TRY(cudaMemset(vl_stale.ptr, 0, sizeof(int)));
       vl_valid = false;
@@ -1072,8 +1080,15 @@ b200dp_status Engine::compute_host(int nloc, int nghost, const double* coord, co
                         atom_virial ? h_aviral.as<double>() : nullptr);
   }
   if (rc != B200DP_OK) return rc;
-  double sc[10];
+  // scalars, error flags and the stale flag in one pinned block: [10 f64][kErrCount i32][stale i32]
+  if (!pin) B200DP_CUDA_TRY(cudaHostAlloc(reinterpret_cast<void**>(&pin), 256, cudaHostAllocDefault));
+  double* sc = reinterpret_cast<double*>(pin);
+  int* flags = reinterpret_cast<int*>(pin + 80);
+  flags[kErrCount] = 0;
   B200DP_CUDA_TRY(cudaMemcpyAsync(sc, d_scal, sizeof(double) * 10, cudaMemcpyDeviceToHost, st));
+  B200DP_CUDA_TRY(cudaMemcpyAsync(flags, err_buf.ptr, sizeof(int) * kErrCount, cudaMemcpyDeviceToHost, st));
+  if (vl_stale.ptr)
+    B200DP_CUDA_TRY(cudaMemcpyAsync(flags + kErrCount, vl_stale.ptr, sizeof(int), cudaMemcpyDeviceToHost, st));
   if (nall > 0) B200DP_CUDA_TRY(cudaMemcpyAsync(force, h_force.ptr, sizeof(double) * 3 * nall, cudaMemcpyDeviceToHost, st));
   if (atom_energy && nloc > 0)
     B200DP_CUDA_TRY(cudaMemcpyAsync(atom_energy, h_ae.ptr, sizeof(double) * nloc, cudaMemcpyDeviceToHost, st));
@@ -1082,7 +1097,7 @@ b200dp_status Engine::compute_host(int nloc, int nghost, const double* coord, co
   B200DP_CUDA_TRY(cudaStreamSynchronize(st));
   *energy = sc[0];
   std::memcpy(virial, sc + 1, 9 * sizeof(double));
-  return check();
+  return check_flags(flags, flags[kErrCount]);
 }
 
 b200dp_status Engine::compute_with_nlist(cudaStream_t st, int nloc, int nall, const double* d_coord, const int* d_atype,

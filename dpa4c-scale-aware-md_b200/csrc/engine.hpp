@@ -100,6 +100,9 @@ struct Engine {
   }
   // host-call staging
   DevBuf h_coord, h_atype, h_force, h_aviral, h_ae;
+  // pinned host block for the host call's scalars and error flags (one D2H, one sync)
+  unsigned char* pin = nullptr;
+  b200dp_status check_flags(const int* h, int stale);
 
   cudaStream_t own_stream = nullptr;
   cudaStream_t last_stream = nullptr;
