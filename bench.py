@@ -11,7 +11,8 @@ random-init weights, seed 0).  Inputs are seeded synthetic data.
 
 * ``value``: device-timed throughput, inputs resident in HBM, CUDA events on
   the launch stream around each step; L2 is flushed (256 MB write) before
-  every timed step, outside the events.  Multi-GPU (weak scaling): one
+  every timed step, outside the events.  The force call (its 24 kernels) is
+  recorded once as a CUDA graph and replayed each step.  Multi-GPU (weak scaling): one
   process per GPU, one global water box of 4096 H2O per GPU split by spatial
   domain decomposition (slab for 2 GPUs, 2x2x1 for 4, 2x2x2 for 8; 8 A ghost
   shell); a step is the forward halo of coordinates over NCCL, the force call
@@ -232,10 +233,37 @@ class Periodic:
         self.e = torch.zeros(1, dtype=torch.float64, device=dev)
         self.f = torch.zeros(self.n, 3, dtype=torch.float64, device=dev)
         self.v = torch.zeros(9, dtype=torch.float64, device=dev)
+        self.torch = torch
+        self.graph = None
+
+    def _call(self, stream):
+        self.dp.compute_device(stream.cuda_stream, self.n, 0, self.x.data_ptr(), self.t.data_ptr(),
+                               self.system.box, None, self.e.data_ptr(), self.f.data_ptr(), self.v.data_ptr())
+
+    def capture(self):
+        """Records the force call (24 kernels) as one CUDA graph; step() replays it.  The call
+        is capture-safe: no host synchronisation, fixed buffers, the same box every step."""
+        torch = self.torch
+        side = torch.cuda.Stream()
+        side.wait_stream(self.stream)
+        with torch.cuda.stream(side):
+            self._call(side)
+        self.stream.wait_stream(side)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            self._call(side)
+        torch.cuda.synchronize()
+        self.graph = g
+
+    def release(self):
+        self.graph = None
 
     def step(self):
-        self.dp.compute_device(self.stream.cuda_stream, self.n, 0, self.x.data_ptr(), self.t.data_ptr(),
-                               self.system.box, None, self.e.data_ptr(), self.f.data_ptr(), self.v.data_ptr())
+        if self.graph is not None:
+            self.graph.replay()
+            return
+        self._call(self.stream)
 
 
 class Decomposed:
@@ -307,8 +335,9 @@ def run_b200dp(args, world, rank, local):
 
     def device_loop(dp, w, steps, warmup):
         """Timed steps: CUDA events around each step on the launch stream, L2 flushed before each,
-        no host synchronisation inside the loop.  N > 1 replays the decomposed step as a CUDA graph;
-        its kernel count per step is the number the capture recorded."""
+        no host synchronisation inside the loop.  The step is replayed as a CUDA graph (the periodic
+        force call on 1 GPU, the decomposed step on N); its kernel count per step is the number the
+        capture recorded."""
         for _ in range(warmup):
             w.step()
         dp.check()
@@ -466,7 +495,7 @@ def run_b200dp(args, world, rank, local):
                        f"NCCL send/recv, {rev}, step replayed as one CUDA graph")
         cfg_extra = {"global_atoms": w.total, "ghosts_rank0": w.nghost}
     else:
-        parallelism, cfg_extra = "single", {}
+        parallelism, cfg_extra = "single GPU, force call replayed as one CUDA graph", {}
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "atom-steps/s", "n_gpus": world, "steps": args.steps,

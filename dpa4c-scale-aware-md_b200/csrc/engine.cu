@@ -368,6 +368,8 @@ void Engine::release() {
     for (auto& b : *arr) b.release();
   for (auto* arr : {&Z_hi, &Z_lo, &DYf})
     for (auto& b : *arr) b.release();
+  dt_part.release();
+  dt_cnt.release();
   for (auto& b : th_l) b.release();
   for (auto& b : y_l) b.release();
   for (auto& b : dy_l) b.release();
@@ -477,6 +479,8 @@ b200dp_status Engine::ensure_buffers(int nloc, int nall, int ncells, int ncand) 
       B200DP_CUDA_TRY(DYf[q].ensure(sizeof(float) * rp * 256));
     }
     fit_rows_padded = rp;
+    B200DP_CUDA_TRY(dt_part.ensure(sizeof(float) * (size_t)kDtSplitSlots * 128 * 64));
+    B200DP_CUDA_TRY(grow_zero(dt_cnt, sizeof(unsigned) * kDtSplitSlots));
   }
   return B200DP_OK;
 }
@@ -614,6 +618,8 @@ b200dp_status Engine::run_model(cudaStream_t st, int nloc, int nall, const int* 
     FitTcBuffers fb;
     std::memset(&fb, 0, sizeof(fb));
     fb.rows_padded = fit_rows_padded;
+    fb.dt_part = dt_part.as<float>();
+    fb.dt_cnt = dt_cnt.as<unsigned>();
     for (int l = 0; l < fplan.L; ++l) {
       fb.At_hi[l] = At_hi[l].as<unsigned char>();
       fb.At_lo[l] = At_lo[l].as<unsigned char>();

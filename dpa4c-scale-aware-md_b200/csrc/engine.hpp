@@ -99,6 +99,7 @@ struct Engine {
     return PeerSet{pf_ptrs.as<unsigned char*>(), 0, pf_off_nf, pf_off_x};
   }
   // host-call staging
+  DevBuf dt_part, dt_cnt;  // split final fitting backward (few row tiles)
   DevBuf h_coord, h_atype, h_force, h_aviral, h_ae;
   // pinned host block for the host call's scalars and error flags (one D2H, one sync)
   unsigned char* pin = nullptr;

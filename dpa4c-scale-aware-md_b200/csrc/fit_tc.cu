@@ -258,7 +258,11 @@ __global__ void __launch_bounds__(kFitThreads, 2) k_fit_gemm(GemmArgs a) {
 // dD = dz0 W0^T fused with the descriptor contraction (D = T^T T_<, with T
 // already divided by N):
 //   dT[k][a] = (sum_b dD[a][b] T[k][b] + [a < M2] sum_c dD[c][a] T[k][c]) / N
-// One CTA per 128-row tile.  The whole dz0 tile stays in shared memory; dD is
+// One CTA per 128-row tile and chunk range: with few row tiles (small
+// systems) the N chunks of a tile are split over gridDim.y CTAs so that the
+// SMs are used; the second term's partial sums then go to dt_part and the
+// last CTA of the tile to arrive adds them in split order (deterministic).
+// The whole dz0 tile stays in shared memory; dD is
 // produced in N chunks of BN = 16 NA columns (NA descriptor rows a) into two
 // TMEM buffers, so the epilogue of chunk j overlaps the MMAs of chunk j + 1.
 // Warps 0-15 run the epilogue: four warps per TMEM lane quadrant, one per
@@ -285,6 +289,8 @@ struct DtArgs {
   const int* perm_atom;
   float* dT;  // [row][4][M1]
   float* dD;  // [row][16 M1] or null
+  float* part;     // split partials (gridDim.y > 1)
+  unsigned* cnt;   // per-tile arrival counters (gridDim.y > 1)
   int* err;
 };
 
@@ -292,9 +298,12 @@ __global__ void __launch_bounds__(kDtThreads, 1) k_fit_dT(DtArgs a) {
   extern __shared__ __align__(1024) unsigned char smem[];
   __shared__ uint64_t a_full, b_full[kDtMaxStages], b_empty[kDtMaxStages], acc_full[2], acc_empty[2];
   __shared__ uint32_t tbase;
-  __shared__ int s_fail;
+  __shared__ int s_fail, s_last;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = blockIdx.x;
+  const int nsplit = gridDim.y, split = blockIdx.y;
+  const int per = (a.nchunks + nsplit - 1) / nsplit;
+  const int j0 = min(a.nchunks, split * per), j1 = min(a.nchunks, j0 + per);
   if (g >= a.ftile[a.ntypes]) return;  // CTA-uniform, before any TMEM allocation
   int t = 0;
   while (t + 1 < a.ntypes && a.ftile[t + 1] <= g) ++t;
@@ -321,7 +330,7 @@ __global__ void __launch_bounds__(kDtThreads, 1) k_fit_dT(DtArgs a) {
   umma::fence_before_sync();
   __syncthreads();
   umma::fence_after_sync();
-  const int total = a.nchunks * a.nk;
+  const int total = (j1 - j0) * a.nk;
   const int S = a.stages;
   if (warp == 16 && lane == 0) {  // loader: the dz0 tile once, then the W0 blocks through the ring
     const unsigned char* Ah = a.A_hi + (size_t)g * AH;
@@ -331,10 +340,10 @@ __global__ void __launch_bounds__(kDtThreads, 1) k_fit_dT(DtArgs a) {
       umma::bulk_g2s(sA + kc * kABlock, Ah + (size_t)kc * kABlock, kABlock, &a_full);
       umma::bulk_g2s(sA + AH + kc * kABlock, Al + (size_t)kc * kABlock, kABlock, &a_full);
     }
-    const unsigned char* Bh = a.B_hi[t];
-    const unsigned char* Bl = a.B_lo[t];
+    const unsigned char* Bh = a.B_hi[t] + (size_t)j0 * a.nk * BB;  // B blocks are ordered (N chunk, K chunk)
+    const unsigned char* Bl = a.B_lo[t] + (size_t)j0 * a.nk * BB;
     int s = 0, round = 0;
-    for (int it = 0; it < total; ++it) {  // B blocks are ordered (N chunk, K chunk)
+    for (int it = 0; it < total; ++it) {
       if (round > 0 && !umma::mbar_wait(&b_empty[s], (round - 1) & 1, kWaitLimit)) {
         s_fail = 1;
         break;
@@ -357,7 +366,7 @@ __global__ void __launch_bounds__(kDtThreads, 1) k_fit_dT(DtArgs a) {
     const uint64_t db0 = umma::desc(umma::smem_u32(sB), 128, kSbo);
     const uint64_t sstep = (2 * BB) >> 4, o_bl = BB >> 4, kstep = kABlock >> 4;
     int s = 0, round = 0;
-    for (int j = 0; j < a.nchunks && ok; ++j) {
+    for (int j = 0; j < j1 - j0 && ok; ++j) {  // j counts this CTA's chunks
       const int buf = j & 1;
       if (j >= 2) {
         ok = umma::mbar_wait(&acc_empty[buf], ((j - 2) >> 1) & 1, kWaitLimit);
@@ -403,12 +412,12 @@ __global__ void __launch_bounds__(kDtThreads, 1) k_fit_dT(DtArgs a) {
     }
     const int NA = a.BN / 16;  // at most 16
     bool ok = true;
-    for (int j = 0; j < a.nchunks; ++j) {
-      const int buf = j & 1;
+    for (int jj = 0; jj < j1 - j0; ++jj) {
+      const int j = j0 + jj, buf = jj & 1;
       float tav[16];  // T[k][a] of the chunk's rows a, loaded before waiting for the MMA
 #pragma unroll
       for (int i = 0; i < 16; ++i) tav[i] = (valid && i < NA) ? Tk[j * NA + i] : 0.f;
-      if (ok) ok = umma::mbar_wait(&acc_full[buf], (j >> 1) & 1, kWaitLimit);
+      if (ok) ok = umma::mbar_wait(&acc_full[buf], (jj >> 1) & 1, kWaitLimit);
       umma::fence_after_sync();
       if (ok) {
 #pragma unroll
@@ -440,10 +449,17 @@ __global__ void __launch_bounds__(kDtThreads, 1) k_fit_dT(DtArgs a) {
       umma::fence_before_sync();
       umma::mbar_arrive(&acc_empty[buf]);
     }
-    // second term for a < 16: this thread wrote the first term itself
-    if (valid && ok) {
+    if (nsplit == 1) {
+      // second term for a < 16: this thread wrote the first term itself
+      if (valid && ok) {
 #pragma unroll
-      for (int b = 0; b < 16; ++b) dTk[b] += acc2[b] * a.inv_nnei;
+        for (int b = 0; b < 16; ++b) dTk[b] += acc2[b] * a.inv_nnei;
+      }
+    } else {
+      float4* pp = reinterpret_cast<float4*>(a.part + (((size_t)split * gridDim.x + g) * 128 + r) * 64 + k * 16);
+#pragma unroll
+      for (int b = 0; b < 16; b += 4) pp[b / 4] = make_float4(acc2[b], acc2[b + 1], acc2[b + 2], acc2[b + 3]);
+      __threadfence();
     }
     if (!ok) s_fail = 1;
   }
@@ -451,6 +467,34 @@ __global__ void __launch_bounds__(kDtThreads, 1) k_fit_dT(DtArgs a) {
   __syncthreads();
   if (tid == 0 && s_fail) atomicAdd(a.err + 3, 1);
   if (warp == 0) umma::tmem_dealloc(tbase, 512);
+  if (nsplit == 1) return;
+  // the tile's last CTA adds the splits' second terms, in split order
+  if (tid == 0) {
+    s_last = atomicAdd(a.cnt + g, 1u) == (unsigned)nsplit - 1;
+    if (s_last) a.cnt[g] = 0u;  // ready for the next launch
+  }
+  __syncthreads();
+  if (!s_last || warp >= 16 || s_fail) return;
+  __threadfence();
+  const int k = warp >> 2, r = (warp & 3) * 32 + lane;
+  if (r >= nrows) return;
+  float sum[16];
+#pragma unroll
+  for (int b = 0; b < 16; ++b) sum[b] = 0.f;
+  for (int sp = 0; sp < nsplit; ++sp) {
+    const float4* pp = reinterpret_cast<const float4*>(a.part + (((size_t)sp * gridDim.x + g) * 128 + r) * 64 + k * 16);
+#pragma unroll
+    for (int b = 0; b < 16; b += 4) {
+      const float4 v = __ldcg(pp + b / 4);
+      sum[b] += v.x;
+      sum[b + 1] += v.y;
+      sum[b + 2] += v.z;
+      sum[b + 3] += v.w;
+    }
+  }
+  float* dTk = a.dT + (size_t)(row0 + r) * 4 * a.M1 + k * a.M1;
+#pragma unroll
+  for (int b = 0; b < 16; ++b) dTk[b] = __ldcg(dTk + b) + sum[b] * a.inv_nnei;
 }
 
 __global__ void k_fit_tile_table(int ntypes, const int* __restrict__ type_start, int* __restrict__ ftile) {
@@ -683,7 +727,16 @@ void launch_fit_tc(cudaStream_t st, const FitTcPlan& p, int ntypes, int nloc, co
       d.perm_atom = perm_atom;
       d.dT = dT;
       d.dD = dD;
+      d.part = b.dt_part;
+      d.cnt = b.dt_cnt;
       d.err = err;
+      // few row tiles: split each tile's chunks over CTAs so that the SMs are used
+      int nsplit = 1;
+      if (b.dt_part && b.dt_cnt && row_tiles > 0) {
+        nsplit = std::max(1, std::min(d.nchunks, kDtSplitSlots / row_tiles));
+        const int per = (d.nchunks + nsplit - 1) / nsplit;
+        nsplit = (d.nchunks + per - 1) / per;  // no CTA without a chunk
+      }
       // as many W0 stages as fit beside the resident dz0 tile: the stream is L2-latency bound
       const size_t abytes = 2 * (size_t)d.nk * kABlock, sbytes = 2 * (size_t)d.BN * kFitBK * 2;
       d.stages = (int)std::min<size_t>(kDtMaxStages, (kDtSmemMax - abytes) / sbytes);
@@ -694,7 +747,7 @@ void launch_fit_tc(cudaStream_t st, const FitTcPlan& p, int ntypes, int nloc, co
         attr = smem;
       }
       count_launch();
-      k_fit_dT<<<row_tiles, kDtThreads, smem, st>>>(d);
+      k_fit_dT<<<dim3(row_tiles, nsplit), kDtThreads, smem, st>>>(d);
     }
   }
 }

@@ -65,7 +65,13 @@ struct FitTcBuffers {
   unsigned char* Z_hi[2];               // tiled dz ping-pong
   unsigned char* Z_lo[2];
   float* DY[2];                         // residual gradients ping-pong
+  // final backward split over several CTAs per row tile (few row tiles):
+  // partial second terms [kDtSplitSlots][128][4][16] and per-tile arrival
+  // counters [kDtSplitSlots] (zero between launches)
+  float* dt_part;
+  unsigned* dt_cnt;
 };
+constexpr int kDtSplitSlots = 148;  // split CTAs of one launch: row tiles x splits <= this
 
 // First row tile of each type (exclusive prefix of ceil(n_t/128)); [ntypes+1].
 void launch_fit_tile_table(cudaStream_t st, int ntypes, const int* type_start, int* ftile);

@@ -368,6 +368,12 @@ struct b200dp_md {
   double omega_dot = 0, w_mass = 0, vol0 = 0, t_current = 0, vir_trace = 0, epot = 0;
   std::string err;
   SnapHeader snap_stage{};
+  // NVE / NVT: one neighbour-rebuild cycle of steps recorded as a CUDA graph
+  // and replayed (every step's work is enqueued with no host decision left,
+  // the skin check and rebuild being gated on the device)
+  cudaGraphExec_t cycle = nullptr;
+  int cycle_len = 0;
+  bool cycle_failed = false;
 };
 
 extern "C" {
@@ -579,6 +585,70 @@ static b200dp_status npt_step(b200dp_md* md, int grid) {
   return cudaGetLastError() == cudaSuccess ? B200DP_OK : B200DP_ERR_CUDA;
 }
 
+// One NVE / NVT step enqueued on the MD stream.
+static b200dp_status md_step(b200dp_md* md) {
+  const int n = md->n;
+  const double dtf = 0.5 * md->p.dt * kFtm2v, dt = md->p.dt;
+  const int grid = std::min(kRedBlocks * 4, (n + kMdThreads - 1) / kMdThreads);
+  const bool nvt = md->ensemble == B200DP_MD_NVT;
+  cudaStream_t st = md->stream;
+  if (nvt) {
+    count_launch();
+    k_md_chain<<<1, 32, 0, st>>>(md->cp, md->chain.p, nullptr, 0, nullptr);
+  }
+  count_launch();
+  k_md_first<<<grid, kMdThreads, 0, st>>>(n, md->x.p, md->v.p, md->f.p, md->minv.p, nvt ? md->chain.p : nullptr,
+                                          dtf, dt);
+  const b200dp_status rc = b200dp_compute_device(md->engine, st, n, 0, md->x.p, md->atype.p, md->box, nullptr,
+                                                 md->e.p, md->f.p, md->vir.p, nullptr, nullptr);
+  if (rc != B200DP_OK) return rc;
+  count_launch();
+  k_md_second<<<kRedBlocks, kMdThreads, 0, st>>>(n, md->v.p, md->f.p, md->minv.p, md->mass.p, dtf, md->part.p);
+  if (nvt) {
+    count_launch();
+    k_md_chain<<<1, 32, 0, st>>>(md->cp, md->chain.p, md->part.p, kRedBlocks, nullptr);
+    count_launch();
+    k_md_scale<<<grid, kMdThreads, 0, st>>>(n, md->v.p, md->chain.p);
+    count_launch();
+    k_md_ke<<<kRedBlocks, kMdThreads, 0, st>>>(n, md->v.p, md->mass.p, md->part.p);
+  }
+  return B200DP_OK;
+}
+
+// Records `len` steps into a graph (the recording executes nothing; the
+// caller replays it).  The cycle starts with the scheduled candidate build,
+// so every replay repeats the same rebuild cadence.  A failed recording
+// leaves the stream usable and the run continues step by step.
+static b200dp_status record_cycle(b200dp_md* md, int len) {
+  cudaStream_t st = md->stream;
+  const int every = md->p.rebuild_every > 1 ? md->p.rebuild_every : 0;
+  if (b200dp_set_neighbor_reuse(md->engine, md->p.skin, every) != B200DP_OK) return B200DP_ERR_INVALID;
+  if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+    cudaGetLastError();
+    md->cycle_failed = true;
+    return B200DP_OK;
+  }
+  b200dp_status rc = B200DP_OK;
+  for (int k = 0; k < len && rc == B200DP_OK; ++k) rc = md_step(md);
+  cudaGraph_t g = nullptr;
+  const cudaError_t ce = cudaStreamEndCapture(st, &g);
+  cudaGraphExec_t ex = nullptr;
+  if (rc == B200DP_OK && ce == cudaSuccess && g && cudaGraphInstantiate(&ex, g, 0) == cudaSuccess) {
+    md->cycle = ex;
+    md->cycle_len = len;
+  } else {
+    md->cycle_failed = true;
+    cudaGetLastError();
+  }
+  if (g) cudaGraphDestroy(g);
+  if (rc != B200DP_OK) return rc;
+  // the engine's host-side neighbour cycle advanced during the recording as the
+  // replays will advance the device state (a cycle ends where the next one's
+  // scheduled build begins); after a failed recording nothing ran: restart it
+  if (!md->cycle) return b200dp_set_neighbor_reuse(md->engine, md->p.skin, every);
+  return B200DP_OK;
+}
+
 b200dp_status b200dp_md_run(b200dp_md* md, int nsteps) {
   if (!md || nsteps < 0) return B200DP_ERR_INVALID;
   if (md->ensemble == B200DP_MD_NPT) {
@@ -597,33 +667,25 @@ b200dp_status b200dp_md_run(b200dp_md* md, int nsteps) {
     }
     return B200DP_OK;
   }
-  const int n = md->n;
-  const double dtf = 0.5 * md->p.dt * kFtm2v, dt = md->p.dt;
-  const int grid = std::min(kRedBlocks * 4, (n + kMdThreads - 1) / kMdThreads);
-  const bool nvt = md->ensemble == B200DP_MD_NVT;
-  cudaStream_t st = md->stream;
-  for (int s = 0; s < nsteps; ++s) {
-    if (nvt) {
-      count_launch();
-      k_md_chain<<<1, 32, 0, st>>>(md->cp, md->chain.p, nullptr, 0, nullptr);
+  for (int s = 0; s < nsteps;) {
+    // whole cycles replay the recorded graph; the rest (and a first cycle that
+    // is being recorded) are enqueued step by step
+    const int L = md->p.rebuild_every > 1 ? md->p.rebuild_every : 1;
+    if (md->cycle && nsteps - s >= md->cycle_len) {
+      if (cudaGraphLaunch(md->cycle, md->stream) != cudaSuccess) return B200DP_ERR_CUDA;
+      md->step += md->cycle_len;
+      s += md->cycle_len;
+      continue;
     }
-    count_launch();
-    k_md_first<<<grid, kMdThreads, 0, st>>>(n, md->x.p, md->v.p, md->f.p, md->minv.p, nvt ? md->chain.p : nullptr,
-                                            dtf, dt);
-    const b200dp_status rc = b200dp_compute_device(md->engine, st, n, 0, md->x.p, md->atype.p, md->box, nullptr,
-                                                   md->e.p, md->f.p, md->vir.p, nullptr, nullptr);
+    if (!md->cycle && !md->cycle_failed && nsteps - s >= L) {
+      const b200dp_status rc = record_cycle(md, L);
+      if (rc != B200DP_OK) return rc;
+      if (md->cycle) continue;
+    }
+    const b200dp_status rc = md_step(md);
     if (rc != B200DP_OK) return rc;
-    count_launch();
-    k_md_second<<<kRedBlocks, kMdThreads, 0, st>>>(n, md->v.p, md->f.p, md->minv.p, md->mass.p, dtf, md->part.p);
-    if (nvt) {
-      count_launch();
-      k_md_chain<<<1, 32, 0, st>>>(md->cp, md->chain.p, md->part.p, kRedBlocks, nullptr);
-      count_launch();
-      k_md_scale<<<grid, kMdThreads, 0, st>>>(n, md->v.p, md->chain.p);
-      count_launch();
-      k_md_ke<<<kRedBlocks, kMdThreads, 0, st>>>(n, md->v.p, md->mass.p, md->part.p);
-    }
     ++md->step;
+    ++s;
   }
   return cudaGetLastError() == cudaSuccess ? B200DP_OK : B200DP_ERR_CUDA;
 }
@@ -802,6 +864,7 @@ b200dp_status b200dp_md_read_restart(b200dp_md* md, const char* path) {
 b200dp_status b200dp_md_destroy(b200dp_md* md) {
   if (!md) return B200DP_OK;
   cudaStreamSynchronize(md->stream);
+  if (md->cycle) cudaGraphExecDestroy(md->cycle);
   cudaStreamDestroy(md->stream);
   b200dp_set_neighbor_reuse(md->engine, 0.0, 0);  // the engine's other callers bin from scratch again
   delete md;
