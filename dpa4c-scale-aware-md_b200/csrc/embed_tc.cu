@@ -452,7 +452,8 @@ __global__ void __launch_bounds__(256 * FwdGroup::NG, 1) k_embed_fwd_tc(FwdArgs 
 // so the MMAs with scaled weights return true gradients.
 struct BwdGroup {
   static constexpr uint32_t A1B = 128 * 32 * 2, XB = 128 * 64 * 2, DTB = kItemRows * 128 * 16;
-  static constexpr uint32_t O_A1 = 0, O_X = 2 * A1B, O_DT = O_X + 2 * XB, BYTES = O_DT + DTB;
+  static constexpr uint32_t T2B = 16 * 256 * 4;  // layer-2 tanh outputs 16..31 (0..15 reuse the A1 slot)
+  static constexpr uint32_t O_A1 = 0, O_X = 2 * A1B, O_DT = O_X + 2 * XB, O_T2 = O_DT + DTB, BYTES = O_T2 + T2B;
   static constexpr uint32_t SBO_A1 = (32 / 8) * 128, SBO_X = (64 / 8) * 128;
   static constexpr uint32_t C_D2 = 0, C_D3 = 64, C_DH1 = 192, COLS = 256;  // TMEM columns per group
   static constexpr int NG = 2;
@@ -500,9 +501,24 @@ __device__ __forceinline__ void mma_ta(uint32_t d, uint32_t a_tmem, uint64_t b, 
       "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate));
 }
 
+// The layer-2 tanh outputs of a group's 256 threads, [position j][thread] fp32
+// (bank-conflict free): positions 0..15 in the layer-1 operand slot, which is
+// free from the completion of the layer-2 MMA until the next subtile's layer-1
+// stores (every read happens before the barrier ahead of the dh1 MMA),
+// positions 16..31 in a slot of their own.  Keeping them out of registers
+// leaves the backward epilogues without spills.
+struct T2Slots {
+  float* lo;
+  float* hi;
+  int t;
+  __device__ __forceinline__ float& operator[](int j) const {
+    return j < 16 ? lo[j * 256 + t] : hi[(j - 16) * 256 + t];
+  }
+};
+
 template <int D1, int D2, int D3, int H>
 __device__ __forceinline__ void bwd_epi2(const float* f, uint32_t taddr, const float (&h1p)[16], float (&h2)[32],
-                                         float (&t2)[32]) {
+                                         const T2Slots& t2) {
   using P = Split<D1, D2, D3>;
   float v[32];
   umma::ld16(taddr + H * 32, v);
@@ -526,7 +542,7 @@ __device__ __forceinline__ void bwd_epi2(const float* f, uint32_t taddr, const f
 // gradient into layer 2, scaled by 1/c); writes dz3' into TMEM in place.
 template <int D1, int D2, int D3, int H>
 __device__ __forceinline__ void bwd_epi3(const float* f, uint32_t taddr, const float4* dts, float4 rt,
-                                         const float (&h1p)[16], const float (&t2)[32], float (&racc)[32],
+                                         const float (&h1p)[16], const T2Slots& t2, float (&racc)[32],
                                          float4& dR) {
   using P = Split<D1, D2, D3>;
 #pragma unroll
@@ -571,7 +587,7 @@ __device__ __forceinline__ void bwd_epi3(const float* f, uint32_t taddr, const f
 // dh2 total = MMA + layer-3 residual gradient; dz2' = dh2 (1 - t2^2) / c;
 // racc1 collects the layer-2 residual gradient into layer 1.
 template <int D1, int D2, int D3, int H>
-__device__ __forceinline__ void bwd_epi_dh2(uint32_t taddr, const float (&t2)[32], const float (&racc)[32],
+__device__ __forceinline__ void bwd_epi_dh2(uint32_t taddr, const T2Slots& t2, const float (&racc)[32],
                                             float (&racc1)[16], float (&zz)[32]) {
   using P = Split<D1, D2, D3>;
   float v[32];
@@ -585,7 +601,8 @@ __device__ __forceinline__ void bwd_epi_dh2(uint32_t taddr, const float (&t2)[32
     if (j < P::c2(H)) {
       const float dh = fmaf(kTanhScale, racc[j], v[j]);
       if constexpr (P::R2 != 0) racc1[P::src2(H, j)] += dh;
-      zz[j] = dh * kInvTanhScale * fmaf(-t2[j], t2[j], 1.0f);
+      const float tj = t2[j];
+      zz[j] = dh * kInvTanhScale * fmaf(-tj, tj, 1.0f);
     } else {
       zz[j] = 0.f;
     }
@@ -631,6 +648,7 @@ __global__ void __launch_bounds__(256 * BwdGroup::NG, 1) k_embed_bwd_tc(BwdArgs 
   unsigned char* xh = gbase + S::O_X;
   unsigned char* xl = xh + S::XB;
   float4* dts = reinterpret_cast<float4*>(gbase + S::O_DT);
+  const T2Slots t2{reinterpret_cast<float*>(a1h), reinterpret_cast<float*>(gbase + S::O_T2), t};
   uint64_t* bar = &bars[g];
   if ((gtid >> 5) == 0) umma::tmem_alloc(&tbase, 512);
   if (t == 0) {
@@ -708,7 +726,7 @@ __global__ void __launch_bounds__(256 * BwdGroup::NG, 1) k_embed_bwd_tc(BwdArgs 
       const bool valid = e < ne;
       const float4 rt = valid ? L.rt[sub + e] : make_float4(0.f, 0.f, 0.f, 0.f);
       const int rloc = valid ? L.row[sub + e] - I.rb : 0;
-      float h1[16], h1p[16], h2[32], t2[32];
+      float h1[16], h1p[16], h2[32];
       if (hf == 0)
         fwd_layer1<D1, D2, D3, 0>(f, rt.x, h1, h1p);
       else
