@@ -410,13 +410,30 @@ __global__ void __launch_bounds__(kDtThreads, 1) k_fit_dT(DtArgs a) {
       Tb[b] = valid ? Tk[b] : 0.f;
       acc2[b] = 0.f;
     }
-    const int NA = a.BN / 16;  // at most 16
+    const int NA = a.BN / 16;  // at most 16, even (BN is a multiple of 32)
+    // T and dT rows are read and written as 8-byte pairs when a row's M1 floats
+    // keep them aligned: one row per thread, so each access is its own sector
+    const bool pairs = (M1 & 1) == 0;
     bool ok = true;
     for (int jj = 0; jj < j1 - j0; ++jj) {
       const int j = j0 + jj, buf = jj & 1;
       float tav[16];  // T[k][a] of the chunk's rows a, loaded before waiting for the MMA
+      float dtv[16];  // the chunk's first terms, stored after the loop
 #pragma unroll
-      for (int i = 0; i < 16; ++i) tav[i] = (valid && i < NA) ? Tk[j * NA + i] : 0.f;
+      for (int i = 0; i < 16; i += 2) {
+        float2 v = make_float2(0.f, 0.f);
+        if (valid && i < NA) {
+          if (pairs) {
+            v = *reinterpret_cast<const float2*>(Tk + j * NA + i);
+          } else {
+            v.x = Tk[j * NA + i];
+            v.y = Tk[j * NA + i + 1];
+          }
+        }
+        tav[i] = v.x;
+        tav[i + 1] = v.y;
+        dtv[i] = dtv[i + 1] = 0.f;
+      }
       if (ok) ok = umma::mbar_wait(&acc_full[buf], (jj >> 1) & 1, kWaitLimit);
       umma::fence_after_sync();
       if (ok) {
@@ -437,7 +454,7 @@ __global__ void __launch_bounds__(kDtThreads, 1) k_fit_dT(DtArgs a) {
               acc2[b] = fmaf(dv[b], ta, acc2[b]);
               acc2[b + 1] = fmaf(dv[b + 1], ta, acc2[b + 1]);
             }
-            dTk[aa] = (s0 + s1) * a.inv_nnei;
+            dtv[i] = (s0 + s1) * a.inv_nnei;
             if (a.dD && k == 0) {
               float4* dst = reinterpret_cast<float4*>(a.dD + (size_t)urow * 16 * M1 + aa * 16);
 #pragma unroll
@@ -448,6 +465,18 @@ __global__ void __launch_bounds__(kDtThreads, 1) k_fit_dT(DtArgs a) {
       }
       umma::fence_before_sync();
       umma::mbar_arrive(&acc_empty[buf]);
+      if (valid && ok) {
+#pragma unroll
+        for (int i = 0; i < 16; i += 2) {
+          if (i >= NA) break;
+          if (pairs) {
+            *reinterpret_cast<float2*>(dTk + j * NA + i) = make_float2(dtv[i], dtv[i + 1]);
+          } else {
+            dTk[j * NA + i] = dtv[i];
+            dTk[j * NA + i + 1] = dtv[i + 1];
+          }
+        }
+      }
     }
     if (nsplit == 1) {
       // second term for a < 16: this thread wrote the first term itself
