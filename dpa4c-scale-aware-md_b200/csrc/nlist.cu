@@ -511,25 +511,35 @@ __device__ __forceinline__ void gather_stencil(const FormatSpec& f, const GridSp
   const int ci[3] = {cell / (g.n[1] * g.n[2]), (cell / g.n[2]) % g.n[1], cell % g.n[2]};
   const int sy = 2 * g.reach[1] + 1, sz = 2 * g.reach[2] + 1;
   const int nstencil = (2 * g.reach[0] + 1) * sy * sz;
+  // a stencil that reaches at most one cell row past the box wraps by one image
+  // per dimension (no division); wider reaches (boxes thinner than the cutoff)
+  // take the general floor division
+  const bool one_image = g.reach[0] <= g.n[0] && g.reach[1] <= g.n[1] && g.reach[2] <= g.n[2];
   for (int s0 = 0; s0 < nstencil; s0 += kStencilChunk) {
     // counts of this lane's cells, then a warp scan
     int cnt[kStencilPerLane], st[kStencilPerLane], cd[kStencilPerLane];
     int local = 0;
+    // this lane's first stencil cell, decoded once; the next ones step in z with carries
+    const int sfirst = s0 + lane * kStencilPerLane;
+    int dz = sfirst % sz, dy = (sfirst / sz) % sy, dx = sfirst / (sz * sy);
 #pragma unroll
     for (int u = 0; u < kStencilPerLane; ++u) {
-      const int sidx = s0 + lane * kStencilPerLane + u;
+      const int sidx = sfirst + u;
       cnt[u] = 0;
       st[u] = 0;
       cd[u] = 0;
       if (sidx < nstencil) {
-        const int dz = sidx % sz, dy = (sidx / sz) % sy, dx = sidx / (sz * sy);
         int uu[3] = {ci[0] + dx - g.reach[0], ci[1] + dy - g.reach[1], ci[2] + dz - g.reach[2]};
         int img[3] = {0, 0, 0};
         bool ok = true;
 #pragma unroll
         for (int d = 0; d < 3; ++d) {
           if (g.periodic) {
-            img[d] = floor_div(uu[d], g.n[d]);
+            if (one_image) {
+              img[d] = uu[d] < 0 ? -1 : (uu[d] >= g.n[d] ? 1 : 0);
+            } else {
+              img[d] = floor_div(uu[d], g.n[d]);
+            }
             uu[d] -= img[d] * g.n[d];
           } else {
             ok = ok && uu[d] >= 0 && uu[d] < g.n[d];
@@ -543,6 +553,13 @@ __device__ __forceinline__ void gather_stencil(const FormatSpec& f, const GridSp
         }
       }
       local += cnt[u];
+      if (++dz == sz) {
+        dz = 0;
+        if (++dy == sy) {
+          dy = 0;
+          ++dx;
+        }
+      }
     }
     int total;
     int run = warp_exclusive_scan(local, lane, total);
