@@ -951,11 +951,16 @@ __global__ void __launch_bounds__(256) k_t_combine(TcLists L, int M2, float inv_
     const float* st = sT[rr];
     const int k0 = g * 8;
     float v[8];
+    // descriptor column k = aa M2 + b: one division per group of 8, then a carry
+    int aa = k0 / M2, b = k0 - aa * M2;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const int k = k0 + j, aa = k / M2, b = k - aa * M2;
       v[j] = st[aa] * st[b] + st[D3 + aa] * st[D3 + b] + st[2 * D3 + aa] * st[2 * D3 + b] +
              st[3 * D3 + aa] * st[3 * D3 + b];
+      if (++b == M2) {
+        b = 0;
+        ++aa;
+      }
     }
     if (D) {
       float4* drow = reinterpret_cast<float4*>(D + (size_t)r * dim + k0);
