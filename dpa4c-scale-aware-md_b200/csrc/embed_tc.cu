@@ -940,10 +940,21 @@ __global__ void __launch_bounds__(256) k_t_combine(TcLists L, int M2, float inv_
     for (int k = 0; k < 4; ++k) {
       const float v = acc[k] * inv_nnei;
       sT[rr][k * D3 + c] = v;
-      T[(size_t)atom * 4 * D3 + k * D3 + c] = v;
+      if (!Dt_hi) T[(size_t)atom * 4 * D3 + k * D3 + c] = v;
     }
   }
   __syncthreads();
+  if (Dt_hi) {
+    // for the tensor-core fitting, T in its 128-row tiles, [tile][k][c][row in tile]: the
+    // final fitting backward (one thread per row) then reads it coalesced
+    for (int idx = tid; idx < kCombRows * 4 * D3; idx += blockDim.x) {
+      const int rr = idx % kCombRows, kc = idx / kCombRows, r = r0 + rr;
+      if (r >= nrows) continue;
+      const int t = s_type[rr];
+      const int prow = 128 * ftile[t] + (r - L.type_start[t]);
+      T[((size_t)(prow >> 7) * 4 * D3 + kc) * 128 + (prow & 127)] = sT[rr][kc];
+    }
+  }
   const int dim = D3 * M2;
   for (int idx = tid; idx < kCombRows * (dim / 8); idx += blockDim.x) {
     const int rr = idx % kCombRows, g = idx / kCombRows, r = r0 + rr;

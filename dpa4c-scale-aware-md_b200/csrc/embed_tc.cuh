@@ -62,9 +62,10 @@ int embed_tc_grid(const SeaDev& s, bool backward);
 // Forward: Tq[net][row][4][M1] = sum over the net's edges of the row of R~ (x) G.
 void launch_embed_fwd_tc(cudaStream_t st, const SeaDev& s, const TcLists& L, int grid, const unsigned char* nets,
                          float* Tq, int* err);
-// T_i = sum over nets (fixed order) / N -> T (atom order, fp32), D (row order,
-// fp32) and, when Dt_hi != nullptr, D pre-tiled for the tensor-core fitting
-// (padded rows from ftile).
+// T_i = sum over nets (fixed order) / N -> T, D (row order, fp32) and, when
+// Dt_hi != nullptr, D pre-tiled for the tensor-core fitting (padded rows from
+// ftile).  T is [atom][4][M1] without Dt_hi, and with it [tile][4][M1][128]
+// in the fitting's padded row tiles (what the fused final backward reads).
 void launch_t_combine(cudaStream_t st, const SeaDev& s, const TcLists& L, const int* perm_atom, const int* ftile,
                       const float* Tq, float* T, float* D, unsigned char* Dt_hi, unsigned char* Dt_lo);
 // dE/dT per centre row (scaled by 1/N) from T (atom order) and dE/dD (row order).

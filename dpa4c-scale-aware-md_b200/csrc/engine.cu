@@ -479,6 +479,7 @@ b200dp_status Engine::ensure_buffers(int nloc, int nall, int ncells, int ncand) 
       B200DP_CUDA_TRY(DYf[q].ensure(sizeof(float) * rp * 256));
     }
     fit_rows_padded = rp;
+    B200DP_CUDA_TRY(Tbuf.ensure(sizeof(float) * rp * 4 * sd.M1));  // T in the fitting's row tiles
     B200DP_CUDA_TRY(dt_part.ensure(sizeof(float) * (size_t)kDtSplitSlots * 128 * 64));
     B200DP_CUDA_TRY(grow_zero(dt_cnt, sizeof(unsigned) * kDtSplitSlots));
   }

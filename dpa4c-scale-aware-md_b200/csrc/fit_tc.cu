@@ -285,7 +285,7 @@ struct DtArgs {
   const unsigned char* B_lo[kMaxTypes];
   int BN, nchunks, M1, stages;
   float inv_nnei;
-  const float* T;  // [atom][4][M1]
+  const float* T;  // in the fitting's row tiles: [tile][4][M1][128]
   const int* perm_atom;
   float* dT;  // [row][4][M1]
   float* dD;  // [row][16 M1] or null
@@ -401,18 +401,18 @@ __global__ void __launch_bounds__(kDtThreads, 1) k_fit_dT(DtArgs a) {
     const bool valid = r < nrows;
     const int urow = row0 + r;
     const int M1 = a.M1;
-    const float* Tk = a.T + (size_t)(valid ? a.perm_atom[urow] : 0) * 4 * M1 + k * M1;
+    const float* Tk = a.T + ((size_t)g * 4 + k) * M1 * 128 + r;  // element c at Tk[128 c]: lanes read a line
     float* dTk = a.dT + (size_t)urow * 4 * M1 + k * M1;
     const uint32_t lb = (uint32_t)(q * 32) << 16;
     float Tb[16], acc2[16];
 #pragma unroll
     for (int b = 0; b < 16; ++b) {
-      Tb[b] = valid ? Tk[b] : 0.f;
+      Tb[b] = valid ? Tk[128 * b] : 0.f;
       acc2[b] = 0.f;
     }
     const int NA = a.BN / 16;  // at most 16, even (BN is a multiple of 32)
-    // T and dT rows are read and written as 8-byte pairs when a row's M1 floats
-    // keep them aligned: one row per thread, so each access is its own sector
+    // dT rows are written as 8-byte pairs when a row's M1 floats keep them
+    // aligned (one row per thread, so each access is its own sector)
     const bool pairs = (M1 & 1) == 0;
     bool ok = true;
     for (int jj = 0; jj < j1 - j0; ++jj) {
@@ -420,19 +420,9 @@ __global__ void __launch_bounds__(kDtThreads, 1) k_fit_dT(DtArgs a) {
       float tav[16];  // T[k][a] of the chunk's rows a, loaded before waiting for the MMA
       float dtv[16];  // the chunk's first terms, stored after the loop
 #pragma unroll
-      for (int i = 0; i < 16; i += 2) {
-        float2 v = make_float2(0.f, 0.f);
-        if (valid && i < NA) {
-          if (pairs) {
-            v = *reinterpret_cast<const float2*>(Tk + j * NA + i);
-          } else {
-            v.x = Tk[j * NA + i];
-            v.y = Tk[j * NA + i + 1];
-          }
-        }
-        tav[i] = v.x;
-        tav[i + 1] = v.y;
-        dtv[i] = dtv[i + 1] = 0.f;
+      for (int i = 0; i < 16; ++i) {
+        tav[i] = (valid && i < NA) ? Tk[128 * (j * NA + i)] : 0.f;
+        dtv[i] = 0.f;
       }
       if (ok) ok = umma::mbar_wait(&acc_full[buf], (jj >> 1) & 1, kWaitLimit);
       umma::fence_after_sync();

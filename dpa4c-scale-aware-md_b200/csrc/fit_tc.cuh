@@ -80,8 +80,9 @@ void launch_fit_tile_D(cudaStream_t st, int nloc, int ntypes, int dim, const int
                        const float* D, unsigned char* hi, unsigned char* lo);
 // Whole fitting forward + backward; energies to atom_energy (atom order) and
 // dE/dT (rows in type-grouped order, [row][4][M1], through D = T^T T_< with T
-// in atom order already divided by N) to dT; dE/dD to dD only when dD is not
-// null.
+// already divided by N and laid out in the fitting's 128-row tiles,
+// [tile][4][M1][128], as launch_t_combine writes it) to dT; dE/dD to dD only
+// when dD is not null.
 void launch_fit_tc(cudaStream_t st, const FitTcPlan& p, int ntypes, int nloc, const int* type_start,
                    const int* ftile, const int* perm_atom, const FitTcWeights* w, const FitTcBuffers& b,
                    double* atom_energy, const float* T, float inv_nnei, float* dT, float* dD, int* err);
