@@ -75,6 +75,82 @@ def b200dp_compute(model, precision, device, staged):
     return compute
 
 
+class SharedMemoryFold:
+    """CPU stand-in for domain.PeerFold (oracle ranks over gloo): the peers'
+    buffers are POSIX shared-memory segments, one per rank, holding the owned
+    positions and one force slot per (owner, source rank) so that no two ranks
+    add into the same memory.  The step follows PeerFold's sequence and its
+    ordering rules (publish, barrier, gather; force call whose ghost rows go to
+    the owners' slots; all-reduce; finish), so the host orchestration of the
+    peer mode is exercised without GPUs."""
+
+    gathers = True
+
+    def __init__(self, compute, tag):
+        self.compute_rows = compute
+        self.tag = tag
+        self.segs = []
+
+    def setup(self, rank, nranks, nloc, origin, shift):
+        from multiprocessing import shared_memory
+
+        self.rank, self.nranks = rank, nranks
+        nlocs = [None] * nranks
+        dist.all_gather_object(nlocs, nloc)
+        self.cap = max(nlocs)
+        nbytes = 8 * self.cap * 3 * (1 + nranks)  # positions, then a force slot per source rank
+        mine = shared_memory.SharedMemory(name=f"{self.tag}_{rank}", create=True, size=nbytes)
+        self.segs = [mine]
+        dist.barrier()
+        self.views = []
+        for r in range(nranks):
+            seg = mine if r == rank else shared_memory.SharedMemory(name=f"{self.tag}_{r}")
+            if r != rank:
+                self.segs.append(seg)
+            self.views.append(np.ndarray((1 + nranks, self.cap, 3), dtype=np.float64, buffer=seg.buf))
+        self.views[rank][:] = 0.0
+        dist.barrier()
+        self.origin = origin.numpy().astype(np.int64)
+        self.shift = shift.numpy()
+
+    def publish(self, x_all, nloc):
+        self.views[self.rank][0, :nloc] = x_all[:nloc].numpy()
+
+    def gather(self, x_all, nloc, nghost):
+        o = self.origin
+        xs = np.empty((nghost, 3))
+        for r in range(self.nranks):
+            m = o[:, 0] == r
+            xs[m] = self.views[r][0, o[m, 1]]
+        x_all[nloc:] = torch.from_numpy(xs + self.shift)
+
+    def compute(self, x_all, t_all, nloc, nghost, region, e, f, v):
+        fa = torch.zeros_like(x_all)
+        self.compute_rows(x_all, t_all, nloc, nghost, region, e, fa, v)
+        f[:nloc] = fa[:nloc]
+        gf = fa[nloc:].numpy()
+        o = self.origin
+        for r in range(self.nranks):  # ghost rows into the owners' slot for this source rank
+            m = o[:, 0] == r
+            slot = self.views[r][1 + self.rank]
+            np.add.at(slot, o[m, 1], gf[m])
+
+    def finish(self, f, nloc):
+        acc = self.views[self.rank]
+        total = np.zeros((nloc, 3))
+        for src in range(self.nranks):  # fixed order
+            total += acc[1 + src, :nloc]
+            acc[1 + src, :nloc] = 0.0
+        f[:nloc] += torch.from_numpy(total)
+
+    def close(self):
+        for seg in self.segs:
+            seg.close()
+        if self.segs:
+            self.segs[0].unlink()
+        self.segs = []
+
+
 class StagedFold:
     """PeerFold for ranks that exchange CPU tensors over gloo and share one GPU
     (the host synchronises after every device step, so no rank's kernel waits
@@ -145,6 +221,8 @@ def main():
     fold = None
     if a.engine == "oracle":
         compute = oracle_compute(a.model)
+        if a.fold:
+            fold = SharedMemoryFold(compute, f"b2dp_fold_{os.environ['MASTER_PORT']}")
     else:
         compute = b200dp_compute(a.model, a.precision, device if a.backend == "nccl" else "cuda:0",
                                  staged=a.backend == "gloo")
@@ -165,6 +243,8 @@ def main():
              x_owned=ddp.x[: ddp.nloc].cpu().numpy(), x_ghost=ddp.x[ddp.nloc:].cpu().numpy())
     ddp.release()  # the graph holds NCCL calls: release it before the group goes
     dist.barrier()
+    if isinstance(fold, SharedMemoryFold):
+        fold.close()
     dist.destroy_process_group()
 
 

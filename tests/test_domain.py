@@ -70,6 +70,20 @@ def run_ranks(tmp_path, model, mol, grid, halo, extra=()):
     return [dict(np.load(tmp_path / f"r{r}.npz")) for r in range(world)]
 
 
+@pytest.mark.parametrize("grid,mol", [((2, 1, 1), (8, 4, 4)), ((2, 2, 1), (8, 8, 4))])
+def test_peer_mode_orchestration_on_cpu_ranks(tmp_path, model_dir, grid, mol):
+    """The peer mode's step (publish, barrier, gather of ghost positions from the
+    owners' buffers with the recorded shifts, force call with ghost rows added
+    into the owners' buffers, all-reduce, finish) on gloo ranks with shared
+    memory standing in for the GPUs' peer memory: equal to one periodic
+    evaluation, over two replayed steps."""
+    model = str(model_dir / "water.b2dp")
+    s, ref = reference(model, mol)
+    parts = run_ranks(tmp_path, model, mol, grid, 6.0, extra=("--fold",))
+    check(s, ref, parts)
+    check_origins(parts)
+
+
 def test_single_rank_self_exchange_equals_periodic(model_dir):
     """grid 1x1x1: the ghost shell is the periodic images, made by self-exchange."""
     model = str(model_dir / "water.b2dp")
