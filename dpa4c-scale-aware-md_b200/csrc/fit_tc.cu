@@ -286,7 +286,6 @@ struct DtArgs {
   int BN, nchunks, M1, stages;
   float inv_nnei;
   const float* T;  // in the fitting's row tiles: [tile][4][M1][128]
-  const int* perm_atom;
   float* dT;  // [row][4][M1]
   float* dD;  // [row][16 M1] or null
   float* part;     // split partials (gridDim.y > 1)
@@ -743,7 +742,6 @@ void launch_fit_tc(cudaStream_t st, const FitTcPlan& p, int ntypes, int nloc, co
       d.M1 = p.dim / 16;
       d.inv_nnei = inv_nnei;
       d.T = T;
-      d.perm_atom = perm_atom;
       d.dT = dT;
       d.dD = dD;
       d.part = b.dt_part;
