@@ -33,7 +33,9 @@ EXPORTS = [
     "b200dp_set_neighbor_reuse", "b200dp_neighbor_stats", "b200dp_fold_export", "b200dp_fold_connect", "b200dp_fold_origins",
     "b200dp_compute_device_fold", "b200dp_fold_finish", "b200dp_halo_publish", "b200dp_halo_gather",
     "b200dp_stage_times", "b200dp_kernel_launches", "b200dp_selftest_mma", "b200dp_build_nlist_noalloc",
-    "b200dp_direct_bind", "b200dp_direct_energy_force", "b200dp_md_params_default", "b200dp_md_create",
+    "b200dp_direct_bind", "b200dp_direct_energy_force", "b200dp_direct_destination_only_ready",
+    "b200dp_bind_direct_neighbor_view", "b200dp_get_direct_neighbor_view", "b200dp_direct_set_need_virial",
+    "b200dp_direct_fp32_global_virial_pointer", "b200dp_md_params_default", "b200dp_md_create",
     "b200dp_md_run", "b200dp_md_thermo", "b200dp_md_state", "b200dp_md_destroy", "b200dp_md_snapshot_bytes",
     "b200dp_md_snapshot", "b200dp_md_restore", "b200dp_md_write_restart", "b200dp_md_read_restart",
 ]
@@ -47,6 +49,14 @@ class MDParams(ctypes.Structure):
                 ("seed", ctypes.c_ulonglong), ("mass", ctypes.c_double * 8), ("p_target", ctypes.c_double),
                 ("p_damp", ctypes.c_double), ("pchain", ctypes.c_int), ("rebuild_every", ctypes.c_int),
                 ("skin", ctypes.c_double), ("reserved", ctypes.c_int * 8)]
+
+
+class NeighborView(ctypes.Structure):
+    """b200dp_neighbor_view (the layout of the reference's DpaDirectNeighborView)."""
+    _fields_ = [("x", ctypes.c_void_p), ("model_to_atom", ctypes.c_void_p), ("candidate_atom", ctypes.c_void_p),
+                ("source", ctypes.c_void_p), ("stride_atom", ctypes.c_int64), ("stride_xyz", ctypes.c_int64),
+                ("node_count", ctypes.c_int64), ("cutoff_squared", ctypes.c_double),
+                ("inverse_distance_unit", ctypes.c_double)]
 
 
 class B200DPError(RuntimeError):
@@ -133,6 +143,16 @@ def load_library(path: str = LIB_PATH):
     L.b200dp_md_restore.argtypes = [_vp, _vp]
     L.b200dp_md_write_restart.argtypes = [_vp, ctypes.c_char_p]
     L.b200dp_md_read_restart.argtypes = [_vp, ctypes.c_char_p]
+    L.b200dp_direct_destination_only_ready.restype = ctypes.c_int
+    L.b200dp_direct_destination_only_ready.argtypes = [ctypes.c_int64, ctypes.c_int64]
+    L.b200dp_bind_direct_neighbor_view.argtypes = [ctypes.POINTER(NeighborView)]
+    L.b200dp_bind_direct_neighbor_view.restype = None
+    L.b200dp_get_direct_neighbor_view.argtypes = []
+    L.b200dp_get_direct_neighbor_view.restype = NeighborView
+    L.b200dp_direct_set_need_virial.argtypes = [ctypes.c_int, _vp]
+    L.b200dp_direct_set_need_virial.restype = None
+    L.b200dp_direct_fp32_global_virial_pointer.argtypes = []
+    L.b200dp_direct_fp32_global_virial_pointer.restype = ctypes.c_void_p
     L.b200dp_direct_energy_force.restype = ctypes.c_int
     L.b200dp_direct_energy_force.argtypes = [_vp, _vp, _vp, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                              _vp, _vp, _vp]
@@ -403,6 +423,34 @@ def direct_energy_force(atype_ptr, row_ptr_ptr, source_ptr, edge_vec_ptr, node_c
     return int(load_library().b200dp_direct_energy_force(atype_ptr or None, row_ptr_ptr or None, source_ptr or None,
                                                          edge_vec_ptr or None, node_count, nloc, edge_storage,
                                                          energy_ptr or None, force_ptr or None, virial_ptr or None))
+
+
+def direct_destination_only_ready(node_count: int, nloc: int) -> int:
+    return int(load_library().b200dp_direct_destination_only_ready(node_count, nloc))
+
+
+def bind_direct_neighbor_view(x_ptr=0, model_to_atom_ptr=0, candidate_atom_ptr=0, source_ptr=0, stride_atom=3,
+                              stride_xyz=1, node_count=0, cutoff_squared=0.0, inverse_distance_unit=1.0) -> None:
+    """Binds the raw-neighbour view (x_ptr = 0 unbinds)."""
+    L = load_library()
+    if not x_ptr:
+        L.b200dp_bind_direct_neighbor_view(None)
+        return
+    v = NeighborView(x_ptr, model_to_atom_ptr, candidate_atom_ptr, source_ptr, stride_atom, stride_xyz, node_count,
+                     cutoff_squared, inverse_distance_unit)
+    L.b200dp_bind_direct_neighbor_view(ctypes.byref(v))
+
+
+def get_direct_neighbor_view() -> NeighborView:
+    return load_library().b200dp_get_direct_neighbor_view()
+
+
+def direct_set_need_virial(need_virial: int, stream: int = 0) -> None:
+    load_library().b200dp_direct_set_need_virial(int(need_virial), stream or None)
+
+
+def direct_fp32_global_virial_pointer() -> int:
+    return int(load_library().b200dp_direct_fp32_global_virial_pointer() or 0)
 
 
 def kernel_launches() -> int:

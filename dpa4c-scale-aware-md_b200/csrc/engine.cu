@@ -10,6 +10,7 @@
 // force / widen (components/deepmd-op/overlays/op/pt/dpa4c/graph_compress.cu:1690-1900).
 #include <algorithm>
 #include <atomic>
+#include <mutex>
 #include <type_traits>
 #include <cmath>
 #include <cstdio>
@@ -1156,9 +1157,15 @@ b200dp_status Engine::compute_with_nlist(cudaStream_t st, int nloc, int nall, co
   return B200DP_OK;
 }
 
+namespace {
+__global__ void k_virial_f32(const double* __restrict__ v, float* __restrict__ out) {
+  if (threadIdx.x < 9) out[threadIdx.x] = (float)v[threadIdx.x];
+}
+}  // namespace
+
 b200dp_status Engine::compute_graph(cudaStream_t st, int n, const int64_t* d_atype64, const int64_t* d_row_ptr,
                                     const uint32_t* d_source, const float* d_edge_vec, double* d_atom_energy,
-                                    double* d_force, double* d_atom_virial) {
+                                    double* d_force, double* d_atom_virial, const RawGeometry& raw) {
   g_err_sink = &err;
   B200DP_CUDA_TRY(cudaSetDevice(opt.device));
   last_stream = st;
@@ -1171,7 +1178,7 @@ b200dp_status Engine::compute_graph(cudaStream_t st, int n, const int64_t* d_aty
   int* err_d = err_buf.as<int>();
   B200DP_CUDA_TRY(cudaMemsetAsync(err_d, 0, sizeof(int) * kErrCount, st));
   launch_format_graph(st, format_spec(n, n), d_atype64, d_row_ptr, d_source, d_edge_vec, graph_atype.as<int>(),
-                      nl_j.as<int>(), nl_code.as<int>(), nl_rij.as<double>(), nl_cnt.as<int>(), err_d);
+                      nl_j.as<int>(), nl_code.as<int>(), nl_rij.as<double>(), nl_cnt.as<int>(), err_d, raw);
   B200DP_CUDA_TRY(cudaGetLastError());
   double* d_scal = scalars.as<double>();
   rc = (opt.precision == B200DP_FP64)
@@ -1180,6 +1187,9 @@ b200dp_status Engine::compute_graph(cudaStream_t st, int n, const int64_t* d_aty
            : run_model<float>(st, n, n, graph_atype.as<int>(), d_force, d_atom_energy, d_atom_virial, d_scal,
                               d_scal + 1);
   if (rc != B200DP_OK) return rc;
+  B200DP_CUDA_TRY(vir32.ensure(sizeof(float) * 16));
+  count_launch();
+  k_virial_f32<<<1, 32, 0, st>>>(d_scal + 1, vir32.as<float>());
   B200DP_CUDA_TRY(cudaGetLastError());
   return B200DP_OK;
 }
@@ -1397,16 +1407,56 @@ b200dp_status b200dp_direct_bind(b200dp_engine* engine, void* stream) {
   return B200DP_OK;
 }
 
+// The raw-neighbour view bound by the graph builder and the virial request
+// (process-wide, as the reference keeps them).
+static std::mutex g_view_mutex;
+static b200dp_neighbor_view g_view{};
+static std::atomic<int> g_need_virial{1};
+
+int b200dp_direct_destination_only_ready(int64_t node_count, int64_t nloc) {
+  return (g_direct_engine.load() && node_count > 0 && nloc == node_count && node_count <= INT32_MAX) ? 1 : 0;
+}
+
+void b200dp_bind_direct_neighbor_view(const b200dp_neighbor_view* view) {
+  std::lock_guard<std::mutex> lock(g_view_mutex);
+  g_view = view ? *view : b200dp_neighbor_view{};
+}
+
+b200dp_neighbor_view b200dp_get_direct_neighbor_view(void) {
+  std::lock_guard<std::mutex> lock(g_view_mutex);
+  return g_view;
+}
+
+void b200dp_direct_set_need_virial(int need_virial, void* /*stream*/) { g_need_virial.store((need_virial & 3) != 0); }
+
+const float* b200dp_direct_fp32_global_virial_pointer(void) {
+  b200dp_engine* eng = g_direct_engine.load();
+  return eng ? eng->e.vir32.as<float>() : nullptr;
+}
+
 int b200dp_direct_energy_force(const int64_t* atype, const int64_t* row_ptr, const uint32_t* source,
                                const float* edge_vec, int64_t node_count, int64_t nloc, int64_t edge_storage,
                                double* energy_out, double* force_out, double* virial_out) {
   b200dp_engine* eng = g_direct_engine.load();
   if (!eng || nloc != node_count || node_count <= 0 || node_count > INT32_MAX || edge_storage < 0) return 0;
-  if (!atype || !row_ptr || !energy_out || !force_out || !virial_out || (edge_storage > 0 && (!source || !edge_vec)))
+  const b200dp_neighbor_view v = b200dp_get_direct_neighbor_view();
+  const bool raw = v.x && v.model_to_atom && v.candidate_atom && v.stride_atom > 0 && v.source == source &&
+                   v.node_count == node_count;
+  if (!atype || !row_ptr || !energy_out || !force_out || !virial_out ||
+      (edge_storage > 0 && (!source || (!edge_vec && !raw))))
     return 0;
+  b200dp::RawGeometry geo;
+  if (raw) {
+    geo.x = v.x;
+    geo.m2a = v.model_to_atom;
+    geo.cand = v.candidate_atom;
+    geo.sa = v.stride_atom;
+    geo.sx = v.stride_xyz;
+    geo.unit = v.inverse_distance_unit;
+  }
   const b200dp_status rc =
       eng->e.compute_graph(static_cast<cudaStream_t>(g_direct_stream.load()), (int)node_count, atype, row_ptr, source,
-                           edge_vec, energy_out, force_out, virial_out);
+                           edge_vec, energy_out, force_out, g_need_virial.load() ? virial_out : nullptr, geo);
   return rc == B200DP_OK ? 1 : 0;
 }
 

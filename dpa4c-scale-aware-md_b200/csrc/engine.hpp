@@ -140,7 +140,8 @@ struct Engine {
   // Canonical destination-major graph (n nodes, all local), device pointers.
   b200dp_status compute_graph(cudaStream_t st, int n, const int64_t* d_atype64, const int64_t* d_row_ptr,
                               const uint32_t* d_source, const float* d_edge_vec, double* d_atom_energy,
-                              double* d_force, double* d_atom_virial);
+                              double* d_force, double* d_atom_virial, const RawGeometry& raw = RawGeometry{});
+  DevBuf vir32;  // fp32 global virial of the last graph call
   b200dp_status compute_with_nlist(cudaStream_t st, int nloc, int nall, const double* d_coord, const int* d_atype,
                                    const b200dp_nlist* nl, double* d_energy, double* d_force, double* d_virial,
                                    double* d_atom_energy, double* d_atom_virial);

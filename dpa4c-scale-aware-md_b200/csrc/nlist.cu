@@ -883,7 +883,7 @@ __global__ void __launch_bounds__(kFmtWarps * 32)
     k_format_graph(FormatSpec f, const int64_t* __restrict__ atype64, const int64_t* __restrict__ row_ptr,
                    const uint32_t* __restrict__ source, const float* __restrict__ edge_vec, int* __restrict__ atype32,
                    int* __restrict__ nl_j, int* __restrict__ nl_code, double* __restrict__ nl_rij,
-                   int* __restrict__ nl_cnt, int* __restrict__ err) {
+                   int* __restrict__ nl_cnt, int* __restrict__ err, RawGeometry raw) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int i = blockIdx.x * kFmtWarps + warp;
@@ -896,6 +896,18 @@ __global__ void __launch_bounds__(kFmtWarps * 32)
   const CandBuf b = cand_buf(smem, warp, f);
   const unsigned lt_mask = (1u << lane) - 1u;
   const int64_t beg = row_ptr[i], end = row_ptr[i + 1];
+  // the edge vector: the graph's fp32 one, or recomputed in fp64 from the bound positions
+  const double* xi = raw.x ? raw.x + (long long)raw.m2a[i] * raw.sa : nullptr;
+  auto edge = [&](int64_t k, double (&r)[3]) {
+    if (raw.x) {
+      const double* xj = raw.x + (long long)raw.cand[k] * raw.sa;
+#pragma unroll
+      for (int c = 0; c < 3; ++c) r[c] = dmul(dsub(xj[c * raw.sx], xi[c * raw.sx]), raw.unit);
+    } else {
+#pragma unroll
+      for (int c = 0; c < 3; ++c) r[c] = (double)edge_vec[3 * k + c];
+    }
+  };
   int ncnt[kMaxTypes];
 #pragma unroll
   for (int t = 0; t < kMaxTypes; ++t) ncnt[t] = 0;
@@ -908,8 +920,7 @@ __global__ void __launch_bounds__(kFmtWarps * 32)
       if (src < (uint32_t)f.nall) {
         j = (int)src;
         double r[3];
-#pragma unroll
-        for (int c = 0; c < 3; ++c) r[c] = (double)edge_vec[3 * k + c];
+        edge(k, r);
         r2 = dadd(dadd(dmul(r[0], r[0]), dmul(r[1], r[1])), dmul(r[2], r[2]));
         const int64_t t64 = atype64[j];
         const bool type_ok = (t64 >= 0 && t64 < f.ntypes);
@@ -923,21 +934,19 @@ __global__ void __launch_bounds__(kFmtWarps * 32)
   }
   __syncwarp();
   emit_row(f, i, b, ncnt, lane, nl_j, nl_code, nl_rij, nl_cnt, err, [&](int src, int, double (&r)[3]) {
-    const int64_t k = beg + src;
-#pragma unroll
-    for (int c = 0; c < 3; ++c) r[c] = (double)edge_vec[3 * k + c];
+    edge(beg + src, r);
   });
 }
 
 void launch_format_graph(cudaStream_t st, const FormatSpec& f, const int64_t* atype64, const int64_t* row_ptr,
                          const uint32_t* source, const float* edge_vec, int* atype32, int* nl_j, int* nl_code,
-                         double* nl_rij, int* nl_cnt, int* err) {
+                         double* nl_rij, int* nl_cnt, int* err, const RawGeometry& raw) {
   if (f.nloc <= 0) return;
   const size_t smem = format_smem_bytes(f);
   format_attr(k_format_graph, smem);
   count_launch();
   k_format_graph<<<(f.nloc + kFmtWarps - 1) / kFmtWarps, kFmtWarps * 32, smem, st>>>(
-      f, atype64, row_ptr, source, edge_vec, atype32, nl_j, nl_code, nl_rij, nl_cnt, err);
+      f, atype64, row_ptr, source, edge_vec, atype32, nl_j, nl_code, nl_rij, nl_cnt, err, raw);
 }
 
 void launch_format_candidates(cudaStream_t st, const FormatSpec& f, const double* coord, const int* atype,

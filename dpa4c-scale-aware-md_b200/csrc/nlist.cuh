@@ -99,9 +99,20 @@ void launch_format_verlet(cudaStream_t st, const FormatSpec& f, const GridSpec& 
 // Formats a caller-provided candidate list (LAMMPS full list in CSR form).
 // Formats a canonical destination-major edge graph (fp32 edge vectors) and
 // converts the int64 node types to int32 (invalid types become -1).
+// Raw-neighbour geometry for the graph formatter: when x is set, edge k of
+// row i is (x[cand[k]] - x[m2a[i]]) * unit in fp64 (component c of atom a at
+// x[a * sa + c * sx]) instead of the graph's fp32 edge vector; candidates past
+// the cutoff are dropped as usual.
+struct RawGeometry {
+  const double* x = nullptr;
+  const int* m2a = nullptr;
+  const int* cand = nullptr;
+  long long sa = 0, sx = 0;
+  double unit = 1.0;
+};
 void launch_format_graph(cudaStream_t st, const FormatSpec& f, const int64_t* atype64, const int64_t* row_ptr,
                          const uint32_t* source, const float* edge_vec, int* atype32, int* nl_j, int* nl_code,
-                         double* nl_rij, int* nl_cnt, int* err);
+                         double* nl_rij, int* nl_cnt, int* err, const RawGeometry& raw = RawGeometry{});
 void launch_format_candidates(cudaStream_t st, const FormatSpec& f, const double* coord, const int* atype,
                               const int* ilist, const int* cand_start, const int* cand, int* nl_j, int* nl_code,
                               double* nl_rij, int* nl_cnt, int* err);

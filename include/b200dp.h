@@ -209,6 +209,45 @@ int b200dp_direct_energy_force(const int64_t* atype, const int64_t* row_ptr, con
                                const float* edge_vec, int64_t node_count, int64_t nloc, int64_t edge_storage,
                                double* energy_out, double* force_out, double* virial_out);
 
+/* Companions of the direct entry, as the LAMMPS Kokkos graph builder and pair
+ * style resolve them (components/lammps-deepmd-plugin/src/
+ * compact_canonical_graph_kokkos.h:280-300, 825-845; pair_deepmd_kokkos.cpp:
+ * 640-665, 725-745):
+ *   b200dp_direct_destination_only_ready  1 when an engine is bound and the
+ *     call would be handled (node_count > 0, nloc == node_count): the builder
+ *     may then omit the source-major CSR (replaces
+ *     dpa_direct_destination_only_ready, graph_compress.cu:1804-1815);
+ *   b200dp_bind_direct_neighbor_view / b200dp_get_direct_neighbor_view  the
+ *     raw-neighbour view (same fields as DpaDirectNeighborView,
+ *     direct_neighbor_view.h:1-14): positions x (component c of atom a at
+ *     x[a * stride_atom + c * stride_xyz]), model node -> atom, per edge the
+ *     candidate atom (ghost images included) and the graph's source array.  While
+ *     a view is bound whose source pointer and node count match the call, the
+ *     direct entry recomputes every edge vector in fp64 as
+ *     (x[candidate] - x[model_to_atom[node]]) * inverse_distance_unit and keeps
+ *     the edges within the model's cutoff (so the graph may carry skin
+ *     candidates); a null view unbinds;
+ *   b200dp_direct_set_need_virial  need_virial & 3 == 0: the next direct calls
+ *     leave virial_out untouched and skip the per-atom virial (replaces
+ *     dpa_chain_set_need_virial_stream, src/entry/chain_entry.cu:29-41; read at
+ *     call time, so a captured graph keeps the request it was captured with);
+ *   b200dp_direct_fp32_global_virial_pointer  device pointer to the 9-float
+ *     global virial of the last direct call, stable across calls (replaces
+ *     dpa_direct_fp32_global_virial_pointer, graph_compress.cu:1512-1517). */
+typedef struct b200dp_neighbor_view {
+  const double* x;
+  const int* model_to_atom;
+  const int* candidate_atom;
+  const uint32_t* source;
+  int64_t stride_atom, stride_xyz, node_count;
+  double cutoff_squared, inverse_distance_unit;
+} b200dp_neighbor_view;
+int b200dp_direct_destination_only_ready(int64_t node_count, int64_t nloc);
+void b200dp_bind_direct_neighbor_view(const b200dp_neighbor_view* view);
+b200dp_neighbor_view b200dp_get_direct_neighbor_view(void);
+void b200dp_direct_set_need_virial(int need_virial, void* stream);
+const float* b200dp_direct_fp32_global_virial_pointer(void);
+
 /* ------------------------------------------------------------------ MD
  * Molecular-dynamics driver around an engine (metal units: Angstrom, ps,
  * g/mol, eV, K, bar).  Velocity Verlet (NVE), with a Nose-Hoover chain
