@@ -62,3 +62,33 @@ def test_null_engine_is_rejected():
     L = b200dp.load_library()
     assert L.b200dp_check(None) == 1
     assert L.b200dp_compute_host(None, 0, 0, None, None, None, None, None, None, None, None) == 1
+
+
+def test_header_is_plain_c_and_links(tmp_path):
+    """A C11 translation unit that takes the address of every declared function compiles
+    with warnings as errors and links against the library (what a cgo / plain-C binding
+    needs); the program runs without touching a GPU."""
+    import shutil
+    import subprocess
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    names = declared_functions()
+    src = tmp_path / "abi.c"
+    src.write_text('#include <stdio.h>\n#include "b200dp.h"\n'
+                   "typedef void (*fn)(void);\n"
+                   "int main(void) {\n  fn table[] = {\n"
+                   + "".join(f"    (fn){n},\n" for n in names)
+                   + "  };\n  int n = 0;\n"
+                   "  for (size_t i = 0; i < sizeof(table) / sizeof(table[0]); ++i) n += table[i] != 0;\n"
+                   '  printf("%d\\n", n);\n  return 0;\n}\n')
+    lib_dir = os.path.dirname(b200dp.LIB_PATH)
+    exe = tmp_path / "abi"
+    r = subprocess.run([cc, "-std=c11", "-Wall", "-Wextra", "-Werror", "-I", os.path.join(ROOT, "include"),
+                        str(src), "-o", str(exe), "-L", lib_dir, "-lb200dp", f"-Wl,-rpath,{lib_dir}",
+                        "-Wl,--allow-shlib-undefined"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert out.returncode == 0, out.stderr
+    assert int(out.stdout.strip()) == len(names)
