@@ -77,6 +77,8 @@ def parse():
     ap.add_argument("--impl", default="b200dp", choices=["b200dp", "reference"])
     ap.add_argument("--precision", default="mixed", choices=["mixed", "fp64"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="headline device loop only (no e2e, fp64, MD, C8L2 or CPU legs): the ncu captures' command")
     ap.add_argument("--sweep", action="store_true", help="measure the five configurations (see module doc)")
     ap.add_argument("--only", default="", help="--sweep: comma-separated labels to run")
     ap.add_argument("--reverse", default="peer", choices=["peer", "nccl"],
@@ -181,43 +183,54 @@ def ncu_traffic(kernel: str):
 
 
 # ----------------------------------------------------------------- arms
-def cpu_oracle_rate(model_file, system, threads=None, repeats=1):
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle
+class OracleArm:
+    """The CPU oracle loaded once: model read and first touch happen here, outside any timing."""
 
-    used = oracle.set_threads(threads or os.cpu_count() or 1)
-    o = oracle.Oracle(model_file)
-    o.compute(system.coord[:192], system.atype[:192], None)  # load / first-touch
-    t0 = time.perf_counter()
-    for _ in range(repeats):
-        o.compute(system.coord, system.atype, system.box, atomic=False)
-    dt = (time.perf_counter() - t0) / repeats
-    return system.natoms / dt, used, dt
+    def __init__(self, model_file, threads=None):
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle
+
+        self.cores = oracle.set_threads(threads or os.cpu_count() or 1)
+        self.o = oracle.Oracle(model_file)
+        s0 = systems.config0()
+        self.o.compute(s0.coord, s0.atype, s0.box, atomic=False)
+
+    def evaluate(self, system):
+        """Seconds for one full E+F+virial evaluation of `system`."""
+        t0 = time.perf_counter()
+        self.o.compute(system.coord, system.atype, system.box, atomic=False)
+        return time.perf_counter() - t0
+
+
+def bench_config(world):
+    """The `config` dict shared by both arms at N GPUs (same keys and values): 4096 H2O per GPU."""
+    return {"workload": WORKLOAD, "atoms_per_gpu": 12288, "global_atoms": 12288 * world,
+            "model": "water se_e2_a-type (sel [46,92], embedding [25,50,100], axis 16, fitting [240]*3), random init",
+            "l2": "GPU arm: flushed before every timed step (256 MB write), flush outside the events"}
 
 
 def run_reference(args, world, rank):
     if rank != 0:
         return
-    system = systems.config1()
-    mp = model_path("water")
+    system, _ = global_system(1, 0)
+    arm = OracleArm(model_path("water"))
     for _ in range(args.warmup):
-        cpu_oracle_rate(mp, system)
-    t0 = time.perf_counter()
-    used = None
-    for _ in range(args.steps):
-        _, used, _ = cpu_oracle_rate(mp, system)
-    dt = (time.perf_counter() - t0) / args.steps
+        arm.evaluate(system)
+    secs = [arm.evaluate(system) for _ in range(args.steps)]
+    dt = sum(secs) / len(secs)
     value = system.natoms / dt
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "atom-steps/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic (seeded)",
-        "config": {"workload": WORKLOAD, "atoms": system.natoms, "model": "water se_e2_a-type, random init"},
-        "cpu_baseline": {"value": value, "unit": "atom-steps/s", "cores": used, "kind": "port",
-                         "sample": "one full evaluation of the 12,288-atom system per step"},
+        "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic (seeded water, random-init weights)",
+        "config": bench_config(world),
+        "cpu_baseline": {"value": value, "unit": "atom-steps/s", "cores": arm.cores, "kind": "port",
+                         "sample": "one full evaluation of the 12,288-atom system per step (model loaded and "
+                                   "warmed up before the timed steps)"},
         "e2e": {"value": value, "unit": "atom-steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference has no CPU or NVIDIA implementation of this path; the reference arm is the "
-                "C++ fp64 restatement (oracle/) on all host threads",
+                "C++ fp64 restatement (oracle/) on all host threads; at N > 1 rank 0 times one 12,288-atom "
+                "evaluation per step (the CPU cost per atom does not depend on the box size)",
     }
     print(json.dumps(line), flush=True)
 
@@ -409,26 +422,41 @@ def run_b200dp(args, world, rank, local):
     bwd_ms = float(stage_ms[3])
     achieved = fl["descriptor_bwd"] / (bwd_ms / 1e3) / 1e12 if bwd_ms > 0 else 0.0
     peak = float(pk["bf16_tflops"])
-    roofline = {"kernel": "k_embed_bwd_tc" if prec == b200dp.MIXED else "k_descriptor_bwd", "bound": "tensor",
+    mixed = prec == b200dp.MIXED
+    roofline = {"kernel": "k_embed_bwd_tc" if mixed else "k_descriptor_bwd<double>", "bound": "tensor",
                 "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                "traffic": ncu_traffic("embed_bwd_tc" if prec == b200dp.MIXED else "descriptor_bwd"),
+                "traffic": ncu_traffic("embed_bwd_tc" if mixed else "descriptor_bwd_f64"),
                 "peak_source": f"{pk_kind} bf16 burst (MEASURED_PEAKS.json)" if pk_kind == "measured"
                 else "fallback 1.59 PFLOP/s",
                 "flops_per_launch": fl["descriptor_bwd"], "avg_launch_ms": bwd_ms,
                 "note": "algorithmic FLOPs of the embedding backward over the CUDA-event time of its stage"}
+    if mixed:
+        # the pipe that bounds the embedding kernels: the multi-function unit (MUFU / XU), 16 results per
+        # clock per SM; every tanh feature of every edge costs one ex2 and one rcp, and the backward
+        # recomputes all layers
+        mufu = 2 * edges * sum(m.emb)
+        mhz = (clocks or {}).get("sm_mhz") or float(pk.get("sm_max_mhz", 1965.0))
+        xu_peak = 148 * 16 * mhz * 1e6
+        roofline["xu"] = {"mufu_ops_per_launch": mufu, "sm_mhz": mhz, "peak_ops_per_s": xu_peak,
+                          "frac": mufu / (bwd_ms / 1e3) / xu_peak if bwd_ms > 0 else 0.0,
+                          "note": "MUFU ops (2 per tanh feature per edge) over the stage time, against "
+                                  "148 SMs x 16 per clock at the median SM clock of the timed region"}
     # e2e through the public API with pinned host buffers
     e2e = None
-    try:
-        e2e = e2e_loop(dp, w, system, args.steps, max(1, min(args.warmup, 3)), torch, dist)
-    except Exception as ex:  # report, never hide
-        e2e = {"error": repr(ex)}
+    if args.profile:
+        e2e = {"skipped": "--profile"}
+    else:
+        try:
+            e2e = e2e_loop(dp, w, system, args.steps, max(1, min(args.warmup, 3)), torch, dist)
+        except Exception as ex:  # report, never hide
+            e2e = {"error": repr(ex)}
     if "seconds" in e2e:
         secs = max_over_ranks(e2e["seconds"])
         e2e["value"] = w.total * args.steps / secs
         e2e["seconds"] = secs
     # fp64 mode (secondary line item)
     fp64 = None
-    if prec == b200dp.MIXED:
+    if prec == b200dp.MIXED and not args.profile:
         dp64 = b200dp.DeepPot(mp, precision=b200dp.FP64, device=local)
         w64 = workload(dp64)
         k64 = max(2, min(args.steps, 5))
@@ -442,7 +470,7 @@ def run_b200dp(args, world, rank, local):
     # MD loop (N = 1): the same force call inside the device MD driver (NVT Nose-Hoover chain,
     # velocity Verlet), reported beside the force-call metric
     md_loop = None
-    if world == 1 and prec == b200dp.MIXED:
+    if world == 1 and prec == b200dp.MIXED and not args.profile:
         try:
             md = b200dp.MD(dp, system.coord, system.atype, system.box, [15.9994, 1.00794], dt=0.0005,
                            ensemble=b200dp.NVT, t_init=300.0, t_target=300.0, t_damp=0.05, seed=1)
@@ -462,7 +490,7 @@ def run_b200dp(args, world, rank, local):
     # C8L2 profile (the reference's production descriptor), secondary line item at N = 1:
     # the same device loop on the headline water system and on a 98,304-atom water box
     c8 = None
-    if world == 1 and prec == b200dp.MIXED:
+    if world == 1 and prec == b200dp.MIXED and not args.profile:
         try:
             c8 = {"model": "C8L2: 8 channels, lmax 2, 70 invariants, 70-96-96-96 SiLU fitting (random-init)",
                   "dtype": "f32 (the reference's precision for this model)", "unit": "atom-steps/s"}
@@ -484,10 +512,12 @@ def run_b200dp(args, world, rank, local):
         except Exception as ex:  # report, never hide
             c8 = {"error": repr(ex)}
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rate, used, dt = cpu_oracle_rate(mp, system)
-        cpu = {"value": rate, "unit": "atom-steps/s", "cores": used, "kind": "port",
-               "sample": f"one full evaluation of the 12,288-atom system ({dt:.2f} s), fp64 C++ oracle, OpenMP"}
+    if rank == 0 and world == 1 and not (args.no_cpu_baseline or args.profile):
+        arm = OracleArm(mp)
+        dt = min(arm.evaluate(system) for _ in range(2))
+        cpu = {"value": system.natoms / dt, "unit": "atom-steps/s", "cores": arm.cores, "kind": "port",
+               "sample": f"best of two full evaluations of the 12,288-atom system ({dt:.2f} s each), fp64 C++ "
+                         "oracle, OpenMP, model loaded beforehand"}
     if world > 1:
         rev = ("ghost forces added into the owners' accumulators over NVLink peer memory"
                if args.reverse == "peer" else "ghost forces folded back by NCCL send/recv")
@@ -502,9 +532,9 @@ def run_b200dp(args, world, rank, local):
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32-mixed" if prec == b200dp.MIXED else "f64",
             "data": "synthetic (seeded water, random-init weights)",
-            "config": {"workload": WORKLOAD, "atoms": n, "edges": edges, "model": "water se_e2_a-type",
-                       "precision": args.precision, "parallelism": parallelism, **cfg_extra,
-                       "l2": "flushed before every timed step (256 MB write), flush outside the events"},
+            "config": bench_config(world),
+            "setup": {"atoms_rank0": n, "edges_rank0": edges, "precision": args.precision,
+                      "parallelism": parallelism, **cfg_extra},
             "stage_ms": {k: round(float(q), 4) for k, q in
                          zip(["neighbour", "descriptor_fwd", "fitting", "descriptor_bwd", "assembly"], stage_ms)},
             "stage_note": "stage times from a separate pass with the engine's stage events (rank 0)",

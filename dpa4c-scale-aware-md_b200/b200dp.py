@@ -129,7 +129,7 @@ def load_library(path: str = LIB_PATH):
                                       ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_float),
                                       ctypes.POINTER(ctypes.c_float)]
     L.b200dp_build_nlist_noalloc.argtypes = [_vp, ctypes.c_int, ctypes.c_int, _vp, _vp, _dp, _dp, ctypes.c_double,
-                                             ctypes.c_int, _ip, _vp, _vp, _vp]
+                                             ctypes.c_int, _ip, _vp, _vp, _vp, ctypes.POINTER(ctypes.c_longlong)]
     L.b200dp_kernel_launches.argtypes = []
     L.b200dp_kernel_launches.restype = ctypes.c_longlong
     L.b200dp_direct_bind.argtypes = [_vp, _vp]

@@ -11,6 +11,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstring>
 
@@ -41,9 +42,11 @@ constexpr size_t kScratchBytes = kOffErr + align256(sizeof(int) * kErrCount);  /
 // device symbol: its device address comes from cudaGetSymbolAddress below.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 
-// Device address of g_noalloc_scratch, looked up once per device.
+// Device address of g_noalloc_scratch, looked up once per device.  Host
+// threads may race on the first lookup; each finds the same address, and the
+// atomic keeps the cache itself free of a data race.
 constexpr int kMaxDevices = 64;
-void* g_scratch_ptr[kMaxDevices] = {nullptr};
+std::atomic<void*> g_scratch_ptr[kMaxDevices];
 
 }  // namespace
 }  // namespace b200dp
@@ -51,9 +54,10 @@ void* g_scratch_ptr[kMaxDevices] = {nullptr};
 extern "C" b200dp_status b200dp_build_nlist_noalloc(void* stream, int nlocal, int nghost, const double* d_coord,
                                                      const int* d_atype, const double* box, const double* region,
                                                      double rcut, int ntypes, const int* sel, int* d_nlist,
-                                                     int* d_image, double* d_rij) {
+                                                     int* d_image, double* d_rij, long long* sel_overflow) {
   using namespace b200dp;
   const int nall = nlocal + nghost;
+  if (sel_overflow) *sel_overflow = 0;
   if (nlocal < 0 || nghost < 0 || ntypes <= 0 || ntypes > kNoAllocMaxTypes || !sel || !(rcut > 0) ||
       (nall > 0 && (!d_coord || !d_atype)) || (nlocal > 0 && (!d_nlist || !d_image || !d_rij))) {
     return B200DP_ERR_INVALID;
@@ -68,13 +72,15 @@ extern "C" b200dp_status b200dp_build_nlist_noalloc(void* stream, int nlocal, in
   }
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return B200DP_ERR_CUDA;
-  // First call on this device: look up the scratch address with the device current.
-  if (!g_scratch_ptr[dev]) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return B200DP_ERR_CUDA;
-    g_scratch_ptr[dev] = p;
+  // First call on this device: look up the scratch address with the device
+  // current.  Under CUDA's lazy module loading this lookup is also what loads
+  // the module holding the array, i.e. the moment its memory is reserved.
+  void* sp = g_scratch_ptr[dev].load(std::memory_order_acquire);
+  if (!sp) {
+    if (cudaGetSymbolAddress(&sp, g_noalloc_scratch) != cudaSuccess || !sp) return B200DP_ERR_CUDA;
+    g_scratch_ptr[dev].store(sp, std::memory_order_release);
   }
-  unsigned char* base = static_cast<unsigned char*>(g_scratch_ptr[dev]);
+  unsigned char* base = static_cast<unsigned char*>(sp);
   double* xw = reinterpret_cast<double*>(base + kOffXw);
   int* cell_of = reinterpret_cast<int*>(base + kOffCellOf);
   int* cell_count = reinterpret_cast<int*>(base + kOffCellCount);
@@ -126,6 +132,7 @@ extern "C" b200dp_status b200dp_build_nlist_noalloc(void* stream, int nlocal, in
   if (cudaStreamSynchronize(st) != cudaSuccess) return B200DP_ERR_CUDA;
   int h[kErrCount] = {0};
   if (cudaMemcpy(h, err, sizeof(h), cudaMemcpyDeviceToHost) != cudaSuccess) return B200DP_ERR_CUDA;
+  if (sel_overflow) *sel_overflow = h[kErrSelOverflow];
   if (h[kErrBadType]) return B200DP_ERR_BAD_TYPE;
   if (h[kErrCandCapacity]) return B200DP_ERR_CAPACITY;
   return B200DP_OK;

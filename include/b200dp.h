@@ -175,15 +175,25 @@ b200dp_status b200dp_selftest_mma(int K, int N, int a_mn_major, int b_mn_major, 
  * all caller-owned device buffers.  Scratch lives in one static device array
  * of about 6.5 MiB that every GPU loading the library keeps until exit; it
  * limits nlocal + nghost to 65536 (larger inputs return B200DP_ERR_CAPACITY)
- * and the binning grid to 65536 cells (coarsened automatically).  The first
- * call on a device looks up that array's device address (cudaGetSymbolAddress)
- * with the device current; make that first call before any stream capture.
- * All calls share the array, so calls that overlap on the GPU (other streams,
- * other host threads) race; the call synchronises `stream` before returning
- * and reports bad types / candidate overflow through its status. */
+ * and the binning grid to 65536 cells (coarsened automatically).
+ * First call on a device: it looks up that array's device address
+ * (cudaGetSymbolAddress) with the device current, and under CUDA's lazy
+ * module loading (the default since CUDA 12.2) that lookup is what loads the
+ * module holding the array, so the array's memory is reserved then, not when
+ * the library is opened.  Make that first call (nlocal = nghost = 0 is
+ * enough) before the caller's pool reserves the device's memory and before
+ * any stream capture; later calls reserve nothing.
+ * Every call synchronises `stream` and reads the device's status counters
+ * back with a blocking copy before it returns.  All calls share the array, so
+ * calls that overlap on the GPU (other streams, other host threads) race.
+ * Status: B200DP_ERR_BAD_TYPE / B200DP_ERR_CAPACITY as for the engine.  A type
+ * section holding more than sel neighbours keeps its nearest sel (as DeePMD
+ * does); *sel_overflow (optional, may be NULL) receives the number of
+ * candidates dropped that way, 0 when no row was truncated. */
 b200dp_status b200dp_build_nlist_noalloc(void* stream, int nlocal, int nghost, const double* d_coord,
                                          const int* d_atype, const double* box, const double* region, double rcut,
-                                         int ntypes, const int* sel, int* d_nlist, int* d_image, double* d_rij);
+                                         int ntypes, const int* sel, int* d_nlist, int* d_image, double* d_rij,
+                                         long long* sel_overflow);
 /* Engine and CUDA stream used by b200dp_direct_energy_force (process-wide;
  * the reference's counterpart is the direct-engine cache primed at model load,
  * components/deepmd-op/overlays/op/pt/dpa4c/graph_compress.cu:1451-1476).

@@ -229,3 +229,34 @@ def test_restart_file_in_a_new_run(model_dir, tmp_path):
     assert e.value.status == 2  # B200DP_ERR_IO
     for o in (md2, md3, dp2, dp3):
         o.close()
+
+
+def test_nve_drift_config1_mixed(model_dir):
+    """The reference's NVE limit (data/numeric-tolerances.json:8,
+    nve_drift_eV_per_atom_per_ps <= 6e-6) on config 1: 12,288 water atoms in
+    mixed precision, 2,000 steps of 0.5 fs (1 ps) with skin neighbour reuse
+    (2 A, candidates rebuilt every 10 steps).  The drift is the slope of a
+    least-squares line through the conserved energy sampled every 20 steps.
+    The random-init model holds no bonds, so every atom gets the oxygen mass:
+    with hydrogen masses free-flying atoms would cross into the 1/r core of
+    the environment rows within the picosecond, which tests the time step,
+    not the force path."""
+    s = systems.config1()
+    dp = b200dp.DeepPot(str(model_dir / "water.b2dp"), precision=b200dp.MIXED)
+    dt = 0.0005
+    md = b200dp.MD(dp, s.coord, s.atype, s.box, [15.9994, 15.9994], dt=dt, ensemble=b200dp.NVE, t_init=300.0,
+                   seed=21, skin=2.0, rebuild_every=10)
+    every, nsteps = 20, 2000
+    t, e = [0.0], [md.thermo()["conserved"]]
+    for k in range(nsteps // every):
+        md.run(every)
+        t.append((k + 1) * every * dt)
+        e.append(md.thermo()["conserved"])
+    dp.check()
+    md.close()
+    dp.close()
+    t, e = np.array(t), np.array(e) / s.natoms
+    slope = np.polyfit(t, e, 1)[0]
+    assert abs(slope) <= 6e-6, slope
+    # the excursion bound of test_conserved_energy, per atom
+    assert np.abs(e - e[0]).max() < 0.05 * BOLTZ * 300.0 / 100
