@@ -32,6 +32,7 @@ EXPORTS = [
     "b200dp_sel_overflow_count", "b200dp_last_nlist", "b200dp_last_descriptor", "b200dp_set_stage_timing",
     "b200dp_set_neighbor_reuse", "b200dp_neighbor_stats", "b200dp_fold_export", "b200dp_fold_connect", "b200dp_fold_origins",
     "b200dp_compute_device_fold", "b200dp_fold_finish", "b200dp_halo_publish", "b200dp_halo_gather",
+    "b200dp_peer_reduce",
     "b200dp_stage_times", "b200dp_kernel_launches", "b200dp_selftest_mma", "b200dp_build_nlist_noalloc",
     "b200dp_direct_bind", "b200dp_direct_energy_force", "b200dp_direct_destination_only_ready",
     "b200dp_bind_direct_neighbor_view", "b200dp_get_direct_neighbor_view", "b200dp_direct_set_need_virial",
@@ -124,6 +125,7 @@ def load_library(path: str = LIB_PATH):
     L.b200dp_halo_gather.argtypes = [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp]
     L.b200dp_compute_device_fold.argtypes = [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp, _vp, _dp, _vp, _vp, _vp]
     L.b200dp_fold_finish.argtypes = [_vp, _vp, ctypes.c_int, _vp]
+    L.b200dp_peer_reduce.argtypes = [_vp, _vp, ctypes.c_int, _vp, _vp, ctypes.c_longlong]
     L.b200dp_stage_times.argtypes = [_vp, ctypes.POINTER(ctypes.c_float)]
     L.b200dp_selftest_mma.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                       ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_float),
@@ -297,6 +299,11 @@ class DeepPot:
 
     def fold_finish(self, stream: int, nloc: int, force_ptr: int) -> None:
         self._raise(self.L.b200dp_fold_finish(self.h, stream or None, int(nloc), force_ptr))
+
+    def peer_reduce(self, stream: int, nv: int, in_ptr: int = 0, out_ptr: int = 0, max_polls: int = 0) -> None:
+        """Device-side rendezvous of the ranks (sum of nv doubles in rank order, or a barrier for nv = 0)."""
+        self._raise(self.L.b200dp_peer_reduce(self.h, stream or None, int(nv), in_ptr or None, out_ptr or None,
+                                              int(max_polls)))
 
     def neighbor_stats(self) -> dict:
         """Candidate builds so far: scheduled and triggered by the displacement check."""

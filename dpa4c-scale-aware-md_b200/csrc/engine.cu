@@ -855,6 +855,15 @@ b200dp_status Engine::check() {
   B200DP_CUDA_TRY(cudaMemcpy(h, err_buf.ptr, sizeof(h), cudaMemcpyDeviceToHost));
   int stale = 0;
   if (vl_stale.ptr) B200DP_CUDA_TRY(cudaMemcpy(&stale, vl_stale.ptr, sizeof(int), cudaMemcpyDeviceToHost));
+  if (pf_sync_err.ptr) {
+    int timeouts = 0;
+    B200DP_CUDA_TRY(cudaMemcpy(&timeouts, pf_sync_err.ptr, sizeof(int), cudaMemcpyDeviceToHost));
+    if (timeouts) {
+      B200DP_CUDA_TRY(cudaMemset(pf_sync_err.ptr, 0, sizeof(int)));
+      err = "a peer rendezvous gave up waiting for another rank (bounded wait expired)";
+      return B200DP_ERR_PEER_TIMEOUT;
+    }
+  }
   return check_flags(h, stale);
 }
 
@@ -904,12 +913,17 @@ b200dp_status Engine::fold_export(int cap, void* handle) {
   if (!pf_buf) {
     const size_t acc = sizeof(unsigned long long) * 6 * (size_t)cap;
     const size_t nf = (sizeof(unsigned) * (size_t)cap + 255) & ~(size_t)255;
-    const size_t xb = sizeof(double) * 3 * (size_t)cap;
-    B200DP_CUDA_TRY(cudaMalloc(&pf_buf, acc + nf + xb));
-    B200DP_CUDA_TRY(cudaMemset(pf_buf, 0, acc + nf + xb));
+    const size_t xb = (sizeof(double) * 3 * (size_t)cap + 255) & ~(size_t)255;
+    B200DP_CUDA_TRY(cudaMalloc(&pf_buf, acc + nf + xb + kPeerSyncBytes));
+    B200DP_CUDA_TRY(cudaMemset(pf_buf, 0, acc + nf + xb + kPeerSyncBytes));
+    B200DP_CUDA_TRY(pf_seq.ensure(sizeof(unsigned long long)));
+    B200DP_CUDA_TRY(cudaMemset(pf_seq.ptr, 0, sizeof(unsigned long long)));
+    B200DP_CUDA_TRY(pf_sync_err.ensure(sizeof(int)));
+    B200DP_CUDA_TRY(cudaMemset(pf_sync_err.ptr, 0, sizeof(int)));
     B200DP_CUDA_TRY(cudaDeviceSynchronize());
     pf_off_nf = acc;
     pf_off_x = acc + nf;
+    pf_off_sync = acc + nf + xb;
     pf_cap = cap;
   }
   cudaIpcMemHandle_t h;
@@ -929,8 +943,12 @@ b200dp_status Engine::fold_connect(int nranks, int rank, const void* handles) {
   pf_opened.clear();
   std::vector<unsigned char*> ptrs(nranks);
   const auto* hs = static_cast<const cudaIpcMemHandle_t*>(handles);
+  cudaIpcMemHandle_t own;
+  B200DP_CUDA_TRY(cudaIpcGetMemHandle(&own, pf_buf));
   for (int r = 0; r < nranks; ++r) {
-    if (r == rank) {
+    // this rank's own buffer (its handle may also stand for another rank: one
+    // process then plays both, e.g. to test a rendezvous that nobody joins)
+    if (r == rank || std::memcmp(&hs[r], &own, sizeof(own)) == 0) {
       ptrs[r] = pf_buf;
       continue;
     }
@@ -1012,6 +1030,19 @@ b200dp_status Engine::fold_finish(cudaStream_t st, int nloc, double* d_force) {
   }
   launch_fold_finish(st, nloc, d_force, reinterpret_cast<unsigned long long*>(pf_buf),
                      reinterpret_cast<unsigned*>(pf_buf + pf_off_nf));
+  B200DP_CUDA_TRY(cudaGetLastError());
+  return B200DP_OK;
+}
+
+b200dp_status Engine::peer_reduce(cudaStream_t st, int nv, const double* d_in, double* d_out, long long max_polls) {
+  g_err_sink = &err;
+  if (!pf_buf || !pf_ptrs.ptr || pf_nranks > kPeerMaxRanks || nv < 0 || nv > kPeerMaxValues ||
+      (nv > 0 && (!d_in || !d_out))) {
+    err = "peer_reduce: export and connect first; 0 <= nv <= 16, device buffers for nv > 0; at most 64 ranks";
+    return B200DP_ERR_INVALID;
+  }
+  launch_peer_reduce(st, peer_sync(), pf_seq.as<unsigned long long>(), d_in, nv, d_out, pf_sync_err.as<int>(),
+                     max_polls > 0 ? max_polls : (1LL << 24));
   B200DP_CUDA_TRY(cudaGetLastError());
   return B200DP_OK;
 }
@@ -1379,6 +1410,12 @@ b200dp_status b200dp_compute_device_fold(b200dp_engine* engine, void* stream, in
   if (!engine) return B200DP_ERR_INVALID;
   return engine->e.compute_device_fold(static_cast<cudaStream_t>(stream), nlocal, nghost, d_coord, d_atype, region,
                                        d_energy, d_force, d_virial);
+}
+
+b200dp_status b200dp_peer_reduce(b200dp_engine* engine, void* stream, int nv, const double* d_in, double* d_out,
+                                 long long max_polls) {
+  if (!engine) return B200DP_ERR_INVALID;
+  return engine->e.peer_reduce(static_cast<cudaStream_t>(stream), nv, d_in, d_out, max_polls);
 }
 
 b200dp_status b200dp_fold_finish(b200dp_engine* engine, void* stream, int nlocal, double* d_force) {

@@ -89,14 +89,19 @@ struct Engine {
   // peer fold (domain decomposition): this rank's owned-atom accumulator is
   // exported by CUDA IPC; peers add their ghost edges' reverse contributions
   // into it over NVLink
-  unsigned char* pf_buf = nullptr;  // [accumulator | flags | positions] of `pf_cap` owned atoms
-  size_t pf_off_nf = 0, pf_off_x = 0;
+  unsigned char* pf_buf = nullptr;  // [accumulator | flags | positions | rendezvous area] of `pf_cap` owned atoms
+  size_t pf_off_nf = 0, pf_off_x = 0, pf_off_sync = 0;
+  DevBuf pf_seq, pf_sync_err;  // this rank's rendezvous counter; rendezvous timeouts (sticky until b200dp_check)
   int pf_cap = 0, pf_nranks = 0, pf_rank = 0, pf_nghost = 0;
   bool pf_active = false, pf_has_shift = false;
   std::vector<void*> pf_opened;
   DevBuf pf_ptrs, pf_origin, pf_shift;
   PeerSet peer_set() const {
     return PeerSet{pf_ptrs.as<unsigned char*>(), 0, pf_off_nf, pf_off_x};
+  }
+  PeerSync peer_sync() const {
+    return PeerSync{pf_ptrs.as<unsigned char*>(), pf_off_sync,
+                    pf_off_sync + sizeof(unsigned long long) * kPeerMaxRanks, pf_nranks, pf_rank};
   }
   // host-call staging
   DevBuf dt_part, dt_cnt;  // split final fitting backward (few row tiles)
@@ -160,6 +165,7 @@ struct Engine {
                                     const int* d_atype, const double* region, double* d_energy, double* d_force,
                                     double* d_virial);
   b200dp_status fold_finish(cudaStream_t st, int nloc, double* d_force);
+  b200dp_status peer_reduce(cudaStream_t st, int nv, const double* d_in, double* d_out, long long max_polls);
 };
 
 }  // namespace b200dp

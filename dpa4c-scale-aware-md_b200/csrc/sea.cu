@@ -775,6 +775,74 @@ void launch_halo_gather(cudaStream_t st, int nloc, int nghost, double* x, const 
   k_halo_gather<<<(nghost + 255) / 256, 256, 0, st>>>(nloc, nghost, x, peers, origin, shift);
 }
 
+// One rendezvous of all ranks (see launch_peer_reduce).  One warp: lane q
+// handles rank q (q < nranks <= 32 per pass of the loops below).
+__global__ void __launch_bounds__(32) k_peer_reduce(PeerSync ps, unsigned long long* __restrict__ seqp,
+                                                    const double* __restrict__ in, int nv, double* __restrict__ out,
+                                                    int* __restrict__ err, long long limit) {
+  const int lane = threadIdx.x;
+  const unsigned long long seq = *seqp + 1;
+  const size_t mail = ps.off_mail + sizeof(double) * ((size_t)(seq & 1) * kPeerMaxRanks * kPeerMaxValues +
+                                                      (size_t)ps.rank * kPeerMaxValues);
+  // 1. this rank's values into every rank's mailbox slot, then its arrival counter
+  for (int q = lane; q < ps.nranks; q += 32) {
+    double* dst = reinterpret_cast<double*>(ps.base[q] + mail);
+    for (int v = 0; v < nv; ++v) dst[v] = in[v];
+  }
+  __threadfence_system();
+  __syncwarp();
+  for (int q = lane; q < ps.nranks; q += 32) {
+    unsigned long long* flag = reinterpret_cast<unsigned long long*>(ps.base[q] + ps.off_flags) + ps.rank;
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(flag), "l"(seq) : "memory");
+  }
+  // 2. wait until every rank has arrived (bounded)
+  const unsigned long long* own =
+      reinterpret_cast<const unsigned long long*>(ps.base[ps.rank] + ps.off_flags);
+  bool ok = true;
+  for (int q = lane; q < ps.nranks; q += 32) {
+    long long it = 0;
+    for (;;) {
+      unsigned long long f;
+      asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(f) : "l"(own + q) : "memory");
+      if (f >= seq) break;
+      if (++it >= limit) {
+        ok = false;
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  ok = __all_sync(0xffffffffu, ok);
+  if (!ok) {
+    if (lane == 0) {
+      atomicAdd(err, 1);
+      *seqp = seq;
+    }
+    return;
+  }
+  __threadfence_system();
+  // 3. the sum over ranks in rank order
+  const double* box = reinterpret_cast<const double*>(ps.base[ps.rank] + ps.off_mail) +
+                      (size_t)(seq & 1) * kPeerMaxRanks * kPeerMaxValues;
+  for (int v = lane; v < nv; v += 32) {
+    double acc = 0.0;
+    for (int q = 0; q < ps.nranks; ++q) {
+      const double* src = box + (size_t)q * kPeerMaxValues + v;
+      double x;
+      asm volatile("ld.relaxed.sys.global.f64 %0, [%1];" : "=d"(x) : "l"(src) : "memory");
+      acc += x;
+    }
+    out[v] = acc;
+  }
+  if (lane == 0) *seqp = seq;
+}
+
+void launch_peer_reduce(cudaStream_t st, const PeerSync& ps, unsigned long long* seq, const double* in, int nv,
+                        double* out, int* err, long long limit) {
+  count_launch();
+  k_peer_reduce<<<1, 32, 0, st>>>(ps, seq, in, nv, out, err, limit);
+}
+
 // ---------------------------------------------------------------- instantiations
 #define B200DP_INST(P)                                                                                              \
   template size_t descriptor_fwd_smem<P>(const SeaDev&, int);                                                      \

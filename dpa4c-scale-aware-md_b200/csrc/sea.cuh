@@ -82,6 +82,31 @@ struct PeerSet {
   unsigned char* const* base;
   size_t off_acc, off_nf, off_x;
 };
+// Device-side rendezvous of the ranks through their exported buffers: a
+// sync area per buffer holds one arrival counter per source rank (u64, at
+// off_flags) and two mailboxes of kPeerMaxValues doubles per source rank
+// (at off_mail, alternating between consecutive rendezvous).
+constexpr int kPeerMaxRanks = 64;
+constexpr int kPeerMaxValues = 16;
+constexpr size_t kPeerSyncBytes = sizeof(unsigned long long) * kPeerMaxRanks +
+                                  sizeof(double) * 2 * kPeerMaxRanks * kPeerMaxValues;
+struct PeerSync {
+  unsigned char* const* base;  // every rank's buffer as mapped in this process
+  size_t off_flags, off_mail;
+  int nranks, rank;
+};
+// One rendezvous of all ranks on `st`: this rank's nv values (device memory,
+// nv <= kPeerMaxValues; nv = 0 is a plain barrier) go to every rank's mailbox
+// with plain peer stores, then its arrival counter is raised in every rank's
+// buffer; the kernel waits until every rank has arrived at this rendezvous
+// and writes the sum of all ranks' values, in rank order, to out.  Every rank
+// must call it the same number of times in the same order.  The wait is
+// bounded: after `limit` polls the kernel adds 1 to err[kErrPeerTimeout],
+// writes nothing to out and returns.  `seq` is this rank's device-side
+// rendezvous counter (u64, starts at 0).  Ranks must run on different GPUs:
+// kernels of one GPU are not guaranteed to run at the same time.
+void launch_peer_reduce(cudaStream_t st, const PeerSync& ps, unsigned long long* seq, const double* in, int nv,
+                        double* out, int* err, long long limit);
 // The assembly with owned neighbours' contributions added to this rank's
 // exported accumulator (own_acc, own_nf) and ghost rows (acc_f rows
 // nloc..nall) then pushed to their owners' accumulators, origin[g] = (owner

@@ -27,6 +27,10 @@ owners' buffers over NVLink.  After the force call the engine adds each ghost
 row's reverse contribution directly into the owner's fixed-point force
 accumulator in the owner's memory; the all-reduce of energy and virial orders
 every rank's additions before any rank converts its accumulator into forces.
+When every rank has a GPU of its own, the barrier and the all-reduce are the
+engine's device-side rendezvous through the same peer buffers
+(b200dp_peer_reduce: plain peer stores, an arrival counter per rank, bounded
+waits); ranks that share a GPU use the process group instead.
 """
 from __future__ import annotations
 
@@ -279,12 +283,15 @@ class PeerFold:
 
     gathers = True
 
-    def __init__(self, dp, device, stream=None, capacity_margin: float = 2.0):
+    def __init__(self, dp, device, stream=None, capacity_margin: float = 2.0, device_sync: bool | None = None):
         self.dp = dp
         self.device = torch.device(device)
         self.stream = stream
         self.margin = capacity_margin
         self.origin = self.shift = None
+        # None: the device-side rendezvous (b200dp_peer_reduce) when every rank has a GPU of its own,
+        # else the process group's all-reduce
+        self.device_sync = device_sync
 
     def _stream(self) -> int:
         if self.stream is not None:
@@ -304,6 +311,15 @@ class PeerFold:
             handles = [None] * nranks
             dist.all_gather_object(handles, h)
         self.dp.fold_connect(rank, handles)
+        if self.device_sync is None:
+            import socket
+
+            me = (socket.gethostname(), str(torch.cuda.get_device_properties(self.device).uuid))
+            ids = [me]
+            if dist.is_initialized():
+                ids = [None] * nranks
+                dist.all_gather_object(ids, me)
+            self.device_sync = len(set(ids)) == len(ids)
         self.origin = origin.to(device=self.device, dtype=torch.int32).contiguous()
         self.shift = shift.to(device=self.device, dtype=torch.float64).contiguous()
         self.dp.fold_origins(self.origin.shape[0], self.origin.data_ptr(), self.shift.data_ptr())
@@ -320,6 +336,21 @@ class PeerFold:
 
     def finish(self, f, nloc) -> None:
         self.dp.fold_finish(self._stream(), nloc, f.data_ptr())
+
+    def barrier(self) -> None:
+        """Every rank's publish is complete before any rank's gather reads it."""
+        if self.device_sync:
+            self.dp.peer_reduce(self._stream(), 0)
+        elif dist.is_initialized():
+            dist.all_reduce(torch.zeros(1, device=self.device))
+
+    def reduce(self, ev) -> None:
+        """Sum of energy and virial over the ranks (in place); also orders every rank's force
+        additions before any rank's finish."""
+        if self.device_sync:
+            self.dp.peer_reduce(self._stream(), ev.numel(), ev.data_ptr(), ev.data_ptr())
+        elif dist.is_initialized():
+            dist.all_reduce(ev, op=dist.ReduceOp.SUM)
 
 
 class DistributedDeepPot:
@@ -375,16 +406,14 @@ class DistributedDeepPot:
             return self.ev[0:1], self.force[: self.nloc], self.ev[1:10]
         if self.fold is not None and self.fold.gathers:
             self.fold.publish(self.x, self.nloc)
-            if dist.is_initialized():  # every rank's positions are published before any is read
-                dist.all_reduce(self._bar)
+            self._barrier()  # every rank's positions are published before any is read
             self.fold.gather(self.x, self.nloc, self.nghost)
         else:
             self.plan.forward(self.x)
         if self.fold is not None:
             self.fold.compute(self.x, self.types, self.nloc, self.nghost, self.region, self.ev[0:1], self.force,
                               self.ev[1:10])
-            if dist.is_initialized():  # every rank's additions are done once this completes
-                dist.all_reduce(self.ev, op=dist.ReduceOp.SUM)
+            self._reduce_ev()  # every rank's additions are done once this completes
             self.fold.finish(self.force, self.nloc)
             return self.ev[0:1], self.force[: self.nloc], self.ev[1:10]
         self.compute(self.x, self.types, self.nloc, self.nghost, self.region, self.ev[0:1], self.force,
@@ -393,6 +422,18 @@ class DistributedDeepPot:
         if dist.is_initialized():
             dist.all_reduce(self.ev, op=dist.ReduceOp.SUM)
         return self.ev[0:1], self.force[: self.nloc], self.ev[1:10]
+
+    def _barrier(self) -> None:
+        if hasattr(self.fold, "barrier"):
+            self.fold.barrier()
+        elif dist.is_initialized():
+            dist.all_reduce(self._bar)
+
+    def _reduce_ev(self) -> None:
+        if hasattr(self.fold, "reduce"):
+            self.fold.reduce(self.ev)
+        elif dist.is_initialized():
+            dist.all_reduce(self.ev, op=dist.ReduceOp.SUM)
 
     _graph = None
 

@@ -50,7 +50,9 @@ typedef enum b200dp_status {
   B200DP_ERR_CAPACITY = 5,     /* a centre had more in-cutoff candidates than the
                                   builder's per-centre buffer */
   B200DP_ERR_BAD_TYPE = 6,     /* an atom type outside [0, ntypes) */
-  B200DP_ERR_UNSUPPORTED = 7   /* configuration this build does not handle */
+  B200DP_ERR_UNSUPPORTED = 7,  /* configuration this build does not handle */
+  B200DP_ERR_PEER_TIMEOUT = 8  /* a device-side rendezvous of the ranks (b200dp_peer_reduce) gave up
+                                  waiting: another rank never arrived */
 } b200dp_status;
 
 typedef enum b200dp_precision {
@@ -329,6 +331,23 @@ b200dp_status b200dp_compute_device_fold(b200dp_engine* engine, void* stream, in
                                          const double* d_coord, const int* d_atype, const double* region,
                                          double* d_energy, double* d_force, double* d_virial);
 b200dp_status b200dp_fold_finish(b200dp_engine* engine, void* stream, int nlocal, double* d_force);
+/* Device-side rendezvous of the ranks through their exported buffers, the
+ * per-step synchronisation of the peer path without a collective library:
+ * the rank's nv values (device memory, 0 <= nv <= 16) are stored into every
+ * rank's buffer over NVLink, then its arrival counter; one warp waits until
+ * every rank has arrived at this rendezvous and writes the sum of all ranks'
+ * values in rank order to d_out (the same bits on every rank).  nv = 0 is a
+ * plain barrier (e.g. between halo_publish and halo_gather); nv = 10 with
+ * energy and virial is the reduction ahead of fold_finish.  Enqueued on
+ * `stream` without host synchronisation (capturable).  Every rank makes the
+ * same sequence of calls.  The wait is bounded by max_polls (<= 0: 2^24 polls
+ * of ~0.1 us): on expiry d_out is not written and the next b200dp_check
+ * returns B200DP_ERR_PEER_TIMEOUT.  Ranks must be on different GPUs (two
+ * kernels of one GPU are not guaranteed to run at the same time). Replaces
+ * the MPI all-reduce of energy and virial in the pair style
+ * (PL/pair_deepmd_kokkos.cpp:937-993). */
+b200dp_status b200dp_peer_reduce(b200dp_engine* engine, void* stream, int nv, const double* d_in, double* d_out,
+                                 long long max_polls);
 
 typedef struct b200dp_md_params {
   double dt;        /* time step, ps (default 0.0005) */
