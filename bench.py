@@ -82,7 +82,11 @@ def parse():
     ap.add_argument("--sweep", action="store_true", help="measure the five configurations (see module doc)")
     ap.add_argument("--only", default="", help="--sweep: comma-separated labels to run")
     ap.add_argument("--reverse", default="peer", choices=["peer", "nccl"],
-                    help="N > 1: ghost forces to their owners by peer-memory atomics or by NCCL send/recv")
+                    help="N > 1 with --driver python: ghost forces to their owners by peer-memory atomics or by "
+                         "NCCL send/recv")
+    ap.add_argument("--driver", default="cpp", choices=["cpp", "python"],
+                    help="N > 1: the C++ decomposed driver (b200dp_dd_*) or the torch.distributed one (domain.py)")
+    ap.add_argument("--no-strong", action="store_true", help="skip the 3.1M-atom strong-scaling leg")
     return ap.parse_args()
 
 
@@ -309,6 +313,98 @@ class Decomposed:
         self.ddp.step()
 
 
+class DecomposedCpp:
+    """N GPUs: the C++ decomposed driver (b200dp_dd_*): NCCL for the setup and the plan, peer memory
+    and device-side rendezvous for the per-step exchange; the step replayed as one CUDA graph."""
+
+    def __init__(self, dp, system, grid, rank, world, dev, stream, torch, dist):
+        import b200dp
+
+        uid = [b200dp.dd_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        self.dd = b200dp.DD(dp, uid[0], world, rank, system.coord, system.atype, system.box, grid, halo=HALO)
+        self.dp, self.stream, self.torch = dp, stream, torch
+        self.n, self.nghost = self.dd.counts()
+        self.total = system.natoms
+        self.graph = None
+
+    def capture(self):
+        torch = self.torch
+        side = torch.cuda.Stream()
+        side.wait_stream(self.stream)
+        with torch.cuda.stream(side):
+            self.dd.force(side.cuda_stream)
+        self.stream.wait_stream(side)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            self.dd.force(side.cuda_stream)
+        torch.cuda.synchronize()
+        self.graph = g
+
+    def release(self):
+        self.graph = None
+
+    def step(self):
+        if self.graph is not None:
+            self.graph.replay()
+            return
+        self.dd.force(self.stream.cuda_stream)
+
+    def close(self):
+        self.graph = None
+        self.dd.close()
+
+
+def overlap_probe(torch, b200dp, mp, system, dev, local, flush, steps=10):
+    """Speed-up of two force calls running concurrently on two streams over the same two calls in turn."""
+    engines, works, streams = [], [], []
+    for _ in range(2):
+        st = torch.cuda.Stream(device=dev)
+        dp = b200dp.DeepPot(mp, precision=b200dp.MIXED, device=local)
+        w = Periodic(dp, system, dev, st, torch)
+        for _ in range(3):
+            with torch.cuda.stream(st):
+                w.step()
+        w.capture()
+        engines.append(dp)
+        works.append(w)
+        streams.append(st)
+    torch.cuda.synchronize()
+
+    def run(concurrent):
+        flush.fill_(1)
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        base = torch.cuda.current_stream(dev)
+        t0.record(base)
+        for st in streams:
+            st.wait_stream(base)
+        for _ in range(steps):
+            if concurrent:
+                for w, st in zip(works, streams):
+                    with torch.cuda.stream(st):
+                        w.step()
+            else:
+                for w, st in zip(works, streams):
+                    with torch.cuda.stream(streams[0]):
+                        w.step()
+        for st in streams:
+            base.wait_stream(st)
+        t1.record(base)
+        torch.cuda.synchronize()
+        return t0.elapsed_time(t1)
+
+    serial = min(run(False) for _ in range(2))
+    both = min(run(True) for _ in range(2))
+    for w, dp in zip(works, engines):
+        w.release()
+        dp.close()
+    torch.cuda.empty_cache()
+    return {"atoms": system.natoms, "serial_ms_per_pair": serial / steps, "concurrent_ms_per_pair": both / steps,
+            "speedup": serial / both}
+
+
 def global_system(world, rank):
     """Weak scaling: 4096 H2O per GPU, the global box grows with the rank grid."""
     import domain
@@ -341,10 +437,14 @@ def run_b200dp(args, world, rank, local):
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     sync = torch.zeros(1, device=dev)
 
-    def workload(dp):
+    def workload(dp, sys_=None, grid_=None):
+        sys_ = sys_ or system
+        grid_ = grid_ or grid
         if world == 1:
-            return Periodic(dp, system, dev, stream, torch)
-        return Decomposed(dp, system, grid, rank, dev, stream, torch, peer_fold=args.reverse == "peer")
+            return Periodic(dp, sys_, dev, stream, torch)
+        if args.driver == "cpp":
+            return DecomposedCpp(dp, sys_, grid_, rank, world, dev, stream, torch, dist)
+        return Decomposed(dp, sys_, grid_, rank, dev, stream, torch, peer_fold=args.reverse == "peer")
 
     def device_loop(dp, w, steps, warmup):
         """Timed steps: CUDA events around each step on the launch stream, L2 flushed before each,
@@ -511,6 +611,48 @@ def run_b200dp(args, world, rank, local):
                 dp8.close()
         except Exception as ex:  # report, never hide
             c8 = {"error": repr(ex)}
+    # execution-window probe (N = 1): two independent force calls on two streams at once against one
+    # after the other.  Windowed overlap of one call's stages (the reference's model_pipeline) can only
+    # use the capacity that two whole calls running together find idle, so a ratio near 1 bounds it.
+    overlap = None
+    if world == 1 and prec == b200dp.MIXED and not args.profile and not args.no_strong:
+        try:
+            overlap = {"note": "throughput of two concurrent force calls (two engines, two streams, each replaying "
+                               "its CUDA graph) over that of one call after the other; 1.0 = no idle capacity for "
+                               "execution windows to use"}
+            for label, sysf in (("c1_water_12288", systems.config1), ("c4_water_786k", lambda: systems.config4("786k"))):
+                overlap[label] = overlap_probe(torch, b200dp, mp, sysf(), dev, local, flush)
+        except Exception as ex:  # report, never hide
+            overlap = {"error": repr(ex)[:400]}
+    # strong scaling of the 3,145,728-atom water box (the same global system at every N): periodic on one
+    # GPU, the decomposed driver on N; a secondary key beside the weak-scaling headline
+    strong = None
+    if not (args.no_strong or args.profile) and prec == b200dp.MIXED:
+        import domain
+
+        if hasattr(w, "release"):
+            w.release()
+        try:
+            s3 = systems.config4("3.1M")
+            g3 = domain.rank_grid(world)
+            dp3 = b200dp.DeepPot(mp, precision=b200dp.MIXED, device=local)
+            w3 = workload(dp3, s3, g3)
+            k3 = 5
+            ms3, _ = device_loop(dp3, w3, k3, 3)
+            ms3 = max_over_ranks(ms3)
+            strong = {"atoms": s3.natoms, "value": s3.natoms * k3 / (ms3 / 1e3), "unit": "atom-steps/s",
+                      "ms_per_step": ms3 / k3, "steps": k3, "n_gpus": world, "grid": list(g3),
+                      "scaling": "strong (the same 3.1M-atom system at every N)",
+                      "driver": "periodic engine" if world == 1 else
+                      ("C++ decomposed driver" if args.driver == "cpp" else "domain.py"),
+                      "timing": "CUDA events per step, max over ranks, L2 flushed before each, step as a CUDA graph"}
+            if hasattr(w3, "close"):
+                w3.close()
+            del w3
+            dp3.close()
+            torch.cuda.empty_cache()
+        except Exception as ex:  # report, never hide
+            strong = {"error": repr(ex)[:400]}
     cpu = None
     if rank == 0 and world == 1 and not (args.no_cpu_baseline or args.profile):
         arm = OracleArm(mp)
@@ -518,7 +660,13 @@ def run_b200dp(args, world, rank, local):
         cpu = {"value": system.natoms / dt, "unit": "atom-steps/s", "cores": arm.cores, "kind": "port",
                "sample": f"best of two full evaluations of the 12,288-atom system ({dt:.2f} s each), fp64 C++ "
                          "oracle, OpenMP, model loaded beforehand"}
-    if world > 1:
+    if world > 1 and args.driver == "cpp":
+        parallelism = (f"C++ decomposed driver (b200dp_dd), domain decomposition {grid[0]}x{grid[1]}x{grid[2]}, "
+                       f"halo {HALO} A: ghost rows gathered from the owners over NVLink peer memory, ghost forces "
+                       "added into the owners' accumulators, device-side rendezvous for the barrier and the "
+                       "energy/virial sum (no collective library per step), step replayed as one CUDA graph")
+        cfg_extra = {"global_atoms": w.total, "ghosts_rank0": w.nghost}
+    elif world > 1:
         rev = ("ghost forces added into the owners' accumulators over NVLink peer memory"
                if args.reverse == "peer" else "ghost forces folded back by NCCL send/recv")
         parallelism = (f"domain decomposition {grid[0]}x{grid[1]}x{grid[2]}, halo {HALO} A, coordinate halo by "
@@ -544,11 +692,15 @@ def run_b200dp(args, world, rank, local):
             "fp64": fp64,
             "md_loop": md_loop,
             "c8l2": c8,
+            "strong_3.1M": strong,
+            "overlap_probe": overlap,
             "cpu_baseline": cpu,
             "clocks": clocks,
             "flops_per_step": fl["total"],
         }
         print(json.dumps(line), flush=True)
+    if hasattr(w, "close"):
+        w.close()
     del w
     dp.close()
     if dist:
@@ -596,6 +748,8 @@ def e2e_loop(dp, w, system, steps, warmup, torch, dist):
 
 def e2e_decomposed(w, steps, warmup, torch, dist):
     """Per rank: owned coordinates from pinned host memory, owned forces and energy/virial back."""
+    if isinstance(w, DecomposedCpp):
+        return e2e_decomposed_cpp(w, steps, warmup, torch, dist)
     ddp = w.ddp
     n = ddp.nloc
     x_host = ddp.x[:n].cpu().pin_memory()
@@ -624,6 +778,40 @@ def e2e_decomposed(w, steps, warmup, torch, dist):
             "entry": "domain.DistributedDeepPot.step (captured CUDA graph) over "
                      + ("b200dp_compute_device_fold + b200dp_fold_finish" if ddp.fold is not None
                         else "b200dp_compute_device") + " (pinned host buffers, per rank)",
+            "bytes_rank": "rank 0's own counts"}
+
+
+def e2e_decomposed_cpp(w, steps, warmup, torch, dist):
+    """The C++ driver through its C ABI: owned positions H2D from pinned memory, the step (replayed
+    graph), owned forces and the global energy + virial D2H, every step."""
+    dd = w.dd
+    n = w.n
+    _, x0, _, _ = dd.owned()
+    x_host = torch.tensor(x0).pin_memory()
+    f_host = torch.zeros(n, 3, dtype=torch.float64).pin_memory()
+    ev_host = torch.zeros(10, dtype=torch.float64).pin_memory()
+    st = w.stream.cuda_stream
+
+    def call():
+        dd.set_positions(st, x_host.data_ptr())
+        w.step()
+        dd.get_forces(st, f_host.data_ptr(), ev_host.data_ptr())
+        w.stream.synchronize()
+
+    for _ in range(warmup):
+        call()
+    w.capture()
+    dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        call()
+    dt = time.perf_counter() - t0
+    w.release()
+    return {"value": None, "unit": "atom-steps/s", "seconds": dt,
+            "h2d_bytes_per_step": n * 3 * 8, "d2h_bytes_per_step": n * 3 * 8 + 8 * 10,
+            "entry": "b200dp_dd_set_positions + b200dp_dd_force (captured CUDA graph) + b200dp_dd_get_forces "
+                     "(pinned host buffers, per rank)",
             "bytes_rank": "rank 0's own counts"}
 
 

@@ -28,7 +28,7 @@ STATUS = {0: "OK", 1: "INVALID", 2: "IO", 3: "CUDA", 4: "SEL_OVERFLOW", 5: "CAPA
 
 EXPORTS = [
     "b200dp_options_default", "b200dp_create", "b200dp_destroy", "b200dp_last_error", "b200dp_model_info_get",
-    "b200dp_compute_host", "b200dp_compute_host_nlist", "b200dp_compute_device", "b200dp_check",
+    "b200dp_engine_device", "b200dp_compute_host", "b200dp_compute_host_nlist", "b200dp_compute_device", "b200dp_check",
     "b200dp_sel_overflow_count", "b200dp_last_nlist", "b200dp_last_descriptor", "b200dp_set_stage_timing",
     "b200dp_set_neighbor_reuse", "b200dp_neighbor_stats", "b200dp_fold_export", "b200dp_fold_connect", "b200dp_fold_origins",
     "b200dp_compute_device_fold", "b200dp_fold_finish", "b200dp_halo_publish", "b200dp_halo_gather",
@@ -39,6 +39,10 @@ EXPORTS = [
     "b200dp_direct_fp32_global_virial_pointer", "b200dp_md_params_default", "b200dp_md_create",
     "b200dp_md_run", "b200dp_md_thermo", "b200dp_md_state", "b200dp_md_destroy", "b200dp_md_snapshot_bytes",
     "b200dp_md_snapshot", "b200dp_md_restore", "b200dp_md_write_restart", "b200dp_md_read_restart",
+    "b200dp_dd_params_default", "b200dp_dd_unique_id", "b200dp_dd_create", "b200dp_dd_destroy",
+    "b200dp_dd_last_error", "b200dp_dd_stream", "b200dp_dd_counts", "b200dp_dd_force", "b200dp_dd_result",
+    "b200dp_dd_owned", "b200dp_dd_set_positions", "b200dp_dd_get_forces", "b200dp_dd_md_start", "b200dp_dd_md_run",
+    "b200dp_dd_md_thermo", "b200dp_dd_plan_emulate",
 ]
 
 NVE, NVT, NPT = 0, 1, 2
@@ -50,6 +54,11 @@ class MDParams(ctypes.Structure):
                 ("seed", ctypes.c_ulonglong), ("mass", ctypes.c_double * 8), ("p_target", ctypes.c_double),
                 ("p_damp", ctypes.c_double), ("pchain", ctypes.c_int), ("rebuild_every", ctypes.c_int),
                 ("skin", ctypes.c_double), ("reserved", ctypes.c_int * 8)]
+
+
+class DDParams(ctypes.Structure):
+    _fields_ = [("grid", ctypes.c_int * 3), ("halo", ctypes.c_double), ("max_polls", ctypes.c_longlong),
+                ("capacity", ctypes.c_int), ("reserved", ctypes.c_int * 9)]
 
 
 class NeighborView(ctypes.Structure):
@@ -140,6 +149,29 @@ def load_library(path: str = LIB_PATH):
     L.b200dp_md_thermo.argtypes = [_vp, _dp]
     L.b200dp_md_state.argtypes = [_vp, _dp, _dp, _dp]
     L.b200dp_md_destroy.argtypes = [_vp]
+    _lp = ctypes.POINTER(ctypes.c_longlong)
+    L.b200dp_dd_params_default.argtypes = [ctypes.POINTER(DDParams)]
+    L.b200dp_dd_params_default.restype = None
+    L.b200dp_dd_unique_id.argtypes = [_vp]
+    L.b200dp_dd_create.argtypes = [_vp, _vp, ctypes.c_int, ctypes.c_int, _dp, ctypes.POINTER(DDParams), ctypes.c_int,
+                                   _dp, _ip, ctypes.POINTER(_vp)]
+    L.b200dp_dd_destroy.argtypes = [_vp]
+    L.b200dp_dd_destroy.restype = None
+    L.b200dp_dd_last_error.argtypes = [_vp]
+    L.b200dp_dd_last_error.restype = ctypes.c_char_p
+    L.b200dp_dd_stream.argtypes = [_vp]
+    L.b200dp_dd_stream.restype = _vp
+    L.b200dp_dd_counts.argtypes = [_vp, _ip, _ip]
+    L.b200dp_dd_force.argtypes = [_vp, _vp]
+    L.b200dp_dd_result.argtypes = [_vp, _vp, _dp, _dp]
+    L.b200dp_dd_owned.argtypes = [_vp, _lp, _dp, _dp, _dp]
+    L.b200dp_dd_set_positions.argtypes = [_vp, _vp, _vp]
+    L.b200dp_dd_get_forces.argtypes = [_vp, _vp, _vp, _vp]
+    L.b200dp_dd_md_start.argtypes = [_vp, ctypes.POINTER(MDParams), _dp]
+    L.b200dp_dd_md_run.argtypes = [_vp, ctypes.c_int]
+    L.b200dp_dd_md_thermo.argtypes = [_vp, _dp]
+    L.b200dp_dd_plan_emulate.argtypes = [ctypes.c_int, _ip, _dp, ctypes.c_double, ctypes.c_int, _dp, _dp, _lp, _ip,
+                                         _lp, _dp, _dp, _ip, _ip, ctypes.c_int]
     L.b200dp_md_snapshot_bytes.argtypes = [_vp, ctypes.POINTER(ctypes.c_size_t)]
     L.b200dp_md_snapshot.argtypes = [_vp, _vp]
     L.b200dp_md_restore.argtypes = [_vp, _vp]
@@ -458,6 +490,145 @@ def direct_set_need_virial(need_virial: int, stream: int = 0) -> None:
 
 def direct_fp32_global_virial_pointer() -> int:
     return int(load_library().b200dp_direct_fp32_global_virial_pointer() or 0)
+
+
+def dd_unique_id() -> bytes:
+    """128 bytes identifying one group of ranks (made by rank 0, handed to all)."""
+    L = load_library()
+    buf = ctypes.create_string_buffer(128)
+    rc = L.b200dp_dd_unique_id(buf)
+    if rc != 0:
+        raise B200DPError(rc, "ncclGetUniqueId failed")
+    return buf.raw
+
+
+class DD:
+    """Domain-decomposed force evaluation and MD (b200dp_dd_*), one process per GPU.
+
+    Every rank passes the whole system; the rank keeps the atoms of its sub-box."""
+
+    THERMO = MD.THERMO
+
+    def __init__(self, dp: DeepPot, uid: bytes, nranks: int, rank: int, coord, atype, box, grid, halo=8.0,
+                 max_polls=0, capacity=0):
+        L = load_library()
+        p = DDParams()
+        L.b200dp_dd_params_default(ctypes.byref(p))
+        for k in range(3):
+            p.grid[k] = int(grid[k])
+        p.halo, p.max_polls, p.capacity = float(halo), int(max_polls), int(capacity)
+        coord = np.ascontiguousarray(coord, dtype=np.float64).reshape(-1, 3)
+        atype = np.ascontiguousarray(atype, dtype=np.int32)
+        box = np.ascontiguousarray(box, dtype=np.float64).reshape(9)
+        self.natoms = coord.shape[0]
+        self.L, self.dp = L, dp
+        h = _vp()
+        idb = ctypes.create_string_buffer(bytes(uid), 128)
+        rc = L.b200dp_dd_create(dp.h, idb, int(nranks), int(rank), _p(box, _dp), ctypes.byref(p), self.natoms,
+                                _p(coord, _dp), _p(atype, _ip), ctypes.byref(h))
+        if rc != 0:
+            raise B200DPError(rc, "b200dp_dd_create failed: " + dp.L.b200dp_last_error(dp.h).decode())
+        self.h = h
+
+    def _check(self, rc):
+        if rc != 0:
+            raise B200DPError(rc, self.L.b200dp_dd_last_error(self.h).decode())
+
+    @property
+    def stream(self) -> int:
+        return self.L.b200dp_dd_stream(self.h) or 0
+
+    def counts(self):
+        n, g = ctypes.c_int(), ctypes.c_int()
+        self._check(self.L.b200dp_dd_counts(self.h, ctypes.byref(n), ctypes.byref(g)))
+        return n.value, g.value
+
+    def force(self, stream: int = 0) -> None:
+        self._check(self.L.b200dp_dd_force(self.h, stream or None))
+
+    def result(self, stream: int = 0):
+        e = np.zeros(1)
+        v = np.zeros(9)
+        self._check(self.L.b200dp_dd_result(self.h, stream or None, _p(e, _dp), _p(v, _dp)))
+        return float(e[0]), v.reshape(3, 3)
+
+    def owned(self):
+        n, _ = self.counts()
+        ids = np.zeros(n, np.int64)
+        x, v, f = (np.zeros((n, 3)) for _ in range(3))
+        self._check(self.L.b200dp_dd_owned(self.h, ids.ctypes.data_as(ctypes.POINTER(ctypes.c_longlong)),
+                                           _p(x, _dp), _p(v, _dp), _p(f, _dp)))
+        return ids, x, v, f
+
+    def set_positions(self, stream: int, host_ptr: int) -> None:
+        self._check(self.L.b200dp_dd_set_positions(self.h, stream or None, host_ptr))
+
+    def get_forces(self, stream: int, force_ptr: int, ev_ptr: int) -> None:
+        self._check(self.L.b200dp_dd_get_forces(self.h, stream or None, force_ptr or None, ev_ptr or None))
+
+    def md_start(self, masses, dt=0.0005, ensemble=NVE, vel=None, t_init=0.0, t_target=300.0, t_damp=0.05, chain=3,
+                 seed=0, rebuild_every=10):
+        p = MDParams()
+        self.L.b200dp_md_params_default(ctypes.byref(p))
+        p.dt, p.ensemble, p.chain = dt, ensemble, chain
+        p.t_target, p.t_damp, p.t_init, p.seed = t_target, t_damp, t_init, seed
+        p.rebuild_every = rebuild_every
+        for t, m in enumerate(masses):
+            p.mass[t] = m
+        v = None if vel is None else np.ascontiguousarray(vel, dtype=np.float64).reshape(-1, 3)
+        self._check(self.L.b200dp_dd_md_start(self.h, ctypes.byref(p), _p(v, _dp)))
+
+    def md_run(self, nsteps: int) -> None:
+        self._check(self.L.b200dp_dd_md_run(self.h, int(nsteps)))
+
+    def thermo(self) -> dict:
+        t = np.zeros(8)
+        self._check(self.L.b200dp_dd_md_thermo(self.h, _p(t, _dp)))
+        return dict(zip(self.THERMO, t))
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.L.b200dp_dd_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def dd_plan_emulate(nranks, grid, box, halo, coord, disp=None, ghost_cap=None):
+    """The decomposed driver's host plan for nranks ranks emulated by threads (no GPU):
+    per rank the owned ids and the ghosts (id, position, shift, origin)."""
+    L = load_library()
+    coord = np.ascontiguousarray(coord, dtype=np.float64).reshape(-1, 3)
+    n = coord.shape[0]
+    box = np.ascontiguousarray(box, dtype=np.float64).reshape(9)
+    g = (ctypes.c_int * 3)(*[int(x) for x in grid])
+    d = None if disp is None else np.ascontiguousarray(disp, dtype=np.float64).reshape(-1, 3)
+    cap = int(ghost_cap if ghost_cap is not None else 8 * n + 1024)
+    oid = np.zeros(n, np.int64)
+    ocnt = np.zeros(nranks, np.int32)
+    gid = np.zeros(cap, np.int64)
+    gx = np.zeros((cap, 3))
+    gs = np.zeros((cap, 3))
+    go = np.zeros((cap, 2), np.int32)
+    gcnt = np.zeros(nranks, np.int32)
+    lp = ctypes.POINTER(ctypes.c_longlong)
+    rc = L.b200dp_dd_plan_emulate(int(nranks), g, _p(box, _dp), float(halo), n, _p(coord, _dp), _p(d, _dp),
+                                  oid.ctypes.data_as(lp), _p(ocnt, _ip), gid.ctypes.data_as(lp), _p(gx, _dp),
+                                  _p(gs, _dp), _p(go, _ip), _p(gcnt, _ip), cap)
+    if rc != 0:
+        raise B200DPError(rc, "plan emulation failed")
+    ranks, o, q = [], 0, 0
+    for r in range(nranks):
+        no, ng = int(ocnt[r]), int(gcnt[r])
+        ranks.append(dict(owned=oid[o:o + no].copy(), ghost_ids=gid[q:q + ng].copy(), ghost_x=gx[q:q + ng].copy(),
+                          ghost_shift=gs[q:q + ng].copy(), ghost_origin=go[q:q + ng].copy()))
+        o += no
+        q += ng
+    return ranks
 
 
 def kernel_launches() -> int:

@@ -24,9 +24,10 @@ NVCC = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ARCH + ["-lineinfo", "-O3", "-std=c++17", "--expt-relaxed-constexpr", "-Xcompiler",
                 "-fPIC,-ffp-contract=off,-O3", "-ccbin", shutil.which("g++", path="/usr/bin") or "g++"]
-SOURCES = ["nlist.cu", "sea.cu", "embed_tc.cu", "fit_tc.cu", "c8l2.cu", "engine.cu", "selftest.cu", "noalloc.cu", "md.cu"]
+SOURCES = ["nlist.cu", "sea.cu", "embed_tc.cu", "fit_tc.cu", "c8l2.cu", "engine.cu", "selftest.cu", "noalloc.cu", "md.cu",
+           "dd.cu"]
 HEADERS = ["common.cuh", "nlist.cuh", "sea.cuh", "engine.hpp", "model.hpp", "umma.cuh", "embed_tc.cuh", "fit_tc.cuh",
-           "c8l2.cuh", "simt_gemm.cuh"]
+           "c8l2.cuh", "simt_gemm.cuh", "md_kernels.cuh"]
 
 
 def _stale(target: str, deps: list[str]) -> bool:
@@ -62,7 +63,7 @@ def build(force: bool = False, jobs: int = 4, verbose: bool = False) -> str:
             if verbose and out:
                 sys.stderr.write(out)
     if force or todo or _stale(LIB, objs):
-        cmd = [NVCC] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcudart_static", "-lrt", "-lpthread", "-ldl"]
+        cmd = [NVCC] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcudart_static", "-lnccl", "-lrt", "-lpthread", "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

@@ -326,7 +326,9 @@ b200dp_status Engine::init_tail() {
   B200DP_CUDA_TRY(scalars.ensure(sizeof(double) * 16));
   ch_fwd = 32;
   ch_bwd = 32;
-  const size_t budget = 110 * 1024;
+  // shared memory per block of the SIMT backward: in fp64 the chunk is cut until four blocks
+  // (16 warps) share an SM -- at two blocks the fp64 pipe idled on latency (9.9 % active)
+  const size_t budget = fp64 ? 56 * 1024 : 110 * 1024;
   auto bwd_smem = [&](int ch) {
     return fp64 ? descriptor_bwd_smem<double>(sd, ch) : descriptor_bwd_smem<float>(sd, ch);
   };
@@ -1274,6 +1276,8 @@ void b200dp_destroy(b200dp_engine* engine) {
 }
 
 const char* b200dp_last_error(const b200dp_engine* engine) { return engine ? engine->e.err.c_str() : "null engine"; }
+
+int b200dp_engine_device(const b200dp_engine* engine) { return engine ? engine->e.opt.device : -1; }
 
 b200dp_status b200dp_model_info_get(const b200dp_engine* engine, b200dp_model_info* out) {
   if (!engine || !out) return B200DP_ERR_INVALID;

@@ -79,6 +79,18 @@ int make_grid(bool periodic, const double* box, const double* region, double rcu
     if (2 * g.reach[d] + 1 > 31) return 2;
   }
   g.ncells = g.n[0] * g.n[1] * g.n[2];
+  g.prune = 1;
+  for (int d = 0; d < 3; ++d) {
+    if (periodic) {
+      for (int e = 0; e < 3; ++e)
+        if (e != d && box[3 * d + e] != 0.0) g.prune = 0;
+      g.org[d] = 0.0;
+      g.h[d] = box[4 * d] / g.n[d];
+    } else {
+      g.org[d] = g.lo[d];
+      g.h[d] = ext[d] / g.n[d];
+    }
+  }
   return 0;
 }
 
@@ -532,6 +544,23 @@ __device__ __forceinline__ void gather_stencil(const FormatSpec& f, const GridSp
         int uu[3] = {ci[0] + dx - g.reach[0], ci[1] + dy - g.reach[1], ci[2] + dz - g.reach[2]};
         int img[3] = {0, 0, 0};
         bool ok = true;
+        if (g.prune) {
+          // skip a cell whose nearest point lies beyond the cutoff (with a relative margin of
+          // 1e-9 in r^2, far above the rounding of the binning): its candidates would all fail
+          // r^2 < rc2, so the rows do not change
+          double d2 = 0.0;
+#pragma unroll
+          for (int d = 0; d < 3; ++d) {
+            double clo = g.org[d] + uu[d] * g.h[d], chi = clo + g.h[d];
+            if (!g.periodic) {
+              if (uu[d] <= 0) clo = -INFINITY;
+              if (uu[d] >= g.n[d] - 1) chi = INFINITY;
+            }
+            const double t = fmax(fmax(clo - xi[d], xi[d] - chi), 0.0);
+            d2 += t * t;
+          }
+          ok = d2 <= rc2 * (1.0 + 1e-9);
+        }
 #pragma unroll
         for (int d = 0; d < 3; ++d) {
           if (g.periodic) {

@@ -25,6 +25,12 @@ struct GridSpec {
   int n[3];         // cells per dimension
   int reach[3];     // stencil half-width in cells
   int ncells;
+  // Cartesian cell geometry for skipping stencil cells wholly beyond the
+  // cutoff (orthorhombic periodic boxes and open grids): cell u of dimension d
+  // spans [org + u h, org + (u + 1) h); the open grid's edge cells also hold
+  // the atoms clamped into them, so they extend to infinity outwards
+  int prune;
+  double org[3], h[3];
 };
 
 // Cell-sorted atom record written by the fill kernel: the wrapped position

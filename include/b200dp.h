@@ -102,6 +102,8 @@ b200dp_status b200dp_create(const char* model_path, const b200dp_options* opt, b
 void b200dp_destroy(b200dp_engine* engine);
 const char* b200dp_last_error(const b200dp_engine* engine);
 b200dp_status b200dp_model_info_get(const b200dp_engine* engine, b200dp_model_info* out);
+/* CUDA device ordinal the engine runs on (-1 for NULL). */
+int b200dp_engine_device(const b200dp_engine* engine);
 
 /* Host buffers in and out (synchronous).  nghost == 0 with a box: periodic
  * system, every periodic image is a neighbour candidate.  nghost > 0: atoms
@@ -313,7 +315,7 @@ b200dp_status b200dp_neighbor_stats(b200dp_engine* engine, long long* builds);
  *   b200dp_compute_device_fold  the ghost-mode force call: energy and virial
  *                        of the owned atoms' edges as usual; the ghost rows'
  *                        reverse contributions are added into the owners'
- *                        accumulators (128-bit integer atomics over NVLink:
+ *                        accumulators (64-bit integer reductions over NVLink:
  *                        order-independent sums) and d_force is not complete
  *                        yet;
  *   b200dp_fold_finish   after EVERY rank's compute_device_fold has completed
@@ -406,6 +408,90 @@ b200dp_status b200dp_md_destroy(b200dp_md* md);
 /* Total kernels this library has launched in the process (all engines). */
 long long b200dp_kernel_launches(void);
 b200dp_status b200dp_stage_times(b200dp_engine* engine, float* ms5);
+
+/* ------------------------------------------------------------------ multi-GPU driver (C++)
+ * Spatially decomposed force evaluation and NVE / NVT molecular dynamics over
+ * the GPUs of one node, one process per GPU, orchestrated in C++ with no
+ * Python on the path.  Replaces the LAMMPS Kokkos machinery around the pair
+ * style in the reference: atom exchange at reneighbouring
+ * (components/lammps/overlays/src/KOKKOS/comm_kokkos.cpp:809-1000), ghost
+ * borders and forward / reverse communication
+ * (components/lammps-deepmd-plugin/src/pair_deepmd_kokkos.cpp:84-124, 931-993)
+ * and fix nvt with its chain on the device
+ * (components/lammps/overlays/src/KOKKOS/dpa_fast_step_kokkos.h:307-400).
+ * Each rank owns the atoms of its sub-box of an orthorhombic periodic box
+ * (grid px x py x pz) plus a ghost shell of width `halo` (>= rcut; rcut +
+ * skin for MD).  NCCL carries the setup, the atom migration and the ghost
+ * plan (host side, at creation and every rebuild_every MD steps); every step
+ * runs on the device without host synchronisation: positions published into
+ * the ranks' exported buffers, a device-side rendezvous, the ghost gather
+ * over NVLink, the force call adding ghost contributions into the owners'
+ * fixed-point accumulators, a rendezvous summing energy and virial in rank
+ * order, the owners' conversion.  Ranks must be on different GPUs that are
+ * NVLink peers.  The engine is the rank's own b200dp_engine (its exported
+ * buffer is created here). */
+typedef struct b200dp_dd b200dp_dd;
+typedef struct b200dp_dd_params {
+  int grid[3];         /* ranks along x, y, z (product = number of ranks) */
+  double halo;         /* ghost shell width, Angstrom (default 8) */
+  long long max_polls; /* bound of every device-side wait (<= 0: the default of b200dp_peer_reduce) */
+  int capacity;        /* owned atoms a rank may hold (<= 0: 1.5 x the largest initial count + 1024) */
+  int reserved[9];
+} b200dp_dd_params;
+void b200dp_dd_params_default(b200dp_dd_params* params);
+/* 128 bytes that identify one group of ranks (ncclGetUniqueId); rank 0 makes
+ * it and the caller hands it to every rank (any host channel). */
+b200dp_status b200dp_dd_unique_id(void* id);
+/* Collective over the ranks.  Every rank passes the whole system (host
+ * arrays: coord [natoms*3], atype [natoms], box [9]) and keeps the atoms whose
+ * wrapped position lies in its sub-box; an atom's global index is its id. */
+b200dp_status b200dp_dd_create(b200dp_engine* engine, const void* id, int nranks, int rank, const double* box,
+                               const b200dp_dd_params* params, int natoms, const double* coord, const int* atype,
+                               b200dp_dd** out);
+void b200dp_dd_destroy(b200dp_dd* dd);
+const char* b200dp_dd_last_error(const b200dp_dd* dd);
+/* The driver's CUDA stream (work of the calls below runs on it unless a stream is given). */
+void* b200dp_dd_stream(b200dp_dd* dd);
+b200dp_status b200dp_dd_counts(b200dp_dd* dd, int* nowned, int* nghost);
+/* One decomposed force call on the current positions, enqueued on `stream`
+ * (NULL: the driver's), no host synchronisation (capturable).  Every rank
+ * calls it the same number of times. */
+b200dp_status b200dp_dd_force(b200dp_dd* dd, void* stream);
+/* Waits for `stream` and reports the global energy and virial [9] of the last
+ * force call (device error counters checked). */
+b200dp_status b200dp_dd_result(b200dp_dd* dd, void* stream, double* energy, double* virial);
+/* Host copies of the owned atoms (any pointer may be NULL): global ids
+ * [nowned], positions, velocities and forces [nowned*3] (synchronises). */
+b200dp_status b200dp_dd_owned(b200dp_dd* dd, long long* ids, double* coord, double* vel, double* force);
+/* Asynchronous copies on `stream`: new positions of the owned atoms (same
+ * atoms and order as b200dp_dd_owned) from host memory, and the owned
+ * forces [nowned*3] and the global energy + virial [10] to host memory. */
+b200dp_status b200dp_dd_set_positions(b200dp_dd* dd, void* stream, const double* coord);
+b200dp_status b200dp_dd_get_forces(b200dp_dd* dd, void* stream, double* force, double* energy_virial);
+/* MD over the decomposition: velocity Verlet (NVE) or with the Nose-Hoover
+ * chain (NVT), in the order of the single-GPU driver; the global kinetic
+ * energy is a device-side rendezvous sum.  vel: global velocities
+ * [natoms*3], or NULL for the seeded draw at t_init (the same draw as the
+ * single-GPU driver).  Atoms migrate and the ghost plan is rebuilt every
+ * rebuild_every steps (0 or 1: every step), between the first half-step and
+ * the force call; halo must exceed rcut by twice the largest displacement
+ * between rebuilds (checked by b200dp_dd_md_thermo).  NPT is not offered
+ * here (B200DP_ERR_UNSUPPORTED). */
+b200dp_status b200dp_dd_md_start(b200dp_dd* dd, const b200dp_md_params* params, const double* vel);
+b200dp_status b200dp_dd_md_run(b200dp_dd* dd, int nsteps);
+/* Global thermodynamic state, as b200dp_md_thermo. */
+b200dp_status b200dp_dd_md_thermo(b200dp_dd* dd, double* thermo);
+/* Check of the host plan without GPUs: nranks threads stand in for the
+ * ranks.  The atoms are distributed by position; with disp [natoms*3] they
+ * are then displaced and migrated to their new owners.  Outputs, rank after
+ * rank: owned_ids [natoms] and owned_count [nranks]; ghost_ids, ghost_x /
+ * ghost_shift [.*3], ghost_origin [.*2] (owner rank, owner's row) up to
+ * ghost_cap rows, ghost_count [nranks] (B200DP_ERR_CAPACITY if the ghosts
+ * exceed ghost_cap). */
+b200dp_status b200dp_dd_plan_emulate(int nranks, const int* grid, const double* box, double halo, int natoms,
+                                     const double* coord, const double* disp, long long* owned_ids,
+                                     int* owned_count, long long* ghost_ids, double* ghost_x, double* ghost_shift,
+                                     int* ghost_origin, int* ghost_count, int ghost_cap);
 
 #ifdef __cplusplus
 }

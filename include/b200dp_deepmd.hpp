@@ -15,9 +15,11 @@
  * deepmd::hpp, so a pair style that says `namespace deepmd_compat =
  * deepmd::hpp;` compiles against this header in place of deepmd.hpp.
  *
- * Precision: B200DP_PRECISION=fp64 in the environment selects the fp64
- * engine, anything else the mixed-precision engine.  The GPU is
- * gpu_rank % (number of visible devices).
+ * Precision: a DeepPot is constructed for the mixed-precision engine
+ * (DeepPot(), DeePMD's default constructor) or for a given one
+ * (DeepPot(B200DP_FP64)); set_precision() changes it before init.  No
+ * environment variable is read.  The GPU is gpu_rank % (number of visible
+ * devices).
  *
  * Conventions are DeePMD's: coord [nall*3], atype [nall] (0-based), box [9]
  * (empty: no periodic box), nghost trailing ghost atoms; force [nall*3]
@@ -90,6 +92,12 @@ class DeepBaseModel {
 class DeepPot : public DeepBaseModel {
  public:
   DeepPot() = default;
+  explicit DeepPot(int precision) : precision_(precision) {}
+  // B200DP_FP64 or B200DP_MIXED, before init
+  void set_precision(int precision) {
+    if (eng_) throw deepmd_exception("set_precision must come before init");
+    precision_ = precision;
+  }
   explicit DeepPot(const std::string& model, const int& gpu_rank = 0, const std::string& file_content = "") {
     init(model, gpu_rank, file_content);
   }
@@ -106,8 +114,7 @@ class DeepPot : public DeepBaseModel {
     if (!file_content.empty()) throw deepmd_exception("in-memory model content is not supported; pass a file");
     b200dp_options opt;
     b200dp_options_default(&opt);
-    const char* p = std::getenv("B200DP_PRECISION");
-    opt.precision = (p && std::string(p) == "fp64") ? B200DP_FP64 : B200DP_MIXED;
+    opt.precision = precision_;
     int ndev = 1;
     if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev < 1) ndev = 1;
     opt.device = gpu_rank >= 0 ? gpu_rank % ndev : 0;
@@ -213,6 +220,7 @@ class DeepPot : public DeepBaseModel {
   }
 
   b200dp_engine* eng_ = nullptr;
+  int precision_ = B200DP_MIXED;
   b200dp_model_info info_{};
 };
 

@@ -15,6 +15,7 @@
 #include "b200dp_deepmd.hpp"
 
 #include <cstdio>
+#include <string>
 #include <vector>
 
 namespace deepmd_compat = deepmd::hpp;
@@ -27,7 +28,7 @@ static bool rd(FILE* f, T* p, size_t n) {
 }
 
 int main(int argc, char** argv) {
-  if (argc != 4) return 2;
+  if (argc != 4 && argc != 5) return 2;  // model, input, output[, "fp64"]
   FILE* in = fopen(argv[2], "rb");
   if (!in) return 3;
   int hdr[3];
@@ -49,6 +50,7 @@ int main(int argc, char** argv) {
   }
   try {
     deepmd_compat::DeepPot deep_pot;
+    if (argc > 4 && std::string(argv[4]) == "fp64") deep_pot.set_precision(B200DP_FP64);
     deep_pot.init(argv[1], 0, "");
     std::string tm;
     deep_pot.get_type_map(tm);

@@ -64,8 +64,7 @@ def test_stub_caller_matches_periodic(tmp_path, model_dir):
     model = str(model_dir / "water.b2dp")
     exe = build_stub(tmp_path)
     out = tmp_path / "out.bin"
-    env = dict(os.environ, B200DP_PRECISION="fp64")
-    r = subprocess.run([exe, model, str(inp), str(out)], capture_output=True, text=True, env=env)
+    r = subprocess.run([exe, model, str(inp), str(out), "fp64"], capture_output=True, text=True)
     assert r.returncode == 0, r.stderr
     res = np.fromfile(out, np.float64)
     e, f, v = res[0], res[1:1 + 3 * n].reshape(n, 3), res[1 + 3 * n:10 + 3 * n].reshape(3, 3)
