@@ -32,7 +32,7 @@ EXPORTS = [
     "b200dp_sel_overflow_count", "b200dp_last_nlist", "b200dp_last_descriptor", "b200dp_set_stage_timing",
     "b200dp_set_neighbor_reuse", "b200dp_neighbor_stats", "b200dp_fold_export", "b200dp_fold_connect", "b200dp_fold_origins",
     "b200dp_compute_device_fold", "b200dp_fold_finish", "b200dp_halo_publish", "b200dp_halo_gather",
-    "b200dp_peer_reduce",
+    "b200dp_peer_reduce", "b200dp_fold_scale_shifts", "b200dp_compute_device_dbox",
     "b200dp_stage_times", "b200dp_kernel_launches", "b200dp_selftest_mma", "b200dp_build_nlist_noalloc",
     "b200dp_direct_bind", "b200dp_direct_energy_force", "b200dp_direct_destination_only_ready",
     "b200dp_bind_direct_neighbor_view", "b200dp_get_direct_neighbor_view", "b200dp_direct_set_need_virial",
@@ -567,11 +567,12 @@ class DD:
         self._check(self.L.b200dp_dd_get_forces(self.h, stream or None, force_ptr or None, ev_ptr or None))
 
     def md_start(self, masses, dt=0.0005, ensemble=NVE, vel=None, t_init=0.0, t_target=300.0, t_damp=0.05, chain=3,
-                 seed=0, rebuild_every=10):
+                 seed=0, rebuild_every=10, p_target=1.0, p_damp=0.5, pchain=3):
         p = MDParams()
         self.L.b200dp_md_params_default(ctypes.byref(p))
         p.dt, p.ensemble, p.chain = dt, ensemble, chain
         p.t_target, p.t_damp, p.t_init, p.seed = t_target, t_damp, t_init, seed
+        p.p_target, p.p_damp, p.pchain = p_target, p_damp, pchain
         p.rebuild_every = rebuild_every
         for t, m in enumerate(masses):
             p.mass[t] = m

@@ -185,6 +185,14 @@ struct Decomp {
     if (dir < 0 && cell[dim] == 0) return L[dim];
     return 0.0;
   }
+  // the box scaled by `r` about the origin (a barostat step): every bound scales with it
+  void scale(double r) {
+    for (int d = 0; d < 3; ++d) {
+      L[d] *= r;
+      lo[d] *= r;
+      hi[d] *= r;
+    }
+  }
   bool owns(const double* w) const {
     for (int d = 0; d < 3; ++d)
       if (!(w[d] >= lo[d] && w[d] < hi[d])) return false;
@@ -339,6 +347,9 @@ struct b200dp_dd {
   long long step = 0, last_rebuild = 0;
   std::vector<double> x_at_rebuild;
   double max_move = 0;
+  // NPT (isotropic, host-side scalars as the single-GPU driver)
+  HostChain tch, pch;
+  double omega_dot = 0, w_mass = 0, vol0 = 0, t_current = 0, vir_trace = 0;
   std::string err;
   ~b200dp_dd() {
     if (stream) {
@@ -505,6 +516,74 @@ b200dp_status md_step(b200dp_dd* dd) {
     count_launch();
     k_md_scale<<<grid, kMdThreads, 0, st>>>(dd->nown, dd->v.p, dd->chain.p);
   }
+  return cudaGetLastError() == cudaSuccess ? B200DP_OK : B200DP_ERR_CUDA;
+}
+
+// One NPT step in LAMMPS' fix npt iso order (as the single-GPU driver): the
+// barostat and thermostat scalars on the host of every rank, fed by the
+// global kinetic energy and virial of the rendezvous (the same bits on every
+// rank, so every rank computes the same box); one host read per step.
+b200dp_status npt_step(b200dp_dd* dd) {
+  const b200dp_md_params& p = dd->mp;
+  const int n = dd->nown;
+  const double natoms = (double)dd->natoms;
+  const double dt = p.dt, dthalf = 0.5 * dt, dtf = 0.5 * dt * kFtm2v;
+  const double kt = kBoltz * p.t_target, dof_boltz = dd->dof * kBoltz;
+  const double ke_target = dof_boltz * p.t_target, p_hydro = p.p_target;
+  cudaStream_t st = dd->stream;
+  const int grid = std::max(1, std::min(kRedBlocks * 4, (n + kMdThreads - 1) / kMdThreads));
+  auto omega_force = [&](double t_cur, double vir_tr) {
+    const double vol = dd->box[0] * dd->box[4] * dd->box[8];
+    const double p_cur = (dof_boltz * t_cur + vir_tr) / (3.0 * vol) * kNktv2p;
+    const double mtk1 = dof_boltz * t_cur / (3.0 * natoms);
+    dd->omega_dot += ((p_cur - p_hydro) * vol / (dd->w_mass * kNktv2p) + mtk1 / dd->w_mass) * dthalf;
+  };
+  // ---- initial half
+  dd->pch.barostat(dd->omega_dot, dd->w_mass, kt, dt);
+  const double s_t = dd->tch.thermostat(dd->t_current, dof_boltz, ke_target, kt, dt);
+  omega_force(dd->t_current, dd->vir_trace);
+  const double mtk2 = 3.0 * dd->omega_dot / (3.0 * natoms);
+  const double fp = std::exp(-0.25 * dt * (dd->omega_dot + mtk2));
+  const double e = std::exp(dthalf * dd->omega_dot);
+  count_launch();
+  k_npt_first<<<grid, kMdThreads, 0, st>>>(n, dd->x.p, dd->v.p, dd->f.p, dd->minv.p, s_t * fp * fp, dtf, dt, e);
+  const double r = e * e;
+  for (int d = 0; d < 3; ++d) dd->box[4 * d] *= r;
+  dd->dcmp.scale(r);
+  for (int d = 0; d < 3; ++d) {
+    dd->region[d] = dd->dcmp.lo[d] - dd->dcmp.halo;
+    dd->region[3 + d] = dd->dcmp.hi[d] + dd->dcmp.halo;
+  }
+  ++dd->step;
+  b200dp_status rc;
+  const int every = std::max(1, p.rebuild_every);
+  if (dd->step - dd->last_rebuild >= every) {
+    if ((rc = rebuild(dd)) != B200DP_OK) return rc;
+    dd->last_rebuild = dd->step;
+  } else {
+    const double ratio[3] = {r, r, r};
+    if ((rc = b200dp_fold_scale_shifts(dd->engine, st, ratio)) != B200DP_OK) return rc;
+  }
+  if ((rc = force_call(dd, st)) != B200DP_OK) return rc;
+  // ---- final half
+  count_launch();
+  k_npt_second<<<kRedBlocks, kMdThreads, 0, st>>>(n, dd->v.p, dd->f.p, dd->minv.p, dd->mass.p, dtf, fp * fp,
+                                                  dd->part.p);
+  count_launch();
+  k_dd_sum<<<1, 32, 0, st>>>(dd->part.p, kRedBlocks, dd->ke.p);
+  if ((rc = b200dp_peer_reduce(dd->engine, st, 1, dd->ke.p, dd->ke.p, dd->max_polls)) != B200DP_OK) return rc;
+  double mv2 = 0, ev[10];
+  if (cudaMemcpyAsync(&mv2, dd->ke.p, sizeof(double), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaMemcpyAsync(ev, dd->ev.p, sizeof(ev), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return dd_fail(dd, "reading the global kinetic energy and virial failed");
+  dd->t_current = mv2 * kMvv2e / dof_boltz;
+  dd->vir_trace = ev[1] + ev[5] + ev[9];
+  omega_force(dd->t_current, dd->vir_trace);
+  const double s_t2 = dd->tch.thermostat(dd->t_current, dof_boltz, ke_target, kt, dt);
+  count_launch();
+  k_md_scale_by<<<grid, kMdThreads, 0, st>>>(n, dd->v.p, s_t2);
+  dd->pch.barostat(dd->omega_dot, dd->w_mass, kt, dt);
   return cudaGetLastError() == cudaSuccess ? B200DP_OK : B200DP_ERR_CUDA;
 }
 
@@ -681,10 +760,12 @@ b200dp_status b200dp_dd_md_start(b200dp_dd* dd, const b200dp_md_params* params, 
   if (!dd || !params) return B200DP_ERR_INVALID;
   if (cudaSetDevice(dd->device) != cudaSuccess) return B200DP_ERR_CUDA;
   const b200dp_md_params& p = *params;
-  if (!(p.dt > 0) || (p.ensemble != B200DP_MD_NVE && p.ensemble != B200DP_MD_NVT))
-    return dd_fail(dd, "the decomposed driver runs NVE and NVT", B200DP_ERR_UNSUPPORTED);
-  if (p.ensemble == B200DP_MD_NVT && (p.chain < 1 || p.chain > kMaxChain || !(p.t_target > 0) || !(p.t_damp > 0)))
+  if (!(p.dt > 0) || (p.ensemble != B200DP_MD_NVE && p.ensemble != B200DP_MD_NVT && p.ensemble != B200DP_MD_NPT))
     return B200DP_ERR_INVALID;
+  if (p.ensemble != B200DP_MD_NVE && (p.chain < 1 || p.chain > kMaxChain || !(p.t_target > 0) || !(p.t_damp > 0)))
+    return B200DP_ERR_INVALID;
+  if (p.ensemble == B200DP_MD_NPT && (p.pchain < 1 || p.pchain > kMaxChain || !(p.p_damp > 0)))
+    return B200DP_ERR_INVALID;  // the box is orthorhombic (checked at creation); isotropic barostat
   if (!vel && !(p.t_init > 0)) return B200DP_ERR_INVALID;
   const int natoms = dd->natoms;
   std::vector<double> mass(natoms);
@@ -714,7 +795,7 @@ b200dp_status b200dp_dd_md_start(b200dp_dd* dd, const b200dp_md_params* params, 
   ch.t_current = mv2 * kMvv2e / (dd->dof * kBoltz);
   ChainParams& cp = dd->cp;
   std::memset(&cp, 0, sizeof(cp));
-  if (p.ensemble == B200DP_MD_NVT) {
+  if (p.ensemble != B200DP_MD_NVE) {
     const double w = 1.0 / p.t_damp;
     cp.M = p.chain;
     cp.dof_boltz = dd->dof * kBoltz;
@@ -737,6 +818,22 @@ b200dp_status b200dp_dd_md_start(b200dp_dd* dd, const b200dp_md_params* params, 
   // forces and kinetic energy of the initial configuration
   if ((rc = force_call(dd, dd->stream)) != B200DP_OK) return rc;
   if ((rc = global_mv2(dd, false, 0.0)) != B200DP_OK) return rc;
+  if (p.ensemble == B200DP_MD_NPT) {
+    const double wp = 1.0 / p.p_damp, kt = kBoltz * p.t_target;
+    dd->tch = HostChain();
+    dd->pch = HostChain();
+    dd->tch.init(p.chain, cp.mass[0], p.chain > 1 ? cp.mass[1] : 0.0, cp.boltz_t);
+    dd->pch.init(p.pchain, kt / (wp * wp), kt / (wp * wp), kt);
+    dd->w_mass = (natoms + 1) * kt / (wp * wp);
+    dd->vol0 = dd->box[0] * dd->box[4] * dd->box[8];
+    dd->omega_dot = 0;
+    dd->t_current = ch.t_current;
+    double ev[10];
+    if (cudaMemcpyAsync(ev, dd->ev.p, sizeof(ev), cudaMemcpyDeviceToHost, dd->stream) != cudaSuccess ||
+        cudaStreamSynchronize(dd->stream) != cudaSuccess)
+      return B200DP_ERR_CUDA;
+    dd->vir_trace = ev[1] + ev[5] + ev[9];
+  }
   return cudaStreamSynchronize(dd->stream) == cudaSuccess ? B200DP_OK : B200DP_ERR_CUDA;
 }
 
@@ -744,7 +841,7 @@ b200dp_status b200dp_dd_md_run(b200dp_dd* dd, int nsteps) {
   if (!dd || !dd->md || nsteps < 0) return B200DP_ERR_INVALID;
   if (cudaSetDevice(dd->device) != cudaSuccess) return B200DP_ERR_CUDA;
   for (int s = 0; s < nsteps; ++s) {
-    const b200dp_status rc = md_step(dd);
+    const b200dp_status rc = dd->mp.ensemble == B200DP_MD_NPT ? npt_step(dd) : md_step(dd);
     if (rc != B200DP_OK) return rc;
   }
   return B200DP_OK;
@@ -768,18 +865,23 @@ b200dp_status b200dp_dd_md_thermo(b200dp_dd* dd, double* thermo) {
   if (dd->max_move > 0.5 * (dd->dcmp.halo - info.rcut))
     return dd_fail(dd, "an atom moved more than (halo - rcut) / 2 between ghost plans: rebuild more often",
                    B200DP_ERR_CAPACITY);
-  const bool nvt = dd->mp.ensemble == B200DP_MD_NVT;
-  // kinetic energy: after the chain's rescaling (NVT) the state's temperature, else the reduced sum
-  const double temp = nvt ? ch.t_current : mv2 * kMvv2e / (dd->dof * kBoltz);
+  const bool nvt = dd->mp.ensemble == B200DP_MD_NVT, npt = dd->mp.ensemble == B200DP_MD_NPT;
+  // kinetic energy: after the chain's rescaling the chain's temperature (NVT: device state, NPT:
+  // the host scalars), else the reduced sum
+  const double temp = nvt ? ch.t_current : npt ? dd->t_current : mv2 * kMvv2e / (dd->dof * kBoltz);
   const double ke = 0.5 * dd->dof * kBoltz * temp;
   double e_chain = 0;
-  if (nvt) {
+  const double vol = dd->box[0] * dd->box[4] * dd->box[8];
+  if (npt) {
+    const double kt = kBoltz * dd->mp.t_target;
+    e_chain = dd->tch.energy(dd->cp.ke_target, kt) + dd->pch.energy(kt, kt) +
+              1.5 * dd->w_mass * dd->omega_dot * dd->omega_dot + dd->mp.p_target * (vol - dd->vol0) / kNktv2p;
+  } else if (nvt) {
     const ChainParams& cp = dd->cp;
     e_chain = cp.ke_target * ch.eta[0];
     for (int i = 1; i < cp.M; ++i) e_chain += cp.boltz_t * ch.eta[i];
     for (int i = 0; i < cp.M; ++i) e_chain += 0.5 * cp.mass[i] * ch.eta_dot[i] * ch.eta_dot[i];
   }
-  const double vol = dd->box[0] * dd->box[4] * dd->box[8];
   thermo[0] = (double)dd->step;
   thermo[1] = ev[0];
   thermo[2] = ke;

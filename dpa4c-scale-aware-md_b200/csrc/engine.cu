@@ -493,7 +493,10 @@ b200dp_status Engine::ensure_buffers(int nloc, int nall, int ncells, int ncand) 
 // or the region (open).
 b200dp_status Engine::make_grid(int nall, const double* box, const double* region, bool periodic, GridSpec& g) {
   const long long max_cells = std::max<long long>(4096, 4LL * nall);
-  switch (b200dp::make_grid(periodic, box, region, hm.rcut, max_cells, g)) {
+  const int rcode = periodic && dbox_dev
+                        ? b200dp::make_grid_dbox(box, dbox_min, dbox_bb.as<double>(), hm.rcut, max_cells, g)
+                        : b200dp::make_grid(periodic, box, region, hm.rcut, max_cells, g);
+  switch (rcode) {
     case 0:
       return B200DP_OK;
     case 1:
@@ -754,6 +757,7 @@ b200dp_status Engine::compute_device(cudaStream_t st, int nloc, int nghost, cons
   if (rc != B200DP_OK) return rc;
   B200DP_CUDA_TRY(cudaSetDevice(opt.device));
   mark(st, 0);
+  if (periodic && dbox_dev) launch_box_setup(st, dbox_dev, dbox_bb.as<double>());
   int* err_d = err_buf.as<int>();
   B200DP_CUDA_TRY(cudaMemsetAsync(err_d, 0, sizeof(int) * kErrCount, st));
   if (nall == 0) {
@@ -768,7 +772,9 @@ b200dp_status Engine::compute_device(cudaStream_t st, int nloc, int nghost, cons
     // (the rebuild kernels are gated by the device-side check, so no host
     // round trip); the rows are formed from the candidates on every call
     GridSpec gc;
-    switch (b200dp::make_grid(true, box, nullptr, hm.rcut + vl_skin, std::max<long long>(4096, 4LL * nall), gc)) {
+    const long long mc = std::max<long long>(4096, 4LL * nall);
+    switch (dbox_dev ? b200dp::make_grid_dbox(box, dbox_min, dbox_bb.as<double>(), hm.rcut + vl_skin, mc, gc)
+                     : b200dp::make_grid(true, box, nullptr, hm.rcut + vl_skin, mc, gc)) {
       case 0:
         break;
       case 1:
@@ -848,6 +854,24 @@ b200dp_status Engine::compute_device(cudaStream_t st, int nloc, int nghost, cons
   if (rc != B200DP_OK) return rc;
   B200DP_CUDA_TRY(cudaGetLastError());
   return B200DP_OK;
+}
+
+b200dp_status Engine::compute_device_dbox(cudaStream_t st, int nloc, const double* d_coord, const int* d_atype,
+                                          const double* box_ref, double min_scale, const double* d_box,
+                                          double* d_energy, double* d_force, double* d_virial) {
+  g_err_sink = &err;
+  if (!box_ref || !d_box || !(min_scale > 0) || min_scale > 1) {
+    err = "compute_device_dbox: a reference box, a device box and 0 < min_scale <= 1";
+    return B200DP_ERR_INVALID;
+  }
+  B200DP_CUDA_TRY(dbox_bb.ensure(sizeof(double) * 18));
+  dbox_dev = d_box;
+  dbox_min = min_scale;
+  const b200dp_status rc = compute_device(st, nloc, 0, d_coord, d_atype, box_ref, nullptr, d_energy, d_force, d_virial,
+                                          nullptr, nullptr);
+  dbox_dev = nullptr;
+  dbox_min = 1.0;
+  return rc;
 }
 
 b200dp_status Engine::check() {
@@ -982,6 +1006,17 @@ b200dp_status Engine::fold_origins(int nghost, const int* d_origin, const double
       B200DP_CUDA_TRY(cudaMemcpy(pf_shift.ptr, d_shift, sizeof(double) * 3 * nghost, cudaMemcpyDeviceToDevice));
   }
   pf_nghost = nghost;
+  return B200DP_OK;
+}
+
+b200dp_status Engine::fold_scale_shifts(cudaStream_t st, const double* ratio) {
+  g_err_sink = &err;
+  if (!ratio || !pf_has_shift) {
+    err = "fold_scale_shifts: set the ghost origins with their shifts first";
+    return B200DP_ERR_INVALID;
+  }
+  launch_scale_shifts(st, pf_nghost, pf_shift.as<double>(), ratio);
+  B200DP_CUDA_TRY(cudaGetLastError());
   return B200DP_OK;
 }
 
@@ -1396,6 +1431,19 @@ b200dp_status b200dp_fold_connect(b200dp_engine* engine, int nranks, int rank, c
 b200dp_status b200dp_fold_origins(b200dp_engine* engine, int nghost, const int* d_origin, const double* d_shift) {
   if (!engine) return B200DP_ERR_INVALID;
   return engine->e.fold_origins(nghost, d_origin, d_shift);
+}
+
+b200dp_status b200dp_compute_device_dbox(b200dp_engine* engine, void* stream, int nlocal, const double* d_coord,
+                                         const int* d_atype, const double* box_ref, double min_scale,
+                                         const double* d_box, double* d_energy, double* d_force, double* d_virial) {
+  if (!engine) return B200DP_ERR_INVALID;
+  return engine->e.compute_device_dbox(static_cast<cudaStream_t>(stream), nlocal, d_coord, d_atype, box_ref,
+                                       min_scale, d_box, d_energy, d_force, d_virial);
+}
+
+b200dp_status b200dp_fold_scale_shifts(b200dp_engine* engine, void* stream, const double* ratio) {
+  if (!engine) return B200DP_ERR_INVALID;
+  return engine->e.fold_scale_shifts(static_cast<cudaStream_t>(stream), ratio);
 }
 
 b200dp_status b200dp_halo_publish(b200dp_engine* engine, void* stream, int nlocal, const double* d_coord) {

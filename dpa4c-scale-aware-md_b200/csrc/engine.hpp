@@ -142,6 +142,13 @@ struct Engine {
   b200dp_status compute_device(cudaStream_t st, int nloc, int nghost, const double* d_coord, const int* d_atype,
                                const double* box, const double* region, double* d_energy, double* d_force,
                                double* d_virial, double* d_atom_energy, double* d_atom_virial);
+  // periodic call whose box lives in device memory (d_box); box_ref x min_scale sizes the grid
+  b200dp_status compute_device_dbox(cudaStream_t st, int nloc, const double* d_coord, const int* d_atype,
+                                    const double* box_ref, double min_scale, const double* d_box, double* d_energy,
+                                    double* d_force, double* d_virial);
+  const double* dbox_dev = nullptr;  // set during compute_device_dbox
+  double dbox_min = 1.0;
+  DevBuf dbox_bb;                    // [B | Binv] of the device box
   // Canonical destination-major graph (n nodes, all local), device pointers.
   b200dp_status compute_graph(cudaStream_t st, int n, const int64_t* d_atype64, const int64_t* d_row_ptr,
                               const uint32_t* d_source, const float* d_edge_vec, double* d_atom_energy,
@@ -159,6 +166,7 @@ struct Engine {
   b200dp_status fold_export(int cap, void* handle);
   b200dp_status fold_connect(int nranks, int rank, const void* handles);
   b200dp_status fold_origins(int nghost, const int* d_origin, const double* d_shift);
+  b200dp_status fold_scale_shifts(cudaStream_t st, const double* ratio);
   b200dp_status halo_publish(cudaStream_t st, int nloc, const double* d_coord);
   b200dp_status halo_gather(cudaStream_t st, int nloc, int nghost, double* d_coord);
   b200dp_status compute_device_fold(cudaStream_t st, int nloc, int nghost, const double* d_coord,

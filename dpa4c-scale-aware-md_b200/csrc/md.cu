@@ -26,9 +26,16 @@
 //   force call in the new box
 //   final:   v += dt/2 F/m; v *= exp(-dt/2 (omega_dot + mtk2)); temperature and
 //            pressure; omega_dot += dt/2 F_omega; thermostat chain; barostat chain
-// The scalar chains run on the host (one 12-number read per step); every
-// per-atom operation is a device kernel.  The box is scaled about the origin
-// (LAMMPS scales about the box centre; the two differ by a uniform translation).
+// The scalar chains and the box live on the device too (NptState, advanced by
+// one-thread kernels), and the force call reads the box from device memory
+// (b200dp_compute_device_dbox), so an NPT step needs no host round trip and
+// whole neighbour cycles replay as CUDA graphs, as for NVT.  The host reads the
+// state back only at its synchronisation points (thermo, snapshot, restore),
+// where it also re-references the binning grid when the box has drifted more
+// than 5 % from the box the grid was built for (the grid serves boxes down to
+// 90 % of it; a step that goes lower sets a flag reported as an error).  The
+// box is scaled about the origin (LAMMPS scales about the box centre; the two
+// differ by a uniform translation).
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -47,9 +54,51 @@ namespace {
 
 #include "md_kernels.cuh"
 
-// v = v * sv + dtf F / m ; x = e (e x + dt v)   (NPT first half: remap, drift, remap)
-__global__ void k_npt_first(int n, double* __restrict__ x, double* __restrict__ v, const double* __restrict__ f,
-                            const double* __restrict__ minv, double sv, double dtf, double dt, double e) {
+// Device state of the NPT integrator: the two chains, the barostat scalars,
+// the box and the step's velocity / position factors.
+struct NptState {
+  HostChain tch, pch;
+  double omega_dot, w_mass, vol0, t_current, vir_trace, epot;
+  double box[9];
+  double sv1, e, fp2, s_t2;
+  int box_low;  // the box fell below the range the binning grid serves
+};
+struct NptParams {
+  double dt, kt, dof_boltz, ke_target, p_hydro, natoms;
+  double min_box[3];
+};
+
+__device__ void npt_omega_force(const NptParams& p, NptState* s, double t_cur, double vir_tr) {
+  const double vol = s->box[0] * s->box[4] * s->box[8];
+  const double p_cur = (p.dof_boltz * t_cur + vir_tr) / (3.0 * vol) * kNktv2p;
+  const double mtk1 = p.dof_boltz * t_cur / (3.0 * p.natoms);
+  s->omega_dot += ((p_cur - p.p_hydro) * vol / (s->w_mass * kNktv2p) + mtk1 / s->w_mass) * (0.5 * p.dt);
+}
+
+// Initial half of an NPT step: barostat chain, thermostat chain, the barostat
+// force, the velocity / remap factors and the new box.
+__global__ void k_npt_pre(NptParams p, NptState* __restrict__ s) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  s->pch.barostat(s->omega_dot, s->w_mass, p.kt, p.dt);
+  const double s_t = s->tch.thermostat(s->t_current, p.dof_boltz, p.ke_target, p.kt, p.dt);
+  npt_omega_force(p, s, s->t_current, s->vir_trace);
+  const double mtk2 = 3.0 * s->omega_dot / (3.0 * p.natoms);
+  const double fp = exp(-0.25 * p.dt * (s->omega_dot + mtk2));
+  const double e = exp(0.5 * p.dt * s->omega_dot);
+  s->sv1 = s_t * fp * fp;
+  s->e = e;
+  s->fp2 = fp * fp;
+  for (int d = 0; d < 3; ++d) {
+    s->box[4 * d] *= e * e;
+    if (s->box[4 * d] < p.min_box[d]) s->box_low = 1;
+  }
+}
+
+// k_npt_first / k_npt_second with their factors from the device state.
+__global__ void k_npt_first_dev(int n, double* __restrict__ x, double* __restrict__ v, const double* __restrict__ f,
+                                const double* __restrict__ minv, const NptState* __restrict__ s, double dtf,
+                                double dt) {
+  const double sv = s->sv1, e = s->e;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     const double w = dtf * minv[i];
 #pragma unroll
@@ -61,13 +110,14 @@ __global__ void k_npt_first(int n, double* __restrict__ x, double* __restrict__ 
   }
 }
 
-// v = (v + dtf F / m) * sv, with per-block partial sums of m v^2
-__global__ void __launch_bounds__(kMdThreads) k_npt_second(int n, double* __restrict__ v,
-                                                           const double* __restrict__ f,
-                                                           const double* __restrict__ minv,
-                                                           const double* __restrict__ mass, double dtf, double sv,
-                                                           double* __restrict__ part) {
+__global__ void __launch_bounds__(kMdThreads) k_npt_second_dev(int n, double* __restrict__ v,
+                                                               const double* __restrict__ f,
+                                                               const double* __restrict__ minv,
+                                                               const double* __restrict__ mass, double dtf,
+                                                               const NptState* __restrict__ s,
+                                                               double* __restrict__ part) {
   __shared__ double sh[kMdThreads / 32];
+  const double sv = s->fp2;
   double acc = 0.0;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     const double w = dtf * minv[i];
@@ -90,74 +140,25 @@ __global__ void __launch_bounds__(kMdThreads) k_npt_second(int n, double* __rest
   }
 }
 
-__global__ void k_md_scale_by(int n, double* __restrict__ v, double s) {
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < 3 * n; i += gridDim.x * blockDim.x) v[i] *= s;
+// Final half: temperature from the kinetic-energy partials, the virial's trace,
+// the barostat force, the thermostat (its factor applied by k_npt_scale) and
+// the barostat chain.  One warp.
+__global__ void k_npt_post(NptParams p, NptState* __restrict__ s, const double* __restrict__ part, int nparts,
+                           const double* __restrict__ vir, const double* __restrict__ epot) {
+  const double mv2 = sum_parts(part, nparts);
+  if (threadIdx.x != 0) return;
+  s->t_current = mv2 * kMvv2e / p.dof_boltz;
+  s->vir_trace = vir[0] + vir[4] + vir[8];
+  s->epot = epot[0];
+  npt_omega_force(p, s, s->t_current, s->vir_trace);
+  s->s_t2 = s->tch.thermostat(s->t_current, p.dof_boltz, p.ke_target, p.kt, p.dt);
+  s->pch.barostat(s->omega_dot, s->w_mass, p.kt, p.dt);
 }
 
-// Host Nose-Hoover chain (same recurrence as k_md_chain) for the NPT path.
-struct HostChain {
-  int M = 0;
-  double eta[kMaxChain] = {0}, eta_dot[kMaxChain + 1] = {0}, eta_dotdot[kMaxChain] = {0}, mass[kMaxChain] = {0};
-  void init(int m, double q0, double qi, double boltz_t) {
-    M = m;
-    mass[0] = q0;
-    for (int i = 1; i < M; ++i) mass[i] = qi;
-    for (int i = 1; i < M; ++i) eta_dotdot[i] = (mass[i - 1] * eta_dot[i - 1] * eta_dot[i - 1] - boltz_t) / mass[i];
-  }
-  // Thermostat half-step for kinetic energy `ke` (target ke_target); returns the velocity factor.
-  double thermostat(double& t_current, double dof_boltz, double ke_target, double boltz_t, double dt) {
-    const double dt4 = 0.25 * dt, dt8 = 0.125 * dt, dthalf = 0.5 * dt;
-    eta_dotdot[0] = (dof_boltz * t_current - ke_target) / mass[0];
-    double expfac = 1.0;
-    for (int i = M - 1; i > 0; --i) {
-      expfac = std::exp(-dt8 * eta_dot[i + 1]);
-      eta_dot[i] = (eta_dot[i] * expfac + eta_dotdot[i] * dt4) * expfac;
-    }
-    expfac = std::exp(-dt8 * eta_dot[1]);
-    eta_dot[0] = (eta_dot[0] * expfac + eta_dotdot[0] * dt4) * expfac;
-    const double factor = std::exp(-dthalf * eta_dot[0]);
-    t_current *= factor * factor;
-    eta_dotdot[0] = (dof_boltz * t_current - ke_target) / mass[0];
-    for (int i = 0; i < M; ++i) eta[i] += dthalf * eta_dot[i];
-    eta_dot[0] = (eta_dot[0] * expfac + eta_dotdot[0] * dt4) * expfac;
-    for (int i = 1; i < M; ++i) {
-      expfac = std::exp(-dt8 * eta_dot[i + 1]);
-      eta_dotdot[i] = (mass[i - 1] * eta_dot[i - 1] * eta_dot[i - 1] - boltz_t) / mass[i];
-      eta_dot[i] = (eta_dot[i] * expfac + eta_dotdot[i] * dt4) * expfac;
-    }
-    return factor;
-  }
-  // Barostat-chain half-step (FixNH::nhc_press_integrate, isotropic): scales
-  // omega_dot; kinetic energy 3 W omega_dot^2 against kB T0.
-  void barostat(double& omega_dot, double w_mass, double kt, double dt) {
-    const double dt4 = 0.25 * dt, dt8 = 0.125 * dt, dthalf = 0.5 * dt;
-    double ke = 3.0 * w_mass * omega_dot * omega_dot;
-    eta_dotdot[0] = (ke - kt) / mass[0];
-    double expfac = 1.0;
-    for (int i = M - 1; i > 0; --i) {
-      expfac = std::exp(-dt8 * eta_dot[i + 1]);
-      eta_dot[i] = (eta_dot[i] * expfac + eta_dotdot[i] * dt4) * expfac;
-    }
-    expfac = std::exp(-dt8 * eta_dot[1]);
-    eta_dot[0] = (eta_dot[0] * expfac + eta_dotdot[0] * dt4) * expfac;
-    for (int i = 0; i < M; ++i) eta[i] += dthalf * eta_dot[i];
-    omega_dot *= std::exp(-dthalf * eta_dot[0]);
-    ke = 3.0 * w_mass * omega_dot * omega_dot;
-    eta_dotdot[0] = (ke - kt) / mass[0];
-    eta_dot[0] = (eta_dot[0] * expfac + eta_dotdot[0] * dt4) * expfac;
-    for (int i = 1; i < M; ++i) {
-      expfac = std::exp(-dt8 * eta_dot[i + 1]);
-      eta_dotdot[i] = (mass[i - 1] * eta_dot[i - 1] * eta_dot[i - 1] - kt) / mass[i];
-      eta_dot[i] = (eta_dot[i] * expfac + eta_dotdot[i] * dt4) * expfac;
-    }
-  }
-  double energy(double first_kt, double kt) const {
-    double e = first_kt * eta[0];
-    for (int i = 1; i < M; ++i) e += kt * eta[i];
-    for (int i = 0; i < M; ++i) e += 0.5 * mass[i] * eta_dot[i] * eta_dot[i];
-    return e;
-  }
-};
+__global__ void k_npt_scale(int n, double* __restrict__ v, const NptState* __restrict__ s) {
+  const double f = s->s_t2;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < 3 * n; i += gridDim.x * blockDim.x) v[i] *= f;
+}
 
 template <class T>
 struct Dev {
@@ -190,10 +191,10 @@ struct SnapHeader {
   double dt;
   unsigned long long bytes;
 };
-constexpr char kSnapMagic[8] = {'B', '2', 'D', 'P', 'M', 'D', 'S', '1'};
+constexpr char kSnapMagic[8] = {'B', '2', 'D', 'P', 'M', 'D', 'S', '2'};
 constexpr size_t snap_align(size_t b) { return (b + 255) & ~(size_t)255; }
 struct SnapLayout {
-  size_t x, v, f, e, vir, part, chain, total;
+  size_t x, v, f, e, vir, part, chain, npt, total;
   explicit SnapLayout(int n) {
     const size_t n3 = sizeof(double) * 3 * (size_t)n;
     x = snap_align(sizeof(SnapHeader));
@@ -203,7 +204,8 @@ struct SnapLayout {
     vir = e + snap_align(sizeof(double));
     part = vir + snap_align(9 * sizeof(double));
     chain = part + snap_align(kRedBlocks * sizeof(double));
-    total = chain + snap_align(sizeof(Chain));
+    npt = chain + snap_align(sizeof(Chain));
+    total = npt + snap_align(sizeof(NptState));
   }
 };
 }  // namespace
@@ -220,18 +222,73 @@ struct b200dp_md {
   Dev<int> atype;
   Dev<Chain> chain;
   ChainParams cp{};
-  // NPT (host-side scalars)
+  // NPT: host copies of the device state (refreshed at the synchronisation
+  // points) and the reference box of the binning grid
   HostChain tch, pch;
   double omega_dot = 0, w_mass = 0, vol0 = 0, t_current = 0, vir_trace = 0, epot = 0;
+  Dev<NptState> npt;
+  double box_ref[9] = {0};
   std::string err;
   SnapHeader snap_stage{};
-  // NVE / NVT: one neighbour-rebuild cycle of steps recorded as a CUDA graph
-  // and replayed (every step's work is enqueued with no host decision left,
-  // the skin check and rebuild being gated on the device)
+  // one neighbour-rebuild cycle of steps recorded as a CUDA graph and replayed
+  // (every step's work is enqueued with no host decision left, the skin check
+  // and rebuild being gated on the device, the NPT scalars advanced there)
   cudaGraphExec_t cycle = nullptr;
   int cycle_len = 0;
   bool cycle_failed = false;
 };
+
+namespace {
+constexpr double kGridMinScale = 0.9;   // the grid serves boxes down to this fraction of the reference
+constexpr double kGridReref = 0.05;     // re-reference when the box drifted this much (relative)
+
+NptParams npt_params(const b200dp_md* md) {
+  NptParams q;
+  q.dt = md->p.dt;
+  q.kt = kBoltz * md->p.t_target;
+  q.dof_boltz = md->dof * kBoltz;
+  q.ke_target = q.dof_boltz * md->p.t_target;
+  q.p_hydro = md->p.p_target;
+  q.natoms = (double)md->n;
+  for (int d = 0; d < 3; ++d) q.min_box[d] = kGridMinScale * md->box_ref[4 * d];
+  return q;
+}
+double* npt_box(b200dp_md* md) { return reinterpret_cast<double*>(reinterpret_cast<char*>(md->npt.p) + offsetof(NptState, box)); }
+
+// Host copies of the device NPT state (the caller synchronised the stream); a
+// box that drifted from the grid's reference re-references the grid (and drops
+// the recorded cycle, whose calls carry the old grid).
+b200dp_status npt_refresh(b200dp_md* md) {
+  NptState h;
+  if (cudaMemcpyAsync(&h, md->npt.p, sizeof(h), cudaMemcpyDeviceToHost, md->stream) != cudaSuccess ||
+      cudaStreamSynchronize(md->stream) != cudaSuccess)
+    return B200DP_ERR_CUDA;
+  md->tch = h.tch;
+  md->pch = h.pch;
+  md->omega_dot = h.omega_dot;
+  md->w_mass = h.w_mass;
+  md->vol0 = h.vol0;
+  md->t_current = h.t_current;
+  md->vir_trace = h.vir_trace;
+  md->epot = h.epot;
+  std::memcpy(md->box, h.box, sizeof(md->box));
+  md->volume = md->box[0] * md->box[4] * md->box[8];
+  if (h.box_low) {
+    md->err = "the box shrank below the range of the binning grid within one run call";
+    return B200DP_ERR_CAPACITY;
+  }
+  bool reref = false;
+  for (int d = 0; d < 3; ++d)
+    reref = reref || std::fabs(md->box[4 * d] / md->box_ref[4 * d] - 1.0) > kGridReref;
+  if (reref) {
+    std::memcpy(md->box_ref, md->box, sizeof(md->box_ref));
+    if (md->cycle) cudaGraphExecDestroy(md->cycle);
+    md->cycle = nullptr;
+    md->cycle_failed = false;
+  }
+  return B200DP_OK;
+}
+}  // namespace
 
 extern "C" {
 
@@ -368,64 +425,68 @@ b200dp_status b200dp_md_create(b200dp_engine* engine, int natoms, const double* 
   }
   count_launch();
   k_md_ke<<<kRedBlocks, kMdThreads, 0, md->stream>>>(natoms, md->v.p, md->mass.p, md->part.p);
+  if (p.ensemble == B200DP_MD_NPT) {
+    // the device NPT state, with the virial of the initial forces
+    double vir[9];
+    NptState h;
+    std::memset(&h, 0, sizeof(h));
+    if (md->npt.alloc(1) != cudaSuccess ||
+        cudaMemcpyAsync(vir, md->vir.p, sizeof(vir), cudaMemcpyDeviceToHost, md->stream) != cudaSuccess ||
+        cudaStreamSynchronize(md->stream) != cudaSuccess) {
+      cudaStreamDestroy(md->stream);
+      delete md;
+      return B200DP_ERR_CUDA;
+    }
+    md->vir_trace = vir[0] + vir[4] + vir[8];
+    h.tch = md->tch;
+    h.pch = md->pch;
+    h.w_mass = md->w_mass;
+    h.vol0 = md->vol0;
+    h.t_current = md->t_current;
+    h.vir_trace = md->vir_trace;
+    std::memcpy(h.box, md->box, sizeof(h.box));
+    std::memcpy(md->box_ref, md->box, sizeof(md->box_ref));
+    if (cudaMemcpy(md->npt.p, &h, sizeof(h), cudaMemcpyHostToDevice) != cudaSuccess) {
+      cudaStreamDestroy(md->stream);
+      delete md;
+      return B200DP_ERR_CUDA;
+    }
+  }
   *out = md;
   return cudaGetLastError() == cudaSuccess ? B200DP_OK : B200DP_ERR_CUDA;
 }
 
-// One NPT step (host-side scalars, device kernels), LAMMPS fix npt iso order.
-static b200dp_status npt_step(b200dp_md* md, int grid) {
+// One NPT step, LAMMPS fix npt iso order, entirely on the device: the chains,
+// the barostat and the box advance in one-thread kernels and the force call
+// reads the box from device memory.
+static b200dp_status npt_step(b200dp_md* md) {
   const int n = md->n;
-  const double dt = md->p.dt, dthalf = 0.5 * dt, dtf = 0.5 * dt * kFtm2v;
-  const double kt = kBoltz * md->p.t_target, dof_boltz = md->dof * kBoltz;
-  const double ke_target = dof_boltz * md->p.t_target, p_hydro = md->p.p_target;
+  const double dt = md->p.dt, dtf = 0.5 * dt * kFtm2v;
+  const int grid = std::min(kRedBlocks * 4, (n + kMdThreads - 1) / kMdThreads);
+  const NptParams q = npt_params(md);
   cudaStream_t st = md->stream;
-  auto omega_force = [&](double t_cur, double vir_tr) {
-    const double vol = md->box[0] * md->box[4] * md->box[8];
-    const double p_cur = (dof_boltz * t_cur + vir_tr) / (3.0 * vol) * kNktv2p;
-    const double mtk1 = dof_boltz * t_cur / (3.0 * md->n);
-    md->omega_dot += ((p_cur - p_hydro) * vol / (md->w_mass * kNktv2p) + mtk1 / md->w_mass) * dthalf;
-  };
-  // ---- initial half
-  md->pch.barostat(md->omega_dot, md->w_mass, kt, dt);
-  const double s_t = md->tch.thermostat(md->t_current, dof_boltz, ke_target, kt, dt);
-  omega_force(md->t_current, md->vir_trace);
-  const double mtk2 = 3.0 * md->omega_dot / (3.0 * md->n);
-  const double fp = std::exp(-0.25 * dt * (md->omega_dot + mtk2));
-  const double e = std::exp(dthalf * md->omega_dot);
   count_launch();
-  k_npt_first<<<grid, kMdThreads, 0, st>>>(n, md->x.p, md->v.p, md->f.p, md->minv.p, s_t * fp * fp, dtf, dt, e);
-  for (int d = 0; d < 3; ++d) md->box[4 * d] *= e * e;
-  md->volume = md->box[0] * md->box[4] * md->box[8];
-  b200dp_status rc = b200dp_compute_device(md->engine, st, n, 0, md->x.p, md->atype.p, md->box, nullptr, md->e.p,
-                                           md->f.p, md->vir.p, nullptr, nullptr);
+  k_npt_pre<<<1, 1, 0, st>>>(q, md->npt.p);
+  count_launch();
+  k_npt_first_dev<<<grid, kMdThreads, 0, st>>>(n, md->x.p, md->v.p, md->f.p, md->minv.p, md->npt.p, dtf, dt);
+  const b200dp_status rc = b200dp_compute_device_dbox(md->engine, st, n, md->x.p, md->atype.p, md->box_ref,
+                                                      kGridMinScale, npt_box(md), md->e.p, md->f.p, md->vir.p);
   if (rc != B200DP_OK) return rc;
-  // ---- final half
   count_launch();
-  k_npt_second<<<kRedBlocks, kMdThreads, 0, st>>>(n, md->v.p, md->f.p, md->minv.p, md->mass.p, dtf, fp * fp,
-                                                  md->part.p);
-  double part[kRedBlocks], vir[9], epot = 0;
-  if (cudaMemcpyAsync(part, md->part.p, sizeof(part), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
-      cudaMemcpyAsync(vir, md->vir.p, sizeof(vir), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
-      cudaMemcpyAsync(&epot, md->e.p, sizeof(double), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
-      cudaStreamSynchronize(st) != cudaSuccess)
-    return B200DP_ERR_CUDA;
-  double mv2 = 0;
-  for (int k = 0; k < kRedBlocks; ++k) mv2 += part[k];
-  md->t_current = mv2 * kMvv2e / dof_boltz;
-  md->vir_trace = vir[0] + vir[4] + vir[8];
-  md->epot = epot;
-  omega_force(md->t_current, md->vir_trace);
-  const double s_t2 = md->tch.thermostat(md->t_current, dof_boltz, ke_target, kt, dt);
+  k_npt_second_dev<<<kRedBlocks, kMdThreads, 0, st>>>(n, md->v.p, md->f.p, md->minv.p, md->mass.p, dtf, md->npt.p,
+                                                      md->part.p);
   count_launch();
-  k_md_scale_by<<<grid, kMdThreads, 0, st>>>(n, md->v.p, s_t2);
-  md->pch.barostat(md->omega_dot, md->w_mass, kt, dt);
+  k_npt_post<<<1, 32, 0, st>>>(q, md->npt.p, md->part.p, kRedBlocks, md->vir.p, md->e.p);
+  count_launch();
+  k_npt_scale<<<grid, kMdThreads, 0, st>>>(n, md->v.p, md->npt.p);
   count_launch();
   k_md_ke<<<kRedBlocks, kMdThreads, 0, st>>>(n, md->v.p, md->mass.p, md->part.p);
   return cudaGetLastError() == cudaSuccess ? B200DP_OK : B200DP_ERR_CUDA;
 }
 
-// One NVE / NVT step enqueued on the MD stream.
+// One step enqueued on the MD stream.
 static b200dp_status md_step(b200dp_md* md) {
+  if (md->ensemble == B200DP_MD_NPT) return npt_step(md);
   const int n = md->n;
   const double dtf = 0.5 * md->p.dt * kFtm2v, dt = md->p.dt;
   const int grid = std::min(kRedBlocks * 4, (n + kMdThreads - 1) / kMdThreads);
@@ -490,22 +551,6 @@ static b200dp_status record_cycle(b200dp_md* md, int len) {
 
 b200dp_status b200dp_md_run(b200dp_md* md, int nsteps) {
   if (!md || nsteps < 0) return B200DP_ERR_INVALID;
-  if (md->ensemble == B200DP_MD_NPT) {
-    const int grid = std::min(kRedBlocks * 4, (md->n + kMdThreads - 1) / kMdThreads);
-    if (md->step == 0 && md->vir_trace == 0) {  // virial of the initial forces (computed at creation)
-      double vir[9];
-      if (cudaMemcpyAsync(vir, md->vir.p, sizeof(vir), cudaMemcpyDeviceToHost, md->stream) != cudaSuccess ||
-          cudaStreamSynchronize(md->stream) != cudaSuccess)
-        return B200DP_ERR_CUDA;
-      md->vir_trace = vir[0] + vir[4] + vir[8];
-    }
-    for (int s = 0; s < nsteps; ++s) {
-      const b200dp_status rc = npt_step(md, grid);
-      if (rc != B200DP_OK) return rc;
-      ++md->step;
-    }
-    return B200DP_OK;
-  }
   for (int s = 0; s < nsteps;) {
     // whole cycles replay the recorded graph; the rest (and a first cycle that
     // is being recorded) are enqueued step by step
@@ -539,8 +584,9 @@ b200dp_status b200dp_md_thermo(b200dp_md* md, double* thermo) {
       cudaMemcpyAsync(&ch, md->chain.p, sizeof(ch), cudaMemcpyDeviceToHost, md->stream) != cudaSuccess ||
       cudaStreamSynchronize(md->stream) != cudaSuccess)
     return B200DP_ERR_CUDA;
-  const b200dp_status rc = b200dp_check(md->engine);
+  b200dp_status rc = b200dp_check(md->engine);
   if (rc != B200DP_OK) return rc;
+  if (md->ensemble == B200DP_MD_NPT && (rc = npt_refresh(md)) != B200DP_OK) return rc;
   double mv2 = 0;
   for (int k = 0; k < kRedBlocks; ++k) mv2 += part[k];
   const double ke = 0.5 * mv2 * kMvv2e;
@@ -587,6 +633,8 @@ b200dp_status b200dp_md_snapshot_bytes(const b200dp_md* md, size_t* bytes) {
 b200dp_status b200dp_md_snapshot(b200dp_md* md, void* d_buf) {
   if (!md || !d_buf) return B200DP_ERR_INVALID;
   const SnapLayout L(md->n);
+  // (NPT: the chains, barostat and box are copied from their device state below;
+  // the header's copies are informational)
   SnapHeader& h = md->snap_stage;
   std::memset(&h, 0, sizeof(h));
   std::memcpy(h.magic, kSnapMagic, sizeof(h.magic));
@@ -618,7 +666,8 @@ b200dp_status b200dp_md_snapshot(b200dp_md* md, void* d_buf) {
       cudaMemcpyAsync(b + L.e, md->e.p, sizeof(double), d2d, st) != cudaSuccess ||
       cudaMemcpyAsync(b + L.vir, md->vir.p, 9 * sizeof(double), d2d, st) != cudaSuccess ||
       cudaMemcpyAsync(b + L.part, md->part.p, kRedBlocks * sizeof(double), d2d, st) != cudaSuccess ||
-      cudaMemcpyAsync(b + L.chain, md->chain.p, sizeof(Chain), d2d, st) != cudaSuccess)
+      cudaMemcpyAsync(b + L.chain, md->chain.p, sizeof(Chain), d2d, st) != cudaSuccess ||
+      (md->npt.p && cudaMemcpyAsync(b + L.npt, md->npt.p, sizeof(NptState), d2d, st) != cudaSuccess))
     return B200DP_ERR_CUDA;
   return B200DP_OK;
 }
@@ -643,7 +692,8 @@ b200dp_status b200dp_md_restore(b200dp_md* md, const void* d_buf) {
       cudaMemcpyAsync(md->e.p, b + L.e, sizeof(double), d2d, st) != cudaSuccess ||
       cudaMemcpyAsync(md->vir.p, b + L.vir, 9 * sizeof(double), d2d, st) != cudaSuccess ||
       cudaMemcpyAsync(md->part.p, b + L.part, kRedBlocks * sizeof(double), d2d, st) != cudaSuccess ||
-      cudaMemcpyAsync(md->chain.p, b + L.chain, sizeof(Chain), d2d, st) != cudaSuccess)
+      cudaMemcpyAsync(md->chain.p, b + L.chain, sizeof(Chain), d2d, st) != cudaSuccess ||
+      (md->npt.p && cudaMemcpyAsync(md->npt.p, b + L.npt, sizeof(NptState), d2d, st) != cudaSuccess))
     return B200DP_ERR_CUDA;
   md->step = h.step;
   std::memcpy(md->box, h.box, sizeof(md->box));
@@ -658,6 +708,10 @@ b200dp_status b200dp_md_restore(b200dp_md* md, const void* d_buf) {
   md->t_current = h.t_current;
   md->vir_trace = h.vir_trace;
   md->epot = h.epot;
+  if (md->npt.p) {  // the device state is the restored one; its host copies follow it
+    const b200dp_status rc = npt_refresh(md);
+    if (rc != B200DP_OK) return rc;
+  }
   // candidates are rebuilt from the restored positions on the next step
   return b200dp_set_neighbor_reuse(md->engine, md->p.skin, md->p.rebuild_every > 1 ? md->p.rebuild_every : 0);
 }

@@ -178,3 +178,117 @@ inline void init_velocities(int natoms, const double* mass, double t_init, unsig
   const double s = t_now > 0 ? std::sqrt(t_init / t_now) : 0.0;
   for (size_t k = 0; k < 3 * (size_t)natoms; ++k) v[k] *= s;
 }
+
+// v = v * sv + dtf F / m ; x = e (e x + dt v)   (NPT first half: remap, drift, remap)
+__global__ void k_npt_first(int n, double* __restrict__ x, double* __restrict__ v, const double* __restrict__ f,
+                            const double* __restrict__ minv, double sv, double dtf, double dt, double e) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const double w = dtf * minv[i];
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+      const double vv = v[3 * i + c] * sv + w * f[3 * i + c];
+      v[3 * i + c] = vv;
+      x[3 * i + c] = e * (e * x[3 * i + c] + dt * vv);
+    }
+  }
+}
+
+// v = (v + dtf F / m) * sv, with per-block partial sums of m v^2
+__global__ void __launch_bounds__(kMdThreads) k_npt_second(int n, double* __restrict__ v,
+                                                           const double* __restrict__ f,
+                                                           const double* __restrict__ minv,
+                                                           const double* __restrict__ mass, double dtf, double sv,
+                                                           double* __restrict__ part) {
+  __shared__ double sh[kMdThreads / 32];
+  double acc = 0.0;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const double w = dtf * minv[i];
+    double s2 = 0.0;
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+      const double vv = (v[3 * i + c] + w * f[3 * i + c]) * sv;
+      v[3 * i + c] = vv;
+      s2 += vv * vv;
+    }
+    acc += mass[i] * s2;
+  }
+  acc = warp_sum(acc);
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double b = 0.0;
+    for (int w = 0; w < kMdThreads / 32; ++w) b += sh[w];
+    part[blockIdx.x] = b;
+  }
+}
+
+__global__ void k_md_scale_by(int n, double* __restrict__ v, double s) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < 3 * n; i += gridDim.x * blockDim.x) v[i] *= s;
+}
+
+// Nose-Hoover chain of the NPT path (same recurrence as k_md_chain), usable on
+// the host and, as part of the device NPT state, in one-thread kernels.
+struct HostChain {
+  int M = 0;
+  double eta[kMaxChain] = {0}, eta_dot[kMaxChain + 1] = {0}, eta_dotdot[kMaxChain] = {0}, mass[kMaxChain] = {0};
+  __host__ __device__ void init(int m, double q0, double qi, double boltz_t) {
+    M = m;
+    mass[0] = q0;
+    for (int i = 1; i < M; ++i) mass[i] = qi;
+    for (int i = 1; i < M; ++i) eta_dotdot[i] = (mass[i - 1] * eta_dot[i - 1] * eta_dot[i - 1] - boltz_t) / mass[i];
+  }
+  // Thermostat half-step for kinetic energy `ke` (target ke_target); returns the velocity factor.
+  __host__ __device__ double thermostat(double& t_current, double dof_boltz, double ke_target, double boltz_t, double dt) {
+    const double dt4 = 0.25 * dt, dt8 = 0.125 * dt, dthalf = 0.5 * dt;
+    eta_dotdot[0] = (dof_boltz * t_current - ke_target) / mass[0];
+    double expfac = 1.0;
+    for (int i = M - 1; i > 0; --i) {
+      expfac = exp(-dt8 * eta_dot[i + 1]);
+      eta_dot[i] = (eta_dot[i] * expfac + eta_dotdot[i] * dt4) * expfac;
+    }
+    expfac = exp(-dt8 * eta_dot[1]);
+    eta_dot[0] = (eta_dot[0] * expfac + eta_dotdot[0] * dt4) * expfac;
+    const double factor = exp(-dthalf * eta_dot[0]);
+    t_current *= factor * factor;
+    eta_dotdot[0] = (dof_boltz * t_current - ke_target) / mass[0];
+    for (int i = 0; i < M; ++i) eta[i] += dthalf * eta_dot[i];
+    eta_dot[0] = (eta_dot[0] * expfac + eta_dotdot[0] * dt4) * expfac;
+    for (int i = 1; i < M; ++i) {
+      expfac = exp(-dt8 * eta_dot[i + 1]);
+      eta_dotdot[i] = (mass[i - 1] * eta_dot[i - 1] * eta_dot[i - 1] - boltz_t) / mass[i];
+      eta_dot[i] = (eta_dot[i] * expfac + eta_dotdot[i] * dt4) * expfac;
+    }
+    return factor;
+  }
+  // Barostat-chain half-step (FixNH::nhc_press_integrate, isotropic): scales
+  // omega_dot; kinetic energy 3 W omega_dot^2 against kB T0.
+  __host__ __device__ void barostat(double& omega_dot, double w_mass, double kt, double dt) {
+    const double dt4 = 0.25 * dt, dt8 = 0.125 * dt, dthalf = 0.5 * dt;
+    double ke = 3.0 * w_mass * omega_dot * omega_dot;
+    eta_dotdot[0] = (ke - kt) / mass[0];
+    double expfac = 1.0;
+    for (int i = M - 1; i > 0; --i) {
+      expfac = exp(-dt8 * eta_dot[i + 1]);
+      eta_dot[i] = (eta_dot[i] * expfac + eta_dotdot[i] * dt4) * expfac;
+    }
+    expfac = exp(-dt8 * eta_dot[1]);
+    eta_dot[0] = (eta_dot[0] * expfac + eta_dotdot[0] * dt4) * expfac;
+    for (int i = 0; i < M; ++i) eta[i] += dthalf * eta_dot[i];
+    omega_dot *= exp(-dthalf * eta_dot[0]);
+    ke = 3.0 * w_mass * omega_dot * omega_dot;
+    eta_dotdot[0] = (ke - kt) / mass[0];
+    eta_dot[0] = (eta_dot[0] * expfac + eta_dotdot[0] * dt4) * expfac;
+    for (int i = 1; i < M; ++i) {
+      expfac = exp(-dt8 * eta_dot[i + 1]);
+      eta_dotdot[i] = (mass[i - 1] * eta_dot[i - 1] * eta_dot[i - 1] - kt) / mass[i];
+      eta_dot[i] = (eta_dot[i] * expfac + eta_dotdot[i] * dt4) * expfac;
+    }
+  }
+  __host__ __device__ double energy(double first_kt, double kt) const {
+    double e = first_kt * eta[0];
+    for (int i = 1; i < M; ++i) e += kt * eta[i];
+    for (int i = 0; i < M; ++i) e += 0.5 * mass[i] * eta_dot[i] * eta_dot[i];
+    return e;
+  }
+};
+

@@ -94,6 +94,53 @@ int make_grid(bool periodic, const double* box, const double* region, double rcu
   return 0;
 }
 
+int make_grid_dbox(const double* box_ref, double min_scale, const double* dbox, double rcut, long long max_cells,
+                   GridSpec& g) {
+  double b[9];
+  for (int k = 0; k < 9; ++k) b[k] = box_ref[k] * min_scale;
+  const int rc = make_grid(true, b, nullptr, rcut, max_cells, g);
+  g.prune = 0;
+  g.dB = dbox;
+  return rc;
+}
+
+// The inverse of the box rows on the device, in the same operation order as
+// make_box_inverse (explicit round-to-nearest operations, no contraction).
+__global__ void k_box_setup(const double* __restrict__ box, double* __restrict__ bb) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  double B[3][3];
+  for (int a = 0; a < 3; ++a)
+    for (int b = 0; b < 3; ++b) B[a][b] = box[3 * a + b];
+  const double c00 = dsub(dmul(B[1][1], B[2][2]), dmul(B[1][2], B[2][1]));
+  const double c01 = dsub(dmul(B[1][2], B[2][0]), dmul(B[1][0], B[2][2]));
+  const double c02 = dsub(dmul(B[1][0], B[2][1]), dmul(B[1][1], B[2][0]));
+  const double det = dadd(dadd(dmul(B[0][0], c00), dmul(B[0][1], c01)), dmul(B[0][2], c02));
+  const double id = __drcp_rn(det);
+  double I[3][3];
+  I[0][0] = dmul(c00, id);
+  I[1][0] = dmul(c01, id);
+  I[2][0] = dmul(c02, id);
+  I[0][1] = dmul(dsub(dmul(B[0][2], B[2][1]), dmul(B[0][1], B[2][2])), id);
+  I[1][1] = dmul(dsub(dmul(B[0][0], B[2][2]), dmul(B[0][2], B[2][0])), id);
+  I[2][1] = dmul(dsub(dmul(B[0][1], B[2][0]), dmul(B[0][0], B[2][1])), id);
+  I[0][2] = dmul(dsub(dmul(B[0][1], B[1][2]), dmul(B[0][2], B[1][1])), id);
+  I[1][2] = dmul(dsub(dmul(B[0][2], B[1][0]), dmul(B[0][0], B[1][2])), id);
+  I[2][2] = dmul(dsub(dmul(B[0][0], B[1][1]), dmul(B[0][1], B[1][0])), id);
+  for (int k = 0; k < 9; ++k) bb[k] = box[k];
+  for (int a = 0; a < 3; ++a)
+    for (int b = 0; b < 3; ++b) bb[9 + 3 * a + b] = I[a][b];
+}
+
+void launch_box_setup(cudaStream_t st, const double* d_box, double* d_bb) {
+  count_launch();
+  k_box_setup<<<1, 1, 0, st>>>(d_box, d_bb);
+}
+
+// The box rows and their inverse of a grid: from device memory when the box
+// lives there, else the host-built copies in the grid.
+__device__ __forceinline__ double gB(const GridSpec& g, int k) { return g.dB ? __ldg(g.dB + k) : g.B[k]; }
+__device__ __forceinline__ double gBinv(const GridSpec& g, int k) { return g.dB ? __ldg(g.dB + 9 + k) : g.Binv[k]; }
+
 // ---------------------------------------------------------------- binning
 __global__ void k_bin(int nall, const double* __restrict__ coord, GridSpec g, double* __restrict__ xw,
                       int* __restrict__ cell_of, int* __restrict__ cell_count, int* __restrict__ lshift,
@@ -108,16 +155,16 @@ __global__ void k_bin(int nall, const double* __restrict__ coord, GridSpec g, do
     double f[3];
 #pragma unroll
     for (int d = 0; d < 3; ++d) {
-      const double s = dadd(dadd(dmul(x[0], g.Binv[d]), dmul(x[1], g.Binv[3 + d])), dmul(x[2], g.Binv[6 + d]));
+      const double s = dadd(dadd(dmul(x[0], gBinv(g, d)), dmul(x[1], gBinv(g, 3 + d))), dmul(x[2], gBinv(g, 6 + d)));
       f[d] = floor(s);
       if (lshift) lshift[3 * i + d] = (int)f[d];
     }
 #pragma unroll
     for (int k = 0; k < 3; ++k)
-      w[k] = dsub(x[k], dadd(dadd(dmul(f[0], g.B[k]), dmul(f[1], g.B[3 + k])), dmul(f[2], g.B[6 + k])));
+      w[k] = dsub(x[k], dadd(dadd(dmul(f[0], gB(g, k)), dmul(f[1], gB(g, 3 + k))), dmul(f[2], gB(g, 6 + k))));
 #pragma unroll
     for (int d = 0; d < 3; ++d) {
-      const double s = (w[0] * g.Binv[d] + w[1] * g.Binv[3 + d]) + w[2] * g.Binv[6 + d];
+      const double s = (w[0] * gBinv(g, d) + w[1] * gBinv(g, 3 + d)) + w[2] * gBinv(g, 6 + d);
       double v = floor(s * g.n[d]);
       v = fmin(fmax(v, 0.0), (double)(g.n[d] - 1));
       c[d] = (int)v;
@@ -486,7 +533,7 @@ __device__ __forceinline__ void image_vector(const GridSpec& g, const double (&x
     const double m0 = (double)(((code >> 20) & 1023) - kImageBias), m1 = (double)(((code >> 10) & 1023) - kImageBias),
                  m2 = (double)((code & 1023) - kImageBias);
 #pragma unroll
-    for (int c = 0; c < 3; ++c) sh[c] = dadd(dadd(dmul(m0, g.B[c]), dmul(m1, g.B[3 + c])), dmul(m2, g.B[6 + c]));
+    for (int c = 0; c < 3; ++c) sh[c] = dadd(dadd(dmul(m0, gB(g, c)), dmul(m1, gB(g, 3 + c))), dmul(m2, gB(g, 6 + c)));
   }
   r[0] = dsub(dadd(x0, sh[0]), xi[0]);
   r[1] = dsub(dadd(x1, sh[1]), xi[1]);
@@ -719,7 +766,7 @@ __device__ __forceinline__ void shifted(const GridSpec& g, const double* __restr
   const double f0 = (double)ls[3 * j], f1 = (double)ls[3 * j + 1], f2 = (double)ls[3 * j + 2];
 #pragma unroll
   for (int k = 0; k < 3; ++k)
-    w[k] = dsub(x[3 * j + k], dadd(dadd(dmul(f0, g.B[k]), dmul(f1, g.B[3 + k])), dmul(f2, g.B[6 + k])));
+    w[k] = dsub(x[3 * j + k], dadd(dadd(dmul(f0, gB(g, k)), dmul(f1, gB(g, 3 + k))), dmul(f2, gB(g, 6 + k))));
 }
 
 __global__ void __launch_bounds__(kFmtWarps * 32)

@@ -31,7 +31,20 @@ struct GridSpec {
   // the atoms clamped into them, so they extend to infinity outwards
   int prune;
   double org[3], h[3];
+  // periodic box read from device memory ([B | Binv], 18 doubles) instead of
+  // B / Binv above, when set: the box of a barostat changes on the device
+  // between calls; the cell counts and the stencil reach then come from a
+  // reference box that the device box may not undercut (see make_grid_dbox)
+  const double* dB;
 };
+
+// Grid for a periodic box that lives in device memory: cell counts and reach
+// from box_ref scaled by min_scale (the smallest box the grid must serve),
+// no cell pruning, kernels reading [B | Binv] from dbox.
+int make_grid_dbox(const double* box_ref, double min_scale, const double* dbox, double rcut, long long max_cells,
+                   GridSpec& g);
+// [B | Binv] of a device box (one thread).
+void launch_box_setup(cudaStream_t st, const double* d_box, double* d_bb);
 
 // Cell-sorted atom record written by the fill kernel: the wrapped position
 // and the atom's index and type, so the list kernel reaches a candidate's

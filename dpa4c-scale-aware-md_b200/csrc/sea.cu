@@ -773,6 +773,21 @@ void launch_fold_finish(cudaStream_t st, int nloc, double* force, unsigned long 
   k_assemble_finish<false><<<(nloc + 255) / 256, 256, 0, st>>>(nloc, nloc, force, nullptr, acc, nullptr, nonfinite);
 }
 
+// shift[g][d] *= ratio[d] (an isotropic or orthorhombic rescaling of the box)
+__global__ void k_scale_shifts(int nghost, double* __restrict__ shift, double r0, double r1, double r2) {
+  const int g = blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= nghost) return;
+  shift[3 * (size_t)g] *= r0;
+  shift[3 * (size_t)g + 1] *= r1;
+  shift[3 * (size_t)g + 2] *= r2;
+}
+
+void launch_scale_shifts(cudaStream_t st, int nghost, double* shift, const double* ratio) {
+  if (nghost <= 0) return;
+  count_launch();
+  k_scale_shifts<<<(nghost + 255) / 256, 256, 0, st>>>(nghost, shift, ratio[0], ratio[1], ratio[2]);
+}
+
 void launch_halo_gather(cudaStream_t st, int nloc, int nghost, double* x, const PeerSet& peers, const int2* origin,
                         const double* shift) {
   if (nghost <= 0) return;

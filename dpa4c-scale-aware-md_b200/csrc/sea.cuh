@@ -117,6 +117,8 @@ void launch_assemble_fold(cudaStream_t st, int nloc, int nall, int selt, const i
                           unsigned* nonfinite, unsigned long long* own_acc, unsigned* own_nf, const PeerSet& peers,
                           const int2* origin, double* partial, unsigned* done, double* energy, double* virial);
 void launch_fold_finish(cudaStream_t st, int nloc, double* force, unsigned long long* acc, unsigned* nonfinite);
+// shift [nghost][3] scaled per component by ratio[3] (the box scaled by a barostat).
+void launch_scale_shifts(cudaStream_t st, int nghost, double* shift, const double* ratio);
 // x rows nloc..nloc+nghost from the owners' published positions (+ shift [nghost][3]).
 void launch_halo_gather(cudaStream_t st, int nloc, int nghost, double* x, const PeerSet& peers, const int2* origin,
                         const double* shift);

@@ -137,6 +137,18 @@ b200dp_status b200dp_compute_device(b200dp_engine* engine, void* stream, int nlo
                                     const double* region, double* d_energy, double* d_force,
                                     double* d_virial, double* d_atom_energy, double* d_atom_virial);
 
+/* As b200dp_compute_device for a periodic system (nghost = 0) whose box
+ * lives in device memory: d_box [9] (rows are cell vectors) is read by the
+ * kernels when they run, so a barostat can change it on the device between
+ * calls with no host round trip.  The binning grid (cell counts, stencil
+ * reach) comes from the host reference box_ref [9] scaled by min_scale
+ * (0 < min_scale <= 1): it serves every device box whose cell vectors are
+ * at least min_scale times box_ref's; the caller keeps the box in that range
+ * (the MD driver re-references at its synchronisation points). */
+b200dp_status b200dp_compute_device_dbox(b200dp_engine* engine, void* stream, int nlocal, const double* d_coord,
+                                         const int* d_atype, const double* box_ref, double min_scale,
+                                         const double* d_box, double* d_energy, double* d_force, double* d_virial);
+
 /* Synchronises the engine's last stream and converts device error counters
  * into a status (B200DP_ERR_SEL_OVERFLOW / _CAPACITY / _BAD_TYPE). */
 b200dp_status b200dp_check(b200dp_engine* engine);
@@ -327,6 +339,10 @@ b200dp_status b200dp_neighbor_stats(b200dp_engine* engine, long long* builds);
 b200dp_status b200dp_fold_export(b200dp_engine* engine, int capacity, void* handle);
 b200dp_status b200dp_fold_connect(b200dp_engine* engine, int nranks, int rank, const void* handles);
 b200dp_status b200dp_fold_origins(b200dp_engine* engine, int nghost, const int* d_origin, const double* d_shift);
+/* Scales every ghost row's periodic shift per component by ratio[3] (host
+ * array), enqueued on `stream`: the box of a barostat changed by that ratio
+ * and the plan was not rebuilt. */
+b200dp_status b200dp_fold_scale_shifts(b200dp_engine* engine, void* stream, const double* ratio);
 b200dp_status b200dp_halo_publish(b200dp_engine* engine, void* stream, int nlocal, const double* d_coord);
 b200dp_status b200dp_halo_gather(b200dp_engine* engine, void* stream, int nlocal, int nghost, double* d_coord);
 b200dp_status b200dp_compute_device_fold(b200dp_engine* engine, void* stream, int nlocal, int nghost,
@@ -475,8 +491,11 @@ b200dp_status b200dp_dd_get_forces(b200dp_dd* dd, void* stream, double* force, d
  * single-GPU driver).  Atoms migrate and the ghost plan is rebuilt every
  * rebuild_every steps (0 or 1: every step), between the first half-step and
  * the force call; halo must exceed rcut by twice the largest displacement
- * between rebuilds (checked by b200dp_dd_md_thermo).  NPT is not offered
- * here (B200DP_ERR_UNSUPPORTED). */
+ * between rebuilds (checked by b200dp_dd_md_thermo).  NPT (isotropic, fix
+ * npt iso order as b200dp_md_*): the barostat and thermostat scalars run on
+ * every rank's host from the rendezvous' global kinetic energy and virial (one
+ * host read per step); the box, the sub-boxes and the ghost shifts scale with
+ * the barostat between plan rebuilds. */
 b200dp_status b200dp_dd_md_start(b200dp_dd* dd, const b200dp_md_params* params, const double* vel);
 b200dp_status b200dp_dd_md_run(b200dp_dd* dd, int nsteps);
 /* Global thermodynamic state, as b200dp_md_thermo. */

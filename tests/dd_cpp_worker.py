@@ -27,7 +27,9 @@ def main():
     ap.add_argument("--nranks", type=int, required=True)
     ap.add_argument("--grid", type=int, nargs=3, required=True)
     ap.add_argument("--model", required=True)
-    ap.add_argument("--mol", type=int, nargs=3, required=True)
+    ap.add_argument("--mol", type=int, nargs=3, required=True, help="water molecules per axis, or FCC cells")
+    ap.add_argument("--system", default="water", choices=["water", "cu"])
+    ap.add_argument("--ensemble", default="nvt", choices=["nvt", "npt"])
     ap.add_argument("--idfile", required=True)
     ap.add_argument("--out", required=True)
     ap.add_argument("--precision", default="fp64")
@@ -35,7 +37,7 @@ def main():
     ap.add_argument("--rebuild-every", type=int, default=5)
     ap.add_argument("--halo", type=float, default=8.0)
     a = ap.parse_args()
-    s = systems.water(*a.mol)
+    s = systems.water(*a.mol) if a.system == "water" else systems.fcc(a.mol[0])
     if a.rank == 0:
         uid = b200dp.dd_unique_id()
         tmp = a.idfile + ".tmp"
@@ -58,12 +60,11 @@ def main():
     ids, x, _, f = dd.owned()
     out.update(energy=e, virial=v, ids=ids, force=f)
     if a.md_steps:
-        rng = np.random.default_rng(3)
-        m = np.where(s.atype == 0, 15.9994, 15.9994)
-        vel = rng.normal(size=s.coord.shape) * np.sqrt(8.617343e-5 * 300.0 / (m[:, None] * 1.0364269e-4))
-        vel -= vel.mean(0)
-        dd.md_start([15.9994, 15.9994], dt=0.0005, ensemble=b200dp.NVT, vel=vel, t_target=300.0, t_damp=0.025,
-                    rebuild_every=a.rebuild_every)
+        sys.path.insert(0, HERE)
+        from test_gpu_dd import md_setup
+
+        masses, vel, kw = md_setup(s, a.system, a.ensemble)
+        dd.md_start(masses, vel=vel, rebuild_every=a.rebuild_every, **kw)
         dd.md_run(a.md_steps)
         th = dd.thermo()
         ids, x, vv, f = dd.owned()
