@@ -30,6 +30,21 @@ HEADERS = ["common.cuh", "nlist.cuh", "sea.cuh", "engine.hpp", "model.hpp", "umm
            "c8l2.cuh", "simt_gemm.cuh", "md_kernels.cuh"]
 
 
+def nccl_paths():
+    """Include and library directories of the NCCL that PyTorch ships (the nvidia-nccl package), so
+    that this library and torch load the same libnccl.so.2 in one process whichever comes first;
+    the system NCCL when the package is absent."""
+    import importlib.util
+
+    spec = importlib.util.find_spec("nvidia.nccl")
+    if spec and spec.submodule_search_locations:
+        root = list(spec.submodule_search_locations)[0]
+        inc, lib = os.path.join(root, "include"), os.path.join(root, "lib")
+        if os.path.exists(os.path.join(inc, "nccl.h")) and os.path.exists(os.path.join(lib, "libnccl.so.2")):
+            return ["-I" + inc], ["-L" + lib, "-l:libnccl.so.2", "-Xlinker", "-rpath=" + lib]
+    return [], ["-lnccl"]
+
+
 def _stale(target: str, deps: list[str]) -> bool:
     if not os.path.exists(target):
         return True
@@ -48,9 +63,11 @@ def build(force: bool = False, jobs: int = 4, verbose: bool = False) -> str:
         if force or _stale(o, [s] + headers):
             todo.append((s, o))
 
+    nccl_inc, nccl_link = nccl_paths()
+
     def compile_one(so):
         s, o = so
-        cmd = [NVCC] + FLAGS + ["-c", s, "-o", o]
+        cmd = [NVCC] + FLAGS + nccl_inc + ["-c", s, "-o", o]
         if verbose:
             cmd.insert(1, "-Xptxas=-v")
         r = subprocess.run(cmd, capture_output=True, text=True)
@@ -63,7 +80,8 @@ def build(force: bool = False, jobs: int = 4, verbose: bool = False) -> str:
             if verbose and out:
                 sys.stderr.write(out)
     if force or todo or _stale(LIB, objs):
-        cmd = [NVCC] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcudart_static", "-lnccl", "-lrt", "-lpthread", "-ldl"]
+        cmd = [NVCC] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcudart_static"] + nccl_link + ["-lrt", "-lpthread",
+                                                                                                 "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

@@ -324,6 +324,7 @@ b200dp_status Engine::init_tail() {
   B200DP_CUDA_TRY(asm_done.ensure(sizeof(unsigned)));
   B200DP_CUDA_TRY(cudaMemset(asm_done.ptr, 0, sizeof(unsigned)));
   B200DP_CUDA_TRY(scalars.ensure(sizeof(double) * 16));
+  B200DP_CUDA_TRY(dbox_bb.ensure(sizeof(double) * 18));  // device-box calls may run under stream capture
   ch_fwd = 32;
   ch_bwd = 32;
   // shared memory per block of the SIMT backward: in fp64 the chunk is cut until four blocks
@@ -864,7 +865,6 @@ b200dp_status Engine::compute_device_dbox(cudaStream_t st, int nloc, const doubl
     err = "compute_device_dbox: a reference box, a device box and 0 < min_scale <= 1";
     return B200DP_ERR_INVALID;
   }
-  B200DP_CUDA_TRY(dbox_bb.ensure(sizeof(double) * 18));
   dbox_dev = d_box;
   dbox_min = min_scale;
   const b200dp_status rc = compute_device(st, nloc, 0, d_coord, d_atype, box_ref, nullptr, d_energy, d_force, d_virial,

@@ -747,23 +747,12 @@ void launch_fit_tc(cudaStream_t st, const FitTcPlan& p, int ntypes, int nloc, co
       d.part = b.dt_part;
       d.cnt = b.dt_cnt;
       d.err = err;
-      // few row tiles: split each tile's chunks over CTAs so that the SMs are used -- the
-      // smallest split count that minimises (waves of one CTA per SM) / (splits), e.g. 3 for
-      // the 98 tiles of 12,288 water atoms (294 CTAs of a third of the work in 2 waves
-      // instead of 98 whole tiles in one wave on 148 SMs)
+      // few row tiles: split each tile's chunks over CTAs so that the SMs are used
+      // (splitting more tiles than fill one wave was measured slower: each split CTA
+      // reloads the tile's whole dz0 operand and the partial sums add a pass)
       int nsplit = 1;
       if (b.dt_part && b.dt_cnt && row_tiles > 0) {
-        int dev = 0, nsm = 148;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-        double best = (double)((row_tiles + nsm - 1) / nsm);
-        for (int ns = 2; ns <= std::min(d.nchunks, kDtSplitSlots / row_tiles); ++ns) {
-          const double waves = (double)((row_tiles * ns + nsm - 1) / nsm) / ns;
-          if (waves < best - 1e-9) {
-            best = waves;
-            nsplit = ns;
-          }
-        }
+        nsplit = std::max(1, std::min(d.nchunks, kDtSplitSlots / row_tiles));
         const int per = (d.nchunks + nsplit - 1) / nsplit;
         nsplit = (d.nchunks + per - 1) / per;  // no CTA without a chunk
       }

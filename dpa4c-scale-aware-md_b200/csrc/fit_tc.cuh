@@ -71,7 +71,7 @@ struct FitTcBuffers {
   float* dt_part;
   unsigned* dt_cnt;
 };
-constexpr int kDtSplitSlots = 2 * 148;  // split CTAs of one launch: row tiles x splits <= this
+constexpr int kDtSplitSlots = 148;  // split CTAs of one launch: row tiles x splits <= this
 
 // First row tile of each type (exclusive prefix of ceil(n_t/128)); [ntypes+1].
 void launch_fit_tile_table(cudaStream_t st, int ntypes, const int* type_start, int* ftile);

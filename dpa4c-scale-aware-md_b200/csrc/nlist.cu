@@ -79,18 +79,6 @@ int make_grid(bool periodic, const double* box, const double* region, double rcu
     if (2 * g.reach[d] + 1 > 31) return 2;
   }
   g.ncells = g.n[0] * g.n[1] * g.n[2];
-  g.prune = 1;
-  for (int d = 0; d < 3; ++d) {
-    if (periodic) {
-      for (int e = 0; e < 3; ++e)
-        if (e != d && box[3 * d + e] != 0.0) g.prune = 0;
-      g.org[d] = 0.0;
-      g.h[d] = box[4 * d] / g.n[d];
-    } else {
-      g.org[d] = g.lo[d];
-      g.h[d] = ext[d] / g.n[d];
-    }
-  }
   return 0;
 }
 
@@ -99,7 +87,6 @@ int make_grid_dbox(const double* box_ref, double min_scale, const double* dbox, 
   double b[9];
   for (int k = 0; k < 9; ++k) b[k] = box_ref[k] * min_scale;
   const int rc = make_grid(true, b, nullptr, rcut, max_cells, g);
-  g.prune = 0;
   g.dB = dbox;
   return rc;
 }
@@ -138,10 +125,22 @@ void launch_box_setup(cudaStream_t st, const double* d_box, double* d_bb) {
 
 // The box rows and their inverse of a grid: from device memory when the box
 // lives there, else the host-built copies in the grid.
-__device__ __forceinline__ double gB(const GridSpec& g, int k) { return g.dB ? __ldg(g.dB + k) : g.B[k]; }
-__device__ __forceinline__ double gBinv(const GridSpec& g, int k) { return g.dB ? __ldg(g.dB + 9 + k) : g.Binv[k]; }
+// DB: the box lives in device memory (a barostat's), else in the grid's host-built copies
+// (kernel parameters); the kernels are instantiated for both, so the common case keeps
+// its constant-bank operands.
+template <bool DB>
+__device__ __forceinline__ double gB(const GridSpec& g, int k) {
+  if constexpr (DB) return __ldg(g.dB + k);
+  return g.B[k];
+}
+template <bool DB>
+__device__ __forceinline__ double gBinv(const GridSpec& g, int k) {
+  if constexpr (DB) return __ldg(g.dB + 9 + k);
+  return g.Binv[k];
+}
 
 // ---------------------------------------------------------------- binning
+template <bool DB>
 __global__ void k_bin(int nall, const double* __restrict__ coord, GridSpec g, double* __restrict__ xw,
                       int* __restrict__ cell_of, int* __restrict__ cell_count, int* __restrict__ lshift,
                       const int* __restrict__ gate) {
@@ -155,16 +154,16 @@ __global__ void k_bin(int nall, const double* __restrict__ coord, GridSpec g, do
     double f[3];
 #pragma unroll
     for (int d = 0; d < 3; ++d) {
-      const double s = dadd(dadd(dmul(x[0], gBinv(g, d)), dmul(x[1], gBinv(g, 3 + d))), dmul(x[2], gBinv(g, 6 + d)));
+      const double s = dadd(dadd(dmul(x[0], gBinv<DB>(g, d)), dmul(x[1], gBinv<DB>(g, 3 + d))), dmul(x[2], gBinv<DB>(g, 6 + d)));
       f[d] = floor(s);
       if (lshift) lshift[3 * i + d] = (int)f[d];
     }
 #pragma unroll
     for (int k = 0; k < 3; ++k)
-      w[k] = dsub(x[k], dadd(dadd(dmul(f[0], gB(g, k)), dmul(f[1], gB(g, 3 + k))), dmul(f[2], gB(g, 6 + k))));
+      w[k] = dsub(x[k], dadd(dadd(dmul(f[0], gB<DB>(g, k)), dmul(f[1], gB<DB>(g, 3 + k))), dmul(f[2], gB<DB>(g, 6 + k))));
 #pragma unroll
     for (int d = 0; d < 3; ++d) {
-      const double s = (w[0] * gBinv(g, d) + w[1] * gBinv(g, 3 + d)) + w[2] * gBinv(g, 6 + d);
+      const double s = (w[0] * gBinv<DB>(g, d) + w[1] * gBinv<DB>(g, 3 + d)) + w[2] * gBinv<DB>(g, 6 + d);
       double v = floor(s * g.n[d]);
       v = fmin(fmax(v, 0.0), (double)(g.n[d] - 1));
       c[d] = (int)v;
@@ -190,7 +189,10 @@ void launch_bin(cudaStream_t st, int nall, const double* coord, const GridSpec& 
                 int* cell_count, int* lshift, const int* gate) {
   if (nall <= 0) return;
   count_launch();
-  k_bin<<<(nall + 255) / 256, 256, 0, st>>>(nall, coord, g, xw, cell_of, cell_count, lshift, gate);
+  if (g.dB)
+    k_bin<true><<<(nall + 255) / 256, 256, 0, st>>>(nall, coord, g, xw, cell_of, cell_count, lshift, gate);
+  else
+    k_bin<false><<<(nall + 255) / 256, 256, 0, st>>>(nall, coord, g, xw, cell_of, cell_count, lshift, gate);
 }
 
 // Single-block exclusive scan; out has n+1 entries (out[n] = total).  Each
@@ -526,6 +528,7 @@ __device__ void emit_row(const FormatSpec& f, int i, const CandBuf& b, const int
 
 // Shift of periodic image (n0, n1, n2) and the vector from centre xi to
 // neighbour xj in that image: (xj + shift) - xi, fp64, fixed operation order.
+template <bool DB>
 __device__ __forceinline__ void image_vector(const GridSpec& g, const double (&xi)[3], double x0, double x1,
                                              double x2, int code, double (&r)[3]) {
   double sh[3] = {0, 0, 0};
@@ -533,7 +536,7 @@ __device__ __forceinline__ void image_vector(const GridSpec& g, const double (&x
     const double m0 = (double)(((code >> 20) & 1023) - kImageBias), m1 = (double)(((code >> 10) & 1023) - kImageBias),
                  m2 = (double)((code & 1023) - kImageBias);
 #pragma unroll
-    for (int c = 0; c < 3; ++c) sh[c] = dadd(dadd(dmul(m0, gB(g, c)), dmul(m1, gB(g, 3 + c))), dmul(m2, gB(g, 6 + c)));
+    for (int c = 0; c < 3; ++c) sh[c] = dadd(dadd(dmul(m0, gB<DB>(g, c)), dmul(m1, gB<DB>(g, 3 + c))), dmul(m2, gB<DB>(g, 6 + c)));
   }
   r[0] = dsub(dadd(x0, sh[0]), xi[0]);
   r[1] = dsub(dadd(x1, sh[1]), xi[1]);
@@ -545,12 +548,13 @@ constexpr int kStencilPerLane = 4;
 constexpr int kStencilChunk = 32 * kStencilPerLane;
 constexpr int kGatherBatch = 4;  // candidate records loaded per lane before any is used
 
-template <typename K>
-static void format_attr(K kernel, size_t smem) {
-  // the attribute is raised (never lowered) as larger type capacities arrive
+template <auto Kernel>
+static void format_attr(size_t smem) {
+  // the attribute is raised (never lowered) as larger type capacities arrive; one
+  // record per kernel instantiation
   static size_t set = 48 * 1024;
   if (smem > set) {
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     set = smem;
   }
 }
@@ -562,7 +566,7 @@ static void format_attr(K kernel, size_t smem) {
 // cell-sorted record.  push(valid, tj, r2, j, code, ridx) is called by all
 // lanes together for each batch slot (r2 < rc2, not the centre itself, type
 // in range).
-template <typename Push>
+template <bool DB, typename Push>
 __device__ __forceinline__ void gather_stencil(const FormatSpec& f, const GridSpec& g, const double (&xi)[3], int i,
                                                int cell, double rc2, const int* __restrict__ cell_start,
                                                const CellRec* __restrict__ cell_rec, int* __restrict__ err,
@@ -591,23 +595,6 @@ __device__ __forceinline__ void gather_stencil(const FormatSpec& f, const GridSp
         int uu[3] = {ci[0] + dx - g.reach[0], ci[1] + dy - g.reach[1], ci[2] + dz - g.reach[2]};
         int img[3] = {0, 0, 0};
         bool ok = true;
-        if (g.prune) {
-          // skip a cell whose nearest point lies beyond the cutoff (with a relative margin of
-          // 1e-9 in r^2, far above the rounding of the binning): its candidates would all fail
-          // r^2 < rc2, so the rows do not change
-          double d2 = 0.0;
-#pragma unroll
-          for (int d = 0; d < 3; ++d) {
-            double clo = g.org[d] + uu[d] * g.h[d], chi = clo + g.h[d];
-            if (!g.periodic) {
-              if (uu[d] <= 0) clo = -INFINITY;
-              if (uu[d] >= g.n[d] - 1) chi = INFINITY;
-            }
-            const double t = fmax(fmax(clo - xi[d], xi[d] - chi), 0.0);
-            d2 += t * t;
-          }
-          ok = d2 <= rc2 * (1.0 + 1e-9);
-        }
 #pragma unroll
         for (int d = 0; d < 3; ++d) {
           if (g.periodic) {
@@ -678,7 +665,7 @@ __device__ __forceinline__ void gather_stencil(const FormatSpec& f, const GridSp
         double r2 = 0;
         if (code >= 0) {
           double r[3];
-          image_vector(g, xi, ra[u].x, ra[u].y, rc[u].x, code, r);
+          image_vector<DB>(g, xi, ra[u].x, ra[u].y, rc[u].x, code, r);
           r2 = dadd(dadd(dmul(r[0], r[0]), dmul(r[1], r[1])), dmul(r[2], r[2]));
           const bool self = (j == i) && code == image_code(0, 0, 0);
           const bool type_ok = (tj >= 0 && tj < f.ntypes);
@@ -692,6 +679,7 @@ __device__ __forceinline__ void gather_stencil(const FormatSpec& f, const GridSp
   }
 }
 
+template <bool DB>
 __global__ void __launch_bounds__(kFmtWarps * 32)
     k_format(FormatSpec f, GridSpec g, const double* __restrict__ xw, const int* __restrict__ cell_of,
              const int* __restrict__ cell_start, const CellRec* __restrict__ cell_rec, int* __restrict__ nl_j,
@@ -708,7 +696,7 @@ __global__ void __launch_bounds__(kFmtWarps * 32)
   int ncnt[kMaxTypes];
 #pragma unroll
   for (int t = 0; t < kMaxTypes; ++t) ncnt[t] = 0;
-  gather_stencil(f, g, xi, i, cell_of[i], f.rc2, cell_start, cell_rec, err, s_start[warp], s_pref[warp],
+  gather_stencil<DB>(f, g, xi, i, cell_of[i], f.rc2, cell_start, cell_rec, err, s_start[warp], s_pref[warp],
                  s_code[warp], lane, [&](bool valid, int tj, double r2, int j, int code, int ridx) {
                    cand_push(f, b, ncnt, valid, tj, r2, j, code, ridx, lt_mask);
                  });
@@ -717,7 +705,7 @@ __global__ void __launch_bounds__(kFmtWarps * 32)
            [&](int src, int code, double (&r)[3]) {
              const double2* p = reinterpret_cast<const double2*>(cell_rec + src);
              const double2 a = __ldg(p), c = __ldg(p + 1);
-             image_vector(g, xi, a.x, a.y, c.x, code, r);
+             image_vector<DB>(g, xi, a.x, a.y, c.x, code, r);
            });
 }
 
@@ -727,6 +715,7 @@ __global__ void __launch_bounds__(kFmtWarps * 32)
 // with the positions of each call, shifted by the lattice vectors each atom
 // was wrapped by when the candidates were built (so the image codes stay
 // valid as atoms cross the cell boundary, and under a changing cell).
+template <bool DB>
 __global__ void __launch_bounds__(kFmtWarps * 32)
     k_verlet_build(FormatSpec f, GridSpec g, double rcand2, int capS, const double* __restrict__ xw,
                    const int* __restrict__ cell_of, const int* __restrict__ cell_start,
@@ -742,7 +731,7 @@ __global__ void __launch_bounds__(kFmtWarps * 32)
   int n = 0;
   int* cj = cand_j + (size_t)i * capS;
   int* cc = cand_code + (size_t)i * capS;
-  gather_stencil(f, g, xi, i, cell_of[i], rcand2, cell_start, cell_rec, err, s_start[warp], s_pref[warp],
+  gather_stencil<DB>(f, g, xi, i, cell_of[i], rcand2, cell_start, cell_rec, err, s_start[warp], s_pref[warp],
                  s_code[warp], lane, [&](bool valid, int, double, int j, int code, int) {
                    const unsigned m = __ballot_sync(0xffffffffu, valid);
                    const int pos = n + __popc(m & lt_mask);
@@ -761,14 +750,16 @@ __global__ void __launch_bounds__(kFmtWarps * 32)
 // Position of atom j shifted by its build-time lattice shift, with the
 // arithmetic of k_bin's wrap (so a call right after a build sees the wrapped
 // coordinates bit for bit).
+template <bool DB>
 __device__ __forceinline__ void shifted(const GridSpec& g, const double* __restrict__ x, const int* __restrict__ ls,
                                         int j, double (&w)[3]) {
   const double f0 = (double)ls[3 * j], f1 = (double)ls[3 * j + 1], f2 = (double)ls[3 * j + 2];
 #pragma unroll
   for (int k = 0; k < 3; ++k)
-    w[k] = dsub(x[3 * j + k], dadd(dadd(dmul(f0, gB(g, k)), dmul(f1, gB(g, 3 + k))), dmul(f2, gB(g, 6 + k))));
+    w[k] = dsub(x[3 * j + k], dadd(dadd(dmul(f0, gB<DB>(g, k)), dmul(f1, gB<DB>(g, 3 + k))), dmul(f2, gB<DB>(g, 6 + k))));
 }
 
+template <bool DB>
 __global__ void __launch_bounds__(kFmtWarps * 32)
     k_format_verlet(FormatSpec f, GridSpec g, int capS, double half_skin2, const double* __restrict__ x,
                     const int* __restrict__ atype, const int* __restrict__ lshift, const double* __restrict__ xref,
@@ -782,7 +773,7 @@ __global__ void __launch_bounds__(kFmtWarps * 32)
   if (i >= f.nloc) return;
   const CandBuf b = cand_buf(smem, warp, f);
   double xi[3];
-  shifted(g, x, lshift, i, xi);
+  shifted<DB>(g, x, lshift, i, xi);
   if (lane == 0) {
     double d2 = 0;
 #pragma unroll
@@ -809,8 +800,8 @@ __global__ void __launch_bounds__(kFmtWarps * 32)
       code = cc[k];
       tj = atype[j];
       double xj[3], r[3];
-      shifted(g, x, lshift, j, xj);
-      image_vector(g, xi, xj[0], xj[1], xj[2], code, r);
+      shifted<DB>(g, x, lshift, j, xj);
+      image_vector<DB>(g, xi, xj[0], xj[1], xj[2], code, r);
       r2 = dadd(dadd(dmul(r[0], r[0]), dmul(r[1], r[1])), dmul(r[2], r[2]));
       valid = (tj >= 0 && tj < f.ntypes) && r2 < f.rc2;
     }
@@ -819,8 +810,8 @@ __global__ void __launch_bounds__(kFmtWarps * 32)
   __syncwarp();
   emit_row(f, i, b, ncnt, lane, nl_j, nl_code, nl_rij, nl_cnt, err, [&](int src, int code, double (&r)[3]) {
     double xj[3];
-    shifted(g, x, lshift, cj[src], xj);
-    image_vector(g, xi, xj[0], xj[1], xj[2], code, r);
+    shifted<DB>(g, x, lshift, cj[src], xj);
+    image_vector<DB>(g, xi, xj[0], xj[1], xj[2], code, r);
   });
 }
 
@@ -829,8 +820,13 @@ void launch_verlet_build(cudaStream_t st, const FormatSpec& f, const GridSpec& g
                          int* cand_j, int* cand_code, int* cand_cnt, int* err, const int* gate) {
   if (f.nloc <= 0) return;
   count_launch();
-  k_verlet_build<<<(f.nloc + kFmtWarps - 1) / kFmtWarps, kFmtWarps * 32, 0, st>>>(
-      f, g, rcand * rcand, capS, xw, cell_of, cell_start, cell_rec, cand_j, cand_code, cand_cnt, err, gate);
+  const dim3 grid((f.nloc + kFmtWarps - 1) / kFmtWarps);
+  if (g.dB)
+    k_verlet_build<true><<<grid, kFmtWarps * 32, 0, st>>>(f, g, rcand * rcand, capS, xw, cell_of, cell_start,
+                                                          cell_rec, cand_j, cand_code, cand_cnt, err, gate);
+  else
+    k_verlet_build<false><<<grid, kFmtWarps * 32, 0, st>>>(f, g, rcand * rcand, capS, xw, cell_of, cell_start,
+                                                           cell_rec, cand_j, cand_code, cand_cnt, err, gate);
 }
 
 // Displacement check of every atom against the positions the candidates were
@@ -882,11 +878,19 @@ void launch_format_verlet(cudaStream_t st, const FormatSpec& f, const GridSpec& 
                           double* nl_rij, int* nl_cnt, int* err, int* stale) {
   if (f.nloc <= 0) return;
   const size_t smem = format_smem_bytes(f);
-  format_attr(k_format_verlet, smem);
+  const dim3 grid((f.nloc + kFmtWarps - 1) / kFmtWarps);
   count_launch();
-  k_format_verlet<<<(f.nloc + kFmtWarps - 1) / kFmtWarps, kFmtWarps * 32, smem, st>>>(
-      f, g, capS, 0.25 * skin * skin, x, atype, lshift, xref, cand_j, cand_code, cand_cnt, nl_j, nl_code, nl_rij,
-      nl_cnt, err, stale);
+  if (g.dB) {
+    format_attr<k_format_verlet<true>>(smem);
+    k_format_verlet<true><<<grid, kFmtWarps * 32, smem, st>>>(f, g, capS, 0.25 * skin * skin, x, atype, lshift, xref,
+                                                              cand_j, cand_code, cand_cnt, nl_j, nl_code, nl_rij,
+                                                              nl_cnt, err, stale);
+  } else {
+    format_attr<k_format_verlet<false>>(smem);
+    k_format_verlet<false><<<grid, kFmtWarps * 32, smem, st>>>(f, g, capS, 0.25 * skin * skin, x, atype, lshift,
+                                                               xref, cand_j, cand_code, cand_cnt, nl_j, nl_code,
+                                                               nl_rij, nl_cnt, err, stale);
+  }
 }
 
 void launch_format(cudaStream_t st, const FormatSpec& f, const GridSpec& g, const double* xw, const int* cell_of,
@@ -894,11 +898,17 @@ void launch_format(cudaStream_t st, const FormatSpec& f, const GridSpec& g, cons
                    int* nl_cnt, int* err) {
   if (f.nloc <= 0) return;
   const size_t smem = format_smem_bytes(f);
-  format_attr(k_format, smem);
+  const dim3 grid((f.nloc + kFmtWarps - 1) / kFmtWarps);
   count_launch();
-  k_format<<<(f.nloc + kFmtWarps - 1) / kFmtWarps, kFmtWarps * 32, smem, st>>>(f, g, xw, cell_of, cell_start,
-                                                                               cell_rec, nl_j, nl_code, nl_rij,
-                                                                               nl_cnt, err);
+  if (g.dB) {
+    format_attr<k_format<true>>(smem);
+    k_format<true><<<grid, kFmtWarps * 32, smem, st>>>(f, g, xw, cell_of, cell_start, cell_rec, nl_j, nl_code, nl_rij,
+                                                       nl_cnt, err);
+  } else {
+    format_attr<k_format<false>>(smem);
+    k_format<false><<<grid, kFmtWarps * 32, smem, st>>>(f, g, xw, cell_of, cell_start, cell_rec, nl_j, nl_code,
+                                                        nl_rij, nl_cnt, err);
+  }
 }
 
 // Caller-provided candidates (LAMMPS full list): cand_start is a CSR over
@@ -1019,7 +1029,7 @@ void launch_format_graph(cudaStream_t st, const FormatSpec& f, const int64_t* at
                          double* nl_rij, int* nl_cnt, int* err, const RawGeometry& raw) {
   if (f.nloc <= 0) return;
   const size_t smem = format_smem_bytes(f);
-  format_attr(k_format_graph, smem);
+  format_attr<k_format_graph>(smem);
   count_launch();
   k_format_graph<<<(f.nloc + kFmtWarps - 1) / kFmtWarps, kFmtWarps * 32, smem, st>>>(
       f, atype64, row_ptr, source, edge_vec, atype32, nl_j, nl_code, nl_rij, nl_cnt, err, raw);
@@ -1030,7 +1040,7 @@ void launch_format_candidates(cudaStream_t st, const FormatSpec& f, const double
                               double* nl_rij, int* nl_cnt, int* err) {
   if (f.nloc <= 0) return;
   const size_t smem = format_smem_bytes(f);
-  format_attr(k_format_candidates, smem);
+  format_attr<k_format_candidates>(smem);
   count_launch();
   k_format_candidates<<<(f.nloc + kFmtWarps - 1) / kFmtWarps, kFmtWarps * 32, smem, st>>>(
       f, coord, atype, ilist, cand_start, cand, nl_j, nl_code, nl_rij, nl_cnt, err);

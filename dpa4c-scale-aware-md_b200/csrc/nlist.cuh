@@ -25,12 +25,6 @@ struct GridSpec {
   int n[3];         // cells per dimension
   int reach[3];     // stencil half-width in cells
   int ncells;
-  // Cartesian cell geometry for skipping stencil cells wholly beyond the
-  // cutoff (orthorhombic periodic boxes and open grids): cell u of dimension d
-  // spans [org + u h, org + (u + 1) h); the open grid's edge cells also hold
-  // the atoms clamped into them, so they extend to infinity outwards
-  int prune;
-  double org[3], h[3];
   // periodic box read from device memory ([B | Binv], 18 doubles) instead of
   // B / Binv above, when set: the box of a barostat changes on the device
   // between calls; the cell counts and the stencil reach then come from a

@@ -514,11 +514,11 @@ void launch_fit_seed(cudaStream_t st, int Mmax, const int* range, int N, const P
 // F_j = sum_{own row} g - sum_{edges into j} g.  One warp per centre i sums its
 // own row in a fixed order (slot order, xor-tree warp reduction) and scatters
 // -g of every edge into the neighbour's accumulator.  The accumulators are
-// fixed point with 64 fractional bits, added with integer atomics: integer
-// addition is associative, so the sum does not depend on the order in which
-// edges arrive (deterministic), and it is exact to 2^-64 per term.  A second
-// pass converts each accumulator to fp64, adds the own-row part and clears
-// the accumulator for the next call.
+// 128-bit two's-complement fixed point with 64 fractional bits, added with
+// integer atomics: integer addition is associative, so the sum does not
+// depend on the order in which edges arrive (deterministic), and it is exact
+// to 2^-64 per term.  A second pass converts each accumulator to fp64, adds
+// the own-row part and clears the accumulator for the next call.
 //
 // The total virial -sum g (x) r runs over every edge once and is summed over
 // the own rows; the per-atom virial (edges into j) is scattered the same way
@@ -528,32 +528,27 @@ void launch_fit_seed(cudaStream_t st, int Mmax, const int* range, int N, const P
 constexpr int kAsmWarps = 8;
 constexpr int kAsmCols = 10;  // virial (9) + energy
 
-// An accumulator is two 64-bit words that are added independently: the
-// coarse word sums c = floor(v 2^32) (two's complement) and the fine word
-// sums f = (v 2^32 - c) 2^32 in [0, 2^32), so that v 2^64 truncated toward
-// -inf at 2^-64 is c 2^32 + f (|v| < 2^31; fewer than 2^32 terms per word).
-// No carry travels between the words, so both additions are fire-and-forget
-// reductions (the atomics' results are not used), and zero parts are not sent.
+// v * 2^64 as (lo, hi), truncated toward -inf at 2^-64; |v| < 2^63.  For
+// |v| < 1 the high word's increment (integer part + carry) is usually zero
+// and is then not sent.
 __device__ __forceinline__ void fix_add(unsigned long long* __restrict__ p, double v) {
-  const double s = v * 0x1p32;
-  const double c = floor(s);
-  const long long ci = (long long)c;
-  const unsigned long long f = (unsigned long long)((s - c) * 0x1p32);
-  if (ci) atomicAdd(p, (unsigned long long)ci);
-  if (f) atomicAdd(p + 1, f);
+  const double fl = floor(v);
+  const unsigned long long hi = (unsigned long long)(long long)fl;
+  const unsigned long long lo = (unsigned long long)((v - fl) * 0x1p64);
+  const unsigned long long old = atomicAdd(p, lo);
+  const unsigned long long inc = hi + (old + lo < old ? 1ull : 0ull);
+  if (inc) atomicAdd(p + 1, inc);
 }
 
-// The value of an accumulator: the 128-bit integer c 2^32 + f times 2^-64.
-__device__ __forceinline__ double fix_value(unsigned long long c, unsigned long long f) {
-  const __int128 t = ((__int128)(long long)c << 32) + (__int128)f;
-  const unsigned long long lo = (unsigned long long)t, hi = (unsigned long long)(t >> 64);
+__device__ __forceinline__ double fix_value(unsigned long long lo, unsigned long long hi) {
   return (double)(long long)hi + (double)lo * 0x1p-64;
 }
 
-// Another accumulator's words (c, f) added to the accumulator at p.
-__device__ __forceinline__ void fix_add128(unsigned long long* p, unsigned long long c, unsigned long long f) {
-  if (c) atomicAdd(p, c);
-  if (f) atomicAdd(p + 1, f);
+// (lo, hi) added to the 128-bit accumulator at p.
+__device__ __forceinline__ void fix_add128(unsigned long long* p, unsigned long long lo, unsigned long long hi) {
+  const unsigned long long old = atomicAdd(p, lo);
+  const unsigned long long inc = hi + (old + lo < old ? 1ull : 0ull);
+  if (inc) atomicAdd(p + 1, inc);
 }
 
 // Peer fold (domain decomposition): owned neighbours' contributions go to
@@ -712,7 +707,7 @@ void launch_assemble(cudaStream_t st, int nloc, int nall, int selt, const int* n
 }
 
 // Each ghost row's sums (acc_f rows nloc..nall) are added to its owner's
-// accumulator in the owner's memory (its two words per component), and
+// accumulator in the owner's memory (one 128-bit addition per component), and
 // the local rows are cleared for the next call.
 __global__ void k_fold_push(int nloc, int nghost, unsigned long long* __restrict__ acc_f,
                             unsigned* __restrict__ nonfinite, PeerSet peers, const int2* __restrict__ origin) {

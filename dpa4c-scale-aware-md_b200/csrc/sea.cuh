@@ -75,7 +75,7 @@ void launch_assemble(cudaStream_t st, int nloc, int nall, int selt, const int* n
 int assemble_blocks(int nloc);
 // Domain decomposition over NVLink peers.  Every rank exports one device
 // buffer (CUDA IPC) holding its owned atoms' fixed-point force accumulator
-// ([cap][3][coarse, fine] u64 at off_acc, the two words of k_assemble's fixed point), their non-finite flags (u32 at off_nf)
+// ([cap][3][lo, hi] u64 at off_acc), their non-finite flags (u32 at off_nf)
 // and their published positions ([cap][3] f64 at off_x); base[r] is rank r's
 // buffer as mapped in this process.
 struct PeerSet {

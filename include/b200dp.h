@@ -327,7 +327,7 @@ b200dp_status b200dp_neighbor_stats(b200dp_engine* engine, long long* builds);
  *   b200dp_compute_device_fold  the ghost-mode force call: energy and virial
  *                        of the owned atoms' edges as usual; the ghost rows'
  *                        reverse contributions are added into the owners'
- *                        accumulators (64-bit integer reductions over NVLink:
+ *                        accumulators (128-bit integer atomics over NVLink:
  *                        order-independent sums) and d_force is not complete
  *                        yet;
  *   b200dp_fold_finish   after EVERY rank's compute_device_fold has completed
