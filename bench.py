@@ -906,8 +906,13 @@ def run_sweep(args, world, rank, local):
                     w = Periodic(dp, system, dev, stream, torch)
                 else:
                     grid = sweep_grid(label, world)
-                    w = Decomposed(dp, system, grid, rank, dev, stream, torch, peer_fold=args.reverse == "peer")
-                    line["parallelism"] = f"domain decomposition {grid[0]}x{grid[1]}x{grid[2]}, peer fold"
+                    if args.driver == "cpp":
+                        w = DecomposedCpp(dp, system, grid, rank, world, dev, stream, torch, dist)
+                        line["parallelism"] = (f"C++ decomposed driver, {grid[0]}x{grid[1]}x{grid[2]}, peer memory, "
+                                               "device-side rendezvous")
+                    else:
+                        w = Decomposed(dp, system, grid, rank, dev, stream, torch, peer_fold=args.reverse == "peer")
+                        line["parallelism"] = f"domain.py decomposition {grid[0]}x{grid[1]}x{grid[2]}, peer fold"
                 # about 2 s of timed work, at least 3 steps
                 w.step()
                 torch.cuda.synchronize()
@@ -928,6 +933,8 @@ def run_sweep(args, world, rank, local):
                 dp.check()
                 line.update({"mode": "force call", "value": system.natoms * k / (ms / 1e3), "ms_per_step": ms / k,
                              "steps": k, "timing": "CUDA events per step, max over ranks, L2 flushed before each"})
+                if hasattr(w, "close"):
+                    w.close()
                 del w
                 dp.close()
             except Exception as ex:  # report, never hide
@@ -961,6 +968,45 @@ def run_sweep(args, world, rank, local):
             except Exception as ex:  # report, never hide
                 line["error"] = repr(ex)[:400]
             print(json.dumps(line), flush=True)
+            torch.cuda.empty_cache()
+        if md_cfg and world > 1 and args.driver == "cpp":
+            # MD over the decomposition (the C++ driver): atoms migrate and the ghost plan is rebuilt
+            # every 10 steps; time = max over ranks of the host wall clock around the run
+            ens, nsteps, temp = md_cfg
+            grid = sweep_grid(label, world)
+            line = {"sweep": label, "n_gpus": world, "atoms": system.natoms, "precision": "mixed", "model": kind,
+                    "unit": "atom-steps/s",
+                    "mode": f"decomposed MD {ens.upper()} {nsteps} steps, dt 0.5 fs, {temp:g} K"
+                    + (", 1 bar" if ens == "npt" else "") + ", migration and ghost plan every 10 steps",
+                    "parallelism": f"C++ decomposed driver, {grid[0]}x{grid[1]}x{grid[2]}"}
+            try:
+                dp = b200dp.DeepPot(models[kind], precision=b200dp.MIXED, device=local)
+                w = DecomposedCpp(dp, system, grid, rank, world, dev, stream, torch, dist)
+                kw = dict(dt=0.0005, ensemble=b200dp.NPT if ens == "npt" else b200dp.NVT, t_init=temp,
+                          t_target=temp, t_damp=0.05, seed=1, rebuild_every=10)
+                if ens == "npt":
+                    kw.update(p_target=1.0, p_damp=0.5)
+                w.dd.md_start(MASSES[kind], **kw)
+                w.dd.md_run(3)
+                w.dd.thermo()
+                dist.barrier()
+                t0 = time.perf_counter()
+                w.dd.md_run(nsteps)
+                th = w.dd.thermo()
+                dt = time.perf_counter() - t0
+                tt = torch.tensor([dt], dtype=torch.float64, device=dev)
+                dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+                dt = float(tt.item())
+                line.update({"value": system.natoms * nsteps / dt, "ms_per_step": 1e3 * dt / nsteps,
+                             "steps": nsteps, "temperature_K": th["temp"], "conserved": th["conserved"],
+                             "volume": th["volume"],
+                             "timing": "host wall clock around the run + final read, max over ranks"})
+                w.close()
+                dp.close()
+            except Exception as ex:  # report, never hide
+                line["error"] = repr(ex)[:400]
+            if rank == 0:
+                print(json.dumps(line), flush=True)
             torch.cuda.empty_cache()
     if dist:
         dist.barrier()

@@ -482,15 +482,6 @@ __device__ __forceinline__ float tanh_r(float zc) {
   return r;
 }
 
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
-          taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
-      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
-      : "memory");
-}
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // D[tmem] (+)= A[tmem] * B^T: the A operand is read from tensor memory.
 __device__ __forceinline__ void mma_ta(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t accumulate) {
@@ -579,9 +570,9 @@ __device__ __forceinline__ void bwd_epi3(const float* f, uint32_t taddr, const f
     uint32_t pk[16];
 #pragma unroll
     for (int q = 0; q < 8; ++q) umma::split_pair(v[2 * q], v[2 * q + 1], pk[q], pk[8 + q]);
-    tmem_st16(taddr + H * 64 + c * 16, pk);
+    umma::st16(taddr + H * 64 + c * 16, pk);
   }
-  tmem_wait_st();
+  umma::wait_st();
 }
 
 // dh2 total = MMA + layer-3 residual gradient; dz2' = dh2 (1 - t2^2) / c;

@@ -47,8 +47,15 @@ b200dp_status cuda_fail(cudaError_t e, const char* expr, const char* file, int l
   return B200DP_ERR_CUDA;
 }
 
+// Bumped whenever a device buffer is freed or (re)allocated: a recorded host
+// call (Engine::compute_host) is valid only while no buffer it names moved.
+static std::atomic<long long> g_buffer_epoch{0};
+
 void DevBuf::release() {
-  if (ptr) cudaFree(ptr);
+  if (ptr) {
+    cudaFree(ptr);
+    g_buffer_epoch.fetch_add(1, std::memory_order_relaxed);
+  }
   ptr = nullptr;
   bytes = 0;
 }
@@ -56,6 +63,7 @@ void DevBuf::release() {
 cudaError_t DevBuf::ensure(size_t need) {
   if (need <= bytes) return cudaSuccess;
   release();
+  g_buffer_epoch.fetch_add(1, std::memory_order_relaxed);
   const size_t alloc = std::max<size_t>(need + need / 8, 256);
   cudaError_t e = cudaMalloc(&ptr, alloc);
   if (e == cudaSuccess) bytes = alloc;
@@ -380,6 +388,7 @@ void Engine::release() {
   for (auto& b : dz_l) b.release();
   for (auto& ev : events)
     if (ev) cudaEventDestroy(ev);
+  hc_drop();
   if (own_stream) cudaStreamDestroy(own_stream);
   own_stream = nullptr;
 }
@@ -1108,6 +1117,37 @@ b200dp_status Engine::set_neighbor_reuse(double skin, int every) {
   return B200DP_OK;
 }
 
+bool Engine::HostCallKey::operator==(const HostCallKey& o) const {
+  if (nloc != o.nloc || epoch != o.epoch) return false;
+  for (int i = 0; i < 5; ++i)
+    if (ptrs[i] != o.ptrs[i]) return false;
+  for (int i = 0; i < 9; ++i)
+    if (box[i] != o.box[i]) return false;
+  return true;
+}
+
+void Engine::hc_drop() {
+  if (hc_exec) cudaGraphExecDestroy(hc_exec);
+  hc_exec = nullptr;
+  hc_key = HostCallKey{};
+  hc_failed = false;
+}
+
+// True when every non-null pointer is page-locked host memory (a recorded copy
+// reads and writes it directly; pageable memory goes through the direct path).
+static bool all_pinned(const void* const* p, int n) {
+  for (int i = 0; i < n; ++i) {
+    if (!p[i]) continue;
+    cudaPointerAttributes at{};
+    if (cudaPointerGetAttributes(&at, p[i]) != cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+    if (at.type != cudaMemoryTypeHost) return false;
+  }
+  return true;
+}
+
 b200dp_status Engine::compute_host(int nloc, int nghost, const double* coord, const int* atype, const double* box,
                                    const b200dp_nlist* nlist, double* energy, double* force, double* virial,
                                    double* atom_energy, double* atom_virial) {
@@ -1124,52 +1164,115 @@ b200dp_status Engine::compute_host(int nloc, int nghost, const double* coord, co
   B200DP_CUDA_TRY(h_force.ensure(sizeof(double) * 3 * std::max(nall, 1)));
   if (atom_virial) B200DP_CUDA_TRY(h_aviral.ensure(sizeof(double) * 9 * std::max(nall, 1)));
   if (atom_energy) B200DP_CUDA_TRY(h_ae.ensure(sizeof(double) * std::max(nloc, 1)));
-  if (nall > 0) {
-    B200DP_CUDA_TRY(cudaMemcpyAsync(h_coord.ptr, coord, sizeof(double) * 3 * nall, cudaMemcpyHostToDevice, st));
-    B200DP_CUDA_TRY(cudaMemcpyAsync(h_atype.ptr, atype, sizeof(int) * nall, cudaMemcpyHostToDevice, st));
-  }
-  double* d_scal = scalars.as<double>();
-  b200dp_status rc;
-  if (nlist) {
-    rc = compute_with_nlist(st, nloc, nall, h_coord.as<double>(), h_atype.as<int>(), nlist, d_scal, h_force.as<double>(),
-                            d_scal + 1, atom_energy ? h_ae.as<double>() : nullptr,
-                            atom_virial ? h_aviral.as<double>() : nullptr);
-  } else {
-    double region[6];
-    const double* reg = nullptr;
-    if (!(box && nghost == 0)) {
-      for (int d = 0; d < 3; ++d) {
-        region[d] = 1e300;
-        region[3 + d] = -1e300;
-      }
-      for (int i = 0; i < nall; ++i)
-        for (int d = 0; d < 3; ++d) {
-          region[d] = std::min(region[d], coord[3 * i + d]);
-          region[3 + d] = std::max(region[3 + d], coord[3 * i + d]);
-        }
-      if (nall == 0)
-        for (int d = 0; d < 6; ++d) region[d] = 0;
-      reg = region;
-    }
-    rc = compute_device(st, nloc, nghost, h_coord.as<double>(), h_atype.as<int>(), (box && nghost == 0) ? box : nullptr,
-                        reg, d_scal, h_force.as<double>(), d_scal + 1, atom_energy ? h_ae.as<double>() : nullptr,
-                        atom_virial ? h_aviral.as<double>() : nullptr);
-  }
-  if (rc != B200DP_OK) return rc;
   // scalars, error flags and the stale flag in one pinned block: [10 f64][kErrCount i32][stale i32]
   if (!pin) B200DP_CUDA_TRY(cudaHostAlloc(reinterpret_cast<void**>(&pin), 256, cudaHostAllocDefault));
   double* sc = reinterpret_cast<double*>(pin);
   int* flags = reinterpret_cast<int*>(pin + 80);
   flags[kErrCount] = 0;
-  B200DP_CUDA_TRY(cudaMemcpyAsync(sc, d_scal, sizeof(double) * 10, cudaMemcpyDeviceToHost, st));
-  B200DP_CUDA_TRY(cudaMemcpyAsync(flags, err_buf.ptr, sizeof(int) * kErrCount, cudaMemcpyDeviceToHost, st));
-  if (vl_stale.ptr)
-    B200DP_CUDA_TRY(cudaMemcpyAsync(flags + kErrCount, vl_stale.ptr, sizeof(int), cudaMemcpyDeviceToHost, st));
-  if (nall > 0) B200DP_CUDA_TRY(cudaMemcpyAsync(force, h_force.ptr, sizeof(double) * 3 * nall, cudaMemcpyDeviceToHost, st));
-  if (atom_energy && nloc > 0)
-    B200DP_CUDA_TRY(cudaMemcpyAsync(atom_energy, h_ae.ptr, sizeof(double) * nloc, cudaMemcpyDeviceToHost, st));
-  if (atom_virial && nall > 0)
-    B200DP_CUDA_TRY(cudaMemcpyAsync(atom_virial, h_aviral.ptr, sizeof(double) * 9 * nall, cudaMemcpyDeviceToHost, st));
+  double* d_scal = scalars.as<double>();
+
+  // the stream work of one call: inputs in, the evaluation, results out
+  auto enqueue = [&]() -> b200dp_status {
+    if (nall > 0) {
+      B200DP_CUDA_TRY(cudaMemcpyAsync(h_coord.ptr, coord, sizeof(double) * 3 * nall, cudaMemcpyHostToDevice, st));
+      B200DP_CUDA_TRY(cudaMemcpyAsync(h_atype.ptr, atype, sizeof(int) * nall, cudaMemcpyHostToDevice, st));
+    }
+    b200dp_status rc;
+    if (nlist) {
+      rc = compute_with_nlist(st, nloc, nall, h_coord.as<double>(), h_atype.as<int>(), nlist, d_scal,
+                              h_force.as<double>(), d_scal + 1, atom_energy ? h_ae.as<double>() : nullptr,
+                              atom_virial ? h_aviral.as<double>() : nullptr);
+    } else {
+      double region[6];
+      const double* reg = nullptr;
+      if (!(box && nghost == 0)) {
+        for (int d = 0; d < 3; ++d) {
+          region[d] = 1e300;
+          region[3 + d] = -1e300;
+        }
+        for (int i = 0; i < nall; ++i)
+          for (int d = 0; d < 3; ++d) {
+            region[d] = std::min(region[d], coord[3 * i + d]);
+            region[3 + d] = std::max(region[3 + d], coord[3 * i + d]);
+          }
+        if (nall == 0)
+          for (int d = 0; d < 6; ++d) region[d] = 0;
+        reg = region;
+      }
+      rc = compute_device(st, nloc, nghost, h_coord.as<double>(), h_atype.as<int>(),
+                          (box && nghost == 0) ? box : nullptr, reg, d_scal, h_force.as<double>(), d_scal + 1,
+                          atom_energy ? h_ae.as<double>() : nullptr, atom_virial ? h_aviral.as<double>() : nullptr);
+    }
+    if (rc != B200DP_OK) return rc;
+    B200DP_CUDA_TRY(cudaMemcpyAsync(sc, d_scal, sizeof(double) * 10, cudaMemcpyDeviceToHost, st));
+    B200DP_CUDA_TRY(cudaMemcpyAsync(flags, err_buf.ptr, sizeof(int) * kErrCount, cudaMemcpyDeviceToHost, st));
+    if (vl_stale.ptr)
+      B200DP_CUDA_TRY(cudaMemcpyAsync(flags + kErrCount, vl_stale.ptr, sizeof(int), cudaMemcpyDeviceToHost, st));
+    if (nall > 0)
+      B200DP_CUDA_TRY(cudaMemcpyAsync(force, h_force.ptr, sizeof(double) * 3 * nall, cudaMemcpyDeviceToHost, st));
+    if (atom_energy && nloc > 0)
+      B200DP_CUDA_TRY(cudaMemcpyAsync(atom_energy, h_ae.ptr, sizeof(double) * nloc, cudaMemcpyDeviceToHost, st));
+    if (atom_virial && nall > 0)
+      B200DP_CUDA_TRY(
+          cudaMemcpyAsync(atom_virial, h_aviral.ptr, sizeof(double) * 9 * nall, cudaMemcpyDeviceToHost, st));
+    return B200DP_OK;
+  };
+
+  // Replay: a periodic call (box, no ghosts, no caller list) without neighbour
+  // reuse (whose host-side schedule changes from call to call), stage timing or
+  // peer mode, on page-locked host buffers.  Keyed by the atom count, the host
+  // pointers, the box and the device-buffer epoch; the first call of a key runs
+  // directly, the second is recorded and replayed, later ones replay.
+  const void* hp[5] = {coord, atype, force, atom_energy, atom_virial};
+  const bool replayable = !nlist && box && nghost == 0 && nall > 0 && vl_every == 0 && !timing && !dbox_dev &&
+                          pf_nranks == 0 && all_pinned(hp, 5);
+  HostCallKey key;
+  if (replayable) {
+    key.nloc = nloc;
+    for (int i = 0; i < 5; ++i) key.ptrs[i] = hp[i];
+    for (int i = 0; i < 9; ++i) key.box[i] = box[i];
+    key.epoch = g_buffer_epoch.load(std::memory_order_relaxed);
+  }
+  b200dp_status rc = B200DP_OK;
+  bool done = false;
+  if (replayable && key == hc_key && hc_exec) {
+    g_launches.fetch_add(hc_launches, std::memory_order_relaxed);
+    B200DP_CUDA_TRY(cudaGraphLaunch(hc_exec, st));
+    done = true;
+  } else if (replayable && key == hc_key && !hc_failed) {
+    const long long l0 = launch_count();
+    cudaGraph_t g = nullptr;
+    if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+      rc = enqueue();
+      const cudaError_t ce = cudaStreamEndCapture(st, &g);
+      cudaGraphExec_t ex = nullptr;
+      if (rc == B200DP_OK && ce == cudaSuccess && g &&
+          g_buffer_epoch.load(std::memory_order_relaxed) == key.epoch && cudaGraphInstantiate(&ex, g, 0) == cudaSuccess) {
+        hc_exec = ex;
+        hc_launches = launch_count() - l0;
+      }
+      if (g) cudaGraphDestroy(g);
+    }
+    cudaGetLastError();
+    g_launches.fetch_sub(launch_count() - l0, std::memory_order_relaxed);  // the recording ran nothing
+    if (hc_exec) {
+      g_launches.fetch_add(hc_launches, std::memory_order_relaxed);
+      B200DP_CUDA_TRY(cudaGraphLaunch(hc_exec, st));
+      done = true;
+    } else {
+      hc_failed = true;  // this key runs directly from now on
+    }
+  } else if (!(replayable && key == hc_key) && (hc_exec || hc_key.nloc >= 0)) {
+    hc_drop();  // another shape, buffer or mode: forget the recorded call
+  }
+  if (!done) {
+    rc = enqueue();
+    if (rc != B200DP_OK) return rc;
+    if (replayable && !hc_failed) {
+      hc_key = key;
+      hc_key.epoch = g_buffer_epoch.load(std::memory_order_relaxed);  // buffers the call itself sized
+    }
+  }
   B200DP_CUDA_TRY(cudaStreamSynchronize(st));
   *energy = sc[0];
   std::memcpy(virial, sc + 1, 9 * sizeof(double));

@@ -109,6 +109,21 @@ struct Engine {
   // pinned host block for the host call's scalars and error flags (one D2H, one sync)
   unsigned char* pin = nullptr;
   b200dp_status check_flags(const int* h, int stale);
+  // A periodic host call whose shape, host buffers, box and device buffers
+  // repeat is recorded once (at its second occurrence) and then replayed as
+  // one CUDA graph: copies in, the evaluation, copies out.
+  struct HostCallKey {
+    int nloc = -1;
+    const void* ptrs[5] = {};
+    double box[9] = {};
+    long long epoch = -1;
+    bool operator==(const HostCallKey& o) const;
+  };
+  HostCallKey hc_key;
+  cudaGraphExec_t hc_exec = nullptr;
+  long long hc_launches = 0;
+  bool hc_failed = false;
+  void hc_drop();
 
   cudaStream_t own_stream = nullptr;
   cudaStream_t last_stream = nullptr;

@@ -254,6 +254,301 @@ __global__ void __launch_bounds__(kFitThreads, 2) k_fit_gemm(GemmArgs a) {
   if (warp == 0) umma::tmem_dealloc(tm, 256);
 }
 
+// ------------------------------------------------------------ hidden chain
+// Layers 1 .. L-1 forward and then backward (down to dz0) for one 128-row
+// tile per CTA, in one launch.  The tile's activation operand (at most 256
+// columns, bf16 hi and lo, 128 KB) stays in shared memory from layer to layer:
+// each epilogue writes the next GEMM's A operand in place, after the GEMM that
+// read it has completed.  The weights of all steps stream through one ring of
+// shared-memory stages (warp 16), so the next step's first K chunks arrive
+// while the current epilogue runs; warp 17 issues the MMAs (N = the layer's
+// whole width).  TMEM: the accumulator in columns [0, 256), and in [256, 512)
+// the fp32 value a later epilogue of the same thread adds as a residual
+// (layer output y_l in the forward, dE/dy_l in the backward).  The tanh
+// outputs that the backward needs stay in global memory (L2-resident).
+// Every step keeps the arithmetic of the per-layer kernel above (k_fit_gemm),
+// column by column; the energy adds the partial sums of four column parts.
+constexpr int kChainK = 256;  // widest activation operand (columns)
+constexpr int kChainEpiWarps = 16;
+constexpr int kChainThreads = kChainEpiWarps * 32 + 64;
+constexpr uint32_t kChainAct = 2 * (kChainK / kFitBK) * kABlock;  // hi region, then lo region
+constexpr size_t kChainSmemMax = 227 * 1024 - 8192;  // dynamic shared memory budget of k_fit_chain
+
+struct ChainArgs {
+  int ntypes;
+  const int* type_start;
+  const int* ftile;
+  int L;
+  int width[kFitMaxLayers], kpad[kFitMaxLayers], res[kFitMaxLayers];
+  int bnf[kFitMaxLayers], bnb[kFitMaxLayers];
+  const unsigned char* A_hi;  // tiled input of layer 1 (y0)
+  const unsigned char* A_lo;
+  const unsigned char* fB_hi[kMaxTypes][kFitMaxLayers];
+  const unsigned char* fB_lo[kMaxTypes][kFitMaxLayers];
+  const unsigned char* bB_hi[kMaxTypes][kFitMaxLayers];
+  const unsigned char* bB_lo[kMaxTypes][kFitMaxLayers];
+  const float* bias[kMaxTypes][kFitMaxLayers];
+  const float* wo[kMaxTypes];
+  double bo[kMaxTypes];
+  const float* Y0;                  // layer-0 output (residual of layer 1)
+  float* TH[kFitMaxLayers];         // tanh outputs (TH[0] written by the layer-0 launch)
+  const int* perm_atom;
+  double* atom_e;
+  unsigned char* Z_hi;  // dz0, tiled (kpad_z columns), the final backward's A operand
+  unsigned char* Z_lo;
+  int kpad_z;
+  int stages;
+  int* err;
+};
+
+// GEMM step j: forward layer j + 1 for j < L - 1, then backward layers L - 1 .. 1.
+struct ChainStep {
+  int l, fwd, N, nk, bn;
+};
+__device__ __forceinline__ ChainStep chain_step(const ChainArgs& a, int j) {
+  ChainStep c;
+  c.fwd = j < a.L - 1;
+  c.l = c.fwd ? j + 1 : 2 * a.L - 2 - j;
+  c.N = c.fwd ? a.width[c.l] : a.width[c.l - 1];
+  c.nk = c.fwd ? a.kpad[c.l] / kFitBK : (a.width[c.l] + kFitBK - 1) / kFitBK;
+  c.bn = c.fwd ? a.bnf[c.l] : a.bnb[c.l];
+  return c;
+}
+
+__device__ __forceinline__ uint32_t act_off(int r, int k) {
+  return (uint32_t)(k / kFitBK) * kABlock + (uint32_t)(r >> 3) * kSbo + (uint32_t)((k % kFitBK) >> 3) * 128u +
+         (uint32_t)(r & 7) * 16u;
+}
+
+__global__ void __launch_bounds__(kChainThreads, 1) k_fit_chain(ChainArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem[];
+  __shared__ uint64_t full[kMaxStages], empty[kMaxStages], a_in, acc_full, act_full;
+  __shared__ uint32_t tbase;
+  __shared__ int s_fail;
+  __shared__ double s_e[kChainEpiWarps / 4][128];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = blockIdx.x;
+  if (g >= a.ftile[a.ntypes]) return;  // CTA-uniform, before any TMEM allocation
+  int t = 0;
+  while (t + 1 < a.ntypes && a.ftile[t + 1] <= g) ++t;
+  const int row0 = a.type_start[t] + 128 * (g - a.ftile[t]);
+  const int nrows = min(128, a.type_start[t + 1] - row0);
+  const int nsteps = 2 * (a.L - 1);
+  unsigned char* act = smem;
+  unsigned char* ring = smem + kChainAct;
+  uint32_t SB = 0;  // ring stage: the widest step's B chunk, hi then lo
+  for (int j = 0; j < nsteps; ++j) SB = max(SB, (uint32_t)chain_step(a, j).N * kFitBK * 2 * 2);
+  const int S = a.stages;
+  if (warp == 0) umma::tmem_alloc(&tbase, 512);
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      umma::mbar_init(&full[s], 1);
+      umma::mbar_init(&empty[s], 1);
+    }
+    umma::mbar_init(&a_in, 1);
+    umma::mbar_init(&acc_full, 1);
+    umma::mbar_init(&act_full, kChainEpiWarps * 32);
+    umma::fence_mbar_init();
+    s_fail = 0;
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+  const int nk1 = a.kpad[1] / kFitBK;
+  if (warp == kChainEpiWarps && lane == 0) {  // loader: y0 once, then every step's weights through the ring
+    const uint32_t half = (uint32_t)nk1 * kABlock;
+    umma::mbar_expect_tx(&a_in, 2 * half);
+    umma::bulk_g2s(act, a.A_hi + (size_t)g * half, half, &a_in);
+    umma::bulk_g2s(act + kChainAct / 2, a.A_lo + (size_t)g * half, half, &a_in);
+    int s = 0, round = 0;
+    bool ok = true;
+    for (int j = 0; j < nsteps && ok; ++j) {
+      const ChainStep c = chain_step(a, j);
+      const unsigned char* Bh = c.fwd ? a.fB_hi[t][c.l] : a.bB_hi[t][c.l];
+      const unsigned char* Bl = c.fwd ? a.fB_lo[t][c.l] : a.bB_lo[t][c.l];
+      const uint32_t blk = (uint32_t)c.bn * kFitBK * 2, nb = (uint32_t)(c.N / c.bn);
+      for (int kc = 0; kc < c.nk; ++kc) {
+        if (round > 0 && !umma::mbar_wait(&empty[s], (round - 1) & 1, kWaitLimit)) {
+          ok = false;
+          break;
+        }
+        unsigned char* st = ring + s * SB;
+        umma::mbar_expect_tx(&full[s], 2 * nb * blk);
+        // the N blocks of the packed weights (BN rows each) side by side make one N-row operand
+        for (uint32_t nt = 0; nt < nb; ++nt) {
+          umma::bulk_g2s(st + nt * blk, Bh + ((size_t)nt * c.nk + kc) * blk, blk, &full[s]);
+          umma::bulk_g2s(st + nb * blk + nt * blk, Bl + ((size_t)nt * c.nk + kc) * blk, blk, &full[s]);
+        }
+        if (++s == S) {
+          s = 0;
+          ++round;
+        }
+      }
+    }
+    if (!ok) s_fail = 1;
+  } else if (warp == kChainEpiWarps + 1 && lane == 0) {  // MMA issuer
+    bool ok = umma::mbar_wait(&a_in, 0, kWaitLimit);
+    int s = 0, round = 0;
+    for (int j = 0; j < nsteps && ok; ++j) {
+      const ChainStep c = chain_step(a, j);
+      // the A operand is ready: the zero fill (j = 0) or the previous epilogue
+      ok = umma::mbar_wait(&act_full, j & 1, kWaitLimit);
+      if (!ok) break;
+      umma::fence_after_sync();
+      const uint32_t idesc = umma::idesc_bf16(128, c.N, false, false);
+      const uint64_t dah = umma::desc(umma::smem_u32(act), 128, kSbo);
+      const uint64_t dal = umma::desc(umma::smem_u32(act + kChainAct / 2), 128, kSbo);
+      const uint64_t db0 = umma::desc(umma::smem_u32(ring), 128, kSbo);
+      const uint64_t o_bl = ((uint64_t)c.N * kFitBK * 2) >> 4, sstep = SB >> 4, kstep = kABlock >> 4;
+      for (int kc = 0; kc < c.nk; ++kc) {
+        ok = umma::mbar_wait(&full[s], round & 1, kWaitLimit);
+        if (!ok) break;
+        umma::fence_after_sync();
+        const uint64_t ah = dah + (uint64_t)kc * kstep, al = dal + (uint64_t)kc * kstep;
+        const uint64_t bh = db0 + (uint64_t)s * sstep, bl = bh + o_bl;
+#pragma unroll
+        for (int ks = 0; ks < kFitBK / 16; ++ks) {
+          const uint64_t o = (uint64_t)(ks * (256 >> 4));
+          umma::mma(tbase, ah + o, bh + o, idesc, (kc | ks) ? 1u : 0u);
+          umma::mma(tbase, ah + o, bl + o, idesc, 1u);
+          umma::mma(tbase, al + o, bh + o, idesc, 1u);
+        }
+        umma::commit(&empty[s]);
+        if (++s == S) {
+          s = 0;
+          ++round;
+        }
+      }
+      if (ok) umma::commit(&acc_full);
+    }
+    if (!ok) s_fail = 1;
+  } else if (warp < kChainEpiWarps) {  // epilogue
+    const int q = warp & 3, part = warp >> 2, nparts = kChainEpiWarps / 4;
+    const int r = q * 32 + lane;  // row within the tile (TMEM lane)
+    const bool valid = r < nrows;
+    const int prow = g * 128 + r;
+    const uint32_t lb = (uint32_t)(q * 32) << 16;
+    const uint32_t acc = tbase + lb, car = tbase + lb + 256;
+    unsigned char* ah = act;
+    unsigned char* al = act + kChainAct / 2;
+    // the activation chunks that y0 does not fill are zero (K padding of wider layers)
+    for (uint32_t i = (uint32_t)nk1 * kABlock / 16 + (tid & 511); i < kChainAct / 32; i += kChainEpiWarps * 32) {
+      reinterpret_cast<uint4*>(ah)[i] = make_uint4(0u, 0u, 0u, 0u);
+      reinterpret_cast<uint4*>(al)[i] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    umma::fence_proxy_async();
+    umma::fence_before_sync();
+    umma::mbar_arrive(&act_full);
+    bool ok = true;
+    double e_acc = 0.0;
+    for (int j = 0; j < nsteps; ++j) {
+      const ChainStep c = chain_step(a, j);
+      const int l = c.l, N = c.N;
+      const bool last_fwd = c.fwd && l == a.L - 1;
+      if (ok) ok = umma::mbar_wait(&acc_full, j & 1, kWaitLimit);
+      ok = __all_sync(0xffffffffu, ok);  // the TMEM loads below are warp-collective
+      umma::fence_after_sync();
+      for (int cc = part; ok && cc < N / 16; cc += nparts) {
+        const int col0 = cc * 16;
+        float v[16], x[16], u[16];
+        if (c.fwd) {
+          // x: residual input (y_{l-1}), u: bias; loaded before the accumulator
+          const bool res = a.res[l] != 0;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            u[i] = __ldg(a.bias[t][l] + col0 + i);
+            x[i] = (res && l == 1 && valid) ? a.Y0[colmajor_off(prow, col0 + i, a.width[0])] : 0.f;
+          }
+          umma::ld16(acc + col0, v);
+          if (res && l >= 2) umma::ld16(car + col0, x);
+          umma::wait_ld();
+          float y[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float th = umma::tanh_fast(v[i] + u[i]);
+            y[i] = res ? th + x[i] : th;
+            v[i] = th;
+          }
+          if (l + 1 < a.L && a.res[l + 1]) umma::st16f(car + col0, y);
+          if (valid) {
+            if (!last_fwd) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) a.TH[l][colmajor_off(prow, col0 + i, N)] = v[i];
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const uint32_t o = act_off(r, col0 + 8 * h);
+                store8_split(ah + o, al + o, y + 8 * h);
+              }
+            } else {
+              float zs[16];
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const float w = __ldg(a.wo[t] + col0 + i);
+                e_acc += (double)(y[i] * w);
+                zs[i] = w * (1.f - v[i] * v[i]);
+              }
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const uint32_t o = act_off(r, col0 + 8 * h);
+                store8_split(ah + o, al + o, zs + 8 * h);
+              }
+            }
+          }
+        } else {
+          // x: dE/dy_l (residual of layer l), u: tanh outputs of layer l - 1
+          const bool res = a.res[l] != 0, top = l == a.L - 1;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            u[i] = valid ? a.TH[l - 1][colmajor_off(prow, col0 + i, N)] : 0.f;
+            x[i] = (res && top) ? __ldg(a.wo[t] + col0 + i) : 0.f;
+          }
+          umma::ld16(acc + col0, v);
+          if (res && !top) umma::ld16(car + col0, x);
+          umma::wait_ld();
+          float z[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float d = v[i] + x[i];
+            v[i] = d;
+            z[i] = d * (1.f - u[i] * u[i]);
+          }
+          if (a.res[l - 1]) umma::st16f(car + col0, v);
+          if (valid) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              if (l > 1) {
+                const uint32_t o = act_off(r, col0 + 8 * h);
+                store8_split(ah + o, al + o, z + 8 * h);
+              } else {
+                const size_t o = tiled_off(prow, col0 + 8 * h, a.kpad_z);
+                store8_split(a.Z_hi + o, a.Z_lo + o, z + 8 * h);
+              }
+            }
+          }
+        }
+      }
+      umma::wait_st();
+      if (last_fwd) {  // partial energies of the column parts, summed in part order
+        s_e[part][r] = e_acc;
+        umma::bar_sync(1, kChainEpiWarps * 32);
+        if (part == 0 && valid && ok) {
+          double e = a.bo[t];
+          for (int p2 = 0; p2 < nparts; ++p2) e += s_e[p2][r];
+          a.atom_e[a.perm_atom[row0 + r]] = e;
+        }
+      }
+      umma::fence_proxy_async();
+      umma::fence_before_sync();
+      umma::mbar_arrive(&act_full);
+    }
+    if (!ok) s_fail = 1;
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  if (tid == 0 && s_fail) atomicAdd(a.err + 3, 1);
+  if (warp == 0) umma::tmem_dealloc(tbase, 512);
+}
+
 // ------------------------------------------------------------ final backward
 // dD = dz0 W0^T fused with the descriptor contraction (D = T^T T_<, with T
 // already divided by N):
@@ -588,6 +883,17 @@ FitTcPlan fit_tc_plan(const HostModel& m) {
                       kDtSmemMax)
     p.bn_out = 0;
   p.ok = p.bn_out > 0;
+  // hidden layers 1 .. L-1 in one launch: every operand at most kChainK wide, and the
+  // activation tile plus two ring stages of the widest step fit in shared memory
+  p.chain = p.ok && p.L >= 2;
+  int nmax = 0;
+  for (int l = 1; l < p.L && p.chain; ++l) {
+    if (p.kpad[l] > kChainK || round32(p.width[l]) > kChainK) p.chain = false;
+    nmax = std::max(nmax, std::max(p.width[l], p.width[l - 1]));
+  }
+  if (p.chain && kChainAct + 2 * (size_t)nmax * kFitBK * 4 > kChainSmemMax) p.chain = false;
+  p.chain_stages = p.chain ? (int)std::min<size_t>(kMaxStages, (kChainSmemMax - kChainAct) / ((size_t)nmax * kFitBK * 4))
+                           : 0;
   return p;
 }
 
@@ -658,7 +964,8 @@ void launch_fit_tc(cudaStream_t st, const FitTcPlan& p, int ntypes, int nloc, co
   if (nloc <= 0) return;
   const int row_tiles = (nloc + 127) / 128 + ntypes;
   const int L = p.L;
-  for (int l = 0; l < L; ++l) {
+  const bool chain = p.chain;
+  for (int l = 0; l < (chain ? 1 : L); ++l) {
     GemmArgs a;
     std::memset(&a, 0, sizeof(a));
     a.ntypes = ntypes;
@@ -696,7 +1003,54 @@ void launch_fit_tc(cudaStream_t st, const FitTcPlan& p, int ntypes, int nloc, co
     a.err = err;
     run_gemm(st, a, row_tiles, p.width[l] / p.bnf[l]);
   }
-  for (int s = 0; s < L; ++s) {
+  if (chain) {
+    ChainArgs c;
+    std::memset(&c, 0, sizeof(c));
+    c.ntypes = ntypes;
+    c.type_start = type_start;
+    c.ftile = ftile;
+    c.L = L;
+    for (int l = 0; l < L; ++l) {
+      c.width[l] = p.width[l];
+      c.kpad[l] = p.kpad[l];
+      c.res[l] = p.res[l];
+      c.bnf[l] = p.bnf[l];
+      c.bnb[l] = p.bnb[l];
+      c.TH[l] = b.TH[l];
+      for (int t = 0; t < ntypes; ++t) {
+        c.fB_hi[t][l] = w[t].fB_hi[l];
+        c.fB_lo[t][l] = w[t].fB_lo[l];
+        c.bB_hi[t][l] = w[t].bB_hi[l];
+        c.bB_lo[t][l] = w[t].bB_lo[l];
+        c.bias[t][l] = w[t].bias[l];
+      }
+    }
+    for (int t = 0; t < ntypes; ++t) {
+      c.wo[t] = w[t].wo;
+      c.bo[t] = w[t].bo;
+    }
+    c.A_hi = b.At_hi[1];
+    c.A_lo = b.At_lo[1];
+    c.Y0 = b.Y[0];
+    c.perm_atom = perm_atom;
+    c.atom_e = atom_energy;
+    c.Z_hi = b.Z_hi[(L - 1) & 1];  // where the final backward below reads dz0
+    c.Z_lo = b.Z_lo[(L - 1) & 1];
+    c.kpad_z = round32(p.width[0]);
+    c.stages = p.chain_stages;
+    c.err = err;
+    int nmax = 0;
+    for (int l = 1; l < L; ++l) nmax = std::max(nmax, std::max(p.width[l], p.width[l - 1]));
+    const size_t smem = kChainAct + (size_t)c.stages * nmax * kFitBK * 4;
+    static size_t attr = 0;
+    if (smem > attr) {
+      cudaFuncSetAttribute(k_fit_chain, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      attr = smem;
+    }
+    count_launch();
+    k_fit_chain<<<row_tiles, kChainThreads, smem, st>>>(c);
+  }
+  for (int s = chain ? L - 1 : 0; s < L; ++s) {
     const int l = L - 1 - s;
     GemmArgs a;
     std::memset(&a, 0, sizeof(a));

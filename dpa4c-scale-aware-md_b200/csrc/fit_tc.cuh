@@ -34,6 +34,8 @@ struct FitTcPlan {
   int bnf[kFitMaxLayers] = {};    // N tile of each forward layer (the last one keeps whole rows)
   int bnb[kFitMaxLayers] = {};    // N tile of each backward layer
   bool ok = false;
+  bool chain = false;             // layers 1 .. L-1 (forward and backward) in one launch
+  int chain_stages = 0;
 };
 
 FitTcPlan fit_tc_plan(const HostModel& m);
