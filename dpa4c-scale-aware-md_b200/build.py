@@ -24,9 +24,9 @@ NVCC = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ARCH + ["-lineinfo", "-O3", "-std=c++17", "--expt-relaxed-constexpr", "-Xcompiler",
                 "-fPIC,-ffp-contract=off,-O3", "-ccbin", shutil.which("g++", path="/usr/bin") or "g++"]
-SOURCES = ["nlist.cu", "sea.cu", "embed_tc.cu", "fit_tc.cu", "c8l2.cu", "engine.cu", "selftest.cu", "noalloc.cu", "md.cu",
+SOURCES = ["nlist.cu", "sea.cu", "embed_tc.cu", "embed_f64.cu", "fit_tc.cu", "c8l2.cu", "engine.cu", "selftest.cu", "noalloc.cu", "md.cu",
            "dd.cu"]
-HEADERS = ["common.cuh", "nlist.cuh", "sea.cuh", "engine.hpp", "model.hpp", "umma.cuh", "embed_tc.cuh", "fit_tc.cuh",
+HEADERS = ["common.cuh", "nlist.cuh", "sea.cuh", "engine.hpp", "model.hpp", "umma.cuh", "embed_tc.cuh", "embed_f64.cuh", "fit_tc.cuh",
            "c8l2.cuh", "simt_gemm.cuh", "md_kernels.cuh"]
 
 

@@ -1,0 +1,36 @@
+// fp64 embedding path (the parity mode) over the compacted edge lists of the
+// tensor-core path: work items of kItemRows centre rows of one embedding net,
+// their edges in subtiles of kF64Edges.  Per subtile the embedding layers run
+// as register-tiled fp64 GEMMs (4 edges x 4 features per thread, the net in
+// shared memory for every edge of the item), then the contraction
+// T = R~^T G accumulates in a fixed order (one thread per position and pair of
+// environment components, edges in list order).  The backward recomputes the
+// forward per subtile and forms dG, dR~, dz3, dh2, dz2, dh1 and dE/ds the same
+// way, writing per slot the environment-row gradient that the assembly chains
+// to r_ij.  Replaces the per-centre SIMT kernels (k_descriptor_fwd/bwd) for
+// the [25, 50, 100] embedding; results agree with them to fp64 rounding (the
+// sums run in another order).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "embed_tc.cuh"
+#include "sea.cuh"
+
+namespace b200dp {
+
+constexpr int kF64Edges = 32;
+constexpr int kF64Threads = 256;
+
+bool f64_tiled_supported(const SeaDev& s);
+int embed_f64_grid(const SeaDev& s, bool backward);
+// Tq[net][row][4][M1] per net, then T (atom order, / N) and D = T^T T_< (rows in
+// the type-grouped order) summed over the nets in a fixed order.
+void launch_embed_fwd_f64(cudaStream_t st, const SeaDev& s, const TcLists& L, int grid, const double* rij,
+                          const double* emb, double* Tq, double* T, double* D, const int* perm_atom, int nloc);
+// dT[row][4][M1] from T and dD (rows), then the backward -> genv (4 doubles per slot).
+void launch_embed_bwd_f64(cudaStream_t st, const SeaDev& s, const TcLists& L, int grid, const double* rij,
+                          const double* emb, const double* T, const double* dD, double* dT, double* genv,
+                          const int* type_start, const int* perm_atom, int nloc);
+
+}  // namespace b200dp

@@ -466,10 +466,8 @@ struct BwdArgs {
   const unsigned char* nets;
   size_t net_bytes, fwd_off;
   const float* dT;    // [row][4][D3], already scaled by 1/N
-  const double* rij;  // formatted neighbour list vectors
-  double* gslot;      // dE/dr per slot
+  double* genv;       // per slot: dE/d(environment row) as (dE/ds + dE/dR~_0, dE/dR~_1..3), fp64
   int* err;
-  double rcut, rcut_smth;
 };
 
 constexpr float kInvTanhScale = 0.34657359027997264f;  // 1 / c
@@ -816,34 +814,14 @@ __global__ void __launch_bounds__(256 * BwdGroup::NG, 1) k_embed_bwd_tc(BwdArgs 
       umma::bar_sync(bid, 256);
       umma::fence_after_sync();
       if (hf == 0 && valid) {
+        // the environment-row gradient in fp64; the chain rule to r_ij runs in the assembly
         const float4 o4 = xdr[g][e];
         const double dR0 = kTanhScale * ((double)dR.x + o4.x), dR1 = kTanhScale * ((double)dR.y + o4.y);
         const double dR2 = kTanhScale * ((double)dR.z + o4.z), dR3 = kTanhScale * ((double)dR.w + o4.w);
-        const double dRv[3] = {dR1, dR2, dR3};
         const double dsum = (double)ds + xds[g][e];
-        const int slot = L.slot[sub + e];
-        // chain rule to r_ij in fp64
-        const double* rp = a.rij + 3 * (size_t)slot;
-        const double x = rp[0], y = rp[1], zc = rp[2];
-        const double r2 = x * x + y * y + zc * zc, rr = sqrt(r2);
-        double sw, dsw;
-        smooth_switch(rr, a.rcut_smth, a.rcut, sw, dsw);
-        const double ir = 1.0 / rr, ir2 = ir * ir;
-        const double d0 = dsw * ir - sw * ir2;
-        const double rvec[3] = {x, y, zc};
-        const double g0 = dR0 + dsum;
-        double* go = a.gslot + 3 * (size_t)slot;
-#pragma unroll
-        for (int cc = 0; cc < 3; ++cc) {
-          double acc = g0 * d0 * rvec[cc] * ir;
-#pragma unroll
-          for (int aa = 0; aa < 3; ++aa) {
-            const double J = dsw * rvec[cc] * ir * rvec[aa] * ir2 +
-                             sw * ((aa == cc ? ir2 : 0.0) - 2.0 * rvec[aa] * rvec[cc] * ir2 * ir2);
-            acc += dRv[aa] * J;
-          }
-          go[cc] = acc;
-        }
+        double2* go = reinterpret_cast<double2*>(a.genv + 4 * (size_t)L.slot[sub + e]);
+        go[0] = make_double2(dR0 + dsum, dR1);
+        go[1] = make_double2(dR2, dR3);
       }
     }
     if (aborted) continue;
@@ -1133,14 +1111,14 @@ void launch_fwd(cudaStream_t st, const TcLists& L, int grid, const unsigned char
 
 template <int D1, int D2, int D3>
 void launch_bwd(cudaStream_t st, const TcLists& L, int grid, const unsigned char* nets, const float* dT,
-                const double* rij, double* gslot, int* err, double rcut, double rs) {
+                double* genv, int* err) {
   using S = BwdGroup;
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(k_embed_bwd_tc<D1, D2, D3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::SMEM);
     attr = true;
   }
-  BwdArgs a{L, nets, NetBlob<D1, D2, D3>::BYTES, NetBlob<D1, D2, D3>::OFF_FWD, dT, rij, gslot, err, rcut, rs};
+  BwdArgs a{L, nets, NetBlob<D1, D2, D3>::BYTES, NetBlob<D1, D2, D3>::OFF_FWD, dT, genv, err};
   count_launch();
   k_embed_bwd_tc<D1, D2, D3><<<grid, 256 * S::NG, S::SMEM, st>>>(a);
 }
@@ -1216,9 +1194,9 @@ void launch_embed_fwd_tc(cudaStream_t st, const SeaDev& s, const TcLists& L, int
 }
 
 void launch_embed_bwd_tc(cudaStream_t st, const SeaDev& s, const TcLists& L, int grid, const unsigned char* nets,
-                         const float* dT, const double* rij, double* gslot, int* err) {
-  if (which(s) == Inst::W25) launch_bwd<25, 50, 100>(st, L, grid, nets, dT, rij, gslot, err, s.rcut, s.rcut_smth);
-  if (which(s) == Inst::W32) launch_bwd<32, 64, 128>(st, L, grid, nets, dT, rij, gslot, err, s.rcut, s.rcut_smth);
+                         const float* dT, double* genv, int* err) {
+  if (which(s) == Inst::W25) launch_bwd<25, 50, 100>(st, L, grid, nets, dT, genv, err);
+  if (which(s) == Inst::W32) launch_bwd<32, 64, 128>(st, L, grid, nets, dT, genv, err);
 }
 
 void launch_dT(cudaStream_t st, const SeaDev& s, int nloc, const int* type_start, const int* perm_atom, const float* T,

@@ -72,10 +72,15 @@ void launch_t_combine(cudaStream_t st, const SeaDev& s, const TcLists& L, const 
 void launch_dT(cudaStream_t st, const SeaDev& s, int nloc, const int* type_start, const int* perm_atom, const float* T,
                const float* dD, float* dT);
 // Embedding backward: recomputes the forward per subtile, then dG, dR~ (CUDA
-// cores), the layer backprop (tensor cores) and the chain rule to r_ij (fp64)
-// -> gslot.
+// cores) and the layer backprop (tensor cores) -> genv, per slot the gradient
+// of the energy with respect to the environment row R~ = (sw/r, sw x/r^2,
+// sw y/r^2, sw z/r^2) (sw the smooth switch of r) in fp64: [4 slot] = dE/dR~_0
+// (through both the embedding input and the contraction), [4 slot + 1..3] =
+// dE/dR~_1..3.  The
+// assembly (launch_assemble with an environment gradient) applies the chain
+// rule to r_ij.
 void launch_embed_bwd_tc(cudaStream_t st, const SeaDev& s, const TcLists& L, int grid, const unsigned char* nets,
-                         const float* dT, const double* rij, double* gslot, int* err);
+                         const float* dT, double* genv, int* err);
 // Device error slot written by the tensor-core kernels when a bounded wait expires.
 constexpr int kErrTcTimeout = 3;
 

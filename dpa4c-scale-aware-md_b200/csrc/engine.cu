@@ -20,6 +20,7 @@
 #include <vector>
 
 #include "../../include/b200dp.h"
+#include "embed_f64.cuh"
 #include "engine.hpp"
 #include "model.hpp"
 #include "nlist.cuh"
@@ -172,6 +173,7 @@ b200dp_status Engine::init(const char* path, const b200dp_options* o) {
   maxfit = 1;
   for (int v : hm.fit) maxfit = std::max(maxfit, v);
   use_tc = !fp64 && !opt.simt_only && tc_supported(sd);
+  use_f64t = fp64 && !opt.simt_only && f64_tiled_supported(sd);
   if (use_tc) {
     const size_t nb = tc_net_bytes(sd);
     std::vector<unsigned char> all(nb * sd.nnets), one;
@@ -453,12 +455,13 @@ b200dp_status Engine::ensure_buffers(int nloc, int nall, int ncells, int ncand) 
     B200DP_CUDA_TRY(c8_q.ensure(ps * L * kC8State));
   }
   B200DP_CUDA_TRY(atom_e.ensure(sizeof(double) * L));
-  B200DP_CUDA_TRY(gslot.ensure(sizeof(double) * 3 * S));
+  // per slot dE/dr_ij (3 doubles), or the environment-row gradient of the tensor-core backward (4)
+  B200DP_CUDA_TRY(gslot.ensure(sizeof(double) * ((use_tc || use_f64t) ? 4 : 3) * S));
   B200DP_CUDA_TRY(reduce_part.ensure(sizeof(double) * 10 * assemble_blocks((int)L)));
   if (ncand > 0) B200DP_CUDA_TRY(cand_list.ensure(sizeof(int) * (size_t)ncand));
   const size_t nscan = std::max({(size_t)C, A, (size_t)sd.nnets * L}) + 1;
   B200DP_CUDA_TRY(scan_scratch.ensure(sizeof(int) * scan_scratch_ints((int)nscan)));
-  if (use_tc) {
+  if (use_tc || use_f64t) {  // compacted edge lists and work items
     const size_t NL = (size_t)sd.nnets * L;
     B200DP_CUDA_TRY(ecount.ensure(sizeof(int) * (NL + 1)));
     B200DP_CUDA_TRY(eoff.ensure(sizeof(int) * (NL + 1)));
@@ -467,8 +470,8 @@ b200dp_status Engine::ensure_buffers(int nloc, int nall, int ncells, int ncand) 
     B200DP_CUDA_TRY(rec_rt.ensure(sizeof(float4) * S));
     B200DP_CUDA_TRY(rec_row.ensure(sizeof(int) * S));
     B200DP_CUDA_TRY(rec_slot.ensure(sizeof(int) * S));
-    B200DP_CUDA_TRY(partial.ensure(sizeof(float) * NL * 4 * sd.M1));
-    B200DP_CUDA_TRY(dTbuf.ensure(sizeof(float) * L * 4 * sd.M1));
+    B200DP_CUDA_TRY(partial.ensure(ps * NL * 4 * sd.M1));
+    B200DP_CUDA_TRY(dTbuf.ensure(ps * L * 4 * sd.M1));
   }
   if (use_fit_tc) {
     const size_t rp = 128 * ((L + 127) / 128 + sd.ntypes);
@@ -590,7 +593,7 @@ b200dp_status Engine::run_c8(cudaStream_t st, int nloc, int nall, const int* d_a
   launch_c8_edge_backward<P>(st, c8m, nloc, sd.selt, nl_j.as<int>(), nl_rij.as<double>(), d_atype, w,
                              gslot.as<double>());
   mark(st, 4);
-  return finish_assembly(st, nloc, nall, d_force, d_atom_energy, d_atom_virial, d_energy, d_virial);
+  return finish_assembly(st, nloc, nall, d_force, d_atom_energy, d_atom_virial, d_energy, d_virial, false);
 }
 
 template <typename P>
@@ -601,7 +604,8 @@ b200dp_status Engine::run_model(cudaStream_t st, int nloc, int nall, const int* 
   launch_type_partition(st, nloc, hm.ntypes, d_atype, blk_counts.as<int>(), type_start.as<int>(),
                         perm_pos.as<int>(), perm_atom.as<int>(), err_d);
   mark(st, 1);
-  if (std::is_same<P, float>::value && use_tc) {
+  const bool f64t = std::is_same<P, double>::value && use_f64t;
+  if ((std::is_same<P, float>::value && use_tc) || f64t) {
     const int NL = sd.nnets * nloc;
     launch_edge_count(st, sd, nloc, type_start.as<int>(), perm_atom.as<int>(), d_atype, nl_cnt.as<int>(),
                       ecount.as<int>());
@@ -610,8 +614,15 @@ b200dp_status Engine::run_model(cudaStream_t st, int nloc, int nall, const int* 
                         nl_rij.as<double>(), eoff.as<int>(), rec_rt.as<float4>(), rec_row.as<int>(),
                         rec_slot.as<int>());
     launch_item_table(st, sd, nloc, type_start.as<int>(), tstart.as<int>());
+    launch_item_records(st, sd, tc_lists(nloc), reinterpret_cast<int4*>(item_rec.ptr));
+  }
+  if (f64t) {
+    launch_embed_fwd_f64(st, sd, tc_lists(nloc), embed_f64_grid(sd, false), nl_rij.as<double>(),
+                         reinterpret_cast<const double*>(w_emb.ptr), partial.as<double>(),
+                         reinterpret_cast<double*>(Tbuf.ptr), reinterpret_cast<double*>(Dbuf.ptr), perm_atom.as<int>(),
+                         nloc);
+  } else if (std::is_same<P, float>::value && use_tc) {
     const TcLists Lst = tc_lists(nloc);
-    launch_item_records(st, sd, Lst, reinterpret_cast<int4*>(item_rec.ptr));
     launch_embed_fwd_tc(st, sd, Lst, embed_tc_grid(sd, false), tc_nets.as<unsigned char>(), partial.as<float>(),
                         err_d);
     unsigned char* dth = nullptr;
@@ -694,10 +705,15 @@ b200dp_status Engine::run_model(cudaStream_t st, int nloc, int nall, const int* 
     launch_dT(st, sd, nloc, type_start.as<int>(), perm_atom.as<int>(), reinterpret_cast<const float*>(Tbuf.ptr),
               reinterpret_cast<const float*>(dDbuf.ptr), dTbuf.as<float>());
   mark(st, 3);
-  if (std::is_same<P, float>::value && use_tc) {
+  if (f64t) {
+    launch_embed_bwd_f64(st, sd, tc_lists(nloc), embed_f64_grid(sd, true), nl_rij.as<double>(),
+                         reinterpret_cast<const double*>(w_emb.ptr), reinterpret_cast<const double*>(Tbuf.ptr),
+                         reinterpret_cast<const double*>(dDbuf.ptr), dTbuf.as<double>(), gslot.as<double>(),
+                         type_start.as<int>(), perm_atom.as<int>(), nloc);
+  } else if (std::is_same<P, float>::value && use_tc) {
     const TcLists Lst = tc_lists(nloc);
     launch_embed_bwd_tc(st, sd, Lst, embed_tc_grid(sd, true), tc_nets.as<unsigned char>(), dTbuf.as<float>(),
-                        nl_rij.as<double>(), gslot.as<double>(), err_d);
+                        gslot.as<double>(), err_d);
   } else {
     const int gb = descriptor_grid<P>(sd, ch_bwd, true, nloc);
     launch_descriptor_bwd<P>(st, sd, nloc, ch_bwd, gb, nl_rij.as<double>(), nl_cnt.as<int>(), d_atype,
@@ -705,13 +721,16 @@ b200dp_status Engine::run_model(cudaStream_t st, int nloc, int nall, const int* 
                              gslot.as<double>());
   }
   mark(st, 4);
-  return finish_assembly(st, nloc, nall, d_force, d_atom_energy, d_atom_virial, d_energy, d_virial);
+  return finish_assembly(st, nloc, nall, d_force, d_atom_energy, d_atom_virial, d_energy, d_virial,
+                         (std::is_same<P, float>::value && use_tc) || f64t);
 }
 
 // Force / virial assembly over the slot gradients in gslot and the energy
-// reduction of atom_e (shared by both model profiles).
+// reduction of atom_e (shared by both model profiles); env: gslot holds
+// environment-row gradients (the tensor-core backward), chained to r_ij here.
 b200dp_status Engine::finish_assembly(cudaStream_t st, int nloc, int nall, double* d_force, double* d_atom_energy,
-                                      double* d_atom_virial, double* d_energy, double* d_virial) {
+                                      double* d_atom_virial, double* d_energy, double* d_virial, bool env) {
+  const EnvChain ec{env, sd.rcut, sd.rcut_smth};
   if (acc_fresh) {
     B200DP_CUDA_TRY(cudaMemsetAsync(acc_f.ptr, 0, acc_f.bytes, st));
     B200DP_CUDA_TRY(cudaMemsetAsync(nonfinite.ptr, 0, nonfinite.bytes, st));
@@ -722,7 +741,7 @@ b200dp_status Engine::finish_assembly(cudaStream_t st, int nloc, int nall, doubl
                          atom_e.as<double>(), d_force, acc_f.as<unsigned long long>(), nonfinite.as<unsigned>(),
                          reinterpret_cast<unsigned long long*>(pf_buf), reinterpret_cast<unsigned*>(pf_buf + pf_off_nf),
                          peer_set(), pf_origin.as<int2>(), reduce_part.as<double>(), asm_done.as<unsigned>(),
-                         d_energy, d_virial);
+                         d_energy, d_virial, ec);
     if (d_atom_energy)
       B200DP_CUDA_TRY(cudaMemcpyAsync(d_atom_energy, atom_e.ptr, sizeof(double) * nloc, cudaMemcpyDeviceToDevice, st));
     mark(st, 5);
@@ -736,7 +755,7 @@ b200dp_status Engine::finish_assembly(cudaStream_t st, int nloc, int nall, doubl
   launch_assemble(st, nloc, nall, sd.selt, nl_j.as<int>(), gslot.as<double>(), nl_rij.as<double>(),
                   atom_e.as<double>(), d_force, d_atom_virial, acc_f.as<unsigned long long>(),
                   d_atom_virial ? acc_v.as<unsigned long long>() : nullptr, nonfinite.as<unsigned>(),
-                  reduce_part.as<double>(), asm_done.as<unsigned>(), d_energy, d_virial);
+                  reduce_part.as<double>(), asm_done.as<unsigned>(), d_energy, d_virial, ec);
   if (d_atom_energy)
     B200DP_CUDA_TRY(cudaMemcpyAsync(d_atom_energy, atom_e.ptr, sizeof(double) * nloc, cudaMemcpyDeviceToDevice, st));
   mark(st, 5);

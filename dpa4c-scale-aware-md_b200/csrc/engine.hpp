@@ -54,6 +54,7 @@ struct Engine {
   DevBuf cand_start, cand_list, ilist_d;
   // tensor-core embedding path (mixed mode)
   bool use_tc = false;
+  bool use_f64t = false;  // fp64 mode: the tiled item kernels (embed_f64.cu) over the compacted edge lists
   DevBuf graph_atype, item_rec;
   DevBuf tc_nets, ecount, eoff, tstart, rec_rt, rec_row, rec_slot, partial, scan_scratch, dTbuf;
   // tensor-core fitting (mixed mode)
@@ -153,7 +154,7 @@ struct Engine {
   b200dp_status run_model(cudaStream_t st, int nloc, int nall, const int* d_atype, double* d_force,
                           double* d_atom_energy, double* d_atom_virial, double* d_energy, double* d_virial);
   b200dp_status finish_assembly(cudaStream_t st, int nloc, int nall, double* d_force, double* d_atom_energy,
-                                double* d_atom_virial, double* d_energy, double* d_virial);
+                                double* d_atom_virial, double* d_energy, double* d_virial, bool env);
   b200dp_status compute_device(cudaStream_t st, int nloc, int nghost, const double* d_coord, const int* d_atype,
                                const double* box, const double* region, double* d_energy, double* d_force,
                                double* d_virial, double* d_atom_energy, double* d_atom_virial);

@@ -441,24 +441,40 @@ __global__ void __launch_bounds__(kChainThreads, 1) k_fit_chain(ChainArgs a) {
     umma::mbar_arrive(&act_full);
     bool ok = true;
     double e_acc = 0.0;
+    // the operand a chunk reads from global memory (L2): y0 for the residual of
+    // layer 1, the tanh outputs of layer l - 1 in the backward; fetched one chunk
+    // ahead, the first chunk of a step while its GEMM runs
+    auto fetch = [&](const ChainStep& c, int cc, float* dst) {
+      const int col0 = cc * 16;
+      if (c.fwd) {
+        const bool use = a.res[c.l] && c.l == 1 && valid;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) dst[i] = use ? a.Y0[colmajor_off(prow, col0 + i, a.width[0])] : 0.f;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) dst[i] = valid ? a.TH[c.l - 1][colmajor_off(prow, col0 + i, c.N)] : 0.f;
+      }
+    };
     for (int j = 0; j < nsteps; ++j) {
       const ChainStep c = chain_step(a, j);
       const int l = c.l, N = c.N;
       const bool last_fwd = c.fwd && l == a.L - 1;
+      float gn[16];
+      if (part < N / 16) fetch(c, part, gn);
       if (ok) ok = umma::mbar_wait(&acc_full, j & 1, kWaitLimit);
       ok = __all_sync(0xffffffffu, ok);  // the TMEM loads below are warp-collective
       umma::fence_after_sync();
       for (int cc = part; ok && cc < N / 16; cc += nparts) {
         const int col0 = cc * 16;
         float v[16], x[16], u[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) x[i] = gn[i];
+        if (cc + nparts < N / 16) fetch(c, cc + nparts, gn);
         if (c.fwd) {
-          // x: residual input (y_{l-1}), u: bias; loaded before the accumulator
+          // x: residual input (y_{l-1}; layer 1's came with the fetch), u: bias
           const bool res = a.res[l] != 0;
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            u[i] = __ldg(a.bias[t][l] + col0 + i);
-            x[i] = (res && l == 1 && valid) ? a.Y0[colmajor_off(prow, col0 + i, a.width[0])] : 0.f;
-          }
+          for (int i = 0; i < 16; ++i) u[i] = __ldg(a.bias[t][l] + col0 + i);
           umma::ld16(acc + col0, v);
           if (res && l >= 2) umma::ld16(car + col0, x);
           umma::wait_ld();
@@ -495,11 +511,11 @@ __global__ void __launch_bounds__(kChainThreads, 1) k_fit_chain(ChainArgs a) {
             }
           }
         } else {
-          // x: dE/dy_l (residual of layer l), u: tanh outputs of layer l - 1
+          // x: dE/dy_l (residual of layer l), u: tanh outputs of layer l - 1 (the fetch)
           const bool res = a.res[l] != 0, top = l == a.L - 1;
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            u[i] = valid ? a.TH[l - 1][colmajor_off(prow, col0 + i, N)] : 0.f;
+            u[i] = x[i];
             x[i] = (res && top) ? __ldg(a.wo[t] + col0 + i) : 0.f;
           }
           umma::ld16(acc + col0, v);

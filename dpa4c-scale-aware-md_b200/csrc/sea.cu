@@ -559,13 +559,39 @@ struct FoldTargets {
   unsigned* own_nf;
 };
 
-template <bool kAtomVirial>
+// dE/dr_ij from the environment-row gradient g4 = dE/dR~ (R~ = (sw/r, sw x/r^2,
+// sw y/r^2, sw z/r^2)) by the chain rule through R~(r), in fp64.
+__device__ __forceinline__ void env_chain(const double* g4, const double* r3, double rc, double rs, double* g3) {
+  const double x = r3[0], y = r3[1], zc = r3[2];
+  const double r2 = x * x + y * y + zc * zc, rr = sqrt(r2);
+  double sw, dsw;
+  smooth_switch(rr, rs, rc, sw, dsw);
+  const double ir = 1.0 / rr, ir2 = ir * ir;
+  const double d0 = dsw * ir - sw * ir2;
+  const double rvec[3] = {x, y, zc};
+#pragma unroll
+  for (int cc = 0; cc < 3; ++cc) {
+    double acc = g4[0] * d0 * rvec[cc] * ir;
+#pragma unroll
+    for (int aa = 0; aa < 3; ++aa) {
+      const double J = dsw * rvec[cc] * ir * rvec[aa] * ir2 +
+                       sw * ((aa == cc ? ir2 : 0.0) - 2.0 * rvec[aa] * rvec[cc] * ir2 * ir2);
+      acc += g4[1 + aa] * J;
+    }
+    g3[cc] = acc;
+  }
+}
+
+// One warp per centre over its slots.  gsrc holds per slot either dE/dr_ij
+// (3 doubles) or, with kEnv, the environment-row gradient (4 doubles) that
+// env_chain turns into dE/dr_ij.
+template <bool kAtomVirial, bool kEnv>
 __global__ void __launch_bounds__(kAsmWarps * 32)
-    k_assemble(int nloc, int selt, const int* __restrict__ nl_j, const double* __restrict__ gslot,
+    k_assemble(int nloc, int selt, const int* __restrict__ nl_j, const double* __restrict__ gsrc,
                const double* __restrict__ rij, const double* __restrict__ atom_e, double* __restrict__ force,
                unsigned long long* __restrict__ acc_f, unsigned long long* __restrict__ acc_v,
                unsigned* __restrict__ nonfinite, double* __restrict__ partial, unsigned* __restrict__ done,
-               double* __restrict__ energy, double* __restrict__ virial, FoldTargets fold) {
+               double* __restrict__ energy, double* __restrict__ virial, FoldTargets fold, double rc, double rs) {
   __shared__ double s_part[kAsmWarps][kAsmCols];
   __shared__ int s_last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -579,9 +605,20 @@ __global__ void __launch_bounds__(kAsmWarps * 32)
     for (int s = lane; s < selt; s += 32) {
       const int j = nl_j[row + s];
       if (j >= 0) {
-        const double* g = gslot + 3 * (row + s);
         const double* r = rij + 3 * (row + s);
-        const double g3[3] = {g[0], g[1], g[2]}, r3[3] = {r[0], r[1], r[2]};
+        const double r3[3] = {r[0], r[1], r[2]};
+        double g3[3];
+        if (kEnv) {
+          const double2* g = reinterpret_cast<const double2*>(gsrc + 4 * (row + s));
+          const double2 ga = g[0], gb = g[1];
+          const double g4[4] = {ga.x, ga.y, gb.x, gb.y};
+          env_chain(g4, r3, rc, rs, g3);
+        } else {
+          const double* g = gsrc + 3 * (row + s);
+          g3[0] = g[0];
+          g3[1] = g[1];
+          g3[2] = g[2];
+        }
         f[0] += g3[0];
         f[1] += g3[1];
         f[2] += g3[2];
@@ -688,20 +725,32 @@ int assemble_blocks(int nloc) { return std::max(1, std::min((nloc + kAsmWarps - 
 void launch_assemble(cudaStream_t st, int nloc, int nall, int selt, const int* nl_j, const double* gslot,
                      const double* rij, const double* atom_e, double* force, double* atom_virial,
                      unsigned long long* acc_f, unsigned long long* acc_v, unsigned* nonfinite, double* partial,
-                     unsigned* done, double* energy, double* virial) {
+                     unsigned* done, double* energy, double* virial, const EnvChain& env) {
   if (nall <= 0) return;
   const int nb = assemble_blocks(nloc);
   const int fb = (nall + 255) / 256;
   count_launch();
   count_launch();
   const FoldTargets none{nullptr, nullptr};
+  const double rc = env.rcut, rs = env.rcut_smth;
   if (atom_virial) {
-    k_assemble<true><<<nb, kAsmWarps * 32, 0, st>>>(nloc, selt, nl_j, gslot, rij, atom_e, force, acc_f, acc_v,
-                                                    nonfinite, partial, done, energy, virial, none);
+    if (env.on)
+      k_assemble<true, true><<<nb, kAsmWarps * 32, 0, st>>>(nloc, selt, nl_j, gslot, rij, atom_e, force, acc_f, acc_v,
+                                                            nonfinite, partial, done, energy, virial, none, rc, rs);
+    else
+      k_assemble<true, false><<<nb, kAsmWarps * 32, 0, st>>>(nloc, selt, nl_j, gslot, rij, atom_e, force, acc_f,
+                                                             acc_v, nonfinite, partial, done, energy, virial, none, rc,
+                                                             rs);
     k_assemble_finish<true><<<fb, 256, 0, st>>>(nloc, nall, force, atom_virial, acc_f, acc_v, nonfinite);
   } else {
-    k_assemble<false><<<nb, kAsmWarps * 32, 0, st>>>(nloc, selt, nl_j, gslot, rij, atom_e, force, acc_f, nullptr,
-                                                     nonfinite, partial, done, energy, virial, none);
+    if (env.on)
+      k_assemble<false, true><<<nb, kAsmWarps * 32, 0, st>>>(nloc, selt, nl_j, gslot, rij, atom_e, force, acc_f,
+                                                             nullptr, nonfinite, partial, done, energy, virial, none,
+                                                             rc, rs);
+    else
+      k_assemble<false, false><<<nb, kAsmWarps * 32, 0, st>>>(nloc, selt, nl_j, gslot, rij, atom_e, force, acc_f,
+                                                              nullptr, nonfinite, partial, done, energy, virial, none,
+                                                              rc, rs);
     k_assemble_finish<false><<<fb, 256, 0, st>>>(nloc, nall, force, nullptr, acc_f, nullptr, nonfinite);
   }
 }
@@ -750,11 +799,18 @@ __global__ void k_halo_gather(int nloc, int nghost, double* __restrict__ x, Peer
 void launch_assemble_fold(cudaStream_t st, int nloc, int nall, int selt, const int* nl_j, const double* gslot,
                           const double* rij, const double* atom_e, double* force, unsigned long long* acc_f,
                           unsigned* nonfinite, unsigned long long* own_acc, unsigned* own_nf, const PeerSet& peers,
-                          const int2* origin, double* partial, unsigned* done, double* energy, double* virial) {
+                          const int2* origin, double* partial, unsigned* done, double* energy, double* virial,
+                          const EnvChain& env) {
   count_launch();
   const FoldTargets fold{own_acc, own_nf};
-  k_assemble<false><<<assemble_blocks(nloc), kAsmWarps * 32, 0, st>>>(
-      nloc, selt, nl_j, gslot, rij, atom_e, force, acc_f, nullptr, nonfinite, partial, done, energy, virial, fold);
+  if (env.on)
+    k_assemble<false, true><<<assemble_blocks(nloc), kAsmWarps * 32, 0, st>>>(
+        nloc, selt, nl_j, gslot, rij, atom_e, force, acc_f, nullptr, nonfinite, partial, done, energy, virial, fold,
+        env.rcut, env.rcut_smth);
+  else
+    k_assemble<false, false><<<assemble_blocks(nloc), kAsmWarps * 32, 0, st>>>(
+        nloc, selt, nl_j, gslot, rij, atom_e, force, acc_f, nullptr, nonfinite, partial, done, energy, virial, fold,
+        env.rcut, env.rcut_smth);
   const int nghost = nall - nloc;
   if (nghost > 0) {
     count_launch();

@@ -68,10 +68,18 @@ void launch_fit_backward_layer(cudaStream_t st, int Mmax, const int* range, int 
 // (assemble_blocks(nloc)); acc_f (6 x u64 per atom), acc_v (18 x u64 per atom,
 // only with atom_virial), nonfinite (one per atom) and *done must be zero
 // before the first launch and are zero again after each.
+// With env.on, gslot holds per slot the gradient with respect to the
+// environment row R~ = (sw/r, sw x/r^2, sw y/r^2, sw z/r^2) (4 doubles; the
+// tensor-core backward writes it) and the assembly applies the chain rule to
+// r_ij with the cutoffs in env; otherwise dE/dr_ij (3 doubles).
+struct EnvChain {
+  bool on;
+  double rcut, rcut_smth;
+};
 void launch_assemble(cudaStream_t st, int nloc, int nall, int selt, const int* nl_j, const double* gslot,
                      const double* rij, const double* atom_e, double* force, double* atom_virial,
                      unsigned long long* acc_f, unsigned long long* acc_v, unsigned* nonfinite, double* partial,
-                     unsigned* done, double* energy, double* virial);
+                     unsigned* done, double* energy, double* virial, const EnvChain& env);
 int assemble_blocks(int nloc);
 // Domain decomposition over NVLink peers.  Every rank exports one device
 // buffer (CUDA IPC) holding its owned atoms' fixed-point force accumulator
@@ -115,7 +123,8 @@ void launch_peer_reduce(cudaStream_t st, const PeerSync& ps, unsigned long long*
 void launch_assemble_fold(cudaStream_t st, int nloc, int nall, int selt, const int* nl_j, const double* gslot,
                           const double* rij, const double* atom_e, double* force, unsigned long long* acc_f,
                           unsigned* nonfinite, unsigned long long* own_acc, unsigned* own_nf, const PeerSet& peers,
-                          const int2* origin, double* partial, unsigned* done, double* energy, double* virial);
+                          const int2* origin, double* partial, unsigned* done, double* energy, double* virial,
+                          const EnvChain& env);
 void launch_fold_finish(cudaStream_t st, int nloc, double* force, unsigned long long* acc, unsigned* nonfinite);
 // shift [nghost][3] scaled per component by ratio[3] (the box scaled by a barostat).
 void launch_scale_shifts(cudaStream_t st, int nghost, double* shift, const double* ratio);
