@@ -19,6 +19,43 @@ __device__ __forceinline__ int src_of(int n) {
   return resid(DIN, DOUT) == 1 ? n : (n < DIN ? n : n - DIN);
 }
 
+// tanh in fp64 from e^(2|x|) = 2^n e^r (Cody and Waite's reduction: n the nearest
+// integer to 2|x| / ln 2, r = 2|x| - n ln 2 in two parts, ln 2 split after its
+// 32nd significant bit so that n times the high part is exact), e^r by its Taylor
+// series to degree 11 (|r| <= ln 2 / 2: remainder < 7e-15 relative), then
+// 1 - 2 / (e^(2|x|) + 1) with the reciprocal from a single-precision estimate and
+// two Newton steps.  Absolute error < 5e-15 over the real line (a host emulation
+// of these steps against the C library's tanh on 220,000 points); 2|x| is capped
+// at 80, where tanh is 1 in fp64.  About 30 fp64 operations.
+__device__ __forceinline__ double tanh_d(double x) {
+  constexpr double kLn2Hi = 0.6931471803691238, kLn2Lo = 1.9082149292705877e-10, kInvLn2 = 1.4426950408889634;
+  const double y = fmin(2.0 * fabs(x), 80.0);
+  const double n = rint(y * kInvLn2);
+  double r = fma(-n, kLn2Hi, y);
+  r = fma(-n, kLn2Lo, r);
+  double p = 2.505210838544172e-08;          // 1/11!
+  p = fma(p, r, 2.755731922398589e-07);      // 1/10!
+  p = fma(p, r, 2.7557319223985893e-06);     // 1/9!
+  p = fma(p, r, 2.48015873015873e-05);       // 1/8!
+  p = fma(p, r, 0.0001984126984126984);      // 1/7!
+  p = fma(p, r, 0.001388888888888889);       // 1/6!
+  p = fma(p, r, 0.008333333333333333);       // 1/5!
+  p = fma(p, r, 0.041666666666666664);       // 1/4!
+  p = fma(p, r, 0.16666666666666666);        // 1/3!
+  p = fma(p, r, 0.5);
+  p = fma(p, r, 1.0);
+  p = fma(p, r, 1.0);
+  const double E = __longlong_as_double(__double_as_longlong(p) + ((long long)n << 52));
+  const double d = E + 1.0;  // in [2, 6e34]
+  float rf;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(rf) : "f"((float)d));
+  double q = (double)rf;
+  q = fma(q, fma(-d, q, 1.0), q);
+  q = fma(q, fma(-d, q, 1.0), q);
+  const double t = fma(-2.0, q, 1.0);
+  return isnan(x) ? x : copysign(t, x);
+}
+
 // One net in shared memory (the layout of the SIMT weights: W[k][n] row-major, then b).
 template <int D1, int D2, int D3>
 struct F64Net {
@@ -83,17 +120,18 @@ __device__ __forceinline__ void stage_edges(const TcLists& L, const double* __re
 }
 
 // outT[n][e] = tanh(sum_k inT[k][e] W[k][n] + b[n]) (+ residual inT[src(n)][e]),
-// thread tiles of 4 edges x 4 outputs; consecutive threads take consecutive
-// edge groups (the weight loads of a warp then hit few addresses).
-template <int DIN, int DOUT>
+// thread tiles of 4 edges x TN outputs (TN = 2 for narrow layers, so that the
+// block's threads have work); consecutive threads take consecutive edge groups
+// (the weight loads of a warp then hit few addresses).
+template <int DIN, int DOUT, int TN = 4>
 __device__ __forceinline__ void dense_fwd(const double* inT, const double* W, const double* b, double* outT) {
-  constexpr int EG = kE / 4, NG = (DOUT + 3) / 4;
+  constexpr int EG = kE / 4, NG = (DOUT + TN - 1) / TN;
   constexpr int RM = resid(DIN, DOUT);
   for (int it = threadIdx.x; it < EG * NG; it += blockDim.x) {
-    const int e0 = (it % EG) * 4, n0 = (it / EG) * 4;
-    double acc[4][4];
+    const int e0 = (it % EG) * 4, n0 = (it / EG) * TN;
+    double acc[4][TN];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < TN; ++j) {
       const double bj = n0 + j < DOUT ? b[n0 + j] : 0.0;
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[i][j] = bj;
@@ -103,22 +141,22 @@ __device__ __forceinline__ void dense_fwd(const double* inT, const double* W, co
       const double2 xa = *reinterpret_cast<const double2*>(inT + k * kE + e0);
       const double2 xb = *reinterpret_cast<const double2*>(inT + k * kE + e0 + 2);
       const double x[4] = {xa.x, xa.y, xb.x, xb.y};
-      double w[4];
+      double w[TN];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) w[j] = n0 + j < DOUT ? W[k * DOUT + n0 + j] : 0.0;
+      for (int j = 0; j < TN; ++j) w[j] = n0 + j < DOUT ? W[k * DOUT + n0 + j] : 0.0;
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fma(x[i], w[j], acc[i][j]);
+        for (int j = 0; j < TN; ++j) acc[i][j] = fma(x[i], w[j], acc[i][j]);
     }
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < TN; ++j) {
       const int n = n0 + j;
       if (n >= DOUT) break;
       double h[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        h[i] = tanh(acc[i][j]);
+        h[i] = tanh_d(acc[i][j]);
         if (RM != 0) h[i] += inT[src_of<DIN, DOUT>(n) * kE + e0 + i];
       }
       *reinterpret_cast<double2*>(outT + n * kE + e0) = make_double2(h[0], h[1]);
@@ -132,7 +170,7 @@ template <int D1>
 __device__ __forceinline__ void layer1(const double* rtS, const double* net, double* A1T) {
   for (int i = threadIdx.x; i < D1 * kE; i += blockDim.x) {
     const int n = i / kE, e = i - n * kE;
-    A1T[i] = tanh(rtS[4 * e] * net[n] + net[D1 + n]);
+    A1T[i] = tanh_d(rtS[4 * e] * net[n] + net[D1 + n]);
   }
 }
 
@@ -195,7 +233,7 @@ __global__ void __launch_bounds__(kT) k_embed_fwd_f64(TcLists L, SeaDev s, const
       __syncthreads();
       layer1<D1>(rtS, net + N::W1, A1T);
       __syncthreads();
-      dense_fwd<D1, D2>(A1T, net + N::W2, net + N::B2, A2T);
+      dense_fwd<D1, D2, 2>(A1T, net + N::W2, net + N::B2, A2T);
       __syncthreads();
       dense_fwd<D2, D3>(A2T, net + N::W3, net + N::B3, GT);
       __syncthreads();
@@ -321,10 +359,13 @@ __global__ void k_dT_f64(int nloc, int ntypes, int M2, double inv_nnei, const in
 // outputs minus their residual inputs.
 template <int D1, int D2, int D3>
 struct BwdSmem {
+  // G is overwritten by dz3 in place, the residual gradient of layer 3 goes to the
+  // dz2 region (each element read back by the thread that writes dz2 over it),
+  // the partial dR~ wait in registers until the dz3 region is free again, and dT
+  // is read from global memory (L2): two blocks share an SM
   static constexpr int NET = F64Net<D1, D2, D3>::N;
-  static constexpr int DT = NET, RT = DT + kItemRows * 4 * D3, A1 = RT + 4 * kE, A2 = A1 + D1 * kE,
-                       G = A2 + D2 * kE, Z3 = G + D3 * kE, Z2 = Z3 + D3 * kE, DR = Z2 + D2 * kE,
-                       END = DR + (kT / 32) * kE * 4;
+  static constexpr int RT = NET, A1 = RT + 4 * kE, A2 = A1 + D1 * kE, G = A2 + D2 * kE, Z2 = G + D3 * kE,
+                       END = Z2 + D2 * kE;
   static constexpr size_t BYTES = (size_t)END * sizeof(double) + 2 * kE * sizeof(int);
 };
 
@@ -356,28 +397,26 @@ __device__ __forceinline__ void dense_bwd_tile(const double* gzT, const double* 
 }
 
 template <int D1, int D2, int D3>
-__global__ void __launch_bounds__(kT) k_embed_bwd_f64(TcLists L, SeaDev s, const double* __restrict__ rij,
-                                                     const double* __restrict__ emb, const double* __restrict__ dT,
-                                                     double* __restrict__ genv) {
+__global__ void __launch_bounds__(kT, 2) k_embed_bwd_f64(TcLists L, SeaDev s, const double* __restrict__ rij,
+                                                        const double* __restrict__ emb, const double* __restrict__ dT,
+                                                        double* __restrict__ genv) {
   using N = F64Net<D1, D2, D3>;
   using S = BwdSmem<D1, D2, D3>;
   constexpr int R2 = resid(D1, D2), R3 = resid(D2, D3);
   static_assert(resid(1, D1) == 0, "layer 1 without residual");
   extern __shared__ __align__(16) double sm[];
   double* net = sm;
-  double* dTs = sm + S::DT;   // [row][k][p]
   double* rtS = sm + S::RT;   // [e][4]
   double* A1T = sm + S::A1;   // t1, later dz1
   double* A2T = sm + S::A2;   // h2, later dh2
-  double* GT = sm + S::G;     // G, later dG
-  double* Z3T = sm + S::Z3;   // dz3
-  double* Z2T = sm + S::Z2;   // dz2
-  double* dRp = sm + S::DR;   // [warp][e][4] partial dR~
+  double* GT = sm + S::G;     // G, then dz3, then the partial dR~ [warp][e][4]
+  double* Z2T = sm + S::Z2;   // residual gradient of layer 3, then dz2
   int* rowS = reinterpret_cast<int*>(sm + S::END);
   int* slotS = rowS + kE;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   constexpr int NW = kT / 32;
   static_assert(kE == 32, "one lane per edge in the dG pass");
+  static_assert(NW * kE * 4 <= D3 * kE, "the partial dR~ fit the dz3 region");
   const int nitems = L.istart[L.nnets];
   int loaded = -1;
   for (int it = blockIdx.x; it < nitems; it += gridDim.x) {
@@ -388,10 +427,6 @@ __global__ void __launch_bounds__(kT) k_embed_bwd_f64(TcLists L, SeaDev s, const
       load_net(net, emb, s, I.q, D1, D2, D3);
       loaded = I.q;
     }
-    for (int i = tid; i < kItemRows * 4 * D3; i += kT) {
-      const int r = i / (4 * D3);
-      dTs[i] = I.rb + r < I.re ? dT[(size_t)(I.rb + r) * 4 * D3 + (i - r * 4 * D3)] : 0.0;
-    }
     for (int sub = I.e0; sub < I.e1; sub += kE) {
       const int ne = min(kE, I.e1 - sub);
       __syncthreads();
@@ -399,57 +434,71 @@ __global__ void __launch_bounds__(kT) k_embed_bwd_f64(TcLists L, SeaDev s, const
       __syncthreads();
       layer1<D1>(rtS, net + N::W1, A1T);
       __syncthreads();
-      dense_fwd<D1, D2>(A1T, net + N::W2, net + N::B2, A2T);
+      dense_fwd<D1, D2, 2>(A1T, net + N::W2, net + N::B2, A2T);
       __syncthreads();
       dense_fwd<D2, D3>(A2T, net + N::W3, net + N::B3, GT);
       __syncthreads();
-      {  // dG, dz3, partial dR~: lane = edge, warps over positions
-        const int e = lane, row = rowS[e];
-        const double r0 = rtS[4 * e], r1 = rtS[4 * e + 1], r2 = rtS[4 * e + 2], r3 = rtS[4 * e + 3];
-        const double* dtr = dTs + row * 4 * D3;
-        double q0 = 0.0, q1 = 0.0, q2 = 0.0, q3 = 0.0;
-        for (int p = warp; p < D3; p += NW) {
-          const double d0 = dtr[p], d1 = dtr[D3 + p], d2 = dtr[2 * D3 + p], d3 = dtr[3 * D3 + p];
-          const double g = GT[p * kE + e];
-          const double dg = ((r0 * d0 + r1 * d1) + r2 * d2) + r3 * d3;
-          q0 = fma(g, d0, q0);
-          q1 = fma(g, d1, q1);
-          q2 = fma(g, d2, q2);
-          q3 = fma(g, d3, q3);
-          const double t3 = R3 != 0 ? g - A2T[src_of<D2, D3>(p) * kE + e] : g;
-          Z3T[p * kE + e] = dg * (1.0 - t3 * t3);
-          GT[p * kE + e] = dg;
+      // dG, dz3 (over G), the residual gradient into layer 2, partial dR~:
+      // lane = edge, warps over positions; the positions that share a residual
+      // source (s and s + D2 under the concat rule) go to the same thread
+      const int e = lane, row = rowS[e];
+      const double r0 = rtS[4 * e], r1 = rtS[4 * e + 1], r2 = rtS[4 * e + 2], r3 = rtS[4 * e + 3];
+      const double* dtr = dT + (size_t)(I.rb + row) * 4 * D3;
+      double q0 = 0.0, q1 = 0.0, q2 = 0.0, q3 = 0.0;
+      auto position = [&](int p, double base) -> double {  // returns dG
+        const double d0 = __ldg(dtr + p), d1 = __ldg(dtr + D3 + p), d2 = __ldg(dtr + 2 * D3 + p),
+                     d3 = __ldg(dtr + 3 * D3 + p);
+        const double g = GT[p * kE + e];
+        const double dg = ((r0 * d0 + r1 * d1) + r2 * d2) + r3 * d3;
+        q0 = fma(g, d0, q0);
+        q1 = fma(g, d1, q1);
+        q2 = fma(g, d2, q2);
+        q3 = fma(g, d3, q3);
+        const double t3 = g - base;
+        GT[p * kE + e] = dg * (1.0 - t3 * t3);
+        return dg;
+      };
+      if constexpr (R3 == 2) {
+        for (int sp = warp; sp < D2; sp += NW) {
+          const double h2 = A2T[sp * kE + e];
+          const double ga = position(sp, h2), gb = position(sp + D2, h2);
+          Z2T[sp * kE + e] = ga + gb;
         }
-        double* pr = dRp + (warp * kE + e) * 4;
-        pr[0] = q0;
-        pr[1] = q1;
-        pr[2] = q2;
-        pr[3] = q3;
+      } else if constexpr (R3 == 1) {
+        for (int p = warp; p < D3; p += NW) Z2T[p * kE + e] = position(p, A2T[p * kE + e]);
+      } else {
+        for (int p = warp; p < D3; p += NW) position(p, 0.0);
       }
       __syncthreads();
       // dh2 = dz3 W3^T + residual of layer 3; dz2 = dh2 (1 - t2^2)
       for (int it2 = tid; it2 < (kE / 4) * ((D2 + 3) / 4); it2 += kT) {
         double acc[4][4];
         int e0, m0;
-        dense_bwd_tile<D2, D3>(Z3T, net + N::W3, it2, acc, e0, m0);
+        dense_bwd_tile<D2, D3>(GT, net + N::W3, it2, acc, e0, m0);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int m = m0 + j;
           if (m >= D2) break;
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const int e = e0 + i;
+            const int ee = e0 + i;
             double dh = acc[i][j];
-            if (R3 == 1) dh += GT[m * kE + e];
-            if (R3 == 2) dh += GT[m * kE + e] + GT[(m + D2) * kE + e];
-            const double h2 = A2T[m * kE + e];
-            const double t2 = R2 != 0 ? h2 - A1T[src_of<D1, D2>(m) * kE + e] : h2;
-            Z2T[m * kE + e] = dh * (1.0 - t2 * t2);
-            A2T[m * kE + e] = dh;  // read above by this thread only
+            if (R3 != 0) dh += Z2T[m * kE + ee];
+            const double h2 = A2T[m * kE + ee];
+            const double t2 = R2 != 0 ? h2 - A1T[src_of<D1, D2>(m) * kE + ee] : h2;
+            Z2T[m * kE + ee] = dh * (1.0 - t2 * t2);  // over the residual gradient read above
+            A2T[m * kE + ee] = dh;                     // read above by this thread only
           }
         }
       }
       __syncthreads();
+      {  // the dz3 region is free: the partial dR~ of this warp
+        double* pr = GT + (warp * kE + e) * 4;
+        pr[0] = q0;
+        pr[1] = q1;
+        pr[2] = q2;
+        pr[3] = q3;
+      }
       // dh1 = dz2 W2^T + residual of layer 2; dz1 = dh1 (1 - t1^2) over t1
       for (int it2 = tid; it2 < (kE / 4) * ((D1 + 3) / 4); it2 += kT) {
         double acc[4][4];
@@ -461,25 +510,25 @@ __global__ void __launch_bounds__(kT) k_embed_bwd_f64(TcLists L, SeaDev s, const
           if (m >= D1) break;
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const int e = e0 + i;
+            const int ee = e0 + i;
             double dh = acc[i][j];
-            if (R2 == 1) dh += A2T[m * kE + e];
-            if (R2 == 2) dh += A2T[m * kE + e] + A2T[(m + D1) * kE + e];
-            const double t1 = A1T[m * kE + e];
-            A1T[m * kE + e] = dh * (1.0 - t1 * t1);
+            if (R2 == 1) dh += A2T[m * kE + ee];
+            if (R2 == 2) dh += A2T[m * kE + ee] + A2T[(m + D1) * kE + ee];
+            const double t1 = A1T[m * kE + ee];
+            A1T[m * kE + ee] = dh * (1.0 - t1 * t1);
           }
         }
       }
       __syncthreads();
       if (tid < ne) {  // dE/ds, the partial dR~ in warp order, the slot's environment-row gradient
-        const int e = tid;
+        const int ee = tid;
         double ds = 0.0;
-        for (int m = 0; m < D1; ++m) ds = fma(A1T[m * kE + e], net[N::W1 + m], ds);
+        for (int m = 0; m < D1; ++m) ds = fma(A1T[m * kE + ee], net[N::W1 + m], ds);
         double g[4] = {0.0, 0.0, 0.0, 0.0};
         for (int w = 0; w < NW; ++w)
 #pragma unroll
-          for (int k = 0; k < 4; ++k) g[k] += dRp[(w * kE + e) * 4 + k];
-        double2* go = reinterpret_cast<double2*>(genv + 4 * (size_t)slotS[e]);
+          for (int k = 0; k < 4; ++k) g[k] += GT[(w * kE + ee) * 4 + k];
+        double2* go = reinterpret_cast<double2*>(genv + 4 * (size_t)slotS[ee]);
         go[0] = make_double2(g[0] + ds, g[1]);
         go[1] = make_double2(g[2], g[3]);
       }

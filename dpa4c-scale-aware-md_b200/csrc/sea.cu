@@ -4,6 +4,8 @@
 // and virial stay in fp64 in both modes.
 #include <algorithm>
 
+#include <type_traits>
+
 #include "sea.cuh"
 #include "simt_gemm.cuh"
 
@@ -448,10 +450,15 @@ template <typename P>
 void launch_fit_forward_layer(cudaStream_t st, int Mmax, const int* range, int N, int K, const P* X, int ldx,
                               const P* W, const P* b, bool residual, P* th, P* Y) {
   if (Mmax <= 0) return;
-  dim3 grid((N + kBN - 1) / kBN, (Mmax + kBM - 1) / kBM);
   EpiForward<P> epi{b, X, ldx, residual, th, Y, N};
   count_launch();
-  k_gemm<P, false, EpiForward<P>><<<grid, 256, 0, st>>>(range, N, K, X, ldx, W, N, epi);
+  if constexpr (std::is_same<P, double>::value) {
+    dim3 grid((N + kDN - 1) / kDN, (Mmax + kDM - 1) / kDM);
+    k_dgemm<false, EpiForward<P>><<<grid, 128, 0, st>>>(range, N, K, X, ldx, W, N, epi);
+  } else {
+    dim3 grid((N + kBN - 1) / kBN, (Mmax + kBM - 1) / kBM);
+    k_gemm<P, false, EpiForward<P>><<<grid, 256, 0, st>>>(range, N, K, X, ldx, W, N, epi);
+  }
 }
 
 template <typename P>
@@ -459,10 +466,15 @@ void launch_fit_backward_layer(cudaStream_t st, int Mmax, const int* range, int 
                                const P* W, const P* dY_next, P* dX, const P* th_prev, P* dZ_prev) {
   if (Mmax <= 0) return;
   // dX[m][n] = sum_k dZ[m][k] W[n][k]   (W is [Nin][Nout] row-major)
-  dim3 grid((Nin + kBN - 1) / kBN, (Mmax + kBM - 1) / kBM);
   EpiBackward<P> epi{dY_next, dX, th_prev, dZ_prev, Nin};
   count_launch();
-  k_gemm<P, true, EpiBackward<P>><<<grid, 256, 0, st>>>(range, Nin, Nout, dZ, Nout, W, Nout, epi);
+  if constexpr (std::is_same<P, double>::value) {
+    dim3 grid((Nin + kDN - 1) / kDN, (Mmax + kDM - 1) / kDM);
+    k_dgemm<true, EpiBackward<P>><<<grid, 128, 0, st>>>(range, Nin, Nout, dZ, Nout, W, Nout, epi);
+  } else {
+    dim3 grid((Nin + kBN - 1) / kBN, (Mmax + kBM - 1) / kBM);
+    k_gemm<P, true, EpiBackward<P>><<<grid, 256, 0, st>>>(range, Nin, Nout, dZ, Nout, W, Nout, epi);
+  }
 }
 
 template <typename P>
