@@ -565,9 +565,11 @@ b200dp_status npt_step(b200dp_dd* dd) {
     if ((rc = b200dp_fold_scale_shifts(dd->engine, st, ratio)) != B200DP_OK) return rc;
   }
   if ((rc = force_call(dd, st)) != B200DP_OK) return rc;
-  // ---- final half
+  // ---- final half, over the atoms owned after the rebuild (migration changes the count)
+  const int n2 = dd->nown;
+  const int grid2 = std::max(1, std::min(kRedBlocks * 4, (n2 + kMdThreads - 1) / kMdThreads));
   count_launch();
-  k_npt_second<<<kRedBlocks, kMdThreads, 0, st>>>(n, dd->v.p, dd->f.p, dd->minv.p, dd->mass.p, dtf, fp * fp,
+  k_npt_second<<<kRedBlocks, kMdThreads, 0, st>>>(n2, dd->v.p, dd->f.p, dd->minv.p, dd->mass.p, dtf, fp * fp,
                                                   dd->part.p);
   count_launch();
   k_dd_sum<<<1, 32, 0, st>>>(dd->part.p, kRedBlocks, dd->ke.p);
@@ -582,7 +584,7 @@ b200dp_status npt_step(b200dp_dd* dd) {
   omega_force(dd->t_current, dd->vir_trace);
   const double s_t2 = dd->tch.thermostat(dd->t_current, dof_boltz, ke_target, kt, dt);
   count_launch();
-  k_md_scale_by<<<grid, kMdThreads, 0, st>>>(n, dd->v.p, s_t2);
+  k_md_scale_by<<<grid2, kMdThreads, 0, st>>>(n2, dd->v.p, s_t2);
   dd->pch.barostat(dd->omega_dot, dd->w_mass, kt, dt);
   return cudaGetLastError() == cudaSuccess ? B200DP_OK : B200DP_ERR_CUDA;
 }

@@ -14,6 +14,7 @@ namespace {
 
 constexpr long long kWaitLimit = 1LL << 26;
 constexpr int kFwdGroups = 2;  // groups of 8 warps per CTA in the forward kernel
+static_assert(kFwdGroups == kItemPad, "the item table's padding is the forward's group count");
 
 // Writes 8 consecutive fp32 values as bf16 hi and lo 16-byte chunks.
 __device__ __forceinline__ void store8_split(unsigned char* hi, unsigned char* lo, const float* v) {
@@ -34,6 +35,20 @@ __device__ __forceinline__ void mma3d(uint32_t d, uint64_t a_hi, uint64_t a_lo, 
     umma::mma(d, a_hi + oa, b_hi + ob, idesc, (accumulate || s > 0) ? 1u : 0u);
     umma::mma(d, a_hi + oa, b_lo + ob, idesc, 1u);
     umma::mma(d, a_lo + oa, b_hi + ob, idesc, 1u);
+  }
+}
+
+// Layer 2 with the hi and lo halves of W2 side by side as one N = 128 operand
+// (they are adjacent in the blob: lo's rows follow hi's at the row-group stride):
+// D[0, 64) += A_hi W_hi + A_lo W_hi, D[64, 128) += A_hi W_lo; the epilogue adds
+// the two halves.  Four MMAs instead of six, and A_hi is read once per K step.
+__device__ __forceinline__ void mma_l2(uint32_t d, uint64_t a_hi, uint64_t a_lo, uint64_t w_hi, uint32_t id128,
+                                       uint32_t id64) {
+#pragma unroll
+  for (int s = 0; s < 2; ++s) {
+    const uint64_t o = (uint64_t)(s * (256 >> 4));
+    umma::mma(d, a_hi + o, w_hi + o, id128, s > 0 ? 1u : 0u);
+    umma::mma(d, a_lo + o, w_hi + o, id64, 1u);
   }
 }
 
@@ -149,15 +164,18 @@ struct NetBlob {
 
 // Shared memory of one group (256 threads): A1 (layer-2 A), X (layer-3 A),
 // then G^T (contraction A, MN-major, 128 positions x 128 edges) over both,
-// and R~ (contraction B, MN-major, 32 columns x 128 edges).
+// and R~ (contraction B, MN-major, 32 columns x 128 edges, bf16 hi and lo side
+// by side as 64 columns).
 struct FwdGroup {
   static constexpr uint32_t A1B = 128 * 32 * 2, XB = 128 * 64 * 2, GB = 128 * 128 * 2, RB = 32 * 128 * 2;
   static constexpr uint32_t O_A1 = 0, O_X = 2 * A1B, O_G = 0, O_R = 2 * GB;
   static constexpr uint32_t BYTES = O_R + 2 * RB;
   static constexpr uint32_t SBO_A1 = (32 / 8) * 128, SBO_X = (64 / 8) * 128;
   static constexpr uint32_t SBO_G = 128, LBO_G = 16 * 128;  // MN-major, 16 position blocks per edge block
-  static constexpr uint32_t SBO_R = 128, LBO_R = 4 * 128;   // MN-major, 4 column blocks per edge block
-  static constexpr uint32_t C_D = 0, C_T = 128, COLS = 256;  // TMEM columns per group
+  // R~ as one MN-major operand of 64 columns: per block of 8 edges, the 4 column
+  // blocks of the hi half, then the 4 of the lo half
+  static constexpr uint32_t SBO_R = 128, LBO_R = 8 * 128;
+  static constexpr uint32_t C_D = 0, C_T = 128, COLS = 256;  // TMEM columns per group (T: 64)
   static constexpr int NG = 2;
   static constexpr uint32_t SMEM = FwdBlob::O_END + NG * BYTES;
 };
@@ -198,9 +216,15 @@ __device__ __forceinline__ void fwd_epi2(const float* f, uint32_t taddr, const f
                                          float (&h2p)[32]) {
   using P = Split<D1, D2, D3>;
   float v[32];
-  umma::ld16(taddr + H * 32, v);
-  umma::ld16(taddr + H * 32 + 16, v + 16);
-  umma::wait_ld();
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {  // the two column halves of the layer-2 accumulator
+    float w[16];
+    umma::ld16(taddr + H * 32 + 16 * c, v + 16 * c);
+    umma::ld16(taddr + 64 + H * 32 + 16 * c, w);
+    umma::wait_ld();
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[16 * c + j] += w[j];
+  }
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
     if (j < P::c2(H)) {
@@ -269,7 +293,7 @@ __global__ void __launch_bounds__(256 * FwdGroup::NG, 1) k_embed_fwd_tc(FwdArgs 
   unsigned char* gh = gbase + S::O_G;
   unsigned char* gl = gh + S::GB;
   unsigned char* rh = gbase + S::O_R;
-  unsigned char* rl = rh + S::RB;
+
   uint64_t* bar = &bars[g];
   if ((gtid >> 5) == 0) umma::tmem_alloc(&tbase, 512);
   if (t == 0) {
@@ -287,7 +311,6 @@ __global__ void __launch_bounds__(256 * FwdGroup::NG, 1) k_embed_fwd_tc(FwdArgs 
   const int nitems = L.istart[L.nnets];
   // descriptors of the fixed operands (later K steps add (bytes >> 4))
   const uint64_t dw2h = umma::desc(umma::smem_u32(smem + B::O_W2), 128, B::SBO_W2);
-  const uint64_t dw2l = umma::desc(umma::smem_u32(smem + B::O_W2 + B::W2B), 128, B::SBO_W2);
   const uint64_t dw3h = umma::desc(umma::smem_u32(smem + B::O_W3), 128, B::SBO_W3);
   const uint64_t dw3l = umma::desc(umma::smem_u32(smem + B::O_W3 + B::W3B), 128, B::SBO_W3);
   const uint64_t da1h = umma::desc(umma::smem_u32(a1h), 128, S::SBO_A1);
@@ -297,10 +320,10 @@ __global__ void __launch_bounds__(256 * FwdGroup::NG, 1) k_embed_fwd_tc(FwdArgs 
   const uint64_t dgh = umma::desc(umma::smem_u32(gh), S::LBO_G, S::SBO_G);
   const uint64_t dgl = umma::desc(umma::smem_u32(gl), S::LBO_G, S::SBO_G);
   const uint64_t drh = umma::desc(umma::smem_u32(rh), S::LBO_R, S::SBO_R);
-  const uint64_t drl = umma::desc(umma::smem_u32(rl), S::LBO_R, S::SBO_R);
   const uint32_t id2 = umma::idesc_bf16(128, 64, false, false);
   const uint32_t id3 = umma::idesc_bf16(128, 128, false, false);
-  const uint32_t idT = umma::idesc_bf16(128, 32, true, true);
+  const uint32_t idT = umma::idesc_bf16(128, 32, true, true), idT64 = umma::idesc_bf16(128, 64, true, true);
+  const uint32_t id2w = umma::idesc_bf16(128, 128, false, false);
   bool aborted = false;
   auto sync_mma = [&]() {
     umma::fence_proxy_async();
@@ -362,12 +385,12 @@ __global__ void __launch_bounds__(256 * FwdGroup::NG, 1) k_embed_fwd_tc(FwdArgs 
           }
           const int nb = 2 * hf + nn;
           const uint32_t o = nb * S::SBO_R + (e >> 3) * S::LBO_R + (e & 7) * 16;
-          store8_split(rh + o, rl + o, v);
+          store8_split(rh + o, rh + o + 4 * S::SBO_R, v);
         }
       }
       sync_mma();
       if (t == 0) {
-        mma3d(tm + S::C_D, da1h, da1l, dw2h, dw2l, id2, 2, 256 >> 4, 256 >> 4, false);
+        mma_l2(tm + S::C_D, da1h, da1l, dw2h, id2w, id2);
         umma::commit(bar);
       }
       if (!wait_mma()) {
@@ -398,7 +421,13 @@ __global__ void __launch_bounds__(256 * FwdGroup::NG, 1) k_embed_fwd_tc(FwdArgs 
         fwd_epi3<D1, D2, D3, 1>(f, tm + lane_base + S::C_D, h2p, gh, gl, e);
       sync_mma();
       if (t == 0) {
-        mma3d(tm + S::C_T, dgh, dgl, drh, drl, idT, (ne + 15) / 16, (2 * S::LBO_G) >> 4, (2 * S::LBO_R) >> 4, !first);
+        // T[:, 0, 32) += G_hi R_hi + G_lo R_hi, T[:, 32, 64) += G_hi R_lo (summed at the store)
+        const int steps = (ne + 15) / 16;
+        for (int s2 = 0; s2 < steps; ++s2) {
+          const uint64_t oa = (uint64_t)(s2 * ((2 * S::LBO_G) >> 4)), ob = (uint64_t)(s2 * ((2 * S::LBO_R) >> 4));
+          umma::mma(tm + S::C_T, dgh + oa, drh + ob, idT64, (!first || s2 > 0) ? 1u : 0u);
+          umma::mma(tm + S::C_T, dgl + oa, drh + ob, idT, 1u);
+        }
         umma::commit(bar);
       }
       first = false;
@@ -413,8 +442,12 @@ __global__ void __launch_bounds__(256 * FwdGroup::NG, 1) k_embed_fwd_tc(FwdArgs 
     const int a_idx = pmap[e];
     float v[16];
     if (I.e1 > I.e0) {
+      float w[16];
       umma::ld16(tm + lane_base + S::C_T + 16 * hf, v);
+      umma::ld16(tm + lane_base + S::C_T + 32 + 16 * hf, w);
       umma::wait_ld();
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] += w[j];
     } else {
 #pragma unroll
       for (int j = 0; j < 16; ++j) v[j] = 0.f;
@@ -510,9 +543,15 @@ __device__ __forceinline__ void bwd_epi2(const float* f, uint32_t taddr, const f
                                          const T2Slots& t2) {
   using P = Split<D1, D2, D3>;
   float v[32];
-  umma::ld16(taddr + H * 32, v);
-  umma::ld16(taddr + H * 32 + 16, v + 16);
-  umma::wait_ld();
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {  // the two column halves of the layer-2 accumulator
+    float w[16];
+    umma::ld16(taddr + H * 32 + 16 * c, v + 16 * c);
+    umma::ld16(taddr + 64 + H * 32 + 16 * c, w);
+    umma::wait_ld();
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[16 * c + j] += w[j];
+  }
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
     if (j < P::c2(H)) {
@@ -654,7 +693,6 @@ __global__ void __launch_bounds__(256 * BwdGroup::NG, 1) k_embed_bwd_tc(BwdArgs 
   const TcLists& L = a.L;
   const int nitems = L.istart[L.nnets];
   const uint64_t dw2h = umma::desc(umma::smem_u32(smem + B::O_W2), 128, B::SBO_W2);
-  const uint64_t dw2l = umma::desc(umma::smem_u32(smem + B::O_W2 + B::W2B), 128, B::SBO_W2);
   const uint64_t dw3h = umma::desc(umma::smem_u32(smem + B::O_W3), 128, B::SBO_W3);
   const uint64_t dw3l = umma::desc(umma::smem_u32(smem + B::O_W3 + B::W3B), 128, B::SBO_W3);
   // the same blobs read MN-major: W3 as B of dh2 (N = layer-2 positions, K = layer-3
@@ -667,6 +705,7 @@ __global__ void __launch_bounds__(256 * BwdGroup::NG, 1) k_embed_bwd_tc(BwdArgs 
   const uint64_t da1l = umma::desc(umma::smem_u32(a1l), 128, S::SBO_A1);
   const uint64_t dxh = umma::desc(umma::smem_u32(xh), 128, S::SBO_X);
   const uint64_t dxl = umma::desc(umma::smem_u32(xl), 128, S::SBO_X);
+  const uint32_t id2w = umma::idesc_bf16(128, 128, false, false);
   const uint32_t id2 = umma::idesc_bf16(128, 64, false, false);
   const uint32_t id3 = umma::idesc_bf16(128, 128, false, false);
   const uint32_t id_h2 = umma::idesc_bf16(128, 64, false, true);
@@ -727,7 +766,7 @@ __global__ void __launch_bounds__(256 * BwdGroup::NG, 1) k_embed_bwd_tc(BwdArgs 
       }
       sync_mma();
       if (t == 0) {
-        mma3d(tm + S::C_D2, da1h, da1l, dw2h, dw2l, id2, 2, 256 >> 4, 256 >> 4, false);
+        mma_l2(tm + S::C_D2, da1h, da1l, dw2h, id2w, id2);  // columns [0, 128): over the idle layer-3 region
         umma::commit(bar);
       }
       if (!wait_mma()) {
@@ -878,7 +917,7 @@ __global__ void __launch_bounds__(256) k_t_combine(TcLists L, int M2, float inv_
                                                     const int* __restrict__ ftile, const float* __restrict__ Tq,
                                                     float* __restrict__ T, float* __restrict__ D,
                                                     unsigned char* __restrict__ Dt_hi,
-                                                    unsigned char* __restrict__ Dt_lo) {
+                                                    unsigned char* __restrict__ Dt_lo, int tiled) {
   __shared__ float sT[kCombRows][4 * D3 + 1];  // odd row stride: the 8 rows of a warp read distinct banks
   __shared__ int s_type[kCombRows];
   const int nrows = L.type_start[L.ntypes];
@@ -909,11 +948,11 @@ __global__ void __launch_bounds__(256) k_t_combine(TcLists L, int M2, float inv_
     for (int k = 0; k < 4; ++k) {
       const float v = acc[k] * inv_nnei;
       sT[rr][k * D3 + c] = v;
-      if (!Dt_hi) T[(size_t)atom * 4 * D3 + k * D3 + c] = v;
+      if (!tiled) T[(size_t)atom * 4 * D3 + k * D3 + c] = v;
     }
   }
   __syncthreads();
-  if (Dt_hi) {
+  if (tiled) {
     // for the tensor-core fitting, T in its 128-row tiles, [tile][k][c][row in tile]: the
     // final fitting backward (one thread per row) then reads it coalesced
     for (int idx = tid; idx < kCombRows * 4 * D3; idx += blockDim.x) {
@@ -925,7 +964,7 @@ __global__ void __launch_bounds__(256) k_t_combine(TcLists L, int M2, float inv_
     }
   }
   const int dim = D3 * M2;
-  for (int idx = tid; idx < kCombRows * (dim / 8); idx += blockDim.x) {
+  for (int idx = tid; (D || Dt_hi) && idx < kCombRows * (dim / 8); idx += blockDim.x) {
     const int rr = idx % kCombRows, g = idx / kCombRows, r = r0 + rr;
     if (r >= nrows) continue;
     const float* st = sT[rr];
@@ -1211,15 +1250,15 @@ void launch_dT(cudaStream_t st, const SeaDev& s, int nloc, const int* type_start
 }
 
 void launch_t_combine(cudaStream_t st, const SeaDev& s, const TcLists& L, const int* perm_atom, const int* ftile,
-                      const float* Tq, float* T, float* D, unsigned char* Dt_hi, unsigned char* Dt_lo) {
+                      const float* Tq, float* T, float* D, unsigned char* Dt_hi, unsigned char* Dt_lo, bool tiled) {
   if (L.nloc <= 0) return;
   count_launch();
   if (which(s) == Inst::W25)
     k_t_combine<100><<<(L.nloc + kCombRows - 1) / kCombRows, 256, 0, st>>>(L, s.M2, (float)s.inv_nnei, perm_atom,
-                                                                            ftile, Tq, T, D, Dt_hi, Dt_lo);
+                                                                            ftile, Tq, T, D, Dt_hi, Dt_lo, tiled);
   else
     k_t_combine<128><<<(L.nloc + kCombRows - 1) / kCombRows, 256, 0, st>>>(L, s.M2, (float)s.inv_nnei, perm_atom,
-                                                                            ftile, Tq, T, D, Dt_hi, Dt_lo);
+                                                                            ftile, Tq, T, D, Dt_hi, Dt_lo, tiled);
 }
 
 }  // namespace b200dp

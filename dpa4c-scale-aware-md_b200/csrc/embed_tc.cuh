@@ -33,6 +33,7 @@ size_t tc_net_bytes(const SeaDev& s);
 void tc_pack_net(const SeaDev& s, const std::vector<HostLayer>& net, std::vector<unsigned char>& out);
 
 constexpr int kItemRows = 8;  // centre rows per work item
+constexpr int kItemPad = 2;   // items per net padded to a multiple of this (the forward's groups per CTA)
 
 struct TcLists {
   int nloc, nnets, ntypes, type_one_side;
@@ -64,10 +65,11 @@ void launch_embed_fwd_tc(cudaStream_t st, const SeaDev& s, const TcLists& L, int
                          float* Tq, int* err);
 // T_i = sum over nets (fixed order) / N -> T, D (row order, fp32) and, when
 // Dt_hi != nullptr, D pre-tiled for the tensor-core fitting (padded rows from
-// ftile).  T is [atom][4][M1] without Dt_hi, and with it [tile][4][M1][128]
-// in the fitting's padded row tiles (what the fused final backward reads).
+// ftile).  T is [atom][4][M1] unless tiled, then [tile][4][M1][128] in the
+// fitting's padded row tiles (what the fused final backward and, when the
+// descriptor is formed inside the layer-0 GEMM, its producers read).
 void launch_t_combine(cudaStream_t st, const SeaDev& s, const TcLists& L, const int* perm_atom, const int* ftile,
-                      const float* Tq, float* T, float* D, unsigned char* Dt_hi, unsigned char* Dt_lo);
+                      const float* Tq, float* T, float* D, unsigned char* Dt_hi, unsigned char* Dt_lo, bool tiled);
 // dE/dT per centre row (scaled by 1/N) from T (atom order) and dE/dD (row order).
 void launch_dT(cudaStream_t st, const SeaDev& s, int nloc, const int* type_start, const int* perm_atom, const float* T,
                const float* dD, float* dT);

@@ -483,7 +483,8 @@ b200dp_status Engine::ensure_buffers(int nloc, int nall, int ncells, int ncand) 
       return e;
     };
     for (int l = 0; l < fplan.L; ++l) {
-      const size_t tb = tiled_bytes(rp, fplan.kpad[l]);
+      // layer 0 forms its operand from T inside the GEMM: no tiled copy of D
+      const size_t tb = l == 0 ? 256 : tiled_bytes(rp, fplan.kpad[l]);
       B200DP_CUDA_TRY(grow_zero(At_hi[l], tb));
       B200DP_CUDA_TRY(grow_zero(At_lo[l], tb));
       B200DP_CUDA_TRY(THf[l].ensure(sizeof(float) * rp * fplan.width[l]));
@@ -601,11 +602,20 @@ b200dp_status Engine::run_model(cudaStream_t st, int nloc, int nall, const int* 
                                 double* d_atom_energy, double* d_atom_virial, double* d_energy, double* d_virial) {
   if (c8) return run_c8<P>(st, nloc, nall, d_atype, d_force, d_atom_energy, d_atom_virial, d_energy, d_virial);
   int* err_d = static_cast<int*>(err_buf.ptr);
-  launch_type_partition(st, nloc, hm.ntypes, d_atype, blk_counts.as<int>(), type_start.as<int>(),
-                        perm_pos.as<int>(), perm_atom.as<int>(), err_d);
-  mark(st, 1);
   const bool f64t = std::is_same<P, double>::value && use_f64t;
-  if ((std::is_same<P, float>::value && use_tc) || f64t) {
+  const bool items = (std::is_same<P, float>::value && use_tc) || f64t;
+  const bool fit_tiles = std::is_same<P, float>::value && use_tc && use_fit_tc;
+  RowTables tabs;  // the item table and the fitting's tile table come with the partition's scan
+  tabs.nnets = sd.nnets;
+  tabs.tos = sd.type_one_side;
+  tabs.item_rows = kItemRows;
+  tabs.item_pad = kItemPad;
+  tabs.istart = items ? tstart.as<int>() : nullptr;
+  tabs.ftile = fit_tiles ? ftile.as<int>() : nullptr;
+  launch_type_partition(st, nloc, hm.ntypes, d_atype, blk_counts.as<int>(), type_start.as<int>(),
+                        perm_pos.as<int>(), perm_atom.as<int>(), err_d, tabs);
+  mark(st, 1);
+  if (items) {
     const int NL = sd.nnets * nloc;
     launch_edge_count(st, sd, nloc, type_start.as<int>(), perm_atom.as<int>(), d_atype, nl_cnt.as<int>(),
                       ecount.as<int>());
@@ -613,7 +623,6 @@ b200dp_status Engine::run_model(cudaStream_t st, int nloc, int nall, const int* 
     launch_edge_compact(st, sd, nloc, type_start.as<int>(), perm_atom.as<int>(), d_atype, nl_cnt.as<int>(),
                         nl_rij.as<double>(), eoff.as<int>(), rec_rt.as<float4>(), rec_row.as<int>(),
                         rec_slot.as<int>());
-    launch_item_table(st, sd, nloc, type_start.as<int>(), tstart.as<int>());
     launch_item_records(st, sd, tc_lists(nloc), reinterpret_cast<int4*>(item_rec.ptr));
   }
   if (f64t) {
@@ -625,17 +634,11 @@ b200dp_status Engine::run_model(cudaStream_t st, int nloc, int nall, const int* 
     const TcLists Lst = tc_lists(nloc);
     launch_embed_fwd_tc(st, sd, Lst, embed_tc_grid(sd, false), tc_nets.as<unsigned char>(), partial.as<float>(),
                         err_d);
-    unsigned char* dth = nullptr;
-    unsigned char* dtl = nullptr;
-    if (use_fit_tc) {
-      launch_fit_tile_table(st, hm.ntypes, type_start.as<int>(), ftile.as<int>());
-      dth = At_hi[0].as<unsigned char>();
-      dtl = At_lo[0].as<unsigned char>();
-    }
-    // fp32 D rows feed the SIMT fitting; the tensor-core fitting reads the tiled copy only
+    // fp32 D rows feed the SIMT fitting; the tensor-core fitting forms D from the
+    // row-tiled T inside its first GEMM (D rows only when they are kept)
     float* Drows = (!use_fit_tc || opt.keep_descriptor) ? reinterpret_cast<float*>(Dbuf.ptr) : nullptr;
     launch_t_combine(st, sd, Lst, perm_atom.as<int>(), ftile.as<int>(), partial.as<float>(),
-                     reinterpret_cast<float*>(Tbuf.ptr), Drows, dth, dtl);
+                     reinterpret_cast<float*>(Tbuf.ptr), Drows, nullptr, nullptr, use_fit_tc);
   } else {
     const int gf = descriptor_grid<P>(sd, ch_fwd, false, nloc);
     launch_descriptor_fwd<P>(st, sd, nloc, ch_fwd, gf, nl_rij.as<double>(), nl_cnt.as<int>(), d_atype,

@@ -12,6 +12,7 @@ namespace b200dp {
 namespace {
 
 constexpr int kMaxStages = 8;
+constexpr uint32_t kTSlice = 8 * 512;  // T of one layer-0 K chunk: 4 components x 2 a values x 128 rows
 constexpr uint32_t kABlock = 128 * kFitBK * 2;  // one half of a 128 x 32 activation block (8 KB)
 constexpr uint32_t kSbo = (kFitBK / 8) * 128;    // K-major SBO inside a block (512 B)
 constexpr long long kWaitLimit = 1LL << 26;
@@ -43,6 +44,10 @@ struct GemmArgs {
   int nk;  // K chunks of 32
   const unsigned char* A_hi;
   const unsigned char* A_lo;
+  // layer 0 with A formed in the kernel: the descriptor D = T^T T_< from T in the
+  // fitting's row tiles ([tile][4][M1][128], already divided by N), axis 16
+  const float* Tt;
+  int M1;
   const unsigned char* B_hi[kMaxTypes];
   const unsigned char* B_lo[kMaxTypes];
   int BN, N;
@@ -85,7 +90,7 @@ constexpr int kFitThreads = kFitEpiThreads + 64;
 
 __global__ void __launch_bounds__(kFitThreads, 2) k_fit_gemm(GemmArgs a) {
   extern __shared__ __align__(1024) unsigned char smem[];
-  __shared__ uint64_t full[kMaxStages], empty[kMaxStages], done;
+  __shared__ uint64_t full[kMaxStages], empty[kMaxStages], tfull[kMaxStages], done;
   __shared__ uint32_t tbase;
   __shared__ int s_ok;
   __shared__ double s_e[kFitEpiThreads / 128][128];
@@ -97,13 +102,16 @@ __global__ void __launch_bounds__(kFitThreads, 2) k_fit_gemm(GemmArgs a) {
   const int row0 = a.type_start[t] + 128 * (g - a.ftile[t]);
   const int nrows = min(128, a.type_start[t + 1] - row0);
   const uint32_t BB = (uint32_t)a.BN * kFitBK * 2;
-  const uint32_t SB = 2 * kABlock + 2 * BB;
+  // a stage: A (hi, lo), B (hi, lo) and, when A is formed here, the chunk's slice of T
+  const uint32_t SB = 2 * kABlock + 2 * BB + (a.Tt ? kTSlice : 0u);
   if (warp == 0) umma::tmem_alloc(&tbase, 256);
   const int S = a.stages;
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
-      umma::mbar_init(&full[s], 1);
+      // the loader's arrival (with the bulk bytes), plus every epilogue thread's when it forms A
+      umma::mbar_init(&full[s], a.Tt ? 1 + kFitEpiThreads : 1);
       umma::mbar_init(&empty[s], 1);
+      umma::mbar_init(&tfull[s], 1);
     }
     umma::mbar_init(&done, 1);
     umma::fence_mbar_init();
@@ -125,9 +133,19 @@ __global__ void __launch_bounds__(kFitThreads, 2) k_fit_gemm(GemmArgs a) {
         break;
       }
       unsigned char* st = smem + s * SB;
-      umma::mbar_expect_tx(&full[s], SB);
-      umma::bulk_g2s(st, Ah + (size_t)kc * kABlock, kABlock, &full[s]);
-      umma::bulk_g2s(st + kABlock, Al + (size_t)kc * kABlock, kABlock, &full[s]);
+      if (a.Tt) {  // T[tile][k][a][128 rows] for the chunk's two a values: 8 rows of 512 bytes
+        umma::mbar_expect_tx(&tfull[s], kTSlice);
+        const float* tsrc = a.Tt + (size_t)g * 4 * a.M1 * 128;
+        for (int k = 0; k < 4; ++k)
+          for (int q = 0; q < 2; ++q)
+            umma::bulk_g2s(st + 2 * kABlock + 2 * BB + (2 * k + q) * 512,
+                           tsrc + ((size_t)k * a.M1 + 2 * kc + q) * 128, 512, &tfull[s]);
+      }
+      umma::mbar_expect_tx(&full[s], a.Tt ? 2 * BB : SB);
+      if (!a.Tt) {
+        umma::bulk_g2s(st, Ah + (size_t)kc * kABlock, kABlock, &full[s]);
+        umma::bulk_g2s(st + kABlock, Al + (size_t)kc * kABlock, kABlock, &full[s]);
+      }
       umma::bulk_g2s(st + 2 * kABlock, Bh + (size_t)kc * BB, BB, &full[s]);
       umma::bulk_g2s(st + 2 * kABlock + BB, Bl + (size_t)kc * BB, BB, &full[s]);
       if (++s == S) {
@@ -161,6 +179,50 @@ __global__ void __launch_bounds__(kFitThreads, 2) k_fit_gemm(GemmArgs a) {
     }
     umma::commit(&done);
     if (!ok) s_ok = 0;
+  }
+  if (a.Tt && warp < kFitEpiThreads / 32) {
+    // producers of A: row r, descriptor columns a*16 + b of the chunk's two a
+    // values, b in [8 h, 8 h + 8): D[r][a][b] = sum_k T[r][k][a] T[r][k][b],
+    // written as bf16 hi / lo into the stage's A block (zero rows past the tile)
+    const int r = tid & 127, h = tid >> 7;
+    const bool rv = r < nrows;
+    const float* Tg = a.Tt + (size_t)g * 4 * a.M1 * 128 + r;  // element (k, c) at Tg[(k M1 + c) 128]
+    float tb[4][8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) tb[k][j] = rv ? Tg[((size_t)k * a.M1 + 8 * h + j) * 128] : 0.f;
+    const uint32_t o0 = (uint32_t)(r >> 3) * kSbo + (uint32_t)h * 128 + (uint32_t)(r & 7) * 16;
+    const uint32_t o1 = o0 + 2 * 128;
+    int s = 0, round = 0;
+    for (int kc = 0; kc < a.nk; ++kc) {
+      // the stage is free once its slice of T has landed (the loader waited for it)
+      if (!umma::mbar_wait(&tfull[s], round & 1, kWaitLimit)) {
+        s_ok = 0;
+        break;
+      }
+      unsigned char* st = smem + s * SB;
+      const float* ts = reinterpret_cast<const float*>(st + 2 * kABlock + 2 * BB) + r;
+      float ta[4][2];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+#pragma unroll
+        for (int q = 0; q < 2; ++q) ta[k][q] = rv ? ts[(2 * k + q) * 128] : 0.f;
+      float v[2][8];
+#pragma unroll
+      for (int q = 0; q < 2; ++q)
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          v[q][j] = ta[0][q] * tb[0][j] + ta[1][q] * tb[1][j] + ta[2][q] * tb[2][j] + ta[3][q] * tb[3][j];
+      store8_split(st + o0, st + kABlock + o0, v[0]);
+      store8_split(st + o1, st + kABlock + o1, v[1]);
+      umma::fence_proxy_async();
+      umma::mbar_arrive(&full[s]);
+      if (++s == S) {
+        s = 0;
+        ++round;
+      }
+    }
   }
   const bool ok = umma::mbar_wait(&done, 0, kWaitLimit);
   const int q = warp & 3, part = warp >> 2;  // lane quadrant, column part
@@ -882,7 +944,9 @@ FitTcPlan fit_tc_plan(const HostModel& m) {
     din = w;
   }
   for (int l = 0; l < p.L; ++l) {
-    p.bnf[l] = (l == p.L - 1) ? p.width[l] : split_bn(p.width[l]);
+    // layer 0 forms its operand (the descriptor) from T inside the GEMM: one CTA per
+    // row tile takes the whole width, so that the operand is formed once
+    p.bnf[l] = (l == p.L - 1 || l == 0) ? p.width[l] : split_bn(p.width[l]);
     p.bnb[l] = (l == 0) ? 0 : split_bn(p.width[l - 1]);
   }
   // final backward: N chunks of whole descriptor rows (16 columns each), an
@@ -961,8 +1025,9 @@ void launch_fit_tile_D(cudaStream_t st, int nloc, int ntypes, int dim, const int
 static void run_gemm(cudaStream_t st, GemmArgs& a, int row_tiles, int ntn) {
   // K chunks stream from L2: a deep pipeline hides its latency.  With several
   // N tiles two CTAs share an SM (4 stages each), else one CTA takes up to 8.
-  const size_t sb = 2 * kABlock + 2 * (size_t)a.BN * kFitBK * 2;
-  a.stages = ntn > 1 ? 4 : (int)std::min<size_t>(kMaxStages, (200 * 1024) / sb);
+  const size_t sb = 2 * kABlock + 2 * (size_t)a.BN * kFitBK * 2 + (a.Tt ? kTSlice : 0);
+  // (with the slice of T a stage is 4 KB larger: three stages keep two CTAs on an SM)
+  a.stages = ntn > 1 ? (a.Tt ? 3 : 4) : (int)std::min<size_t>(kMaxStages, (200 * 1024) / sb);
   a.stages = std::max(2, std::min(a.stages, a.nk));
   const size_t smem = (size_t)a.stages * sb;
   static bool attr = false;
@@ -990,6 +1055,10 @@ void launch_fit_tc(cudaStream_t st, const FitTcPlan& p, int ntypes, int nloc, co
     a.nk = p.kpad[l] / kFitBK;
     a.A_hi = b.At_hi[l];
     a.A_lo = b.At_lo[l];
+    if (l == 0) {  // the descriptor is formed from T inside the GEMM (no tiled copy of D)
+      a.Tt = T;
+      a.M1 = p.dim / 16;
+    }
     for (int t = 0; t < ntypes; ++t) {
       a.B_hi[t] = w[t].fB_hi[l];
       a.B_lo[t] = w[t].fB_lo[l];

@@ -1070,19 +1070,50 @@ __global__ void __launch_bounds__(kPartBlock) k_type_count(int nloc, int ntypes,
   if (threadIdx.x < ntypes) blk_counts[blockIdx.x * ntypes + threadIdx.x] = cnt[threadIdx.x];
 }
 
-__global__ void k_type_scan(int nblk, int ntypes, int* __restrict__ blk_counts, int* __restrict__ type_start) {
-  // one thread; nblk is small (nloc / 1024)
-  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+// One warp: per type, the blocks' counts in chunks of 32 by a warp scan (each
+// count becomes its block's base), then type_start and the row tables.
+__global__ void k_type_scan(int nblk, int ntypes, int* __restrict__ blk_counts, int* __restrict__ type_start,
+                            RowTables tab) {
+  if (blockIdx.x != 0) return;
+  const int lane = threadIdx.x & 31;
   int base = 0;
   for (int t = 0; t < ntypes; ++t) {
-    type_start[t] = base;
-    for (int b = 0; b < nblk; ++b) {
-      const int c = blk_counts[b * ntypes + t];
-      blk_counts[b * ntypes + t] = base;
-      base += c;
+    if (lane == 0) type_start[t] = base;
+    for (int b0 = 0; b0 < nblk; b0 += 32) {
+      const int b = b0 + lane;
+      const int c = b < nblk ? blk_counts[b * ntypes + t] : 0;
+      int incl = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+      }
+      if (b < nblk) blk_counts[b * ntypes + t] = base + incl - c;
+      base += __shfl_sync(0xffffffffu, incl, 31);
     }
   }
+  if (lane != 0) return;
   type_start[ntypes] = base;
+  __threadfence_block();
+  if (tab.istart) {
+    int acc = 0;
+    tab.istart[0] = 0;
+    for (int q = 0; q < tab.nnets; ++q) {
+      const int ti = q / ntypes;
+      const int rows = tab.tos ? base : type_start[ti + 1] - type_start[ti];
+      const int items = (rows + tab.item_rows - 1) / tab.item_rows;
+      acc += (items + tab.item_pad - 1) / tab.item_pad * tab.item_pad;
+      tab.istart[q + 1] = acc;
+    }
+  }
+  if (tab.ftile) {
+    int acc = 0;
+    tab.ftile[0] = 0;
+    for (int t = 0; t < ntypes; ++t) {
+      acc += (type_start[t + 1] - type_start[t] + 127) / 128;
+      tab.ftile[t + 1] = acc;
+    }
+  }
 }
 
 __global__ void __launch_bounds__(kPartBlock) k_type_place(int nloc, int ntypes, const int* __restrict__ atype,
@@ -1121,16 +1152,18 @@ __global__ void __launch_bounds__(kPartBlock) k_type_place(int nloc, int ntypes,
 }
 
 void launch_type_partition(cudaStream_t st, int nloc, int ntypes, const int* atype, int* blk_counts,
-                           int* type_start, int* perm_pos, int* perm_atom, int* err) {
+                           int* type_start, int* perm_pos, int* perm_atom, int* err, const RowTables& tables) {
   const int nblk = (int)type_partition_blocks(nloc);
   if (nblk == 0) {
     cudaMemsetAsync(type_start, 0, sizeof(int) * (ntypes + 1), st);
+    if (tables.istart) cudaMemsetAsync(tables.istart, 0, sizeof(int) * (tables.nnets + 1), st);
+    if (tables.ftile) cudaMemsetAsync(tables.ftile, 0, sizeof(int) * (ntypes + 1), st);
     return;
   }
   count_launch();
   k_type_count<<<nblk, kPartBlock, 0, st>>>(nloc, ntypes, atype, blk_counts, err);
   count_launch();
-  k_type_scan<<<1, 32, 0, st>>>(nblk, ntypes, blk_counts, type_start);
+  k_type_scan<<<1, 32, 0, st>>>(nblk, ntypes, blk_counts, type_start, tables);
   count_launch();
   k_type_place<<<nblk, kPartBlock, 0, st>>>(nloc, ntypes, atype, blk_counts, perm_pos, perm_atom);
 }

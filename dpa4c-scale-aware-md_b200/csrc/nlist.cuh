@@ -129,8 +129,20 @@ void launch_format_graph(cudaStream_t st, const FormatSpec& f, const int64_t* at
 void launch_format_candidates(cudaStream_t st, const FormatSpec& f, const double* coord, const int* atype,
                               const int* ilist, const int* cand_start, const int* cand, int* nl_j, int* nl_code,
                               double* nl_rij, int* nl_cnt, int* err);
+// Tables over the type-grouped rows that later kernels need, filled by the
+// partition's scan (no launches of their own): istart[nnets + 1], the first
+// work item of each embedding net (a net's rows are all rows, or its centre
+// type's rows when tos == 0; ceil(rows / item_rows) items padded to a multiple
+// of item_pad), and ftile[ntypes + 1], the first 128-row fitting tile of each
+// type.  Either pointer may be null.
+struct RowTables {
+  int nnets = 0, tos = 1, item_rows = 8, item_pad = 1;
+  int* istart = nullptr;
+  int* ftile = nullptr;
+};
 void launch_type_partition(cudaStream_t st, int nloc, int ntypes, const int* atype, int* blk_counts,
-                           int* type_start, int* perm_pos, int* perm_atom, int* err);
+                           int* type_start, int* perm_pos, int* perm_atom, int* err,
+                           const RowTables& tables = RowTables{});
 size_t type_partition_blocks(int nloc);
 
 }  // namespace b200dp

@@ -574,24 +574,20 @@ struct FoldTargets {
 // dE/dr_ij from the environment-row gradient g4 = dE/dR~ (R~ = (sw/r, sw x/r^2,
 // sw y/r^2, sw z/r^2)) by the chain rule through R~(r), in fp64.
 __device__ __forceinline__ void env_chain(const double* g4, const double* r3, double rc, double rs, double* g3) {
+  // with u = r / |r| and g = (g4[1], g4[2], g4[3]):
+  //   d(sw/r)/dr_c = (dsw/r - sw/r^2) u_c,
+  //   sum_a g_a d(sw r_a/r^2)/dr_c = r_c (g.r)(dsw/r^3 - 2 sw/r^4) + (sw/r^2) g_c
   const double x = r3[0], y = r3[1], zc = r3[2];
   const double r2 = x * x + y * y + zc * zc, rr = sqrt(r2);
   double sw, dsw;
   smooth_switch(rr, rs, rc, sw, dsw);
   const double ir = 1.0 / rr, ir2 = ir * ir;
-  const double d0 = dsw * ir - sw * ir2;
-  const double rvec[3] = {x, y, zc};
-#pragma unroll
-  for (int cc = 0; cc < 3; ++cc) {
-    double acc = g4[0] * d0 * rvec[cc] * ir;
-#pragma unroll
-    for (int aa = 0; aa < 3; ++aa) {
-      const double J = dsw * rvec[cc] * ir * rvec[aa] * ir2 +
-                       sw * ((aa == cc ? ir2 : 0.0) - 2.0 * rvec[aa] * rvec[cc] * ir2 * ir2);
-      acc += g4[1 + aa] * J;
-    }
-    g3[cc] = acc;
-  }
+  const double gr = g4[1] * x + g4[2] * y + g4[3] * zc;
+  const double a = g4[0] * (dsw * ir - sw * ir2) * ir + gr * ir2 * (dsw * ir - 2.0 * sw * ir2);
+  const double b = sw * ir2;
+  g3[0] = a * x + b * g4[1];
+  g3[1] = a * y + b * g4[2];
+  g3[2] = a * zc + b * g4[3];
 }
 
 // One warp per centre over its slots.  gsrc holds per slot either dE/dr_ij
