@@ -112,7 +112,14 @@ int b200dp_engine_device(const b200dp_engine* engine);
  * atoms so the caller can fold ghost forces back (reverse communication).
  * coord [nall*3], atype [nall], box [9] (rows are cell vectors; may be NULL
  * when nghost > 0).  force [nall*3], virial [9], atom_energy [nlocal] and
- * atom_virial [nall*9] (both optional, may be NULL). */
+ * atom_virial [nall*9] (both optional, may be NULL).
+ * A periodic call (nghost == 0, a box) on page-locked host buffers, without
+ * neighbour reuse or stage timing, whose atom count, buffer addresses and box
+ * repeat the previous call's is recorded once (at its second occurrence) and
+ * then replayed as one CUDA graph: the copies in, the evaluation and the copies
+ * out, with the buffers' current contents.  Any other call (pageable buffers,
+ * ghosts, a new shape or box) runs directly and drops the recording.  Results
+ * are the same either way. */
 b200dp_status b200dp_compute_host(b200dp_engine* engine, int nlocal, int nghost, const double* coord,
                                   const int* atype, const double* box, double* energy, double* force,
                                   double* virial, double* atom_energy, double* atom_virial);
