@@ -370,30 +370,29 @@ struct BwdSmem {
 };
 
 // gxT[m][e] = sum_n gzT[n][e] W[m][n] (the transposed product of a layer with
-// weights W[DIN][DOUT]); thread tiles of 4 edges x TM inputs m (TM < 4 for the
-// narrow layers, so that the block's threads have work).
-template <int DIN, int DOUT, int TM>
-__device__ __forceinline__ void dense_bwd_tile(const double* gzT, const double* W, int it, double (&acc)[4][TM],
+// weights W[DIN][DOUT]); thread tiles of 4 edges x 4 inputs m.
+template <int DIN, int DOUT>
+__device__ __forceinline__ void dense_bwd_tile(const double* gzT, const double* W, int it, double (&acc)[4][4],
                                                int& e0, int& m0) {
   constexpr int EG = kE / 4;
   e0 = (it % EG) * 4;
-  m0 = (it / EG) * TM;
+  m0 = (it / EG) * 4;
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
-    for (int j = 0; j < TM; ++j) acc[i][j] = 0.0;
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.0;
 #pragma unroll 4
   for (int n = 0; n < DOUT; ++n) {
     const double2 za = *reinterpret_cast<const double2*>(gzT + n * kE + e0);
     const double2 zb = *reinterpret_cast<const double2*>(gzT + n * kE + e0 + 2);
     const double z[4] = {za.x, za.y, zb.x, zb.y};
-    double w[TM];
+    double w[4];
 #pragma unroll
-    for (int j = 0; j < TM; ++j) w[j] = m0 + j < DIN ? W[(m0 + j) * DOUT + n] : 0.0;
+    for (int j = 0; j < 4; ++j) w[j] = m0 + j < DIN ? W[(m0 + j) * DOUT + n] : 0.0;
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
-      for (int j = 0; j < TM; ++j) acc[i][j] = fma(z[i], w[j], acc[i][j]);
+      for (int j = 0; j < 4; ++j) acc[i][j] = fma(z[i], w[j], acc[i][j]);
   }
 }
 
@@ -472,13 +471,12 @@ __global__ void __launch_bounds__(kT, 2) k_embed_bwd_f64(TcLists L, SeaDev s, co
       }
       __syncthreads();
       // dh2 = dz3 W3^T + residual of layer 3; dz2 = dh2 (1 - t2^2)
-      constexpr int TM2 = 2, TM1 = 1;  // 200 / 200 thread tiles at the water model's widths
-      for (int it2 = tid; it2 < (kE / 4) * ((D2 + TM2 - 1) / TM2); it2 += kT) {
-        double acc[4][TM2];
+      for (int it2 = tid; it2 < (kE / 4) * ((D2 + 3) / 4); it2 += kT) {
+        double acc[4][4];
         int e0, m0;
-        dense_bwd_tile<D2, D3, TM2>(GT, net + N::W3, it2, acc, e0, m0);
+        dense_bwd_tile<D2, D3>(GT, net + N::W3, it2, acc, e0, m0);
 #pragma unroll
-        for (int j = 0; j < TM2; ++j) {
+        for (int j = 0; j < 4; ++j) {
           const int m = m0 + j;
           if (m >= D2) break;
 #pragma unroll
@@ -502,12 +500,12 @@ __global__ void __launch_bounds__(kT, 2) k_embed_bwd_f64(TcLists L, SeaDev s, co
         pr[3] = q3;
       }
       // dh1 = dz2 W2^T + residual of layer 2; dz1 = dh1 (1 - t1^2) over t1
-      for (int it2 = tid; it2 < (kE / 4) * ((D1 + TM1 - 1) / TM1); it2 += kT) {
-        double acc[4][TM1];
+      for (int it2 = tid; it2 < (kE / 4) * ((D1 + 3) / 4); it2 += kT) {
+        double acc[4][4];
         int e0, m0;
-        dense_bwd_tile<D1, D2, TM1>(Z2T, net + N::W2, it2, acc, e0, m0);
+        dense_bwd_tile<D1, D2>(Z2T, net + N::W2, it2, acc, e0, m0);
 #pragma unroll
-        for (int j = 0; j < TM1; ++j) {
+        for (int j = 0; j < 4; ++j) {
           const int m = m0 + j;
           if (m >= D1) break;
 #pragma unroll
