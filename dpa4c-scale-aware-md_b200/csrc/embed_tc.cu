@@ -1049,27 +1049,6 @@ __global__ void k_item_records(TcLists L, int cap, int4* __restrict__ items) {
   }
 }
 
-// Items per net are padded to a multiple of kFwdGroups so that a round of
-// the grouped forward kernel never mixes nets (padded items are empty).
-__global__ void k_item_table(int nnets, int ntypes, int tos, const int* __restrict__ type_start,
-                             int* __restrict__ istart) {
-  if (threadIdx.x != 0 || blockIdx.x != 0) return;
-  int acc = 0;
-  istart[0] = 0;
-  for (int q = 0; q < nnets; ++q) {
-    int rows;
-    if (tos) {
-      rows = type_start[ntypes];
-    } else {
-      const int ti = q / ntypes;
-      rows = type_start[ti + 1] - type_start[ti];
-    }
-    const int items = (rows + kItemRows - 1) / kItemRows;
-    acc += (items + kFwdGroups - 1) / kFwdGroups * kFwdGroups;
-    istart[q + 1] = acc;
-  }
-}
-
 template <int D1, int D2, int D3>
 void pack_net(const std::vector<HostLayer>& net, std::vector<unsigned char>& out) {
   out.assign(NetBlob<D1, D2, D3>::BYTES, 0);
@@ -1210,12 +1189,6 @@ void launch_item_records(cudaStream_t st, const SeaDev& s, const TcLists& L, int
   const int cap = tc_item_capacity(s, L.nloc);
   count_launch();
   k_item_records<<<std::max(1, std::min(148 * 4, (cap + 255) / 256)), 256, 0, st>>>(L, cap, items);
-}
-
-void launch_item_table(cudaStream_t st, const SeaDev& s, int nloc, const int* type_start, int* istart) {
-  (void)nloc;
-  count_launch();
-  k_item_table<<<1, 32, 0, st>>>(s.nnets, s.ntypes, s.type_one_side, type_start, istart);
 }
 
 int embed_tc_grid(const SeaDev&, bool backward) {

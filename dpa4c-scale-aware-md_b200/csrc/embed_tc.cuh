@@ -57,7 +57,6 @@ void launch_edge_count(cudaStream_t st, const SeaDev& s, int nloc, const int* ty
 void launch_edge_compact(cudaStream_t st, const SeaDev& s, int nloc, const int* type_start, const int* perm_atom,
                          const int* atype, const int* cnt, const double* rij, const int* eoff, float4* rt, int* row,
                          int* slot);
-void launch_item_table(cudaStream_t st, const SeaDev& s, int nloc, const int* type_start, int* istart);
 // Grid for the persistent kernels (CTAs per SM times SMs).
 int embed_tc_grid(const SeaDev& s, bool backward);
 // Forward: Tq[net][row][4][M1] = sum over the net's edges of the row of R~ (x) G.

@@ -888,35 +888,6 @@ __global__ void __launch_bounds__(kDtThreads, 1) k_fit_dT(DtArgs a) {
   for (int b = 0; b < 16; ++b) dTk[b] = __ldcg(dTk + b) + sum[b] * a.inv_nnei;
 }
 
-__global__ void k_fit_tile_table(int ntypes, const int* __restrict__ type_start, int* __restrict__ ftile) {
-  if (threadIdx.x != 0 || blockIdx.x != 0) return;
-  int acc = 0;
-  ftile[0] = 0;
-  for (int t = 0; t < ntypes; ++t) {
-    acc += (type_start[t + 1] - type_start[t] + 127) / 128;
-    ftile[t + 1] = acc;
-  }
-}
-
-// One thread per (row, 8-column group) of D.
-__global__ void k_fit_tile_D(int nloc, int ntypes, int dim, const int* __restrict__ type_start,
-                             const int* __restrict__ ftile, const float* __restrict__ D, unsigned char* __restrict__ hi,
-                             unsigned char* __restrict__ lo) {
-  const int groups = dim / 8;
-  const size_t total = (size_t)type_start[ntypes] * groups;
-  for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total; idx += (size_t)gridDim.x * blockDim.x) {
-    const int r = (int)(idx / groups), kg = (int)(idx % groups);
-    int t = 0;
-    while (t + 1 < ntypes && type_start[t + 1] <= r) ++t;
-    const int prow = 128 * ftile[t] + (r - type_start[t]);
-    const float4* src = reinterpret_cast<const float4*>(D + (size_t)r * dim + kg * 8);
-    const float4 x0 = src[0], x1 = src[1];
-    const float v[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-    const size_t o = tiled_off(prow, kg * 8, dim);
-    store8_split(hi + o, lo + o, v);
-  }
-}
-
 int round32(int x) { return (x + 31) / 32 * 32; }
 
 // Largest N tile that is a multiple of 16, at most 128 and divides w into at
@@ -1006,20 +977,6 @@ void fit_pack_B(int N, int Kp, int BN, const std::function<double(int, int)>& va
       std::memcpy(&hi[o], &h, 2);
       std::memcpy(&lo[o], &l, 2);
     }
-}
-
-void launch_fit_tile_table(cudaStream_t st, int ntypes, const int* type_start, int* ftile) {
-  count_launch();
-  k_fit_tile_table<<<1, 32, 0, st>>>(ntypes, type_start, ftile);
-}
-
-void launch_fit_tile_D(cudaStream_t st, int nloc, int ntypes, int dim, const int* type_start, const int* ftile,
-                       const float* D, unsigned char* hi, unsigned char* lo) {
-  if (nloc <= 0) return;
-  const size_t total = (size_t)nloc * (dim / 8);
-  const int blocks = (int)std::min<size_t>((total + 255) / 256, 148 * 16);
-  count_launch();
-  k_fit_tile_D<<<blocks, 256, 0, st>>>(nloc, ntypes, dim, type_start, ftile, D, hi, lo);
 }
 
 static void run_gemm(cudaStream_t st, GemmArgs& a, int row_tiles, int ntn) {

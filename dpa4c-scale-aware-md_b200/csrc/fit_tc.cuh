@@ -75,11 +75,6 @@ struct FitTcBuffers {
 };
 constexpr int kDtSplitSlots = 148;  // split CTAs of one launch: row tiles x splits <= this
 
-// First row tile of each type (exclusive prefix of ceil(n_t/128)); [ntypes+1].
-void launch_fit_tile_table(cudaStream_t st, int ntypes, const int* type_start, int* ftile);
-// Writes D (fp32 rows in type-grouped order) into the tiled layer-0 input.
-void launch_fit_tile_D(cudaStream_t st, int nloc, int ntypes, int dim, const int* type_start, const int* ftile,
-                       const float* D, unsigned char* hi, unsigned char* lo);
 // Whole fitting forward + backward; energies to atom_energy (atom order) and
 // dE/dT (rows in type-grouped order, [row][4][M1], through D = T^T T_< with T
 // already divided by N and laid out in the fitting's 128-row tiles,
