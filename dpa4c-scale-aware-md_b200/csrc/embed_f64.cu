@@ -4,13 +4,14 @@
 
 #include "common.cuh"
 #include "embed_f64.cuh"
+#include "simt_gemm.cuh"
 
 namespace b200dp {
 
 namespace {
 
-constexpr int kE = kF64Edges;  // edges per subtile
-constexpr int kT = kF64Threads;
+constexpr int kW = kF64Warps;
+constexpr int kCh = 8;  // edges per chunk: the M (or N) extent of one m8n8k4 product
 
 constexpr int resid(int din, int dout) { return dout == din ? 1 : (dout == 2 * din ? 2 : 0); }
 // input feature feeding the residual of output n (DeePMD's identity / concat rule)
@@ -56,28 +57,6 @@ __device__ __forceinline__ double tanh_d(double x) {
   return isnan(x) ? x : copysign(t, x);
 }
 
-// One net in shared memory (the layout of the SIMT weights: W[k][n] row-major, then b).
-template <int D1, int D2, int D3>
-struct F64Net {
-  static constexpr int W1 = 0, B1 = D1, W2 = 2 * D1, B2 = W2 + D1 * D2, W3 = B2 + D2, B3 = W3 + D2 * D3;
-  static constexpr int N = (B3 + D3 + 1) / 2 * 2;  // doubles, even (16-byte aligned regions after it)
-};
-
-__device__ __forceinline__ void load_net(double* dst, const double* __restrict__ emb, const SeaDev& s, int q,
-                                         int d1, int d2, int d3) {
-  const double* src = emb + (size_t)q * s.net_stride;
-  // the SIMT layout: layer l weights at w_off[l] ([din][dout]), biases at b_off[l]
-  const int W1 = 0, B1 = d1, W2 = 2 * d1, B2 = W2 + d1 * d2, W3 = B2 + d2, B3 = W3 + d2 * d3;
-  for (int i = threadIdx.x; i < d1; i += blockDim.x) {
-    dst[W1 + i] = src[s.w_off[0] + i];
-    dst[B1 + i] = src[s.b_off[0] + i];
-  }
-  for (int i = threadIdx.x; i < d1 * d2; i += blockDim.x) dst[W2 + i] = src[s.w_off[1] + i];
-  for (int i = threadIdx.x; i < d2; i += blockDim.x) dst[B2 + i] = src[s.b_off[1] + i];
-  for (int i = threadIdx.x; i < d2 * d3; i += blockDim.x) dst[W3 + i] = src[s.w_off[2] + i];
-  for (int i = threadIdx.x; i < d3; i += blockDim.x) dst[B3 + i] = src[s.b_off[2] + i];
-}
-
 // Environment row R~ = (sw/r, sw x/r^2, sw y/r^2, sw z/r^2) of one edge.
 __device__ __forceinline__ void env_row64(const double* r, double rc, double rs, double* rt) {
   const double r2 = r[0] * r[0] + r[1] * r[1] + r[2] * r[2];
@@ -90,94 +69,165 @@ __device__ __forceinline__ void env_row64(const double* r, double rc, double rs,
   for (int c = 0; c < 3; ++c) rt[1 + c] = sw * r[c] * inv_r2;
 }
 
-// Item record {net, first row, end row, first edge}, {end edge}.
-struct F64Item {
-  int q, rb, re, e0, e1;
+// Padded extents of one net and its layout in shared memory (doubles): layer-1
+// weights and biases, then W2, b2, W3, b3, every weight matrix in the swizzled
+// 8 x 8 block layout of swz().
+template <int D1, int D2, int D3>
+struct Dims {
+  static constexpr int K1 = (D1 + 7) / 8 * 8, F2 = (D2 + 7) / 8 * 8, P3 = (D3 + 7) / 8 * 8;
+  static constexpr int NK = K1 / 8, NF = F2 / 8, NP = P3 / 8;
+  static constexpr int W1 = 0, B1 = K1, W2 = 2 * K1, B2 = W2 + K1 * F2, W3 = B2 + F2, B3 = W3 + F2 * P3;
+  static constexpr int NET = (B3 + P3 + 1) / 2 * 2;
 };
-__device__ __forceinline__ F64Item item_at(const TcLists& L, int it) {
-  const int4 a = L.items[2 * it], b = L.items[2 * it + 1];
-  return F64Item{a.x, a.y, a.z, a.w, b.x};
+
+// W[r][c] (r the layer input, c its output, both padded to multiples of 8) in
+// 8 x 8 blocks, row-block major; inside a block, row ri starts at
+// 16 ((ri & 1) + 2 (ri >> 2)) and is rotated by (ri & 1) + 8 ((ri >> 1) & 1) + 4 (ri >> 2)
+// within its 16 doubles.  The two fragment patterns of the products,
+//   A: r = 8i + 2 (lane & 3) + s, c = 8j + (lane >> 2)   (the input index is K)
+//   B: r = 8i + (lane >> 2), c = 8j + 2 (lane & 3) + s   (the output index is K)
+// then touch 16 distinct 8-byte bank pairs in each half warp, so one copy of the
+// weights serves the forward products and the transposed backward products.
+__host__ __device__ constexpr int swz_rot(int ri) { return (ri & 1) + 8 * ((ri >> 1) & 1) + 4 * (ri >> 2); }
+__host__ __device__ constexpr int swz_row(int ri) { return 16 * ((ri & 1) + 2 * (ri >> 2)); }
+__device__ __forceinline__ int swz(int r, int c, int nc8) {
+  const int ri = r & 7, ci = c & 7;
+  return 64 * ((r >> 3) * nc8 + (c >> 3)) + swz_row(ri) + ((ci + swz_rot(ri)) & 15);
 }
 
-// Subtile inputs: slot, centre row (relative to the item) and environment row
-// of each edge; edges past ne get a zero row.
-__device__ __forceinline__ void stage_edges(const TcLists& L, const double* __restrict__ rij, const SeaDev& s,
-                                            int sub, int ne, int rb, double* rtS, int* rowS, int* slotS) {
-  for (int e = threadIdx.x; e < kE; e += blockDim.x) {
-    double rt[4] = {0.0, 0.0, 0.0, 0.0};
-    int row = 0, slot = -1;
-    if (e < ne) {
-      slot = L.slot[sub + e];
-      row = L.row[sub + e] - rb;
+// The net of pair q from the SIMT layout (W[k][n] row-major [din][dout] at
+// w_off[l], biases at b_off[l]), zero-padded.
+template <int D1, int D2, int D3>
+__device__ void load_net_sw(double* net, const double* __restrict__ emb, const SeaDev& s, int q) {
+  using Dm = Dims<D1, D2, D3>;
+  const double* src = emb + (size_t)q * s.net_stride;
+  for (int i = threadIdx.x; i < Dm::K1; i += blockDim.x) {
+    net[Dm::W1 + i] = i < D1 ? src[s.w_off[0] + i] : 0.0;
+    net[Dm::B1 + i] = i < D1 ? src[s.b_off[0] + i] : 0.0;
+  }
+  for (int i = threadIdx.x; i < Dm::K1 * Dm::F2; i += blockDim.x) {
+    const int r = i / Dm::F2, c = i - r * Dm::F2;
+    net[Dm::W2 + swz(r, c, Dm::NF)] = (r < D1 && c < D2) ? src[s.w_off[1] + r * D2 + c] : 0.0;
+  }
+  for (int i = threadIdx.x; i < Dm::F2; i += blockDim.x) net[Dm::B2 + i] = i < D2 ? src[s.b_off[1] + i] : 0.0;
+  for (int i = threadIdx.x; i < Dm::F2 * Dm::P3; i += blockDim.x) {
+    const int r = i / Dm::P3, c = i - r * Dm::P3;
+    net[Dm::W3 + swz(r, c, Dm::NP)] = (r < D2 && c < D3) ? src[s.w_off[2] + r * D3 + c] : 0.0;
+  }
+  for (int i = threadIdx.x; i < Dm::P3; i += blockDim.x) net[Dm::B3 + i] = i < D3 ? src[s.b_off[2] + i] : 0.0;
+}
+
+// First work item whose first edge is at or after e (the items are in net
+// order with non-decreasing first edges).
+__device__ __forceinline__ int first_item_at(const TcLists& L, int nitems, long long e) {
+  int lo = 0, hi = nitems;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if ((long long)L.items[2 * mid].w < e)
+      lo = mid + 1;
+    else
+      hi = mid;
+  }
+  return lo;
+}
+
+// One chunk's inputs (lanes 0-7, one edge each): environment row and slot;
+// edges past ne get a zero row.
+__device__ __forceinline__ void stage_chunk(const TcLists& L, const double* __restrict__ rij, const SeaDev& s,
+                                            int c0, int ne, int lane, double* rt, int* slotS) {
+  if (lane < kCh) {
+    double r4[4] = {0.0, 0.0, 0.0, 0.0};
+    int slot = -1;
+    if (lane < ne) {
+      slot = L.slot[c0 + lane];
       const double r[3] = {rij[3 * (size_t)slot], rij[3 * (size_t)slot + 1], rij[3 * (size_t)slot + 2]};
-      env_row64(r, s.rcut, s.rcut_smth, rt);
+      env_row64(r, s.rcut, s.rcut_smth, r4);
     }
-#pragma unroll
-    for (int k = 0; k < 4; ++k) rtS[4 * e + k] = rt[k];
-    rowS[e] = row;
-    if (slotS) slotS[e] = slot;
+    *reinterpret_cast<double2*>(rt + 4 * lane) = make_double2(r4[0], r4[1]);
+    *reinterpret_cast<double2*>(rt + 4 * lane + 2) = make_double2(r4[2], r4[3]);
+    if (slotS) slotS[lane] = slot;
   }
 }
 
-// outT[n][e] = tanh(sum_k inT[k][e] W[k][n] + b[n]) (+ residual inT[src(n)][e]),
-// thread tiles of 4 edges x TN outputs (TN = 2 for narrow layers, so that the
-// block's threads have work); consecutive threads take consecutive edge groups
-// (the weight loads of a warp then hit few addresses).
-template <int DIN, int DOUT, int TN = 4>
-__device__ __forceinline__ void dense_fwd(const double* inT, const double* W, const double* b, double* outT) {
-  constexpr int EG = kE / 4, NG = (DOUT + TN - 1) / TN;
-  constexpr int RM = resid(DIN, DOUT);
-  for (int it = threadIdx.x; it < EG * NG; it += blockDim.x) {
-    const int e0 = (it % EG) * 4, n0 = (it / EG) * TN;
-    double acc[4][TN];
+// Lane offsets of the two fragment patterns inside a swizzled 8 x 8 block.
+__device__ __forceinline__ void frag_offsets(int g, int t, int (&oA)[2], int (&oB)[2]) {
 #pragma unroll
-    for (int j = 0; j < TN; ++j) {
-      const double bj = n0 + j < DOUT ? b[n0 + j] : 0.0;
+  for (int h = 0; h < 2; ++h) {
+    const int ri = 2 * t + h;
+    oA[h] = swz_row(ri) + ((g + swz_rot(ri)) & 15);
+    oB[h] = swz_row(g) + ((2 * t + h + swz_rot(g)) & 15);
+  }
+}
+
+// Layers 1 and 2 of one chunk, shared by both kernels.  Lane (g, t) =
+// (lane >> 2, lane & 3) owns edge g in the row-major fragments.  Layer 1 is
+// formed directly in the A fragments of layer 2, with K permuted so that
+// k-step (nk, h) holds feature 8 nk + 2t + h (the positions a C fragment
+// holds); h2 stays in its C fragments (edge g, feature 8 nt + 2t + h), which
+// the next product takes as an operand with the same permutation.  t1s[e][k]
+// and h2s[e][f] keep the values other lanes need (residuals, derivatives).
+template <int D1, int D2, int D3>
+__device__ __forceinline__ void layers12(const double* net, const double* rt, double* t1s, double* h2s, int g, int t,
+                                         const int (&oA)[2], double (&acc2)[Dims<D1, D2, D3>::NF][2]) {
+  using Dm = Dims<D1, D2, D3>;
+  constexpr int NK = Dm::NK, NF = Dm::NF, R2 = resid(D1, D2);
+  const double sv = rt[4 * g];
+  double a1[NK][2];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) acc[i][j] = bj;
-    }
-#pragma unroll 5
-    for (int k = 0; k < DIN; ++k) {
-      const double2 xa = *reinterpret_cast<const double2*>(inT + k * kE + e0);
-      const double2 xb = *reinterpret_cast<const double2*>(inT + k * kE + e0 + 2);
-      const double x[4] = {xa.x, xa.y, xb.x, xb.y};
-      double w[TN];
+  for (int nk = 0; nk < NK; ++nk)
 #pragma unroll
-      for (int j = 0; j < TN; ++j) w[j] = n0 + j < DOUT ? W[k * DOUT + n0 + j] : 0.0;
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < TN; ++j) acc[i][j] = fma(x[i], w[j], acc[i][j]);
-    }
-#pragma unroll
-    for (int j = 0; j < TN; ++j) {
-      const int n = n0 + j;
-      if (n >= DOUT) break;
-      double h[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        h[i] = tanh_d(acc[i][j]);
-        if (RM != 0) h[i] += inT[src_of<DIN, DOUT>(n) * kE + e0 + i];
+    for (int h = 0; h < 2; ++h) {
+      const int k = 8 * nk + 2 * t + h;
+      double v = 0.0;
+      if (k < D1) {
+        v = tanh_d(fma(sv, net[Dm::W1 + k], net[Dm::B1 + k]));
+        t1s[g * D1 + k] = v;
       }
-      *reinterpret_cast<double2*>(outT + n * kE + e0) = make_double2(h[0], h[1]);
-      *reinterpret_cast<double2*>(outT + n * kE + e0 + 2) = make_double2(h[2], h[3]);
+      a1[nk][h] = v;
     }
-  }
+#pragma unroll
+  for (int nt = 0; nt < NF; ++nt)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) acc2[nt][h] = net[Dm::B2 + 8 * nt + 2 * t + h];
+#pragma unroll
+  for (int nk = 0; nk < NK; ++nk)
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int nt = 0; nt < NF; ++nt) dmma_8x8x4(acc2[nt], a1[nk][h], net[Dm::W2 + 64 * (nk * NF + nt) + oA[h]]);
+  __syncwarp();  // t1s complete
+#pragma unroll
+  for (int nt = 0; nt < NF; ++nt)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int f = 8 * nt + 2 * t + h;
+      double v = 0.0;
+      if (f < D2) {
+        v = tanh_d(acc2[nt][h]);
+        if (R2 != 0) v += t1s[g * D1 + src_of<D1, D2>(f)];
+        h2s[g * D2 + f] = v;
+      }
+      acc2[nt][h] = v;
+    }
+  __syncwarp();  // h2s complete
 }
 
-// First layer from the scalar input s = R~_0 (no residual: D1 > 2).
-template <int D1>
-__device__ __forceinline__ void layer1(const double* rtS, const double* net, double* A1T) {
-  for (int i = threadIdx.x; i < D1 * kE; i += blockDim.x) {
-    const int n = i / kE, e = i - n * kE;
-    A1T[i] = tanh_d(rtS[4 * e] * net[n] + net[D1 + n]);
-  }
-}
+// Per-warp shared buffers (doubles).
+template <int D1, int D2, int D3>
+struct FwdWarp {
+  static constexpr int TS = Dims<D1, D2, D3>::P3 + 4;  // T row stride: rows 2 apart land 8 bank pairs apart
+  static constexpr int RT = 0, T1 = RT + 4 * kCh, H2 = T1 + kCh * D1, TA = H2 + kCh * D2,
+                       SIZE = (TA + 4 * TS + 1) / 2 * 2;
+};
+template <int D1, int D2, int D3>
+struct BwdWarp {
+  static constexpr int RT = 0, T1 = RT + 4 * kCh, H2 = T1 + kCh * D1, DG = H2 + kCh * D2, SL = DG + kCh * D2,
+                       SIZE = (SL + kCh / 2 + 1) / 2 * 2;  // slots: kCh ints
+};
 
 }  // namespace
 
-// The [25, 50, 100] embedding (the water model); wider nets keep the SIMT path
-// (their backward's working set does not fit one block's shared memory).
+// The [25, 50, 100] embedding (the water model); wider nets keep the SIMT path.
 bool f64_tiled_supported(const SeaDev& s) {
   return s.nl == 3 && s.ed[1] == 25 && s.ed[2] == 50 && s.ed[3] == 100;
 }
@@ -185,100 +235,114 @@ bool f64_tiled_supported(const SeaDev& s) {
 namespace {
 
 // ---------------------------------------------------------------- forward
-// One block per item at a time (persistent over the items): the item's net
-// in shared memory, its edges in subtiles of kE, layers 1-3 as register-tiled
-// fp64 GEMMs over the subtile, then T[row][k][p] += R~[e][k] G[e][p] with
-// one thread per (position, component pair) summing its edges in list order
-// (fixed order: results are run-to-run identical).
+// One block per SM takes the work items whose first edges fall in its share of
+// the edge list (consecutive items of one net form a segment: the net is loaded
+// once per segment); its warps take the segment's centre rows one at a time (a
+// shared counter), and a warp runs its row's edges in chunks of 8 through
+//   layer 1 (scalar input), layer 2 (edges x features),
+//   layer 3 transposed (G^T: positions x edges, so that G^T is the A operand of)
+//   T^T[p][c] += sum_e G^T[p][e] R~[e][c]   (N = the 4 components, padded to 8).
+// T of the row accumulates in shared memory in chunk order and is written once
+// (rows without edges write zeros): results do not depend on which warp or
+// block ran a row.
 template <int D1, int D2, int D3>
-struct FwdSmem {
-  static constexpr int NET = F64Net<D1, D2, D3>::N;
-  static constexpr int RT = NET, A1 = RT + 4 * kE, A2 = A1 + D1 * kE, G = A2 + D2 * kE, END = G + D3 * kE;
-  static constexpr size_t BYTES = (size_t)END * sizeof(double) + kE * sizeof(int);
-};
-
-template <int D1, int D2, int D3>
-__global__ void __launch_bounds__(kT) k_embed_fwd_f64(TcLists L, SeaDev s, const double* __restrict__ rij,
-                                                     const double* __restrict__ emb, double* __restrict__ Tq) {
-  using N = F64Net<D1, D2, D3>;
-  using S = FwdSmem<D1, D2, D3>;
+__global__ void __launch_bounds__(32 * kW, 1) k_embed_fwd_f64(TcLists L, SeaDev s, const double* __restrict__ rij,
+                                                             const double* __restrict__ emb, double* __restrict__ Tq) {
+  using Dm = Dims<D1, D2, D3>;
+  using Wb = FwdWarp<D1, D2, D3>;
+  constexpr int NF = Dm::NF, NP = Dm::NP, TS = Wb::TS, R3 = resid(D2, D3);
   static_assert(resid(1, D1) == 0, "layer 1 without residual");
-  static_assert(2 * D3 <= kT, "one thread per (position, component pair)");
+  static_assert((2 * TS) % 16 == 8, "T rows 2t and 2t + 2 on different bank pairs");
   extern __shared__ __align__(16) double sm[];
+  __shared__ int s_next;
   double* net = sm;
-  double* rtS = sm + S::RT;
-  double* A1T = sm + S::A1;
-  double* A2T = sm + S::A2;
-  double* GT = sm + S::G;
-  int* rowS = reinterpret_cast<int*>(sm + S::END);
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  double* wb = sm + Dm::NET + warp * Wb::SIZE;
+  double* rt = wb + Wb::RT;
+  double* t1s = wb + Wb::T1;
+  double* h2s = wb + Wb::H2;
+  double* tacc = wb + Wb::TA;
+  int oA[2], oB[2];
+  frag_offsets(g, t, oA, oB);
   const int nitems = L.istart[L.nnets];
-  const int p = tid % D3, kp = 2 * (tid / D3);  // contraction role (tid < 2 D3)
-  int loaded = -1;
-  for (int it = blockIdx.x; it < nitems; it += gridDim.x) {
-    const F64Item I = item_at(L, it);
-    if (I.re <= I.rb) continue;  // padding item (block-uniform); rows without edges still write zeros
-    if (I.q != loaded) {
-      __syncthreads();
-      load_net(net, emb, s, I.q, D1, D2, D3);
-      loaded = I.q;
-    }
-    double tacc[kItemRows][2];
+  const long long E = L.eoff[(size_t)L.nnets * L.nloc];
+  const int it0 = first_item_at(L, nitems, E * blockIdx.x / gridDim.x);
+  const int it1 = blockIdx.x + 1 == gridDim.x ? nitems : first_item_at(L, nitems, E * (blockIdx.x + 1) / gridDim.x);
+  for (int it = it0; it < it1;) {
+    const int q = L.items[2 * it].x;
+    int seg = it + 1;
+    while (seg < it1 && L.items[2 * seg].x == q) ++seg;
+    __syncthreads();  // the previous segment's rows are done with the net
+    load_net_sw<D1, D2, D3>(net, emb, s, q);
+    if (tid == 0) s_next = 0;
+    __syncthreads();
+    const int nslots = (seg - it) * kItemRows;
+    for (;;) {
+      int j = 0;
+      if (lane == 0) j = atomicAdd(&s_next, 1);
+      j = __shfl_sync(0xffffffffu, j, 0);
+      if (j >= nslots) break;
+      const int4 rec = L.items[2 * (it + j / kItemRows)];
+      const int row = rec.y + j % kItemRows;
+      if (row >= rec.z) continue;  // short or padding item
+      const int rs = L.eoff[(size_t)q * L.nloc + row], re = L.eoff[(size_t)q * L.nloc + row + 1];
+      __syncwarp();
+      for (int i = lane; i < 4 * TS; i += 32) tacc[i] = 0.0;
+      for (int c0 = rs; c0 < re; c0 += kCh) {
+        __syncwarp();  // the previous chunk's readers are done
+        stage_chunk(L, rij, s, c0, min(kCh, re - c0), lane, rt, nullptr);
+        __syncwarp();
+        double acc2[NF][2];
+        layers12<D1, D2, D3>(net, rt, t1s, h2s, g, t, oA, acc2);
+        // layer 3 transposed: lane holds G^T[p = 8 mt + g][e = 2t + h]
+        double acc3[NP][2];
 #pragma unroll
-    for (int r = 0; r < kItemRows; ++r) tacc[r][0] = tacc[r][1] = 0.0;
-    for (int sub = I.e0; sub < I.e1; sub += kE) {
-      const int ne = min(kE, I.e1 - sub);
-      __syncthreads();  // the previous subtile's readers are done
-      stage_edges(L, rij, s, sub, ne, I.rb, rtS, rowS, nullptr);
-      __syncthreads();
-      layer1<D1>(rtS, net + N::W1, A1T);
-      __syncthreads();
-      dense_fwd<D1, D2, 2>(A1T, net + N::W2, net + N::B2, A2T);
-      __syncthreads();
-      dense_fwd<D2, D3>(A2T, net + N::W3, net + N::B3, GT);
-      __syncthreads();
-      if (tid < 2 * D3) {
-        // edges in list order; the running sum of a row goes to its slot when the row changes
-        double c0 = 0.0, c1 = 0.0;
-        int cur = rowS[0];
-        for (int e = 0; e < ne; ++e) {
-          const int r = rowS[e];
-          if (r != cur) {
+        for (int mt = 0; mt < NP; ++mt) acc3[mt][0] = acc3[mt][1] = net[Dm::B3 + 8 * mt + g];
 #pragma unroll
-            for (int rr = 0; rr < kItemRows; ++rr)
-              if (rr == cur) {
-                tacc[rr][0] += c0;
-                tacc[rr][1] += c1;
-              }
-            c0 = c1 = 0.0;
-            cur = r;
+        for (int kt = 0; kt < NF; ++kt)
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int mt = 0; mt < NP; ++mt)
+              dmma_8x8x4(acc3[mt], net[Dm::W3 + 64 * (kt * NP + mt) + oA[h]], acc2[kt][h]);
+#pragma unroll
+        for (int mt = 0; mt < NP; ++mt)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int p = 8 * mt + g;
+            double v = 0.0;
+            if (p < D3) {
+              v = tanh_d(acc3[mt][h]);
+              if (R3 != 0) v += h2s[(2 * t + h) * D2 + src_of<D2, D3>(p)];
+            }
+            acc3[mt][h] = v;
           }
-          const double g = GT[p * kE + e];
-          c0 = fma(rtS[4 * e + kp], g, c0);
-          c1 = fma(rtS[4 * e + kp + 1], g, c1);
+        // T^T[p][c] += sum_e G^T[p][e] R~[e][c]: k-step h takes edges 2t + h
+        double bR[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) bR[h] = g < 4 ? rt[4 * (2 * t + h) + g] : 0.0;
+#pragma unroll
+        for (int mt = 0; mt < NP; ++mt) {
+          const int p = 8 * mt + g;
+          double tc[2];
+          tc[0] = t < 2 ? tacc[(2 * t) * TS + p] : 0.0;
+          tc[1] = t < 2 ? tacc[(2 * t + 1) * TS + p] : 0.0;
+          dmma_8x8x4(tc, acc3[mt][0], bR[0]);
+          dmma_8x8x4(tc, acc3[mt][1], bR[1]);
+          if (t < 2) {
+            tacc[(2 * t) * TS + p] = tc[0];
+            tacc[(2 * t + 1) * TS + p] = tc[1];
+          }
         }
-#pragma unroll
-        for (int rr = 0; rr < kItemRows; ++rr)
-          if (rr == cur) {
-            tacc[rr][0] += c0;
-            tacc[rr][1] += c1;
-          }
+      }
+      __syncwarp();
+      double* dst = Tq + ((size_t)q * L.nloc + row) * 4 * D3;
+      for (int i = lane; i < 4 * D3; i += 32) {
+        const int c = i / D3, p = i - c * D3;
+        dst[i] = tacc[c * TS + p];
       }
     }
-    if (tid < 2 * D3) {
-      for (int r = 0; r < I.re - I.rb; ++r) {
-        double* dst = Tq + (((size_t)I.q * L.nloc + I.rb + r) * 4 + kp) * D3 + p;
-        double v0 = 0.0, v1 = 0.0;
-#pragma unroll
-        for (int rr = 0; rr < kItemRows; ++rr)
-          if (rr == r) {
-            v0 = tacc[rr][0];
-            v1 = tacc[rr][1];
-          }
-        dst[0] = v0;
-        dst[D3] = v1;
-      }
-    }
+    it = seg;
   }
 }
 
@@ -350,203 +414,231 @@ __global__ void k_dT_f64(int nloc, int ntypes, int M2, double inv_nnei, const in
 }
 
 // ---------------------------------------------------------------- backward
-// Per subtile: the forward recomputed (as above), then
-//   dG[e][p] = sum_k R~[e][k] dT[row][k][p],  dR~[e][k] = sum_p G[e][p] dT[row][k][p]
+// Same division of work as the forward.  Per chunk: layers 1-3 recomputed
+// (layer 3 row-major this time: lane holds z3[e = g][p = 8 nt + 2t + h]), then
+//   dG[e][p] = sum_c R~[e][c] dT[row][c][p],  dR~[e][c] = sum_p G[e][p] dT[row][c][p]
 //   dz3 = dG (1 - t3^2);  dh2 = dz3 W3^T + residual(dG);  dz2 = dh2 (1 - t2^2)
 //   dh1 = dz2 W2^T + residual(dh2);  dz1 = dh1 (1 - t1^2);  dE/ds = dz1 . w1
-// and per slot the environment-row gradient (dR~_0 + dE/ds, dR~_1..3) for the
-// assembly's chain rule.  The tanh outputs are recovered from the layer
-// outputs minus their residual inputs.
+// with dz3 and dz2 taken from their C fragments as the A operands of the next
+// products (the weights' transposed fragments come from the same swizzled
+// copy), and per slot the environment-row gradient (dR~_0 + dE/ds, dR~_1..3)
+// for the assembly's chain rule.  The tanh outputs of layers 1 and 2 are
+// recovered from the stored layer outputs.
 template <int D1, int D2, int D3>
-struct BwdSmem {
-  // G is overwritten by dz3 in place, the residual gradient of layer 3 goes to the
-  // dz2 region (each element read back by the thread that writes dz2 over it),
-  // the partial dR~ wait in registers until the dz3 region is free again, and dT
-  // is read from global memory (L2): two blocks share an SM
-  static constexpr int NET = F64Net<D1, D2, D3>::N;
-  static constexpr int RT = NET, A1 = RT + 4 * kE, A2 = A1 + D1 * kE, G = A2 + D2 * kE, Z2 = G + D3 * kE,
-                       END = Z2 + D2 * kE;
-  static constexpr size_t BYTES = (size_t)END * sizeof(double) + 2 * kE * sizeof(int);
-};
-
-// gxT[m][e] = sum_n gzT[n][e] W[m][n] (the transposed product of a layer with
-// weights W[DIN][DOUT]); thread tiles of 4 edges x 4 inputs m.
-template <int DIN, int DOUT>
-__device__ __forceinline__ void dense_bwd_tile(const double* gzT, const double* W, int it, double (&acc)[4][4],
-                                               int& e0, int& m0) {
-  constexpr int EG = kE / 4;
-  e0 = (it % EG) * 4;
-  m0 = (it / EG) * 4;
+__global__ void __launch_bounds__(32 * kW, 1) k_embed_bwd_f64(TcLists L, SeaDev s, const double* __restrict__ rij,
+                                                             const double* __restrict__ emb,
+                                                             const double* __restrict__ dT, double* __restrict__ genv) {
+  using Dm = Dims<D1, D2, D3>;
+  using Wb = BwdWarp<D1, D2, D3>;
+  constexpr int NK = Dm::NK, NF = Dm::NF, NP = Dm::NP, R2 = resid(D1, D2), R3 = resid(D2, D3);
+  static_assert(resid(1, D1) == 0, "layer 1 without residual");
+  static_assert(D3 % 2 == 0, "dT pairs as 16-byte loads");
+  extern __shared__ __align__(16) double sm[];
+  __shared__ int s_next;
+  double* net = sm;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  double* wb = sm + Dm::NET + warp * Wb::SIZE;
+  double* rt = wb + Wb::RT;
+  double* t1s = wb + Wb::T1;
+  double* h2s = wb + Wb::H2;
+  double* dgs = wb + Wb::DG;  // dG[e][D2 + f], later dh2[e][f]
+  int* slotS = reinterpret_cast<int*>(wb + Wb::SL);
+  int oA[2], oB[2];
+  frag_offsets(g, t, oA, oB);
+  const int nitems = L.istart[L.nnets];
+  const long long E = L.eoff[(size_t)L.nnets * L.nloc];
+  const int it0 = first_item_at(L, nitems, E * blockIdx.x / gridDim.x);
+  const int it1 = blockIdx.x + 1 == gridDim.x ? nitems : first_item_at(L, nitems, E * (blockIdx.x + 1) / gridDim.x);
+  for (int it = it0; it < it1;) {
+    const int q = L.items[2 * it].x;
+    int seg = it + 1;
+    while (seg < it1 && L.items[2 * seg].x == q) ++seg;
+    __syncthreads();
+    load_net_sw<D1, D2, D3>(net, emb, s, q);
+    if (tid == 0) s_next = 0;
+    __syncthreads();
+    const int nslots = (seg - it) * kItemRows;
+    for (;;) {
+      int j = 0;
+      if (lane == 0) j = atomicAdd(&s_next, 1);
+      j = __shfl_sync(0xffffffffu, j, 0);
+      if (j >= nslots) break;
+      const int4 rec = L.items[2 * (it + j / kItemRows)];
+      const int row = rec.y + j % kItemRows;
+      if (row >= rec.z) continue;
+      const int rs = L.eoff[(size_t)q * L.nloc + row], re = L.eoff[(size_t)q * L.nloc + row + 1];
+      const double* dtr = dT + (size_t)row * 4 * D3;
+      for (int c0 = rs; c0 < re; c0 += kCh) {
+        const int ne = min(kCh, re - c0);
+        __syncwarp();
+        stage_chunk(L, rij, s, c0, ne, lane, rt, slotS);
+        __syncwarp();
+        double acc2[NF][2];
+        layers12<D1, D2, D3>(net, rt, t1s, h2s, g, t, oA, acc2);
+        // layer 3: lane holds z3[e = g][p = 8 nt + 2t + h]
+        double acc3[NP][2];
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+        for (int nt = 0; nt < NP; ++nt)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = 0.0;
-#pragma unroll 4
-  for (int n = 0; n < DOUT; ++n) {
-    const double2 za = *reinterpret_cast<const double2*>(gzT + n * kE + e0);
-    const double2 zb = *reinterpret_cast<const double2*>(gzT + n * kE + e0 + 2);
-    const double z[4] = {za.x, za.y, zb.x, zb.y};
-    double w[4];
+          for (int h = 0; h < 2; ++h) acc3[nt][h] = net[Dm::B3 + 8 * nt + 2 * t + h];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) w[j] = m0 + j < DIN ? W[(m0 + j) * DOUT + n] : 0.0;
+        for (int kt = 0; kt < NF; ++kt)
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+          for (int h = 0; h < 2; ++h)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) acc[i][j] = fma(z[i], w[j], acc[i][j]);
+            for (int nt = 0; nt < NP; ++nt)
+              dmma_8x8x4(acc3[nt], acc2[kt][h], net[Dm::W3 + 64 * (kt * NP + nt) + oA[h]]);
+        // dG, dR~ (partial over this lane's positions), dz3; the residual
+        // gradient of layer 3 starts dh2 (own positions directly, the concat
+        // rule's second half through dgs)
+        const double2 ra = *reinterpret_cast<const double2*>(rt + 4 * g);
+        const double2 rb = *reinterpret_cast<const double2*>(rt + 4 * g + 2);
+        double qv[4] = {0.0, 0.0, 0.0, 0.0};
+        double dh2[NF][2];
+#pragma unroll
+        for (int nt = 0; nt < NF; ++nt) dh2[nt][0] = dh2[nt][1] = 0.0;
+#pragma unroll
+        for (int nt = 0; nt < NP; ++nt) {
+          const int p0 = 8 * nt + 2 * t;
+          double2 d[4];
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            d[c] = p0 < D3 ? __ldg(reinterpret_cast<const double2*>(dtr + c * D3 + p0)) : make_double2(0.0, 0.0);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int p = p0 + h;
+            double dz = 0.0;
+            if (p < D3) {
+              const double d0 = h ? d[0].y : d[0].x, d1 = h ? d[1].y : d[1].x, d2 = h ? d[2].y : d[2].x,
+                           d3 = h ? d[3].y : d[3].x;
+              const double t3 = tanh_d(acc3[nt][h]);
+              const double G = R3 != 0 ? t3 + h2s[g * D2 + src_of<D2, D3>(p)] : t3;
+              const double dg = ((ra.x * d0 + ra.y * d1) + rb.x * d2) + rb.y * d3;
+              qv[0] = fma(G, d0, qv[0]);
+              qv[1] = fma(G, d1, qv[1]);
+              qv[2] = fma(G, d2, qv[2]);
+              qv[3] = fma(G, d3, qv[3]);
+              if (R3 != 0) {
+                if (p < D2) {
+                  if (nt < NF) dh2[nt < NF ? nt : 0][h] += dg;
+                } else {
+                  dgs[g * D2 + (p - D2)] = dg;
+                }
+              }
+              dz = dg * (1.0 - t3 * t3);
+            }
+            acc3[nt][h] = dz;
+          }
+        }
+        __syncwarp();  // dgs complete
+        if (R3 == 2) {
+#pragma unroll
+          for (int nt = 0; nt < NF; ++nt)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int f = 8 * nt + 2 * t + h;
+              if (f < D2) dh2[nt][h] += dgs[g * D2 + f];
+            }
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          qv[c] += __shfl_xor_sync(0xffffffffu, qv[c], 1);
+          qv[c] += __shfl_xor_sync(0xffffffffu, qv[c], 2);
+        }
+        // dh2 += dz3 W3^T (K = positions: k-step (kt, h) holds 8 kt + 2t + h)
+#pragma unroll
+        for (int kt = 0; kt < NP; ++kt)
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int nt = 0; nt < NF; ++nt)
+              dmma_8x8x4(dh2[nt], acc3[kt][h], net[Dm::W3 + 64 * (nt * NP + kt) + oB[h]]);
+        __syncwarp();  // every lane has read dgs
+        // dz2 = dh2 (1 - t2^2); dh2 to dgs for the layer-2 residual of dh1
+#pragma unroll
+        for (int nt = 0; nt < NF; ++nt)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int f = 8 * nt + 2 * t + h;
+            double dz = 0.0;
+            if (f < D2) {
+              const double dh = dh2[nt][h];
+              if (R2 != 0) dgs[g * D2 + f] = dh;
+              const double t2 = R2 != 0 ? h2s[g * D2 + f] - t1s[g * D1 + src_of<D1, D2>(f)] : h2s[g * D2 + f];
+              dz = dh * (1.0 - t2 * t2);
+            }
+            dh2[nt][h] = dz;
+          }
+        __syncwarp();  // dh2 in dgs
+        double dh1[NK][2];
+#pragma unroll
+        for (int nk = 0; nk < NK; ++nk)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int k = 8 * nk + 2 * t + h;
+            double v = 0.0;
+            if (k < D1) {
+              if (R2 == 2) v = dgs[g * D2 + k] + dgs[g * D2 + k + D1];
+              if (R2 == 1) v = dgs[g * D2 + k];
+            }
+            dh1[nk][h] = v;
+          }
+#pragma unroll
+        for (int kt = 0; kt < NF; ++kt)
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int nk = 0; nk < NK; ++nk)
+              dmma_8x8x4(dh1[nk], dh2[kt][h], net[Dm::W2 + 64 * (nk * NF + kt) + oB[h]]);
+        // dz1 = dh1 (1 - t1^2), dE/ds = dz1 . w1 (this lane's features, then the quad)
+        double ds = 0.0;
+#pragma unroll
+        for (int nk = 0; nk < NK; ++nk)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int k = 8 * nk + 2 * t + h;
+            if (k < D1) {
+              const double t1 = t1s[g * D1 + k];
+              ds = fma(dh1[nk][h] * (1.0 - t1 * t1), net[Dm::W1 + k], ds);
+            }
+          }
+        ds += __shfl_xor_sync(0xffffffffu, ds, 1);
+        ds += __shfl_xor_sync(0xffffffffu, ds, 2);
+        if (g < ne) {
+          const double v = t == 0 ? qv[0] + ds : (t == 1 ? qv[1] : (t == 2 ? qv[2] : qv[3]));
+          genv[4 * (size_t)slotS[g] + t] = v;
+        }
+      }
+    }
+    it = seg;
   }
 }
 
+template <class K>
+void allow_smem(K kern, size_t smem) {
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+}
+
 template <int D1, int D2, int D3>
-__global__ void __launch_bounds__(kT, 2) k_embed_bwd_f64(TcLists L, SeaDev s, const double* __restrict__ rij,
-                                                        const double* __restrict__ emb, const double* __restrict__ dT,
-                                                        double* __restrict__ genv) {
-  using N = F64Net<D1, D2, D3>;
-  using S = BwdSmem<D1, D2, D3>;
-  constexpr int R2 = resid(D1, D2), R3 = resid(D2, D3);
-  static_assert(resid(1, D1) == 0, "layer 1 without residual");
-  extern __shared__ __align__(16) double sm[];
-  double* net = sm;
-  double* rtS = sm + S::RT;   // [e][4]
-  double* A1T = sm + S::A1;   // t1, later dz1
-  double* A2T = sm + S::A2;   // h2, later dh2
-  double* GT = sm + S::G;     // G, then dz3, then the partial dR~ [warp][e][4]
-  double* Z2T = sm + S::Z2;   // residual gradient of layer 3, then dz2
-  int* rowS = reinterpret_cast<int*>(sm + S::END);
-  int* slotS = rowS + kE;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  constexpr int NW = kT / 32;
-  static_assert(kE == 32, "one lane per edge in the dG pass");
-  static_assert(NW * kE * 4 <= D3 * kE, "the partial dR~ fit the dz3 region");
-  const int nitems = L.istart[L.nnets];
-  int loaded = -1;
-  for (int it = blockIdx.x; it < nitems; it += gridDim.x) {
-    const F64Item I = item_at(L, it);
-    if (I.e1 <= I.e0) continue;
-    __syncthreads();
-    if (I.q != loaded) {
-      load_net(net, emb, s, I.q, D1, D2, D3);
-      loaded = I.q;
-    }
-    for (int sub = I.e0; sub < I.e1; sub += kE) {
-      const int ne = min(kE, I.e1 - sub);
-      __syncthreads();
-      stage_edges(L, rij, s, sub, ne, I.rb, rtS, rowS, slotS);
-      __syncthreads();
-      layer1<D1>(rtS, net + N::W1, A1T);
-      __syncthreads();
-      dense_fwd<D1, D2, 2>(A1T, net + N::W2, net + N::B2, A2T);
-      __syncthreads();
-      dense_fwd<D2, D3>(A2T, net + N::W3, net + N::B3, GT);
-      __syncthreads();
-      // dG, dz3 (over G), the residual gradient into layer 2, partial dR~:
-      // lane = edge, warps over positions; the positions that share a residual
-      // source (s and s + D2 under the concat rule) go to the same thread
-      const int e = lane, row = rowS[e];
-      const double r0 = rtS[4 * e], r1 = rtS[4 * e + 1], r2 = rtS[4 * e + 2], r3 = rtS[4 * e + 3];
-      const double* dtr = dT + (size_t)(I.rb + row) * 4 * D3;
-      double q0 = 0.0, q1 = 0.0, q2 = 0.0, q3 = 0.0;
-      auto position = [&](int p, double base) -> double {  // returns dG
-        const double d0 = __ldg(dtr + p), d1 = __ldg(dtr + D3 + p), d2 = __ldg(dtr + 2 * D3 + p),
-                     d3 = __ldg(dtr + 3 * D3 + p);
-        const double g = GT[p * kE + e];
-        const double dg = ((r0 * d0 + r1 * d1) + r2 * d2) + r3 * d3;
-        q0 = fma(g, d0, q0);
-        q1 = fma(g, d1, q1);
-        q2 = fma(g, d2, q2);
-        q3 = fma(g, d3, q3);
-        const double t3 = g - base;
-        GT[p * kE + e] = dg * (1.0 - t3 * t3);
-        return dg;
-      };
-      if constexpr (R3 == 2) {
-        for (int sp = warp; sp < D2; sp += NW) {
-          const double h2 = A2T[sp * kE + e];
-          const double ga = position(sp, h2), gb = position(sp + D2, h2);
-          Z2T[sp * kE + e] = ga + gb;
-        }
-      } else if constexpr (R3 == 1) {
-        for (int p = warp; p < D3; p += NW) Z2T[p * kE + e] = position(p, A2T[p * kE + e]);
-      } else {
-        for (int p = warp; p < D3; p += NW) position(p, 0.0);
-      }
-      __syncthreads();
-      // dh2 = dz3 W3^T + residual of layer 3; dz2 = dh2 (1 - t2^2)
-      for (int it2 = tid; it2 < (kE / 4) * ((D2 + 3) / 4); it2 += kT) {
-        double acc[4][4];
-        int e0, m0;
-        dense_bwd_tile<D2, D3>(GT, net + N::W3, it2, acc, e0, m0);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int m = m0 + j;
-          if (m >= D2) break;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int ee = e0 + i;
-            double dh = acc[i][j];
-            if (R3 != 0) dh += Z2T[m * kE + ee];
-            const double h2 = A2T[m * kE + ee];
-            const double t2 = R2 != 0 ? h2 - A1T[src_of<D1, D2>(m) * kE + ee] : h2;
-            Z2T[m * kE + ee] = dh * (1.0 - t2 * t2);  // over the residual gradient read above
-            A2T[m * kE + ee] = dh;                     // read above by this thread only
-          }
-        }
-      }
-      __syncthreads();
-      {  // the dz3 region is free: the partial dR~ of this warp
-        double* pr = GT + (warp * kE + e) * 4;
-        pr[0] = q0;
-        pr[1] = q1;
-        pr[2] = q2;
-        pr[3] = q3;
-      }
-      // dh1 = dz2 W2^T + residual of layer 2; dz1 = dh1 (1 - t1^2) over t1
-      for (int it2 = tid; it2 < (kE / 4) * ((D1 + 3) / 4); it2 += kT) {
-        double acc[4][4];
-        int e0, m0;
-        dense_bwd_tile<D1, D2>(Z2T, net + N::W2, it2, acc, e0, m0);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int m = m0 + j;
-          if (m >= D1) break;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int ee = e0 + i;
-            double dh = acc[i][j];
-            if (R2 == 1) dh += A2T[m * kE + ee];
-            if (R2 == 2) dh += A2T[m * kE + ee] + A2T[(m + D1) * kE + ee];
-            const double t1 = A1T[m * kE + ee];
-            A1T[m * kE + ee] = dh * (1.0 - t1 * t1);
-          }
-        }
-      }
-      __syncthreads();
-      if (tid < ne) {  // dE/ds, the partial dR~ in warp order, the slot's environment-row gradient
-        const int ee = tid;
-        double ds = 0.0;
-        for (int m = 0; m < D1; ++m) ds = fma(A1T[m * kE + ee], net[N::W1 + m], ds);
-        double g[4] = {0.0, 0.0, 0.0, 0.0};
-        for (int w = 0; w < NW; ++w)
-#pragma unroll
-          for (int k = 0; k < 4; ++k) g[k] += GT[(w * kE + ee) * 4 + k];
-        double2* go = reinterpret_cast<double2*>(genv + 4 * (size_t)slotS[ee]);
-        go[0] = make_double2(g[0] + ds, g[1]);
-        go[1] = make_double2(g[2], g[3]);
-      }
-    }
-  }
+size_t fwd_smem() {
+  return sizeof(double) * (Dims<D1, D2, D3>::NET + (size_t)kW * FwdWarp<D1, D2, D3>::SIZE);
+}
+template <int D1, int D2, int D3>
+size_t bwd_smem() {
+  return sizeof(double) * (Dims<D1, D2, D3>::NET + (size_t)kW * BwdWarp<D1, D2, D3>::SIZE);
 }
 
 template <int D1, int D2, int D3>
 void run_fwd(cudaStream_t st, const SeaDev& s, const TcLists& L, int grid, const double* rij, const double* emb,
              double* Tq, double* T, double* D, const int* perm_atom, int nloc) {
-  const size_t smem = FwdSmem<D1, D2, D3>::BYTES;
+  const size_t smem = fwd_smem<D1, D2, D3>();
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(k_embed_fwd_f64<D1, D2, D3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    allow_smem(k_embed_fwd_f64<D1, D2, D3>, smem);
     attr = true;
   }
   count_launch();
-  k_embed_fwd_f64<D1, D2, D3><<<grid, kT, smem, st>>>(L, s, rij, emb, Tq);
+  k_embed_fwd_f64<D1, D2, D3><<<grid, 32 * kW, smem, st>>>(L, s, rij, emb, Tq);
   count_launch();
   k_t_combine_f64<D3><<<nloc, 256, 0, st>>>(L, s.M2, s.inv_nnei, perm_atom, Tq, T, D);
 }
@@ -558,33 +650,30 @@ void run_bwd(cudaStream_t st, const SeaDev& s, const TcLists& L, int grid, const
   const size_t dsm = sizeof(double) * (4 * D3 + (size_t)D3 * (s.M2 + 1));
   static size_t dattr = 0;
   if (dsm > dattr) {
-    cudaFuncSetAttribute(k_dT_f64<D3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dsm);
+    allow_smem(k_dT_f64<D3>, dsm);
     dattr = dsm;
   }
   count_launch();
   k_dT_f64<D3><<<nloc, 128, dsm, st>>>(nloc, s.ntypes, s.M2, s.inv_nnei, type_start, perm_atom, T, dD, dT);
-  const size_t smem = BwdSmem<D1, D2, D3>::BYTES;
+  const size_t smem = bwd_smem<D1, D2, D3>();
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(k_embed_bwd_f64<D1, D2, D3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    allow_smem(k_embed_bwd_f64<D1, D2, D3>, smem);
     attr = true;
   }
   count_launch();
-  k_embed_bwd_f64<D1, D2, D3><<<grid, kT, smem, st>>>(L, s, rij, emb, dT, genv);
+  k_embed_bwd_f64<D1, D2, D3><<<grid, 32 * kW, smem, st>>>(L, s, rij, emb, dT, genv);
 }
 
 }  // namespace
 
 int embed_f64_grid(const SeaDev& s, bool backward) {
-  int dev = 0, nsm = 148, occ = 1;
+  (void)s;
+  (void)backward;
+  int dev = 0, nsm = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-  (void)s;
-  const size_t smem = backward ? BwdSmem<25, 50, 100>::BYTES : FwdSmem<25, 50, 100>::BYTES;
-  int smem_sm = 0;
-  cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
-  occ = std::max(1, std::min(4, smem_sm / (int)(smem + 1024)));
-  return nsm * occ;
+  return nsm;  // one block of kF64Warps warps per SM
 }
 
 void launch_embed_fwd_f64(cudaStream_t st, const SeaDev& s, const TcLists& L, int grid, const double* rij,

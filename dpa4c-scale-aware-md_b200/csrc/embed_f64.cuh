@@ -1,15 +1,16 @@
 // fp64 embedding path (the parity mode) over the compacted edge lists of the
-// tensor-core path: work items of kItemRows centre rows of one embedding net,
-// their edges in subtiles of kF64Edges.  Per subtile the embedding layers run
-// as register-tiled fp64 GEMMs (4 edges x 4 features per thread, the net in
-// shared memory for every edge of the item), then the contraction
-// T = R~^T G accumulates in a fixed order (one thread per position and pair of
-// environment components, edges in list order).  The backward recomputes the
-// forward per subtile and forms dG, dR~, dz3, dh2, dz2, dh1 and dE/ds the same
-// way, writing per slot the environment-row gradient that the assembly chains
-// to r_ij.  Replaces the per-centre SIMT kernels (k_descriptor_fwd/bwd) for
-// the [25, 50, 100] embedding; results agree with them to fp64 rounding (the
-// sums run in another order).
+// tensor-core path.  One block per SM takes the work items (kItemRows centre
+// rows of one embedding net) whose edges fall in its share of the edge list;
+// its kF64Warps warps take the centre rows one at a time and run each row's
+// edges in chunks of 8 through the embedding layers as fp64 tensor-core
+// products (mma.sync m8n8k4 .f64: the edges are the 8-row M or N extent), the
+// net in shared memory once per block and net.  The forward accumulates
+// T = R~^T G of the row in chunk order (results do not depend on the schedule);
+// the backward recomputes the forward per chunk and forms dG, dR~, dz3, dh2,
+// dz2, dh1 and dE/ds, writing per slot the environment-row gradient that the
+// assembly chains to r_ij.  Replaces the per-centre SIMT kernels
+// (k_descriptor_fwd/bwd) for the [25, 50, 100] embedding; results agree with
+// them to fp64 rounding (the sums run in another order).
 #pragma once
 
 #include <cuda_runtime.h>
@@ -19,8 +20,7 @@
 
 namespace b200dp {
 
-constexpr int kF64Edges = 32;
-constexpr int kF64Threads = 256;
+constexpr int kF64Warps = 12;  // warps per block (one block per SM)
 
 bool f64_tiled_supported(const SeaDev& s);
 int embed_f64_grid(const SeaDev& s, bool backward);
