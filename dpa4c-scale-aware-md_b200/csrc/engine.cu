@@ -327,6 +327,10 @@ b200dp_status Engine::init_tail() {
     err = "neighbour selection too large for the list-format kernel";
     return B200DP_ERR_UNSUPPORTED;
   }
+  if (sd.selt > kAssembleMaxSlots) {
+    err = "neighbour selection above 512 slots per centre is not supported";
+    return B200DP_ERR_UNSUPPORTED;
+  }
   B200DP_CUDA_TRY(cudaStreamCreateWithFlags(&own_stream, cudaStreamNonBlocking));
   for (auto& ev : events) B200DP_CUDA_TRY(cudaEventCreate(&ev));
   B200DP_CUDA_TRY(err_buf.ensure(sizeof(int) * kErrCount));

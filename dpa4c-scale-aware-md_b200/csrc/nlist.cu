@@ -79,6 +79,11 @@ int make_grid(bool periodic, const double* box, const double* region, double rcu
     if (2 * g.reach[d] + 1 > 31) return 2;
   }
   g.ncells = g.n[0] * g.n[1] * g.n[2];
+  if (periodic && box[1] == 0.0 && box[2] == 0.0 && box[3] == 0.0 && box[5] == 0.0 && box[6] == 0.0 &&
+      box[7] == 0.0) {
+    g.prune = 1;
+    for (int d = 0; d < 3; ++d) g.cw[d] = box[4 * d] / g.n[d];
+  }
   return 0;
 }
 
@@ -88,6 +93,7 @@ int make_grid_dbox(const double* box_ref, double min_scale, const double* dbox, 
   for (int k = 0; k < 9; ++k) b[k] = box_ref[k] * min_scale;
   const int rc = make_grid(true, b, nullptr, rcut, max_cells, g);
   g.dB = dbox;
+  g.prune = 0;  // the device box may differ from the reference box
   return rc;
 }
 
@@ -608,6 +614,18 @@ __device__ __forceinline__ void gather_stencil(const FormatSpec& f, const GridSp
             ok = ok && uu[d] >= 0 && uu[d] < g.n[d];
           }
         }
+        if (!DB && ok && g.prune) {  // distance from the centre to the cell's box
+          const int o[3] = {dx - g.reach[0], dy - g.reach[1], dz - g.reach[2]};
+          double d2 = 0.0;
+#pragma unroll
+          for (int d = 0; d < 3; ++d) {
+            const double pc = xi[d] - ci[d] * g.cw[d];  // the centre's offset inside its cell
+            const double gap = o[d] > 0 ? o[d] * g.cw[d] - pc : (o[d] < 0 ? pc + (-o[d] - 1) * g.cw[d] : 0.0);
+            const double gm = fmax(gap - 1e-6, 0.0);
+            d2 += gm * gm;
+          }
+          ok = d2 < rc2;
+        }
         if (ok) {
           const int cc = (uu[0] * g.n[1] + uu[1]) * g.n[2] + uu[2];
           st[u] = cell_start[cc];
@@ -680,7 +698,7 @@ __device__ __forceinline__ void gather_stencil(const FormatSpec& f, const GridSp
 }
 
 template <bool DB>
-__global__ void __launch_bounds__(kFmtWarps * 32)
+__global__ void __launch_bounds__(kFmtWarps * 32, 3)
     k_format(FormatSpec f, GridSpec g, const double* __restrict__ xw, const int* __restrict__ cell_of,
              const int* __restrict__ cell_start, const CellRec* __restrict__ cell_rec, int* __restrict__ nl_j,
              int* __restrict__ nl_code, double* __restrict__ nl_rij, int* __restrict__ nl_cnt,

@@ -25,6 +25,11 @@ struct GridSpec {
   int n[3];         // cells per dimension
   int reach[3];     // stencil half-width in cells
   int ncells;
+  // stencil cells whose nearest point is beyond the cutoff are skipped: set for
+  // periodic orthorhombic boxes held on the host (every wrapped atom lies in its
+  // cell's box of widths cw, so the test is exact up to a 1e-6 A margin)
+  int prune;
+  double cw[3];
   // periodic box read from device memory ([B | Binv], 18 doubles) instead of
   // B / Binv above, when set: the box of a barostat changes on the device
   // between calls; the cell counts and the stencil reach then come from a

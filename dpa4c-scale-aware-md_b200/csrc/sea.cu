@@ -524,13 +524,14 @@ void launch_fit_seed(cudaStream_t st, int Mmax, const int* range, int N, const P
 
 // ---------------------------------------------------------------- assembly
 // F_j = sum_{own row} g - sum_{edges into j} g.  One warp per centre i sums its
-// own row in a fixed order (slot order, xor-tree warp reduction) and scatters
-// -g of every edge into the neighbour's accumulator.  The accumulators are
-// 128-bit two's-complement fixed point with 64 fractional bits, added with
-// integer atomics: integer addition is associative, so the sum does not
-// depend on the order in which edges arrive (deterministic), and it is exact
-// to 2^-64 per term.  A second pass converts each accumulator to fp64, adds
-// the own-row part and clears the accumulator for the next call.
+// own row in a fixed order (the row's occupied slots in slot order, dealt to
+// the lanes in turn, then an xor-tree warp reduction) and scatters -g of every
+// edge into the neighbour's accumulator.  The accumulators are 128-bit
+// two's-complement fixed point with 64 fractional bits, added with integer
+// atomics: integer addition is associative, so the sum does not depend on the
+// order in which edges arrive (deterministic).  A second pass converts each
+// accumulator to fp64, adds the own-row part and clears the accumulator for
+// the next call.
 //
 // The total virial -sum g (x) r runs over every edge once and is summed over
 // the own rows; the per-atom virial (edges into j) is scattered the same way
@@ -602,7 +603,9 @@ __global__ void __launch_bounds__(kAsmWarps * 32)
                double* __restrict__ energy, double* __restrict__ virial, FoldTargets fold, double rc, double rs) {
   __shared__ double s_part[kAsmWarps][kAsmCols];
   __shared__ int s_last;
+  __shared__ short s_slot[kAsmWarps][kAssembleMaxSlots];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  short* slots = s_slot[warp];
   double v[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
   double e = 0;
   // a fixed grid strides over the atoms: the same atoms land in the same
@@ -610,9 +613,21 @@ __global__ void __launch_bounds__(kAsmWarps * 32)
   for (int i = blockIdx.x * kAsmWarps + warp; i < nloc; i += gridDim.x * kAsmWarps) {
     double f[3] = {0, 0, 0};
     const size_t row = (size_t)i * selt;
-    for (int s = lane; s < selt; s += 32) {
+    // the row's occupied slots in slot order (a ballot per 32 slots)
+    int nreal = 0;
+    __syncwarp();
+    for (int s0 = 0; s0 < selt; s0 += 32) {
+      const int s = s0 + lane;
+      const bool occ = s < selt && nl_j[row + s] >= 0;
+      const unsigned m = __ballot_sync(0xffffffffu, occ);
+      if (occ) slots[nreal + __popc(m & ((1u << lane) - 1u))] = (short)s;
+      nreal += __popc(m);
+    }
+    __syncwarp();
+    for (int k = lane; k < nreal; k += 32) {
+      const int s = slots[k];
       const int j = nl_j[row + s];
-      if (j >= 0) {
+      {
         const double* r = rij + 3 * (row + s);
         const double r3[3] = {r[0], r[1], r[2]};
         double g3[3];

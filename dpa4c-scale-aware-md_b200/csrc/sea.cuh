@@ -76,6 +76,7 @@ struct EnvChain {
   bool on;
   double rcut, rcut_smth;
 };
+constexpr int kAssembleMaxSlots = 512;  // neighbour slots per centre (sum of sel) the assembly takes
 void launch_assemble(cudaStream_t st, int nloc, int nall, int selt, const int* nl_j, const double* gslot,
                      const double* rij, const double* atom_e, double* force, double* atom_virial,
                      unsigned long long* acc_f, unsigned long long* acc_v, unsigned* nonfinite, double* partial,
