@@ -210,28 +210,9 @@ __device__ __forceinline__ void split_pair(float a, float b, uint32_t& hi, uint3
   lo = __byte_perm(__float_as_uint(ar), __float_as_uint(br), 0x7632);
 }
 
-#ifdef B200DP_TANH_NEWTON
-// tanh(x) = 1 - 2 / (1 + e^{2x}) with one exponential on the special-function
-// unit and the reciprocal by Newton's iteration r <- r (2 - d r) from the
-// integer-subtraction first guess (relative error < 5.1 % for d >= 1), three
-// steps.  x is clamped to [-9, 9], where tanh is +-1 to fp32 precision.
-// Absolute error < 4e-7.
-__device__ __forceinline__ float tanh_fast(float x) {
-  x = fminf(fmaxf(x, -9.0f), 9.0f);
-  float e;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(x * 2.8853900817779268f));
-  const float d = 1.0f + e;
-  float r = __uint_as_float(0x7EF311C7u - __float_as_uint(d));
-  r = r * fmaf(-d, r, 2.0f);
-  r = r * fmaf(-d, r, 2.0f);
-  r = r * fmaf(-d, r, 2.0f);
-  return fmaf(-2.0f, r, 1.0f);
-}
-#else
 // tanh from the exponential: 1 - 2 / (exp(2x) + 1).  Absolute error ~1e-7,
 // saturates correctly at both ends (exp overflow -> 1, underflow -> -1).
 __device__ __forceinline__ float tanh_fast(float x) { return 1.0f - __fdividef(2.0f, __expf(2.0f * x) + 1.0f); }
-#endif
 
 // Packs two bf16 into one 32-bit word (first element in the low half).
 __device__ __forceinline__ uint32_t pack2(__nv_bfloat16 a, __nv_bfloat16 b) {

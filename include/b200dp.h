@@ -290,9 +290,11 @@ const float* b200dp_direct_fp32_global_virial_pointer(void);
  * fix nve / fix nvt / fix npt iso, which drives the reference's force call
  * (components/lammps/overlays/src/KOKKOS/fix_nh_kokkos.cpp:863-1001; device
  * chain: components/lammps/overlays/src/KOKKOS/dpa_fast_step_kokkos.h:307-400).
- * Positions, velocities, forces and the chain state stay on the device; a
- * run enqueues its steps on the driver's stream without host
- * synchronisation (NPT reads 12 numbers back per step for the barostat).
+ * Positions, velocities, forces, the chain and barostat state and the NPT
+ * box stay on the device; a run enqueues its steps on the driver's stream
+ * without host synchronisation (the NPT force call reads the box from device
+ * memory), and the host reads the state back only at thermo output,
+ * snapshot and restore.
  * The box is periodic; positions are not wrapped (the engine images them). */
 typedef enum b200dp_md_ensemble { B200DP_MD_NVE = 0, B200DP_MD_NVT = 1, B200DP_MD_NPT = 2 } b200dp_md_ensemble;
 
