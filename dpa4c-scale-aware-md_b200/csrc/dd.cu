@@ -102,9 +102,11 @@ class NcclComm : public Comm {
     }
     if (sb && cudaMemcpyAsync(dbuf, s, sb, cudaMemcpyHostToDevice, st) != cudaSuccess) return false;
     if (ncclGroupStart() != ncclSuccess) return false;
-    if (sb) ncclSend(dbuf, sb, ncclChar, to, comm, st);
-    if (rb) ncclRecv(dbuf + so, rb, ncclChar, from, comm, st);
-    if (ncclGroupEnd() != ncclSuccess) return false;
+    ncclResult_t rs = ncclSuccess, rr = ncclSuccess;
+    if (sb) rs = ncclSend(dbuf, sb, ncclChar, to, comm, st);
+    if (rb) rr = ncclRecv(dbuf + so, rb, ncclChar, from, comm, st);
+    // the group is closed whatever the two calls returned
+    if (ncclGroupEnd() != ncclSuccess || rs != ncclSuccess || rr != ncclSuccess) return false;
     if (rb && cudaMemcpyAsync(r, dbuf + so, rb, cudaMemcpyDeviceToHost, st) != cudaSuccess) return false;
     return cudaStreamSynchronize(st) == cudaSuccess;
   }
