@@ -192,16 +192,18 @@ b200dp_status Engine::init(const char* path, const b200dp_options* o) {
     auto up_bytes = [&](const std::vector<unsigned char>& v) -> const unsigned char* {
       fit_dev.emplace_back();
       DevBuf& d = fit_dev.back();
-      if (d.ensure(v.size()) != cudaSuccess) return nullptr;
-      cudaMemcpy(d.ptr, v.data(), v.size(), cudaMemcpyHostToDevice);
+      if (d.ensure(v.size()) != cudaSuccess ||
+          cudaMemcpy(d.ptr, v.data(), v.size(), cudaMemcpyHostToDevice) != cudaSuccess)
+        return nullptr;
       return static_cast<const unsigned char*>(d.ptr);
     };
     auto up_f = [&](const std::vector<double>& v) -> const float* {
       std::vector<float> f(v.begin(), v.end());
       fit_dev.emplace_back();
       DevBuf& d = fit_dev.back();
-      if (d.ensure(f.size() * 4) != cudaSuccess) return nullptr;
-      cudaMemcpy(d.ptr, f.data(), f.size() * 4, cudaMemcpyHostToDevice);
+      if (d.ensure(f.size() * 4) != cudaSuccess ||
+          cudaMemcpy(d.ptr, f.data(), f.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+        return nullptr;
       return static_cast<const float*>(d.ptr);
     };
     for (int t = 0; t < hm.ntypes; ++t) {

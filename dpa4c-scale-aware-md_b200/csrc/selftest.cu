@@ -98,22 +98,22 @@ extern "C" b200dp_status b200dp_selftest_mma(int K, int N, int a_mn_major, int b
     st = B200DP_ERR_CUDA;
     goto done;
   }
-  cudaMemcpy(dA, A, sizeof(float) * 128 * K, cudaMemcpyHostToDevice);
-  cudaMemcpy(dB, B, sizeof(float) * N * K, cudaMemcpyHostToDevice);
-  cudaMemset(dErr, 0, sizeof(int));
-  cudaFuncSetAttribute(k_umma_selftest, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (cudaMemcpy(dA, A, sizeof(float) * 128 * K, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(dB, B, sizeof(float) * N * K, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemset(dErr, 0, sizeof(int)) != cudaSuccess ||
+      cudaFuncSetAttribute(k_umma_selftest, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+    st = B200DP_ERR_CUDA;
+    goto done;
+  }
   count_launch();
   k_umma_selftest<<<1, 128, smem>>>(K, N, a_mn_major, b_mn_major, passes, dA, dB, dC, dErr);
   if (cudaDeviceSynchronize() != cudaSuccess || cudaGetLastError() != cudaSuccess) {
     st = B200DP_ERR_CUDA;
     goto done;
   }
-  cudaMemcpy(&herr, dErr, sizeof(int), cudaMemcpyDeviceToHost);
-  if (herr) {
+  if (cudaMemcpy(&herr, dErr, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess || herr ||
+      cudaMemcpy(C, dC, sizeof(float) * 128 * N, cudaMemcpyDeviceToHost) != cudaSuccess)
     st = B200DP_ERR_CUDA;
-    goto done;
-  }
-  cudaMemcpy(C, dC, sizeof(float) * 128 * N, cudaMemcpyDeviceToHost);
 done:
   cudaFree(dA);
   cudaFree(dB);
