@@ -176,15 +176,20 @@ def peaks():
 
 
 def ncu_traffic(kernel: str):
-    """DRAM bytes per launch of `kernel` recorded in the committed ncu summary."""
+    """DRAM bytes per launch of `kernel` recorded in the committed ncu summary, and the summary's
+    note on which build of the kernel that capture measured (None when it has none)."""
     path = os.path.join(ROOT, "profiles", f"{kernel}_c1_water.md")
     if not os.path.exists(path):
-        return None
+        return None, None
+    value = note = None
     for line in open(path):
         m = re.match(r"\s*traffic_bytes_per_launch:\s*([0-9.eE+]+)", line)
         if m:
-            return float(m.group(1))
-    return None
+            value = float(m.group(1))
+        m = re.match(r"\s*traffic_note:\s*(.+)", line)
+        if m:
+            note = m.group(1).strip()
+    return value, note
 
 
 # ----------------------------------------------------------------- arms
@@ -530,11 +535,14 @@ def run_b200dp(args, world, rank, local):
     else:  # the fp64 products and fp64 instructions share one pipe; no fp64 peak is measured on this pool
         peak = FP64_NOMINAL_TFLOPS
         peak_source = "nominal B200 fp64 (tensor and vector), no measured fp64 peak"
+    traffic, traffic_note = ncu_traffic("embed_bwd_tc" if mixed else "embed_f64")
     roofline = {"kernel": "k_embed_bwd_tc" if mixed else "k_embed_bwd_f64", "bound": "tensor",
                 "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                "traffic": ncu_traffic("embed_bwd_tc" if mixed else "embed_f64"), "peak_source": peak_source,
+                "traffic": traffic, "peak_source": peak_source,
                 "flops_per_launch": fl["descriptor_bwd"], "avg_launch_ms": bwd_ms,
                 "note": "algorithmic FLOPs of the embedding backward over the CUDA-event time of its stage"}
+    if traffic_note:
+        roofline["traffic_note"] = traffic_note
     if mixed:
         # the pipe that bounds the embedding kernels: the multi-function unit (MUFU / XU), 16 results per
         # clock per SM; every tanh feature of every edge costs one ex2 and one rcp, and the backward
