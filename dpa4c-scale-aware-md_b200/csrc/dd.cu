@@ -349,7 +349,7 @@ struct b200dp_dd {
   long long step = 0, last_rebuild = 0;
   std::vector<double> x_at_rebuild;
   double max_move = 0;
-  // NPT (isotropic, host-side scalars as the single-GPU driver)
+  // NPT (isotropic): thermostat and barostat scalars on the host of every rank
   HostChain tch, pch;
   double omega_dot = 0, w_mass = 0, vol0 = 0, t_current = 0, vir_trace = 0;
   std::string err;
@@ -521,10 +521,11 @@ b200dp_status md_step(b200dp_dd* dd) {
   return cudaGetLastError() == cudaSuccess ? B200DP_OK : B200DP_ERR_CUDA;
 }
 
-// One NPT step in LAMMPS' fix npt iso order (as the single-GPU driver): the
-// barostat and thermostat scalars on the host of every rank, fed by the
-// global kinetic energy and virial of the rendezvous (the same bits on every
-// rank, so every rank computes the same box); one host read per step.
+// One NPT step in LAMMPS' fix npt iso order (the order of the single-GPU
+// driver, which keeps these scalars on the device): here the barostat and
+// thermostat scalars live on the host of every rank, fed by the global
+// kinetic energy and virial of the rendezvous (the same bits on every rank,
+// so every rank computes the same box); one host read per step.
 b200dp_status npt_step(b200dp_dd* dd) {
   const b200dp_md_params& p = dd->mp;
   const int n = dd->nown;
