@@ -95,12 +95,26 @@ typedef struct b200dp_nlist {
 
 typedef struct b200dp_engine b200dp_engine;
 
+/* Options with their defaults (mixed precision, device 0).  No single
+ * counterpart: the reference takes the device from DeepPot::init's gpu_rank
+ * and its precision settings from its engine configuration
+ * (config/engine.production.json.in). */
 void b200dp_options_default(b200dp_options* opt);
 
-/* Loads a model file and prepares device-resident weights. */
+/* Loads a model file and prepares device-resident weights.  Replaces
+ * DeepPot::init (components/deepmd-op/overlays/api_cc/include/DeepPot.h:475)
+ * with the PT-expt backend's load and priming
+ * (components/deepmd-op/overlays/api_cc/src/DeepPotPTExpt.cc:324). */
 b200dp_status b200dp_create(const char* model_path, const b200dp_options* opt, b200dp_engine** out);
+/* Releases the engine's device memory and streams (DeePMD's ~DeepPot,
+ * DeepPot.h:457). */
 void b200dp_destroy(b200dp_engine* engine);
+/* Message of the engine's last failed call: the text that the reference's
+ * translate_error (DeepPotPTExpt.cc:295) puts into the exception it throws. */
 const char* b200dp_last_error(const b200dp_engine* engine);
+/* Model shape: DeepPotPTExpt::cutoff() / numb_types()
+ * (components/deepmd-op/overlays/api_cc/include/DeepPotPTExpt.h:103-110),
+ * plus the sel and network widths the caller's buffers depend on. */
 b200dp_status b200dp_model_info_get(const b200dp_engine* engine, b200dp_model_info* out);
 /* CUDA device ordinal the engine runs on (-1 for NULL). */
 int b200dp_engine_device(const b200dp_engine* engine);
@@ -126,14 +140,22 @@ b200dp_status b200dp_compute_host(b200dp_engine* engine, int nlocal, int nghost,
 
 /* As b200dp_compute_host, with the caller's LAMMPS full neighbour list
  * (indices into [0, nall)); nghost atoms are ghosts.  Mirrors
- * DeepPot::compute(..., nghost, lmp_list, ago). */
+ * DeepPot::compute(..., nghost, lmp_list, ago)
+ * (components/deepmd-op/overlays/api_cc/include/DeepPot.h:605-690), as
+ * PairDeepMD::compute calls it
+ * (components/lammps-deepmd-plugin/src/pair_deepmd.cpp:356-371). */
 b200dp_status b200dp_compute_host_nlist(b200dp_engine* engine, int nlocal, int nghost, const double* coord,
                                         const int* atype, const b200dp_nlist* nlist, double* energy,
                                         double* force, double* virial, double* atom_energy,
                                         double* atom_virial);
 
 /* Device buffers, work enqueued on `stream` (a cudaStream_t; NULL = legacy
- * default stream).  No host synchronisation: device-side error counters are
+ * default stream): DeepPot::compute_canonical_graph_gpu on the pair style's
+ * device views and stream
+ * (components/deepmd-op/overlays/api_cc/include/DeepPot.h:903-915, called
+ * from components/lammps-deepmd-plugin/src/pair_deepmd_kokkos.cpp:702-709),
+ * with coordinates in place of the caller's graph (the engine builds its own
+ * neighbour list).  No host synchronisation: device-side error counters are
  * read by b200dp_check.  box and region are HOST arrays (9 and 6 doubles):
  * region = {lo_x, lo_y, lo_z, hi_x, hi_y, hi_z} bounds the binning grid in
  * ghost mode (atoms outside it are still handled correctly, only slower); it
@@ -145,7 +167,9 @@ b200dp_status b200dp_compute_device(b200dp_engine* engine, void* stream, int nlo
                                     double* d_virial, double* d_atom_energy, double* d_atom_virial);
 
 /* As b200dp_compute_device for a periodic system (nghost = 0) whose box
- * lives in device memory: d_box [9] (rows are cell vectors) is read by the
+ * lives in device memory (no counterpart in the reference's force call; it
+ * serves this library's device-resident NPT driver): d_box [9] (rows are
+ * cell vectors) is read by the
  * kernels when they run, so a barostat can change it on the device between
  * calls with no host round trip.  The binning grid (cell counts, stencil
  * reach) comes from the host reference box_ref [9] scaled by min_scale
@@ -157,31 +181,38 @@ b200dp_status b200dp_compute_device_dbox(b200dp_engine* engine, void* stream, in
                                          const double* d_box, double* d_energy, double* d_force, double* d_virial);
 
 /* Synchronises the engine's last stream and converts device error counters
- * into a status (B200DP_ERR_SEL_OVERFLOW / _CAPACITY / _BAD_TYPE). */
+ * into a status (B200DP_ERR_SEL_OVERFLOW / _CAPACITY / _BAD_TYPE /
+ * _PEER_TIMEOUT): where the reference raises TORCH_CHECK exceptions that
+ * translate_error catches
+ * (components/deepmd-op/overlays/api_cc/src/DeepPotPTExpt.cc:295). */
 b200dp_status b200dp_check(b200dp_engine* engine);
 
 /* Number of neighbour candidates the last call dropped because a type
- * section exceeded sel (synchronises). */
+ * section exceeded sel (synchronises).  No counterpart: DeePMD truncates at
+ * sel silently. */
 long long b200dp_sel_overflow_count(b200dp_engine* engine);
 
 /* The canonical neighbour list of the last call, copied to host: nlist and
  * image [nlocal*sel_total] (j index or -1; image code ((n0+512)<<20 |
  * (n1+512)<<10 | (n2+512))), rij [nlocal*sel_total*3].  Any pointer may be
- * NULL.  For parity tests and debugging. */
+ * NULL.  For parity tests and debugging (no counterpart in the reference). */
 b200dp_status b200dp_last_nlist(b200dp_engine* engine, int* nlist, int* image, double* rij);
 
 /* Descriptor and its energy gradient of the last call, [nlocal * descriptor_dim]
- * in atom order, widened to fp64.  In mixed precision with the tensor-core
+ * in atom order, widened to fp64 (no counterpart in the reference; for parity
+ * tests).  In mixed precision with the tensor-core
  * path this needs an engine created with keep_descriptor = 1 (else
  * B200DP_ERR_INVALID). */
 b200dp_status b200dp_last_descriptor(b200dp_engine* engine, double* descriptor, double* grad_descriptor);
 
 /* Per-stage device times of the last call in milliseconds (CUDA events on
- * the launch stream): [0] neighbour build, [1] descriptor forward,
+ * the launch stream; the reference's profile families,
+ * data/profile-families.csv, time the same stages): [0] neighbour build, [1] descriptor forward,
  * [2] fitting, [3] descriptor backward, [4] force/virial assembly.
  * Timing is enabled by b200dp_set_stage_timing(engine, 1). */
 b200dp_status b200dp_set_stage_timing(b200dp_engine* engine, int enable);
-/* Self-test of the tensor-core (tcgen05) layer: C[128 x N] = A[128 x K] *
+/* Self-test of the tensor-core (tcgen05) layer (no counterpart in the
+ * reference, whose kernels have no tcgen05 path): C[128 x N] = A[128 x K] *
  * B[N x K]^T from host fp32 arrays, bf16 split with 1 or 3 products,
  * operands in K-major or MN-major layout.  K, N multiples of 16, K <= 256,
  * 16 <= N <= 256, 4*K*(128+N) <= 200 KiB.  Synchronous; allocates its own
@@ -312,7 +343,9 @@ typedef enum b200dp_md_ensemble { B200DP_MD_NVE = 0, B200DP_MD_NVT = 1, B200DP_M
  * (LO/KOKKOS/npair_kokkos.cpp:151-460; neighbor->decide()). */
 b200dp_status b200dp_set_neighbor_reuse(b200dp_engine* engine, double skin, int every);
 /* builds[0] = scheduled candidate builds, builds[1] = builds triggered by the
- * displacement check (synchronises the engine's last stream). */
+ * displacement check (synchronises the engine's last stream); the
+ * counterpart of the neighbour-list build counts LAMMPS reports at the end of
+ * a run. */
 b200dp_status b200dp_neighbor_stats(b200dp_engine* engine, long long* builds);
 
 /* Halo exchange and reverse fold for spatial domain decomposition, one
@@ -430,8 +463,10 @@ b200dp_status b200dp_md_write_restart(b200dp_md* md, const char* path);
 b200dp_status b200dp_md_read_restart(b200dp_md* md, const char* path);
 b200dp_status b200dp_md_destroy(b200dp_md* md);
 
-/* Total kernels this library has launched in the process (all engines). */
+/* Total kernels this library has launched in the process (all engines).
+ * Measurement only (no counterpart in the reference). */
 long long b200dp_kernel_launches(void);
+/* The five stage times of b200dp_set_stage_timing, in milliseconds. */
 b200dp_status b200dp_stage_times(b200dp_engine* engine, float* ms5);
 
 /* ------------------------------------------------------------------ multi-GPU driver (C++)
