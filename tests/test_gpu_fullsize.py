@@ -1,7 +1,9 @@
 """Full-size configurations through size-independent properties.
 
-At the benchmark configurations' full sizes the CPU oracle is too slow to be
-the reference, so these checks use properties that hold at any size:
+These checks sit beside the oracle comparisons of test_gpu_fullsize_oracle.py
+(configs 2, 3, the 786,432-atom water box and slab against one CPU oracle
+evaluation each) and add properties that hold at any size, including the
+98,304- and 3,145,728-atom water boxes that have no oracle run:
   * fp64 and mixed precision agree (energy per atom, force RMSE and maximum,
     virial) within the mixed-mode acceptance limits;
   * the total force vanishes (translation invariance) and the virial is
