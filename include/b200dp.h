@@ -365,7 +365,8 @@ b200dp_status b200dp_neighbor_stats(b200dp_engine* engine, long long* builds);
  *   b200dp_halo_gather   writes the ghost rows nlocal.. of d_coord from the
  *                        owners' published positions (+ shift) -- only after
  *                        every rank's publish of this step has completed
- *                        (e.g. after a one-element all-reduce on the stream);
+ *                        (b200dp_peer_reduce with nv = 0 on the stream, or
+ *                        a one-element all-reduce of the caller's own);
  *   b200dp_compute_device_fold  the ghost-mode force call: energy and virial
  *                        of the owned atoms' edges as usual; the ghost rows'
  *                        reverse contributions are added into the owners'
@@ -373,8 +374,9 @@ b200dp_status b200dp_neighbor_stats(b200dp_engine* engine, long long* builds);
  *                        order-independent sums) and d_force is not complete
  *                        yet;
  *   b200dp_fold_finish   after EVERY rank's compute_device_fold has completed
- *                        (e.g. after the all-reduce of energy and virial on
- *                        the same stream), writes the owned rows of d_force
+ *                        (b200dp_peer_reduce of energy and virial, nv = 10,
+ *                        or a caller's all-reduce of them, on the same
+ *                        stream), writes the owned rows of d_force
  *                        and clears the accumulator.
  * Replaces the pair style's forward and reverse ghost communication
  * (PL/pair_deepmd_kokkos.cpp:931, comm->reverse_comm; LAMMPS comm->forward_comm). */
