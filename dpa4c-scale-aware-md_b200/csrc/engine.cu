@@ -1437,7 +1437,9 @@ b200dp_status b200dp_create(const char* model_path, const b200dp_options* opt, b
 
 void b200dp_destroy(b200dp_engine* engine) {
   if (!engine) return;
+  b200dp::g_err_sink = &engine->e.err;
   engine->e.release();
+  b200dp::g_err_sink = nullptr;  // this thread's error sink must not outlive the engine
   delete engine;
 }
 
